@@ -1,0 +1,454 @@
+"""Benchmark of the GDN-2 hot path on B200: prints ONE JSON line.
+
+Headline workload (per GPU): chunked GDN-2 prefill, B=8, H=16, T=4096,
+d_k = d_v = 128, chunk 64, bf16 q/k/v, f32 alpha/beta and state.  A step is one prefill pass over
+one batch.  With N GPUs every rank runs its own B=8 batch (batch x head sharding with no
+data-path collective: weak scaling); the time is the max over ranks.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+value  : tokens (B*T, all heads) per second over all ranks, inputs resident in HBM.
+e2e    : the same through the public API (delta_block_lm_b200.gdn2_prefill) with the step's
+         inputs copied from pinned host memory and its outputs copied back inside the timed region.
+--impl reference: the reference's CPU algorithm (chunk::scan, crates/mixers/src/chunk.rs:129-250,
+         restated in C under oracle/ because the Rust workspace cannot be built here), timed on
+         the host cores on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "GDN-2 prefill Mtok/s/GPU, decode tok/s; % of HBM / tensor-core roofline"
+B, T, H, D, CHUNK = 8, 4096, 16, 128, 64
+# algorithmic minimum bytes per token-head: q,k,v,o bf16 (4 x 128 x 2) + alpha, beta f32
+BYTES_PER_TOKEN_HEAD = 4 * D * 2 + 8
+FLOPS_PER_TOKEN_HEAD = 2 * (CHUNK * (3 * D + 2 * D) + 3 * D * D)
+L2_BYTES = 126 * 2 ** 20
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def ncu_traffic(kernel_key: str):
+    """DRAM bytes per launch of `kernel_key` from the committed ncu summary, if one exists."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
+            return json.load(f).get(kernel_key)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples for one GPU during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        self.ident = None
+        try:
+            import torch
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            self.ident = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+        except Exception:
+            self.ident = str(device_index)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.ident, f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "20"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[3:7]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------ CPU baseline
+def cpu_chunk_sample(target_s: float, nthreads: int, reps: int = 1):
+    """Time the reference CPU algorithm (chunk.rs restated, f32, chunk 16) on B8/H16/d128 with a
+    T chosen so one call takes about target_s seconds.  Returns (tok_per_s, T_sample, secs)."""
+    import numpy as np
+
+    from oracle import oracle as O
+
+    def inputs(t):
+        rng = np.random.default_rng(0)
+        q = rng.standard_normal((B, t, H, D), dtype=np.float32)
+        k = rng.standard_normal((B, t, H, D), dtype=np.float32)
+        q /= np.linalg.norm(q, axis=-1, keepdims=True)
+        k /= np.linalg.norm(k, axis=-1, keepdims=True)
+        v = rng.standard_normal((B, t, H, D), dtype=np.float32)
+        beta = (1 / (1 + np.exp(-rng.standard_normal((B, t, H))))).astype(np.float32)
+        alpha = np.exp(-np.logaddexp(0, -rng.normal(3, 1, (B, t, H)))).astype(np.float32)
+        a = np.ascontiguousarray(np.broadcast_to(alpha[..., None], (B, t, H, D)))
+        e = np.ascontiguousarray(np.broadcast_to(beta[..., None], (B, t, H, D)))
+        return q / math.sqrt(D), k, v, a, e, e
+
+    def run(t):
+        x = inputs(t)
+        t0 = time.perf_counter()
+        O.chunk_scan_f32(*x, chunk=16, nthreads=nthreads, want_scores=False)
+        return time.perf_counter() - t0
+
+    probe_t = 32
+    dt = run(probe_t)
+    t_s = int(max(16, min(T, probe_t * target_s / max(dt, 1e-6))) // 16 * 16)
+    times = [run(t_s) for _ in range(reps)]
+    secs = statistics.median(times)
+    return B * t_s / secs, t_s, secs
+
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return 0
+    cores = host_cores()
+    from oracle import oracle as O
+    O.build()
+    # warm-up and timed samples of the same workload (B8/H16/d128, shorter T)
+    vals = []
+    t_s = None
+    for i in range(args.warmup + args.steps):
+        v, t_s, _ = cpu_chunk_sample(target_s=2.0 if t_s is None else 2.0, nthreads=cores)
+        if i >= args.warmup:
+            vals.append(v)
+    value = statistics.median(vals) / 1e6
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "Mtok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": B * t_s / (value * 1e6) * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"c1 prefill sample B{B}/H{H}/T{t_s}/d{D} (chunk 16, the reference's maximum)",
+                   "batch_per_gpu": B, "heads": H, "seq_len_sample": t_s, "d_k": D, "d_v": D},
+        "cpu_baseline": {"value": value, "unit": "Mtok/s", "cores": cores, "kind": "port",
+                         "sample": f"B{B}/H{H}/T{t_s}/d{D} per step, chunk::scan restated in C (OpenMP)"},
+        "e2e": {"value": value, "unit": "Mtok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------ GPU workloads
+def make_prefill_inputs(torch, dev, seed, b=B, t=T, h=H, d=D):
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    q = torch.randn((b, t, h, d), device=dev, generator=g)
+    k = torch.randn((b, t, h, d), device=dev, generator=g)
+    q = (q / q.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    k = (k / k.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    v = torch.randn((b, t, h, d), device=dev, generator=g).to(torch.bfloat16)
+    beta = torch.sigmoid(torch.randn((b, t, h), device=dev, generator=g))
+    alpha = torch.exp(torch.nn.functional.logsigmoid(3.0 + torch.randn((b, t, h), device=dev, generator=g)))
+    return q, k, v, alpha.contiguous(), beta.contiguous()
+
+
+def bench_prefill(torch, dist, args, dev, rank, world):
+    import ctypes
+
+    import delta_block_lm_b200 as dbl
+    from delta_block_lm_b200 import _native as N
+    from delta_block_lm_b200.kernels import _prefill_args
+
+    q, k, v, alpha, beta = make_prefill_inputs(torch, dev, 1234 + rank)
+    out = torch.empty((B, T, H, D), device=dev, dtype=torch.bfloat16)
+    fin = torch.empty((B, H, D, D), device=dev, dtype=torch.float32)
+    a = _prefill_args(q, k, v, alpha, beta, 1.0 / math.sqrt(D), None, None, None, out, fin, CHUNK)
+    lib = N.lib()
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+
+    def step():
+        N.check(lib.dbl_gdn2_prefill(ctypes.byref(a), sh))
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    sampler = ClockSampler(dev.index)
+    sampler.start()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        step()
+        ev[i][1].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    if world > 1:
+        dist.barrier()
+    elapsed_ms = t_start.elapsed_time(t_end)
+    launch_ms = statistics.mean(s.elapsed_time(e) for s, e in ev)
+    if world > 1:
+        tt = torch.tensor([elapsed_ms, launch_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        elapsed_ms, launch_ms = tt.tolist()
+    ms_per_step = elapsed_ms / args.steps
+    tokens = B * T * world * args.steps
+    value = tokens / (elapsed_ms / 1e3) / 1e6
+
+    # e2e through the public API with host buffers
+    e2e_steps = max(1, min(args.steps, 5))
+    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+    ha, hb = alpha.cpu().pin_memory(), beta.cpu().pin_memory()
+    ho = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    hf = torch.empty(fin.shape, dtype=fin.dtype).pin_memory()
+    dq, dk, dv, da, db = (torch.empty_like(x) for x in (q, k, v, alpha, beta))
+
+    def e2e_step():
+        for d_, h_ in ((dq, hq), (dk, hk), (dv, hv), (da, ha), (db, hb)):
+            d_.copy_(h_, non_blocking=True)
+        o, f = dbl.gdn2_prefill(dq, dk, dv, da, db, out=out, final_state=fin)
+        ho.copy_(o, non_blocking=True)
+        hf.copy_(f, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    s1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = s0.elapsed_time(s1)
+    if world > 1:
+        tt = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_ms = tt.item()
+    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv, ha, hb))
+    d2h = ho.numel() * ho.element_size() + hf.numel() * hf.element_size()
+    e2e = {"value": B * T * world * e2e_steps / (e2e_ms / 1e3) / 1e6, "unit": "Mtok/s",
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps}
+
+    hbm, tflops, src = peaks()
+    token_heads = B * T * H
+    alg_bytes = token_heads * BYTES_PER_TOKEN_HEAD + B * H * D * D * 4
+    alg_flops = token_heads * FLOPS_PER_TOKEN_HEAD
+    achieved = alg_bytes / (launch_ms / 1e3) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": achieved / hbm, "peak_source": src,
+                "traffic": ncu_traffic("gdn2_prefill_c1"),
+                "algorithmic_bytes_per_launch": alg_bytes,
+                "tensor_tflops": alg_flops / (launch_ms / 1e3) / 1e12,
+                "tensor_frac": alg_flops / (launch_ms / 1e3) / 1e12 / tflops,
+                "roofline_time_us": max(alg_bytes / hbm / 1e3, alg_flops / tflops / 1e6)}
+    input_bytes = sum(x.numel() * x.element_size() for x in (q, k, v, alpha, beta))
+    result = {
+        "value": value, "ms_per_step": ms_per_step, "launch_ms": launch_ms, "clocks": clocks,
+        "e2e": e2e, "gpu_launches": args.steps, "roofline": roofline,
+        "config": {"workload": f"c1 prefill B{B}/H{H}/T{T}/d{D} bf16 chunk {CHUNK} per GPU",
+                   "batch_per_gpu": B, "heads": H, "seq_len": T, "d_k": D, "d_v": D, "chunk": CHUNK,
+                   "global_batch": B * world,
+                   "parallelism": f"batch x head sharded over {world} GPU(s), no data-path collective",
+                   "l2": f"no flush: inputs {input_bytes / 1e6:.0f} MB > {L2_BYTES / 1e6:.0f} MB L2"},
+    }
+    return result
+
+
+def bench_decode(torch, args, dev):
+    """Config 2: 256 sequences x 16 heads x 128^2 f32 state, 64 consecutive in-place steps."""
+    import ctypes
+
+    from delta_block_lm_b200 import _native as N
+    from delta_block_lm_b200.kernels import _strides
+
+    n, steps = 256, 64
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    state = 0.02 * torch.randn((n, H, D, D), device=dev, generator=g)
+    q = torch.randn((steps, n, H, D), device=dev, generator=g)
+    k = torch.randn((steps, n, H, D), device=dev, generator=g)
+    q = (q / q.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    k = (k / k.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    v = torch.randn((steps, n, H, D), device=dev, generator=g).to(torch.bfloat16)
+    beta = torch.sigmoid(torch.randn((steps, n, H), device=dev, generator=g))
+    alpha = torch.exp(torch.nn.functional.logsigmoid(3.0 + torch.randn((steps, n, H), device=dev, generator=g)))
+    out = torch.empty((n, H, D), device=dev, dtype=torch.bfloat16)
+    lib = N.lib()
+    argv = []
+    for s in range(steps):
+        a = N.DecodeArgs()
+        a.batch, a.heads, a.key_dim, a.value_dim, a.dtype, a.scale = n, H, D, D, N.DBL_BF16, 1 / math.sqrt(D)
+        a.q, a.k, a.v = q[s].data_ptr(), k[s].data_ptr(), v[s].data_ptr()
+        a.q_stride, a.k_stride, a.v_stride = _strides(q[s], 3), _strides(k[s], 3), _strides(v[s], 3)
+        a.alpha, a.beta, a.state = alpha[s].data_ptr(), beta[s].data_ptr(), state.data_ptr()
+        a.out, a.out_stride = out.data_ptr(), _strides(out, 3)
+        argv.append(a)
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+
+    def run64():
+        for a in argv:
+            N.check(lib.dbl_gdn2_decode_step(ctypes.byref(a), sh))
+
+    for _ in range(2):
+        run64()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    e0.record(stream)
+    for _ in range(reps):
+        run64()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms_step = e0.elapsed_time(e1) / (reps * steps)
+    hbm, _, src = peaks()
+    alg = n * H * (2 * D * D * 4 + 3 * D * 2 + D * 2 + 8)
+    gbs = alg / (ms_step / 1e3) / 1e9
+    return {"workload": f"c2 decode {n} seq x H{H} x {D}x{D} f32 state, {steps} steps (x{reps})",
+            "tok_per_s": n / (ms_step / 1e3), "us_per_step": ms_step * 1e3,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                         "peak_source": src, "algorithmic_bytes_per_launch": alg,
+                         "traffic": ncu_traffic("gdn2_decode_c2")},
+            "gpu_launches": reps * steps}
+
+
+def bench_relay(torch, args, dev):
+    """Config 3: shared 4096-token prefix + 64 x 1024 own tokens, H16, hd128, bf16, 1 query/seq."""
+    import delta_block_lm_b200 as dbl
+
+    n, lp, lo = 64, 4096, 1024
+    g = torch.Generator(device=dev)
+    g.manual_seed(9)
+    mk = lambda *s: torch.randn(s, device=dev, generator=g).to(torch.bfloat16)  # noqa: E731
+    q, kp, vp, ko, vo = mk(n, H, D), mk(H, lp, D), mk(H, lp, D), mk(n, H, lo, D), mk(n, H, lo, D)
+    ws = torch.empty(dbl.relay_workspace_bytes(n, H, D, lp, lo), device=dev, dtype=torch.uint8)
+    out = torch.empty((n, H, D), device=dev, dtype=torch.bfloat16)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(3):
+        dbl.relay_merge_decode(q, kp, vp, ko, vo, out=out, workspace=ws, return_stats=False)
+    torch.cuda.synchronize(dev)
+    reps = 20
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        dbl.relay_merge_decode(q, kp, vp, ko, vo, out=out, workspace=ws, return_stats=False)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / reps
+    hbm, _, src = peaks()
+    alg = (2 * H * lp * D + 2 * n * H * lo * D + 2 * n * H * D) * 2
+    gbs = alg / (ms / 1e3) / 1e9
+    return {"workload": f"c3 relay decode prefix {lp} + {n} x {lo} own, H{H}, hd{D}, bf16",
+            "queries_per_s": n * H / (ms / 1e3), "us_per_call": ms * 1e3,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                         "peak_source": src, "algorithmic_bytes_per_launch": alg,
+                         "traffic": ncu_traffic("relay_merge_c3")},
+            "gpu_launches": reps}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-secondary", action="store_true", help="skip the decode / relay lines")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    from delta_block_lm_b200 import _native
+    _native.lib()
+    res = bench_prefill(torch, dist, args, dev, rank, world)
+    line = {"metric": METRIC, "value": res["value"], "unit": "Mtok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded normal q/k/v L2-normalised, beta = sigmoid(N(0,1)), "
+                    "alpha = exp(logsigmoid(N(3,1))))",
+            "config": res["config"], "clocks": res["clocks"], "e2e": res["e2e"],
+            "gpu_launches": res["gpu_launches"], "roofline": res["roofline"],
+            "kernel_ms_per_launch": res["launch_ms"]}
+    if world == 1 and rank == 0:
+        if not args.no_secondary:
+            line["secondary"] = {"decode": bench_decode(torch, args, dev), "relay": bench_relay(torch, args, dev)}
+        if not args.no_cpu_baseline:
+            cores = host_cores()
+            v, t_s, secs = cpu_chunk_sample(target_s=4.0, nthreads=cores, reps=3)
+            line["cpu_baseline"] = {"value": v / 1e6, "unit": "Mtok/s", "cores": cores, "kind": "port",
+                                    "sample": f"B{B}/H{H}/T{t_s}/d{D}, chunk 16, median of 3 x {secs:.1f} s "
+                                              "(chunk::scan restated in C, OpenMP)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,303 @@
+// Token-sequential GDN-2 scan: the reference's stateful fused recurrence, generalised.
+//
+// Serves the reference contracts that carry channel-wise gates and masks:
+//   dbl_gdn_training_scan  <- delta_kernels::gdn_training_scan (gdn_training.rs:12-115)
+//   dbl_gdn2_scan          <- delta_kernels::gdn2_scan (ops.rs:251-276; doc-limit masks)
+// and the scalar-gate prefill at shapes the tensor-core kernel does not take (f32 inputs,
+// K or V other than 128), e.g. BASELINE config 0.
+//
+// One CTA per (b, h); thread j owns state column j (K f32 registers), as the reference kernel's
+// lane-per-value-column layout (gdn_training.rs:28-49).  Tokens are staged TOK at a time in
+// shared memory so a CTA synchronises twice per TOK tokens, not per token.  Step order is the
+// reference's (reference.rs:62-108): padding -> o = 0, state kept; reset -> S = 0; decay;
+// edit = write v - sum_i erase_i k_i S_i; score = |k||edit|; S += k edit; o = q^T S.
+#include "scan_seq_params.cuh"
+
+namespace dbl {
+
+
+
+namespace {
+
+constexpr int TOK = 8;
+
+template <int KMAX, typename T, bool SCALAR>
+__global__ void __launch_bounds__(256) seq_scan_kernel(const SeqParams p) {
+    __shared__ float sk[TOK][KMAX], sq[TOK][KMAX];
+    __shared__ float sa[SCALAR ? 1 : TOK][KMAX], se[SCALAR ? 1 : TOK][KMAX];
+    __shared__ float sga[TOK], sgb[TOK];  // scalar gates
+    __shared__ int sact[TOK], srst[TOK];
+    __shared__ float sd2[TOK][8];         // per-warp partial |edit|^2
+    __shared__ float skk[TOK];
+
+    const int bh = blockIdx.x;
+    const int b = bh / p.H, h = bh - b * p.H;
+    const int j = threadIdx.x;
+    const int nthr = blockDim.x;
+    const bool col = j < p.V;
+    const int warp = j >> 5, lane = j & 31, nwarps = nthr >> 5;
+
+    float S[KMAX];
+    const size_t sbase = ((size_t)b * p.H + h) * p.K * p.V;
+#pragma unroll
+    for (int i = 0; i < KMAX; ++i) {
+        float x = 0.f;
+        if (col && i < p.K) {
+            if (p.init_mode == 1) x = p.initial[sbase + (size_t)i * p.V + j];
+            else if (p.init_mode == 2) x = (i == j) ? 1.f : 0.f;
+        }
+        S[i] = x;
+    }
+
+    const T* qb = static_cast<const T*>(p.q) + b * p.qs[0] + h * p.qs[2];
+    const T* kb = static_cast<const T*>(p.k) + b * p.ks[0] + h * p.ks[2];
+    const T* vb = static_cast<const T*>(p.v) + b * p.vs[0] + h * p.vs[2];
+
+    for (int t0 = 0; t0 < p.T; t0 += TOK) {
+        const int nt = min(TOK, p.T - t0);
+        __syncthreads();  // previous group's shared reads are complete
+        for (int x = j; x < TOK * KMAX; x += nthr) {
+            const int u = x / KMAX, i = x - u * KMAX;
+            float kv = 0.f, qv = 0.f, av = 1.f, ev = 0.f;
+            if (u < nt && i < p.K) {
+                const int t = t0 + u;
+                kv = to_f32(kb[t * p.ks[1] + i * p.ks[3]]);
+                qv = to_f32(qb[t * p.qs[1] + i * p.qs[3]]) * p.scale;
+                if (!SCALAR) {
+                    const size_t ga = (size_t)b * p.as[0] + (size_t)t * p.as[1] + (size_t)h * p.as[2] + (size_t)i * p.as[3];
+                    const size_t ge = (size_t)b * p.es[0] + (size_t)t * p.es[1] + (size_t)h * p.es[2] + (size_t)i * p.es[3];
+                    av = p.alpha[ga];
+                    ev = p.erase[ge];
+                }
+            }
+            sk[u][i] = kv;
+            sq[u][i] = qv;
+            if (!SCALAR) {
+                sa[u][i] = av;
+                se[u][i] = ev;
+            }
+        }
+        if (j < TOK) {
+            const int u = j, t = t0 + u;
+            int act = 0, rst = 0;
+            float ga = 1.f, gb = 0.f;
+            if (u < nt) {
+                if (p.mask_mode == 1) {
+                    act = p.valid[(size_t)b * p.T + t] != 0.f;
+                    rst = p.reset[(size_t)b * p.T + t] != 0.f;
+                } else if (p.mask_mode == 2) {
+                    const int32_t st = p.doc_start[(size_t)b * p.T + t], en = p.doc_end[(size_t)b * p.T + t];
+                    act = en >= st;
+                    rst = st == t;
+                } else {
+                    act = 1;
+                }
+                if (SCALAR) {
+                    ga = p.alpha[(size_t)b * p.as[0] + (size_t)t * p.as[1] + (size_t)h * p.as[2]];
+                    gb = p.erase[(size_t)b * p.es[0] + (size_t)t * p.es[1] + (size_t)h * p.es[2]];
+                }
+            }
+            sact[u] = act;
+            srst[u] = rst;
+            sga[u] = ga;
+            sgb[u] = gb;
+        }
+        __syncthreads();
+
+        for (int u = 0; u < nt; ++u) {
+            const int t = t0 + u;
+            const bool act = sact[u] != 0;
+            float delta = 0.f, o = 0.f;
+            if (act) {
+                float vj = 0.f, wj = 0.f;
+                if (col) {
+                    if (!p.v_zero) vj = to_f32(vb[t * p.vs[1] + j * p.vs[3]]);
+                    wj = SCALAR ? sgb[u]
+                                : p.write[(size_t)b * p.ws[0] + (size_t)t * p.ws[1] + (size_t)h * p.ws[2] + (size_t)j * p.ws[3]];
+                }
+                const bool rst = srst[u] != 0;
+                delta = wj * vj;
+                if (SCALAR) {
+                    const float a = rst ? 0.f : sga[u];
+                    float kS = 0.f;
+#pragma unroll
+                    for (int i = 0; i < KMAX; ++i) {
+                        S[i] *= a;
+                        kS = fmaf(sk[u][i], S[i], kS);
+                    }
+                    delta -= sgb[u] * kS;
+                } else {
+#pragma unroll
+                    for (int i = 0; i < KMAX; ++i) {
+                        S[i] = rst ? 0.f : S[i] * sa[u][i];
+                        delta -= se[u][i] * sk[u][i] * S[i];
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < KMAX; ++i) {
+                    S[i] = fmaf(sk[u][i], delta, S[i]);
+                    o = fmaf(sq[u][i], S[i], o);
+                }
+            }
+            if (p.out && col) {
+                const size_t oi = (size_t)b * p.os[0] + (size_t)t * p.os[1] + (size_t)h * p.os[2] + (size_t)j * p.os[3];
+                if (p.out_dtype == DBL_BF16) static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(o);
+                else static_cast<float*>(p.out)[oi] = o;
+            }
+            if (p.scores) {
+                float d2 = col ? delta * delta : 0.f;
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) d2 += __shfl_xor_sync(0xffffffffu, d2, off);
+                if (lane == 0) sd2[u][warp] = d2;
+            }
+        }
+        if (p.scores) {
+            if (warp == 0 && lane < TOK) {
+                // |k|^2 for the TOK staged tokens (lane = token).
+                float kk = 0.f;
+                for (int i = 0; i < p.K; ++i) kk = fmaf(sk[lane][i], sk[lane][i], kk);
+                skk[lane] = kk;
+            }
+            __syncthreads();
+            if (j < nt) {
+                const int u = j, t = t0 + u;
+                float d2 = 0.f;
+                for (int w = 0; w < nwarps; ++w) d2 += sd2[u][w];
+                const float sc = sact[u] ? sqrtf(skk[u]) * sqrtf(d2) : 0.f;
+                p.scores[((size_t)b * p.T + t) * p.H + h] = sc;
+            }
+        }
+    }
+    if (p.final_state && col) {
+#pragma unroll
+        for (int i = 0; i < KMAX; ++i)
+            if (i < p.K) p.final_state[sbase + (size_t)i * p.V + j] = S[i];
+    }
+}
+
+template <int KMAX, typename T>
+int launch_seq_t(const SeqParams& p, cudaStream_t st) {
+    const int threads = ((p.V + 31) / 32) * 32;
+    const unsigned grid = (unsigned)(p.B * p.H);
+    if (p.gate_mode == 1) seq_scan_kernel<KMAX, T, true><<<grid, threads, 0, st>>>(p);
+    else seq_scan_kernel<KMAX, T, false><<<grid, threads, 0, st>>>(p);
+    return launch_status("seq_scan_kernel");
+}
+
+}  // namespace
+
+// Validates shape limits shared by every caller, then launches.
+int launch_seq_scan(const SeqParams& p, int in_dtype, cudaStream_t st) {
+    if (p.B <= 0 || p.T <= 0 || p.H <= 0 || p.K <= 0 || p.V <= 0)
+        return fail(DBL_ERR_INVALID_ARGUMENT, "GDN-2 requires nonempty axes");
+    if (p.K > 128) return fail(DBL_ERR_UNSUPPORTED, "sequential scan supports key_dim <= 128 (got %d)", p.K);
+    if (p.V > 256) return fail(DBL_ERR_UNSUPPORTED, "sequential scan supports value_dim <= 256 (got %d)", p.V);
+    if ((int64_t)p.B * p.H > 0x7fffffffLL) return fail(DBL_ERR_UNSUPPORTED, "batch*heads exceeds the grid limit");
+    const bool bf = in_dtype == DBL_BF16;
+    if (p.K <= 32) return bf ? launch_seq_t<32, __nv_bfloat16>(p, st) : launch_seq_t<32, float>(p, st);
+    if (p.K <= 64) return bf ? launch_seq_t<64, __nv_bfloat16>(p, st) : launch_seq_t<64, float>(p, st);
+    return bf ? launch_seq_t<128, __nv_bfloat16>(p, st) : launch_seq_t<128, float>(p, st);
+}
+
+}  // namespace dbl
+
+// --------------------------------------------------------------------------------------------
+// delta_kernels::gdn_training_scan (crates/kernels/src/gdn_training_ops.rs:288-333) forward.
+extern "C" int dbl_gdn_training_scan(const dbl_training_scan_args* a, dbl_stream_t stream) {
+    using namespace dbl;
+    if (!a) return fail(DBL_ERR_INVALID_ARGUMENT, "gdn_training_scan: null args");
+    if (a->batch <= 0 || a->time <= 0 || a->heads <= 0)
+        return fail(DBL_ERR_INVALID_ARGUMENT, "GDN-2 requires nonempty axes");
+    if (a->key_dim <= 0 || a->value_dim <= 0)
+        return fail(DBL_ERR_INVALID_ARGUMENT, "GDN-2 requires nonempty key and value widths");
+    if (a->chunk_size < 1 || a->chunk_size > 16)
+        return fail(DBL_ERR_INVALID_ARGUMENT, "GDN-2 checkpoint chunk must be 1..=16");
+    if (a->dtype != DBL_F32 && a->dtype != DBL_BF16)
+        return fail(DBL_ERR_INVALID_ARGUMENT, "fused GDN-2 supports f32 or bf16 q/k/v");
+    if (!a->q || !a->k || !a->v || !a->alpha || !a->erase || !a->write || !a->valid || !a->reset || !a->output)
+        return fail(DBL_ERR_INVALID_ARGUMENT,
+                    "gdn_training_scan: q, k, v, alpha, erase, write, valid, reset and output are required");
+    if (a->batch > 0x7fffffff || a->time > 0x7fffffff || a->heads > 0x7fffffff || a->key_dim > 0x7fffffff ||
+        a->value_dim > 0x7fffffff)
+        return fail(DBL_ERR_UNSUPPORTED, "GDN-2 axis exceeds 32-bit limits");
+    SeqParams p{};
+    p.B = (int)a->batch;
+    p.T = (int)a->time;
+    p.H = (int)a->heads;
+    p.K = (int)a->key_dim;
+    p.V = (int)a->value_dim;
+    const int64_t dk[4] = {a->batch, a->time, a->heads, a->key_dim};
+    const int64_t dv[4] = {a->batch, a->time, a->heads, a->value_dim};
+    const int64_t z[4] = {0, 0, 0, 0};
+    p.q = a->q;
+    p.k = a->k;
+    p.v = a->v;
+    resolve_strides(z, dk, 4, p.qs);
+    resolve_strides(z, dk, 4, p.ks);
+    resolve_strides(z, dv, 4, p.vs);
+    p.gate_mode = 0;
+    p.alpha = a->alpha;
+    p.erase = a->erase;
+    p.write = a->write;
+    resolve_strides(z, dk, 4, p.as);
+    resolve_strides(z, dk, 4, p.es);
+    resolve_strides(z, dv, 4, p.ws);
+    p.scale = 1.f;
+    p.mask_mode = 1;
+    p.valid = a->valid;
+    p.reset = a->reset;
+    p.init_mode = a->initial_state ? 1 : 0;
+    p.initial = a->initial_state;
+    p.out = a->output;
+    p.out_dtype = DBL_F32;
+    resolve_strides(z, dv, 4, p.os);
+    p.final_state = a->final_state;
+    p.scores = a->scores;
+    return launch_seq_scan(p, a->dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+
+// delta_kernels::gdn2_scan (crates/kernels/src/ops.rs:251-276): doc-limit masks, zero initial.
+extern "C" int dbl_gdn2_scan(const dbl_gdn2_scan_args* a, dbl_stream_t stream) {
+    using namespace dbl;
+    if (!a) return fail(DBL_ERR_INVALID_ARGUMENT, "gdn2_scan: null args");
+    if (a->batch <= 0 || a->time <= 0 || a->heads <= 0 || a->key_dim <= 0 || a->value_dim <= 0)
+        return fail(DBL_ERR_INVALID_ARGUMENT, "GDN-2 requires nonempty axes");
+    if (a->dtype != DBL_F32 && a->dtype != DBL_BF16)
+        return fail(DBL_ERR_INVALID_ARGUMENT, "gdn2_scan: dtype must be f32 or bf16");
+    if (!a->q || !a->k || !a->v || !a->alpha || !a->erase || !a->write || !a->doc_start || !a->doc_end || !a->output)
+        return fail(DBL_ERR_INVALID_ARGUMENT, "gdn2_scan: every pointer is required");
+    if (a->batch > 0x7fffffff || a->time > 0x7fffffff || a->heads > 0x7fffffff || a->key_dim > 0x7fffffff ||
+        a->value_dim > 0x7fffffff)
+        return fail(DBL_ERR_UNSUPPORTED, "GDN-2 axis exceeds 32-bit limits");
+    SeqParams p{};
+    p.B = (int)a->batch;
+    p.T = (int)a->time;
+    p.H = (int)a->heads;
+    p.K = (int)a->key_dim;
+    p.V = (int)a->value_dim;
+    const int64_t dk[4] = {a->batch, a->time, a->heads, a->key_dim};
+    const int64_t dv[4] = {a->batch, a->time, a->heads, a->value_dim};
+    const int64_t z[4] = {0, 0, 0, 0};
+    p.q = a->q;
+    p.k = a->k;
+    p.v = a->v;
+    resolve_strides(z, dk, 4, p.qs);
+    resolve_strides(z, dk, 4, p.ks);
+    resolve_strides(z, dv, 4, p.vs);
+    p.gate_mode = 0;
+    p.alpha = a->alpha;
+    p.erase = a->erase;
+    p.write = a->write;
+    resolve_strides(z, dk, 4, p.as);
+    resolve_strides(z, dk, 4, p.es);
+    resolve_strides(z, dv, 4, p.ws);
+    p.scale = 1.f;
+    p.mask_mode = 2;
+    p.doc_start = a->doc_start;
+    p.doc_end = a->doc_end;
+    p.init_mode = 0;
+    p.out = a->output;
+    p.out_dtype = a->dtype;
+    resolve_strides(z, dv, 4, p.os);
+    return launch_seq_scan(p, a->dtype, reinterpret_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,35 @@
+// Parameters of the token-sequential GDN-2 scan kernel (scan_seq.cu), shared with the
+// prefill dispatcher (prefill.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace dbl {
+
+struct SeqParams {
+    int B, T, H, K, V;
+    const void *q, *k, *v;
+    int64_t qs[4], ks[4], vs[4];
+    // gate_mode 0: channel-wise alpha/erase [B,T,H,K], write [B,T,H,V] (strides as/es/ws).
+    // gate_mode 1: scalar alpha [B,T,H] (as[0..2]) and beta = erase pointer (es[0..2]).
+    int gate_mode;
+    const float *alpha, *erase, *write;
+    int64_t as[4], es[4], ws[4];
+    float scale;
+    int mask_mode;  // 0 none, 1 valid/reset [B,T] f32, 2 doc_start/doc_end [B,T] int32
+    const float *valid, *reset;
+    const int32_t *doc_start, *doc_end;
+    int init_mode;  // 0 zeros, 1 initial pointer [B,H,K,V], 2 identity (transition matrices)
+    const float* initial;
+    int v_zero;     // 1: values are treated as zero (span transition)
+    void* out;      // optional
+    int out_dtype;  // DBL_F32 / DBL_BF16
+    int64_t os[4];
+    float* final_state;  // optional, [B,H,K,V]
+    float* scores;       // optional, [B,T,H]
+};
+
+// Validates the shape limits of the sequential kernel and launches it on `st`.
+int launch_seq_scan(const SeqParams& p, int in_dtype, cudaStream_t st);
+
+}  // namespace dbl

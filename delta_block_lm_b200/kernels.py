@@ -1,0 +1,270 @@
+"""Host mirror of the reference kernels crate's GDN-2 entry points, over torch CUDA tensors.
+
+Each function validates like the reference (same conditions, messages adapted), allocates its
+outputs like the reference's ops (which return fresh tensors, ``gdn_training.rs:391-393``), and
+calls the C ABI of ``libdbl_gdn2.so`` on the current CUDA stream.  torch is only the plumbing
+(device memory and streams); every kernel is this package's own CUDA code.
+
+    gdn_training_scan  <- delta_kernels::gdn_training_scan  (crates/kernels/src/gdn_training_ops.rs:288-333)
+    gdn2_scan          <- delta_kernels::gdn2_scan          (crates/kernels/src/ops.rs:251-276)
+    gdn2_prefill       <- scalar-gate chunked forward (the BASELINE prefill; chunk.rs:129-250 semantics)
+    gdn2_span_transition  hand-off matrix for time-sharded prefill (no reference counterpart)
+    gdn2_decode_step   <- the T = 1 continuation scan (crates/mixers/src/lib.rs:544-556), in place
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _native as N
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.float32:
+        return N.DBL_F32
+    if t.dtype == torch.bfloat16:
+        return N.DBL_BF16
+    raise ValueError(f"unsupported dtype {t.dtype}: expected float32 or bfloat16")
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(*tensors: Optional[torch.Tensor]) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("GDN-2 kernels require CUDA tensors; no CPU fallback")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError("GDN-2 inputs must share a device")
+    if dev is None:
+        raise ValueError("no tensor given")
+    return dev
+
+
+def _f32c(t: torch.Tensor) -> torch.Tensor:
+    return t.to(torch.float32).contiguous()
+
+
+@dataclass
+class GdnTrainingOutput:
+    """Mirror of delta_kernels::GdnTrainingOutput (gdn_training_ops.rs:276-282)."""
+
+    output: torch.Tensor        # [B,T,H,V] f32
+    final_state: torch.Tensor   # [B,H,K,V] f32
+    scores: torch.Tensor        # [B,T,H,1] f32: |k| |edit| after decay
+
+
+def gdn_training_scan(q, k, v, alpha, erase, write, valid, reset, initial, chunk_size: int
+                      ) -> GdnTrainingOutput:
+    """Fused GDN-2 forward with initial state, final state and physical scores.
+
+    Shapes as the reference: q,k,alpha,erase [B,T,H,K]; v,write [B,T,H,V]; valid,reset [B,T]
+    {0,1}; initial [B,H,K,V].  chunk_size 1..=16 (it bounds the reference's backward
+    checkpoints; this forward-only build validates it and otherwise ignores it).
+    """
+    dev = _require_cuda(q, k, v, alpha, erase, write, valid, reset, initial)
+    B, T, H, K = q.shape
+    V = v.shape[3]
+    if B == 0 or T == 0 or H == 0:
+        raise ValueError("GDN-2 requires nonempty axes")
+    for name, t, shape in (("k", k, (B, T, H, K)), ("v", v, (B, T, H, V)),
+                           ("alpha", alpha, (B, T, H, K)), ("erase", erase, (B, T, H, K)),
+                           ("write", write, (B, T, H, V)), ("valid", valid, (B, T)),
+                           ("reset", reset, (B, T)), ("initial", initial, (B, H, K, V))):
+        if tuple(t.shape) != shape:
+            raise ValueError(f"{name} must have shape {list(shape)}, got {list(t.shape)}")
+    if not 1 <= chunk_size <= 16:
+        raise ValueError("GDN-2 checkpoint chunk must be 1..=16")
+    dt = _dtype_code(q)
+    if k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("q, k and v must share a dtype")
+    with torch.cuda.device(dev):
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        alpha, erase, write = _f32c(alpha), _f32c(erase), _f32c(write)
+        valid, reset, initial = _f32c(valid), _f32c(reset), _f32c(initial)
+        output = torch.empty((B, T, H, V), device=dev, dtype=torch.float32)
+        final = torch.empty((B, H, K, V), device=dev, dtype=torch.float32)
+        scores = torch.empty((B, T, H, 1), device=dev, dtype=torch.float32)
+        a = N.TrainingScanArgs(B, T, H, K, V, dt, chunk_size, _ptr(q), _ptr(k), _ptr(v), _ptr(alpha),
+                               _ptr(erase), _ptr(write), _ptr(valid), _ptr(reset), _ptr(initial),
+                               _ptr(output), _ptr(final), _ptr(scores))
+        N.check(N.lib().dbl_gdn_training_scan(ctypes.byref(a), _stream(dev)))
+    return GdnTrainingOutput(output, final, scores)
+
+
+def gdn2_scan(q, k, v, alpha, erase, write, doc_start, doc_end) -> torch.Tensor:
+    """Output-only GDN-2 scan with inclusive document limits (ops.rs:251-276).
+
+    Gates are cast to f32 like the reference (``ops.rs:261-264``).  Output in the q dtype.
+    """
+    dev = _require_cuda(q, k, v, alpha, erase, write, doc_start, doc_end)
+    B, T, H, K = q.shape
+    V = v.shape[3]
+    if B == 0 or T == 0 or H == 0:
+        raise ValueError("GDN-2 requires nonempty axes")
+    for name, t, shape in (("k", k, (B, T, H, K)), ("v", v, (B, T, H, V)),
+                           ("alpha", alpha, (B, T, H, K)), ("erase", erase, (B, T, H, K)),
+                           ("write", write, (B, T, H, V)), ("doc_start", doc_start, (B, T)),
+                           ("doc_end", doc_end, (B, T))):
+        if tuple(t.shape) != shape:
+            raise ValueError(f"{name} must have shape {list(shape)}, got {list(t.shape)}")
+    dt = _dtype_code(q)
+    with torch.cuda.device(dev):
+        q, k, v = q.contiguous(), k.to(q.dtype).contiguous(), v.to(q.dtype).contiguous()
+        alpha, erase, write = _f32c(alpha), _f32c(erase), _f32c(write)
+        ds = doc_start.to(torch.int32).contiguous()
+        de = doc_end.to(torch.int32).contiguous()
+        out = torch.empty((B, T, H, V), device=dev, dtype=q.dtype)
+        a = N.Gdn2ScanArgs(B, T, H, K, V, dt, _ptr(q), _ptr(k), _ptr(v), _ptr(alpha), _ptr(erase),
+                           _ptr(write), _ptr(ds), _ptr(de), _ptr(out))
+        N.check(N.lib().dbl_gdn2_scan(ctypes.byref(a), _stream(dev)))
+    return out
+
+
+def _strides(t: torch.Tensor, n: int):
+    s = (ctypes.c_int64 * n)()
+    for i, x in enumerate(t.stride()):
+        s[i] = x
+    return s
+
+
+def _prefill_args(q, k, v, alpha, beta, scale, valid, reset, initial_state, out, final_state,
+                  chunk_size) -> N.PrefillArgs:
+    B, T, H, K = q.shape
+    V = v.shape[3] if v is not None else K
+    a = N.PrefillArgs()
+    a.batch, a.time, a.heads, a.key_dim, a.value_dim = B, T, H, K, V
+    a.dtype = _dtype_code(q)
+    a.chunk_size = chunk_size
+    a.scale = scale
+    a.q, a.k = _ptr(q), _ptr(k)
+    a.q_stride, a.k_stride = _strides(q, 4), _strides(k, 4)
+    if v is not None:
+        a.v, a.v_stride = _ptr(v), _strides(v, 4)
+    a.alpha, a.beta = _ptr(alpha), _ptr(beta)
+    a.alpha_stride, a.beta_stride = _strides(alpha, 3), _strides(beta, 3)
+    a.valid, a.reset = _ptr(valid), _ptr(reset)
+    a.initial_state = _ptr(initial_state)
+    if out is not None:
+        a.out, a.out_stride = _ptr(out), _strides(out, 4)
+    a.final_state = _ptr(final_state)
+    return a
+
+
+def _check_prefill_inputs(q, k, v, alpha, beta, valid, reset):
+    B, T, H, K = q.shape
+    if B == 0 or T == 0 or H == 0:
+        raise ValueError("GDN-2 requires nonempty axes")
+    if tuple(k.shape) != (B, T, H, K):
+        raise ValueError(f"k must have shape {[B, T, H, K]}, got {list(k.shape)}")
+    if v is not None and tuple(v.shape[:3]) != (B, T, H):
+        raise ValueError(f"v must have shape [B,T,H,V] with B,T,H = {B},{T},{H}")
+    for name, t in (("alpha", alpha), ("beta", beta)):
+        if tuple(t.shape) != (B, T, H):
+            raise ValueError(f"{name} must have shape {[B, T, H]}, got {list(t.shape)}")
+        if t.dtype != torch.float32:
+            raise ValueError(f"{name} must be float32 (recurrence gates never use low precision)")
+    if (valid is None) != (reset is None):
+        raise ValueError("valid and reset must be given together")
+    for name, t in (("k", k), ("v", v)):
+        if t is not None and t.dtype != q.dtype:
+            raise ValueError(f"{name} must have the dtype of q")
+
+
+def gdn2_prefill(q, k, v, alpha, beta, *, scale: Optional[float] = None, valid=None, reset=None,
+                 initial_state=None, out=None, final_state=None, chunk_size: int = 64,
+                 want_output: bool = True):
+    """Chunked GDN-2 prefill with scalar gates (1, 4).
+
+    S_t = alpha_t S_{t-1} (I - beta_t k k^T) + beta_t v k^T and o_t = S_t (scale q_t), in the
+    reference's key-major state layout.  q,k [B,T,H,K]; v [B,T,H,V] (f32 or bf16; strided views
+    with unit inner stride are taken as they are); alpha, beta [B,T,H] f32; valid/reset [B,T];
+    initial_state [B,H,K,V] f32.  Returns (out [B,T,H,V] in the q dtype or None, final_state
+    [B,H,K,V] f32).  ``final_state`` may be the initial state tensor (in-place update).
+    """
+    dev = _require_cuda(q, k, v, alpha, beta, valid, reset, initial_state, out, final_state)
+    _check_prefill_inputs(q, k, v, alpha, beta, valid, reset)
+    B, T, H, K = q.shape
+    V = v.shape[3]
+    if scale is None:
+        scale = 1.0 / math.sqrt(K)
+    with torch.cuda.device(dev):
+        if valid is not None:
+            valid, reset = _f32c(valid), _f32c(reset)
+        if initial_state is not None:
+            initial_state = _f32c(initial_state)
+        if out is None and want_output:
+            out = torch.empty((B, T, H, V), device=dev, dtype=q.dtype)
+        if final_state is None:
+            final_state = torch.empty((B, H, K, V), device=dev, dtype=torch.float32)
+        a = _prefill_args(q, k, v, alpha, beta, scale, valid, reset, initial_state, out,
+                          final_state, chunk_size)
+        N.check(N.lib().dbl_gdn2_prefill(ctypes.byref(a), _stream(dev)))
+    return out, final_state
+
+
+def gdn2_span_transition(k, alpha, beta, *, valid=None, reset=None, transition=None,
+                         chunk_size: int = 64) -> torch.Tensor:
+    """Per-(b,h) K x K matrix A of the span: S_end = A S_start + (scan of the span from zero).
+
+    The hand-off object of time-sharded prefill.  k [B,T,H,K]; gates [B,T,H] f32.
+    """
+    dev = _require_cuda(k, alpha, beta, valid, reset, transition)
+    _check_prefill_inputs(k, k, None, alpha, beta, valid, reset)
+    B, T, H, K = k.shape
+    with torch.cuda.device(dev):
+        if valid is not None:
+            valid, reset = _f32c(valid), _f32c(reset)
+        if transition is None:
+            transition = torch.empty((B, H, K, K), device=dev, dtype=torch.float32)
+        a = _prefill_args(k, k, None, alpha, beta, 1.0, valid, reset, None, None, None, chunk_size)
+        N.check(N.lib().dbl_gdn2_span_transition(ctypes.byref(a), _ptr(transition), _stream(dev)))
+    return transition
+
+
+def gdn2_decode_step(q, k, v, alpha, beta, state, *, scale: Optional[float] = None, out=None):
+    """One recurrent step for N sequences; ``state`` [N,H,K,V] f32 is updated IN PLACE.
+
+    q,k [N,H,K]; v [N,H,V] (f32 or bf16); alpha, beta [N,H] f32.  Returns out [N,H,V].
+    """
+    dev = _require_cuda(q, k, v, alpha, beta, state, out)
+    Nn, H, K = q.shape
+    V = v.shape[2]
+    if tuple(k.shape) != (Nn, H, K) or tuple(v.shape[:2]) != (Nn, H):
+        raise ValueError("decode: q,k must be [N,H,K] and v [N,H,V]")
+    if tuple(state.shape) != (Nn, H, K, V) or state.dtype != torch.float32 or not state.is_contiguous():
+        raise ValueError("decode: state must be a contiguous float32 [N,H,K,V] tensor")
+    for name, t in (("alpha", alpha), ("beta", beta)):
+        if tuple(t.shape) != (Nn, H) or t.dtype != torch.float32:
+            raise ValueError(f"decode: {name} must be float32 [N,H]")
+    if scale is None:
+        scale = 1.0 / math.sqrt(K)
+    with torch.cuda.device(dev):
+        alpha, beta = alpha.contiguous(), beta.contiguous()
+        if out is None:
+            out = torch.empty((Nn, H, V), device=dev, dtype=q.dtype)
+        a = N.DecodeArgs()
+        a.batch, a.heads, a.key_dim, a.value_dim = Nn, H, K, V
+        a.dtype = _dtype_code(q)
+        a.scale = scale
+        a.q, a.k, a.v = _ptr(q), _ptr(k), _ptr(v)
+        a.q_stride, a.k_stride, a.v_stride = _strides(q, 3), _strides(k, 3), _strides(v, 3)
+        a.alpha, a.beta = _ptr(alpha), _ptr(beta)
+        a.state = _ptr(state)
+        a.out, a.out_stride = _ptr(out), _strides(out, 3)
+        N.check(N.lib().dbl_gdn2_decode_step(ctypes.byref(a), _stream(dev)))
+    return out

@@ -1,0 +1,197 @@
+/*
+ * dbl_gdn2.h -- C ABI of the B200 (sm_100a) GDN-2 hot path.
+ *
+ * GDN-2 is the gated delta rule.  Per (batch row b, head h) the key-major state S [K,V] evolves,
+ * for every valid token t (crates/mixers/src/reference.rs:57-111):
+ *     if reset[t]:  S = 0
+ *     S      = diag(alpha_t) S
+ *     edit_j = write_j v_j - sum_i erase_i k_i S_ij
+ *     S     += k edit^T
+ *     o_j    = sum_i q_i S_ij            (padding: o = 0, S unchanged)
+ * The scalar-gate form used by the prefill / decode entry points sets alpha[i] = alpha_t,
+ * erase[i] = write[j] = beta_t and pre-scales q by `scale` (1/sqrt(K) in the reference model).
+ *
+ * Conventions shared by every entry point:
+ *   - All pointers are DEVICE pointers on the current CUDA device, owned by the caller.
+ *     No entry point allocates device memory except where a function says so.
+ *   - Strides are in ELEMENTS.  A stride array of all zeros means "contiguous".
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Calls are asynchronous and
+ *     return after enqueueing; errors in arguments are reported before anything is enqueued.
+ *   - Every function returns a dbl_status; it never aborts the process.  A human-readable
+ *     reason for the last failure on the calling thread is returned by dbl_last_error().
+ *   - Layout: inputs [B,T,H,C] (C = channel), states [B,H,K,V] f32 key-major, as the
+ *     reference's tensors (crates/mixers/src/chunk.rs:126).
+ */
+#ifndef DBL_GDN2_H
+#define DBL_GDN2_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *dbl_stream_t; /* == cudaStream_t */
+
+typedef enum {
+    DBL_OK = 0,
+    DBL_ERR_INVALID_ARGUMENT = 1, /* bad shape, null required pointer, bad stride or alignment */
+    DBL_ERR_UNSUPPORTED = 2,      /* valid request outside what the kernels implement         */
+    DBL_ERR_CUDA = 3,             /* a CUDA runtime/driver call failed                         */
+    DBL_ERR_WORKSPACE = 4,        /* workspace missing or smaller than *_workspace_bytes()     */
+    DBL_ERR_TIMEOUT = 5           /* a bounded wait gave up (multi-GPU hand-off)               */
+} dbl_status;
+
+typedef enum { DBL_F32 = 0, DBL_BF16 = 1 } dbl_dtype;
+
+/* Human-readable name of a status code (static storage). */
+const char *dbl_status_string(int status);
+/* Reason for the last non-OK status returned on this thread (thread-local, static storage). */
+const char *dbl_last_error(void);
+/* ABI version: major * 10000 + minor * 100 + patch. */
+int dbl_abi_version(void);
+
+/* =============================================================================================
+ * 1. Chunked prefill scan, scalar gates (the BASELINE prefill: configs 0, 1 and 4).
+ *
+ * Replaces, for scalar gates, the forward of delta_kernels::gdn_training_scan
+ * (crates/kernels/src/gdn_training_ops.rs:288-333) as reached from
+ * chunk::scan_selected(ScanBackend::FusedGdn2, ...) (crates/mixers/src/chunk.rs:40-67), and the
+ * CPU tensor solver chunk::scan (chunk.rs:129-250) it must agree with.  Unlike the reference
+ * (chunk <= 16, K32/V64, f32 only) this runs chunk 64 at K,V in {64,128}, f32 or bf16 inputs,
+ * f32 gates, f32 state.  bf16 inputs at K = V = 128 run on the tcgen05 tensor-core kernel.
+ * ========================================================================================== */
+typedef struct {
+    int64_t batch, time, heads, key_dim, value_dim; /* B, T, H, K, V                         */
+    int32_t dtype;            /* dbl_dtype of q, k, v and out                                 */
+    int32_t chunk_size;       /* 0 or 64                                                      */
+    float scale;              /* q multiplier (1/sqrt(K) in the reference model)              */
+    const void *q;            /* [B,T,H,K]                                                    */
+    const void *k;            /* [B,T,H,K]                                                    */
+    const void *v;            /* [B,T,H,V]                                                    */
+    int64_t q_stride[4], k_stride[4], v_stride[4]; /* innermost stride must be 1            */
+    const float *alpha;       /* [B,T,H] decay in (0,1]; 0 behaves as a reset                 */
+    const float *beta;        /* [B,T,H] erase = write strength                               */
+    int64_t alpha_stride[3], beta_stride[3];
+    const float *valid;       /* optional [B,T] contiguous, nonzero = token present           */
+    const float *reset;       /* optional [B,T] contiguous, nonzero = zero state first        */
+    const float *initial_state; /* optional [B,H,K,V] contiguous f32 (NULL = zeros)           */
+    void *out;                /* optional [B,T,H,V] (dtype); NULL skips the output            */
+    int64_t out_stride[4];
+    float *final_state;       /* optional [B,H,K,V] contiguous f32; may equal initial_state   */
+} dbl_prefill_args;
+
+int dbl_gdn2_prefill(const dbl_prefill_args *args, dbl_stream_t stream);
+
+/* Span transition for time sharding (config 4).  For the token span described by `args`
+ * (q, v, out, initial_state and final_state are ignored) writes, per (b,h), the K x K matrix
+ * A with  S_end = A S_start + B_span  (B_span = dbl_gdn2_prefill from a zero state).
+ * transition: [B,H,K,K] contiguous f32.  No counterpart in the reference, which has no time
+ * sharding; it is the hand-off object of the long-context prefill. */
+int dbl_gdn2_span_transition(const dbl_prefill_args *args, float *transition,
+                             dbl_stream_t stream);
+
+/* =============================================================================================
+ * 2. Single-token recurrent decode step, state updated IN PLACE (config 2).
+ *
+ * Replaces the reference decode, which is chunk::scan_selected with T = 1 and `initial` set
+ * (crates/mixers/src/lib.rs:544-556 -> gdn_training_scan, out of place) and the one-step oracle
+ * gdn2_reference::step (crates/mixers/src/gdn2_reference.rs:52-83).  K, V in {64, 128}.
+ * ========================================================================================== */
+typedef struct {
+    int64_t batch, heads, key_dim, value_dim; /* N sequences, H, K, V                          */
+    int32_t dtype;            /* dtype of q, k, v, out                                         */
+    float scale;              /* q multiplier                                                  */
+    const void *q, *k;        /* [N,H,K]                                                       */
+    const void *v;            /* [N,H,V]                                                       */
+    int64_t q_stride[3], k_stride[3], v_stride[3];
+    const float *alpha, *beta; /* [N,H] contiguous                                             */
+    float *state;             /* [N,H,K,V] contiguous f32, read and written in place          */
+    void *out;                /* [N,H,V] (dtype)                                               */
+    int64_t out_stride[3];
+} dbl_decode_args;
+
+int dbl_gdn2_decode_step(const dbl_decode_args *args, dbl_stream_t stream);
+
+/* =============================================================================================
+ * 3. Reference contract, channel-wise gates: the stateful fused scan.
+ *
+ * Mirrors delta_kernels::gdn_training_scan(q, k, v, alpha, erase, write, valid, reset, initial,
+ * chunk_size) -> GdnTrainingOutput { output, final_state, scores }
+ * (crates/kernels/src/gdn_training_ops.rs:288-333; kernel gdn_training.rs:12-115).
+ * Shapes: q,k,alpha,erase [B,T,H,K]; v,write [B,T,H,V]; valid,reset [B,T] f32 {0,1};
+ * initial [B,H,K,V].  chunk_size must be 1..=16 as in the reference (gdn_training.rs:370-373);
+ * it only bounds the reference's backward checkpoints, which this forward-only build does not
+ * produce.  Generalised to K <= 128, V <= 256 and bf16 q/k/v (the reference: K32/V64 f32).
+ * Outputs f32: output [B,T,H,V], final_state [B,H,K,V], scores [B,T,H] = |k| |edit|.
+ * All arrays contiguous.  initial may be NULL (zeros); scores may be NULL.
+ * ========================================================================================== */
+typedef struct {
+    int64_t batch, time, heads, key_dim, value_dim;
+    int32_t dtype;            /* dtype of q, k, v (gates and masks are always f32)            */
+    int32_t chunk_size;
+    const void *q, *k, *v;
+    const float *alpha, *erase, *write;
+    const float *valid, *reset;     /* required, [B,T]                                       */
+    const float *initial_state;     /* optional                                              */
+    float *output;                  /* required                                              */
+    float *final_state;             /* optional                                              */
+    float *scores;                  /* optional                                              */
+} dbl_training_scan_args;
+
+int dbl_gdn_training_scan(const dbl_training_scan_args *args, dbl_stream_t stream);
+
+/* Mirrors delta_kernels::gdn2_scan(q, k, v, alpha, erase, write, doc_start, doc_end) -> output
+ * (crates/kernels/src/ops.rs:251-276, kernels gdn2.rs:23-283; oracle gdn2_reference.rs:87-105):
+ * inclusive int32 document limits [B,T]; `end < start` marks padding (output 0, state kept),
+ * `start == t` resets.  Zero initial state.  Output [B,T,H,V] in the q dtype.  Contiguous. */
+typedef struct {
+    int64_t batch, time, heads, key_dim, value_dim;
+    int32_t dtype;
+    const void *q, *k, *v;
+    const float *alpha, *erase, *write;
+    const int32_t *doc_start, *doc_end;
+    void *output;
+} dbl_gdn2_scan_args;
+
+int dbl_gdn2_scan(const dbl_gdn2_scan_args *args, dbl_stream_t stream);
+
+/* =============================================================================================
+ * 4. Relay attention, decode case (config 3): one query per (sequence, head) attends to a
+ * shared prefix KV (stored once, read once per head for all sequences) and to the sequence's
+ * own KV; the two softmax parts are merged by log-sum-exp inside one kernel.
+ *
+ * Replaces, for the split prefix/own layout, the forward of
+ * RelayAttentionKernelOps::relay_attention_forward (reuse/crates/dre-attention/src/
+ * relay_attention_kernel.rs:14-20, kernel :38-130, host run_relay_windowed_attention :311-340):
+ * same online-softmax arithmetic, same [max, sum] statistics and the same empty-row convention
+ * (o = 0, max = 0, sum = 1).  head_dim 128 (64 supported too), bf16 or f32.
+ * Layouts (contiguous): q [N,H,D]; prefix_k, prefix_v [H,Lp,D]; own_k, own_v [N,H,Lo,D];
+ * own_len optional int32 [N] (0..Lo, ragged own segments); out [N,H,D] (dtype);
+ * row_max, row_sum optional f32 [N,H].
+ * The kernel needs scratch for the split partials: pass a device buffer of at least
+ * dbl_relay_merge_workspace_bytes(...) bytes (16-byte aligned).  It is reusable across calls on
+ * the same stream; calls that overlap on the GPU must use distinct workspaces.
+ * ========================================================================================== */
+typedef struct {
+    int64_t n_seq, heads, head_dim, prefix_len, own_cap;
+    int32_t dtype;
+    float scale;                      /* softmax scale (1/sqrt(D))                            */
+    const void *q;
+    const void *prefix_k, *prefix_v;
+    const void *own_k, *own_v;
+    const int32_t *own_len;           /* optional                                             */
+    void *out;
+    float *row_max, *row_sum;         /* optional                                             */
+} dbl_relay_merge_args;
+
+size_t dbl_relay_merge_workspace_bytes(int64_t n_seq, int64_t heads, int64_t head_dim,
+                                       int64_t prefix_len, int64_t own_cap);
+int dbl_relay_merge_decode(const dbl_relay_merge_args *args, void *workspace,
+                           size_t workspace_bytes, dbl_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DBL_GDN2_H */

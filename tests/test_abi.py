@@ -1,0 +1,101 @@
+"""CPU tests of the C ABI boundary: the library loads, exports every function the header declares,
+its structures match the ctypes mirror byte for byte, and argument errors come back as status
+codes (no CUDA call is made before validation, so these run without a GPU)."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from delta_block_lm_b200 import _native as N
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "dbl_gdn2.h")
+
+STRUCTS = {
+    "dbl_prefill_args": N.PrefillArgs,
+    "dbl_decode_args": N.DecodeArgs,
+    "dbl_training_scan_args": N.TrainingScanArgs,
+    "dbl_gdn2_scan_args": N.Gdn2ScanArgs,
+    "dbl_relay_merge_args": N.RelayMergeArgs,
+}
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[a-z_]+\s*\*?\s*(dbl_[a-z0-9_]+)\s*\(", text, re.M)))
+
+
+def test_every_declared_function_is_exported(native_lib):
+    names = declared_functions()
+    assert len(names) >= 10
+    for name in names:
+        assert hasattr(native_lib, name), name
+    assert {n for n, _, _ in N.EXPORTS} == set(names)
+
+
+def test_struct_layout_matches_header(tmp_path):
+    lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void) {"]
+    for cname, py in STRUCTS.items():
+        lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')
+        for field, _ in py._fields_:
+            lines.append(f'printf("{cname} {field} %zu\\n", offsetof({cname}, {field}));')
+    lines.append("return 0; }")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.check_call(["gcc", "-std=c11", "-o", str(exe), str(src)])
+    out = subprocess.check_output([str(exe)], text=True).split("\n")
+    got = {}
+    for line in out:
+        if line:
+            s, f, v = line.split()
+            got[(s, f)] = int(v)
+    for cname, py in STRUCTS.items():
+        assert got[(cname, "size")] == ctypes.sizeof(py), cname
+        for field, _ in py._fields_:
+            assert got[(cname, field)] == getattr(py, field).offset, (cname, field)
+
+
+def test_status_strings_and_version(native_lib):
+    assert native_lib.dbl_status_string(0) == b"ok"
+    assert native_lib.dbl_status_string(N.DBL_ERR_WORKSPACE).startswith(b"workspace")
+    assert native_lib.dbl_status_string(99) == b"unknown status"
+    assert native_lib.dbl_abi_version() >= 10000
+
+
+def test_null_and_bad_arguments_return_status(native_lib):
+    assert native_lib.dbl_gdn2_prefill(None, None) == N.DBL_ERR_INVALID_ARGUMENT
+    assert b"null" in native_lib.dbl_last_error()
+    a = N.PrefillArgs()
+    a.batch, a.time, a.heads, a.key_dim, a.value_dim = 1, 0, 1, 64, 64
+    assert native_lib.dbl_gdn2_prefill(ctypes.byref(a), None) == N.DBL_ERR_INVALID_ARGUMENT
+    assert b"nonempty" in native_lib.dbl_last_error()
+    a.time, a.chunk_size = 4, 16
+    assert native_lib.dbl_gdn2_prefill(ctypes.byref(a), None) == N.DBL_ERR_UNSUPPORTED
+    t = N.TrainingScanArgs(1, 4, 1, 32, 64, N.DBL_F32, 17)
+    assert native_lib.dbl_gdn_training_scan(ctypes.byref(t), None) == N.DBL_ERR_INVALID_ARGUMENT
+    assert b"1..=16" in native_lib.dbl_last_error()
+    d = N.DecodeArgs()
+    d.batch, d.heads, d.key_dim, d.value_dim = 1, 1, 96, 128
+    assert native_lib.dbl_gdn2_decode_step(ctypes.byref(d), None) == N.DBL_ERR_UNSUPPORTED
+    r = N.RelayMergeArgs(1, 1, 100, 4, 4, N.DBL_BF16, 0.1)
+    assert native_lib.dbl_relay_merge_decode(ctypes.byref(r), None, 0, None) == N.DBL_ERR_UNSUPPORTED
+
+
+def test_relay_workspace_size_and_check(native_lib):
+    need = native_lib.dbl_relay_merge_workspace_bytes(64, 16, 128, 4096, 1024)
+    # 64 * 16 rows x (2 * 64 prefix + 4 own partials) x (128 + 2) floats + counters
+    assert need >= 64 * 16 * 132 * 130 * 4
+    assert native_lib.dbl_relay_merge_workspace_bytes(0, 16, 128, 4096, 1024) == 0
+    r = N.RelayMergeArgs(64, 16, 128, 4096, 1024, N.DBL_BF16, 0.088, 256, 256, 256, 256, 256, None, 256)
+    assert native_lib.dbl_relay_merge_decode(ctypes.byref(r), None, need, None) == N.DBL_ERR_WORKSPACE
+    assert native_lib.dbl_relay_merge_decode(ctypes.byref(r), 256, need - 1, None) == N.DBL_ERR_WORKSPACE
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(N, "LIB_PATH", str(tmp_path / "absent.so"))
+    monkeypatch.setattr(N, "_lib", None)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        N.lib()

@@ -1,0 +1,228 @@
+"""GPU parity: every kernel against the CPU oracle on the same seeded inputs.
+
+Tolerances: f32 paths at the reference's 2e-5 + 3e-4|ref| (checks.rs:73-74) where the reference
+checks f32 against f64, and the north-star bounds elsewhere (``rel_err``: 2e-3 for f32, 2e-2 for
+bf16 inputs; inputs are rounded to bf16 before the oracle runs, so only kernel rounding counts).
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import delta_block_lm_b200 as dbl
+from fixtures import (TOL_BF16, TOL_F32, baseline_inputs, bf16_round, chunk_test_fixture, edge_edits,
+                      edge_initial, ref_close, rel_err, sinusoid_fixture, splitmix_tokens)
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "gdn2_golden.npz")
+
+
+def dev_t(x, device, dtype=torch.float32):
+    return torch.as_tensor(np.ascontiguousarray(x), dtype=torch.float32).to(device=device, dtype=dtype)
+
+
+def host(t):
+    return t.detach().float().cpu().numpy()
+
+
+# ----------------------------------------------------------------------- reference contract
+@pytest.mark.parametrize("t", [1, 7, 35])
+def test_training_scan_matches_golden_edge_fixture(cuda, native_lib, t):
+    fields, valid, reset = sinusoid_fixture(t)
+    fields, valid, reset = edge_edits(fields, valid, reset)
+    init = edge_initial()
+    g = np.load(GOLDEN)
+    args = [dev_t(x, cuda) for x in fields] + [dev_t(valid, cuda), dev_t(reset, cuda), dev_t(init, cuda)]
+    r = dbl.gdn_training_scan(*args, chunk_size=16)
+    torch.cuda.synchronize()
+    for got, name in ((r.output, "out"), (r.final_state, "final"), (r.scores[..., 0], "scores")):
+        ok, err = ref_close(host(got), g[f"edge_t{t}_{name}"])
+        assert ok, (name, err)
+
+
+def test_training_scan_chunk_fixture_and_padding_zero(cuda, native_lib):
+    fields, valid, reset, initial = chunk_test_fixture()
+    g = np.load(GOLDEN)
+    r = dbl.gdn_training_scan(*[dev_t(x, cuda) for x in fields], dev_t(valid, cuda), dev_t(reset, cuda),
+                              dev_t(initial, cuda), 1)
+    out = host(r.output)
+    ok, err = ref_close(out, g["chunk_out"])
+    assert ok, err
+    assert np.all(out[~valid] == 0.0)
+    ok, err = ref_close(host(r.final_state), g["chunk_final"])
+    assert ok, err
+
+
+def test_training_scan_bf16_inputs(cuda, native_lib):
+    f = splitmix_tokens(77, 2, 40, 3, 32, 64)
+    q, k, v = (bf16_round(x.astype(np.float32)) for x in f[:3])
+    valid = np.ones((2, 40), bool)
+    valid[1, 30:] = False
+    reset = np.zeros((2, 40), bool)
+    reset[0, 17] = True
+    init = np.zeros((2, 3, 32, 64), np.float32)
+    out, fin, sco = O.scan(q, k, v, *f[3:], valid, reset, init)
+    r = dbl.gdn_training_scan(dev_t(q, cuda, torch.bfloat16), dev_t(k, cuda, torch.bfloat16),
+                              dev_t(v, cuda, torch.bfloat16), *[dev_t(x, cuda) for x in f[3:]],
+                              dev_t(valid, cuda), dev_t(reset, cuda), dev_t(init, cuda), 16)
+    assert rel_err(host(r.output), out) < TOL_F32
+    assert rel_err(host(r.final_state), fin) < TOL_F32
+    assert rel_err(host(r.scores[..., 0]), sco) < TOL_F32
+
+
+def test_gdn2_scan_doc_limits(cuda, native_lib):
+    g = np.load(GOLDEN)
+    f = splitmix_tokens(2024, 1, 33, 2, 32, 64)
+    starts = np.array([[0] * 20 + [20] * 10 + [30, 31, 32]], np.int32)
+    ends = np.array([[19] * 20 + [29] * 10 + [29, 32, 32]], np.int32)
+    out = dbl.gdn2_scan(*[dev_t(x, cuda) for x in f], torch.as_tensor(starts, device=cuda),
+                        torch.as_tensor(ends, device=cuda))
+    got = host(out)
+    ok, err = ref_close(got, g["doc_out"])
+    assert ok, err
+    assert np.all(got[0, 30] == 0.0)
+
+
+# ----------------------------------------------------------------------- scalar-gate prefill
+def _prefill_case(cuda, seed, B, T, H, Dk, Dv, dtype, initial=False, masks=False):
+    q, k, v, alpha, beta = baseline_inputs(seed, B, T, H, Dk, Dv)
+    if dtype == torch.bfloat16:
+        q, k, v = bf16_round(q), bf16_round(k), bf16_round(v)
+    rng = np.random.default_rng(seed + 100)
+    init = (0.02 * rng.standard_normal((B, H, Dk, Dv))).astype(np.float32) if initial else None
+    valid = reset = None
+    if masks:
+        valid = rng.random((B, T)) > 0.1
+        reset = rng.random((B, T)) > 0.97
+    ref_out, ref_fin, _ = O.scan_scalar(q, k, v, alpha, beta, valid, reset, init)
+    out, fin = dbl.gdn2_prefill(dev_t(q, cuda, dtype), dev_t(k, cuda, dtype), dev_t(v, cuda, dtype),
+                                dev_t(alpha, cuda), dev_t(beta, cuda),
+                                valid=None if valid is None else dev_t(valid, cuda),
+                                reset=None if reset is None else dev_t(reset, cuda),
+                                initial_state=None if init is None else dev_t(init, cuda))
+    return host(out), host(fin), ref_out, ref_fin
+
+
+def test_prefill_config0_f32(cuda, native_lib):
+    # BASELINE config 0 at full size: B2 H4 T512 d64 f32.
+    out, fin, ro, rf = _prefill_case(cuda, 0, 2, 512, 4, 64, 64, torch.float32)
+    assert rel_err(out, ro) < TOL_F32
+    assert rel_err(fin, rf) < TOL_F32
+
+
+@pytest.mark.parametrize("masks,initial", [(False, False), (True, True)])
+def test_prefill_bf16_d128(cuda, native_lib, masks, initial):
+    out, fin, ro, rf = _prefill_case(cuda, 1, 2, 200, 3, 128, 128, torch.bfloat16, initial, masks)
+    assert rel_err(out, ro) < TOL_BF16
+    assert rel_err(fin, rf) < TOL_BF16
+
+
+def test_span_transition_composes(cuda, native_lib):
+    # S_end = A S0 + B, with B the scan from zero: checked against the scan from S0.
+    B, T, H, D = 1, 130, 2, 64
+    q, k, v, alpha, beta = baseline_inputs(5, B, T, H, D, D)
+    rng = np.random.default_rng(6)
+    S0 = rng.standard_normal((B, H, D, D)).astype(np.float32) * 0.1
+    _, ref_fin, _ = O.scan_scalar(q, k, v, alpha, beta, initial=S0)
+    A = host(dbl.gdn2_span_transition(dev_t(k, cuda), dev_t(alpha, cuda), dev_t(beta, cuda)))
+    _, Bs = dbl.gdn2_prefill(dev_t(q, cuda), dev_t(k, cuda), dev_t(v, cuda), dev_t(alpha, cuda),
+                             dev_t(beta, cuda), want_output=False)
+    comp = np.einsum("bhik,bhkj->bhij", A, S0) + host(Bs)
+    assert rel_err(comp, ref_fin) < TOL_F32
+
+
+# ----------------------------------------------------------------------- decode step
+@pytest.mark.parametrize("dtype,Dk,Dv", [(torch.bfloat16, 128, 128), (torch.float32, 128, 128),
+                                         (torch.bfloat16, 64, 128), (torch.float32, 64, 64)])
+def test_decode_step_64_steps(cuda, native_lib, dtype, Dk, Dv):
+    Nn, H, steps = 8, 4, 64
+    rng = np.random.default_rng(12)
+    S = (0.02 * rng.standard_normal((Nn, H, Dk, Dv))).astype(np.float32)
+    state = dev_t(S, cuda)
+    Sref = S.reshape(Nn * H, Dk, Dv).astype(np.float64)
+    scale = 1.0 / np.sqrt(Dk)
+    worst = 0.0
+    for s in range(steps):
+        q, k, v, alpha, beta = baseline_inputs(1000 + s, Nn, 1, H, Dk, Dv)
+        q, k, v, alpha, beta = q[:, 0], k[:, 0], v[:, 0], alpha[:, 0], beta[:, 0]
+        if dtype == torch.bfloat16:
+            q, k, v = bf16_round(q), bf16_round(k), bf16_round(v)
+        out = dbl.gdn2_decode_step(dev_t(q, cuda, dtype), dev_t(k, cuda, dtype), dev_t(v, cuda, dtype),
+                                   dev_t(alpha, cuda), dev_t(beta, cuda), state)
+        a = np.broadcast_to(alpha.reshape(-1, 1), (Nn * H, Dk))
+        e = np.broadcast_to(beta.reshape(-1, 1), (Nn * H, Dk))
+        w = np.broadcast_to(beta.reshape(-1, 1), (Nn * H, Dv))
+        ro, Sref = O.step(q.reshape(-1, Dk) * scale, k.reshape(-1, Dk), v.reshape(-1, Dv), a, e, w, Sref)
+        worst = max(worst, rel_err(host(out).reshape(-1, Dv), ro))
+    tol = TOL_BF16 if dtype == torch.bfloat16 else TOL_F32
+    assert worst < tol
+    assert rel_err(host(state).reshape(-1, Dk, Dv), Sref) < tol
+
+
+# ----------------------------------------------------------------------- relay merge
+def _relay_case(cuda, dtype, N_, H, D, Lp, Lo, own_len=None, seed=0):
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((N_, H, D)).astype(np.float32)
+    kp, vp = (rng.standard_normal((H, Lp, D)).astype(np.float32) for _ in range(2))
+    ko, vo = (rng.standard_normal((N_, H, Lo, D)).astype(np.float32) for _ in range(2))
+    if dtype == torch.bfloat16:
+        q, kp, vp, ko, vo = (bf16_round(x) for x in (q, kp, vp, ko, vo))
+    scale = 1.0 / np.sqrt(D)
+    ro, rm, rs = O.relay_merge(q, kp, vp, ko, vo, scale, own_len)
+    ol = None if own_len is None else torch.as_tensor(own_len, device=cuda)
+    o, m, s = dbl.relay_merge_decode(dev_t(q, cuda, dtype), dev_t(kp, cuda, dtype), dev_t(vp, cuda, dtype),
+                                     dev_t(ko, cuda, dtype), dev_t(vo, cuda, dtype), own_len=ol)
+    return (host(o), host(m), host(s)), (ro, rm, rs)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("D", [128, 64])
+def test_relay_merge_matches_oracle(cuda, native_lib, dtype, D):
+    got, ref = _relay_case(cuda, dtype, 8, 4, D, 700, 300, seed=D)
+    tol = TOL_BF16 if dtype == torch.bfloat16 else TOL_F32
+    assert rel_err(got[0], ref[0]) < tol
+    # the statistics: max is a plain score, sum = sum exp(score - max)
+    assert rel_err(got[1], ref[1]) < tol and rel_err(got[2], ref[2]) < tol
+
+
+def test_relay_merge_ragged_and_empty(cuda, native_lib):
+    own = np.array([0, 1, 255, 256, 257, 1000, 3, 0], np.int32)
+    got, ref = _relay_case(cuda, torch.bfloat16, 8, 2, 128, 64, 1000, own_len=own, seed=3)
+    assert rel_err(got[0], ref[0]) < TOL_BF16
+    # no prefix and no own keys: o = 0, [0, 1]
+    got, ref = _relay_case(cuda, torch.bfloat16, 3, 2, 128, 0, 16, own_len=np.array([0, 4, 0], np.int32))
+    assert np.all(got[0][0] == 0.0) and np.all(got[1][0] == 0.0) and np.all(got[2][0] == 1.0)
+    assert rel_err(got[0][1], ref[0][1]) < TOL_BF16
+
+
+def test_relay_merge_known_answers(cuda, native_lib):
+    # relay_tests.rs:12-90 restated for the split layout (see tests/test_oracle.py).
+    D = 64
+    for dtype in (torch.float32, torch.bfloat16):
+        q = torch.full((1, 1, D), 1e16, device=cuda, dtype=dtype)
+        ko = torch.full((1, 1, 1, D), -1e16, device=cuda, dtype=dtype)
+        vo = (torch.arange(D, device=cuda, dtype=torch.float32) - 32.0).reshape(1, 1, 1, D).to(dtype)
+        kp = torch.full((1, 16, D), -2e16, device=cuda, dtype=dtype)
+        vp = torch.full((1, 16, D), 23.0, device=cuda, dtype=dtype)
+        o, m, s = dbl.relay_merge_decode(q, kp, vp, ko, vo, scale=0.125)
+        assert torch.equal(o.float(), vo[0, 0].float())
+        assert s.item() == 1.0 and m.item() < -1e30
+        ko2 = torch.full((1, 1, 2, D), -1e16, device=cuda, dtype=dtype)
+        kp2 = torch.full((1, 16, D), -1e16, device=cuda, dtype=dtype)
+        o, m, s = dbl.relay_merge_decode(q, kp2, torch.zeros_like(kp2), ko2, torch.zeros_like(ko2), scale=0.125)
+        assert s.item() == 18.0 and torch.all(o == 0)
+
+
+def test_relay_workspace_is_reusable(cuda, native_lib):
+    rng = np.random.default_rng(1)
+    N_, H, D, Lp, Lo = 4, 2, 128, 128, 256
+    ws = torch.empty(dbl.relay_workspace_bytes(N_, H, D, Lp, Lo), device=cuda, dtype=torch.uint8)
+    for it in range(3):
+        q = torch.randn(N_, H, D, device=cuda, dtype=torch.bfloat16)
+        kp, vp = (torch.randn(H, Lp, D, device=cuda, dtype=torch.bfloat16) for _ in range(2))
+        ko, vo = (torch.randn(N_, H, Lo, D, device=cuda, dtype=torch.bfloat16) for _ in range(2))
+        o, _, _ = dbl.relay_merge_decode(q, kp, vp, ko, vo, workspace=ws)
+        ro, _, _ = O.relay_merge(host(q), host(kp), host(vp), host(ko), host(vo), 1.0 / np.sqrt(D))
+        assert rel_err(host(o), ro) < TOL_BF16
