@@ -88,6 +88,7 @@ EXPORTS = [
     ("dbl_status_string", ctypes.c_char_p, [ctypes.c_int]),
     ("dbl_last_error", ctypes.c_char_p, []),
     ("dbl_abi_version", ctypes.c_int, []),
+    ("dbl_device_error", ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
     ("dbl_gdn2_prefill", ctypes.c_int, [ctypes.POINTER(PrefillArgs), _vp]),
     ("dbl_gdn2_span_transition", ctypes.c_int, [ctypes.POINTER(PrefillArgs), _vp, _vp]),
     ("dbl_gdn2_decode_step", ctypes.c_int, [ctypes.POINTER(DecodeArgs), _vp]),

@@ -1,16 +1,674 @@
-// Chunked GDN-2 prefill on tcgen05 tensor cores (bf16, K = V = 128, chunk 64).
-// Selection hook used by prefill.cu; the kernel itself is added in this file.
+// Chunked GDN-2 prefill on tcgen05 tensor cores: bf16 q/k/v, K = V = 128, chunk C = 64,
+// f32 gates, f32 state (BASELINE configs 1 and 4).
+//
+// Algorithm (the chunkwise solver of crates/mixers/src/chunk.rs:129-250, with scalar gates and
+// the decay products formed in log space instead of the reference's direct products; chunk 64
+// instead of its <= 16 because the triangular system is solved by substitution, not by the
+// nilpotent series).  For a chunk with start state S (key-major, K x V) and rows r = 0..63:
+//   g_r = sum_{u<=r} log alpha_u, gamma_r = exp(g_r), Gamma[r][s] = exp(g_r - g_s) (s <= r);
+//   a zero alpha (a reset, or alpha = 0) zeroes every product that spans it.
+//   A  = strict_lower(beta_r Gamma[r][s] k_r.k_s)      T = (I + A)^-1
+//   R  = beta V - diag(beta gamma) K S                  Delta = T R        (the edits)
+//   O  = diag(gamma) (scale Q) S + (scale Gamma o Q K^T, s <= r) Delta
+//   S' = gamma_63 S + (diag(Gamma[63][r]) K)^T Delta
+// Padding tokens get beta = 0 and alpha = 1 (their edit is exactly zero) and output 0.
+//
+// B200 mapping.  One CTA per (b, h), 512 threads, one CTA per SM (all 512 TMEM columns).
+//   * prep warps 0-7: TMA loads of the chunk tiles (K and Q 128-byte swizzled, V plain), the gate
+//     scan, UMMA [K;Q] K^T -> TMEM, decay masks, the blocked 64x64 unit-lower inverse (16x16
+//     diagonal blocks by substitution, off-diagonal blocks level by level), T and P written as
+//     bf16 UMMA operands.  Prep runs one chunk ahead of the chain (two smem stages).
+//   * chain warps 8-15: the state-dependent chain, transposed so that the value column j of the
+//     state is TMEM lane j and every activation stays in TMEM (A operands of the TS form):
+//       MMA1  D1[j][n]  = sum_i S^T[j][i] [K;Q][n][i]      (A = S^T bf16 in TMEM)
+//       E1    R^T[j][r] = beta_r V[r][j] - beta_r gamma_r D1[j][r]   -> TMEM (bf16 hi + lo pair)
+//       MMA2  D2[j][r'] = sum_r R^T[j][r] T[r'][r]          (Delta^T; hi and lo accumulate)
+//       E2    Delta^T scaled by Gamma[63][r'] and plain                     -> TMEM (bf16)
+//       MMA3  D3[j][i]  = sum_r' (Gamma Delta)^T[j][r'] K[r'][i]   (B = K tile read MN-major)
+//       MMA2b DO[j][r]  = sum_r' Delta^T[j][r'] P[r][r']     (P as a bf16 hi + lo pair)
+//     R and P are carried as bf16 pairs because their rounding dominates the error budget: with
+//     single bf16 operands the output error reaches the 2e-2 bound at T = 4096, with the pairs it
+//     stays near 1e-2 (see tests/chunk_model.py).
+//       E3    S[i][j] = gamma_63 S + D3 (f32 master state in registers, 64 per thread),
+//             S^T -> TMEM bf16; O[r][j] = scale gamma_r D1[j][64+r] + DO[j][r] -> smem -> TMA store.
+// Roofline: HBM (intensity ~172 FLOP/B at the algorithmic minimum of 1032 B per token-head).
+#include <cuda.h>
+
 #include "common.cuh"
+#include "tc_ptx.cuh"
 
 namespace dbl {
 
-int tc_prefill_supported(const dbl_prefill_args*, const int64_t*, const int64_t*, const int64_t*, const int64_t*) {
-    return 0;
+__device__ int g_tc_error = 0;  // set by a bounded wait that gave up (code = site id)
+
+namespace {
+
+constexpr int C = 64;
+constexpr int DK = 128;
+constexpr int NTHREADS = 512;
+constexpr int NPREP = 256;
+constexpr int NCHAIN = 256;
+constexpr int BAR_PREP = 1, BAR_CHAIN = 2;
+
+// TMEM column map (512 columns, f32 accumulators unless noted)
+constexpr uint32_t TM_S = 0;     // S^T bf16 A operand: 64 cols (128 keys, 2 per column)
+constexpr uint32_t TM_D1 = 64;   // [0,64) K S (-> R^T bf16 in place), [64,128) Q S
+constexpr uint32_t TM_D2 = 192;  // Delta^T f32 (-> scaled / plain bf16 in place)
+constexpr uint32_t TM_D3 = 256;  // (Gamma Delta)^T K, 128 cols
+constexpr uint32_t TM_DO = 384;  // Delta^T P^T, 64 cols
+constexpr uint32_t TM_KK = 448;  // prep: [K;Q] K^T, 64 cols
+
+// Shared memory (offsets from a 1024-aligned base)
+constexpr uint32_t X_BYTES = 2 * 128 * 128;  // 2 key blocks x 128 rows ([K;Q]) x 128 B, swizzled
+constexpr uint32_t V_BYTES = C * 128 * 2;    // [64][128] bf16 plain
+constexpr uint32_t T_BYTES = C * 128;        // [64][64] bf16 swizzled
+constexpr uint32_t P_BYTES = 2 * C * 128;     // P as a bf16 pair: hi tile, then lo tile
+constexpr uint32_t G_BYTES = 2048;           // gates
+constexpr uint32_t STAGE_BYTES = X_BYTES + V_BYTES + T_BYTES + P_BYTES + G_BYTES;  // 75776
+constexpr uint32_t OFF_O = 2 * STAGE_BYTES;
+constexpr uint32_t O_BYTES = C * 128 * 2;
+constexpr uint32_t OFF_SA = OFF_O + O_BYTES;
+constexpr int LDA = 65;
+constexpr uint32_t OFF_ST = OFF_SA + C * LDA * 4;
+constexpr uint32_t OFF_SX = OFF_ST + C * LDA * 4;
+constexpr uint32_t OFF_SG = OFF_SX + 768 * 4;
+constexpr uint32_t OFF_SCNT = OFF_SG + 64 * 4;
+constexpr uint32_t OFF_SWT = OFF_SCNT + 64 * 4;
+constexpr uint32_t OFF_BAR = (OFF_SWT + 64 + 7) / 8 * 8;
+constexpr uint32_t NBARS = 11;
+constexpr uint32_t OFF_TSLOT = OFF_BAR + NBARS * 8;
+constexpr uint32_t SMEM_BYTES = OFF_TSLOT + 16 + 1024;  // + alignment slack
+// gate arrays inside a stage's G region (floats)
+constexpr int G_CB = 0, G_CG = 64, G_CD = 128, G_CQ = 192, G_VAL = 256, G_GC = 320;
+
+constexpr uint32_t IDESC_M128_N64 = umma_idesc_bf16(128, 64, false);
+constexpr uint32_t IDESC_M128_N128 = umma_idesc_bf16(128, 128, false);
+constexpr uint32_t IDESC_M128_N128_BMN = umma_idesc_bf16(128, 128, true);
+
+struct TcParams {
+    int B, T, H, nchunks;
+    float scale;
+    const float *alpha, *beta;
+    int64_t as[3], bs[3];
+    const float *valid, *reset;
+    const float* initial;
+    int init_mode;  // 0 zeros, 1 initial pointer, 2 identity
+    int v_zero;     // values treated as zero (span transition)
+    int write_out;
+    float* final_state;
+    int* err;
+};
+
+__device__ __forceinline__ uint64_t kdesc(const uint8_t* p) {  // K-major, 128-B swizzle
+    return umma_sdesc_sw128(smem_u32addr(p), 16, 1024);
 }
 
-int tc_prefill_launch(const dbl_prefill_args*, const int64_t*, const int64_t*, const int64_t*, const int64_t*,
-                      const int64_t*, const int64_t*, int, float*, cudaStream_t) {
-    return fail(DBL_ERR_UNSUPPORTED, "tensor-core prefill is not available");
+__global__ void __launch_bounds__(NTHREADS, 1)
+    gdn2_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                           const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                           const TcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+    uint64_t* bar_full = bars + 0;   // [2] TMA landed
+    uint64_t* bar_empty = bars + 2;  // [2] chain done with the stage
+    uint64_t* bar_prep = bars + 4;   // [2] prep done with the chunk
+    uint64_t* bar_kk = bars + 6;
+    uint64_t* bar_m1 = bars + 7;
+    uint64_t* bar_m2 = bars + 8;
+    uint64_t* bar_m3 = bars + 9;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + OFF_TSLOT);
+    float* sA = reinterpret_cast<float*>(smem + OFF_SA);
+    float* sT = reinterpret_cast<float*>(smem + OFF_ST);
+    float* sXs = reinterpret_cast<float*>(smem + OFF_SX);
+    float* sg = reinterpret_cast<float*>(smem + OFF_SG);
+    int* scnt = reinterpret_cast<int*>(smem + OFF_SCNT);
+    float* swt = reinterpret_cast<float*>(smem + OFF_SWT);
+    int* swc = reinterpret_cast<int*>(smem + OFF_SWT + 32);
+    uint8_t* Ost = smem + OFF_O;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int bh = blockIdx.x;
+    const int b = bh / p.H, h = bh - b * p.H;
+    const int nchunks = p.nchunks;
+
+    auto stX = [&](int s) { return smem + s * STAGE_BYTES; };
+    auto stV = [&](int s) { return smem + s * STAGE_BYTES + X_BYTES; };
+    auto stT = [&](int s) { return smem + s * STAGE_BYTES + X_BYTES + V_BYTES; };
+    auto stP = [&](int s) { return smem + s * STAGE_BYTES + X_BYTES + V_BYTES + T_BYTES; };
+    auto stG = [&](int s) {
+        return reinterpret_cast<float*>(smem + s * STAGE_BYTES + X_BYTES + V_BYTES + T_BYTES + P_BYTES);
+    };
+
+    if (tid == 0) {
+        for (int i = 0; i < (int)NBARS; ++i) mbar_init(bars + i, 1);
+        fence_mbar_init();
+        prefetch_tmap(&tm_q);
+        prefetch_tmap(&tm_k);
+        prefetch_tmap(&tm_v);
+        prefetch_tmap(&tm_o);
+    }
+    if (warp == 0) {
+        tmem_alloc(tslot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+
+    auto issue_loads = [&](int c) {
+        const int s = c & 1;
+        uint8_t* X = stX(s);
+        mbar_arrive_expect_tx(&bar_full[s], p.v_zero ? X_BYTES : X_BYTES + V_BYTES);
+#pragma unroll
+        for (int ib = 0; ib < 2; ++ib) {
+            tma_load_4d(X + ib * 16384, &tm_k, &bar_full[s], ib * 64, c * C, h, b);
+            tma_load_4d(X + ib * 16384 + 8192, &tm_q, &bar_full[s], ib * 64, c * C, h, b);
+        }
+        if (!p.v_zero) tma_load_4d(stV(s), &tm_v, &bar_full[s], 0, c * C, h, b);
+    };
+
+    if (warp < 8) {
+        // =================================================================== prep warps
+        const int q = warp & 3, half = warp >> 2;
+        if (tid == 0) issue_loads(0);
+        for (int c = 0; c < nchunks; ++c) {
+            const int s = c & 1;
+            // ---- gates: threads 0..63, token r = tid
+            float lg = 0.f, be = 0.f, vf = 0.f;
+            int z = 0;
+            if (tid < C) {
+                const int t = c * C + tid;
+                float a = 1.f;
+                if (t < p.T) {
+                    vf = p.valid ? (p.valid[(size_t)b * p.T + t] != 0.f ? 1.f : 0.f) : 1.f;
+                    const bool rs = p.reset ? p.reset[(size_t)b * p.T + t] != 0.f : false;
+                    if (vf != 0.f) {
+                        a = rs ? 0.f : p.alpha[(size_t)b * p.as[0] + (size_t)t * p.as[1] + (size_t)h * p.as[2]];
+                        be = p.beta[(size_t)b * p.bs[0] + (size_t)t * p.bs[1] + (size_t)h * p.bs[2]];
+                    }
+                }
+                z = a <= 0.f;
+                lg = z ? 0.f : logf(a);
+#pragma unroll
+                for (int off = 1; off < 32; off <<= 1) {
+                    const float y = __shfl_up_sync(0xffffffffu, lg, off);
+                    const int yc = __shfl_up_sync(0xffffffffu, z, off);
+                    if (lane >= off) {
+                        lg += y;
+                        z += yc;
+                    }
+                }
+                if (lane == 31) {
+                    swt[warp] = lg;
+                    swc[warp] = z;
+                }
+            }
+            named_bar_sync(BAR_PREP, NPREP);
+            if (tid >= 32 && tid < C) {
+                lg += swt[0];
+                z += swc[0];
+            }
+            // the stage's TMA data (and, through the producer's wait, the stage itself) is ours
+            mbar_wait(&bar_full[s], (c >> 1) & 1, p.err, 1);
+            float* G = stG(s);
+            if (tid < C) {
+                sg[tid] = lg;
+                scnt[tid] = z;
+            }
+            named_bar_sync(BAR_PREP, NPREP);
+            if (tid < C) {
+                const float gC = sg[C - 1];
+                const int cC = scnt[C - 1];
+                const float gamma = (z == 0) ? expf(lg) : 0.f;
+                G[G_CB + tid] = be;
+                G[G_CG + tid] = be * gamma;
+                G[G_CD + tid] = (cC == z) ? expf(gC - lg) : 0.f;
+                G[G_CQ + tid] = gamma * p.scale;
+                G[G_VAL + tid] = vf;
+                if (tid == C - 1) G[G_GC] = gamma;
+            }
+            named_bar_sync(BAR_PREP, NPREP);
+            // ---- [K;Q] K^T on the tensor cores
+            if (tid == 0) {
+                tc_fence_after();
+                const uint8_t* X = stX(s);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint8_t* a = X + (kk >> 2) * 16384 + (kk & 3) * 32;
+                    umma_ss(tmem + TM_KK, kdesc(a), kdesc(a), IDESC_M128_N64, kk > 0 ? 1u : 0u);
+                }
+                umma_commit(bar_kk);
+            }
+            mbar_wait(bar_kk, c & 1, p.err, 2);
+            tc_fence_after();
+            {
+                // row n = 32q + lane of [K;Q]; columns s in [32 half, 32 half + 32)
+                uint32_t g0[16], g1[16];
+                const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + TM_KK + 32 * half;
+                tmem_ld16(ta, g0);
+                tmem_ld16(ta + 16, g1);
+                tmem_ld_wait();
+                const int n = 32 * q + lane;
+                const int r = n & 63;
+                const float gr = sg[r];
+                const int cr = scnt[r];
+                if (n < C) {
+                    const float br = G[G_CB + r];
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        const int sidx = 32 * half + e;
+                        const float gv = __uint_as_float(e < 16 ? g0[e] : g1[e - 16]);
+                        const float dec = (sidx < r && scnt[sidx] == cr) ? expf(gr - sg[sidx]) : 0.f;
+                        sA[r * LDA + sidx] = br * dec * gv;
+                    }
+                } else {
+                    // P = scale Gamma o Q K^T (s <= r) as a bf16 pair hi + lo
+                    uint32_t ph[16], pl[16];
+#pragma unroll
+                    for (int e = 0; e < 32; e += 2) {
+                        float v2[2];
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            const int sidx = 32 * half + e + u;
+                            const float gv = __uint_as_float(e + u < 16 ? g0[e + u] : g1[e + u - 16]);
+                            const float dec = (sidx <= r && scnt[sidx] == cr) ? expf(gr - sg[sidx]) : 0.f;
+                            v2[u] = p.scale * dec * gv;
+                        }
+                        ph[e >> 1] = pack_bf16x2(v2[0], v2[1]);
+                        pl[e >> 1] = pack_bf16x2(v2[0] - bf16_lo(ph[e >> 1]), v2[1] - bf16_hi(ph[e >> 1]));
+                    }
+                    uint8_t* P = stP(s);
+#pragma unroll
+                    for (int x = 0; x < 4; ++x) {
+                        const int cc = 4 * half + x;
+                        const int off = r * 128 + ((cc ^ (r & 7)) << 4);
+                        *reinterpret_cast<uint4*>(P + off) = make_uint4(ph[4 * x], ph[4 * x + 1], ph[4 * x + 2], ph[4 * x + 3]);
+                        *reinterpret_cast<uint4*>(P + C * 128 + off) =
+                            make_uint4(pl[4 * x], pl[4 * x + 1], pl[4 * x + 2], pl[4 * x + 3]);
+                    }
+                }
+            }
+            tc_fence_before();
+            named_bar_sync(BAR_PREP, NPREP);
+            // ---- T = (I + A)^-1: diagonal 16 x 16 blocks by substitution
+            if (tid < C) {
+                const int blk = tid >> 4, c0 = tid & 15;
+                const float* Ab = sA + (16 * blk) * LDA + 16 * blk;
+                float x[16];
+#pragma unroll
+                for (int r = 0; r < 16; ++r) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int s2 = 0; s2 < r; ++s2) acc = fmaf(Ab[r * LDA + s2], x[s2], acc);
+                    x[r] = (r < c0) ? 0.f : (r == c0 ? 1.f : -acc);
+                }
+#pragma unroll
+                for (int r = 0; r < 16; ++r) sT[(16 * blk + r) * LDA + 16 * blk + c0] = x[r];
+            } else {
+                for (int e = tid - C; e < 6 * 256; e += NPREP - C) {
+                    const int pair = e >> 8, rem = e & 255;
+                    const int bb = pair < 3 ? 0 : (pair < 5 ? 1 : 2);
+                    const int aa = pair < 3 ? pair + 1 : (pair < 5 ? pair - 1 : 3);
+                    sT[(16 * bb + (rem >> 4)) * LDA + 16 * aa + (rem & 15)] = 0.f;
+                }
+            }
+            named_bar_sync(BAR_PREP, NPREP);
+            // ---- off-diagonal blocks, by distance d from the diagonal
+#pragma unroll 1
+            for (int d = 1; d < 4; ++d) {
+                const int nb = 4 - d;
+                for (int e = tid; e < nb * 256; e += NPREP) {
+                    const int blk = e >> 8, rem = e & 255, r = rem >> 4, cc = rem & 15;
+                    const int bb = d + blk, aa = bb - d;
+                    float acc = 0.f;
+                    for (int m = 16 * aa; m < 16 * bb; ++m) acc = fmaf(sA[(16 * bb + r) * LDA + m], sT[m * LDA + 16 * aa + cc], acc);
+                    sXs[e] = acc;
+                }
+                named_bar_sync(BAR_PREP, NPREP);
+                for (int e = tid; e < nb * 256; e += NPREP) {
+                    const int blk = e >> 8, rem = e & 255, r = rem >> 4, cc = rem & 15;
+                    const int bb = d + blk, aa = bb - d;
+                    float acc = 0.f;
+#pragma unroll
+                    for (int m = 0; m < 16; ++m) acc = fmaf(sT[(16 * bb + r) * LDA + 16 * bb + m], sXs[blk * 256 + m * 16 + cc], acc);
+                    sT[(16 * bb + r) * LDA + 16 * aa + cc] = -acc;
+                }
+                named_bar_sync(BAR_PREP, NPREP);
+            }
+            // ---- T as a bf16 K-major operand (rows r', 64 columns r, 128-B swizzle)
+            {
+                uint8_t* Tt = stT(s);
+                for (int e = tid; e < 512; e += NPREP) {
+                    const int row = e >> 3, cc = e & 7;
+                    const float* src = sT + row * LDA + cc * 8;
+                    uint4 val = make_uint4(pack_bf16x2(src[0], src[1]), pack_bf16x2(src[2], src[3]),
+                                           pack_bf16x2(src[4], src[5]), pack_bf16x2(src[6], src[7]));
+                    *reinterpret_cast<uint4*>(Tt + row * 128 + ((cc ^ (row & 7)) << 4)) = val;
+                }
+            }
+            fence_proxy_async_smem();
+            named_bar_sync(BAR_PREP, NPREP);
+            if (tid == 0) {
+                mbar_arrive(&bar_prep[s]);
+                const int cn = c + 1;
+                if (cn < nchunks) {
+                    // chunk c + 1 reuses the stage of chunk c - 1: wait until the chain is done with it
+                    if (cn >= 2) mbar_wait(&bar_empty[cn & 1], ((c - 1) >> 1) & 1, p.err, 3);
+                    issue_loads(cn);
+                }
+            }
+        }
+    } else {
+        // =================================================================== chain warps
+        const int ct = tid - NPREP;
+        const int q = warp & 3, hh = (warp - 8) >> 2;
+        const int j = 32 * q + lane;  // state value column == TMEM lane
+        const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16);
+        float S[64];  // S[i][j], i = 64 hh + e
+        const size_t sbase = (size_t)bh * DK * DK;
+#pragma unroll
+        for (int e = 0; e < 64; ++e) {
+            const int i = 64 * hh + e;
+            float x = 0.f;
+            if (p.init_mode == 1) x = p.initial[sbase + (size_t)i * DK + j];
+            else if (p.init_mode == 2) x = (i == j) ? 1.f : 0.f;
+            S[e] = x;
+        }
+        auto store_state_bf16 = [&]() {
+#pragma unroll
+            for (int pc = 0; pc < 4; ++pc) {
+                uint32_t pk[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) pk[u] = pack_bf16x2(S[16 * pc + 2 * u], S[16 * pc + 2 * u + 1]);
+                tmem_st8(tl + TM_S + 32 * hh + 8 * pc, pk);
+            }
+        };
+        store_state_bf16();
+        tmem_st_wait();
+        tc_fence_before();
+        named_bar_sync(BAR_CHAIN, NCHAIN);
+
+        for (int c = 0; c < nchunks; ++c) {
+            const int s = c & 1;
+            const uint32_t par = c & 1;
+            mbar_wait(&bar_prep[s], (c >> 1) & 1, p.err, 4);
+            const float* G = stG(s);
+            // ---- MMA1: D1 = S^T [K;Q]^T
+            if (ct == 0) {
+                tc_fence_after();
+                const uint8_t* X = stX(s);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    umma_ts(tmem + TM_D1, tmem + TM_S + 8 * kk, kdesc(X + (kk >> 2) * 16384 + (kk & 3) * 32),
+                            IDESC_M128_N128, kk > 0 ? 1u : 0u);
+                umma_commit(bar_m1);
+            }
+            mbar_wait(bar_m1, par, p.err, 5);
+            tc_fence_after();
+            // ---- E1: R^T[j][r] = beta_r V[r][j] - beta_r gamma_r (K S)[r][j],  r in [32 hh, 32 hh + 32),
+            //      written in place as a bf16 pair: hi at columns [32 hh, +16), lo at [32 hh + 16, +16)
+            {
+                uint32_t a[32];
+                tmem_ld16(tl + TM_D1 + 32 * hh, *reinterpret_cast<uint32_t(*)[16]>(&a[0]));
+                tmem_ld16(tl + TM_D1 + 32 * hh + 16, *reinterpret_cast<uint32_t(*)[16]>(&a[16]));
+                tmem_ld_wait();
+                const __nv_bfloat16* Vs = reinterpret_cast<const __nv_bfloat16*>(stV(s));
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    const int r = 32 * hh + e;
+                    const float vv = p.v_zero ? 0.f : __bfloat162float(Vs[r * 128 + j]);
+                    a[e] = __float_as_uint(G[G_CB + r] * vv - G[G_CG + r] * __uint_as_float(a[e]));
+                }
+#pragma unroll
+                for (int pc = 0; pc < 2; ++pc) {
+                    uint32_t hi[8], lo[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        const float x0 = __uint_as_float(a[16 * pc + 2 * u]), x1 = __uint_as_float(a[16 * pc + 2 * u + 1]);
+                        hi[u] = pack_bf16x2(x0, x1);
+                        lo[u] = pack_bf16x2(x0 - bf16_lo(hi[u]), x1 - bf16_hi(hi[u]));
+                    }
+                    tmem_st8(tl + TM_D1 + 32 * hh + 8 * pc, hi);
+                    tmem_st8(tl + TM_D1 + 32 * hh + 16 + 8 * pc, lo);
+                }
+                tmem_st_wait();
+            }
+            tc_fence_before();
+            named_bar_sync(BAR_CHAIN, NCHAIN);
+            // ---- MMA2: D2[j][r'] = sum_r R^T[j][r] T[r'][r]
+            if (ct == 0) {
+                tc_fence_after();
+                const uint8_t* Tt = stT(s);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint32_t ra = tmem + TM_D1 + (kk >> 1) * 32 + (kk & 1) * 8;
+                    umma_ts(tmem + TM_D2, ra, kdesc(Tt + kk * 32), IDESC_M128_N64, kk > 0 ? 1u : 0u);
+                    umma_ts(tmem + TM_D2, ra + 16, kdesc(Tt + kk * 32), IDESC_M128_N64, 1u);
+                }
+                umma_commit(bar_m2);
+            }
+            mbar_wait(bar_m2, par, p.err, 6);
+            tc_fence_after();
+            // ---- E2: Delta^T for r' in [32 hh, 32 hh + 32): scaled copy and plain copy, bf16
+            {
+                uint32_t d[32];
+                tmem_ld16(tl + TM_D2 + 32 * hh, *reinterpret_cast<uint32_t(*)[16]>(&d[0]));
+                tmem_ld16(tl + TM_D2 + 32 * hh + 16, *reinterpret_cast<uint32_t(*)[16]>(&d[16]));
+                tmem_ld_wait();
+#pragma unroll
+                for (int pc = 0; pc < 4; ++pc) {  // pc 0,1: scaled copy; pc 2,3: plain copy
+                    uint32_t pk[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        const int e = 16 * (pc & 1) + 2 * u;
+                        const int r = 32 * hh + e;
+                        const float x0 = __uint_as_float(d[e]), x1 = __uint_as_float(d[e + 1]);
+                        pk[u] = pc < 2 ? pack_bf16x2(x0 * G[G_CD + r], x1 * G[G_CD + r + 1]) : pack_bf16x2(x0, x1);
+                    }
+                    tmem_st8(tl + TM_D2 + 32 * hh + 8 * pc, pk);
+                }
+                tmem_st_wait();
+            }
+            tc_fence_before();
+            named_bar_sync(BAR_CHAIN, NCHAIN);
+            // ---- MMA3 (state update) and MMA2b (intra-chunk output)
+            if (ct == 0) {
+                tc_fence_after();
+                const uint8_t* X = stX(s);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_ts(tmem + TM_D3, tmem + TM_D2 + (kk >> 1) * 32 + (kk & 1) * 8,
+                            umma_sdesc_sw128(smem_u32addr(X + kk * 2048), 16384, 1024), IDESC_M128_N128_BMN,
+                            kk > 0 ? 1u : 0u);
+                if (p.write_out) {
+                    const uint8_t* P = stP(s);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint32_t da = tmem + TM_D2 + (kk >> 1) * 32 + 16 + (kk & 1) * 8;
+                        umma_ts(tmem + TM_DO, da, kdesc(P + kk * 32), IDESC_M128_N64, kk > 0 ? 1u : 0u);
+                        umma_ts(tmem + TM_DO, da, kdesc(P + C * 128 + kk * 32), IDESC_M128_N64, 1u);
+                    }
+                }
+                umma_commit(bar_m3);
+                tma_store_wait_read0();  // the previous chunk's output tile has left shared memory
+            }
+            mbar_wait(bar_m3, par, p.err, 7);
+            tc_fence_after();
+            // ---- E3: state update (f32 master copy) and its bf16 image for the next MMA1
+            {
+                const float gC = G[G_GC];
+#pragma unroll
+                for (int pc = 0; pc < 4; ++pc) {
+                    uint32_t d[16];
+                    tmem_ld16(tl + TM_D3 + 64 * hh + 16 * pc, d);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) S[16 * pc + e] = fmaf(gC, S[16 * pc + e], __uint_as_float(d[e]));
+                }
+                store_state_bf16();
+            }
+            if (p.write_out) {
+                named_bar_sync(BAR_CHAIN, NCHAIN);  // output staging buffer is free
+                __nv_bfloat16* Os = reinterpret_cast<__nv_bfloat16*>(Ost);
+#pragma unroll
+                for (int pc = 0; pc < 2; ++pc) {
+                    uint32_t a[16], o[16];
+                    tmem_ld16(tl + TM_D1 + 64 + 32 * hh + 16 * pc, a);
+                    tmem_ld16(tl + TM_DO + 32 * hh + 16 * pc, o);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        const int r = 32 * hh + 16 * pc + e;
+                        const float v = G[G_VAL + r] != 0.f ? fmaf(G[G_CQ + r], __uint_as_float(a[e]), __uint_as_float(o[e])) : 0.f;
+                        Os[r * 128 + j] = __float2bfloat16_rn(v);
+                    }
+                }
+                fence_proxy_async_smem();
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            named_bar_sync(BAR_CHAIN, NCHAIN);
+            if (ct == 0) {
+                if (p.write_out) {
+                    tma_store_4d(&tm_o, Ost, 0, c * C, h, b);
+                    tma_store_commit();
+                }
+                mbar_arrive(&bar_empty[s]);
+            }
+        }
+        if (p.final_state) {
+#pragma unroll
+            for (int e = 0; e < 64; ++e) p.final_state[sbase + (size_t)(64 * hh + e) * DK + j] = S[e];
+        }
+        if (ct == 0) tma_store_wait_all0();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// ------------------------------------------------------------------------------ host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult qr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &qr) == cudaSuccess &&
+            qr == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    }
+    return fn;
+}
+
+// 4-D bf16 map over [B][T][H][128] with element strides `st` (st[3] == 1); box {box0, 64, 1, 1}.
+int make_map(CUtensorMap* m, const void* base, int64_t B, int64_t T, int64_t H, const int64_t* st, uint32_t box0,
+             bool swizzle) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(DBL_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t dims[4] = {128, (cuuint64_t)T, (cuuint64_t)H, (cuuint64_t)B};
+    cuuint64_t strides[3] = {(cuuint64_t)st[1] * 2, (cuuint64_t)st[2] * 2, (cuuint64_t)st[0] * 2};
+    cuuint32_t box[4] = {box0, (cuuint32_t)C, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(DBL_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return DBL_OK;
+}
+
+bool tma_strides_ok(const void* base, const int64_t* st) {
+    if (!base || !aligned(base, 16) || st[3] != 1) return false;
+    for (int d = 0; d < 3; ++d)
+        if (st[d] <= 0 || (st[d] * 2) % 16 != 0 || st[d] * 2 >= (int64_t(1) << 40)) return false;
+    return true;
+}
+
+}  // namespace
+
+int tc_prefill_supported(const dbl_prefill_args* a, const int64_t* qs, const int64_t* ks, const int64_t* vs,
+                         const int64_t* os) {
+    if (a->dtype != DBL_BF16 || a->key_dim != 128 || a->value_dim != 128) return 0;
+    if (a->chunk_size != 0 && a->chunk_size != 64) return 0;
+    if (!tma_strides_ok(a->q, qs) || !tma_strides_ok(a->k, ks)) return 0;
+    if (a->v && !tma_strides_ok(a->v, vs)) return 0;
+    if (a->out && !tma_strides_ok(a->out, os)) return 0;
+    if (a->batch * a->heads > 0x7fffffffLL) return 0;
+    return 1;
+}
+
+int tc_prefill_launch(const dbl_prefill_args* a, const int64_t* qs, const int64_t* ks, const int64_t* vs,
+                      const int64_t* as, const int64_t* bs, const int64_t* os, int mode, float* transition,
+                      cudaStream_t st) {
+    CUtensorMap mq, mk, mv, mo;
+    int rc = make_map(&mq, mode == 1 ? a->k : a->q, a->batch, a->time, a->heads, mode == 1 ? ks : qs, 64, true);
+    if (rc == DBL_OK) rc = make_map(&mk, a->k, a->batch, a->time, a->heads, ks, 64, true);
+    if (rc == DBL_OK) {
+        const bool hv = mode == 0 && a->v;
+        rc = make_map(&mv, hv ? a->v : a->k, a->batch, a->time, a->heads, hv ? vs : ks, 128, false);
+    }
+    const bool write_out = mode == 0 && a->out != nullptr;
+    if (rc == DBL_OK) rc = make_map(&mo, write_out ? a->out : a->k, a->batch, a->time, a->heads, write_out ? os : ks, 128, false);
+    if (rc != DBL_OK) return rc;
+    TcParams p{};
+    p.B = (int)a->batch;
+    p.T = (int)a->time;
+    p.H = (int)a->heads;
+    p.nchunks = (int)((a->time + C - 1) / C);
+    p.scale = a->scale;
+    p.alpha = a->alpha;
+    p.beta = a->beta;
+    for (int d = 0; d < 3; ++d) {
+        p.as[d] = as[d];
+        p.bs[d] = bs[d];
+    }
+    p.valid = a->valid;
+    p.reset = a->reset;
+    if (mode == 1) {
+        p.init_mode = 2;
+        p.v_zero = 1;
+        p.write_out = 0;
+        p.final_state = transition;
+    } else {
+        p.init_mode = a->initial_state ? 1 : 0;
+        p.initial = a->initial_state;
+        p.v_zero = 0;
+        p.write_out = write_out ? 1 : 0;
+        p.final_state = a->final_state;
+    }
+    int* err = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_tc_error);
+    if (e != cudaSuccess) return cuda_status(e, "prefill_tc: error record");
+    p.err = err;
+    static bool attr_set = false;  // per process; the attribute is per device function
+    if (!attr_set) {
+        e = cudaFuncSetAttribute(gdn2_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+        if (e != cudaSuccess) return cuda_status(e, "prefill_tc: cudaFuncSetAttribute");
+        attr_set = true;
+    }
+    gdn2_prefill_tc_kernel<<<(unsigned)(a->batch * a->heads), NTHREADS, SMEM_BYTES, st>>>(mq, mk, mv, mo, p);
+    return launch_status("gdn2_prefill_tc_kernel");
 }
 
 }  // namespace dbl
+
+extern "C" int dbl_device_error(int* code) {
+    int host = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&host, dbl::g_tc_error, sizeof(int));
+    if (e != cudaSuccess) return dbl::cuda_status(e, "dbl_device_error");
+    if (host != 0) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbol(dbl::g_tc_error, &zero, sizeof(int));
+        if (e != cudaSuccess) return dbl::cuda_status(e, "dbl_device_error");
+    }
+    if (code) *code = host;
+    return host ? dbl::fail(DBL_ERR_TIMEOUT, "a kernel gave up a bounded wait (site %d)", host) : DBL_OK;
+}

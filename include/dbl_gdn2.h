@@ -51,6 +51,12 @@ const char *dbl_status_string(int status);
 const char *dbl_last_error(void);
 /* ABI version: major * 10000 + minor * 100 + patch. */
 int dbl_abi_version(void);
+/* Every wait inside the tensor-core kernels is bounded; one that gives up records a site code on
+ * the current device and lets the kernel run to completion (its outputs are then undefined).
+ * This call synchronises with the device, stores that code in *code (0 = none; code may be NULL),
+ * clears the record and returns DBL_OK or DBL_ERR_TIMEOUT.  No counterpart in the reference,
+ * whose kernels have no bounded waits. */
+int dbl_device_error(int *code);
 
 /* =============================================================================================
  * 1. Chunked prefill scan, scalar gates (the BASELINE prefill: configs 0, 1 and 4).

@@ -207,7 +207,7 @@ def test_relay_merge_known_answers(cuda, native_lib):
         kp = torch.full((1, 16, D), -2e16, device=cuda, dtype=dtype)
         vp = torch.full((1, 16, D), 23.0, device=cuda, dtype=dtype)
         o, m, s = dbl.relay_merge_decode(q, kp, vp, ko, vo, scale=0.125)
-        assert torch.equal(o.float(), vo[0, 0].float())
+        assert torch.equal(o[0, 0].float(), vo[0, 0, 0].float())
         assert s.item() == 1.0 and m.item() < -1e30
         ko2 = torch.full((1, 1, 2, D), -1e16, device=cuda, dtype=dtype)
         kp2 = torch.full((1, 16, D), -1e16, device=cuda, dtype=dtype)
@@ -226,3 +226,64 @@ def test_relay_workspace_is_reusable(cuda, native_lib):
         o, _, _ = dbl.relay_merge_decode(q, kp, vp, ko, vo, workspace=ws)
         ro, _, _ = O.relay_merge(host(q), host(kp), host(vp), host(ko), host(vo), 1.0 / np.sqrt(D))
         assert rel_err(host(o), ro) < TOL_BF16
+
+
+# ----------------------------------------------------------------------- tensor-core prefill
+def _device_error_clear(native_lib):
+    import ctypes
+    code = ctypes.c_int(0)
+    rc = native_lib.dbl_device_error(ctypes.byref(code))
+    return rc, code.value
+
+
+def test_prefill_tc_matches_model_and_oracle(cuda, native_lib):
+    from chunk_model import prefill_model
+    B, T, H, D = 2, 333, 2, 128  # partial last chunk
+    q, k, v, alpha, beta = baseline_inputs(11, B, T, H, D, D)
+    q, k, v = bf16_round(q), bf16_round(k), bf16_round(v)
+    rng = np.random.default_rng(4)
+    init = (0.02 * rng.standard_normal((B, H, D, D))).astype(np.float32)
+    valid = rng.random((B, T)) > 0.05
+    reset = rng.random((B, T)) > 0.98
+    out, fin = dbl.gdn2_prefill(dev_t(q, cuda, torch.bfloat16), dev_t(k, cuda, torch.bfloat16),
+                                dev_t(v, cuda, torch.bfloat16), dev_t(alpha, cuda), dev_t(beta, cuda),
+                                valid=dev_t(valid, cuda), reset=dev_t(reset, cuda), initial_state=dev_t(init, cuda))
+    torch.cuda.synchronize()
+    assert _device_error_clear(native_lib) == (0, 0)
+    out, fin = host(out), host(fin)
+    ro, rf, _ = O.scan_scalar(q, k, v, alpha, beta, valid, reset, init)
+    mo, mf = prefill_model(q, k, v, alpha, beta, 1 / np.sqrt(D), valid, reset, init)
+    assert rel_err(out, ro) < TOL_BF16 and rel_err(fin, rf) < TOL_BF16
+    assert rel_err(out, mo) < 1e-2 and rel_err(fin, mf) < 1e-2
+    assert np.all(out[~valid] == 0.0)
+
+
+def test_prefill_tc_config1_full_size_sampled_heads(cuda, native_lib):
+    # BASELINE config 1 at full size on the GPU; two (b, h) heads checked against the oracle.
+    import bench
+    q, k, v, alpha, beta = bench.make_prefill_inputs(torch, cuda, 1234)
+    out, fin = dbl.gdn2_prefill(q, k, v, alpha, beta)
+    torch.cuda.synchronize()
+    assert _device_error_clear(native_lib) == (0, 0)
+    for b, h in ((0, 0), (7, 13)):
+        sl = lambda t: host(t[b:b + 1, :, h:h + 1])  # noqa: E731
+        ro, rf, _ = O.scan_scalar(sl(q), sl(k), sl(v), host(alpha[b:b + 1, :, h:h + 1]),
+                                  host(beta[b:b + 1, :, h:h + 1]))
+        assert rel_err(host(out[b:b + 1, :, h:h + 1]), ro) < TOL_BF16
+        assert rel_err(host(fin[b:b + 1, h:h + 1]), rf) < TOL_BF16
+
+
+def test_prefill_tc_span_transition(cuda, native_lib):
+    B, T, H, D = 1, 300, 2, 128
+    q, k, v, alpha, beta = baseline_inputs(21, B, T, H, D, D)
+    q, k, v = bf16_round(q), bf16_round(k), bf16_round(v)
+    S0 = (0.05 * np.random.default_rng(2).standard_normal((B, H, D, D))).astype(np.float32)
+    _, ref_fin, _ = O.scan_scalar(q, k, v, alpha, beta, initial=S0)
+    A = host(dbl.gdn2_span_transition(dev_t(k, cuda, torch.bfloat16), dev_t(alpha, cuda), dev_t(beta, cuda)))
+    _, Bs = dbl.gdn2_prefill(dev_t(q, cuda, torch.bfloat16), dev_t(k, cuda, torch.bfloat16),
+                             dev_t(v, cuda, torch.bfloat16), dev_t(alpha, cuda), dev_t(beta, cuda),
+                             want_output=False)
+    torch.cuda.synchronize()
+    assert _device_error_clear(native_lib) == (0, 0)
+    comp = np.einsum("bhik,bhkj->bhij", A, S0) + host(Bs)
+    assert rel_err(comp, ref_fin) < TOL_BF16
