@@ -5,7 +5,7 @@
 // the decay products formed in log space instead of the reference's direct products; chunk 64
 // instead of its <= 16 because the triangular system is solved by substitution, not by the
 // nilpotent series).  For a chunk with start state S (key-major, K x V) and rows r = 0..63:
-//   g_r = sum_{u<=r} log alpha_u, gamma_r = exp(g_r), Gamma[r][s] = exp(g_r - g_s) (s <= r);
+//   g_r = sum_{u<=r} log2 alpha_u, gamma_r = 2^g_r, Gamma[r][s] = 2^(g_r - g_s) (s <= r);
 //   a zero alpha (a reset, or alpha = 0) zeroes every product that spans it.
 //   A  = strict_lower(beta_r Gamma[r][s] k_r.k_s)      T = (I + A)^-1
 //   R  = beta V - diag(beta gamma) K S                  Delta = T R        (the edits)
@@ -17,7 +17,8 @@
 //   * prep warps 0-7: TMA loads of the chunk tiles (K and Q 128-byte swizzled, V plain), the gate
 //     scan, UMMA [K;Q] K^T -> TMEM, decay masks, the blocked 64x64 unit-lower inverse (16x16
 //     diagonal blocks by substitution, off-diagonal blocks level by level), T and P written as
-//     bf16 UMMA operands.  Prep runs one chunk ahead of the chain (two smem stages).
+//     bf16 UMMA operands.  Prep runs one chunk ahead of the chain (two smem stages); the chain
+//     leader issues the loads of chunk c + 2 as soon as it is done with chunk c.
 //   * chain warps 8-15: the state-dependent chain, transposed so that the value column j of the
 //     state is TMEM lane j and every activation stays in TMEM (A operands of the TS form):
 //       MMA1  D1[j][n]  = sum_i S^T[j][i] [K;Q][n][i]      (A = S^T bf16 in TMEM)
@@ -68,9 +69,10 @@ constexpr uint32_t STAGE_BYTES = X_BYTES + V_BYTES + T_BYTES + P_BYTES + G_BYTES
 constexpr uint32_t OFF_O = 2 * STAGE_BYTES;
 constexpr uint32_t O_BYTES = C * 128 * 2;
 constexpr uint32_t OFF_SA = OFF_O + O_BYTES;
-constexpr int LDA = 65;
+constexpr int LDA = 65;   // A rows (written row-per-lane: odd stride avoids bank conflicts)
+constexpr int LDT = 68;   // T rows (read as float4: 16-byte aligned stride)
 constexpr uint32_t OFF_ST = OFF_SA + C * LDA * 4;
-constexpr uint32_t OFF_SX = OFF_ST + C * LDA * 4;
+constexpr uint32_t OFF_SX = OFF_ST + C * LDT * 4;
 constexpr uint32_t OFF_SG = OFF_SX + 768 * 4;
 constexpr uint32_t OFF_SCNT = OFF_SG + 64 * 4;
 constexpr uint32_t OFF_SWT = OFF_SCNT + 64 * 4;
@@ -111,7 +113,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
     uint64_t* bar_full = bars + 0;   // [2] TMA landed
-    uint64_t* bar_empty = bars + 2;  // [2] chain done with the stage
     uint64_t* bar_prep = bars + 4;   // [2] prep done with the chunk
     uint64_t* bar_kk = bars + 6;
     uint64_t* bar_m1 = bars + 7;
@@ -172,7 +173,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (warp < 8) {
         // =================================================================== prep warps
         const int q = warp & 3, half = warp >> 2;
-        if (tid == 0) issue_loads(0);
+        if (tid == 0) {
+            issue_loads(0);
+            if (nchunks > 1) issue_loads(1);
+        }
         for (int c = 0; c < nchunks; ++c) {
             const int s = c & 1;
             // ---- gates: threads 0..63, token r = tid
@@ -190,7 +194,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     }
                 }
                 z = a <= 0.f;
-                lg = z ? 0.f : logf(a);
+                lg = z ? 0.f : __log2f(a);  // log2 domain: every decay product is one exp2
 #pragma unroll
                 for (int off = 1; off < 32; off <<= 1) {
                     const float y = __shfl_up_sync(0xffffffffu, lg, off);
@@ -221,10 +225,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (tid < C) {
                 const float gC = sg[C - 1];
                 const int cC = scnt[C - 1];
-                const float gamma = (z == 0) ? expf(lg) : 0.f;
+                const float gamma = (z == 0) ? exp2f(lg) : 0.f;
                 G[G_CB + tid] = be;
                 G[G_CG + tid] = be * gamma;
-                G[G_CD + tid] = (cC == z) ? expf(gC - lg) : 0.f;
+                G[G_CD + tid] = (cC == z) ? exp2f(gC - lg) : 0.f;
                 G[G_CQ + tid] = gamma * p.scale;
                 G[G_VAL + tid] = vf;
                 if (tid == C - 1) G[G_GC] = gamma;
@@ -254,14 +258,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const int r = n & 63;
                 const float gr = sg[r];
                 const int cr = scnt[r];
+                const bool zeros = scnt[C - 1] != 0;  // a reset or a zero decay inside this chunk
                 if (n < C) {
                     const float br = G[G_CB + r];
 #pragma unroll
                     for (int e = 0; e < 32; ++e) {
                         const int sidx = 32 * half + e;
                         const float gv = __uint_as_float(e < 16 ? g0[e] : g1[e - 16]);
-                        const float dec = (sidx < r && scnt[sidx] == cr) ? expf(gr - sg[sidx]) : 0.f;
-                        sA[r * LDA + sidx] = br * dec * gv;
+                        const bool live = sidx < r && (!zeros || scnt[sidx] == cr);
+                        sA[r * LDA + sidx] = live ? br * exp2f(gr - sg[sidx]) * gv : 0.f;
                     }
                 } else {
                     // P = scale Gamma o Q K^T (s <= r) as a bf16 pair hi + lo
@@ -273,8 +278,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         for (int u = 0; u < 2; ++u) {
                             const int sidx = 32 * half + e + u;
                             const float gv = __uint_as_float(e + u < 16 ? g0[e + u] : g1[e + u - 16]);
-                            const float dec = (sidx <= r && scnt[sidx] == cr) ? expf(gr - sg[sidx]) : 0.f;
-                            v2[u] = p.scale * dec * gv;
+                            const bool live = sidx <= r && (!zeros || scnt[sidx] == cr);
+                            v2[u] = live ? p.scale * exp2f(gr - sg[sidx]) * gv : 0.f;
                         }
                         ph[e >> 1] = pack_bf16x2(v2[0], v2[1]);
                         pl[e >> 1] = pack_bf16x2(v2[0] - bf16_lo(ph[e >> 1]), v2[1] - bf16_hi(ph[e >> 1]));
@@ -305,35 +310,53 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     x[r] = (r < c0) ? 0.f : (r == c0 ? 1.f : -acc);
                 }
 #pragma unroll
-                for (int r = 0; r < 16; ++r) sT[(16 * blk + r) * LDA + 16 * blk + c0] = x[r];
+                for (int r = 0; r < 16; ++r) sT[(16 * blk + r) * LDT + 16 * blk + c0] = x[r];
             } else {
                 for (int e = tid - C; e < 6 * 256; e += NPREP - C) {
                     const int pair = e >> 8, rem = e & 255;
                     const int bb = pair < 3 ? 0 : (pair < 5 ? 1 : 2);
                     const int aa = pair < 3 ? pair + 1 : (pair < 5 ? pair - 1 : 3);
-                    sT[(16 * bb + (rem >> 4)) * LDA + 16 * aa + (rem & 15)] = 0.f;
+                    sT[(16 * bb + (rem >> 4)) * LDT + 16 * aa + (rem & 15)] = 0.f;
                 }
             }
             named_bar_sync(BAR_PREP, NPREP);
-            // ---- off-diagonal blocks, by distance d from the diagonal
+            // ---- off-diagonal blocks, by distance d from the diagonal:
+            //      T[b][a] = -T[b][b] (sum_{a <= m < b} A[b][m] T[m][a]); a thread computes 4 columns
 #pragma unroll 1
             for (int d = 1; d < 4; ++d) {
-                const int nb = 4 - d;
-                for (int e = tid; e < nb * 256; e += NPREP) {
-                    const int blk = e >> 8, rem = e & 255, r = rem >> 4, cc = rem & 15;
+                const int units = (4 - d) * 64;  // (block, row, column quad)
+                if (tid < units) {
+                    const int blk = tid >> 6, r = (tid >> 2) & 15, cq = tid & 3;
                     const int bb = d + blk, aa = bb - d;
-                    float acc = 0.f;
-                    for (int m = 16 * aa; m < 16 * bb; ++m) acc = fmaf(sA[(16 * bb + r) * LDA + m], sT[m * LDA + 16 * aa + cc], acc);
-                    sXs[e] = acc;
+                    const float* Arow = sA + (16 * bb + r) * LDA;
+                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int m = 16 * aa; m < 16 * bb; ++m) {
+                        const float a = Arow[m];
+                        const float4 t4 = *reinterpret_cast<const float4*>(sT + m * LDT + 16 * aa + 4 * cq);
+                        acc.x = fmaf(a, t4.x, acc.x);
+                        acc.y = fmaf(a, t4.y, acc.y);
+                        acc.z = fmaf(a, t4.z, acc.z);
+                        acc.w = fmaf(a, t4.w, acc.w);
+                    }
+                    *reinterpret_cast<float4*>(sXs + blk * 256 + r * 16 + 4 * cq) = acc;
                 }
                 named_bar_sync(BAR_PREP, NPREP);
-                for (int e = tid; e < nb * 256; e += NPREP) {
-                    const int blk = e >> 8, rem = e & 255, r = rem >> 4, cc = rem & 15;
+                if (tid < units) {
+                    const int blk = tid >> 6, r = (tid >> 2) & 15, cq = tid & 3;
                     const int bb = d + blk, aa = bb - d;
-                    float acc = 0.f;
+                    const float* Trow = sT + (16 * bb + r) * LDT + 16 * bb;
+                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-                    for (int m = 0; m < 16; ++m) acc = fmaf(sT[(16 * bb + r) * LDA + 16 * bb + m], sXs[blk * 256 + m * 16 + cc], acc);
-                    sT[(16 * bb + r) * LDA + 16 * aa + cc] = -acc;
+                    for (int m = 0; m < 16; ++m) {
+                        const float t = Trow[m];
+                        const float4 x4 = *reinterpret_cast<const float4*>(sXs + blk * 256 + m * 16 + 4 * cq);
+                        acc.x = fmaf(t, x4.x, acc.x);
+                        acc.y = fmaf(t, x4.y, acc.y);
+                        acc.z = fmaf(t, x4.z, acc.z);
+                        acc.w = fmaf(t, x4.w, acc.w);
+                    }
+                    *reinterpret_cast<float4*>(sT + (16 * bb + r) * LDT + 16 * aa + 4 * cq) =
+                        make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
                 }
                 named_bar_sync(BAR_PREP, NPREP);
             }
@@ -342,23 +365,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 uint8_t* Tt = stT(s);
                 for (int e = tid; e < 512; e += NPREP) {
                     const int row = e >> 3, cc = e & 7;
-                    const float* src = sT + row * LDA + cc * 8;
-                    uint4 val = make_uint4(pack_bf16x2(src[0], src[1]), pack_bf16x2(src[2], src[3]),
-                                           pack_bf16x2(src[4], src[5]), pack_bf16x2(src[6], src[7]));
+                    const float4 u = *reinterpret_cast<const float4*>(sT + row * LDT + cc * 8);
+                    const float4 w = *reinterpret_cast<const float4*>(sT + row * LDT + cc * 8 + 4);
+                    uint4 val = make_uint4(pack_bf16x2(u.x, u.y), pack_bf16x2(u.z, u.w), pack_bf16x2(w.x, w.y),
+                                           pack_bf16x2(w.z, w.w));
                     *reinterpret_cast<uint4*>(Tt + row * 128 + ((cc ^ (row & 7)) << 4)) = val;
                 }
             }
             fence_proxy_async_smem();
             named_bar_sync(BAR_PREP, NPREP);
-            if (tid == 0) {
-                mbar_arrive(&bar_prep[s]);
-                const int cn = c + 1;
-                if (cn < nchunks) {
-                    // chunk c + 1 reuses the stage of chunk c - 1: wait until the chain is done with it
-                    if (cn >= 2) mbar_wait(&bar_empty[cn & 1], ((c - 1) >> 1) & 1, p.err, 3);
-                    issue_loads(cn);
-                }
-            }
+            if (tid == 0) mbar_arrive(&bar_prep[s]);
         }
     } else {
         // =================================================================== chain warps
@@ -535,7 +551,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     tma_store_4d(&tm_o, Ost, 0, c * C, h, b);
                     tma_store_commit();
                 }
-                mbar_arrive(&bar_empty[s]);
+                // the chain is done with stage s: it takes chunk c + 2 at once
+                if (c + 2 < nchunks) issue_loads(c + 2);
             }
         }
         if (p.final_state) {

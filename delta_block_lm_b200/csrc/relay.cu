@@ -310,7 +310,8 @@ __device__ void prefix_block_f32(const RelayParams& p, unsigned char* smem) {
             __syncthreads();
             for (int x = tid; x < QT * D; x += THREADS) {
                 const int r = x / D, c = x - r * D;
-                sQ[r * (D + 1) + c] = r < nq ? static_cast<const float*>(p.q)[((size_t)(n0 + r) * p.H + h) * D + c] : 0.f;
+                sQ[r * (D + 1) + c] =
+                    r < nq ? static_cast<const float*>(p.q)[((size_t)(n0 + r) * p.H + h) * D + c] * p.scale : 0.f;
             }
             __syncthreads();
             {  // thread: query tid/8, keys (tid%8) + 8b
@@ -324,7 +325,7 @@ __device__ void prefix_block_f32(const RelayParams& p, unsigned char* smem) {
 #pragma unroll
                 for (int b = 0; b < 4; ++b) {
                     const int key = kg + 8 * b;
-                    sS[qi * (HK + 1) + key] = key < nkeys ? acc[b] * p.scale : -FLT_MAX;
+                    sS[qi * (HK + 1) + key] = key < nkeys ? acc[b] : -FLT_MAX;
                 }
             }
             __syncthreads();
@@ -387,31 +388,45 @@ __device__ void own_block(const RelayParams& p, unsigned char* smem) {
     const int nkeys = max(0, min(BO, own - key0));
     const size_t row = (size_t)n * p.H + h;
     const int sub = lane / LPK, part = lane % LPK;  // key slot within the warp, chunk of the row
-    // this lane's EPL query elements
-    float qv[EPL];
-    {
-        const T* q = static_cast<const T*>(p.q) + row * D + part * EPL;
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) qv[e] = to_f32(q[e]) * p.scale;
-    }
     const T* ko = static_cast<const T*>(p.ko) + (row * p.Lo + key0) * D;
     const T* vo = static_cast<const T*>(p.vo) + (row * p.Lo + key0) * D;
-    // scores: warp w covers keys [w*32, w*32+32), KPW keys per instruction
     constexpr int KEYS_PER_WARP = BO / NW;
     constexpr int ITER = KEYS_PER_WARP / KPW;
-#pragma unroll 4
-    for (int it = 0; it < ITER; ++it) {
-        const int key = warp * KEYS_PER_WARP + it * KPW + sub;
+    if constexpr (sizeof(T) == 4) {
+        // f32: the prefix SIMT path's exact arithmetic (pre-scaled q, one fma chain over d), so
+        // that equal keys in the two segments give bit-equal scores (relay_tests.rs:47-90).
+        float* sq = sacc;  // [D], reused before the value pass
+        for (int c = tid; c < D; c += THREADS) sq[c] = to_f32(static_cast<const T*>(p.q)[row * D + c]) * p.scale;
+        __syncthreads();
+        const int key = tid;
         float d = 0.f;
         if (key < nkeys) {
-            const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(ko + (size_t)key * D + part * EPL));
-            const T* x = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-            for (int e = 0; e < EPL; ++e) d = fmaf(qv[e], to_f32(x[e]), d);
+            const T* kr = ko + (size_t)key * D;
+#pragma unroll 8
+            for (int c = 0; c < D; ++c) d = fmaf(sq[c], to_f32(kr[c]), d);
         }
+        se[key] = key < nkeys ? d : -FLT_MAX;
+    } else {
+        // bf16: warp-cooperative 16-byte loads; products of bf16 values are exact in f32 and the
+        // score is scaled after the sum, as the tensor-core prefix path does.
+        float qv[EPL];
+        const T* q = static_cast<const T*>(p.q) + row * D + part * EPL;
 #pragma unroll
-        for (int o = LPK / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-        if (part == 0) se[key] = key < nkeys ? d : -FLT_MAX;
+        for (int e = 0; e < EPL; ++e) qv[e] = to_f32(q[e]);
+#pragma unroll 4
+        for (int it = 0; it < ITER; ++it) {
+            const int key = warp * KEYS_PER_WARP + it * KPW + sub;
+            float d = 0.f;
+            if (key < nkeys) {
+                const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(ko + (size_t)key * D + part * EPL));
+                const T* x = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+                for (int e = 0; e < EPL; ++e) d = fmaf(qv[e], to_f32(x[e]), d);
+            }
+#pragma unroll
+            for (int o = LPK / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+            if (part == 0) se[key] = key < nkeys ? d * p.scale : -FLT_MAX;
+        }
     }
     __syncthreads();
     float m = -FLT_MAX;
