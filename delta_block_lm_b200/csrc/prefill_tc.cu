@@ -73,8 +73,9 @@ constexpr int LDA = 65;   // A rows (written row-per-lane: odd stride avoids ban
 constexpr int LDT = 68;   // T rows (read as float4: 16-byte aligned stride)
 constexpr uint32_t OFF_ST = OFF_SA + C * LDA * 4;
 constexpr uint32_t OFF_SX = OFF_ST + C * LDT * 4;
-constexpr uint32_t OFF_SG = OFF_SX + 768 * 4;
-constexpr uint32_t OFF_SCNT = OFF_SG + 64 * 4;
+constexpr uint32_t OFF_SG = OFF_SX + 1024 * 4;
+constexpr uint32_t OFF_SEM = OFF_SG + 64 * 4;   // 2^-g_s (fast decay path)
+constexpr uint32_t OFF_SCNT = OFF_SEM + 64 * 4;
 constexpr uint32_t OFF_SWT = OFF_SCNT + 64 * 4;
 constexpr uint32_t OFF_BAR = (OFF_SWT + 64 + 7) / 8 * 8;
 constexpr uint32_t NBARS = 11;
@@ -123,6 +124,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     float* sT = reinterpret_cast<float*>(smem + OFF_ST);
     float* sXs = reinterpret_cast<float*>(smem + OFF_SX);
     float* sg = reinterpret_cast<float*>(smem + OFF_SG);
+    float* sem = reinterpret_cast<float*>(smem + OFF_SEM);
     int* scnt = reinterpret_cast<int*>(smem + OFF_SCNT);
     float* swt = reinterpret_cast<float*>(smem + OFF_SWT);
     int* swc = reinterpret_cast<int*>(smem + OFF_SWT + 32);
@@ -177,22 +179,31 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             issue_loads(0);
             if (nchunks > 1) issue_loads(1);
         }
+        // gates of the next chunk are fetched one iteration ahead (their load latency is hidden)
+        float nx_a = 1.f, nx_b = 0.f, nx_v = 0.f;
+        auto fetch_gates = [&](int c) {
+            nx_a = 1.f;
+            nx_b = 0.f;
+            nx_v = 0.f;
+            const int t = c * C + tid;
+            if (tid < C && t < p.T) {
+                nx_v = p.valid ? (p.valid[(size_t)b * p.T + t] != 0.f ? 1.f : 0.f) : 1.f;
+                const bool rs = p.reset ? p.reset[(size_t)b * p.T + t] != 0.f : false;
+                if (nx_v != 0.f) {
+                    nx_a = rs ? 0.f : p.alpha[(size_t)b * p.as[0] + (size_t)t * p.as[1] + (size_t)h * p.as[2]];
+                    nx_b = p.beta[(size_t)b * p.bs[0] + (size_t)t * p.bs[1] + (size_t)h * p.bs[2]];
+                }
+            }
+        };
+        fetch_gates(0);
         for (int c = 0; c < nchunks; ++c) {
             const int s = c & 1;
             // ---- gates: threads 0..63, token r = tid
-            float lg = 0.f, be = 0.f, vf = 0.f;
+            const float a = nx_a, be = nx_b, vf = nx_v;
+            if (c + 1 < nchunks) fetch_gates(c + 1);
+            float lg = 0.f;
             int z = 0;
             if (tid < C) {
-                const int t = c * C + tid;
-                float a = 1.f;
-                if (t < p.T) {
-                    vf = p.valid ? (p.valid[(size_t)b * p.T + t] != 0.f ? 1.f : 0.f) : 1.f;
-                    const bool rs = p.reset ? p.reset[(size_t)b * p.T + t] != 0.f : false;
-                    if (vf != 0.f) {
-                        a = rs ? 0.f : p.alpha[(size_t)b * p.as[0] + (size_t)t * p.as[1] + (size_t)h * p.as[2]];
-                        be = p.beta[(size_t)b * p.bs[0] + (size_t)t * p.bs[1] + (size_t)h * p.bs[2]];
-                    }
-                }
                 z = a <= 0.f;
                 lg = z ? 0.f : __log2f(a);  // log2 domain: every decay product is one exp2
 #pragma unroll
@@ -220,6 +231,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (tid < C) {
                 sg[tid] = lg;
                 scnt[tid] = z;
+                sem[tid] = exp2f(-lg);
             }
             named_bar_sync(BAR_PREP, NPREP);
             if (tid < C) {
@@ -258,18 +270,24 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const int r = n & 63;
                 const float gr = sg[r];
                 const int cr = scnt[r];
-                const bool zeros = scnt[C - 1] != 0;  // a reset or a zero decay inside this chunk
+                // Fast path: no zero decay in the chunk and a bounded total decay, so
+                // Gamma[r][s] = 2^g_r 2^-g_s is a rank-1 product (no exponential per element).
+                const bool fast = scnt[C - 1] == 0 && sg[C - 1] > -100.f;
+                const float er = exp2f(gr);
                 if (n < C) {
-                    const float br = G[G_CB + r];
+                    const float br = G[G_CB + r] * er;
 #pragma unroll
                     for (int e = 0; e < 32; ++e) {
                         const int sidx = 32 * half + e;
                         const float gv = __uint_as_float(e < 16 ? g0[e] : g1[e - 16]);
-                        const bool live = sidx < r && (!zeros || scnt[sidx] == cr);
-                        sA[r * LDA + sidx] = live ? br * exp2f(gr - sg[sidx]) * gv : 0.f;
+                        float v;
+                        if (fast) v = sidx < r ? br * gv * sem[sidx] : 0.f;
+                        else v = (sidx < r && scnt[sidx] == cr) ? G[G_CB + r] * exp2f(gr - sg[sidx]) * gv : 0.f;
+                        sA[r * LDA + sidx] = v;
                     }
                 } else {
                     // P = scale Gamma o Q K^T (s <= r) as a bf16 pair hi + lo
+                    const float sr = p.scale * er;
                     uint32_t ph[16], pl[16];
 #pragma unroll
                     for (int e = 0; e < 32; e += 2) {
@@ -278,8 +296,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         for (int u = 0; u < 2; ++u) {
                             const int sidx = 32 * half + e + u;
                             const float gv = __uint_as_float(e + u < 16 ? g0[e + u] : g1[e + u - 16]);
-                            const bool live = sidx <= r && (!zeros || scnt[sidx] == cr);
-                            v2[u] = live ? p.scale * exp2f(gr - sg[sidx]) * gv : 0.f;
+                            if (fast) v2[u] = sidx <= r ? sr * gv * sem[sidx] : 0.f;
+                            else v2[u] = (sidx <= r && scnt[sidx] == cr) ? p.scale * exp2f(gr - sg[sidx]) * gv : 0.f;
                         }
                         ph[e >> 1] = pack_bf16x2(v2[0], v2[1]);
                         pl[e >> 1] = pack_bf16x2(v2[0] - bf16_lo(ph[e >> 1]), v2[1] - bf16_hi(ph[e >> 1]));
@@ -321,35 +339,49 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             named_bar_sync(BAR_PREP, NPREP);
             // ---- off-diagonal blocks, by distance d from the diagonal:
-            //      T[b][a] = -T[b][b] (sum_{a <= m < b} A[b][m] T[m][a]); a thread computes 4 columns
+            //      T[b][a] = -T[b][b] (sum_{a <= m < b} A[b][m] T[m][a]).  A thread computes 4 columns of
+            //      one 16-long piece of the m-sum (d pieces per output), the next phase adds the pieces.
 #pragma unroll 1
             for (int d = 1; d < 4; ++d) {
                 const int units = (4 - d) * 64;  // (block, row, column quad)
-                if (tid < units) {
-                    const int blk = tid >> 6, r = (tid >> 2) & 15, cq = tid & 3;
+                if (tid < units * d) {
+                    const int pc = tid / units, u = tid - pc * units;
+                    const int blk = u >> 6, r = (u >> 2) & 15, cq = u & 3;
                     const int bb = d + blk, aa = bb - d;
-                    const float* Arow = sA + (16 * bb + r) * LDA;
+                    const int m0 = 16 * (aa + pc);
+                    const float* Arow = sA + (16 * bb + r) * LDA + m0;
+                    const float* Tcol = sT + m0 * LDT + 16 * aa + 4 * cq;
                     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                    for (int m = 16 * aa; m < 16 * bb; ++m) {
-                        const float a = Arow[m];
-                        const float4 t4 = *reinterpret_cast<const float4*>(sT + m * LDT + 16 * aa + 4 * cq);
-                        acc.x = fmaf(a, t4.x, acc.x);
-                        acc.y = fmaf(a, t4.y, acc.y);
-                        acc.z = fmaf(a, t4.z, acc.z);
-                        acc.w = fmaf(a, t4.w, acc.w);
+#pragma unroll
+                    for (int m = 0; m < 16; ++m) {
+                        const float av = Arow[m];
+                        const float4 t4 = *reinterpret_cast<const float4*>(Tcol + m * LDT);
+                        acc.x = fmaf(av, t4.x, acc.x);
+                        acc.y = fmaf(av, t4.y, acc.y);
+                        acc.z = fmaf(av, t4.z, acc.z);
+                        acc.w = fmaf(av, t4.w, acc.w);
                     }
-                    *reinterpret_cast<float4*>(sXs + blk * 256 + r * 16 + 4 * cq) = acc;
+                    *reinterpret_cast<float4*>(sXs + (pc * units + u) * 4) = acc;
                 }
                 named_bar_sync(BAR_PREP, NPREP);
                 if (tid < units) {
-                    const int blk = tid >> 6, r = (tid >> 2) & 15, cq = tid & 3;
+                    const int u = tid;
+                    const int blk = u >> 6, r = (u >> 2) & 15, cq = u & 3;
                     const int bb = d + blk, aa = bb - d;
                     const float* Trow = sT + (16 * bb + r) * LDT + 16 * bb;
                     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
                     for (int m = 0; m < 16; ++m) {
                         const float t = Trow[m];
-                        const float4 x4 = *reinterpret_cast<const float4*>(sXs + blk * 256 + m * 16 + 4 * cq);
+                        const int um = (blk << 6) | (m << 2) | cq;  // unit (blk, row m, cq)
+                        float4 x4 = *reinterpret_cast<const float4*>(sXs + um * 4);
+                        for (int pc = 1; pc < d; ++pc) {
+                            const float4 y = *reinterpret_cast<const float4*>(sXs + (pc * units + um) * 4);
+                            x4.x += y.x;
+                            x4.y += y.y;
+                            x4.z += y.z;
+                            x4.w += y.w;
+                        }
                         acc.x = fmaf(t, x4.x, acc.x);
                         acc.y = fmaf(t, x4.y, acc.y);
                         acc.z = fmaf(t, x4.z, acc.z);
@@ -516,12 +548,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             {
                 const float gC = G[G_GC];
 #pragma unroll
-                for (int pc = 0; pc < 4; ++pc) {
-                    uint32_t d[16];
-                    tmem_ld16(tl + TM_D3 + 64 * hh + 16 * pc, d);
+                for (int pc = 0; pc < 2; ++pc) {
+                    uint32_t d[32];
+                    tmem_ld16(tl + TM_D3 + 64 * hh + 32 * pc, *reinterpret_cast<uint32_t(*)[16]>(&d[0]));
+                    tmem_ld16(tl + TM_D3 + 64 * hh + 32 * pc + 16, *reinterpret_cast<uint32_t(*)[16]>(&d[16]));
                     tmem_ld_wait();
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) S[16 * pc + e] = fmaf(gC, S[16 * pc + e], __uint_as_float(d[e]));
+                    for (int e = 0; e < 32; ++e) S[32 * pc + e] = fmaf(gC, S[32 * pc + e], __uint_as_float(d[e]));
                 }
                 store_state_bf16();
             }
