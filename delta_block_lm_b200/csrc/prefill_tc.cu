@@ -21,17 +21,19 @@
 //     leader issues the loads of chunk c + 2 as soon as it is done with chunk c.
 //   * chain warps 8-15: the state-dependent chain, transposed so that the value column j of the
 //     state is TMEM lane j and every activation stays in TMEM (A operands of the TS form):
-//       MMA1  D1[j][n]  = sum_i S^T[j][i] [K;Q][n][i]      (A = S^T bf16 in TMEM)
+//       MMA1  D1[j][r]  = sum_i S^T[j][i] K[r][i]          (A = S^T bf16 in TMEM)
 //       E1    R^T[j][r] = beta_r V[r][j] - beta_r gamma_r D1[j][r]   -> TMEM (bf16 hi + lo pair)
 //       MMA2  D2[j][r'] = sum_r R^T[j][r] T[r'][r]          (Delta^T; hi and lo accumulate)
 //       E2    Delta^T scaled by Gamma[63][r'] and plain                     -> TMEM (bf16)
 //       MMA3  D3[j][i]  = sum_r' (Gamma Delta)^T[j][r'] K[r'][i]   (B = K tile read MN-major)
-//       MMA2b DO[j][r]  = sum_r' Delta^T[j][r'] P[r][r']     (P as a bf16 hi + lo pair)
-//     R and P are carried as bf16 pairs because their rounding dominates the error budget: with
+//       MMA4  DO[j][r]  = sum_i S^T[j][i] Q[r][i] + sum_r' Delta^T[j][r'] P~[r][r']
+//             with P~ = P / om_r and om_r = scale gamma_r (P~ as a bf16 hi + lo pair)
+//     R and P~ are carried as bf16 pairs because their rounding dominates the error budget: with
 //     single bf16 operands the output error reaches the 2e-2 bound at T = 4096, with the pairs it
 //     stays near 1e-2 (see tests/chunk_model.py).
 //       E3    S[i][j] = gamma_63 S + D3 (f32 master state in registers, 64 per thread),
-//             S^T -> TMEM bf16; O[r][j] = scale gamma_r D1[j][64+r] + DO[j][r] -> smem -> TMA store.
+//             S^T -> TMEM bf16; then MMA1 of the next chunk is issued and, while it runs,
+//             O[r][j] = om_r DO[j][r] -> smem -> TMA store (DO is double-buffered in TMEM).
 // Roofline: HBM (intensity ~172 FLOP/B at the algorithmic minimum of 1032 B per token-head).
 #include <cuda.h>
 
@@ -52,12 +54,12 @@ constexpr int NCHAIN = 256;
 constexpr int BAR_PREP = 1, BAR_CHAIN = 2;
 
 // TMEM column map (512 columns, f32 accumulators unless noted)
-constexpr uint32_t TM_S = 0;     // S^T bf16 A operand: 64 cols (128 keys, 2 per column)
-constexpr uint32_t TM_D1 = 64;   // [0,64) K S (-> R^T bf16 in place), [64,128) Q S
-constexpr uint32_t TM_D2 = 192;  // Delta^T f32 (-> scaled / plain bf16 in place)
-constexpr uint32_t TM_D3 = 256;  // (Gamma Delta)^T K, 128 cols
-constexpr uint32_t TM_DO = 384;  // Delta^T P^T, 64 cols
-constexpr uint32_t TM_KK = 448;  // prep: [K;Q] K^T, 64 cols
+constexpr uint32_t TM_S = 0;      // S^T bf16 A operand: 64 cols (128 keys, 2 per column)
+constexpr uint32_t TM_D1 = 64;    // K S (64 cols) -> R^T as a bf16 hi/lo pair in place
+constexpr uint32_t TM_D2 = 128;   // Delta^T (64 cols) -> scaled / plain bf16 in place
+constexpr uint32_t TM_D3 = 192;   // (Gamma Delta)^T K, 128 cols
+constexpr uint32_t TM_DO = 320;   // output accumulators, 2 x 64 cols (double-buffered by chunk)
+constexpr uint32_t TM_KK = 448;   // prep: [K;Q] K^T, 64 cols
 
 // Shared memory (offsets from a 1024-aligned base)
 constexpr uint32_t X_BYTES = 2 * 128 * 128;  // 2 key blocks x 128 rows ([K;Q]) x 128 B, swizzled
@@ -82,7 +84,8 @@ constexpr uint32_t NBARS = 11;
 constexpr uint32_t OFF_TSLOT = OFF_BAR + NBARS * 8;
 constexpr uint32_t SMEM_BYTES = OFF_TSLOT + 16 + 1024;  // + alignment slack
 // gate arrays inside a stage's G region (floats)
-constexpr int G_CB = 0, G_CG = 64, G_CD = 128, G_CQ = 192, G_VAL = 256, G_GC = 320;
+constexpr int G_CB = 0, G_CG = 64, G_CD = 128, G_OM = 192, G_VAL = 256, G_GC = 320, G_QZ = 384;
+constexpr float kTinyDecay = 7.888609052210118e-31f;  // 2^-100: a smaller gamma_r counts as zero
 
 constexpr uint32_t IDESC_M128_N64 = umma_idesc_bf16(128, 64, false);
 constexpr uint32_t IDESC_M128_N128 = umma_idesc_bf16(128, 128, false);
@@ -241,7 +244,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 G[G_CB + tid] = be;
                 G[G_CG + tid] = be * gamma;
                 G[G_CD + tid] = (cC == z) ? exp2f(gC - lg) : 0.f;
-                G[G_CQ + tid] = gamma * p.scale;
+                // output multiplier: O_r = om_r (Q S + P~ Delta)_r with P~ = P / om_r
+                G[G_OM + tid] = (gamma > kTinyDecay ? gamma : 1.f) * p.scale;
+                G[G_QZ + tid] = gamma > kTinyDecay ? 0.f : 1.f;  // the row's Q S term is dropped
                 G[G_VAL + tid] = vf;
                 if (tid == C - 1) G[G_GC] = gamma;
             }
@@ -286,30 +291,44 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         sA[r * LDA + sidx] = v;
                     }
                 } else {
-                    // P = scale Gamma o Q K^T (s <= r) as a bf16 pair hi + lo
-                    const float sr = p.scale * er;
-                    uint32_t ph[16], pl[16];
-#pragma unroll
-                    for (int e = 0; e < 32; e += 2) {
-                        float v2[2];
-#pragma unroll
-                        for (int u = 0; u < 2; ++u) {
-                            const int sidx = 32 * half + e + u;
-                            const float gv = __uint_as_float(e + u < 16 ? g0[e + u] : g1[e + u - 16]);
-                            if (fast) v2[u] = sidx <= r ? sr * gv * sem[sidx] : 0.f;
-                            else v2[u] = (sidx <= r && scnt[sidx] == cr) ? p.scale * exp2f(gr - sg[sidx]) * gv : 0.f;
-                        }
-                        ph[e >> 1] = pack_bf16x2(v2[0], v2[1]);
-                        pl[e >> 1] = pack_bf16x2(v2[0] - bf16_lo(ph[e >> 1]), v2[1] - bf16_hi(ph[e >> 1]));
-                    }
+                    // P~ = (scale Gamma o Q K^T, s <= r) / om_r as a bf16 pair hi + lo.  Fast path:
+                    // om_r = scale 2^g_r, so P~[r][s] = 2^-g_s (q_r . k_s).  16 columns at a time.
+                    const float inv_om = p.scale / G[G_OM + r];
                     uint8_t* P = stP(s);
 #pragma unroll
-                    for (int x = 0; x < 4; ++x) {
-                        const int cc = 4 * half + x;
-                        const int off = r * 128 + ((cc ^ (r & 7)) << 4);
-                        *reinterpret_cast<uint4*>(P + off) = make_uint4(ph[4 * x], ph[4 * x + 1], ph[4 * x + 2], ph[4 * x + 3]);
-                        *reinterpret_cast<uint4*>(P + C * 128 + off) =
-                            make_uint4(pl[4 * x], pl[4 * x + 1], pl[4 * x + 2], pl[4 * x + 3]);
+                    for (int hc = 0; hc < 2; ++hc) {
+                        uint32_t ph[8], pl[8];
+#pragma unroll
+                        for (int e = 0; e < 16; e += 2) {
+                            float v2[2];
+#pragma unroll
+                            for (int u = 0; u < 2; ++u) {
+                                const int sidx = 32 * half + 16 * hc + e + u;
+                                const float gv = __uint_as_float(hc == 0 ? g0[e + u] : g1[e + u]);
+                                if (fast) v2[u] = sidx <= r ? gv * sem[sidx] : 0.f;
+                                else v2[u] = (sidx <= r && scnt[sidx] == cr) ? inv_om * exp2f(gr - sg[sidx]) * gv : 0.f;
+                            }
+                            ph[e >> 1] = pack_bf16x2(v2[0], v2[1]);
+                            pl[e >> 1] = pack_bf16x2(v2[0] - bf16_lo(ph[e >> 1]), v2[1] - bf16_hi(ph[e >> 1]));
+                        }
+#pragma unroll
+                        for (int x = 0; x < 2; ++x) {
+                            const int cc = 4 * half + 2 * hc + x;
+                            const int off = r * 128 + ((cc ^ (r & 7)) << 4);
+                            *reinterpret_cast<uint4*>(P + off) = make_uint4(ph[4 * x], ph[4 * x + 1], ph[4 * x + 2], ph[4 * x + 3]);
+                            *reinterpret_cast<uint4*>(P + C * 128 + off) =
+                                make_uint4(pl[4 * x], pl[4 * x + 1], pl[4 * x + 2], pl[4 * x + 3]);
+                        }
+                    }
+                    if (G[G_QZ + r] != 0.f) {
+                        // gamma_r is zero (or below 2^-100): drop the row's Q S term by zeroing its Q row
+                        uint8_t* X = stX(s);
+#pragma unroll
+                        for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+                            for (int x = 0; x < 4; ++x)
+                                *reinterpret_cast<uint4*>(X + kb * 16384 + (64 + r) * 128 + 64 * half + 16 * x) =
+                                    make_uint4(0, 0, 0, 0);
                     }
                 }
             }
@@ -341,7 +360,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             // ---- off-diagonal blocks, by distance d from the diagonal:
             //      T[b][a] = -T[b][b] (sum_{a <= m < b} A[b][m] T[m][a]).  A thread computes 4 columns of
             //      one 16-long piece of the m-sum (d pieces per output), the next phase adds the pieces.
-#pragma unroll 1
+#pragma unroll
             for (int d = 1; d < 4; ++d) {
                 const int units = (4 - d) * 64;  // (block, row, column quad)
                 if (tid < units * d) {
@@ -375,6 +394,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         const float t = Trow[m];
                         const int um = (blk << 6) | (m << 2) | cq;  // unit (blk, row m, cq)
                         float4 x4 = *reinterpret_cast<const float4*>(sXs + um * 4);
+#pragma unroll
                         for (int pc = 1; pc < d; ++pc) {
                             const float4 y = *reinterpret_cast<const float4*>(sXs + (pc * units + um) * 4);
                             x4.x += y.x;
@@ -433,110 +453,122 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 tmem_st8(tl + TM_S + 32 * hh + 8 * pc, pk);
             }
         };
+        // MMA1 of chunk c: D1[j][r] = sum_i S^T[j][i] K[r][i]   (issued by the chain leader)
+        auto issue_mma1 = [&](int c) {
+            mbar_wait(&bar_prep[c & 1], (c >> 1) & 1, p.err, 4);
+            tc_fence_after();
+            const uint8_t* X = stX(c & 1);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+                umma_ts(tmem + TM_D1, tmem + TM_S + 8 * kk, kdesc(X + (kk >> 2) * 16384 + (kk & 3) * 32),
+                        IDESC_M128_N64, kk > 0 ? 1u : 0u);
+            umma_commit(bar_m1);
+        };
         store_state_bf16();
         tmem_st_wait();
         tc_fence_before();
         named_bar_sync(BAR_CHAIN, NCHAIN);
+        if (ct == 0) issue_mma1(0);
 
         for (int c = 0; c < nchunks; ++c) {
             const int s = c & 1;
             const uint32_t par = c & 1;
+            const uint32_t tm_do = TM_DO + 64 * (c & 1);
             mbar_wait(&bar_prep[s], (c >> 1) & 1, p.err, 4);
             const float* G = stG(s);
-            // ---- MMA1: D1 = S^T [K;Q]^T
-            if (ct == 0) {
-                tc_fence_after();
-                const uint8_t* X = stX(s);
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                    umma_ts(tmem + TM_D1, tmem + TM_S + 8 * kk, kdesc(X + (kk >> 2) * 16384 + (kk & 3) * 32),
-                            IDESC_M128_N128, kk > 0 ? 1u : 0u);
-                umma_commit(bar_m1);
-            }
             mbar_wait(bar_m1, par, p.err, 5);
             tc_fence_after();
             // ---- E1: R^T[j][r] = beta_r V[r][j] - beta_r gamma_r (K S)[r][j],  r in [32 hh, 32 hh + 32),
-            //      written in place as a bf16 pair: hi at columns [32 hh, +16), lo at [32 hh + 16, +16)
+            //      written in place as a bf16 pair: for the 16 rows r of TMEM columns [16k, 16k + 16),
+            //      hi goes to columns [16k, +8) and lo to [16k + 8, +8)
             {
-                uint32_t a[32];
-                tmem_ld16(tl + TM_D1 + 32 * hh, *reinterpret_cast<uint32_t(*)[16]>(&a[0]));
-                tmem_ld16(tl + TM_D1 + 32 * hh + 16, *reinterpret_cast<uint32_t(*)[16]>(&a[16]));
-                tmem_ld_wait();
                 const __nv_bfloat16* Vs = reinterpret_cast<const __nv_bfloat16*>(stV(s));
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const int r = 32 * hh + e;
-                    const float vv = p.v_zero ? 0.f : __bfloat162float(Vs[r * 128 + j]);
-                    a[e] = __float_as_uint(G[G_CB + r] * vv - G[G_CG + r] * __uint_as_float(a[e]));
-                }
-#pragma unroll
                 for (int pc = 0; pc < 2; ++pc) {
+                    const uint32_t col = TM_D1 + 32 * hh + 16 * pc;
+                    uint32_t a[16];
+                    tmem_ld16(tl + col, a);
+                    tmem_ld_wait();
                     uint32_t hi[8], lo[8];
 #pragma unroll
                     for (int u = 0; u < 8; ++u) {
-                        const float x0 = __uint_as_float(a[16 * pc + 2 * u]), x1 = __uint_as_float(a[16 * pc + 2 * u + 1]);
-                        hi[u] = pack_bf16x2(x0, x1);
-                        lo[u] = pack_bf16x2(x0 - bf16_lo(hi[u]), x1 - bf16_hi(hi[u]));
+                        float x[2];
+#pragma unroll
+                        for (int w = 0; w < 2; ++w) {
+                            const int r = 32 * hh + 16 * pc + 2 * u + w;
+                            const float vv = p.v_zero ? 0.f : __bfloat162float(Vs[r * 128 + j]);
+                            x[w] = G[G_CB + r] * vv - G[G_CG + r] * __uint_as_float(a[2 * u + w]);
+                        }
+                        hi[u] = pack_bf16x2(x[0], x[1]);
+                        lo[u] = pack_bf16x2(x[0] - bf16_lo(hi[u]), x[1] - bf16_hi(hi[u]));
                     }
-                    tmem_st8(tl + TM_D1 + 32 * hh + 8 * pc, hi);
-                    tmem_st8(tl + TM_D1 + 32 * hh + 16 + 8 * pc, lo);
+                    tmem_st8(tl + col, hi);
+                    tmem_st8(tl + col + 8, lo);
                 }
                 tmem_st_wait();
             }
             tc_fence_before();
             named_bar_sync(BAR_CHAIN, NCHAIN);
-            // ---- MMA2: D2[j][r'] = sum_r R^T[j][r] T[r'][r]
+            // ---- MMA2: D2[j][r'] = sum_r R^T[j][r] T[r'][r]   (hi and lo accumulate)
             if (ct == 0) {
                 tc_fence_after();
                 const uint8_t* Tt = stT(s);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
-                    const uint32_t ra = tmem + TM_D1 + (kk >> 1) * 32 + (kk & 1) * 8;
+                    const uint32_t ra = tmem + TM_D1 + 16 * kk;
                     umma_ts(tmem + TM_D2, ra, kdesc(Tt + kk * 32), IDESC_M128_N64, kk > 0 ? 1u : 0u);
-                    umma_ts(tmem + TM_D2, ra + 16, kdesc(Tt + kk * 32), IDESC_M128_N64, 1u);
+                    umma_ts(tmem + TM_D2, ra + 8, kdesc(Tt + kk * 32), IDESC_M128_N64, 1u);
                 }
                 umma_commit(bar_m2);
             }
             mbar_wait(bar_m2, par, p.err, 6);
             tc_fence_after();
-            // ---- E2: Delta^T for r' in [32 hh, 32 hh + 32): scaled copy and plain copy, bf16
+            // ---- E2: Delta^T for r' in [32 hh, 32 hh + 32) as bf16, in place: for the 16 rows of
+            //      columns [16k, 16k + 16), the Gamma[63][r']-scaled copy goes to [16k, +8) and the plain
+            //      copy to [16k + 8, +8)
             {
-                uint32_t d[32];
-                tmem_ld16(tl + TM_D2 + 32 * hh, *reinterpret_cast<uint32_t(*)[16]>(&d[0]));
-                tmem_ld16(tl + TM_D2 + 32 * hh + 16, *reinterpret_cast<uint32_t(*)[16]>(&d[16]));
-                tmem_ld_wait();
 #pragma unroll
-                for (int pc = 0; pc < 4; ++pc) {  // pc 0,1: scaled copy; pc 2,3: plain copy
-                    uint32_t pk[8];
+                for (int pc = 0; pc < 2; ++pc) {
+                    const uint32_t col = TM_D2 + 32 * hh + 16 * pc;
+                    uint32_t d[16];
+                    tmem_ld16(tl + col, d);
+                    tmem_ld_wait();
+                    uint32_t ps[8], pp[8];
 #pragma unroll
                     for (int u = 0; u < 8; ++u) {
-                        const int e = 16 * (pc & 1) + 2 * u;
-                        const int r = 32 * hh + e;
-                        const float x0 = __uint_as_float(d[e]), x1 = __uint_as_float(d[e + 1]);
-                        pk[u] = pc < 2 ? pack_bf16x2(x0 * G[G_CD + r], x1 * G[G_CD + r + 1]) : pack_bf16x2(x0, x1);
+                        const int r = 32 * hh + 16 * pc + 2 * u;
+                        const float x0 = __uint_as_float(d[2 * u]), x1 = __uint_as_float(d[2 * u + 1]);
+                        ps[u] = pack_bf16x2(x0 * G[G_CD + r], x1 * G[G_CD + r + 1]);
+                        pp[u] = pack_bf16x2(x0, x1);
                     }
-                    tmem_st8(tl + TM_D2 + 32 * hh + 8 * pc, pk);
+                    tmem_st8(tl + col, ps);
+                    tmem_st8(tl + col + 8, pp);
                 }
                 tmem_st_wait();
             }
             tc_fence_before();
             named_bar_sync(BAR_CHAIN, NCHAIN);
-            // ---- MMA3 (state update) and MMA2b (intra-chunk output)
+            // ---- MMA3: D3 = (Gamma Delta)^T K (state increment); DO = S^T Q^T + Delta^T P~^T (output,
+            //      issued now because S^T in TMEM is still the chunk-start state)
             if (ct == 0) {
                 tc_fence_after();
                 const uint8_t* X = stX(s);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                    umma_ts(tmem + TM_D3, tmem + TM_D2 + (kk >> 1) * 32 + (kk & 1) * 8,
+                    umma_ts(tmem + TM_D3, tmem + TM_D2 + 16 * kk,
                             umma_sdesc_sw128(smem_u32addr(X + kk * 2048), 16384, 1024), IDESC_M128_N128_BMN,
                             kk > 0 ? 1u : 0u);
                 if (p.write_out) {
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk)
+                        umma_ts(tmem + tm_do, tmem + TM_S + 8 * kk, kdesc(X + (kk >> 2) * 16384 + 8192 + (kk & 3) * 32),
+                                IDESC_M128_N64, kk > 0 ? 1u : 0u);
                     const uint8_t* P = stP(s);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
-                        const uint32_t da = tmem + TM_D2 + (kk >> 1) * 32 + 16 + (kk & 1) * 8;
-                        umma_ts(tmem + TM_DO, da, kdesc(P + kk * 32), IDESC_M128_N64, kk > 0 ? 1u : 0u);
-                        umma_ts(tmem + TM_DO, da, kdesc(P + C * 128 + kk * 32), IDESC_M128_N64, 1u);
+                        const uint32_t da = tmem + TM_D2 + 16 * kk + 8;
+                        umma_ts(tmem + tm_do, da, kdesc(P + kk * 32), IDESC_M128_N64, 1u);
+                        umma_ts(tmem + tm_do, da, kdesc(P + C * 128 + kk * 32), IDESC_M128_N64, 1u);
                     }
                 }
                 umma_commit(bar_m3);
@@ -557,26 +589,28 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     for (int e = 0; e < 32; ++e) S[32 * pc + e] = fmaf(gC, S[32 * pc + e], __uint_as_float(d[e]));
                 }
                 store_state_bf16();
+                tmem_st_wait();
             }
+            tc_fence_before();
+            named_bar_sync(BAR_CHAIN, NCHAIN);
+            // the recurrence moves on: MMA1 of the next chunk runs while this chunk's output is written
+            if (ct == 0 && c + 1 < nchunks) issue_mma1(c + 1);
             if (p.write_out) {
-                named_bar_sync(BAR_CHAIN, NCHAIN);  // output staging buffer is free
                 __nv_bfloat16* Os = reinterpret_cast<__nv_bfloat16*>(Ost);
 #pragma unroll
                 for (int pc = 0; pc < 2; ++pc) {
-                    uint32_t a[16], o[16];
-                    tmem_ld16(tl + TM_D1 + 64 + 32 * hh + 16 * pc, a);
-                    tmem_ld16(tl + TM_DO + 32 * hh + 16 * pc, o);
+                    uint32_t o[16];
+                    tmem_ld16(tl + tm_do + 32 * hh + 16 * pc, o);
                     tmem_ld_wait();
 #pragma unroll
                     for (int e = 0; e < 16; ++e) {
                         const int r = 32 * hh + 16 * pc + e;
-                        const float v = G[G_VAL + r] != 0.f ? fmaf(G[G_CQ + r], __uint_as_float(a[e]), __uint_as_float(o[e])) : 0.f;
+                        const float v = G[G_VAL + r] != 0.f ? G[G_OM + r] * __uint_as_float(o[e]) : 0.f;
                         Os[r * 128 + j] = __float2bfloat16_rn(v);
                     }
                 }
                 fence_proxy_async_smem();
             }
-            tmem_st_wait();
             tc_fence_before();
             named_bar_sync(BAR_CHAIN, NCHAIN);
             if (ct == 0) {
