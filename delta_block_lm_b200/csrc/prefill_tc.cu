@@ -13,13 +13,13 @@
 //   S' = gamma_63 S + (diag(Gamma[63][r]) K)^T Delta
 // Padding tokens get beta = 0 and alpha = 1 (their edit is exactly zero) and output 0.
 //
-// B200 mapping.  One CTA per (b, h), 512 threads, one CTA per SM (all 512 TMEM columns).
-//   * prep warps 0-7: TMA loads of the chunk tiles (K and Q 128-byte swizzled, V plain), the gate
+// B200 mapping.  One CTA per (b, h), 384 threads, one CTA per SM (all 512 TMEM columns).
+//   * prep warps 0-3: TMA loads of the chunk tiles (K and Q 128-byte swizzled, V plain), the gate
 //     scan, UMMA [K;Q] K^T -> TMEM, decay masks, the blocked 64x64 unit-lower inverse (16x16
 //     diagonal blocks by substitution, off-diagonal blocks level by level), T and P written as
 //     bf16 UMMA operands.  Prep runs one chunk ahead of the chain (two smem stages); the chain
 //     leader issues the loads of chunk c + 2 as soon as it is done with chunk c.
-//   * chain warps 8-15: the state-dependent chain, transposed so that the value column j of the
+//   * chain warps 4-11: the state-dependent chain, transposed so that the value column j of the
 //     state is TMEM lane j and every activation stays in TMEM (A operands of the TS form):
 //       MMA1  D1[j][r]  = sum_i S^T[j][i] K[r][i]          (A = S^T bf16 in TMEM)
 //       E1    R^T[j][r] = beta_r V[r][j] - beta_r gamma_r D1[j][r]   -> TMEM (bf16 hi + lo pair)
@@ -48,9 +48,9 @@ namespace {
 
 constexpr int C = 64;
 constexpr int DK = 128;
-constexpr int NTHREADS = 512;
-constexpr int NPREP = 256;
-constexpr int NCHAIN = 256;
+constexpr int NTHREADS = 384;
+constexpr int NPREP = 128;   // warps 0-3 (one TMEM lane quadrant each)
+constexpr int NCHAIN = 256;  // warps 4-11
 constexpr int BAR_PREP = 1, BAR_CHAIN = 2;
 
 // TMEM column map (512 columns, f32 accumulators unless noted)
@@ -79,7 +79,8 @@ constexpr uint32_t OFF_SG = OFF_SX + 1024 * 4;
 constexpr uint32_t OFF_SEM = OFF_SG + 64 * 4;   // 2^-g_s (fast decay path)
 constexpr uint32_t OFF_SCNT = OFF_SEM + 64 * 4;
 constexpr uint32_t OFF_SWT = OFF_SCNT + 64 * 4;
-constexpr uint32_t OFF_BAR = (OFF_SWT + 64 + 7) / 8 * 8;
+constexpr uint32_t OFF_COM = OFF_SWT + 64;        // chain copy of the output multipliers [2][64]
+constexpr uint32_t OFF_BAR = (OFF_COM + 2 * 64 * 4 + 7) / 8 * 8;
 constexpr uint32_t NBARS = 11;
 constexpr uint32_t OFF_TSLOT = OFF_BAR + NBARS * 8;
 constexpr uint32_t SMEM_BYTES = OFF_TSLOT + 16 + 1024;  // + alignment slack
@@ -132,6 +133,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     float* swt = reinterpret_cast<float*>(smem + OFF_SWT);
     int* swc = reinterpret_cast<int*>(smem + OFF_SWT + 32);
     uint8_t* Ost = smem + OFF_O;
+    float* com = reinterpret_cast<float*>(smem + OFF_COM);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int bh = blockIdx.x;
@@ -175,9 +177,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (!p.v_zero) tma_load_4d(stV(s), &tm_v, &bar_full[s], 0, c * C, h, b);
     };
 
-    if (warp < 8) {
+    if (warp < 4) {
         // =================================================================== prep warps
-        const int q = warp & 3, half = warp >> 2;
+        const int q = warp;
         if (tid == 0) {
             issue_loads(0);
             if (nchunks > 1) issue_loads(1);
@@ -265,12 +267,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             mbar_wait(bar_kk, c & 1, p.err, 2);
             tc_fence_after();
             {
-                // row n = 32q + lane of [K;Q]; columns s in [32 half, 32 half + 32)
-                uint32_t g0[16], g1[16];
-                const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + TM_KK + 32 * half;
-                tmem_ld16(ta, g0);
-                tmem_ld16(ta + 16, g1);
-                tmem_ld_wait();
+                // row n = 32q + lane of [K;Q]; all 64 columns s, 16 at a time
                 const int n = 32 * q + lane;
                 const int r = n & 63;
                 const float gr = sg[r];
@@ -278,33 +275,37 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 // Fast path: no zero decay in the chunk and a bounded total decay, so
                 // Gamma[r][s] = 2^g_r 2^-g_s is a rank-1 product (no exponential per element).
                 const bool fast = scnt[C - 1] == 0 && sg[C - 1] > -100.f;
-                const float er = exp2f(gr);
-                if (n < C) {
-                    const float br = G[G_CB + r] * er;
+                const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + TM_KK;
+                uint8_t* P = stP(s);
+                const float br = G[G_CB + r];
+                const float brer = br * exp2f(gr);
+                const float inv_om = p.scale / G[G_OM + r];
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        const int sidx = 32 * half + e;
-                        const float gv = __uint_as_float(e < 16 ? g0[e] : g1[e - 16]);
-                        float v;
-                        if (fast) v = sidx < r ? br * gv * sem[sidx] : 0.f;
-                        else v = (sidx < r && scnt[sidx] == cr) ? G[G_CB + r] * exp2f(gr - sg[sidx]) * gv : 0.f;
-                        sA[r * LDA + sidx] = v;
-                    }
-                } else {
-                    // P~ = (scale Gamma o Q K^T, s <= r) / om_r as a bf16 pair hi + lo.  Fast path:
-                    // om_r = scale 2^g_r, so P~[r][s] = 2^-g_s (q_r . k_s).  16 columns at a time.
-                    const float inv_om = p.scale / G[G_OM + r];
-                    uint8_t* P = stP(s);
+                for (int pc = 0; pc < 4; ++pc) {
+                    uint32_t g[16];
+                    tmem_ld16(ta + 16 * pc, g);
+                    tmem_ld_wait();
+                    if (n < C) {
 #pragma unroll
-                    for (int hc = 0; hc < 2; ++hc) {
+                        for (int e = 0; e < 16; ++e) {
+                            const int sidx = 16 * pc + e;
+                            const float gv = __uint_as_float(g[e]);
+                            float v;
+                            if (fast) v = sidx < r ? brer * gv * sem[sidx] : 0.f;
+                            else v = (sidx < r && scnt[sidx] == cr) ? br * exp2f(gr - sg[sidx]) * gv : 0.f;
+                            sA[r * LDA + sidx] = v;
+                        }
+                    } else {
+                        // P~ = (scale Gamma o Q K^T, s <= r) / om_r as a bf16 pair hi + lo.  Fast path:
+                        // om_r = scale 2^g_r, so P~[r][s] = 2^-g_s (q_r . k_s).
                         uint32_t ph[8], pl[8];
 #pragma unroll
                         for (int e = 0; e < 16; e += 2) {
                             float v2[2];
 #pragma unroll
                             for (int u = 0; u < 2; ++u) {
-                                const int sidx = 32 * half + 16 * hc + e + u;
-                                const float gv = __uint_as_float(hc == 0 ? g0[e + u] : g1[e + u]);
+                                const int sidx = 16 * pc + e + u;
+                                const float gv = __uint_as_float(g[e + u]);
                                 if (fast) v2[u] = sidx <= r ? gv * sem[sidx] : 0.f;
                                 else v2[u] = (sidx <= r && scnt[sidx] == cr) ? inv_om * exp2f(gr - sg[sidx]) * gv : 0.f;
                             }
@@ -313,23 +314,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         }
 #pragma unroll
                         for (int x = 0; x < 2; ++x) {
-                            const int cc = 4 * half + 2 * hc + x;
+                            const int cc = 2 * pc + x;
                             const int off = r * 128 + ((cc ^ (r & 7)) << 4);
                             *reinterpret_cast<uint4*>(P + off) = make_uint4(ph[4 * x], ph[4 * x + 1], ph[4 * x + 2], ph[4 * x + 3]);
                             *reinterpret_cast<uint4*>(P + C * 128 + off) =
                                 make_uint4(pl[4 * x], pl[4 * x + 1], pl[4 * x + 2], pl[4 * x + 3]);
                         }
                     }
-                    if (G[G_QZ + r] != 0.f) {
-                        // gamma_r is zero (or below 2^-100): drop the row's Q S term by zeroing its Q row
-                        uint8_t* X = stX(s);
+                }
+                if (n >= C && G[G_QZ + r] != 0.f) {
+                    // gamma_r is zero (or below 2^-100): drop the row's Q S term by zeroing its Q row
+                    uint8_t* X = stX(s);
 #pragma unroll
-                        for (int kb = 0; kb < 2; ++kb)
+                    for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
-                            for (int x = 0; x < 4; ++x)
-                                *reinterpret_cast<uint4*>(X + kb * 16384 + (64 + r) * 128 + 64 * half + 16 * x) =
-                                    make_uint4(0, 0, 0, 0);
-                    }
+                        for (int x = 0; x < 8; ++x)
+                            *reinterpret_cast<uint4*>(X + kb * 16384 + (64 + r) * 128 + 16 * x) = make_uint4(0, 0, 0, 0);
                 }
             }
             tc_fence_before();
@@ -349,7 +349,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                 for (int r = 0; r < 16; ++r) sT[(16 * blk + r) * LDT + 16 * blk + c0] = x[r];
             } else {
-                for (int e = tid - C; e < 6 * 256; e += NPREP - C) {
+                for (int e = tid - C; e < 6 * 256; e += NPREP - C) {  // 64 threads
                     const int pair = e >> 8, rem = e & 255;
                     const int bb = pair < 3 ? 0 : (pair < 5 ? 1 : 2);
                     const int aa = pair < 3 ? pair + 1 : (pair < 5 ? pair - 1 : 3);
@@ -363,8 +363,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
             for (int d = 1; d < 4; ++d) {
                 const int units = (4 - d) * 64;  // (block, row, column quad)
-                if (tid < units * d) {
-                    const int pc = tid / units, u = tid - pc * units;
+                for (int w = tid; w < units * d; w += NPREP) {
+                    const int pc = w / units, u = w - pc * units;
                     const int blk = u >> 6, r = (u >> 2) & 15, cq = u & 3;
                     const int bb = d + blk, aa = bb - d;
                     const int m0 = 16 * (aa + pc);
@@ -383,8 +383,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     *reinterpret_cast<float4*>(sXs + (pc * units + u) * 4) = acc;
                 }
                 named_bar_sync(BAR_PREP, NPREP);
-                if (tid < units) {
-                    const int u = tid;
+                for (int u = tid; u < units; u += NPREP) {
                     const int blk = u >> 6, r = (u >> 2) & 15, cq = u & 3;
                     const int bb = d + blk, aa = bb - d;
                     const float* Trow = sT + (16 * bb + r) * LDT + 16 * bb;
@@ -431,7 +430,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     } else {
         // =================================================================== chain warps
         const int ct = tid - NPREP;
-        const int q = warp & 3, hh = (warp - 8) >> 2;
+        const int q = warp & 3, hh = (warp - 4) >> 2;
         const int j = 32 * q + lane;  // state value column == TMEM lane
         const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16);
         float S[64];  // S[i][j], i = 64 hh + e
@@ -476,6 +475,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const uint32_t tm_do = TM_DO + 64 * (c & 1);
             mbar_wait(&bar_prep[s], (c >> 1) & 1, p.err, 4);
             const float* G = stG(s);
+            // private copy of what this chunk's output needs, so stage s can be reloaded early
+            float* om = com + 64 * (c & 1);
+            if (ct < C) om[ct] = G[G_VAL + ct] != 0.f ? G[G_OM + ct] : 0.f;
+            const float gC = G[G_GC];
             mbar_wait(bar_m1, par, p.err, 5);
             tc_fence_after();
             // ---- E1: R^T[j][r] = beta_r V[r][j] - beta_r gamma_r (K S)[r][j],  r in [32 hh, 32 hh + 32),
@@ -576,9 +579,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             mbar_wait(bar_m3, par, p.err, 7);
             tc_fence_after();
+            // every MMA and every E-stage read of stage s is done: load chunk c + 2 into it now
+            if (ct == 0 && c + 2 < nchunks) issue_loads(c + 2);
             // ---- E3: state update (f32 master copy) and its bf16 image for the next MMA1
             {
-                const float gC = G[G_GC];
 #pragma unroll
                 for (int pc = 0; pc < 2; ++pc) {
                     uint32_t d[32];
@@ -605,7 +609,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                     for (int e = 0; e < 16; ++e) {
                         const int r = 32 * hh + 16 * pc + e;
-                        const float v = G[G_VAL + r] != 0.f ? G[G_OM + r] * __uint_as_float(o[e]) : 0.f;
+                        const float v = om[r] * __uint_as_float(o[e]);
                         Os[r * 128 + j] = __float2bfloat16_rn(v);
                     }
                 }
@@ -618,8 +622,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     tma_store_4d(&tm_o, Ost, 0, c * C, h, b);
                     tma_store_commit();
                 }
-                // the chain is done with stage s: it takes chunk c + 2 at once
-                if (c + 2 < nchunks) issue_loads(c + 2);
             }
         }
         if (p.final_state) {
