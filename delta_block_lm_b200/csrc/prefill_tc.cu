@@ -16,7 +16,8 @@
 // B200 mapping.  One CTA per (b, h), 384 threads, one CTA per SM (all 512 TMEM columns).
 //   * prep warps 0-3: TMA loads of the chunk tiles (K and Q 128-byte swizzled, V plain), the gate
 //     scan, UMMA [K;Q] K^T -> TMEM, decay masks, the blocked 64x64 unit-lower inverse (16x16
-//     diagonal blocks by substitution, off-diagonal blocks level by level), T and P written as
+//     diagonal blocks by substitution, off-diagonal blocks level by level on mma.sync tf32 tiles),
+//     T and P written as
 //     bf16 UMMA operands.  Prep runs one chunk ahead of the chain (two smem stages); the chain
 //     leader issues the loads of chunk c + 2 as soon as it is done with chunk c.
 //   * chain warps 4-11: the state-dependent chain, transposed so that the value column j of the
@@ -280,11 +281,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const float br = G[G_CB + r];
                 const float brer = br * exp2f(gr);
                 const float inv_om = p.scale / G[G_OM + r];
+                uint32_t gall[64];
+#pragma unroll
+                for (int pc = 0; pc < 4; ++pc) tmem_ld16(ta + 16 * pc, *reinterpret_cast<uint32_t(*)[16]>(&gall[16 * pc]));
+                tmem_ld_wait();
 #pragma unroll
                 for (int pc = 0; pc < 4; ++pc) {
-                    uint32_t g[16];
-                    tmem_ld16(ta + 16 * pc, g);
-                    tmem_ld_wait();
+                    const uint32_t* g = gall + 16 * pc;
                     if (n < C) {
 #pragma unroll
                         for (int e = 0; e < 16; ++e) {
@@ -357,59 +360,61 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
             }
             named_bar_sync(BAR_PREP, NPREP);
-            // ---- off-diagonal blocks, by distance d from the diagonal:
-            //      T[b][a] = -T[b][b] (sum_{a <= m < b} A[b][m] T[m][a]).  A thread computes 4 columns of
-            //      one 16-long piece of the m-sum (d pieces per output), the next phase adds the pieces.
+            // ---- off-diagonal blocks, by distance d from the diagonal, on tensor cores (mma.sync tf32,
+            //      one warp per 16 x 16 block): X = sum_{a <= m < b} A[b][m] T[m][a], T[b][a] = -T[b][b] X
+            {
+                const int g = lane >> 2, t4 = lane & 3;
 #pragma unroll
-            for (int d = 1; d < 4; ++d) {
-                const int units = (4 - d) * 64;  // (block, row, column quad)
-                for (int w = tid; w < units * d; w += NPREP) {
-                    const int pc = w / units, u = w - pc * units;
-                    const int blk = u >> 6, r = (u >> 2) & 15, cq = u & 3;
-                    const int bb = d + blk, aa = bb - d;
-                    const int m0 = 16 * (aa + pc);
-                    const float* Arow = sA + (16 * bb + r) * LDA + m0;
-                    const float* Tcol = sT + m0 * LDT + 16 * aa + 4 * cq;
-                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int d = 1; d < 4; ++d) {
+                    const int bb = d + warp, aa = warp;  // warp = block index within the level
+                    if (warp < 4 - d) {
+                        float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-                    for (int m = 0; m < 16; ++m) {
-                        const float av = Arow[m];
-                        const float4 t4 = *reinterpret_cast<const float4*>(Tcol + m * LDT);
-                        acc.x = fmaf(av, t4.x, acc.x);
-                        acc.y = fmaf(av, t4.y, acc.y);
-                        acc.z = fmaf(av, t4.z, acc.z);
-                        acc.w = fmaf(av, t4.w, acc.w);
-                    }
-                    *reinterpret_cast<float4*>(sXs + (pc * units + u) * 4) = acc;
-                }
-                named_bar_sync(BAR_PREP, NPREP);
-                for (int u = tid; u < units; u += NPREP) {
-                    const int blk = u >> 6, r = (u >> 2) & 15, cq = u & 3;
-                    const int bb = d + blk, aa = bb - d;
-                    const float* Trow = sT + (16 * bb + r) * LDT + 16 * bb;
-                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                        for (int ks = 0; ks < 2 * d; ++ks) {
+                            const int m0 = 16 * aa + 8 * ks;
+                            const float* Ar = sA + (16 * bb + g) * LDA + m0 + t4;
+                            const uint32_t a0 = to_tf32(Ar[0]), a1 = to_tf32(Ar[8 * LDA]);
+                            const uint32_t a2 = to_tf32(Ar[4]), a3 = to_tf32(Ar[8 * LDA + 4]);
 #pragma unroll
-                    for (int m = 0; m < 16; ++m) {
-                        const float t = Trow[m];
-                        const int um = (blk << 6) | (m << 2) | cq;  // unit (blk, row m, cq)
-                        float4 x4 = *reinterpret_cast<const float4*>(sXs + um * 4);
-#pragma unroll
-                        for (int pc = 1; pc < d; ++pc) {
-                            const float4 y = *reinterpret_cast<const float4*>(sXs + (pc * units + um) * 4);
-                            x4.x += y.x;
-                            x4.y += y.y;
-                            x4.z += y.z;
-                            x4.w += y.w;
+                            for (int nt = 0; nt < 2; ++nt) {
+                                const float* Tc = sT + (m0 + t4) * LDT + 16 * aa + 8 * nt + g;
+                                mma_tf32_16x8x8(c[nt], a0, a1, a2, a3, to_tf32(Tc[0]), to_tf32(Tc[4 * LDT]));
+                            }
                         }
-                        acc.x = fmaf(t, x4.x, acc.x);
-                        acc.y = fmaf(t, x4.y, acc.y);
-                        acc.z = fmaf(t, x4.z, acc.z);
-                        acc.w = fmaf(t, x4.w, acc.w);
+#pragma unroll
+                        for (int nt = 0; nt < 2; ++nt) {
+                            float* Xw = sXs + warp * 256 + 8 * nt + 2 * t4;
+                            Xw[g * 16] = c[nt][0];
+                            Xw[g * 16 + 1] = c[nt][1];
+                            Xw[(g + 8) * 16] = c[nt][2];
+                            Xw[(g + 8) * 16 + 1] = c[nt][3];
+                        }
                     }
-                    *reinterpret_cast<float4*>(sT + (16 * bb + r) * LDT + 16 * aa + 4 * cq) =
-                        make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
+                    named_bar_sync(BAR_PREP, NPREP);
+                    if (warp < 4 - d) {
+                        float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+                        for (int ks = 0; ks < 2; ++ks) {
+                            const float* Tr = sT + (16 * bb + g) * LDT + 16 * bb + 8 * ks + t4;
+                            const uint32_t a0 = to_tf32(Tr[0]), a1 = to_tf32(Tr[8 * LDT]);
+                            const uint32_t a2 = to_tf32(Tr[4]), a3 = to_tf32(Tr[8 * LDT + 4]);
+#pragma unroll
+                            for (int nt = 0; nt < 2; ++nt) {
+                                const float* Xc = sXs + warp * 256 + (8 * ks + t4) * 16 + 8 * nt + g;
+                                mma_tf32_16x8x8(c[nt], a0, a1, a2, a3, to_tf32(Xc[0]), to_tf32(Xc[4 * 16]));
+                            }
+                        }
+#pragma unroll
+                        for (int nt = 0; nt < 2; ++nt) {
+                            float* Tw = sT + (16 * bb + g) * LDT + 16 * aa + 8 * nt + 2 * t4;
+                            Tw[0] = -c[nt][0];
+                            Tw[1] = -c[nt][1];
+                            Tw[8 * LDT] = -c[nt][2];
+                            Tw[8 * LDT + 1] = -c[nt][3];
+                        }
+                    }
+                    named_bar_sync(BAR_PREP, NPREP);
                 }
-                named_bar_sync(BAR_PREP, NPREP);
             }
             // ---- T as a bf16 K-major operand (rows r', 64 columns r, 128-B swizzle)
             {
@@ -462,6 +467,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 umma_ts(tmem + TM_D1, tmem + TM_S + 8 * kk, kdesc(X + (kk >> 2) * 16384 + (kk & 3) * 32),
                         IDESC_M128_N64, kk > 0 ? 1u : 0u);
             umma_commit(bar_m1);
+            if (p.write_out) {
+                // the Q S half of the output accumulator only needs the chunk-start state: it runs
+                // on the tensor cores while E1 and E2 work (its completion is covered by bar_m3)
+                const uint32_t tm_do = TM_DO + 64 * (c & 1);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    umma_ts(tmem + tm_do, tmem + TM_S + 8 * kk, kdesc(X + (kk >> 2) * 16384 + 8192 + (kk & 3) * 32),
+                            IDESC_M128_N64, kk > 0 ? 1u : 0u);
+            }
         };
         store_state_bf16();
         tmem_st_wait();
@@ -562,10 +576,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                             umma_sdesc_sw128(smem_u32addr(X + kk * 2048), 16384, 1024), IDESC_M128_N128_BMN,
                             kk > 0 ? 1u : 0u);
                 if (p.write_out) {
-#pragma unroll
-                    for (int kk = 0; kk < 8; ++kk)
-                        umma_ts(tmem + tm_do, tmem + TM_S + 8 * kk, kdesc(X + (kk >> 2) * 16384 + 8192 + (kk & 3) * 32),
-                                IDESC_M128_N64, kk > 0 ? 1u : 0u);
                     const uint8_t* P = stP(s);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
@@ -601,17 +611,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (ct == 0 && c + 1 < nchunks) issue_mma1(c + 1);
             if (p.write_out) {
                 __nv_bfloat16* Os = reinterpret_cast<__nv_bfloat16*>(Ost);
+                uint32_t o[32];
+                tmem_ld16(tl + tm_do + 32 * hh, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
+                tmem_ld16(tl + tm_do + 32 * hh + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
+                tmem_ld_wait();
 #pragma unroll
-                for (int pc = 0; pc < 2; ++pc) {
-                    uint32_t o[16];
-                    tmem_ld16(tl + tm_do + 32 * hh + 16 * pc, o);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        const int r = 32 * hh + 16 * pc + e;
-                        const float v = om[r] * __uint_as_float(o[e]);
-                        Os[r * 128 + j] = __float2bfloat16_rn(v);
-                    }
+                for (int e = 0; e < 32; ++e) {
+                    const int r = 32 * hh + e;
+                    Os[r * 128 + j] = __float2bfloat16_rn(om[r] * __uint_as_float(o[e]));
                 }
                 fence_proxy_async_smem();
             }
