@@ -285,44 +285,39 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                 for (int pc = 0; pc < 4; ++pc) tmem_ld16(ta + 16 * pc, *reinterpret_cast<uint32_t(*)[16]>(&gall[16 * pc]));
                 tmem_ld_wait();
+                if (n < C) {
+                    float* Arow = sA + r * LDA;
+                    if (fast) {
 #pragma unroll
-                for (int pc = 0; pc < 4; ++pc) {
-                    const uint32_t* g = gall + 16 * pc;
-                    if (n < C) {
-#pragma unroll
-                        for (int e = 0; e < 16; ++e) {
-                            const int sidx = 16 * pc + e;
-                            const float gv = __uint_as_float(g[e]);
-                            float v;
-                            if (fast) v = sidx < r ? brer * gv * sem[sidx] : 0.f;
-                            else v = (sidx < r && scnt[sidx] == cr) ? br * exp2f(gr - sg[sidx]) * gv : 0.f;
-                            sA[r * LDA + sidx] = v;
-                        }
+                        for (int e = 0; e < 64; ++e) Arow[e] = e < r ? brer * __uint_as_float(gall[e]) * sem[e] : 0.f;
                     } else {
-                        // P~ = (scale Gamma o Q K^T, s <= r) / om_r as a bf16 pair hi + lo.  Fast path:
-                        // om_r = scale 2^g_r, so P~[r][s] = 2^-g_s (q_r . k_s).
-                        uint32_t ph[8], pl[8];
 #pragma unroll
-                        for (int e = 0; e < 16; e += 2) {
-                            float v2[2];
+                        for (int e = 0; e < 64; ++e)
+                            Arow[e] = (e < r && scnt[e] == cr) ? br * exp2f(gr - sg[e]) * __uint_as_float(gall[e]) : 0.f;
+                    }
+                } else {
+                    // P~ = (scale Gamma o Q K^T, s <= r) / om_r as a bf16 pair hi + lo.  Fast path:
+                    // om_r = scale 2^g_r, so P~[r][s] = 2^-g_s (q_r . k_s).
+                    if (fast) {
 #pragma unroll
-                            for (int u = 0; u < 2; ++u) {
-                                const int sidx = 16 * pc + e + u;
-                                const float gv = __uint_as_float(g[e + u]);
-                                if (fast) v2[u] = sidx <= r ? gv * sem[sidx] : 0.f;
-                                else v2[u] = (sidx <= r && scnt[sidx] == cr) ? inv_om * exp2f(gr - sg[sidx]) * gv : 0.f;
-                            }
-                            ph[e >> 1] = pack_bf16x2(v2[0], v2[1]);
-                            pl[e >> 1] = pack_bf16x2(v2[0] - bf16_lo(ph[e >> 1]), v2[1] - bf16_hi(ph[e >> 1]));
+                        for (int e = 0; e < 64; ++e) gall[e] = __float_as_uint(e <= r ? __uint_as_float(gall[e]) * sem[e] : 0.f);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 64; ++e)
+                            gall[e] = __float_as_uint((e <= r && scnt[e] == cr) ? inv_om * exp2f(gr - sg[e]) * __uint_as_float(gall[e]) : 0.f);
+                    }
+#pragma unroll
+                    for (int cc = 0; cc < 8; ++cc) {
+                        uint32_t ph[4], pl[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const float v0 = __uint_as_float(gall[8 * cc + 2 * u]), v1 = __uint_as_float(gall[8 * cc + 2 * u + 1]);
+                            ph[u] = pack_bf16x2(v0, v1);
+                            pl[u] = pack_bf16x2(v0 - bf16_lo(ph[u]), v1 - bf16_hi(ph[u]));
                         }
-#pragma unroll
-                        for (int x = 0; x < 2; ++x) {
-                            const int cc = 2 * pc + x;
-                            const int off = r * 128 + ((cc ^ (r & 7)) << 4);
-                            *reinterpret_cast<uint4*>(P + off) = make_uint4(ph[4 * x], ph[4 * x + 1], ph[4 * x + 2], ph[4 * x + 3]);
-                            *reinterpret_cast<uint4*>(P + C * 128 + off) =
-                                make_uint4(pl[4 * x], pl[4 * x + 1], pl[4 * x + 2], pl[4 * x + 3]);
-                        }
+                        const int off = r * 128 + ((cc ^ (r & 7)) << 4);
+                        *reinterpret_cast<uint4*>(P + off) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+                        *reinterpret_cast<uint4*>(P + C * 128 + off) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
                     }
                 }
                 if (n >= C && G[G_QZ + r] != 0.f) {
@@ -500,21 +495,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             //      hi goes to columns [16k, +8) and lo to [16k + 8, +8)
             {
                 const __nv_bfloat16* Vs = reinterpret_cast<const __nv_bfloat16*>(stV(s));
+                uint32_t a[32];
+                tmem_ld16(tl + TM_D1 + 32 * hh, *reinterpret_cast<uint32_t(*)[16]>(&a[0]));
+                tmem_ld16(tl + TM_D1 + 32 * hh + 16, *reinterpret_cast<uint32_t(*)[16]>(&a[16]));
+                tmem_ld_wait();
 #pragma unroll
                 for (int pc = 0; pc < 2; ++pc) {
                     const uint32_t col = TM_D1 + 32 * hh + 16 * pc;
-                    uint32_t a[16];
-                    tmem_ld16(tl + col, a);
-                    tmem_ld_wait();
                     uint32_t hi[8], lo[8];
 #pragma unroll
                     for (int u = 0; u < 8; ++u) {
                         float x[2];
 #pragma unroll
                         for (int w = 0; w < 2; ++w) {
-                            const int r = 32 * hh + 16 * pc + 2 * u + w;
+                            const int e = 16 * pc + 2 * u + w;
+                            const int r = 32 * hh + e;
                             const float vv = p.v_zero ? 0.f : __bfloat162float(Vs[r * 128 + j]);
-                            x[w] = G[G_CB + r] * vv - G[G_CG + r] * __uint_as_float(a[2 * u + w]);
+                            x[w] = G[G_CB + r] * vv - G[G_CG + r] * __uint_as_float(a[e]);
                         }
                         hi[u] = pack_bf16x2(x[0], x[1]);
                         lo[u] = pack_bf16x2(x[0] - bf16_lo(hi[u]), x[1] - bf16_hi(hi[u]));
@@ -544,17 +541,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             //      columns [16k, 16k + 16), the Gamma[63][r']-scaled copy goes to [16k, +8) and the plain
             //      copy to [16k + 8, +8)
             {
+                uint32_t d[32];
+                tmem_ld16(tl + TM_D2 + 32 * hh, *reinterpret_cast<uint32_t(*)[16]>(&d[0]));
+                tmem_ld16(tl + TM_D2 + 32 * hh + 16, *reinterpret_cast<uint32_t(*)[16]>(&d[16]));
+                tmem_ld_wait();
 #pragma unroll
                 for (int pc = 0; pc < 2; ++pc) {
                     const uint32_t col = TM_D2 + 32 * hh + 16 * pc;
-                    uint32_t d[16];
-                    tmem_ld16(tl + col, d);
-                    tmem_ld_wait();
                     uint32_t ps[8], pp[8];
 #pragma unroll
                     for (int u = 0; u < 8; ++u) {
-                        const int r = 32 * hh + 16 * pc + 2 * u;
-                        const float x0 = __uint_as_float(d[2 * u]), x1 = __uint_as_float(d[2 * u + 1]);
+                        const int e = 16 * pc + 2 * u;
+                        const int r = 32 * hh + e;
+                        const float x0 = __uint_as_float(d[e]), x1 = __uint_as_float(d[e + 1]);
                         ps[u] = pack_bf16x2(x0 * G[G_CD + r], x1 * G[G_CD + r + 1]);
                         pp[u] = pack_bf16x2(x0, x1);
                     }
