@@ -34,7 +34,7 @@
 //     stays near 1e-2 (see tests/chunk_model.py).
 //       E3    S[i][j] = gamma_63 S + D3 (f32 master state in registers, 64 per thread),
 //             S^T -> TMEM bf16; then MMA1 of the next chunk is issued and, while it runs,
-//             O[r][j] = om_r DO[j][r] -> smem -> TMA store (DO is double-buffered in TMEM).
+//             O[r][j] = om_r DO[j][r] stored to global memory (DO is double-buffered in TMEM).
 // Roofline: HBM (intensity ~172 FLOP/B at the algorithmic minimum of 1032 B per token-head).
 #include <cuda.h>
 
@@ -69,18 +69,16 @@ constexpr uint32_t T_BYTES = C * 128;        // [64][64] bf16 swizzled
 constexpr uint32_t P_BYTES = 2 * C * 128;     // P as a bf16 pair: hi tile, then lo tile
 constexpr uint32_t G_BYTES = 2048;           // gates
 constexpr uint32_t STAGE_BYTES = X_BYTES + V_BYTES + T_BYTES + P_BYTES + G_BYTES;  // 75776
-constexpr uint32_t OFF_O = 2 * STAGE_BYTES;
-constexpr uint32_t O_BYTES = C * 128 * 2;
-constexpr uint32_t OFF_SA = OFF_O + O_BYTES;
-constexpr int LDA = 65;   // A rows (written row-per-lane: odd stride avoids bank conflicts)
+constexpr uint32_t OFF_SA = 2 * STAGE_BYTES;
+constexpr int LDA = 68;   // A rows (16-byte aligned: a lane writes its row with 16-byte stores)
 constexpr int LDT = 68;   // T rows (read as float4: 16-byte aligned stride)
 constexpr uint32_t OFF_ST = OFF_SA + C * LDA * 4;
 constexpr uint32_t OFF_SX = OFF_ST + C * LDT * 4;
 constexpr uint32_t OFF_SG = OFF_SX + 1024 * 4;
-constexpr uint32_t OFF_SEM = OFF_SG + 64 * 4;   // 2^-g_s (fast decay path)
+constexpr uint32_t OFF_SEM = OFF_SG + 64 * 4;   // 2^-g_s (fast decay path), 16-byte aligned
 constexpr uint32_t OFF_SCNT = OFF_SEM + 64 * 4;
 constexpr uint32_t OFF_SWT = OFF_SCNT + 64 * 4;
-constexpr uint32_t OFF_COM = OFF_SWT + 64;        // chain copy of the output multipliers [2][64]
+constexpr uint32_t OFF_COM = OFF_SWT + 64;        // chain copy of the output multipliers [2][64] (16-B aligned)
 constexpr uint32_t OFF_BAR = (OFF_COM + 2 * 64 * 4 + 7) / 8 * 8;
 constexpr uint32_t NBARS = 11;
 constexpr uint32_t OFF_TSLOT = OFF_BAR + NBARS * 8;
@@ -95,6 +93,8 @@ constexpr uint32_t IDESC_M128_N128_BMN = umma_idesc_bf16(128, 128, true);
 
 struct TcParams {
     int B, T, H, nchunks;
+    __nv_bfloat16* out;  // [B,T,H,128], element strides os (inner stride 1)
+    int64_t os[3];
     float scale;
     const float *alpha, *beta;
     int64_t as[3], bs[3];
@@ -113,8 +113,7 @@ __device__ __forceinline__ uint64_t kdesc(const uint8_t* p) {  // K-major, 128-B
 
 __global__ void __launch_bounds__(NTHREADS, 1)
     gdn2_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                           const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                           const TcParams p) {
+                           const __grid_constant__ CUtensorMap tm_v, const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
@@ -133,7 +132,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     int* scnt = reinterpret_cast<int*>(smem + OFF_SCNT);
     float* swt = reinterpret_cast<float*>(smem + OFF_SWT);
     int* swc = reinterpret_cast<int*>(smem + OFF_SWT + 32);
-    uint8_t* Ost = smem + OFF_O;
     float* com = reinterpret_cast<float*>(smem + OFF_COM);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -155,7 +153,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         prefetch_tmap(&tm_q);
         prefetch_tmap(&tm_k);
         prefetch_tmap(&tm_v);
-        prefetch_tmap(&tm_o);
     }
     if (warp == 0) {
         tmem_alloc(tslot, 512);
@@ -285,22 +282,40 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                 for (int pc = 0; pc < 4; ++pc) tmem_ld16(ta + 16 * pc, *reinterpret_cast<uint32_t(*)[16]>(&gall[16 * pc]));
                 tmem_ld_wait();
+                const float4* sem4 = reinterpret_cast<const float4*>(sem);
                 if (n < C) {
-                    float* Arow = sA + r * LDA;
+                    float4* Arow = reinterpret_cast<float4*>(sA + r * LDA);
                     if (fast) {
 #pragma unroll
-                        for (int e = 0; e < 64; ++e) Arow[e] = e < r ? brer * __uint_as_float(gall[e]) * sem[e] : 0.f;
+                        for (int e4 = 0; e4 < 16; ++e4) {
+                            const float4 m = sem4[e4];
+                            const int e = 4 * e4;
+                            float4 v;
+                            v.x = e < r ? brer * __uint_as_float(gall[e]) * m.x : 0.f;
+                            v.y = e + 1 < r ? brer * __uint_as_float(gall[e + 1]) * m.y : 0.f;
+                            v.z = e + 2 < r ? brer * __uint_as_float(gall[e + 2]) * m.z : 0.f;
+                            v.w = e + 3 < r ? brer * __uint_as_float(gall[e + 3]) * m.w : 0.f;
+                            Arow[e4] = v;
+                        }
                     } else {
+                        float* Af = sA + r * LDA;
 #pragma unroll
                         for (int e = 0; e < 64; ++e)
-                            Arow[e] = (e < r && scnt[e] == cr) ? br * exp2f(gr - sg[e]) * __uint_as_float(gall[e]) : 0.f;
+                            Af[e] = (e < r && scnt[e] == cr) ? br * exp2f(gr - sg[e]) * __uint_as_float(gall[e]) : 0.f;
                     }
                 } else {
                     // P~ = (scale Gamma o Q K^T, s <= r) / om_r as a bf16 pair hi + lo.  Fast path:
                     // om_r = scale 2^g_r, so P~[r][s] = 2^-g_s (q_r . k_s).
                     if (fast) {
 #pragma unroll
-                        for (int e = 0; e < 64; ++e) gall[e] = __float_as_uint(e <= r ? __uint_as_float(gall[e]) * sem[e] : 0.f);
+                        for (int e4 = 0; e4 < 16; ++e4) {
+                            const float4 m = sem4[e4];
+                            const int e = 4 * e4;
+                            gall[e] = __float_as_uint(e <= r ? __uint_as_float(gall[e]) * m.x : 0.f);
+                            gall[e + 1] = __float_as_uint(e + 1 <= r ? __uint_as_float(gall[e + 1]) * m.y : 0.f);
+                            gall[e + 2] = __float_as_uint(e + 2 <= r ? __uint_as_float(gall[e + 2]) * m.z : 0.f);
+                            gall[e + 3] = __float_as_uint(e + 3 <= r ? __uint_as_float(gall[e + 3]) * m.w : 0.f);
+                        }
                     } else {
 #pragma unroll
                         for (int e = 0; e < 64; ++e)
@@ -336,13 +351,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (tid < C) {
                 const int blk = tid >> 4, c0 = tid & 15;
                 const float* Ab = sA + (16 * blk) * LDA + 16 * blk;
-                float x[16];
+                // x = column c0 of the block inverse: x_s = [s == c0] - sum_{s' < s} A[s][s'] x_s',
+                // accumulated column by column so the dependency depth is 16, not 120
+                float x[16], acc[16];
 #pragma unroll
-                for (int r = 0; r < 16; ++r) {
-                    float acc = 0.f;
+                for (int r = 0; r < 16; ++r) acc[r] = 0.f;
 #pragma unroll
-                    for (int s2 = 0; s2 < r; ++s2) acc = fmaf(Ab[r * LDA + s2], x[s2], acc);
-                    x[r] = (r < c0) ? 0.f : (r == c0 ? 1.f : -acc);
+                for (int s2 = 0; s2 < 16; ++s2) {
+                    x[s2] = (s2 < c0) ? 0.f : (s2 == c0 ? 1.f : -acc[s2]);
+#pragma unroll
+                    for (int r = s2 + 1; r < 16; ++r) acc[r] = fmaf(Ab[r * LDA + s2], x[s2], acc[r]);
                 }
 #pragma unroll
                 for (int r = 0; r < 16; ++r) sT[(16 * blk + r) * LDT + 16 * blk + c0] = x[r];
@@ -499,19 +517,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 tmem_ld16(tl + TM_D1 + 32 * hh, *reinterpret_cast<uint32_t(*)[16]>(&a[0]));
                 tmem_ld16(tl + TM_D1 + 32 * hh + 16, *reinterpret_cast<uint32_t(*)[16]>(&a[16]));
                 tmem_ld_wait();
+                const float2* cb2 = reinterpret_cast<const float2*>(G + G_CB + 32 * hh);
+                const float2* cg2 = reinterpret_cast<const float2*>(G + G_CG + 32 * hh);
 #pragma unroll
                 for (int pc = 0; pc < 2; ++pc) {
                     const uint32_t col = TM_D1 + 32 * hh + 16 * pc;
                     uint32_t hi[8], lo[8];
 #pragma unroll
                     for (int u = 0; u < 8; ++u) {
+                        const float2 cb = cb2[8 * pc + u], cg = cg2[8 * pc + u];
                         float x[2];
 #pragma unroll
                         for (int w = 0; w < 2; ++w) {
                             const int e = 16 * pc + 2 * u + w;
                             const int r = 32 * hh + e;
                             const float vv = p.v_zero ? 0.f : __bfloat162float(Vs[r * 128 + j]);
-                            x[w] = G[G_CB + r] * vv - G[G_CG + r] * __uint_as_float(a[e]);
+                            x[w] = (w ? cb.y : cb.x) * vv - (w ? cg.y : cg.x) * __uint_as_float(a[e]);
                         }
                         hi[u] = pack_bf16x2(x[0], x[1]);
                         lo[u] = pack_bf16x2(x[0] - bf16_lo(hi[u]), x[1] - bf16_hi(hi[u]));
@@ -584,7 +605,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     }
                 }
                 umma_commit(bar_m3);
-                tma_store_wait_read0();  // the previous chunk's output tile has left shared memory
             }
             mbar_wait(bar_m3, par, p.err, 7);
             tc_fence_after();
@@ -609,32 +629,32 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             // the recurrence moves on: MMA1 of the next chunk runs while this chunk's output is written
             if (ct == 0 && c + 1 < nchunks) issue_mma1(c + 1);
             if (p.write_out) {
-                __nv_bfloat16* Os = reinterpret_cast<__nv_bfloat16*>(Ost);
+                // O[r][j] = om_r DO[j][r], stored straight to global memory (a warp writes 64 contiguous
+                // bytes of one token row per instruction)
                 uint32_t o[32];
                 tmem_ld16(tl + tm_do + 32 * hh, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
                 tmem_ld16(tl + tm_do + 32 * hh + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
                 tmem_ld_wait();
+                const float4* om4 = reinterpret_cast<const float4*>(om + 32 * hh);
+                __nv_bfloat16* ob = p.out + (size_t)b * p.os[0] + (size_t)h * p.os[2] + j;
+                const int t0 = c * C + 32 * hh;
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const int r = 32 * hh + e;
-                    Os[r * 128 + j] = __float2bfloat16_rn(om[r] * __uint_as_float(o[e]));
-                }
-                fence_proxy_async_smem();
-            }
-            tc_fence_before();
-            named_bar_sync(BAR_CHAIN, NCHAIN);
-            if (ct == 0) {
-                if (p.write_out) {
-                    tma_store_4d(&tm_o, Ost, 0, c * C, h, b);
-                    tma_store_commit();
+                for (int e4 = 0; e4 < 8; ++e4) {
+                    const float4 m = om4[e4];
+                    const float mm[4] = {m.x, m.y, m.z, m.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int e = 4 * e4 + u;
+                        if (t0 + e < p.T) ob[(size_t)(t0 + e) * p.os[1]] = __float2bfloat16_rn(mm[u] * __uint_as_float(o[e]));
+                    }
                 }
             }
+            // ---- end of chunk c
         }
         if (p.final_state) {
 #pragma unroll
             for (int e = 0; e < 64; ++e) p.final_state[sbase + (size_t)(64 * hh + e) * DK + j] = S[e];
         }
-        if (ct == 0) tma_store_wait_all0();
     }
     tc_fence_before();
     __syncthreads();
@@ -700,7 +720,7 @@ int tc_prefill_supported(const dbl_prefill_args* a, const int64_t* qs, const int
 int tc_prefill_launch(const dbl_prefill_args* a, const int64_t* qs, const int64_t* ks, const int64_t* vs,
                       const int64_t* as, const int64_t* bs, const int64_t* os, int mode, float* transition,
                       cudaStream_t st) {
-    CUtensorMap mq, mk, mv, mo;
+    CUtensorMap mq, mk, mv;
     int rc = make_map(&mq, mode == 1 ? a->k : a->q, a->batch, a->time, a->heads, mode == 1 ? ks : qs, 64, true);
     if (rc == DBL_OK) rc = make_map(&mk, a->k, a->batch, a->time, a->heads, ks, 64, true);
     if (rc == DBL_OK) {
@@ -708,13 +728,14 @@ int tc_prefill_launch(const dbl_prefill_args* a, const int64_t* qs, const int64_
         rc = make_map(&mv, hv ? a->v : a->k, a->batch, a->time, a->heads, hv ? vs : ks, 128, false);
     }
     const bool write_out = mode == 0 && a->out != nullptr;
-    if (rc == DBL_OK) rc = make_map(&mo, write_out ? a->out : a->k, a->batch, a->time, a->heads, write_out ? os : ks, 128, false);
     if (rc != DBL_OK) return rc;
     TcParams p{};
     p.B = (int)a->batch;
     p.T = (int)a->time;
     p.H = (int)a->heads;
     p.nchunks = (int)((a->time + C - 1) / C);
+    p.out = write_out ? static_cast<__nv_bfloat16*>(a->out) : nullptr;
+    for (int d = 0; d < 3; ++d) p.os[d] = os[d];
     p.scale = a->scale;
     p.alpha = a->alpha;
     p.beta = a->beta;
@@ -746,7 +767,7 @@ int tc_prefill_launch(const dbl_prefill_args* a, const int64_t* qs, const int64_
         if (e != cudaSuccess) return cuda_status(e, "prefill_tc: cudaFuncSetAttribute");
         attr_set = true;
     }
-    gdn2_prefill_tc_kernel<<<(unsigned)(a->batch * a->heads), NTHREADS, SMEM_BYTES, st>>>(mq, mk, mv, mo, p);
+    gdn2_prefill_tc_kernel<<<(unsigned)(a->batch * a->heads), NTHREADS, SMEM_BYTES, st>>>(mq, mk, mv, p);
     return launch_status("gdn2_prefill_tc_kernel");
 }
 
