@@ -13,14 +13,15 @@
 //   S' = gamma_63 S + (diag(Gamma[63][r]) K)^T Delta
 // Padding tokens get beta = 0 and alpha = 1 (their edit is exactly zero) and output 0.
 //
-// B200 mapping.  One CTA per (b, h), 384 threads, one CTA per SM (all 512 TMEM columns).
-//   * prep warps 0-3: TMA loads of the chunk tiles (K and Q 128-byte swizzled, V plain), the gate
+// B200 mapping.  One CTA per (b, h), 512 threads, one CTA per SM (all 512 TMEM columns); the
+// block launches at 128 registers per thread and setmaxnreg moves them to the chain warps.
+//   * prep warps 0-7: TMA loads of the chunk tiles (K and Q 128-byte swizzled, V plain), the gate
 //     scan, UMMA [K;Q] K^T -> TMEM, decay masks, the blocked 64x64 unit-lower inverse (16x16
 //     diagonal blocks by substitution, off-diagonal blocks level by level on mma.sync tf32 tiles),
 //     T and P written as
 //     bf16 UMMA operands.  Prep runs one chunk ahead of the chain (two smem stages); the chain
 //     leader issues the loads of chunk c + 2 as soon as it is done with chunk c.
-//   * chain warps 4-11: the state-dependent chain, transposed so that the value column j of the
+//   * chain warps 8-15: the state-dependent chain, transposed so that the value column j of the
 //     state is TMEM lane j and every activation stays in TMEM (A operands of the TS form):
 //       MMA1  D1[j][r]  = sum_i S^T[j][i] K[r][i]          (A = S^T bf16 in TMEM)
 //       E1    R^T[j][r] = beta_r V[r][j] - beta_r gamma_r D1[j][r]   -> TMEM (bf16 hi + lo pair)
@@ -34,7 +35,7 @@
 //     stays near 1e-2 (see tests/chunk_model.py).
 //       E3    S[i][j] = gamma_63 S + D3 (f32 master state in registers, 64 per thread),
 //             S^T -> TMEM bf16; then MMA1 of the next chunk is issued and, while it runs,
-//             O[r][j] = om_r DO[j][r] stored to global memory (DO is double-buffered in TMEM).
+//             O[r][j] = om_r DO[j][r] -> smem -> TMA store (DO is double-buffered in TMEM).
 // Roofline: HBM (intensity ~172 FLOP/B at the algorithmic minimum of 1032 B per token-head).
 #include <cuda.h>
 
@@ -49,9 +50,11 @@ namespace {
 
 constexpr int C = 64;
 constexpr int DK = 128;
-constexpr int NTHREADS = 384;
-constexpr int NPREP = 128;   // warps 0-3 (one TMEM lane quadrant each)
-constexpr int NCHAIN = 256;  // warps 4-11
+constexpr int NTHREADS = 512;
+constexpr int NPREP = 256;   // warps 0-7, 96 registers each after setmaxnreg
+constexpr int NCHAIN = 256;  // warps 8-15, 160 registers each (the f32 state lives in registers)
+constexpr int PREP_REGS = 96, CHAIN_REGS = 160;
+static_assert(NPREP * PREP_REGS + NCHAIN * CHAIN_REGS <= 65536, "register split exceeds the launch budget");
 constexpr int BAR_PREP = 1, BAR_CHAIN = 2;
 
 // TMEM column map (512 columns, f32 accumulators unless noted)
@@ -69,7 +72,9 @@ constexpr uint32_t T_BYTES = C * 128;        // [64][64] bf16 swizzled
 constexpr uint32_t P_BYTES = 2 * C * 128;     // P as a bf16 pair: hi tile, then lo tile
 constexpr uint32_t G_BYTES = 2048;           // gates
 constexpr uint32_t STAGE_BYTES = X_BYTES + V_BYTES + T_BYTES + P_BYTES + G_BYTES;  // 75776
-constexpr uint32_t OFF_SA = 2 * STAGE_BYTES;
+constexpr uint32_t OFF_O = 2 * STAGE_BYTES;       // output tile staging [64][128] bf16
+constexpr uint32_t O_BYTES = C * 128 * 2;
+constexpr uint32_t OFF_SA = OFF_O + O_BYTES;
 constexpr int LDA = 68;   // A rows (16-byte aligned: a lane writes its row with 16-byte stores)
 constexpr int LDT = 68;   // T rows (read as float4: 16-byte aligned stride)
 constexpr uint32_t OFF_ST = OFF_SA + C * LDA * 4;
@@ -88,13 +93,10 @@ constexpr int G_CB = 0, G_CG = 64, G_CD = 128, G_OM = 192, G_VAL = 256, G_GC = 3
 constexpr float kTinyDecay = 7.888609052210118e-31f;  // 2^-100: a smaller gamma_r counts as zero
 
 constexpr uint32_t IDESC_M128_N64 = umma_idesc_bf16(128, 64, false);
-constexpr uint32_t IDESC_M128_N128 = umma_idesc_bf16(128, 128, false);
 constexpr uint32_t IDESC_M128_N128_BMN = umma_idesc_bf16(128, 128, true);
 
 struct TcParams {
     int B, T, H, nchunks;
-    __nv_bfloat16* out;  // [B,T,H,128], element strides os (inner stride 1)
-    int64_t os[3];
     float scale;
     const float *alpha, *beta;
     int64_t as[3], bs[3];
@@ -113,7 +115,8 @@ __device__ __forceinline__ uint64_t kdesc(const uint8_t* p) {  // K-major, 128-B
 
 __global__ void __launch_bounds__(NTHREADS, 1)
     gdn2_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                           const __grid_constant__ CUtensorMap tm_v, const TcParams p) {
+                           const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                           const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
@@ -133,6 +136,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     float* swt = reinterpret_cast<float*>(smem + OFF_SWT);
     int* swc = reinterpret_cast<int*>(smem + OFF_SWT + 32);
     float* com = reinterpret_cast<float*>(smem + OFF_COM);
+    uint8_t* Ost = smem + OFF_O;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int bh = blockIdx.x;
@@ -153,6 +157,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         prefetch_tmap(&tm_q);
         prefetch_tmap(&tm_k);
         prefetch_tmap(&tm_v);
+        prefetch_tmap(&tm_o);
     }
     if (warp == 0) {
         tmem_alloc(tslot, 512);
@@ -162,6 +167,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
+    // Register split: launched at 512 x 128; prep warpgroups give up 32 each, chain warpgroups take 32.
+    if (warp < 8) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(PREP_REGS));
+    else asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(CHAIN_REGS));
 
     auto issue_loads = [&](int c) {
         const int s = c & 1;
@@ -175,9 +183,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (!p.v_zero) tma_load_4d(stV(s), &tm_v, &bar_full[s], 0, c * C, h, b);
     };
 
-    if (warp < 4) {
+    if (warp < 8) {
         // =================================================================== prep warps
-        const int q = warp;
+        const int q = warp & 3, half = warp >> 2;
         if (tid == 0) {
             issue_loads(0);
             if (nchunks > 1) issue_loads(1);
@@ -265,7 +273,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             mbar_wait(bar_kk, c & 1, p.err, 2);
             tc_fence_after();
             {
-                // row n = 32q + lane of [K;Q]; all 64 columns s, 16 at a time
+                // row n = 32q + lane of [K;Q]; columns s in [32 half, 32 half + 32)
                 const int n = 32 * q + lane;
                 const int r = n & 63;
                 const float gr = sg[r];
@@ -273,76 +281,79 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 // Fast path: no zero decay in the chunk and a bounded total decay, so
                 // Gamma[r][s] = 2^g_r 2^-g_s is a rank-1 product (no exponential per element).
                 const bool fast = scnt[C - 1] == 0 && sg[C - 1] > -100.f;
-                const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + TM_KK;
-                uint8_t* P = stP(s);
-                const float br = G[G_CB + r];
-                const float brer = br * exp2f(gr);
-                const float inv_om = p.scale / G[G_OM + r];
-                uint32_t gall[64];
-#pragma unroll
-                for (int pc = 0; pc < 4; ++pc) tmem_ld16(ta + 16 * pc, *reinterpret_cast<uint32_t(*)[16]>(&gall[16 * pc]));
+                const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + TM_KK + 32 * half;
+                uint32_t gl[32];
+                tmem_ld16(ta, *reinterpret_cast<uint32_t(*)[16]>(&gl[0]));
+                tmem_ld16(ta + 16, *reinterpret_cast<uint32_t(*)[16]>(&gl[16]));
                 tmem_ld_wait();
-                const float4* sem4 = reinterpret_cast<const float4*>(sem);
+                const float4* sem4 = reinterpret_cast<const float4*>(sem + 32 * half);
+                const int s0 = 32 * half;
                 if (n < C) {
-                    float4* Arow = reinterpret_cast<float4*>(sA + r * LDA);
+                    const float br = G[G_CB + r];
                     if (fast) {
+                        const float brer = br * exp2f(gr);
+                        float4* Arow = reinterpret_cast<float4*>(sA + r * LDA + s0);
 #pragma unroll
-                        for (int e4 = 0; e4 < 16; ++e4) {
+                        for (int e4 = 0; e4 < 8; ++e4) {
                             const float4 m = sem4[e4];
-                            const int e = 4 * e4;
+                            const int e = s0 + 4 * e4;
                             float4 v;
-                            v.x = e < r ? brer * __uint_as_float(gall[e]) * m.x : 0.f;
-                            v.y = e + 1 < r ? brer * __uint_as_float(gall[e + 1]) * m.y : 0.f;
-                            v.z = e + 2 < r ? brer * __uint_as_float(gall[e + 2]) * m.z : 0.f;
-                            v.w = e + 3 < r ? brer * __uint_as_float(gall[e + 3]) * m.w : 0.f;
+                            v.x = e < r ? brer * __uint_as_float(gl[4 * e4]) * m.x : 0.f;
+                            v.y = e + 1 < r ? brer * __uint_as_float(gl[4 * e4 + 1]) * m.y : 0.f;
+                            v.z = e + 2 < r ? brer * __uint_as_float(gl[4 * e4 + 2]) * m.z : 0.f;
+                            v.w = e + 3 < r ? brer * __uint_as_float(gl[4 * e4 + 3]) * m.w : 0.f;
                             Arow[e4] = v;
                         }
                     } else {
-                        float* Af = sA + r * LDA;
+                        float* Af = sA + r * LDA + s0;
 #pragma unroll
-                        for (int e = 0; e < 64; ++e)
-                            Af[e] = (e < r && scnt[e] == cr) ? br * exp2f(gr - sg[e]) * __uint_as_float(gall[e]) : 0.f;
+                        for (int e = 0; e < 32; ++e)
+                            Af[e] = (s0 + e < r && scnt[s0 + e] == cr) ? br * exp2f(gr - sg[s0 + e]) * __uint_as_float(gl[e]) : 0.f;
                     }
                 } else {
                     // P~ = (scale Gamma o Q K^T, s <= r) / om_r as a bf16 pair hi + lo.  Fast path:
                     // om_r = scale 2^g_r, so P~[r][s] = 2^-g_s (q_r . k_s).
                     if (fast) {
 #pragma unroll
-                        for (int e4 = 0; e4 < 16; ++e4) {
+                        for (int e4 = 0; e4 < 8; ++e4) {
                             const float4 m = sem4[e4];
-                            const int e = 4 * e4;
-                            gall[e] = __float_as_uint(e <= r ? __uint_as_float(gall[e]) * m.x : 0.f);
-                            gall[e + 1] = __float_as_uint(e + 1 <= r ? __uint_as_float(gall[e + 1]) * m.y : 0.f);
-                            gall[e + 2] = __float_as_uint(e + 2 <= r ? __uint_as_float(gall[e + 2]) * m.z : 0.f);
-                            gall[e + 3] = __float_as_uint(e + 3 <= r ? __uint_as_float(gall[e + 3]) * m.w : 0.f);
+                            const int e = s0 + 4 * e4;
+                            gl[4 * e4] = __float_as_uint(e <= r ? __uint_as_float(gl[4 * e4]) * m.x : 0.f);
+                            gl[4 * e4 + 1] = __float_as_uint(e + 1 <= r ? __uint_as_float(gl[4 * e4 + 1]) * m.y : 0.f);
+                            gl[4 * e4 + 2] = __float_as_uint(e + 2 <= r ? __uint_as_float(gl[4 * e4 + 2]) * m.z : 0.f);
+                            gl[4 * e4 + 3] = __float_as_uint(e + 3 <= r ? __uint_as_float(gl[4 * e4 + 3]) * m.w : 0.f);
                         }
                     } else {
+                        const float inv_om = p.scale / G[G_OM + r];
 #pragma unroll
-                        for (int e = 0; e < 64; ++e)
-                            gall[e] = __float_as_uint((e <= r && scnt[e] == cr) ? inv_om * exp2f(gr - sg[e]) * __uint_as_float(gall[e]) : 0.f);
+                        for (int e = 0; e < 32; ++e)
+                            gl[e] = __float_as_uint((s0 + e <= r && scnt[s0 + e] == cr) ? inv_om * exp2f(gr - sg[s0 + e]) * __uint_as_float(gl[e]) : 0.f);
                     }
+                    uint8_t* P = stP(s);
 #pragma unroll
-                    for (int cc = 0; cc < 8; ++cc) {
+                    for (int x = 0; x < 4; ++x) {
                         uint32_t ph[4], pl[4];
 #pragma unroll
                         for (int u = 0; u < 4; ++u) {
-                            const float v0 = __uint_as_float(gall[8 * cc + 2 * u]), v1 = __uint_as_float(gall[8 * cc + 2 * u + 1]);
+                            const float v0 = __uint_as_float(gl[8 * x + 2 * u]), v1 = __uint_as_float(gl[8 * x + 2 * u + 1]);
                             ph[u] = pack_bf16x2(v0, v1);
                             pl[u] = pack_bf16x2(v0 - bf16_lo(ph[u]), v1 - bf16_hi(ph[u]));
                         }
+                        const int cc = 4 * half + x;
                         const int off = r * 128 + ((cc ^ (r & 7)) << 4);
                         *reinterpret_cast<uint4*>(P + off) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
                         *reinterpret_cast<uint4*>(P + C * 128 + off) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
                     }
-                }
-                if (n >= C && G[G_QZ + r] != 0.f) {
-                    // gamma_r is zero (or below 2^-100): drop the row's Q S term by zeroing its Q row
-                    uint8_t* X = stX(s);
+                    if (G[G_QZ + r] != 0.f) {
+                        // gamma_r is zero (or below 2^-100): drop the row's Q S term by zeroing its Q row
+                        uint8_t* X = stX(s);
 #pragma unroll
-                    for (int kb = 0; kb < 2; ++kb)
+                        for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
-                        for (int x = 0; x < 8; ++x)
-                            *reinterpret_cast<uint4*>(X + kb * 16384 + (64 + r) * 128 + 16 * x) = make_uint4(0, 0, 0, 0);
+                            for (int x = 0; x < 4; ++x)
+                                *reinterpret_cast<uint4*>(X + kb * 16384 + (64 + r) * 128 + 64 * half + 16 * x) =
+                                    make_uint4(0, 0, 0, 0);
+                    }
                 }
             }
             tc_fence_before();
@@ -365,7 +376,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                 for (int r = 0; r < 16; ++r) sT[(16 * blk + r) * LDT + 16 * blk + c0] = x[r];
             } else {
-                for (int e = tid - C; e < 6 * 256; e += NPREP - C) {  // 64 threads
+                for (int e = tid - C; e < 6 * 256; e += NPREP - C) {
                     const int pair = e >> 8, rem = e & 255;
                     const int bb = pair < 3 ? 0 : (pair < 5 ? 1 : 2);
                     const int aa = pair < 3 ? pair + 1 : (pair < 5 ? pair - 1 : 3);
@@ -448,7 +459,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     } else {
         // =================================================================== chain warps
         const int ct = tid - NPREP;
-        const int q = warp & 3, hh = (warp - 4) >> 2;
+        const int q = warp & 3, hh = (warp - 8) >> 2;
         const int j = 32 * q + lane;  // state value column == TMEM lane
         const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16);
         float S[64];  // S[i][j], i = 64 hh + e
@@ -605,6 +616,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     }
                 }
                 umma_commit(bar_m3);
+                tma_store_wait_read0();  // the previous chunk's output tile has left shared memory
             }
             mbar_wait(bar_m3, par, p.err, 7);
             tc_fence_after();
@@ -629,24 +641,24 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             // the recurrence moves on: MMA1 of the next chunk runs while this chunk's output is written
             if (ct == 0 && c + 1 < nchunks) issue_mma1(c + 1);
             if (p.write_out) {
-                // O[r][j] = om_r DO[j][r], stored straight to global memory (a warp writes 64 contiguous
-                // bytes of one token row per instruction)
+                __nv_bfloat16* Os = reinterpret_cast<__nv_bfloat16*>(Ost);
                 uint32_t o[32];
                 tmem_ld16(tl + tm_do + 32 * hh, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
                 tmem_ld16(tl + tm_do + 32 * hh + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
                 tmem_ld_wait();
-                const float4* om4 = reinterpret_cast<const float4*>(om + 32 * hh);
-                __nv_bfloat16* ob = p.out + (size_t)b * p.os[0] + (size_t)h * p.os[2] + j;
-                const int t0 = c * C + 32 * hh;
 #pragma unroll
-                for (int e4 = 0; e4 < 8; ++e4) {
-                    const float4 m = om4[e4];
-                    const float mm[4] = {m.x, m.y, m.z, m.w};
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int e = 4 * e4 + u;
-                        if (t0 + e < p.T) ob[(size_t)(t0 + e) * p.os[1]] = __float2bfloat16_rn(mm[u] * __uint_as_float(o[e]));
-                    }
+                for (int e = 0; e < 32; ++e) {
+                    const int r = 32 * hh + e;
+                    Os[r * 128 + j] = __float2bfloat16_rn(om[r] * __uint_as_float(o[e]));
+                }
+                fence_proxy_async_smem();
+            }
+            tc_fence_before();
+            named_bar_sync(BAR_CHAIN, NCHAIN);
+            if (ct == 0) {
+                if (p.write_out) {
+                    tma_store_4d(&tm_o, Ost, 0, c * C, h, b);
+                    tma_store_commit();
                 }
             }
             // ---- end of chunk c
@@ -655,6 +667,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
             for (int e = 0; e < 64; ++e) p.final_state[sbase + (size_t)(64 * hh + e) * DK + j] = S[e];
         }
+        if (ct == 0) tma_store_wait_all0();
     }
     tc_fence_before();
     __syncthreads();
@@ -720,7 +733,7 @@ int tc_prefill_supported(const dbl_prefill_args* a, const int64_t* qs, const int
 int tc_prefill_launch(const dbl_prefill_args* a, const int64_t* qs, const int64_t* ks, const int64_t* vs,
                       const int64_t* as, const int64_t* bs, const int64_t* os, int mode, float* transition,
                       cudaStream_t st) {
-    CUtensorMap mq, mk, mv;
+    CUtensorMap mq, mk, mv, mo;
     int rc = make_map(&mq, mode == 1 ? a->k : a->q, a->batch, a->time, a->heads, mode == 1 ? ks : qs, 64, true);
     if (rc == DBL_OK) rc = make_map(&mk, a->k, a->batch, a->time, a->heads, ks, 64, true);
     if (rc == DBL_OK) {
@@ -728,14 +741,13 @@ int tc_prefill_launch(const dbl_prefill_args* a, const int64_t* qs, const int64_
         rc = make_map(&mv, hv ? a->v : a->k, a->batch, a->time, a->heads, hv ? vs : ks, 128, false);
     }
     const bool write_out = mode == 0 && a->out != nullptr;
+    if (rc == DBL_OK) rc = make_map(&mo, write_out ? a->out : a->k, a->batch, a->time, a->heads, write_out ? os : ks, 128, false);
     if (rc != DBL_OK) return rc;
     TcParams p{};
     p.B = (int)a->batch;
     p.T = (int)a->time;
     p.H = (int)a->heads;
     p.nchunks = (int)((a->time + C - 1) / C);
-    p.out = write_out ? static_cast<__nv_bfloat16*>(a->out) : nullptr;
-    for (int d = 0; d < 3; ++d) p.os[d] = os[d];
     p.scale = a->scale;
     p.alpha = a->alpha;
     p.beta = a->beta;
@@ -767,7 +779,7 @@ int tc_prefill_launch(const dbl_prefill_args* a, const int64_t* qs, const int64_
         if (e != cudaSuccess) return cuda_status(e, "prefill_tc: cudaFuncSetAttribute");
         attr_set = true;
     }
-    gdn2_prefill_tc_kernel<<<(unsigned)(a->batch * a->heads), NTHREADS, SMEM_BYTES, st>>>(mq, mk, mv, p);
+    gdn2_prefill_tc_kernel<<<(unsigned)(a->batch * a->heads), NTHREADS, SMEM_BYTES, st>>>(mq, mk, mv, mo, p);
     return launch_status("gdn2_prefill_tc_kernel");
 }
 
