@@ -17,7 +17,7 @@
 // block launches at 128 registers per thread and setmaxnreg moves them to the chain warps.
 //   * prep warps 0-7: TMA loads of the chunk tiles (K and Q 128-byte swizzled, V plain), the gate
 //     scan, UMMA [K;Q] K^T -> TMEM, decay masks, the blocked 64x64 unit-lower inverse (16x16
-//     diagonal blocks by substitution, off-diagonal blocks level by level on mma.sync tf32 tiles),
+//     diagonal blocks by substitution, off-diagonal blocks column by column on mma.sync tf32 tiles),
 //     T and P written as
 //     bf16 UMMA operands.  Prep runs one chunk ahead of the chain (two smem stages); the chain
 //     leader issues the loads of chunk c + 2 as soon as it is done with chunk c.
@@ -384,62 +384,60 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
             }
             named_bar_sync(BAR_PREP, NPREP);
-            // ---- off-diagonal blocks, by distance d from the diagonal, on tensor cores (mma.sync tf32,
-            //      one warp per 16 x 16 block): X = sum_{a <= m < b} A[b][m] T[m][a], T[b][a] = -T[b][b] X
-            {
+            // ---- off-diagonal blocks on tensor cores (mma.sync tf32).  Block T[b][a] depends only on
+            //      the blocks of its own column a and on the diagonal block T[b][b]:
+            //        X = sum_{a <= m < b} A[b][m] T[m][a],   T[b][a] = -T[b][b] X,
+            //      so warp a (a = 0, 1, 2) walks column a downwards with warp-level syncs only.
+            if (warp < 3) {
+                const int aa = warp;
                 const int g = lane >> 2, t4 = lane & 3;
-#pragma unroll
-                for (int d = 1; d < 4; ++d) {
-                    const int bb = d + warp, aa = warp;  // warp = block index within the level
-                    if (warp < 4 - d) {
-                        float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll
-                        for (int ks = 0; ks < 2 * d; ++ks) {
-                            const int m0 = 16 * aa + 8 * ks;
-                            const float* Ar = sA + (16 * bb + g) * LDA + m0 + t4;
-                            const uint32_t a0 = to_tf32(Ar[0]), a1 = to_tf32(Ar[8 * LDA]);
-                            const uint32_t a2 = to_tf32(Ar[4]), a3 = to_tf32(Ar[8 * LDA + 4]);
-#pragma unroll
-                            for (int nt = 0; nt < 2; ++nt) {
-                                const float* Tc = sT + (m0 + t4) * LDT + 16 * aa + 8 * nt + g;
-                                mma_tf32_16x8x8(c[nt], a0, a1, a2, a3, to_tf32(Tc[0]), to_tf32(Tc[4 * LDT]));
-                            }
-                        }
+                float* Xw = sXs + warp * 256;  // warp-private 16 x 16 scratch
+                for (int bb = aa + 1; bb < 4; ++bb) {
+                    float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+                    for (int ks = 0; ks < 2 * (bb - aa); ++ks) {
+                        const int m0 = 16 * aa + 8 * ks;
+                        const float* Ar = sA + (16 * bb + g) * LDA + m0 + t4;
+                        const uint32_t a0 = to_tf32(Ar[0]), a1 = to_tf32(Ar[8 * LDA]);
+                        const uint32_t a2 = to_tf32(Ar[4]), a3 = to_tf32(Ar[8 * LDA + 4]);
 #pragma unroll
                         for (int nt = 0; nt < 2; ++nt) {
-                            float* Xw = sXs + warp * 256 + 8 * nt + 2 * t4;
-                            Xw[g * 16] = c[nt][0];
-                            Xw[g * 16 + 1] = c[nt][1];
-                            Xw[(g + 8) * 16] = c[nt][2];
-                            Xw[(g + 8) * 16 + 1] = c[nt][3];
+                            const float* Tc = sT + (m0 + t4) * LDT + 16 * aa + 8 * nt + g;
+                            mma_tf32_16x8x8(c[nt], a0, a1, a2, a3, to_tf32(Tc[0]), to_tf32(Tc[4 * LDT]));
                         }
                     }
-                    named_bar_sync(BAR_PREP, NPREP);
-                    if (warp < 4 - d) {
-                        float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-                        for (int ks = 0; ks < 2; ++ks) {
-                            const float* Tr = sT + (16 * bb + g) * LDT + 16 * bb + 8 * ks + t4;
-                            const uint32_t a0 = to_tf32(Tr[0]), a1 = to_tf32(Tr[8 * LDT]);
-                            const uint32_t a2 = to_tf32(Tr[4]), a3 = to_tf32(Tr[8 * LDT + 4]);
+                    for (int nt = 0; nt < 2; ++nt) {
+                        float* xw = Xw + 8 * nt + 2 * t4;
+                        xw[g * 16] = c[nt][0];
+                        xw[g * 16 + 1] = c[nt][1];
+                        xw[(g + 8) * 16] = c[nt][2];
+                        xw[(g + 8) * 16 + 1] = c[nt][3];
+                    }
+                    __syncwarp();
+                    float e[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-                            for (int nt = 0; nt < 2; ++nt) {
-                                const float* Xc = sXs + warp * 256 + (8 * ks + t4) * 16 + 8 * nt + g;
-                                mma_tf32_16x8x8(c[nt], a0, a1, a2, a3, to_tf32(Xc[0]), to_tf32(Xc[4 * 16]));
-                            }
-                        }
+                    for (int ks = 0; ks < 2; ++ks) {
+                        const float* Tr = sT + (16 * bb + g) * LDT + 16 * bb + 8 * ks + t4;
+                        const uint32_t a0 = to_tf32(Tr[0]), a1 = to_tf32(Tr[8 * LDT]);
+                        const uint32_t a2 = to_tf32(Tr[4]), a3 = to_tf32(Tr[8 * LDT + 4]);
 #pragma unroll
                         for (int nt = 0; nt < 2; ++nt) {
-                            float* Tw = sT + (16 * bb + g) * LDT + 16 * aa + 8 * nt + 2 * t4;
-                            Tw[0] = -c[nt][0];
-                            Tw[1] = -c[nt][1];
-                            Tw[8 * LDT] = -c[nt][2];
-                            Tw[8 * LDT + 1] = -c[nt][3];
+                            const float* Xc = Xw + (8 * ks + t4) * 16 + 8 * nt + g;
+                            mma_tf32_16x8x8(e[nt], a0, a1, a2, a3, to_tf32(Xc[0]), to_tf32(Xc[4 * 16]));
                         }
                     }
-                    named_bar_sync(BAR_PREP, NPREP);
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt) {
+                        float* Tw = sT + (16 * bb + g) * LDT + 16 * aa + 8 * nt + 2 * t4;
+                        Tw[0] = -e[nt][0];
+                        Tw[1] = -e[nt][1];
+                        Tw[8 * LDT] = -e[nt][2];
+                        Tw[8 * LDT + 1] = -e[nt][3];
+                    }
+                    __syncwarp();  // T[b][a] is read by the next block of this column; Xw is reused
                 }
             }
+            named_bar_sync(BAR_PREP, NPREP);
             // ---- T as a bf16 K-major operand (rows r', 64 columns r, 128-B swizzle)
             {
                 uint8_t* Tt = stT(s);
