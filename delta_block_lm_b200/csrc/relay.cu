@@ -6,13 +6,14 @@
 // statistics [max, sum] per query; a query with no eligible key writes o = 0, [0, 1].
 //
 // Work split (one grid, 256 threads per CTA):
-//   prefix CTAs (head h, 64-key prefix block pb): read the block's keys/values of head h ONCE
-//       and produce partials (max, sum, acc[D]) for the queries of EVERY sequence at head h,
-//       so the shared prefix is read once per head, never once per sequence.  bf16 inputs use
-//       tensor-core tiles (mma.sync m16n8k16; 8 warps = 4 query blocks x 2 key halves, each
-//       warp its own partial); f32 inputs use SIMT tiles with the same partial layout.
-//   own CTAs (sequence n, head h, 256-key own block ob): one query against up to 256 keys,
-//       streamed with 16-byte coalesced loads (HBM-bound).
+//   prefix CTAs (head h, prefix block pb): read the block's keys/values of head h ONCE and
+//       produce partials (max, sum, acc[D]) for the queries of EVERY sequence at head h, so the
+//       shared prefix is read once per head, never once per sequence.  bf16 inputs stream 512
+//       keys per CTA through tensor-core tiles (mma.sync m16n8k16, online softmax over 32-key
+//       sub-tiles; 8 warps = 4 query blocks x 2 output halves); f32 inputs use SIMT tiles of 64
+//       keys (two partials per CTA).
+//   own CTAs (sequence n, head h, 512-key own block ob): one query against up to 512 keys,
+//       streamed with 16-byte coalesced loads, 8 in flight per lane (HBM-bound).
 // Each CTA writes its partials to the workspace and bumps a per-(n, h) arrival counter; the
 // CTA that completes a row merges its P partials (max of partial maxima, rescaled sums) and
 // writes o, max and sum.  The host clears the counters before each launch.
@@ -23,15 +24,18 @@
 namespace dbl {
 namespace {
 
-constexpr int BP = 64;        // prefix keys per prefix CTA
-constexpr int KSPLIT = 2;     // partials per prefix block (key halves of 32)
+constexpr int BP = 64;        // prefix keys per tile
+constexpr int KSPLIT = 2;     // f32 path: partials per prefix CTA (key halves of 32)
+constexpr int TILES_BF16 = 8; // bf16 path: 64-key tiles streamed by one prefix CTA (512 keys)
 constexpr int NQ = 64;        // queries per prefix tile
-constexpr int BO = 256;       // own keys per own CTA
+constexpr int BO = 512;       // own keys per own CTA
 constexpr int THREADS = 256;
+constexpr int MIN_BLOCKS = 3; // CTAs per SM the register budget is sized for
 constexpr int PAD = 8;        // bf16 row padding (row stride D+8 elements: conflict-free ldmatrix)
 
 struct RelayParams {
     int N, H, Lp, Lo, NPB, NOB, P;
+    int bpc, ppc;  // prefix keys per prefix CTA, partials per prefix CTA
     float scale;
     const void *q, *kp, *vp, *ko, *vo;
     const int32_t* own_len;
@@ -78,54 +82,67 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Merges the P partials of row (n, h) and writes the final output and statistics.
+// Merges the P partials of row (n, h) and writes the final output and statistics.  The weights
+// exp(m_i - M) of the partials are computed once into shared memory (wsm, >= P floats).
 template <int D, typename T>
-__device__ void merge_row(const RelayParams& p, int n, int h) {
+__device__ void merge_row(const RelayParams& p, int n, int h, float* wsm) {
+    __shared__ float s_m, s_tot;
+    __shared__ int s_any;
     const int tid = threadIdx.x;
     const size_t row = (size_t)n * p.H + h;
     const float* pm = p.part_max + row * p.P;
     const float* ps = p.part_sum + row * p.P;
-    float m = -FLT_MAX;
-    bool any = false;
-    for (int i = 0; i < p.P; ++i) {
-        if (__ldcg(ps + i) > 0.f) {
-            const float mi = __ldcg(pm + i);
-            m = any ? fmaxf(m, mi) : mi;
-            any = true;
+    if (tid < 32) {
+        float m = -FLT_MAX;
+        int any = 0;
+        for (int i = tid; i < p.P; i += 32)
+            if (__ldcg(ps + i) > 0.f) {
+                m = fmaxf(m, __ldcg(pm + i));
+                any = 1;
+            }
+        m = warp_max(m);
+        any = __any_sync(0xffffffffu, any);
+        float tot = 0.f;
+        for (int i = tid; i < p.P; i += 32) {
+            const float si = __ldcg(ps + i);
+            const float w = si > 0.f ? __expf(__ldcg(pm + i) - m) : 0.f;
+            wsm[i] = w;
+            tot += si * w;
+        }
+        tot = warp_sum(tot);
+        if (tid == 0) {
+            s_m = m;
+            s_tot = tot;
+            s_any = any;
         }
     }
+    __syncthreads();
     T* out = static_cast<T*>(p.out) + row * D;
-    if (!any) {
+    if (!s_any) {
         for (int d = tid; d < D; d += THREADS) out[d] = from_f32<T>(0.f);
         if (tid == 0) {
             if (p.row_max) p.row_max[row] = 0.f;
             if (p.row_sum) p.row_sum[row] = 1.f;
         }
-        return;
-    }
-    float total = 0.f;
-    for (int i = 0; i < p.P; ++i) {
-        const float si = __ldcg(ps + i);
-        if (si > 0.f) total += si * __expf(__ldcg(pm + i) - m);
-    }
-    const float* pa = p.part_acc + row * p.P * D;
-    for (int d = tid; d < D; d += THREADS) {
-        float acc = 0.f;
-        for (int i = 0; i < p.P; ++i) {
-            const float si = __ldcg(ps + i);
-            if (si > 0.f) acc += __ldcg(pa + (size_t)i * D + d) * __expf(__ldcg(pm + i) - m);
+    } else {
+        const float* pa = p.part_acc + row * p.P * D;
+        const float inv = 1.f / s_tot;
+        for (int d = tid; d < D; d += THREADS) {
+            float acc = 0.f;
+            for (int i = 0; i < p.P; ++i) acc = fmaf(wsm[i], __ldcg(pa + (size_t)i * D + d), acc);
+            out[d] = from_f32<T>(acc * inv);
         }
-        out[d] = from_f32<T>(acc / total);
+        if (tid == 0) {
+            if (p.row_max) p.row_max[row] = s_m;
+            if (p.row_sum) p.row_sum[row] = s_tot;
+        }
     }
-    if (tid == 0) {
-        if (p.row_max) p.row_max[row] = m;
-        if (p.row_sum) p.row_sum[row] = total;
-    }
+    __syncthreads();
 }
 
 // Adds `inc` arrivals to rows (n0 + r, h), r < nq, and merges the rows this CTA completed.
 template <int D, typename T>
-__device__ void arrive_rows(const RelayParams& p, int n0, int nq, int h, unsigned inc) {
+__device__ void arrive_rows(const RelayParams& p, int n0, int nq, int h, unsigned inc, float* wsm) {
     __shared__ int s_last[NQ];
     __shared__ int s_nlast;
     __threadfence();
@@ -141,7 +158,7 @@ __device__ void arrive_rows(const RelayParams& p, int n0, int nq, int h, unsigne
     if (nl > 0) {
         __threadfence();
         for (int i = 0; i < nl; ++i) {
-            merge_row<D, T>(p, s_last[i], h);
+            merge_row<D, T>(p, s_last[i], h, wsm);
             if (threadIdx.x == 0) p.counter[(size_t)s_last[i] * p.H + h] = 0u;
         }
     }
@@ -149,32 +166,25 @@ __device__ void arrive_rows(const RelayParams& p, int n0, int nq, int h, unsigne
 }
 
 // ------------------------------------------------------------------ prefix partials, bf16 MMA
+// A prefix CTA streams up to TILES_BF16 x 64 keys of head h through shared memory and keeps, per
+// query, an online-softmax partial (max, sum, acc[D]) -- the relay_attention_kernel.rs:73-111
+// recurrence, applied to 32-key sub-tiles of tensor-core scores.  Warp w owns queries
+// [16 (w & 3), +16) and output dimensions [D/2 (w >> 2), +D/2); both warps of a query block
+// compute the same scores.
 template <int D>
 __device__ void prefix_block_bf16(const RelayParams& p, unsigned char* smem) {
     using T = __nv_bfloat16;
     constexpr int LD = D + PAD;
-    T* sK = reinterpret_cast<T*>(smem);  // [BP][LD]
+    constexpr int DH = D / 2;  // output dims per warp
+    T* sQ = reinterpret_cast<T*>(smem);  // [NQ][LD]
+    T* sK = sQ + NQ * LD;                // [BP][LD]
     T* sV = sK + BP * LD;                // [BP][LD]
-    T* sQ = sV + BP * LD;                // [NQ][LD]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int h = blockIdx.x / p.NPB, pb = blockIdx.x - h * p.NPB;
-    const int key0 = pb * BP;
-    const int nkeys = min(BP, p.Lp - key0);
-    const T* kp = static_cast<const T*>(p.kp) + ((size_t)h * p.Lp + key0) * D;
-    const T* vp = static_cast<const T*>(p.vp) + ((size_t)h * p.Lp + key0) * D;
+    const int qb = warp & 3, dh = warp >> 2;
+    const int keyA = pb * p.bpc;
+    const int keyB = min(p.Lp, keyA + p.bpc);
     constexpr int CPR = D / 8;  // 16-byte chunks per row
-    for (int x = tid; x < BP * CPR; x += THREADS) {
-        const int r = x / CPR, c = (x - r * CPR) * 8;
-        uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-        if (r < nkeys) {
-            kv = __ldcs(reinterpret_cast<const uint4*>(kp + (size_t)r * D + c));
-            vv = __ldcs(reinterpret_cast<const uint4*>(vp + (size_t)r * D + c));
-        }
-        *reinterpret_cast<uint4*>(sK + r * LD + c) = kv;
-        *reinterpret_cast<uint4*>(sV + r * LD + c) = vv;
-    }
-    const int qb = warp & 3, kh = warp >> 2;  // 16-query block, 32-key half
-    const int kbase = kh * 32;
     for (int n0 = 0; n0 < p.N; n0 += NQ) {
         const int nq = min(NQ, p.N - n0);
         __syncthreads();
@@ -184,102 +194,128 @@ __device__ void prefix_block_bf16(const RelayParams& p, unsigned char* smem) {
             if (r < nq) qv = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) + ((size_t)(n0 + r) * p.H + h) * D + c);
             *reinterpret_cast<uint4*>(sQ + r * LD + c) = qv;
         }
-        __syncthreads();
-        // S[16 x 32] = Q[qb] K[kbase..kbase+32]^T
-        float s[4][4];
+        float m0 = -FLT_MAX, m1 = -FLT_MAX, l0 = 0.f, l1 = 0.f;
+        float o[DH / 8][4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
-#pragma unroll
-        for (int k0 = 0; k0 < D; k0 += 16) {
-            uint32_t a0, a1, a2, a3;
-            {
-                const int r = qb * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-                const int c = k0 + (lane >> 4) * 8;
-                ldsm_x4(smem_u32(sQ + r * LD + c), a0, a1, a2, a3);
+        for (int j = 0; j < DH / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+        for (int k0 = keyA; k0 < keyB; k0 += BP) {
+            const int nkeys = min(BP, keyB - k0);
+            const T* kp = static_cast<const T*>(p.kp) + ((size_t)h * p.Lp + k0) * D;
+            const T* vp = static_cast<const T*>(p.vp) + ((size_t)h * p.Lp + k0) * D;
+            __syncthreads();  // previous tile consumed
+            for (int x = tid; x < BP * CPR; x += THREADS) {
+                const int r = x / CPR, c = (x - r * CPR) * 8;
+                uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+                if (r < nkeys) {
+                    kv = __ldcs(reinterpret_cast<const uint4*>(kp + (size_t)r * D + c));
+                    vv = __ldcs(reinterpret_cast<const uint4*>(vp + (size_t)r * D + c));
+                }
+                *reinterpret_cast<uint4*>(sK + r * LD + c) = kv;
+                *reinterpret_cast<uint4*>(sV + r * LD + c) = vv;
             }
+            __syncthreads();
+#pragma unroll 1
+            for (int sub = 0; sub < BP; sub += 32) {
+                // S[16 x 32] = Q[qb] K[sub..sub+32]^T
+                float sc[4][4];
 #pragma unroll
-            for (int nt = 0; nt < 4; nt += 2) {
-                uint32_t b0, b1, b2, b3;
-                const int r = kbase + nt * 8 + (lane & 7) + (lane >> 4) * 8;
-                const int c = k0 + ((lane >> 3) & 1) * 8;
-                ldsm_x4(smem_u32(sK + r * LD + c), b0, b1, b2, b3);
-                mma_bf16(s[nt], a0, a1, a2, a3, b0, b1);
-                mma_bf16(s[nt + 1], a0, a1, a2, a3, b2, b3);
+                for (int j = 0; j < 4; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+#pragma unroll
+                for (int kk = 0; kk < D; kk += 16) {
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4(smem_u32(sQ + (qb * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * LD + kk + (lane >> 4) * 8), a0, a1, a2,
+                            a3);
+#pragma unroll
+                    for (int nt = 0; nt < 4; nt += 2) {
+                        uint32_t b0, b1, b2, b3;
+                        ldsm_x4(smem_u32(sK + (sub + nt * 8 + (lane & 7) + (lane >> 4) * 8) * LD + kk + ((lane >> 3) & 1) * 8), b0,
+                                b1, b2, b3);
+                        mma_bf16(sc[nt], a0, a1, a2, a3, b0, b1);
+                        mma_bf16(sc[nt + 1], a0, a1, a2, a3, b2, b3);
+                    }
+                }
+                float t0 = -FLT_MAX, t1 = -FLT_MAX;
+#pragma unroll
+                for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const bool ok = sub + nt * 8 + (lane & 3) * 2 + e < nkeys;
+                        sc[nt][e] = ok ? sc[nt][e] * p.scale : -FLT_MAX;
+                        sc[nt][2 + e] = ok ? sc[nt][2 + e] * p.scale : -FLT_MAX;
+                        t0 = fmaxf(t0, sc[nt][e]);
+                        t1 = fmaxf(t1, sc[nt][2 + e]);
+                    }
+                t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, 1));
+                t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, 2));
+                t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, 1));
+                t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, 2));
+                if (sub >= nkeys) continue;  // no key in this sub-tile
+                const float n0m = fmaxf(m0, t0), n1m = fmaxf(m1, t1);
+                const float c0 = l0 > 0.f ? __expf(m0 - n0m) : 0.f, c1 = l1 > 0.f ? __expf(m1 - n1m) : 0.f;
+                m0 = n0m;
+                m1 = n1m;
+                float s0 = 0.f, s1 = 0.f;
+                uint32_t pa[2][4];
+#pragma unroll
+                for (int nt = 0; nt < 4; ++nt) {
+                    float e0[2], e1[2];
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const bool ok = sub + nt * 8 + (lane & 3) * 2 + e < nkeys;
+                        e0[e] = ok ? __expf(sc[nt][e] - m0) : 0.f;
+                        e1[e] = ok ? __expf(sc[nt][2 + e] - m1) : 0.f;
+                        s0 += e0[e];
+                        s1 += e1[e];
+                    }
+                    const int ks = nt >> 1, hi = nt & 1;
+                    pa[ks][hi ? 2 : 0] = pack_bf16(e0[0], e0[1]);
+                    pa[ks][hi ? 3 : 1] = pack_bf16(e1[0], e1[1]);
+                }
+                s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+                s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+                s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+                s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+                l0 = l0 * c0 + s0;
+                l1 = l1 * c1 + s1;
+#pragma unroll
+                for (int j = 0; j < DH / 8; ++j) {
+                    o[j][0] *= c0;
+                    o[j][1] *= c0;
+                    o[j][2] *= c1;
+                    o[j][3] *= c1;
+                }
+                // O[16 x DH] += P[16 x 32] V[sub..sub+32][dh*DH ..]
+#pragma unroll
+                for (int ks = 0; ks < 2; ++ks) {
+#pragma unroll
+                    for (int dt = 0; dt < DH / 8; dt += 2) {
+                        uint32_t b0, b1, b2, b3;
+                        ldsm_x4_t(smem_u32(sV + (sub + ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * LD + dh * DH + dt * 8 +
+                                           (lane >> 4) * 8),
+                                  b0, b1, b2, b3);
+                        mma_bf16(o[dt], pa[ks][0], pa[ks][1], pa[ks][2], pa[ks][3], b0, b1);
+                        mma_bf16(o[dt + 1], pa[ks][0], pa[ks][1], pa[ks][2], pa[ks][3], b2, b3);
+                    }
+                }
             }
         }
-        // scale, mask, row max / exp / sum.  Thread rows: lane/4 and lane/4 + 8.
-        float m0 = -FLT_MAX, m1 = -FLT_MAX;
-#pragma unroll
-        for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const int key = kbase + nt * 8 + (lane & 3) * 2 + e;
-                const bool ok = key < nkeys;
-                s[nt][e] = ok ? s[nt][e] * p.scale : -FLT_MAX;
-                s[nt][2 + e] = ok ? s[nt][2 + e] * p.scale : -FLT_MAX;
-                m0 = fmaxf(m0, s[nt][e]);
-                m1 = fmaxf(m1, s[nt][2 + e]);
-            }
-        m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 1));
-        m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, 2));
-        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
-        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 2));
-        float l0 = 0.f, l1 = 0.f;
-        uint32_t pa[2][4];  // P as two k-steps of A fragments
-#pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-            float e0[2], e1[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const int key = kbase + nt * 8 + (lane & 3) * 2 + e;
-                const bool ok = key < nkeys;
-                e0[e] = ok ? __expf(s[nt][e] - m0) : 0.f;
-                e1[e] = ok ? __expf(s[nt][2 + e] - m1) : 0.f;
-                l0 += e0[e];
-                l1 += e1[e];
-            }
-            const int ks = nt >> 1, hi = nt & 1;
-            pa[ks][hi ? 2 : 0] = pack_bf16(e0[0], e0[1]);
-            pa[ks][hi ? 3 : 1] = pack_bf16(e1[0], e1[1]);
-        }
-        l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-        l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-        l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-        l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-        // O[16 x D] = P[16 x 32] V[kbase..kbase+32][D]
-        float o[D / 8][4];
-#pragma unroll
-        for (int j = 0; j < D / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-#pragma unroll
-        for (int ks = 0; ks < 2; ++ks) {
-#pragma unroll
-            for (int dt = 0; dt < D / 8; dt += 2) {
-                uint32_t b0, b1, b2, b3;
-                const int r = kbase + ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-                const int c = dt * 8 + (lane >> 4) * 8;
-                ldsm_x4_t(smem_u32(sV + r * LD + c), b0, b1, b2, b3);
-                mma_bf16(o[dt], pa[ks][0], pa[ks][1], pa[ks][2], pa[ks][3], b0, b1);
-                mma_bf16(o[dt + 1], pa[ks][0], pa[ks][1], pa[ks][2], pa[ks][3], b2, b3);
-            }
-        }
-        const int pidx = pb * KSPLIT + kh;
-        const int keys_here = max(0, min(32, nkeys - kbase));
+        const int pidx = pb;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
             const int r = qb * 16 + (lane >> 2) + half * 8;
             if (r < nq) {
                 const size_t row = (size_t)(n0 + r) * p.H + h;
-                float* dst = p.part_acc + (row * p.P + pidx) * D;
+                float* dst = p.part_acc + (row * p.P + pidx) * D + dh * DH;
 #pragma unroll
-                for (int dt = 0; dt < D / 8; ++dt)
+                for (int dt = 0; dt < DH / 8; ++dt)
                     *reinterpret_cast<float2*>(dst + dt * 8 + (lane & 3) * 2) = make_float2(o[dt][half * 2], o[dt][half * 2 + 1]);
-                if ((lane & 3) == 0) {
+                if (dh == 0 && (lane & 3) == 0) {
                     p.part_max[row * p.P + pidx] = half ? m1 : m0;
-                    p.part_sum[row * p.P + pidx] = keys_here > 0 ? (half ? l1 : l0) : 0.f;
+                    p.part_sum[row * p.P + pidx] = half ? l1 : l0;
                 }
             }
         }
-        arrive_rows<D, T>(p, n0, nq, h, KSPLIT);
+        arrive_rows<D, T>(p, n0, nq, h, 1u, reinterpret_cast<float*>(smem));
     }
 }
 
@@ -365,7 +401,7 @@ __device__ void prefix_block_f32(const RelayParams& p, unsigned char* smem) {
         }
     }
     // Both partials of every row are written: KSPLIT arrivals per row.
-    for (int n0 = 0; n0 < p.N; n0 += NQ) arrive_rows<D, float>(p, n0, min(NQ, p.N - n0), h, KSPLIT);
+    for (int n0 = 0; n0 < p.N; n0 += NQ) arrive_rows<D, float>(p, n0, min(NQ, p.N - n0), h, KSPLIT, reinterpret_cast<float*>(smem));
 }
 
 // ------------------------------------------------------------------------- own-segment partials
@@ -413,7 +449,7 @@ __device__ void own_block(const RelayParams& p, unsigned char* smem) {
         const T* q = static_cast<const T*>(p.q) + row * D + part * EPL;
 #pragma unroll
         for (int e = 0; e < EPL; ++e) qv[e] = to_f32(q[e]);
-#pragma unroll 4
+#pragma unroll 8
         for (int it = 0; it < ITER; ++it) {
             const int key = warp * KEYS_PER_WARP + it * KPW + sub;
             float d = 0.f;
@@ -449,7 +485,7 @@ __device__ void own_block(const RelayParams& p, unsigned char* smem) {
     float acc[EPL];
 #pragma unroll
     for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
-#pragma unroll 4
+#pragma unroll 8
     for (int it = 0; it < ITER; ++it) {
         const int key = warp * KEYS_PER_WARP + it * KPW + sub;
         if (key < nkeys) {
@@ -468,7 +504,7 @@ __device__ void own_block(const RelayParams& p, unsigned char* smem) {
 #pragma unroll
         for (int e = 0; e < EPL; ++e) sacc[warp * D + part * EPL + e] = acc[e];
     __syncthreads();
-    const int pi = p.NPB * KSPLIT + ob;
+    const int pi = p.NPB * p.ppc + ob;
     for (int d = tid; d < D; d += THREADS) {
         float a = 0.f;
 #pragma unroll
@@ -479,11 +515,11 @@ __device__ void own_block(const RelayParams& p, unsigned char* smem) {
         p.part_max[row * p.P + pi] = m;
         p.part_sum[row * p.P + pi] = nkeys > 0 ? l : 0.f;
     }
-    arrive_rows<D, T>(p, n, 1, h, 1u);
+    arrive_rows<D, T>(p, n, 1, h, 1u, se);
 }
 
 template <int D, typename T>
-__global__ void __launch_bounds__(THREADS) relay_merge_kernel(const RelayParams p) {
+__global__ void __launch_bounds__(THREADS, MIN_BLOCKS) relay_merge_kernel(const RelayParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     if ((int)blockIdx.x < p.H * p.NPB) {
         if constexpr (sizeof(T) == 2) prefix_block_bf16<D>(p, smem_raw);
@@ -496,16 +532,19 @@ __global__ void __launch_bounds__(THREADS) relay_merge_kernel(const RelayParams 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 struct Layout {
-    int NPB, NOB, P;
+    int NPB, NOB, P, bpc, ppc;
     size_t off_acc, off_max, off_sum, off_cnt, total;
 };
 
-Layout layout(int64_t N, int64_t H, int64_t D, int64_t Lp, int64_t Lo) {
+// bf16: one partial per 512-key prefix CTA; f32: two partials per 64-key prefix CTA.
+Layout layout(int64_t N, int64_t H, int64_t D, int64_t Lp, int64_t Lo, bool bf16) {
     Layout L{};
-    L.NPB = (int)((Lp + BP - 1) / BP);
+    L.bpc = bf16 ? BP * TILES_BF16 : BP;
+    L.ppc = bf16 ? 1 : KSPLIT;
+    L.NPB = (int)((Lp + L.bpc - 1) / L.bpc);
     L.NOB = (int)((Lo + BO - 1) / BO);
     if (L.NOB == 0) L.NOB = 1;  // one (empty) own partial keeps the arrival count uniform
-    L.P = L.NPB * KSPLIT + L.NOB;
+    L.P = L.NPB * L.ppc + L.NOB;
     const size_t rows = (size_t)N * H;
     L.off_acc = 0;
     L.off_max = align_up(L.off_acc + rows * L.P * D * sizeof(float), 256);
@@ -516,17 +555,19 @@ Layout layout(int64_t N, int64_t H, int64_t D, int64_t Lp, int64_t Lo) {
 }
 
 template <int D, typename T>
-size_t relay_smem() {
+size_t relay_smem(int P) {
     size_t prefix;
-    if (sizeof(T) == 2) prefix = sizeof(__nv_bfloat16) * (size_t)(2 * BP + NQ) * (D + PAD);
+    if (sizeof(T) == 2) prefix = sizeof(__nv_bfloat16) * (size_t)(NQ + 2 * BP) * (D + PAD);
     else prefix = sizeof(float) * (size_t)((BP / KSPLIT) * (D + 1) + (BP / KSPLIT) * D + 32 * (D + 1) + 32 * (BP / KSPLIT + 1));
-    const size_t own = sizeof(float) * (size_t)(BO + (THREADS / 32) * D);
+    size_t own = sizeof(float) * (size_t)(BO + (THREADS / 32) * D);
+    if (own < sizeof(float) * (size_t)P) own = sizeof(float) * (size_t)P;  // merge weights
+    if (prefix < sizeof(float) * (size_t)P) prefix = sizeof(float) * (size_t)P;
     return prefix > own ? prefix : own;
 }
 
 template <int D, typename T>
 int launch_relay(const RelayParams& p, cudaStream_t st) {
-    const size_t smem = relay_smem<D, T>();
+    const size_t smem = relay_smem<D, T>(p.P);
     cudaError_t e = cudaFuncSetAttribute(relay_merge_kernel<D, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_status(e, "relay: cudaFuncSetAttribute");
     const unsigned grid = (unsigned)(p.H * p.NPB + p.N * p.H * p.NOB);
@@ -554,20 +595,22 @@ int relay_validate(const dbl_relay_merge_args* a) {
         if (ptr && !aligned(ptr, 16)) return fail(DBL_ERR_INVALID_ARGUMENT, "relay: q, k and v must be 16-byte aligned");
     if (a->prefix_len > 0x7fffffff || a->own_cap > 0x7fffffff || a->n_seq * a->heads > 0x7fffffff)
         return fail(DBL_ERR_UNSUPPORTED, "relay: sizes exceed 32-bit limits");
-    const Layout L = layout(a->n_seq, a->heads, a->head_dim, a->prefix_len, a->own_cap);
+    const Layout L = layout(a->n_seq, a->heads, a->head_dim, a->prefix_len, a->own_cap, a->dtype == DBL_BF16);
     const int64_t grid = a->heads * (int64_t)L.NPB + a->n_seq * a->heads * (int64_t)L.NOB;
     if (grid > 0x7fffffffLL) return fail(DBL_ERR_UNSUPPORTED, "relay: grid too large");
     return DBL_OK;
 }
 
 size_t relay_workspace_bytes(int64_t N, int64_t H, int64_t D, int64_t Lp, int64_t Lo) {
-    return layout(N, H, D, Lp, Lo).total;
+    // the f32 layout has more prefix partials; it bounds both dtypes
+    const size_t a = layout(N, H, D, Lp, Lo, false).total, b = layout(N, H, D, Lp, Lo, true).total;
+    return a > b ? a : b;
 }
 
 // Launches the merge with its partials placed in `ws` (>= relay_workspace_bytes bytes).  The
 // arrival counters are cleared first on the same stream.
 int relay_launch(const dbl_relay_merge_args* a, void* ws, cudaStream_t st) {
-    const Layout L = layout(a->n_seq, a->heads, a->head_dim, a->prefix_len, a->own_cap);
+    const Layout L = layout(a->n_seq, a->heads, a->head_dim, a->prefix_len, a->own_cap, a->dtype == DBL_BF16);
     RelayParams p{};
     p.N = (int)a->n_seq;
     p.H = (int)a->heads;
@@ -576,6 +619,8 @@ int relay_launch(const dbl_relay_merge_args* a, void* ws, cudaStream_t st) {
     p.NPB = L.NPB;
     p.NOB = L.NOB;
     p.P = L.P;
+    p.bpc = L.bpc;
+    p.ppc = L.ppc;
     p.scale = a->scale;
     p.q = a->q;
     p.kp = a->prefix_k;
