@@ -434,14 +434,15 @@ __device__ void own_block(const RelayParams& p, unsigned char* smem) {
         float* sq = sacc;  // [D], reused before the value pass
         for (int c = tid; c < D; c += THREADS) sq[c] = to_f32(static_cast<const T*>(p.q)[row * D + c]) * p.scale;
         __syncthreads();
-        const int key = tid;
-        float d = 0.f;
-        if (key < nkeys) {
-            const T* kr = ko + (size_t)key * D;
+        for (int key = tid; key < BO; key += THREADS) {
+            float d = 0.f;
+            if (key < nkeys) {
+                const T* kr = ko + (size_t)key * D;
 #pragma unroll 8
-            for (int c = 0; c < D; ++c) d = fmaf(sq[c], to_f32(kr[c]), d);
+                for (int c = 0; c < D; ++c) d = fmaf(sq[c], to_f32(kr[c]), d);
+            }
+            se[key] = key < nkeys ? d : -FLT_MAX;
         }
-        se[key] = key < nkeys ? d : -FLT_MAX;
     } else {
         // bf16: warp-cooperative 16-byte loads; products of bf16 values are exact in f32 and the
         // score is scaled after the sum, as the tensor-core prefix path does.
