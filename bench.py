@@ -305,6 +305,49 @@ def bench_prefill(torch, dist, args, dev, rank, world):
     return result
 
 
+def bench_long(torch, dist, args, dev, rank, world):
+    """Config 4: one sequence B1/H16/T131072/d128 bf16, sharded along time over the ranks
+    (strong scaling); the hand-off is one all_gather of the span boundary objects."""
+    from delta_block_lm_b200 import shard
+
+    t_total = args.long_tokens
+    lo, hi = shard.shard_bounds(t_total, world, rank, align=CHUNK)
+    q, k, v, alpha, beta = make_prefill_inputs(torch, dev, 777 + rank, b=1, t=hi - lo)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        return shard.time_sharded_prefill(q, k, v, alpha, beta) if world > 1 else \
+            __import__("delta_block_lm_b200").gdn2_prefill(q, k, v, alpha, beta)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = tt.item()
+    ms_step = ms / args.steps
+    hbm, _, src = peaks()
+    alg = t_total * H * BYTES_PER_TOKEN_HEAD + H * D * D * 4
+    return {"metric": "GDN-2 long-context prefill Mtok/s (config 4, time-sharded)",
+            "value": t_total / (ms_step / 1e3) / 1e6, "unit": "Mtok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "strong", "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"c4 B1/H{H}/T{t_total}/d{D} bf16 chunk {CHUNK}, time-sharded over {world} GPU(s)",
+                       "span_tokens": hi - lo, "handoff": "all_gather of (A_g [H,K,K], B_g [H,K,V]) f32"},
+            "roofline": {"bound": "hbm", "algorithmic_bytes": alg, "achieved_gbs_aggregate": alg / (ms_step / 1e3) / 1e9,
+                         "peak_per_gpu": hbm, "peak_source": src}}
+
+
 def bench_decode(torch, args, dev):
     """Config 2: 256 sequences x 16 heads x 128^2 f32 state, 64 consecutive in-place steps."""
     import ctypes
@@ -405,6 +448,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true", help="skip the decode / relay lines")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["prefill", "long"], default="prefill",
+                    help="prefill: config 1 (the headline, weak-scaled); long: config 4 (time-sharded)")
+    ap.add_argument("--long-tokens", type=int, default=131072)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
@@ -424,6 +470,14 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     from delta_block_lm_b200 import _native
     _native.lib()
+    if args.workload == "long":
+        line = bench_long(torch, dist, args, dev, rank, world)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
     res = bench_prefill(torch, dist, args, dev, rank, world)
     line = {"metric": METRIC, "value": res["value"], "unit": "Mtok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
