@@ -2,16 +2,17 @@
 
 * Batch x head sharding: the (b, h) pairs are independent, so every rank runs
   ``kernels.gdn2_prefill`` on its own rows with no data-path collective (``shard_batch``).
-* Time sharding of one long sequence: rank g holds the contiguous token span
-  g of the sequence.  Over a span the state map is affine, S_end = A_g S_start + B_g, with A_g a
-  K x K matrix per head (``kernels.gdn2_span_transition``) and B_g the scan of the span from a
-  zero state.  The hand-off is one ``all_gather`` of the per-rank boundary objects (the only
-  collective), after which each rank composes the maps of the ranks before it and rescans its
-  span from its exact start state:
-      rank 0     : scans its span from the true initial state; its final state is S_in(1)
-      rank g > 0 : A_g, B_g from its span; S_in(g) = A_{g-1}(...(A_1 S_in(1) + B_1)...) + B_{g-1};
-                   then the scan from S_in(g) gives its outputs and final state.
-  The reference has no multi-device code; this module is the B200 build's own.
+* Time sharding of one long sequence.  Over a token span the state map is
+  affine, S_end = A S_start + B, with A a K x K matrix per head (``kernels.gdn2_span_transition``)
+  and B the scan of the span from a zero state.  A long span is cut into S segments that run as a
+  batch (a strided [S, T/S, H, D] view of the same memory, so S x H CTAs fill the GPU):
+      pass 1  all segment maps (A_s, B_s) in two batched launches;
+      fold    the start state of every segment by composing the maps before it (tiny);
+      pass 2  every segment rescanned from its exact start state in one batched launch.
+  Across GPUs, rank g holds the contiguous span g; the ranks exchange their composed span maps
+  with one ``all_gather`` (the only collective) and each rank folds the maps of the ranks before it
+  into its own start state before the local fold.
+The reference has no multi-device or time-parallel code; this module is the B200 build's own.
 """
 from __future__ import annotations
 
@@ -21,6 +22,8 @@ import torch
 import torch.distributed as dist
 
 from . import kernels
+
+CHUNK = 64
 
 
 def shard_bounds(n: int, world: int, rank: int, align: int = 1) -> Tuple[int, int]:
@@ -66,31 +69,122 @@ def exchange_span_states(first_or_transition: torch.Tensor, offset: Optional[tor
     return As, Bs
 
 
+def pick_segments(t_span: int, heads: int, sms: int = 148) -> int:
+    """Segments per span: the largest power of two with segments x heads <= sms whose segments are
+    whole 64-token chunks (1 when the span is short or heads alone fill the GPU)."""
+    s = 1
+    while (s * 2) * heads <= sms and t_span % (s * 2 * CHUNK) == 0:
+        s *= 2
+    return s
+
+
+def _segments(x: torch.Tensor, S: int) -> torch.Tensor:
+    """[1, T, ...] -> [S, T/S, ...] view of the same memory (segment s = tokens [s T/S, ...))."""
+    return x.reshape((S, x.shape[1] // S) + tuple(x.shape[2:]))
+
+
+def segment_maps(q, k, v, alpha, beta, S: int, *, scale=None, chunk_size=CHUNK):
+    """(A [S,H,K,K], B [S,H,K,V]) of the S equal segments of a [1, T, H, D] span (pass 1)."""
+    A = kernels.gdn2_span_transition(_segments(k, S), _segments(alpha, S), _segments(beta, S),
+                                     chunk_size=chunk_size)
+    _, Bm = kernels.gdn2_prefill(_segments(q, S), _segments(k, S), _segments(v, S),
+                                 _segments(alpha, S), _segments(beta, S), scale=scale,
+                                 want_output=False, chunk_size=chunk_size)
+    return A, Bm
+
+
+def compose_maps(A: torch.Tensor, Bm: torch.Tensor):
+    """The map of the whole span from its segment maps: (A_{S-1} ... A_0, fold of the B's)."""
+    At, Bt = A[0], Bm[0]
+    for s in range(1, A.shape[0]):
+        At = torch.matmul(A[s], At)
+        Bt = torch.matmul(A[s], Bt) + Bm[s]
+    return At.unsqueeze(0), Bt.unsqueeze(0)
+
+
+def segment_starts(A: torch.Tensor, Bm: torch.Tensor, start: torch.Tensor) -> torch.Tensor:
+    """Start states [S,H,K,V] of the S segments given the span's start state [1,H,K,V]."""
+    S = A.shape[0]
+    out = torch.empty_like(Bm)
+    s_cur = start[0]
+    for s in range(S):
+        out[s] = s_cur
+        if s + 1 < S:
+            s_cur = torch.matmul(A[s], s_cur) + Bm[s]
+    return out
+
+
+def segmented_prefill(q, k, v, alpha, beta, *, segments: Optional[int] = None, scale=None,
+                      initial_state: Optional[torch.Tensor] = None, chunk_size: int = CHUNK,
+                      maps=None, start: Optional[torch.Tensor] = None):
+    """Prefill of one long sequence [1, T, H, D] on one GPU through time segmentation.
+
+    Returns (out [1, T, H, V], final_state [1, H, K, V]).  `maps` reuses pass-1 results and
+    `start` overrides the span's start state (used by the multi-GPU driver).
+    """
+    if q.shape[0] != 1:
+        raise ValueError("segmented_prefill handles one sequence (batch 1)")
+    T, H = q.shape[1], q.shape[2]
+    S = segments or pick_segments(T, H)
+    if S == 1 or T % S:
+        return kernels.gdn2_prefill(q, k, v, alpha, beta, scale=scale,
+                                    initial_state=start if start is not None else initial_state,
+                                    chunk_size=chunk_size)
+    A, Bm = maps if maps is not None else segment_maps(q, k, v, alpha, beta, S, scale=scale,
+                                                       chunk_size=chunk_size)
+    K, V = q.shape[3], v.shape[3]
+    if start is None:
+        start = initial_state if initial_state is not None else torch.zeros(
+            (1, H, K, V), device=q.device, dtype=torch.float32)
+    starts = segment_starts(A, Bm, start.to(torch.float32))
+    out = torch.empty((1, T, H, V), device=q.device, dtype=q.dtype)
+    _, fin = kernels.gdn2_prefill(_segments(q, S), _segments(k, S), _segments(v, S),
+                                  _segments(alpha, S), _segments(beta, S), scale=scale,
+                                  initial_state=starts, out=_segments(out, S), chunk_size=chunk_size)
+    return out, fin[S - 1:S]
+
+
 def time_sharded_prefill(q, k, v, alpha, beta, *, group=None, scale: Optional[float] = None,
-                         initial_state: Optional[torch.Tensor] = None, chunk_size: int = 64
-                         ) -> Tuple[torch.Tensor, torch.Tensor]:
+                         initial_state: Optional[torch.Tensor] = None, chunk_size: int = CHUNK,
+                         segments: Optional[int] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """Prefill of one rank's time span of a sequence sharded along time.
 
-    q, k, v [B, T_span, H, D] and alpha, beta [B, T_span, H] are this rank's contiguous span (rank
-    order = time order; spans should be multiples of the 64-token chunk for best efficiency).
-    ``initial_state`` is the sequence's initial state and is used by rank 0 only.  Returns this
-    rank's outputs [B, T_span, H, V] and the state at the end of its span (on the last rank: the
-    sequence's final state).
+    q, k, v [1, T_span, H, D] and alpha, beta [1, T_span, H] are this rank's contiguous span (rank
+    order = time order).  ``initial_state`` is the sequence's initial state (rank 0 only).  Returns
+    this rank's outputs [1, T_span, H, V] and the state at the end of its span (on the last rank,
+    the sequence's final state).
     """
-    rank = dist.get_rank(group)
-    world = dist.get_world_size(group)
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
     if world == 1:
-        return kernels.gdn2_prefill(q, k, v, alpha, beta, scale=scale, initial_state=initial_state,
+        return segmented_prefill(q, k, v, alpha, beta, segments=segments, scale=scale,
+                                 initial_state=initial_state, chunk_size=chunk_size)
+    T, H = q.shape[1], q.shape[2]
+    S = segments or pick_segments(T, H)
+    if S == 1 or T % S:
+        # unsegmented span: rank 0 scans from the initial state, the others hand off (A_g, B_g)
+        if rank == 0:
+            out, fin = kernels.gdn2_prefill(q, k, v, alpha, beta, scale=scale,
+                                            initial_state=initial_state, chunk_size=chunk_size)
+            exchange_span_states(fin, None, rank, world, group)
+            return out, fin
+        A = kernels.gdn2_span_transition(k, alpha, beta, chunk_size=chunk_size)
+        _, Bspan = kernels.gdn2_prefill(q, k, v, alpha, beta, scale=scale, want_output=False,
+                                        chunk_size=chunk_size)
+        As, Bs = exchange_span_states(A, Bspan, rank, world, group)
+        s_in = fold_span_states(Bs[0], As, Bs, rank)
+        return kernels.gdn2_prefill(q, k, v, alpha, beta, scale=scale, initial_state=s_in,
                                     chunk_size=chunk_size)
+    maps = segment_maps(q, k, v, alpha, beta, S, scale=scale, chunk_size=chunk_size)
+    K, V = q.shape[3], v.shape[3]
+    At, Bt = compose_maps(*maps)
     if rank == 0:
-        out, fin = kernels.gdn2_prefill(q, k, v, alpha, beta, scale=scale,
-                                        initial_state=initial_state, chunk_size=chunk_size)
-        exchange_span_states(fin, None, rank, world, group)
-        return out, fin
-    A = kernels.gdn2_span_transition(k, alpha, beta, chunk_size=chunk_size)
-    _, Bspan = kernels.gdn2_prefill(q, k, v, alpha, beta, scale=scale, want_output=False,
-                                    chunk_size=chunk_size)
-    As, Bs = exchange_span_states(A, Bspan, rank, world, group)
-    s_in = fold_span_states(Bs[0], As, Bs, rank)
-    return kernels.gdn2_prefill(q, k, v, alpha, beta, scale=scale, initial_state=s_in,
-                                chunk_size=chunk_size)
+        s0 = initial_state.to(torch.float32) if initial_state is not None else torch.zeros(
+            (1, H, K, V), device=q.device, dtype=torch.float32)
+        exchange_span_states(torch.matmul(At, s0) + Bt, None, rank, world, group)
+        start = s0
+    else:
+        As, Bs = exchange_span_states(At, Bt, rank, world, group)
+        start = fold_span_states(Bs[0], As, Bs, rank)
+    return segmented_prefill(q, k, v, alpha, beta, segments=S, scale=scale, chunk_size=chunk_size,
+                             maps=maps, start=start)

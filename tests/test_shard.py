@@ -131,3 +131,58 @@ def test_time_sharded_prefill_two_gpus(cuda, native_lib):
     for rank, e_out, e_fin in results:
         # same kernels and inputs; the hand-off adds the f32 fold and one bf16 rounding of S_in
         assert e_out < TOL_BF16 and e_fin < TOL_BF16, (rank, e_out, e_fin)
+
+
+def test_segment_composition_matches_oracle():
+    # compose_maps / segment_starts on oracle segment maps reproduce the sequential scan's states.
+    from delta_block_lm_b200 import shard
+    from oracle import oracle as O
+    B, T, H, D, S = 1, 48, 2, 6, 4
+    q, k, v, alpha, beta = baseline_inputs(12, B, T, H, D, D)
+    L = T // S
+    As, Bs = [], []
+    for s in range(S):
+        sl = slice(s * L, (s + 1) * L)
+        eye = np.broadcast_to(np.eye(D), (1, H, D, D)).copy()
+        _, A, _ = O.scan_scalar(q[:, sl], k[:, sl], np.zeros(k[:, sl].shape), alpha[:, sl], beta[:, sl], initial=eye)
+        _, Bm, _ = O.scan_scalar(q[:, sl], k[:, sl], v[:, sl], alpha[:, sl], beta[:, sl])
+        As.append(A[0])
+        Bs.append(Bm[0])
+    A = torch.tensor(np.stack(As))
+    Bm = torch.tensor(np.stack(Bs))
+    init = torch.tensor(0.1 * np.random.default_rng(0).standard_normal((1, H, D, D)))
+    starts = shard.segment_starts(A, Bm, init)
+    At, Bt = shard.compose_maps(A, Bm)
+    for s in range(S):
+        _, ref, _ = O.scan_scalar(q[:, :s * L], k[:, :s * L], v[:, :s * L], alpha[:, :s * L],
+                                  beta[:, :s * L], initial=init.numpy()) if s else (None, init.numpy(), None)
+        assert np.abs(starts[s].numpy() - ref[0]).max() < 1e-10
+    _, full, _ = O.scan_scalar(q, k, v, alpha, beta, initial=init.numpy())
+    assert np.abs((torch.matmul(At, init) + Bt).numpy() - full).max() < 1e-10
+
+
+def test_pick_segments():
+    from delta_block_lm_b200.shard import pick_segments
+    assert pick_segments(131072, 16) == 8      # 128 CTAs on 148 SMs
+    assert pick_segments(16384, 16) == 8
+    assert pick_segments(4096, 16) == 8
+    assert pick_segments(100, 16) == 1          # not whole chunks
+    assert pick_segments(131072, 128) == 1      # heads already fill the GPU
+
+
+@pytest.mark.gpu
+def test_segmented_prefill_matches_single_scan(cuda, native_lib):
+    import delta_block_lm_b200 as dbl
+    from delta_block_lm_b200 import shard
+    B, T, H, D = 1, 4096, 2, 128
+    q, k, v, alpha, beta = baseline_inputs(31, B, T, H, D, D)
+    q, k, v = bf16_round(q), bf16_round(k), bf16_round(v)
+    tb = lambda x: torch.as_tensor(x).to(cuda, torch.bfloat16)  # noqa: E731
+    tf = lambda x: torch.as_tensor(x).to(cuda, torch.float32)  # noqa: E731
+    init = tf(0.02 * np.random.default_rng(3).standard_normal((1, H, D, D)))
+    out, fin = shard.segmented_prefill(tb(q), tb(k), tb(v), tf(alpha), tf(beta), initial_state=init)
+    ref_out, ref_fin = dbl.gdn2_prefill(tb(q), tb(k), tb(v), tf(alpha), tf(beta), initial_state=init)
+    torch.cuda.synchronize()
+    assert shard.pick_segments(T, H) > 1
+    assert rel_err(out.float().cpu().numpy(), ref_out.float().cpu().numpy()) < TOL_BF16
+    assert rel_err(fin.cpu().numpy(), ref_fin.cpu().numpy()) < TOL_BF16
