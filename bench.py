@@ -315,9 +315,10 @@ def bench_long(torch, dist, args, dev, rank, world):
     q, k, v, alpha, beta = make_prefill_inputs(torch, dev, 777 + rank, b=1, t=hi - lo)
     stream = torch.cuda.current_stream(dev)
 
+    segs = shard.pick_segments(hi - lo, H)
+
     def step():
-        return shard.time_sharded_prefill(q, k, v, alpha, beta) if world > 1 else \
-            __import__("delta_block_lm_b200").gdn2_prefill(q, k, v, alpha, beta)
+        return shard.time_sharded_prefill(q, k, v, alpha, beta, segments=segs)
 
     for _ in range(args.warmup):
         step()
@@ -343,7 +344,8 @@ def bench_long(torch, dist, args, dev, rank, world):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "strong", "dtype": "bf16", "data": "synthetic",
             "config": {"workload": f"c4 B1/H{H}/T{t_total}/d{D} bf16 chunk {CHUNK}, time-sharded over {world} GPU(s)",
-                       "span_tokens": hi - lo, "handoff": "all_gather of (A_g [H,K,K], B_g [H,K,V]) f32"},
+                       "span_tokens": hi - lo, "segments_per_gpu": segs,
+                       "handoff": "all_gather of (A_g [H,K,K], B_g [H,K,V]) f32"},
             "roofline": {"bound": "hbm", "algorithmic_bytes": alg, "achieved_gbs_aggregate": alg / (ms_step / 1e3) / 1e9,
                          "peak_per_gpu": hbm, "peak_source": src}}
 
