@@ -97,7 +97,10 @@ EXPORTS = [
     ("dbl_relay_merge_workspace_bytes", ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64]),
     ("dbl_relay_merge_decode", ctypes.c_int,
      [ctypes.POINTER(RelayMergeArgs), _vp, ctypes.c_size_t, _vp]),
+    ("dbl_relay_merge_decode_noalloc", ctypes.c_int, [ctypes.POINTER(RelayMergeArgs), _vp]),
 ]
+
+RELAY_NOALLOC_SCRATCH_BYTES = 16 << 20  # DBL_RELAY_NOALLOC_SCRATCH_BYTES
 
 _lib = None
 _lock = threading.Lock()

@@ -602,6 +602,11 @@ int relay_validate(const dbl_relay_merge_args* a) {
     return DBL_OK;
 }
 
+// Workspace bytes of one call with the layout of its own dtype.
+size_t relay_call_workspace_bytes(const dbl_relay_merge_args* a) {
+    return layout(a->n_seq, a->heads, a->head_dim, a->prefix_len, a->own_cap, a->dtype == DBL_BF16).total;
+}
+
 size_t relay_workspace_bytes(int64_t N, int64_t H, int64_t D, int64_t Lp, int64_t Lo) {
     // the f32 layout has more prefix partials; it bounds both dtypes
     const size_t a = layout(N, H, D, Lp, Lo, false).total, b = layout(N, H, D, Lp, Lo, true).total;

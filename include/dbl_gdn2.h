@@ -197,6 +197,22 @@ size_t dbl_relay_merge_workspace_bytes(int64_t n_seq, int64_t heads, int64_t hea
 int dbl_relay_merge_decode(const dbl_relay_merge_args *args, void *workspace,
                            size_t workspace_bytes, dbl_stream_t stream);
 
+/* Relay merge for callers that cannot allocate device memory at the call site -- a host whose
+ * device memory belongs to its own pooling allocator, or a serving loop that must not call
+ * cudaMalloc/cudaFree while it runs.  No counterpart in the reference.  Same arguments and results
+ * as dbl_relay_merge_decode; the split-softmax partials go to a fixed array of
+ * DBL_RELAY_NOALLOC_SCRATCH_BYTES that the library keeps in device memory (reserved on every
+ * device that loads the library, until the process exits), so the call allocates nothing.
+ *   - A call whose partials need more than that (see dbl_relay_merge_workspace_bytes) returns
+ *     DBL_ERR_WORKSPACE and launches nothing.
+ *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress) with
+ *     that device current; make that first call before any stream capture.
+ *   - Every call on a device shares the one array and the array keeps the last call's partials
+ *     (the arrival counters are cleared at the start of each call): calls that overlap on the GPU,
+ *     e.g. on two streams, race on it. */
+#define DBL_RELAY_NOALLOC_SCRATCH_BYTES (16u << 20)
+int dbl_relay_merge_decode_noalloc(const dbl_relay_merge_args *args, dbl_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
