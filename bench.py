@@ -57,15 +57,25 @@ def ncu_traffic(kernel_key: str):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples for one GPU during the timed region."""
+    """SM clock and clock-event-reason samples of one GPU during the timed region (read-only).
+
+    NVML is polled from a thread about every millisecond, so a timed region of a few milliseconds
+    still gets samples; the first sample is taken before start() returns.  Without NVML it falls
+    back to an `nvidia-smi -lms 20` process.
+    """
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits (nvml.h: nvmlClocksEventReason*)
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
 
     def __init__(self, device_index: int):
         self.proc = None
+        self.thread = None
         self.ident = None
+        self.samples = []
         try:
             import torch
             uuid = str(torch.cuda.get_device_properties(device_index).uuid)
@@ -73,7 +83,39 @@ class ClockSampler:
         except Exception:
             self.ident = str(device_index)
 
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(self.ident)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(int(os.environ.get("LOCAL_RANK", "0")))
+
     def start(self):
+        import threading
+        try:
+            nv, h = self._nvml_handle()
+            reasons_fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self._stop = threading.Event()
+
+            def poll():
+                while True:
+                    try:
+                        self.samples.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                                             int(reasons_fn(h))))
+                    except Exception:
+                        return
+                    if self._stop.wait(0.001):
+                        return
+
+            self.samples.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)), int(reasons_fn(h))))
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.thread = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", self.ident, f"--query-gpu={self.FIELDS}",
@@ -83,6 +125,14 @@ class ClockSampler:
             self.proc = None
 
     def stop(self):
+        if self.thread is not None:
+            self._stop.set()
+            self.thread.join(timeout=5)
+            if not self.samples:
+                return None
+            reasons = sorted({n for _, bits in self.samples for n, b in self.REASON_BITS.items() if bits & b})
+            return {"sm_mhz": statistics.median(s for s, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                    "reasons": reasons, "samples": len(self.samples), "source": "nvml"}
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -108,7 +158,7 @@ class ClockSampler:
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi"}
 
 
 # ------------------------------------------------------------------------------ CPU baseline
@@ -445,13 +495,14 @@ def bench_relay(torch, args, dev):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true", help="skip the decode / relay lines")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["prefill", "long"], default="prefill",
-                    help="prefill: config 1 (the headline, weak-scaled); long: config 4 (time-sharded)")
+    ap.add_argument("--workload", choices=["prefill", "long", "decode", "relay"], default="prefill",
+                    help="prefill: config 1 (the headline, weak-scaled); long: config 4 (time-sharded); "
+                         "decode: config 2 alone; relay: config 3 alone (1 GPU)")
     ap.add_argument("--long-tokens", type=int, default=131072)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -479,6 +530,23 @@ def main():
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()
+        return 0
+    if args.workload in ("decode", "relay"):
+        # single-kernel lines (the same measurements as the headline's `secondary` object)
+        if world > 1:
+            raise SystemExit("--workload decode/relay runs on one GPU")
+        if args.workload == "decode":
+            r = bench_decode(torch, args, dev)
+            line = {"metric": "GDN-2 decode tok/s (config 2)", "value": r["tok_per_s"], "unit": "tok/s",
+                    "ms_per_step": r["us_per_step"] / 1e3}
+        else:
+            r = bench_relay(torch, args, dev)
+            line = {"metric": "relay merge (sequence, head) queries/s (config 3)", "value": r["queries_per_s"],
+                    "unit": "queries/s", "ms_per_step": r["us_per_call"] / 1e3}
+        line.update({"n_gpus": 1, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+                     "config": {"workload": r["workload"]}, "roofline": r["roofline"],
+                     "gpu_launches": r["gpu_launches"]})
+        print(json.dumps(line), flush=True)
         return 0
     res = bench_prefill(torch, dist, args, dev, rank, world)
     line = {"metric": METRIC, "value": res["value"], "unit": "Mtok/s", "n_gpus": world,
