@@ -16,10 +16,10 @@
 // B200 mapping.  One CTA per (b, h), 512 threads, one CTA per SM (all 512 TMEM columns); the
 // block launches at 128 registers per thread and setmaxnreg moves them to the chain warps.
 //   * prep warps 0-7: TMA loads of the chunk tiles (K and Q 128-byte swizzled, V plain), the gate
-//     scan, UMMA [K;Q] K^T -> TMEM, decay masks, the blocked 64x64 unit-lower inverse (16x16
-//     diagonal blocks by substitution, off-diagonal blocks column by column on mma.sync tf32 tiles),
-//     T and P written as
-//     bf16 UMMA operands.  Prep runs one chunk ahead of the chain (two smem stages); the chain
+//     scan, UMMA [K;Q] K^T -> TMEM, decay masks, the 64x64 unit-lower inverse by block doubling
+//     (8x8 diagonal blocks by substitution, then 8 -> 16 -> 32 -> 64 joins, the last two on
+//     mma.sync tf32 tiles), T and P written as bf16 UMMA operands.  Prep runs one chunk ahead of
+//     the chain (two smem stages); the chain
 //     leader issues the loads of chunk c + 2 as soon as it is done with chunk c.
 //   * chain warps 8-15: the state-dependent chain, transposed so that the value column j of the
 //     state is TMEM lane j and every activation stays in TMEM (A operands of the TS form):
@@ -51,9 +51,9 @@ namespace {
 constexpr int C = 64;
 constexpr int DK = 128;
 constexpr int NTHREADS = 512;
-constexpr int NPREP = 256;   // warps 0-7, 96 registers each after setmaxnreg
-constexpr int NCHAIN = 256;  // warps 8-15, 160 registers each (the f32 state lives in registers)
-constexpr int PREP_REGS = 96, CHAIN_REGS = 160;
+constexpr int NPREP = 256;   // warps 0-7, 104 registers each after setmaxnreg
+constexpr int NCHAIN = 256;  // warps 8-15, 152 registers each (the f32 state lives in registers)
+constexpr int PREP_REGS = 104, CHAIN_REGS = 152;
 static_assert(NPREP * PREP_REGS + NCHAIN * CHAIN_REGS <= 65536, "register split exceeds the launch budget");
 constexpr int BAR_PREP = 1, BAR_CHAIN = 2;
 
@@ -79,7 +79,8 @@ constexpr int LDA = 68;   // A rows (16-byte aligned: a lane writes its row with
 constexpr int LDT = 68;   // T rows (read as float4: 16-byte aligned stride)
 constexpr uint32_t OFF_ST = OFF_SA + C * LDA * 4;
 constexpr uint32_t OFF_SX = OFF_ST + C * LDT * 4;
-constexpr uint32_t OFF_SG = OFF_SX + 1024 * 4;
+constexpr int XLD = 40;   // inverse scratch rows (B-fragment reads hit 32 distinct banks)
+constexpr uint32_t OFF_SG = OFF_SX + 1280 * 4;
 constexpr uint32_t OFF_SEM = OFF_SG + 64 * 4;   // 2^-g_s (fast decay path), 16-byte aligned
 constexpr uint32_t OFF_SCNT = OFF_SEM + 64 * 4;
 constexpr uint32_t OFF_SWT = OFF_SCNT + 64 * 4;
@@ -113,6 +114,39 @@ __device__ __forceinline__ uint64_t kdesc(const uint8_t* p) {  // K-major, 128-B
     return umma_sdesc_sw128(smem_u32addr(p), 16, 1024);
 }
 
+// c (16 x 8) += A[16 x 8 ks] B[8 ks x 8] over the k-steps [ks0, ks1) on mma.sync tf32; A and B are
+// row-major f32 in shared memory (leading dimensions lda, ldb); g = lane / 4, t4 = lane % 4.
+__device__ __forceinline__ void tile_mma_tf32(float (&c)[4], const float* A, int lda, const float* Bm, int ldb,
+                                              int ks0, int ks1, int g, int t4) {
+    for (int ks = ks0; ks < ks1; ++ks) {
+        const float* Ar = A + g * lda + 8 * ks + t4;
+        const float* Bc = Bm + (8 * ks + t4) * ldb + g;
+        mma_tf32_16x8x8(c, to_tf32(Ar[0]), to_tf32(Ar[8 * lda]), to_tf32(Ar[4]), to_tf32(Ar[8 * lda + 4]),
+                        to_tf32(Bc[0]), to_tf32(Bc[4 * ldb]));
+    }
+}
+
+// Writes sgn * c (a 16 x 8 accumulator fragment) to the row-major f32 tile D.
+__device__ __forceinline__ void store_tile(float* D, int ld, const float (&c)[4], int g, int t4, float sgn) {
+    *reinterpret_cast<float2*>(D + g * ld + 2 * t4) = make_float2(sgn * c[0], sgn * c[1]);
+    *reinterpret_cast<float2*>(D + (g + 8) * ld + 2 * t4) = make_float2(sgn * c[2], sgn * c[3]);
+}
+
+// Writes sgn * c as bf16 into a K-major operand tile of 64 columns (128-byte rows, 128-byte swizzle):
+// rows row0 + g and row0 + g + 8 (row0 a multiple of 8), 16-byte chunk `chunk` (columns 8 chunk ..).
+__device__ __forceinline__ void store_tile_bf16(uint8_t* Tt, int row0, int chunk, const float (&c)[4], int g, int t4,
+                                                float sgn) {
+    const int sw = (chunk ^ g) << 4;
+    *reinterpret_cast<uint32_t*>(Tt + (row0 + g) * 128 + sw + 4 * t4) = pack_bf16x2(sgn * c[0], sgn * c[1]);
+    *reinterpret_cast<uint32_t*>(Tt + (row0 + g + 8) * 128 + sw + 4 * t4) = pack_bf16x2(sgn * c[2], sgn * c[3]);
+}
+
+__device__ __forceinline__ void zero_tile_bf16(uint8_t* Tt, int row0, int chunk, int g, int t4) {
+    const int sw = (chunk ^ g) << 4;
+    *reinterpret_cast<uint32_t*>(Tt + (row0 + g) * 128 + sw + 4 * t4) = 0u;
+    *reinterpret_cast<uint32_t*>(Tt + (row0 + g + 8) * 128 + sw + 4 * t4) = 0u;
+}
+
 __global__ void __launch_bounds__(NTHREADS, 1)
     gdn2_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                            const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -127,6 +161,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint64_t* bar_m2 = bars + 8;
     uint64_t* bar_m3 = bars + 9;
     uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + OFF_TSLOT);
+    int* serr = reinterpret_cast<int*>(smem + OFF_TSLOT + 8);  // the block's wait-error word
     float* sA = reinterpret_cast<float*>(smem + OFF_SA);
     float* sT = reinterpret_cast<float*>(smem + OFF_ST);
     float* sXs = reinterpret_cast<float*>(smem + OFF_SX);
@@ -152,6 +187,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     };
 
     if (tid == 0) {
+        *serr = 0;
         for (int i = 0; i < (int)NBARS; ++i) mbar_init(bars + i, 1);
         fence_mbar_init();
         prefetch_tmap(&tm_q);
@@ -212,6 +248,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             // ---- gates: threads 0..63, token r = tid
             const float a = nx_a, be = nx_b, vf = nx_v;
             if (c + 1 < nchunks) fetch_gates(c + 1);
+            if (warp == 2) {
+                // [K;Q] K^T on the tensor cores needs only the TMA tiles: warp 2 (outside the gate scan)
+                // issues it as soon as they land, so it runs while warps 0-1 scan the gates
+                mbar_wait(&bar_full[s], (c >> 1) & 1, serr, 1);
+                if (lane == 0) {
+                    tc_fence_after();
+                    const uint8_t* X = stX(s);
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint8_t* xa = X + (kk >> 2) * 16384 + (kk & 3) * 32;
+                        umma_ss(tmem + TM_KK, kdesc(xa), kdesc(xa), IDESC_M128_N64, kk > 0 ? 1u : 0u);
+                    }
+                    umma_commit(bar_kk);
+                }
+                __syncwarp();
+            }
             float lg = 0.f;
             int z = 0;
             if (tid < C) {
@@ -237,7 +289,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 z += swc[0];
             }
             // the stage's TMA data (and, through the producer's wait, the stage itself) is ours
-            mbar_wait(&bar_full[s], (c >> 1) & 1, p.err, 1);
+            mbar_wait(&bar_full[s], (c >> 1) & 1, serr, 1);
             float* G = stG(s);
             if (tid < C) {
                 sg[tid] = lg;
@@ -259,18 +311,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if (tid == C - 1) G[G_GC] = gamma;
             }
             named_bar_sync(BAR_PREP, NPREP);
-            // ---- [K;Q] K^T on the tensor cores
-            if (tid == 0) {
-                tc_fence_after();
-                const uint8_t* X = stX(s);
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint8_t* a = X + (kk >> 2) * 16384 + (kk & 3) * 32;
-                    umma_ss(tmem + TM_KK, kdesc(a), kdesc(a), IDESC_M128_N64, kk > 0 ? 1u : 0u);
-                }
-                umma_commit(bar_kk);
-            }
-            mbar_wait(bar_kk, c & 1, p.err, 2);
+            mbar_wait(bar_kk, c & 1, serr, 2);
             tc_fence_after();
             {
                 // row n = 32q + lane of [K;Q]; columns s in [32 half, 32 half + 32)
@@ -358,97 +399,86 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             tc_fence_before();
             named_bar_sync(BAR_PREP, NPREP);
-            // ---- T = (I + A)^-1: diagonal 16 x 16 blocks by substitution
+            // ---- T = (I + A)^-1 by block doubling.  Level 0 inverts the eight 8 x 8 diagonal blocks by
+            //      substitution; every later level joins pairs of inverted n x n diagonal blocks into
+            //      2n x 2n ones through the lower-left block of a unit-lower block inverse,
+            //          T10 = -T11 (A10 T00),
+            //      and writes zeros to the upper-right block.  8 -> 16 runs in f32 FMAs (one element per
+            //      thread), 16 -> 32 and 32 -> 64 on mma.sync tf32 tiles (4 and 8 warps).  Depth: one
+            //      8-step substitution and three two-product levels.
             if (tid < C) {
-                const int blk = tid >> 4, c0 = tid & 15;
-                const float* Ab = sA + (16 * blk) * LDA + 16 * blk;
-                // x = column c0 of the block inverse: x_s = [s == c0] - sum_{s' < s} A[s][s'] x_s',
-                // accumulated column by column so the dependency depth is 16, not 120
-                float x[16], acc[16];
+                const int blk = tid >> 3, c0 = tid & 7;
+                const float* Ab = sA + (8 * blk) * LDA + 8 * blk;
+                // column c0 of the block inverse: x_s = [s == c0] - sum_{s' < s} A[s][s'] x_s'
+                float x[8], acc[8];
 #pragma unroll
-                for (int r = 0; r < 16; ++r) acc[r] = 0.f;
+                for (int r = 0; r < 8; ++r) acc[r] = 0.f;
 #pragma unroll
-                for (int s2 = 0; s2 < 16; ++s2) {
+                for (int s2 = 0; s2 < 8; ++s2) {
                     x[s2] = (s2 < c0) ? 0.f : (s2 == c0 ? 1.f : -acc[s2]);
 #pragma unroll
-                    for (int r = s2 + 1; r < 16; ++r) acc[r] = fmaf(Ab[r * LDA + s2], x[s2], acc[r]);
+                    for (int r = s2 + 1; r < 8; ++r) acc[r] = fmaf(Ab[r * LDA + s2], x[s2], acc[r]);
                 }
 #pragma unroll
-                for (int r = 0; r < 16; ++r) sT[(16 * blk + r) * LDT + 16 * blk + c0] = x[r];
-            } else {
-                for (int e = tid - C; e < 6 * 256; e += NPREP - C) {
-                    const int pair = e >> 8, rem = e & 255;
-                    const int bb = pair < 3 ? 0 : (pair < 5 ? 1 : 2);
-                    const int aa = pair < 3 ? pair + 1 : (pair < 5 ? pair - 1 : 3);
-                    sT[(16 * bb + (rem >> 4)) * LDT + 16 * aa + (rem & 15)] = 0.f;
-                }
+                for (int r = 0; r < 8; ++r) sT[(8 * blk + r) * LDT + 8 * blk + c0] = x[r];
             }
             named_bar_sync(BAR_PREP, NPREP);
-            // ---- off-diagonal blocks on tensor cores (mma.sync tf32).  Block T[b][a] depends only on
-            //      the blocks of its own column a and on the diagonal block T[b][b]:
-            //        X = sum_{a <= m < b} A[b][m] T[m][a],   T[b][a] = -T[b][b] X,
-            //      so warp a (a = 0, 1, 2) walks column a downwards with warp-level syncs only.
-            if (warp < 3) {
-                const int aa = warp;
-                const int g = lane >> 2, t4 = lane & 3;
-                float* Xw = sXs + warp * 256;  // warp-private 16 x 16 scratch
-                for (int bb = aa + 1; bb < 4; ++bb) {
-                    float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-                    for (int ks = 0; ks < 2 * (bb - aa); ++ks) {
-                        const int m0 = 16 * aa + 8 * ks;
-                        const float* Ar = sA + (16 * bb + g) * LDA + m0 + t4;
-                        const uint32_t a0 = to_tf32(Ar[0]), a1 = to_tf32(Ar[8 * LDA]);
-                        const uint32_t a2 = to_tf32(Ar[4]), a3 = to_tf32(Ar[8 * LDA + 4]);
-#pragma unroll
-                        for (int nt = 0; nt < 2; ++nt) {
-                            const float* Tc = sT + (m0 + t4) * LDT + 16 * aa + 8 * nt + g;
-                            mma_tf32_16x8x8(c[nt], a0, a1, a2, a3, to_tf32(Tc[0]), to_tf32(Tc[4 * LDT]));
-                        }
-                    }
-#pragma unroll
-                    for (int nt = 0; nt < 2; ++nt) {
-                        float* xw = Xw + 8 * nt + 2 * t4;
-                        xw[g * 16] = c[nt][0];
-                        xw[g * 16 + 1] = c[nt][1];
-                        xw[(g + 8) * 16] = c[nt][2];
-                        xw[(g + 8) * 16 + 1] = c[nt][3];
-                    }
-                    __syncwarp();
-                    float e[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll
-                    for (int ks = 0; ks < 2; ++ks) {
-                        const float* Tr = sT + (16 * bb + g) * LDT + 16 * bb + 8 * ks + t4;
-                        const uint32_t a0 = to_tf32(Tr[0]), a1 = to_tf32(Tr[8 * LDT]);
-                        const uint32_t a2 = to_tf32(Tr[4]), a3 = to_tf32(Tr[8 * LDT + 4]);
-#pragma unroll
-                        for (int nt = 0; nt < 2; ++nt) {
-                            const float* Xc = Xw + (8 * ks + t4) * 16 + 8 * nt + g;
-                            mma_tf32_16x8x8(e[nt], a0, a1, a2, a3, to_tf32(Xc[0]), to_tf32(Xc[4 * 16]));
-                        }
-                    }
-#pragma unroll
-                    for (int nt = 0; nt < 2; ++nt) {
-                        float* Tw = sT + (16 * bb + g) * LDT + 16 * aa + 8 * nt + 2 * t4;
-                        Tw[0] = -e[nt][0];
-                        Tw[1] = -e[nt][1];
-                        Tw[8 * LDT] = -e[nt][2];
-                        Tw[8 * LDT + 1] = -e[nt][3];
-                    }
-                    __syncwarp();  // T[b][a] is read by the next block of this column; Xw is reused
-                }
-            }
-            named_bar_sync(BAR_PREP, NPREP);
-            // ---- T as a bf16 K-major operand (rows r', 64 columns r, 128-B swizzle)
             {
+                // 8 -> 16: pair pr joins the diagonal blocks at a0 = 16 pr and a0 + 8; thread = (pr, i, jj)
+                const int pr = tid >> 6, i = (tid >> 3) & 7, jj = tid & 7, a0 = 16 * pr;
+                float x = 0.f;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) x = fmaf(sA[(a0 + 8 + i) * LDA + a0 + k], sT[(a0 + k) * LDT + a0 + jj], x);
+                sXs[tid] = x;  // X[pr][i][jj]
+                named_bar_sync(BAR_PREP, NPREP);
+                float t = 0.f;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) t = fmaf(sT[(a0 + 8 + i) * LDT + a0 + 8 + k], sXs[64 * pr + 8 * k + jj], t);
+                sT[(a0 + 8 + i) * LDT + a0 + jj] = -t;
+                sT[(a0 + i) * LDT + a0 + 8 + jj] = 0.f;
+            }
+            named_bar_sync(BAR_PREP, NPREP);
+            {
+                // T goes to the stage as the bf16 K-major UMMA operand (rows r', 64 columns r, 128-byte
+                // swizzle) block by block, as soon as each block is final
+                const int g = lane >> 2, t4 = lane & 3;
                 uint8_t* Tt = stT(s);
-                for (int e = tid; e < 512; e += NPREP) {
-                    const int row = e >> 3, cc = e & 7;
+                if (warp < 4) {
+                    // 16 -> 32: warp = (pair pr, column tile nt); X and T10 tiles are 16 x 8 and the
+                    // second product only needs this warp's own X columns
+                    const int pr = warp >> 1, nt = warp & 1, a0 = 32 * pr;
+                    float* Xp = sXs + pr * (16 * XLD);
+                    float c4[4] = {0.f, 0.f, 0.f, 0.f};
+                    // T00 is lower triangular: k-steps below 8 nt contribute nothing
+                    tile_mma_tf32(c4, sA + (a0 + 16) * LDA + a0, LDA, sT + a0 * LDT + a0 + 8 * nt, LDT, nt, 2, g, t4);
+                    store_tile(Xp + 8 * nt, XLD, c4, g, t4, 1.f);
+                    __syncwarp();
+                    float d[4] = {0.f, 0.f, 0.f, 0.f};
+                    tile_mma_tf32(d, sT + (a0 + 16) * LDT + a0 + 16, LDT, Xp + 8 * nt, XLD, 0, 2, g, t4);
+                    store_tile(sT + (a0 + 16) * LDT + a0 + 8 * nt, LDT, d, g, t4, -1.f);  // read by 32 -> 64
+                    store_tile_bf16(Tt, a0 + 16, (a0 >> 3) + nt, d, g, t4, -1.f);
+                    zero_tile_bf16(Tt, a0, ((a0 + 16) >> 3) + nt, g, t4);
+                } else {
+                    // warps 4-7 meanwhile: the four 16 x 16 diagonal blocks are final
+                    const int e = tid - 128, row = e >> 1, cc = 2 * (row >> 4) + (e & 1);
                     const float4 u = *reinterpret_cast<const float4*>(sT + row * LDT + cc * 8);
                     const float4 w = *reinterpret_cast<const float4*>(sT + row * LDT + cc * 8 + 4);
-                    uint4 val = make_uint4(pack_bf16x2(u.x, u.y), pack_bf16x2(u.z, u.w), pack_bf16x2(w.x, w.y),
-                                           pack_bf16x2(w.z, w.w));
-                    *reinterpret_cast<uint4*>(Tt + row * 128 + ((cc ^ (row & 7)) << 4)) = val;
+                    *reinterpret_cast<uint4*>(Tt + row * 128 + ((cc ^ (row & 7)) << 4)) =
+                        make_uint4(pack_bf16x2(u.x, u.y), pack_bf16x2(u.z, u.w), pack_bf16x2(w.x, w.y),
+                                   pack_bf16x2(w.z, w.w));
                 }
+                named_bar_sync(BAR_PREP, NPREP);
+                // 32 -> 64: warp = (row tile mt, column tile nt) of the 32 x 32 lower-left block
+                const int mt = warp >> 2, nt = warp & 3;
+                float c4[4] = {0.f, 0.f, 0.f, 0.f};
+                tile_mma_tf32(c4, sA + (32 + 16 * mt) * LDA, LDA, sT + 8 * nt, LDT, nt, 4, g, t4);
+                store_tile(sXs + 16 * mt * XLD + 8 * nt, XLD, c4, g, t4, 1.f);
+                named_bar_sync(BAR_PREP, NPREP);
+                float d[4] = {0.f, 0.f, 0.f, 0.f};
+                // T11 is lower triangular: rows 16 mt .. 16 mt + 15 need k-steps below 2 mt + 2
+                tile_mma_tf32(d, sT + (32 + 16 * mt) * LDT + 32, LDT, sXs + 8 * nt, XLD, 0, 2 * mt + 2, g, t4);
+                store_tile_bf16(Tt, 32 + 16 * mt, nt, d, g, t4, -1.f);
+                zero_tile_bf16(Tt, 16 * mt, 4 + nt, g, t4);
             }
             fence_proxy_async_smem();
             named_bar_sync(BAR_PREP, NPREP);
@@ -481,7 +511,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         };
         // MMA1 of chunk c: D1[j][r] = sum_i S^T[j][i] K[r][i]   (issued by the chain leader)
         auto issue_mma1 = [&](int c) {
-            mbar_wait(&bar_prep[c & 1], (c >> 1) & 1, p.err, 4);
+            mbar_wait(&bar_prep[c & 1], (c >> 1) & 1, serr, 4);
             tc_fence_after();
             const uint8_t* X = stX(c & 1);
 #pragma unroll
@@ -509,13 +539,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const int s = c & 1;
             const uint32_t par = c & 1;
             const uint32_t tm_do = TM_DO + 64 * (c & 1);
-            mbar_wait(&bar_prep[s], (c >> 1) & 1, p.err, 4);
+            mbar_wait(&bar_prep[s], (c >> 1) & 1, serr, 4);
             const float* G = stG(s);
             // private copy of what this chunk's output needs, so stage s can be reloaded early
             float* om = com + 64 * (c & 1);
             if (ct < C) om[ct] = G[G_VAL + ct] != 0.f ? G[G_OM + ct] : 0.f;
             const float gC = G[G_GC];
-            mbar_wait(bar_m1, par, p.err, 5);
+            mbar_wait(bar_m1, par, serr, 5);
             tc_fence_after();
             // ---- E1: R^T[j][r] = beta_r V[r][j] - beta_r gamma_r (K S)[r][j],  r in [32 hh, 32 hh + 32),
             //      written in place as a bf16 pair: for the 16 rows r of TMEM columns [16k, 16k + 16),
@@ -565,7 +595,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
                 umma_commit(bar_m2);
             }
-            mbar_wait(bar_m2, par, p.err, 6);
+            mbar_wait(bar_m2, par, serr, 6);
             tc_fence_after();
             // ---- E2: Delta^T for r' in [32 hh, 32 hh + 32) as bf16, in place: for the 16 rows of
             //      columns [16k, 16k + 16), the Gamma[63][r']-scaled copy goes to [16k, +8) and the plain
@@ -616,7 +646,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 umma_commit(bar_m3);
                 tma_store_wait_read0();  // the previous chunk's output tile has left shared memory
             }
-            mbar_wait(bar_m3, par, p.err, 7);
+            mbar_wait(bar_m3, par, serr, 7);
             tc_fence_after();
             // every MMA and every E-stage read of stage s is done: load chunk c + 2 into it now
             if (ct == 0 && c + 2 < nchunks) issue_loads(c + 2);
@@ -673,6 +703,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tc_fence_after();
         tmem_dealloc(tmem, 512);
     }
+    if (tid == 0 && *serr != 0) atomicExch(p.err, *serr);  // reported by dbl_device_error
 }
 
 // ------------------------------------------------------------------------------ host side

@@ -52,12 +52,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Waits for phase `parity` of `bar` to complete, for at most kWaitLimitNs.  On expiry stores
-// `code` to *err and returns false.
+// Waits for phase `parity` of `bar` to complete, for at most kWaitLimitNs.  `err` is the block's
+// error word in shared memory: a wait that expires stores `code` there, and while it is set every
+// wait returns false at once, so a block whose protocol broke runs to its end instead of spending
+// kWaitLimitNs at each later wait.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     while (!mbar_try_wait(bar, parity)) {
+        if (*reinterpret_cast<volatile int*>(err) != 0) return false;
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
             atomicExch(err, code);
             return false;
