@@ -19,23 +19,27 @@
 //     scan, UMMA [K;Q] K^T -> TMEM, decay masks, the 64x64 unit-lower inverse by block doubling
 //     (8x8 diagonal blocks by substitution, then 8 -> 16 -> 32 -> 64 joins, the last two on
 //     mma.sync tf32 tiles), T and P written as bf16 UMMA operands.  Prep runs one chunk ahead of
-//     the chain (two smem stages); the chain
-//     leader issues the loads of chunk c + 2 as soon as it is done with chunk c.
+//     the chain.  Shared-memory stages: K/Q tiles x 3 (the chain leader loads chunk c + 3 as soon
+//     as the MMAs of chunk c are done), gates x 3, V x 2 (a chunk's V stage then stages its output
+//     tile), and T / P x 2 (handed back to the prep warps through an mbarrier; the prep warps wait
+//     for it only when they start writing T and P~, after the first half of the inverse).
 //   * chain warps 8-15: the state-dependent chain, transposed so that the value column j of the
 //     state is TMEM lane j and every activation stays in TMEM (A operands of the TS form):
-//       MMA1  D1[j][r]  = sum_i S^T[j][i] K[r][i]          (A = S^T bf16 in TMEM)
-//       E1    R^T[j][r] = beta_r V[r][j] - beta_r gamma_r D1[j][r]   -> TMEM (bf16 hi + lo pair)
-//       MMA2  D2[j][r'] = sum_r R^T[j][r] T[r'][r]          (Delta^T; hi and lo accumulate)
-//       E2    Delta^T scaled by Gamma[63][r'] and plain                     -> TMEM (bf16)
+//       MMA1  D1[j][r]  = sum_i S^T[j][i] K[r][i]          (A = S^T bf16 in TMEM; issued as one
+//             N = 128 product with DQ[j][r] = sum_i S^T[j][i] Q[r][i] over the [K;Q] rows)
+//       E1    R^T[j][r] = beta_r V[r][j] - beta_r gamma_r D1[j][r]   -> TMEM (fp16)
+//       MMA2  D2[j][r'] = sum_r R^T[j][r] T[r'][r]          (Delta^T; T in fp16)
+//       E2    Delta^T scaled by Gamma[63][r'] (bf16, for MMA3) and plain (fp16, for MMA4) -> TMEM
 //       MMA3  D3[j][i]  = sum_r' (Gamma Delta)^T[j][r'] K[r'][i]   (B = K tile read MN-major)
-//       MMA4  DO[j][r]  = sum_i S^T[j][i] Q[r][i] + sum_r' Delta^T[j][r'] P~[r][r']
-//             with P~ = P / om_r and om_r = scale gamma_r (P~ as a bf16 hi + lo pair)
-//     R and P~ are carried as bf16 pairs because their rounding dominates the error budget: with
-//     single bf16 operands the output error reaches the 2e-2 bound at T = 4096, with the pairs it
-//     stays near 1e-2 (see tests/chunk_model.py).
+//       MMA4  DP[j][r]  = sum_r' Delta^T[j][r'] P[r][r'],  P = (scale Gamma o Q K^T, s <= r) in fp16
+//     Operand formats: MMAs whose B operand is an input tile (K, Q) stay bf16; the ones whose
+//     operands are produced inside the kernel (R, T, Delta, P) run in fp16, whose 11-bit mantissa
+//     keeps the output error below the bf16-pair scheme's with half the MMAs (tests/chunk_model.py).
+//     Magnitudes: T has entries of at most 1 for unit keys and beta <= 1; R, Delta and P are of the
+//     order of V and scale; a value beyond fp16 range is reported through dbl_device_error.
 //       E3    S[i][j] = gamma_63 S + D3 (f32 master state in registers, 64 per thread),
 //             S^T -> TMEM bf16; then MMA1 of the next chunk is issued and, while it runs,
-//             O[r][j] = om_r DO[j][r] -> smem -> TMA store (DO is double-buffered in TMEM).
+//             O[r][j] = scale gamma_r DQ[j][r] + DP[j][r] -> the chunk's V stage -> TMA store.
 // Roofline: HBM (intensity ~172 FLOP/B at the algorithmic minimum of 1032 B per token-head).
 #include <cuda.h>
 
@@ -44,7 +48,8 @@
 
 namespace dbl {
 
-__device__ int g_tc_error = 0;  // set by a bounded wait that gave up (code = site id)
+__device__ int g_tc_error = 0;  // set by a bounded wait that gave up (code = site id) or a range check
+constexpr int kTcRangeError = 100;
 
 namespace {
 
@@ -57,24 +62,32 @@ constexpr int PREP_REGS = 104, CHAIN_REGS = 152;
 static_assert(NPREP * PREP_REGS + NCHAIN * CHAIN_REGS <= 65536, "register split exceeds the launch budget");
 constexpr int BAR_PREP = 1, BAR_CHAIN = 2;
 
-// TMEM column map (512 columns, f32 accumulators unless noted)
+// TMEM column map (512 columns, f32 accumulators unless noted).  Two 128-column regions alternate
+// by chunk parity p = c & 1: region p holds [D1 | DO] of chunk c (K S, then the output accumulator
+// that starts as Q S), and region 1 - p holds D3 of chunk c, the state increment.  D3 of chunk c
+// lands on [D1 | DO] of chunk c - 1 only after that chunk's output has been read, and [D1 | DO] of
+// chunk c + 1 lands on D3 of chunk c only after E3 has read it.
 constexpr uint32_t TM_S = 0;      // S^T bf16 A operand: 64 cols (128 keys, 2 per column)
-constexpr uint32_t TM_D1 = 64;    // K S (64 cols) -> R^T as a bf16 hi/lo pair in place
+constexpr uint32_t TM_KK = 64;    // prep: [K;Q] K^T, 64 cols
 constexpr uint32_t TM_D2 = 128;   // Delta^T (64 cols) -> scaled / plain bf16 in place
-constexpr uint32_t TM_D3 = 192;   // (Gamma Delta)^T K, 128 cols
-constexpr uint32_t TM_DO = 320;   // output accumulators, 2 x 64 cols (double-buffered by chunk)
-constexpr uint32_t TM_KK = 448;   // prep: [K;Q] K^T, 64 cols
+constexpr uint32_t TM_R0 = 192;   // regions 0 and 1, 128 cols each (192..447)
+constexpr uint32_t TM_PD = 448;   // P Delta half of the output, 64 cols
 
-// Shared memory (offsets from a 1024-aligned base)
+// Shared memory (offsets from a 1024-aligned base).  The K/Q tiles and the gates have three stages,
+// so the loads of chunk c + 3 go out as soon as the chain is done with chunk c; V, T and P have
+// two.  A chunk's V stage doubles as the staging tile of its output (V is dead after E1).
+constexpr int NXS = 3;
 constexpr uint32_t X_BYTES = 2 * 128 * 128;  // 2 key blocks x 128 rows ([K;Q]) x 128 B, swizzled
-constexpr uint32_t V_BYTES = C * 128 * 2;    // [64][128] bf16 plain
+constexpr uint32_t V_BYTES = C * 128 * 2;    // [64][128] bf16 plain (V in, then O out)
 constexpr uint32_t T_BYTES = C * 128;        // [64][64] bf16 swizzled
-constexpr uint32_t P_BYTES = 2 * C * 128;     // P as a bf16 pair: hi tile, then lo tile
+constexpr uint32_t P_BYTES = C * 128;         // [64][64] fp16 swizzled
 constexpr uint32_t G_BYTES = 2048;           // gates
-constexpr uint32_t STAGE_BYTES = X_BYTES + V_BYTES + T_BYTES + P_BYTES + G_BYTES;  // 75776
-constexpr uint32_t OFF_O = 2 * STAGE_BYTES;       // output tile staging [64][128] bf16
-constexpr uint32_t O_BYTES = C * 128 * 2;
-constexpr uint32_t OFF_SA = OFF_O + O_BYTES;
+constexpr uint32_t OFF_X = 0;
+constexpr uint32_t OFF_V = OFF_X + NXS * X_BYTES;
+constexpr uint32_t OFF_T = OFF_V + 2 * V_BYTES;
+constexpr uint32_t OFF_P = OFF_T + 2 * T_BYTES;
+constexpr uint32_t OFF_G = OFF_P + 2 * P_BYTES;
+constexpr uint32_t OFF_SA = OFF_G + NXS * G_BYTES;
 constexpr int LDA = 68;   // A rows (16-byte aligned: a lane writes its row with 16-byte stores)
 constexpr int LDT = 68;   // T rows (read as float4: 16-byte aligned stride)
 constexpr uint32_t OFF_ST = OFF_SA + C * LDA * 4;
@@ -84,17 +97,21 @@ constexpr uint32_t OFF_SG = OFF_SX + 1280 * 4;
 constexpr uint32_t OFF_SEM = OFF_SG + 64 * 4;   // 2^-g_s (fast decay path), 16-byte aligned
 constexpr uint32_t OFF_SCNT = OFF_SEM + 64 * 4;
 constexpr uint32_t OFF_SWT = OFF_SCNT + 64 * 4;
-constexpr uint32_t OFF_COM = OFF_SWT + 64;        // chain copy of the output multipliers [2][64] (16-B aligned)
-constexpr uint32_t OFF_BAR = (OFF_COM + 2 * 64 * 4 + 7) / 8 * 8;
-constexpr uint32_t NBARS = 11;
+constexpr uint32_t OFF_COM = OFF_SWT + 64;        // chain copy of the output multipliers [2][2][64] (16-B aligned)
+constexpr uint32_t OFF_BAR = (OFF_COM + 2 * 128 * 4 + 7) / 8 * 8;
+constexpr uint32_t NBARS = 13;
 constexpr uint32_t OFF_TSLOT = OFF_BAR + NBARS * 8;
 constexpr uint32_t SMEM_BYTES = OFF_TSLOT + 16 + 1024;  // + alignment slack
+static_assert(SMEM_BYTES <= 232448, "shared memory beyond the 227 KB a block can have");
+static_assert(OFF_T % 1024 == 0 && OFF_P % 1024 == 0 && T_BYTES % 1024 == 0, "swizzled tiles need 1024-B alignment");
 // gate arrays inside a stage's G region (floats)
-constexpr int G_CB = 0, G_CG = 64, G_CD = 128, G_OM = 192, G_VAL = 256, G_GC = 320, G_QZ = 384;
-constexpr float kTinyDecay = 7.888609052210118e-31f;  // 2^-100: a smaller gamma_r counts as zero
+constexpr int G_CB = 0, G_CG = 64, G_CD = 128, G_OM = 192, G_VAL = 256, G_GC = 320;
+constexpr float kF16Max = 65504.f;
 
 constexpr uint32_t IDESC_M128_N64 = umma_idesc_bf16(128, 64, false);
 constexpr uint32_t IDESC_M128_N128_BMN = umma_idesc_bf16(128, 128, true);
+constexpr uint32_t IDESC_M128_N128 = umma_idesc_bf16(128, 128, false);
+constexpr uint32_t IDESC_F16_M128_N64 = umma_idesc_f16(128, 64, false);
 
 struct TcParams {
     int B, T, H, nchunks;
@@ -132,16 +149,16 @@ __device__ __forceinline__ void store_tile(float* D, int ld, const float (&c)[4]
     *reinterpret_cast<float2*>(D + (g + 8) * ld + 2 * t4) = make_float2(sgn * c[2], sgn * c[3]);
 }
 
-// Writes sgn * c as bf16 into a K-major operand tile of 64 columns (128-byte rows, 128-byte swizzle):
+// Writes sgn * c as fp16 into a K-major operand tile of 64 columns (128-byte rows, 128-byte swizzle):
 // rows row0 + g and row0 + g + 8 (row0 a multiple of 8), 16-byte chunk `chunk` (columns 8 chunk ..).
-__device__ __forceinline__ void store_tile_bf16(uint8_t* Tt, int row0, int chunk, const float (&c)[4], int g, int t4,
-                                                float sgn) {
+__device__ __forceinline__ void store_tile_f16(uint8_t* Tt, int row0, int chunk, const float (&c)[4], int g, int t4,
+                                               float sgn) {
     const int sw = (chunk ^ g) << 4;
-    *reinterpret_cast<uint32_t*>(Tt + (row0 + g) * 128 + sw + 4 * t4) = pack_bf16x2(sgn * c[0], sgn * c[1]);
-    *reinterpret_cast<uint32_t*>(Tt + (row0 + g + 8) * 128 + sw + 4 * t4) = pack_bf16x2(sgn * c[2], sgn * c[3]);
+    *reinterpret_cast<uint32_t*>(Tt + (row0 + g) * 128 + sw + 4 * t4) = pack_f16x2(sgn * c[0], sgn * c[1]);
+    *reinterpret_cast<uint32_t*>(Tt + (row0 + g + 8) * 128 + sw + 4 * t4) = pack_f16x2(sgn * c[2], sgn * c[3]);
 }
 
-__device__ __forceinline__ void zero_tile_bf16(uint8_t* Tt, int row0, int chunk, int g, int t4) {
+__device__ __forceinline__ void zero_tile_16(uint8_t* Tt, int row0, int chunk, int g, int t4) {
     const int sw = (chunk ^ g) << 4;
     *reinterpret_cast<uint32_t*>(Tt + (row0 + g) * 128 + sw + 4 * t4) = 0u;
     *reinterpret_cast<uint32_t*>(Tt + (row0 + g + 8) * 128 + sw + 4 * t4) = 0u;
@@ -154,12 +171,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-    uint64_t* bar_full = bars + 0;   // [2] TMA landed
-    uint64_t* bar_prep = bars + 4;   // [2] prep done with the chunk
-    uint64_t* bar_kk = bars + 6;
-    uint64_t* bar_m1 = bars + 7;
-    uint64_t* bar_m2 = bars + 8;
-    uint64_t* bar_m3 = bars + 9;
+    uint64_t* bar_x = bars + 0;      // [3] K/Q tiles landed
+    uint64_t* bar_v = bars + 3;      // [2] V tile landed
+    uint64_t* bar_prep = bars + 5;   // [2] prep done with the chunk (T, P, gates ready)
+    uint64_t* bar_tfree = bars + 7;  // [2] the chain is done with a T / P stage
+    uint64_t* bar_kk = bars + 9;
+    uint64_t* bar_m1 = bars + 10;
+    uint64_t* bar_m2 = bars + 11;
+    uint64_t* bar_m3 = bars + 12;
     uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + OFF_TSLOT);
     int* serr = reinterpret_cast<int*>(smem + OFF_TSLOT + 8);  // the block's wait-error word
     float* sA = reinterpret_cast<float*>(smem + OFF_SA);
@@ -171,20 +190,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     float* swt = reinterpret_cast<float*>(smem + OFF_SWT);
     int* swc = reinterpret_cast<int*>(smem + OFF_SWT + 32);
     float* com = reinterpret_cast<float*>(smem + OFF_COM);
-    uint8_t* Ost = smem + OFF_O;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int bh = blockIdx.x;
     const int b = bh / p.H, h = bh - b * p.H;
     const int nchunks = p.nchunks;
 
-    auto stX = [&](int s) { return smem + s * STAGE_BYTES; };
-    auto stV = [&](int s) { return smem + s * STAGE_BYTES + X_BYTES; };
-    auto stT = [&](int s) { return smem + s * STAGE_BYTES + X_BYTES + V_BYTES; };
-    auto stP = [&](int s) { return smem + s * STAGE_BYTES + X_BYTES + V_BYTES + T_BYTES; };
-    auto stG = [&](int s) {
-        return reinterpret_cast<float*>(smem + s * STAGE_BYTES + X_BYTES + V_BYTES + T_BYTES + P_BYTES);
-    };
+    auto stX = [&](int xs) { return smem + OFF_X + xs * X_BYTES; };
+    auto stV = [&](int s) { return smem + OFF_V + s * V_BYTES; };
+    auto stT = [&](int s) { return smem + OFF_T + s * T_BYTES; };
+    auto stP = [&](int s) { return smem + OFF_P + s * P_BYTES; };
+    auto stG = [&](int xs) { return reinterpret_cast<float*>(smem + OFF_G + xs * G_BYTES); };
 
     if (tid == 0) {
         *serr = 0;
@@ -207,24 +223,30 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (warp < 8) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(PREP_REGS));
     else asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(CHAIN_REGS));
 
-    auto issue_loads = [&](int c) {
-        const int s = c & 1;
-        uint8_t* X = stX(s);
-        mbar_arrive_expect_tx(&bar_full[s], p.v_zero ? X_BYTES : X_BYTES + V_BYTES);
+    auto load_x = [&](int c) {  // K and Q tiles of chunk c into stage c % 3
+        const int xs = c % NXS;
+        uint8_t* X = stX(xs);
+        mbar_arrive_expect_tx(&bar_x[xs], X_BYTES);
 #pragma unroll
         for (int ib = 0; ib < 2; ++ib) {
-            tma_load_4d(X + ib * 16384, &tm_k, &bar_full[s], ib * 64, c * C, h, b);
-            tma_load_4d(X + ib * 16384 + 8192, &tm_q, &bar_full[s], ib * 64, c * C, h, b);
+            tma_load_4d(X + ib * 16384, &tm_k, &bar_x[xs], ib * 64, c * C, h, b);
+            tma_load_4d(X + ib * 16384 + 8192, &tm_q, &bar_x[xs], ib * 64, c * C, h, b);
         }
-        if (!p.v_zero) tma_load_4d(stV(s), &tm_v, &bar_full[s], 0, c * C, h, b);
+    };
+    auto load_v = [&](int c) {  // V tile of chunk c into stage c & 1
+        if (p.v_zero) return;
+        const int s = c & 1;
+        mbar_arrive_expect_tx(&bar_v[s], V_BYTES);
+        tma_load_4d(stV(s), &tm_v, &bar_v[s], 0, c * C, h, b);
     };
 
     if (warp < 8) {
         // =================================================================== prep warps
         const int q = warp & 3, half = warp >> 2;
         if (tid == 0) {
-            issue_loads(0);
-            if (nchunks > 1) issue_loads(1);
+            for (int c = 0; c < NXS && c < nchunks; ++c) load_x(c);
+            load_v(0);
+            if (nchunks > 1) load_v(1);
         }
         // gates of the next chunk are fetched one iteration ahead (their load latency is hidden)
         float nx_a = 1.f, nx_b = 0.f, nx_v = 0.f;
@@ -243,18 +265,65 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
         };
         fetch_gates(0);
+        // P = (scale Gamma o Q K^T, s <= r) in fp16 into stage s, from the Q rows of [K;Q] K^T in TMEM
+        // (lanes 64..127, so warps with q = 2, 3): row r = 32 (q - 2) + lane, columns [32 half, 32 half
+        // + 32).  Fast path: P[r][s] = (scale 2^g_r) 2^-g_s (q_r . k_s), every factor finite in f32.
+        auto write_p = [&](int s, bool fast) {
+            const int r = 32 * (q - 2) + lane;
+            const float gr = sg[r];
+            const int cr = scnt[r];
+            const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + TM_KK + 32 * half;
+            uint32_t gl[32];
+            tmem_ld16(ta, *reinterpret_cast<uint32_t(*)[16]>(&gl[0]));
+            tmem_ld16(ta + 16, *reinterpret_cast<uint32_t(*)[16]>(&gl[16]));
+            tmem_ld_wait();
+            const float4* sem4 = reinterpret_cast<const float4*>(sem + 32 * half);
+            const int s0 = 32 * half;
+            float big = 0.f;
+            if (fast) {
+                const float er = p.scale * exp2f(gr);
+#pragma unroll
+                for (int e4 = 0; e4 < 8; ++e4) {
+                    const float4 m = sem4[e4];
+                    const int e = s0 + 4 * e4;
+                    gl[4 * e4] = __float_as_uint(e <= r ? er * m.x * __uint_as_float(gl[4 * e4]) : 0.f);
+                    gl[4 * e4 + 1] = __float_as_uint(e + 1 <= r ? er * m.y * __uint_as_float(gl[4 * e4 + 1]) : 0.f);
+                    gl[4 * e4 + 2] = __float_as_uint(e + 2 <= r ? er * m.z * __uint_as_float(gl[4 * e4 + 2]) : 0.f);
+                    gl[4 * e4 + 3] = __float_as_uint(e + 3 <= r ? er * m.w * __uint_as_float(gl[4 * e4 + 3]) : 0.f);
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 32; ++e)
+                    gl[e] = __float_as_uint((s0 + e <= r && scnt[s0 + e] == cr) ? p.scale * exp2f(gr - sg[s0 + e]) * __uint_as_float(gl[e]) : 0.f);
+            }
+            uint8_t* P = stP(s);
+#pragma unroll
+            for (int x = 0; x < 4; ++x) {
+                uint32_t ph[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float v0 = __uint_as_float(gl[8 * x + 2 * u]), v1 = __uint_as_float(gl[8 * x + 2 * u + 1]);
+                    big = fmaxf(big, fmaxf(fabsf(v0), fabsf(v1)));
+                    ph[u] = pack_f16x2(v0, v1);
+                }
+                const int cc = 4 * half + x;
+                *reinterpret_cast<uint4*>(P + r * 128 + ((cc ^ (r & 7)) << 4)) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+            }
+            if (!(big <= kF16Max)) atomicExch(p.err, kTcRangeError);
+        };
         for (int c = 0; c < nchunks; ++c) {
-            const int s = c & 1;
+            const int s = c & 1, xs = c % NXS;
+            const uint32_t xpar = (uint32_t)(c / NXS) & 1u;
             // ---- gates: threads 0..63, token r = tid
             const float a = nx_a, be = nx_b, vf = nx_v;
             if (c + 1 < nchunks) fetch_gates(c + 1);
             if (warp == 2) {
                 // [K;Q] K^T on the tensor cores needs only the TMA tiles: warp 2 (outside the gate scan)
                 // issues it as soon as they land, so it runs while warps 0-1 scan the gates
-                mbar_wait(&bar_full[s], (c >> 1) & 1, serr, 1);
+                mbar_wait(&bar_x[xs], xpar, serr, 1);
                 if (lane == 0) {
                     tc_fence_after();
-                    const uint8_t* X = stX(s);
+                    const uint8_t* X = stX(xs);
 #pragma unroll
                     for (int kk = 0; kk < 8; ++kk) {
                         const uint8_t* xa = X + (kk >> 2) * 16384 + (kk & 3) * 32;
@@ -288,9 +357,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 lg += swt[0];
                 z += swc[0];
             }
-            // the stage's TMA data (and, through the producer's wait, the stage itself) is ours
-            mbar_wait(&bar_full[s], (c >> 1) & 1, serr, 1);
-            float* G = stG(s);
+            // the chunk's K/Q tiles have landed.  The gate stage c % 3 was last read by the chain in
+            // chunk c - 3, which finished before this block's wait on bar_tfree for chunk c - 3.
+            mbar_wait(&bar_x[xs], xpar, serr, 1);
+            float* G = stG(xs);
             if (tid < C) {
                 sg[tid] = lg;
                 scnt[tid] = z;
@@ -304,24 +374,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 G[G_CB + tid] = be;
                 G[G_CG + tid] = be * gamma;
                 G[G_CD + tid] = (cC == z) ? exp2f(gC - lg) : 0.f;
-                // output multiplier: O_r = om_r (Q S + P~ Delta)_r with P~ = P / om_r
-                G[G_OM + tid] = (gamma > kTinyDecay ? gamma : 1.f) * p.scale;
-                G[G_QZ + tid] = gamma > kTinyDecay ? 0.f : 1.f;  // the row's Q S term is dropped
+                // output: O_r = om_r (Q S)_r + (P Delta)_r with om_r = scale gamma_r
+                G[G_OM + tid] = gamma * p.scale;
                 G[G_VAL + tid] = vf;
                 if (tid == C - 1) G[G_GC] = gamma;
             }
             named_bar_sync(BAR_PREP, NPREP);
             mbar_wait(bar_kk, c & 1, serr, 2);
             tc_fence_after();
-            {
-                // row n = 32q + lane of [K;Q]; columns s in [32 half, 32 half + 32)
-                const int n = 32 * q + lane;
-                const int r = n & 63;
+            // Fast path: no zero decay in the chunk and a bounded total decay, so
+            // Gamma[r][s] = 2^g_r 2^-g_s is a rank-1 product (no exponential per element).
+            const bool fast = scnt[C - 1] == 0 && sg[C - 1] > -100.f;
+            if (q < 2) {
+                // A = strict_lower(beta_r Gamma[r][s] k_r.k_s): row r = 32q + lane of [K;Q] K^T,
+                // columns s in [32 half, 32 half + 32)
+                const int r = 32 * q + lane;
                 const float gr = sg[r];
                 const int cr = scnt[r];
-                // Fast path: no zero decay in the chunk and a bounded total decay, so
-                // Gamma[r][s] = 2^g_r 2^-g_s is a rank-1 product (no exponential per element).
-                const bool fast = scnt[C - 1] == 0 && sg[C - 1] > -100.f;
                 const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + TM_KK + 32 * half;
                 uint32_t gl[32];
                 tmem_ld16(ta, *reinterpret_cast<uint32_t(*)[16]>(&gl[0]));
@@ -329,72 +398,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 tmem_ld_wait();
                 const float4* sem4 = reinterpret_cast<const float4*>(sem + 32 * half);
                 const int s0 = 32 * half;
-                if (n < C) {
-                    const float br = G[G_CB + r];
-                    if (fast) {
-                        const float brer = br * exp2f(gr);
-                        float4* Arow = reinterpret_cast<float4*>(sA + r * LDA + s0);
+                const float br = G[G_CB + r];
+                if (fast) {
+                    const float brer = br * exp2f(gr);
+                    float4* Arow = reinterpret_cast<float4*>(sA + r * LDA + s0);
 #pragma unroll
-                        for (int e4 = 0; e4 < 8; ++e4) {
-                            const float4 m = sem4[e4];
-                            const int e = s0 + 4 * e4;
-                            float4 v;
-                            v.x = e < r ? brer * __uint_as_float(gl[4 * e4]) * m.x : 0.f;
-                            v.y = e + 1 < r ? brer * __uint_as_float(gl[4 * e4 + 1]) * m.y : 0.f;
-                            v.z = e + 2 < r ? brer * __uint_as_float(gl[4 * e4 + 2]) * m.z : 0.f;
-                            v.w = e + 3 < r ? brer * __uint_as_float(gl[4 * e4 + 3]) * m.w : 0.f;
-                            Arow[e4] = v;
-                        }
-                    } else {
-                        float* Af = sA + r * LDA + s0;
-#pragma unroll
-                        for (int e = 0; e < 32; ++e)
-                            Af[e] = (s0 + e < r && scnt[s0 + e] == cr) ? br * exp2f(gr - sg[s0 + e]) * __uint_as_float(gl[e]) : 0.f;
+                    for (int e4 = 0; e4 < 8; ++e4) {
+                        const float4 m = sem4[e4];
+                        const int e = s0 + 4 * e4;
+                        float4 v;
+                        v.x = e < r ? brer * __uint_as_float(gl[4 * e4]) * m.x : 0.f;
+                        v.y = e + 1 < r ? brer * __uint_as_float(gl[4 * e4 + 1]) * m.y : 0.f;
+                        v.z = e + 2 < r ? brer * __uint_as_float(gl[4 * e4 + 2]) * m.z : 0.f;
+                        v.w = e + 3 < r ? brer * __uint_as_float(gl[4 * e4 + 3]) * m.w : 0.f;
+                        Arow[e4] = v;
                     }
                 } else {
-                    // P~ = (scale Gamma o Q K^T, s <= r) / om_r as a bf16 pair hi + lo.  Fast path:
-                    // om_r = scale 2^g_r, so P~[r][s] = 2^-g_s (q_r . k_s).
-                    if (fast) {
+                    float* Af = sA + r * LDA + s0;
 #pragma unroll
-                        for (int e4 = 0; e4 < 8; ++e4) {
-                            const float4 m = sem4[e4];
-                            const int e = s0 + 4 * e4;
-                            gl[4 * e4] = __float_as_uint(e <= r ? __uint_as_float(gl[4 * e4]) * m.x : 0.f);
-                            gl[4 * e4 + 1] = __float_as_uint(e + 1 <= r ? __uint_as_float(gl[4 * e4 + 1]) * m.y : 0.f);
-                            gl[4 * e4 + 2] = __float_as_uint(e + 2 <= r ? __uint_as_float(gl[4 * e4 + 2]) * m.z : 0.f);
-                            gl[4 * e4 + 3] = __float_as_uint(e + 3 <= r ? __uint_as_float(gl[4 * e4 + 3]) * m.w : 0.f);
-                        }
-                    } else {
-                        const float inv_om = p.scale / G[G_OM + r];
-#pragma unroll
-                        for (int e = 0; e < 32; ++e)
-                            gl[e] = __float_as_uint((s0 + e <= r && scnt[s0 + e] == cr) ? inv_om * exp2f(gr - sg[s0 + e]) * __uint_as_float(gl[e]) : 0.f);
-                    }
-                    uint8_t* P = stP(s);
-#pragma unroll
-                    for (int x = 0; x < 4; ++x) {
-                        uint32_t ph[4], pl[4];
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const float v0 = __uint_as_float(gl[8 * x + 2 * u]), v1 = __uint_as_float(gl[8 * x + 2 * u + 1]);
-                            ph[u] = pack_bf16x2(v0, v1);
-                            pl[u] = pack_bf16x2(v0 - bf16_lo(ph[u]), v1 - bf16_hi(ph[u]));
-                        }
-                        const int cc = 4 * half + x;
-                        const int off = r * 128 + ((cc ^ (r & 7)) << 4);
-                        *reinterpret_cast<uint4*>(P + off) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
-                        *reinterpret_cast<uint4*>(P + C * 128 + off) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
-                    }
-                    if (G[G_QZ + r] != 0.f) {
-                        // gamma_r is zero (or below 2^-100): drop the row's Q S term by zeroing its Q row
-                        uint8_t* X = stX(s);
-#pragma unroll
-                        for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-                            for (int x = 0; x < 4; ++x)
-                                *reinterpret_cast<uint4*>(X + kb * 16384 + (64 + r) * 128 + 64 * half + 16 * x) =
-                                    make_uint4(0, 0, 0, 0);
-                    }
+                    for (int e = 0; e < 32; ++e)
+                        Af[e] = (s0 + e < r && scnt[s0 + e] == cr) ? br * exp2f(gr - sg[s0 + e]) * __uint_as_float(gl[e]) : 0.f;
                 }
             }
             tc_fence_before();
@@ -438,15 +461,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 sT[(a0 + i) * LDT + a0 + 8 + jj] = 0.f;
             }
             named_bar_sync(BAR_PREP, NPREP);
+            // T and P go to stage s: the chain must be done with it (chunk c - 2)
+            if (c >= 2) mbar_wait(&bar_tfree[s], (uint32_t)((c - 2) >> 1) & 1u, serr, 3);
             {
-                // T goes to the stage as the bf16 K-major UMMA operand (rows r', 64 columns r, 128-byte
+                // T goes to the stage as the fp16 K-major UMMA operand (rows r', 64 columns r, 128-byte
                 // swizzle) block by block, as soon as each block is final
                 const int g = lane >> 2, t4 = lane & 3;
                 uint8_t* Tt = stT(s);
-                if (warp < 4) {
-                    // 16 -> 32: warp = (pair pr, column tile nt); X and T10 tiles are 16 x 8 and the
-                    // second product only needs this warp's own X columns
-                    const int pr = warp >> 1, nt = warp & 1, a0 = 32 * pr;
+                if (q < 2) {
+                    // warps 0, 1, 4, 5 -> lw = 0..3.  16 -> 32: lw = (pair pr, column tile nt); X and T10
+                    // tiles are 16 x 8 and the second product only needs this warp's own X columns
+                    const int lw = (warp & 1) | ((warp >> 2) << 1);
+                    const int pr = lw >> 1, nt = lw & 1, a0 = 32 * pr;
                     float* Xp = sXs + pr * (16 * XLD);
                     float c4[4] = {0.f, 0.f, 0.f, 0.f};
                     // T00 is lower triangular: k-steps below 8 nt contribute nothing
@@ -456,16 +482,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     float d[4] = {0.f, 0.f, 0.f, 0.f};
                     tile_mma_tf32(d, sT + (a0 + 16) * LDT + a0 + 16, LDT, Xp + 8 * nt, XLD, 0, 2, g, t4);
                     store_tile(sT + (a0 + 16) * LDT + a0 + 8 * nt, LDT, d, g, t4, -1.f);  // read by 32 -> 64
-                    store_tile_bf16(Tt, a0 + 16, (a0 >> 3) + nt, d, g, t4, -1.f);
-                    zero_tile_bf16(Tt, a0, ((a0 + 16) >> 3) + nt, g, t4);
-                } else {
-                    // warps 4-7 meanwhile: the four 16 x 16 diagonal blocks are final
-                    const int e = tid - 128, row = e >> 1, cc = 2 * (row >> 4) + (e & 1);
+                    store_tile_f16(Tt, a0 + 16, (a0 >> 3) + nt, d, g, t4, -1.f);
+                    zero_tile_16(Tt, a0, ((a0 + 16) >> 3) + nt, g, t4);
+                    // then one 16-byte chunk each of the four 16 x 16 diagonal blocks (final since 8 -> 16)
+                    const int e = 32 * lw + lane, row = e >> 1, cc = 2 * (row >> 4) + (e & 1);
                     const float4 u = *reinterpret_cast<const float4*>(sT + row * LDT + cc * 8);
                     const float4 w = *reinterpret_cast<const float4*>(sT + row * LDT + cc * 8 + 4);
                     *reinterpret_cast<uint4*>(Tt + row * 128 + ((cc ^ (row & 7)) << 4)) =
-                        make_uint4(pack_bf16x2(u.x, u.y), pack_bf16x2(u.z, u.w), pack_bf16x2(w.x, w.y),
-                                   pack_bf16x2(w.z, w.w));
+                        make_uint4(pack_f16x2(u.x, u.y), pack_f16x2(u.z, u.w), pack_f16x2(w.x, w.y),
+                                   pack_f16x2(w.z, w.w));
+                } else {
+                    // warps 2, 3, 6, 7 meanwhile: P from the Q rows of [K;Q] K^T
+                    write_p(s, fast);
+                    tc_fence_before();  // these TMEM reads precede the next chunk's [K;Q] K^T
                 }
                 named_bar_sync(BAR_PREP, NPREP);
                 // 32 -> 64: warp = (row tile mt, column tile nt) of the 32 x 32 lower-left block
@@ -477,8 +506,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 float d[4] = {0.f, 0.f, 0.f, 0.f};
                 // T11 is lower triangular: rows 16 mt .. 16 mt + 15 need k-steps below 2 mt + 2
                 tile_mma_tf32(d, sT + (32 + 16 * mt) * LDT + 32, LDT, sXs + 8 * nt, XLD, 0, 2 * mt + 2, g, t4);
-                store_tile_bf16(Tt, 32 + 16 * mt, nt, d, g, t4, -1.f);
-                zero_tile_bf16(Tt, 16 * mt, 4 + nt, g, t4);
+                store_tile_f16(Tt, 32 + 16 * mt, nt, d, g, t4, -1.f);
+                zero_tile_16(Tt, 16 * mt, 4 + nt, g, t4);
             }
             fence_proxy_async_smem();
             named_bar_sync(BAR_PREP, NPREP);
@@ -509,25 +538,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 tmem_st8(tl + TM_S + 32 * hh + 8 * pc, pk);
             }
         };
-        // MMA1 of chunk c: D1[j][r] = sum_i S^T[j][i] K[r][i]   (issued by the chain leader)
+        // MMA1 of chunk c (issued by the chain leader): one N = 128 product over the 128 rows [K;Q] of
+        // each key block, D[j][r] = sum_i S^T[j][i] K[r][i] into D1 and D[j][64 + r] = sum_i S^T[j][i]
+        // Q[r][i] into DO (the Q S half of the output, which only needs the chunk-start state)
         auto issue_mma1 = [&](int c) {
             mbar_wait(&bar_prep[c & 1], (c >> 1) & 1, serr, 4);
             tc_fence_after();
-            const uint8_t* X = stX(c & 1);
+            const uint8_t* X = stX(c % NXS);
+            const uint32_t tr = TM_R0 + 128 * (c & 1);
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk)
-                umma_ts(tmem + TM_D1, tmem + TM_S + 8 * kk, kdesc(X + (kk >> 2) * 16384 + (kk & 3) * 32),
-                        IDESC_M128_N64, kk > 0 ? 1u : 0u);
+                umma_ts(tmem + tr, tmem + TM_S + 8 * kk, kdesc(X + (kk >> 2) * 16384 + (kk & 3) * 32),
+                        IDESC_M128_N128, kk > 0 ? 1u : 0u);
             umma_commit(bar_m1);
-            if (p.write_out) {
-                // the Q S half of the output accumulator only needs the chunk-start state: it runs
-                // on the tensor cores while E1 and E2 work (its completion is covered by bar_m3)
-                const uint32_t tm_do = TM_DO + 64 * (c & 1);
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                    umma_ts(tmem + tm_do, tmem + TM_S + 8 * kk, kdesc(X + (kk >> 2) * 16384 + 8192 + (kk & 3) * 32),
-                            IDESC_M128_N64, kk > 0 ? 1u : 0u);
-            }
         };
         store_state_bf16();
         tmem_st_wait();
@@ -536,20 +559,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (ct == 0) issue_mma1(0);
 
         for (int c = 0; c < nchunks; ++c) {
-            const int s = c & 1;
+            const int s = c & 1, xs = c % NXS;
             const uint32_t par = c & 1;
-            const uint32_t tm_do = TM_DO + 64 * (c & 1);
+            const uint32_t TM_D1 = TM_R0 + 128 * (c & 1);        // K S -> R^T (bf16 hi/lo) in place
+            const uint32_t tm_do = TM_D1 + 64;                     // Q S half of the output
+            const uint32_t TM_D3 = TM_R0 + 128 * ((c & 1) ^ 1);  // (Gamma Delta)^T K, 128 cols
             mbar_wait(&bar_prep[s], (c >> 1) & 1, serr, 4);
-            const float* G = stG(s);
+            const float* G = stG(xs);
             // private copy of what this chunk's output needs, so stage s can be reloaded early
-            float* om = com + 64 * (c & 1);
-            if (ct < C) om[ct] = G[G_VAL + ct] != 0.f ? G[G_OM + ct] : 0.f;
+            float* om = com + 128 * (c & 1);  // [0, 64): scale gamma_r, [64, 128): the row's P Delta factor
+            if (ct < C) {
+                const bool ok = G[G_VAL + ct] != 0.f;
+                om[ct] = ok ? G[G_OM + ct] : 0.f;
+                om[64 + ct] = ok ? 1.f : 0.f;
+            }
             const float gC = G[G_GC];
             mbar_wait(bar_m1, par, serr, 5);
+            if (!p.v_zero) mbar_wait(&bar_v[s], (uint32_t)(c >> 1) & 1u, serr, 8);
             tc_fence_after();
             // ---- E1: R^T[j][r] = beta_r V[r][j] - beta_r gamma_r (K S)[r][j],  r in [32 hh, 32 hh + 32),
-            //      written in place as a bf16 pair: for the 16 rows r of TMEM columns [16k, 16k + 16),
-            //      hi goes to columns [16k, +8) and lo to [16k + 8, +8)
+            //      written in place as fp16 pairs (r, r + 1) to columns [32 hh, 32 hh + 16)
             {
                 const __nv_bfloat16* Vs = reinterpret_cast<const __nv_bfloat16*>(stV(s));
                 uint32_t a[32];
@@ -560,8 +589,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const float2* cg2 = reinterpret_cast<const float2*>(G + G_CG + 32 * hh);
 #pragma unroll
                 for (int pc = 0; pc < 2; ++pc) {
-                    const uint32_t col = TM_D1 + 32 * hh + 16 * pc;
-                    uint32_t hi[8], lo[8];
+                    uint32_t pk[8];
 #pragma unroll
                     for (int u = 0; u < 8; ++u) {
                         const float2 cb = cb2[8 * pc + u], cg = cg2[8 * pc + u];
@@ -573,38 +601,42 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                             const float vv = p.v_zero ? 0.f : __bfloat162float(Vs[r * 128 + j]);
                             x[w] = (w ? cb.y : cb.x) * vv - (w ? cg.y : cg.x) * __uint_as_float(a[e]);
                         }
-                        hi[u] = pack_bf16x2(x[0], x[1]);
-                        lo[u] = pack_bf16x2(x[0] - bf16_lo(hi[u]), x[1] - bf16_hi(hi[u]));
+                        pk[u] = pack_f16x2(x[0], x[1]);
                     }
-                    tmem_st8(tl + col, hi);
-                    tmem_st8(tl + col + 8, lo);
+                    tmem_st8(tl + TM_D1 + 32 * hh + 8 * pc, pk);
                 }
                 tmem_st_wait();
             }
             tc_fence_before();
             named_bar_sync(BAR_CHAIN, NCHAIN);
-            // ---- MMA2: D2[j][r'] = sum_r R^T[j][r] T[r'][r]   (hi and lo accumulate)
+            // ---- MMA2: D2[j][r'] = sum_r R^T[j][r] T[r'][r]   (fp16; rows r = 16 kk .. 16 kk + 15 of R^T are
+            //      TMEM columns 32 (kk / 2) + 8 (kk % 2) ..)
             if (ct == 0) {
                 tc_fence_after();
                 const uint8_t* Tt = stT(s);
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                    const uint32_t ra = tmem + TM_D1 + 16 * kk;
-                    umma_ts(tmem + TM_D2, ra, kdesc(Tt + kk * 32), IDESC_M128_N64, kk > 0 ? 1u : 0u);
-                    umma_ts(tmem + TM_D2, ra + 8, kdesc(Tt + kk * 32), IDESC_M128_N64, 1u);
-                }
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_ts(tmem + TM_D2, tmem + TM_D1 + 32 * (kk >> 1) + 8 * (kk & 1), kdesc(Tt + kk * 32),
+                            IDESC_F16_M128_N64, kk > 0 ? 1u : 0u);
                 umma_commit(bar_m2);
+                // V stage (c + 1) & 1 holds the output tile of chunk c - 1: once its store has read it,
+                // the stage takes V of chunk c + 1
+                if (c >= 1 && c + 1 < nchunks) {
+                    tma_store_wait_read0();
+                    load_v(c + 1);
+                }
             }
             mbar_wait(bar_m2, par, serr, 6);
             tc_fence_after();
-            // ---- E2: Delta^T for r' in [32 hh, 32 hh + 32) as bf16, in place: for the 16 rows of
-            //      columns [16k, 16k + 16), the Gamma[63][r']-scaled copy goes to [16k, +8) and the plain
-            //      copy to [16k + 8, +8)
+            // ---- E2: Delta^T for r' in [32 hh, 32 hh + 32), in place: for the 16 rows of columns
+            //      [16k, 16k + 16), the Gamma[63][r']-scaled copy (bf16, MMA3) goes to [16k, +8) and the
+            //      plain copy (fp16, MMA4) to [16k + 8, +8)
             {
                 uint32_t d[32];
                 tmem_ld16(tl + TM_D2 + 32 * hh, *reinterpret_cast<uint32_t(*)[16]>(&d[0]));
                 tmem_ld16(tl + TM_D2 + 32 * hh + 16, *reinterpret_cast<uint32_t(*)[16]>(&d[16]));
                 tmem_ld_wait();
+                float big = 0.f;
 #pragma unroll
                 for (int pc = 0; pc < 2; ++pc) {
                     const uint32_t col = TM_D2 + 32 * hh + 16 * pc;
@@ -614,21 +646,24 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         const int e = 16 * pc + 2 * u;
                         const int r = 32 * hh + e;
                         const float x0 = __uint_as_float(d[e]), x1 = __uint_as_float(d[e + 1]);
+                        big = fmaxf(big, fmaxf(fabsf(x0), fabsf(x1)));
                         ps[u] = pack_bf16x2(x0 * G[G_CD + r], x1 * G[G_CD + r + 1]);
-                        pp[u] = pack_bf16x2(x0, x1);
+                        pp[u] = pack_f16x2(x0, x1);
                     }
                     tmem_st8(tl + col, ps);
                     tmem_st8(tl + col + 8, pp);
                 }
+                // an fp16 operand overflowed (R or T, so Delta is not finite) or Delta itself is out of
+                // fp16 range: report it (the NaN test is the negated comparison)
+                if (!(big <= kF16Max)) atomicExch(p.err, kTcRangeError);
                 tmem_st_wait();
             }
             tc_fence_before();
             named_bar_sync(BAR_CHAIN, NCHAIN);
-            // ---- MMA3: D3 = (Gamma Delta)^T K (state increment); DO = S^T Q^T + Delta^T P~^T (output,
-            //      issued now because S^T in TMEM is still the chunk-start state)
+            // ---- MMA3: D3 = (Gamma Delta)^T K (state increment); MMA4: DP = Delta^T P^T (output)
             if (ct == 0) {
                 tc_fence_after();
-                const uint8_t* X = stX(s);
+                const uint8_t* X = stX(xs);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
                     umma_ts(tmem + TM_D3, tmem + TM_D2 + 16 * kk,
@@ -637,19 +672,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if (p.write_out) {
                     const uint8_t* P = stP(s);
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        const uint32_t da = tmem + TM_D2 + 16 * kk + 8;
-                        umma_ts(tmem + tm_do, da, kdesc(P + kk * 32), IDESC_M128_N64, 1u);
-                        umma_ts(tmem + tm_do, da, kdesc(P + C * 128 + kk * 32), IDESC_M128_N64, 1u);
-                    }
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma_ts(tmem + TM_PD, tmem + TM_D2 + 16 * kk + 8, kdesc(P + kk * 32), IDESC_F16_M128_N64,
+                                kk > 0 ? 1u : 0u);
                 }
                 umma_commit(bar_m3);
-                tma_store_wait_read0();  // the previous chunk's output tile has left shared memory
             }
             mbar_wait(bar_m3, par, serr, 7);
             tc_fence_after();
-            // every MMA and every E-stage read of stage s is done: load chunk c + 2 into it now
-            if (ct == 0 && c + 2 < nchunks) issue_loads(c + 2);
+            // every MMA of chunk c is done: its K/Q stage takes chunk c + 3, and its T / P stage goes
+            // back to the prep warps (the output multipliers were copied to `com`)
+            if (ct == 0) {
+                if (c + NXS < nchunks) load_x(c + NXS);
+                mbar_arrive(&bar_tfree[s]);
+            }
             // ---- E3: state update (f32 master copy) and its bf16 image for the next MMA1
             {
 #pragma unroll
@@ -669,15 +705,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             // the recurrence moves on: MMA1 of the next chunk runs while this chunk's output is written
             if (ct == 0 && c + 1 < nchunks) issue_mma1(c + 1);
             if (p.write_out) {
-                __nv_bfloat16* Os = reinterpret_cast<__nv_bfloat16*>(Ost);
-                uint32_t o[32];
+                __nv_bfloat16* Os = reinterpret_cast<__nv_bfloat16*>(stV(s));  // V is dead since E1
+                uint32_t o[32], pd[32];
                 tmem_ld16(tl + tm_do + 32 * hh, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
                 tmem_ld16(tl + tm_do + 32 * hh + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
+                tmem_ld16(tl + TM_PD + 32 * hh, *reinterpret_cast<uint32_t(*)[16]>(&pd[0]));
+                tmem_ld16(tl + TM_PD + 32 * hh + 16, *reinterpret_cast<uint32_t(*)[16]>(&pd[16]));
                 tmem_ld_wait();
 #pragma unroll
                 for (int e = 0; e < 32; ++e) {
                     const int r = 32 * hh + e;
-                    Os[r * 128 + j] = __float2bfloat16_rn(om[r] * __uint_as_float(o[e]));
+                    Os[r * 128 + j] = __float2bfloat16_rn(fmaf(om[r], __uint_as_float(o[e]), om[64 + r] * __uint_as_float(pd[e])));
                 }
                 fence_proxy_async_smem();
             }
@@ -685,7 +723,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             named_bar_sync(BAR_CHAIN, NCHAIN);
             if (ct == 0) {
                 if (p.write_out) {
-                    tma_store_4d(&tm_o, Ost, 0, c * C, h, b);
+                    tma_store_4d(&tm_o, stV(s), 0, c * C, h, b);
                     tma_store_commit();
                 }
             }
@@ -824,5 +862,9 @@ extern "C" int dbl_device_error(int* code) {
         if (e != cudaSuccess) return dbl::cuda_status(e, "dbl_device_error");
     }
     if (code) *code = host;
+    if (host == dbl::kTcRangeError)
+        return dbl::fail(DBL_ERR_UNSUPPORTED,
+                         "tensor-core prefill: an fp16 MMA operand left fp16 range (inputs far outside unit-norm keys "
+                         "and beta in [0, 1]); its outputs are not valid");
     return host ? dbl::fail(DBL_ERR_TIMEOUT, "a kernel gave up a bounded wait (site %d)", host) : DBL_OK;
 }

@@ -1,9 +1,10 @@
 """numpy model of the tensor-core prefill kernel's arithmetic (prefill_tc.cu), for CPU tests.
 
-It follows the kernel step by step -- log-space decay products with reset counting, the blocked
-16 x 16 inverse of (I + A), and bf16 rounding exactly where the kernel rounds an MMA operand
-(S, T and Delta to one bf16; R and P to a bf16 hi + lo pair) -- so the numerical error budget of
-the kernel can be checked against the oracle without a GPU.  Test infrastructure only.
+It follows the kernel step by step -- log-space decay products with reset counting, the inverse
+of (I + A) by block doubling, and rounding exactly where the kernel rounds an MMA operand (S and
+the Gamma-scaled Delta to bf16 because their partner operand is a bf16 input tile; T, R, the
+plain Delta and P to fp16) -- so the numerical error budget of the kernel can be checked against
+the oracle without a GPU.  Test infrastructure only.
 """
 from __future__ import annotations
 
@@ -13,24 +14,25 @@ from fixtures import bf16_round
 
 
 def blocked_unit_lower_inverse(A: np.ndarray) -> np.ndarray:
-    """(I + A)^-1 for strictly lower A (64 x 64): 16 x 16 diagonal blocks by substitution, then
-    off-diagonal blocks by distance from the diagonal, as the kernel's prep warps do."""
+    """(I + A)^-1 for strictly lower A (64 x 64) as the kernel's prep warps compute it: the 8 x 8
+    diagonal blocks by substitution, then pairs of inverted n x n diagonal blocks joined into 2n x 2n
+    ones (n = 8, 16, 32) through the lower-left block T10 = -T11 (A10 T00)."""
     n = A.shape[0]
-    nb = n // 16
     T = np.zeros_like(A)
-    for b in range(nb):
-        blk = A[16 * b:16 * b + 16, 16 * b:16 * b + 16]
-        for c in range(16):
-            x = np.zeros(16, A.dtype)
+    for b in range(n // 8):
+        blk = A[8 * b:8 * b + 8, 8 * b:8 * b + 8]
+        for c in range(8):
+            x = np.zeros(8, A.dtype)
             x[c] = 1.0
-            for r in range(c + 1, 16):
+            for r in range(c + 1, 8):
                 x[r] = -blk[r, c:r] @ x[c:r]
-            T[16 * b:16 * b + 16, 16 * b + c] = x
-    for d in range(1, nb):
-        for b in range(d, nb):
-            a = b - d
-            X = A[16 * b:16 * b + 16, 16 * a:16 * b] @ T[16 * a:16 * b, 16 * a:16 * a + 16]
-            T[16 * b:16 * b + 16, 16 * a:16 * a + 16] = -T[16 * b:16 * b + 16, 16 * b:16 * b + 16] @ X
+            T[8 * b:8 * b + 8, 8 * b + c] = x
+    m = 8
+    while m < n:
+        for a0 in range(0, n, 2 * m):
+            X = A[a0 + m:a0 + 2 * m, a0:a0 + m] @ T[a0:a0 + m, a0:a0 + m]
+            T[a0 + m:a0 + 2 * m, a0:a0 + m] = -T[a0 + m:a0 + 2 * m, a0 + m:a0 + 2 * m] @ X
+        m *= 2
     return T
 
 
@@ -40,10 +42,9 @@ def prefill_model(q, k, v, alpha, beta, scale, valid=None, reset=None, initial=N
     Returns (out [B,T,H,V] f32, final_state [B,H,K,V] f32)."""
     rnd = bf16_round if rounding else (lambda x: np.asarray(x, np.float32))
 
-    def pair(x):  # value carried as bf16 hi + bf16 lo
+    def h16(x):  # fp16 MMA operand
         x = np.asarray(x, np.float32)
-        hi = rnd(x)
-        return hi + rnd(x - hi)
+        return x.astype(np.float16).astype(np.float32) if rounding else x
     q, k, v = (np.asarray(x, np.float32) for x in (q, k, v))
     B, T, H, K = q.shape
     V = v.shape[3]
@@ -83,15 +84,15 @@ def prefill_model(q, k, v, alpha, beta, scale, valid=None, reset=None, initial=N
                 low = np.tril(np.ones((C, C), bool), -1)
                 incl = np.tril(np.ones((C, C), bool), 0)
                 A = np.where(low, be[:, None] * dec * (Kc @ Kc.T), 0.0).astype(np.float32)
-                P = pair(np.where(incl, scale * dec * (Qc @ Kc.T), 0.0))
-                Tm = rnd(blocked_unit_lower_inverse(A))
+                P = h16(np.where(incl, scale * dec * (Qc @ Kc.T), 0.0))
+                Tm = h16(blocked_unit_lower_inverse(A))
                 Sb = rnd(S)
                 KS = Kc @ Sb
                 QS = Qc @ Sb
-                R = pair(be[:, None] * Vc - (be * gamma)[:, None] * KS)
+                R = h16(be[:, None] * Vc - (be * gamma)[:, None] * KS)
                 Delta = Tm @ R
                 Dt = rnd(Delta * dec[C - 1][:, None])
-                Dp = rnd(Delta)
+                Dp = h16(Delta)
                 S = (gamma[C - 1] * S + Kc.T @ Dt).astype(np.float32)
                 O = np.where(vf[:, None] != 0, (scale * gamma)[:, None] * QS + P @ Dp, 0.0)
                 out[b, t0:t0 + n, h] = rnd(O[:n])
