@@ -20,9 +20,9 @@
 //     (8x8 diagonal blocks by substitution, then 8 -> 16 -> 32 -> 64 joins, the last two on
 //     mma.sync tf32 tiles), T and P written as bf16 UMMA operands.  Prep runs one chunk ahead of
 //     the chain.  Shared-memory stages: K/Q tiles x 3 (the chain leader loads chunk c + 3 as soon
-//     as the MMAs of chunk c are done), gates x 3, V x 2 (a chunk's V stage then stages its output
-//     tile), and T / P x 2 (handed back to the prep warps through an mbarrier; the prep warps wait
-//     for it only when they start writing T and P~, after the first half of the inverse).
+//     as the MMAs of chunk c are done), gates x 3, V x 2 (loaded two chunks ahead), T / P x 2
+//     (handed back to the prep warps through an mbarrier; the prep warps wait for it only when they
+//     start writing T and P, after the first half of the inverse), and one output staging tile.
 //   * chain warps 8-15: the state-dependent chain, transposed so that the value column j of the
 //     state is TMEM lane j and every activation stays in TMEM (A operands of the TS form):
 //       MMA1  D1[j][r]  = sum_i S^T[j][i] K[r][i]          (A = S^T bf16 in TMEM; issued as one
@@ -38,8 +38,9 @@
 //     Magnitudes: T has entries of at most 1 for unit keys and beta <= 1; R, Delta and P are of the
 //     order of V and scale; a value beyond fp16 range is reported through dbl_device_error.
 //       E3    S[i][j] = gamma_63 S + D3 (f32 master state in registers, 64 per thread),
-//             S^T -> TMEM bf16; then MMA1 of the next chunk is issued and, while it runs,
-//             O[r][j] = scale gamma_r DQ[j][r] + DP[j][r] -> the chunk's V stage -> TMA store.
+//             S^T -> TMEM bf16; then MMA1 of the next chunk is issued.  The output
+//             O[r][j] = scale gamma_r DQ[j][r] + DP[j][r] -> the chunk's V stage -> TMA store is
+//             written while MMA2 of the next chunk runs.
 // Roofline: HBM (intensity ~172 FLOP/B at the algorithmic minimum of 1032 B per token-head).
 #include <cuda.h>
 
@@ -56,9 +57,9 @@ namespace {
 constexpr int C = 64;
 constexpr int DK = 128;
 constexpr int NTHREADS = 512;
-constexpr int NPREP = 256;   // warps 0-7, 104 registers each after setmaxnreg
-constexpr int NCHAIN = 256;  // warps 8-15, 152 registers each (the f32 state lives in registers)
-constexpr int PREP_REGS = 104, CHAIN_REGS = 152;
+constexpr int NPREP = 256;   // warps 0-7, 112 registers each after setmaxnreg
+constexpr int NCHAIN = 256;  // warps 8-15, 144 registers each (the f32 state lives in registers)
+constexpr int PREP_REGS = 112, CHAIN_REGS = 144;
 static_assert(NPREP * PREP_REGS + NCHAIN * CHAIN_REGS <= 65536, "register split exceeds the launch budget");
 constexpr int BAR_PREP = 1, BAR_CHAIN = 2;
 
@@ -75,10 +76,10 @@ constexpr uint32_t TM_PD = 448;   // P Delta half of the output, 64 cols
 
 // Shared memory (offsets from a 1024-aligned base).  The K/Q tiles and the gates have three stages,
 // so the loads of chunk c + 3 go out as soon as the chain is done with chunk c; V, T and P have
-// two.  A chunk's V stage doubles as the staging tile of its output (V is dead after E1).
+// two (V of chunk c + 2 loads as soon as E1 of chunk c has read its stage).
 constexpr int NXS = 3;
 constexpr uint32_t X_BYTES = 2 * 128 * 128;  // 2 key blocks x 128 rows ([K;Q]) x 128 B, swizzled
-constexpr uint32_t V_BYTES = C * 128 * 2;    // [64][128] bf16 plain (V in, then O out)
+constexpr uint32_t V_BYTES = C * 128 * 2;    // [64][128] bf16 plain
 constexpr uint32_t T_BYTES = C * 128;        // [64][64] bf16 swizzled
 constexpr uint32_t P_BYTES = C * 128;         // [64][64] fp16 swizzled
 constexpr uint32_t G_BYTES = 2048;           // gates
@@ -87,7 +88,9 @@ constexpr uint32_t OFF_V = OFF_X + NXS * X_BYTES;
 constexpr uint32_t OFF_T = OFF_V + 2 * V_BYTES;
 constexpr uint32_t OFF_P = OFF_T + 2 * T_BYTES;
 constexpr uint32_t OFF_G = OFF_P + 2 * P_BYTES;
-constexpr uint32_t OFF_SA = OFF_G + NXS * G_BYTES;
+constexpr uint32_t OFF_O = OFF_G + NXS * G_BYTES;  // output staging tile [64][128] bf16
+constexpr uint32_t O_BYTES = C * 128 * 2;
+constexpr uint32_t OFF_SA = OFF_O + O_BYTES;
 constexpr int LDA = 68;   // A rows (16-byte aligned: a lane writes its row with 16-byte stores)
 constexpr int LDT = 68;   // T rows (read as float4: 16-byte aligned stride)
 constexpr uint32_t OFF_ST = OFF_SA + C * LDA * 4;
@@ -552,6 +555,27 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         IDESC_M128_N128, kk > 0 ? 1u : 0u);
             umma_commit(bar_m1);
         };
+        // Output of chunk cc: O[r][j] = scale gamma_r DQ[j][r] + DP[j][r] (0 for padding rows) into the
+        // staging tile, as bf16 for the TMA store.  DQ sits in the upper half
+        // of region cc & 1; MMA3 of chunk cc + 1 overwrites it and MMA4 of chunk cc + 1 overwrites DP,
+        // so this runs in chunk cc + 1 between MMA2 and the barrier that precedes those MMAs.
+        auto write_output = [&](int cc) {
+            const float* omc = com + 128 * (cc & 1);
+            __nv_bfloat16* Os = reinterpret_cast<__nv_bfloat16*>(smem + OFF_O);
+            const uint32_t tdq = TM_R0 + 128 * (cc & 1) + 64;
+            uint32_t o[32], pd[32];
+            tmem_ld16(tl + tdq + 32 * hh, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
+            tmem_ld16(tl + tdq + 32 * hh + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
+            tmem_ld16(tl + TM_PD + 32 * hh, *reinterpret_cast<uint32_t(*)[16]>(&pd[0]));
+            tmem_ld16(tl + TM_PD + 32 * hh + 16, *reinterpret_cast<uint32_t(*)[16]>(&pd[16]));
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+                const int r = 32 * hh + e;
+                Os[r * 128 + j] = __float2bfloat16_rn(fmaf(omc[r], __uint_as_float(o[e]), omc[64 + r] * __uint_as_float(pd[e])));
+            }
+            fence_proxy_async_smem();
+        };
         store_state_bf16();
         tmem_st_wait();
         tc_fence_before();
@@ -562,7 +586,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const int s = c & 1, xs = c % NXS;
             const uint32_t par = c & 1;
             const uint32_t TM_D1 = TM_R0 + 128 * (c & 1);        // K S -> R^T (bf16 hi/lo) in place
-            const uint32_t tm_do = TM_D1 + 64;                     // Q S half of the output
             const uint32_t TM_D3 = TM_R0 + 128 * ((c & 1) ^ 1);  // (Gamma Delta)^T K, 128 cols
             mbar_wait(&bar_prep[s], (c >> 1) & 1, serr, 4);
             const float* G = stG(xs);
@@ -609,6 +632,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             tc_fence_before();
             named_bar_sync(BAR_CHAIN, NCHAIN);
+            // V stage s is read: it takes V of chunk c + 2
+            if (ct == 0 && c + 2 < nchunks) load_v(c + 2);
             // ---- MMA2: D2[j][r'] = sum_r R^T[j][r] T[r'][r]   (fp16; rows r = 16 kk .. 16 kk + 15 of R^T are
             //      TMEM columns 32 (kk / 2) + 8 (kk % 2) ..)
             if (ct == 0) {
@@ -619,13 +644,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     umma_ts(tmem + TM_D2, tmem + TM_D1 + 32 * (kk >> 1) + 8 * (kk & 1), kdesc(Tt + kk * 32),
                             IDESC_F16_M128_N64, kk > 0 ? 1u : 0u);
                 umma_commit(bar_m2);
-                // V stage (c + 1) & 1 holds the output tile of chunk c - 1: once its store has read it,
-                // the stage takes V of chunk c + 1
-                if (c >= 1 && c + 1 < nchunks) {
-                    tma_store_wait_read0();
-                    load_v(c + 1);
-                }
             }
+            // while MMA2 runs: the output of chunk c - 1
+            if (p.write_out && c >= 1) write_output(c - 1);
             mbar_wait(bar_m2, par, serr, 6);
             tc_fence_after();
             // ---- E2: Delta^T for r' in [32 hh, 32 hh + 32), in place: for the 16 rows of columns
@@ -662,6 +683,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             named_bar_sync(BAR_CHAIN, NCHAIN);
             // ---- MMA3: D3 = (Gamma Delta)^T K (state increment); MMA4: DP = Delta^T P^T (output)
             if (ct == 0) {
+                if (p.write_out && c >= 1) {
+                    tma_store_4d(&tm_o, smem + OFF_O, 0, (c - 1) * C, h, b);
+                    tma_store_commit();
+                }
                 tc_fence_after();
                 const uint8_t* X = stX(xs);
 #pragma unroll
@@ -685,6 +710,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (ct == 0) {
                 if (c + NXS < nchunks) load_x(c + NXS);
                 mbar_arrive(&bar_tfree[s]);
+                // the staging tile is written again in chunk c + 1 (after the barrier that ends E3)
+                tma_store_wait_read0();
             }
             // ---- E3: state update (f32 master copy) and its bf16 image for the next MMA1
             {
@@ -702,32 +729,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             tc_fence_before();
             named_bar_sync(BAR_CHAIN, NCHAIN);
-            // the recurrence moves on: MMA1 of the next chunk runs while this chunk's output is written
+            // the recurrence moves on (the output of chunk c is written during MMA2 of chunk c + 1)
             if (ct == 0 && c + 1 < nchunks) issue_mma1(c + 1);
-            if (p.write_out) {
-                __nv_bfloat16* Os = reinterpret_cast<__nv_bfloat16*>(stV(s));  // V is dead since E1
-                uint32_t o[32], pd[32];
-                tmem_ld16(tl + tm_do + 32 * hh, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
-                tmem_ld16(tl + tm_do + 32 * hh + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
-                tmem_ld16(tl + TM_PD + 32 * hh, *reinterpret_cast<uint32_t(*)[16]>(&pd[0]));
-                tmem_ld16(tl + TM_PD + 32 * hh + 16, *reinterpret_cast<uint32_t(*)[16]>(&pd[16]));
-                tmem_ld_wait();
-#pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const int r = 32 * hh + e;
-                    Os[r * 128 + j] = __float2bfloat16_rn(fmaf(om[r], __uint_as_float(o[e]), om[64 + r] * __uint_as_float(pd[e])));
-                }
-                fence_proxy_async_smem();
-            }
+            // ---- end of chunk c
+        }
+        if (p.write_out && nchunks > 0) {
+            // the last chunk's output (its MMAs completed before its E3)
+            write_output(nchunks - 1);
             tc_fence_before();
             named_bar_sync(BAR_CHAIN, NCHAIN);
             if (ct == 0) {
-                if (p.write_out) {
-                    tma_store_4d(&tm_o, stV(s), 0, c * C, h, b);
-                    tma_store_commit();
-                }
+                tma_store_4d(&tm_o, smem + OFF_O, 0, (nchunks - 1) * C, h, b);
+                tma_store_commit();
             }
-            // ---- end of chunk c
         }
         if (p.final_state) {
 #pragma unroll

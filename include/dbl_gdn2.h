@@ -52,10 +52,12 @@ const char *dbl_last_error(void);
 /* ABI version: major * 10000 + minor * 100 + patch. */
 int dbl_abi_version(void);
 /* Every wait inside the tensor-core kernels is bounded; one that gives up records a site code on
- * the current device and lets the kernel run to completion (its outputs are then undefined).
- * This call synchronises with the device, stores that code in *code (0 = none; code may be NULL),
- * clears the record and returns DBL_OK or DBL_ERR_TIMEOUT.  No counterpart in the reference,
- * whose kernels have no bounded waits. */
+ * the current device and lets the kernel run to completion (its outputs are then undefined).  The
+ * tensor-core prefill also records code 100 when one of its fp16 MMA operands left fp16 range
+ * (inputs far outside unit-norm keys and beta in [0, 1]; its outputs are then not valid).
+ * This call synchronises with the device, stores the code in *code (0 = none; code may be NULL),
+ * clears the record and returns DBL_OK, DBL_ERR_UNSUPPORTED (code 100) or DBL_ERR_TIMEOUT.  No
+ * counterpart in the reference, whose kernels have no bounded waits or range checks. */
 int dbl_device_error(int *code);
 
 /* =============================================================================================
