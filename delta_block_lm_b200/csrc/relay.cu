@@ -443,78 +443,148 @@ __device__ void own_block(const RelayParams& p, unsigned char* smem) {
             }
             se[key] = key < nkeys ? d : -FLT_MAX;
         }
+        __syncthreads();
+        float m = -FLT_MAX;
+        for (int k = lane; k < BO; k += 32) m = fmaxf(m, se[k]);
+        m = warp_max(m);  // every warp computes the block max redundantly
+        __syncthreads();
+        float lsum = 0.f;
+        for (int k = tid; k < BO; k += THREADS) {
+            const float e = k < nkeys ? __expf(se[k] - m) : 0.f;
+            se[k] = e;
+            lsum += e;
+        }
+        lsum = warp_sum(lsum);
+        if (lane == 0) s_red[1][warp] = lsum;
+        __syncthreads();
+        float l = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) l += s_red[1][w];
+        // acc[d] = sum_key e[key] v[key][d]; lane holds EPL dims of one key slot
+        float acc[EPL];
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
+#pragma unroll 8
+        for (int it = 0; it < ITER; ++it) {
+            const int key = warp * KEYS_PER_WARP + it * KPW + sub;
+            if (key < nkeys) {
+                const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(vo + (size_t)key * D + part * EPL));
+                const T* x = reinterpret_cast<const T*>(&raw);
+                const float w = se[key];
+#pragma unroll
+                for (int e = 0; e < EPL; ++e) acc[e] = fmaf(w, to_f32(x[e]), acc[e]);
+            }
+        }
+#pragma unroll
+        for (int o = LPK; o < 32; o <<= 1)
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
+        if (sub == 0)
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) sacc[warp * D + part * EPL + e] = acc[e];
+        __syncthreads();
+        const int pi = p.NPB * p.ppc + ob;
+        for (int d = tid; d < D; d += THREADS) {
+            float a = 0.f;
+#pragma unroll
+            for (int w = 0; w < NW; ++w) a += sacc[w * D + d];
+            p.part_acc[(row * p.P + pi) * D + d] = a;
+        }
+        if (tid == 0) {
+            p.part_max[row * p.P + pi] = m;
+            p.part_sum[row * p.P + pi] = nkeys > 0 ? l : 0.f;
+        }
     } else {
-        // bf16: warp-cooperative 16-byte loads; products of bf16 values are exact in f32 and the
-        // score is scaled after the sum, as the tensor-core prefix path does.
+        // bf16: one pass.  Each warp runs an online softmax over its keys in groups of KPW x U,
+        // loading the K and V rows of a group together (2U 16-byte loads in flight per lane);
+        // products of bf16 values are exact in f32 and the score is scaled after the sum, as the
+        // tensor-core prefix path does.  The warps' (max, sum, acc) are merged at the end.
+        constexpr int U = 4;
         float qv[EPL];
         const T* q = static_cast<const T*>(p.q) + row * D + part * EPL;
 #pragma unroll
         for (int e = 0; e < EPL; ++e) qv[e] = to_f32(q[e]);
-#pragma unroll 8
-        for (int it = 0; it < ITER; ++it) {
-            const int key = warp * KEYS_PER_WARP + it * KPW + sub;
-            float d = 0.f;
-            if (key < nkeys) {
-                const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(ko + (size_t)key * D + part * EPL));
-                const T* x = reinterpret_cast<const T*>(&raw);
+        float m = -FLT_MAX, l = 0.f, acc[EPL];
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
+        for (int g = 0; g < ITER; g += U) {
+            uint4 kr[U], vr[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int key = warp * KEYS_PER_WARP + (g + u) * KPW + sub;
+                if (key < nkeys) {
+                    kr[u] = __ldcs(reinterpret_cast<const uint4*>(ko + (size_t)key * D + part * EPL));
+                    vr[u] = __ldcs(reinterpret_cast<const uint4*>(vo + (size_t)key * D + part * EPL));
+                } else {
+                    kr[u] = make_uint4(0, 0, 0, 0);
+                    vr[u] = make_uint4(0, 0, 0, 0);
+                }
+            }
+            float sc[U];
+            float mg = -FLT_MAX;
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const T* x = reinterpret_cast<const T*>(&kr[u]);
+                float d = 0.f;
 #pragma unroll
                 for (int e = 0; e < EPL; ++e) d = fmaf(qv[e], to_f32(x[e]), d);
+#pragma unroll
+                for (int o = LPK / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+                const int key = warp * KEYS_PER_WARP + (g + u) * KPW + sub;
+                sc[u] = key < nkeys ? d * p.scale : -FLT_MAX;
+                mg = fmaxf(mg, sc[u]);
             }
 #pragma unroll
-            for (int o = LPK / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-            if (part == 0) se[key] = key < nkeys ? d * p.scale : -FLT_MAX;
+            for (int o = LPK; o < 32; o <<= 1) mg = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, o));  // every key slot
+            const float mn = fmaxf(m, mg);
+            const float corr = __expf(m - mn);  // 0 while nothing was seen (acc and l are 0 then)
+            l *= corr;
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) acc[e] *= corr;
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int key = warp * KEYS_PER_WARP + (g + u) * KPW + sub;
+                const float w = key < nkeys ? __expf(sc[u] - mn) : 0.f;
+                if (part == 0) l += w;
+                const T* x = reinterpret_cast<const T*>(&vr[u]);
+#pragma unroll
+                for (int e = 0; e < EPL; ++e) acc[e] = fmaf(w, to_f32(x[e]), acc[e]);
+            }
+            m = mn;
         }
-    }
-    __syncthreads();
-    float m = -FLT_MAX;
-    for (int k = lane; k < BO; k += 32) m = fmaxf(m, se[k]);
-    m = warp_max(m);  // every warp computes the block max redundantly
-    __syncthreads();
-    float lsum = 0.f;
-    for (int k = tid; k < BO; k += THREADS) {
-        const float e = k < nkeys ? __expf(se[k] - m) : 0.f;
-        se[k] = e;
-        lsum += e;
-    }
-    lsum = warp_sum(lsum);
-    if (lane == 0) s_red[1][warp] = lsum;
-    __syncthreads();
-    float l = 0.f;
 #pragma unroll
-    for (int w = 0; w < NW; ++w) l += s_red[1][w];
-    // acc[d] = sum_key e[key] v[key][d]; lane holds EPL dims of one key slot
-    float acc[EPL];
+        for (int o = LPK; o < 32; o <<= 1)
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
-#pragma unroll 8
-    for (int it = 0; it < ITER; ++it) {
-        const int key = warp * KEYS_PER_WARP + it * KPW + sub;
-        if (key < nkeys) {
-            const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(vo + (size_t)key * D + part * EPL));
-            const T* x = reinterpret_cast<const T*>(&raw);
-            const float w = se[key];
+            for (int e = 0; e < EPL; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
+        l = warp_sum(l);
+        if (sub == 0)
 #pragma unroll
-            for (int e = 0; e < EPL; ++e) acc[e] = fmaf(w, to_f32(x[e]), acc[e]);
+            for (int e = 0; e < EPL; ++e) sacc[warp * D + part * EPL + e] = acc[e];
+        if (lane == 0) {
+            s_red[0][warp] = m;
+            s_red[1][warp] = l;
         }
-    }
+        __syncthreads();
+        float mb = -FLT_MAX;
 #pragma unroll
-    for (int o = LPK; o < 32; o <<= 1)
+        for (int w = 0; w < NW; ++w) mb = fmaxf(mb, s_red[0][w]);
+        float fw[NW], lb = 0.f;
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
-    if (sub == 0)
+        for (int w = 0; w < NW; ++w) {
+            fw[w] = __expf(s_red[0][w] - mb);
+            lb = fmaf(fw[w], s_red[1][w], lb);
+        }
+        const int pi = p.NPB * p.ppc + ob;
+        for (int d = tid; d < D; d += THREADS) {
+            float a = 0.f;
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) sacc[warp * D + part * EPL + e] = acc[e];
-    __syncthreads();
-    const int pi = p.NPB * p.ppc + ob;
-    for (int d = tid; d < D; d += THREADS) {
-        float a = 0.f;
-#pragma unroll
-        for (int w = 0; w < NW; ++w) a += sacc[w * D + d];
-        p.part_acc[(row * p.P + pi) * D + d] = a;
-    }
-    if (tid == 0) {
-        p.part_max[row * p.P + pi] = m;
-        p.part_sum[row * p.P + pi] = nkeys > 0 ? l : 0.f;
+            for (int w = 0; w < NW; ++w) a = fmaf(fw[w], sacc[w * D + d], a);
+            p.part_acc[(row * p.P + pi) * D + d] = a;
+        }
+        if (tid == 0) {
+            p.part_max[row * p.P + pi] = mb;
+            p.part_sum[row * p.P + pi] = nkeys > 0 ? lb : 0.f;
+        }
     }
     arrive_rows<D, T>(p, n, 1, h, 1u, se);
 }
