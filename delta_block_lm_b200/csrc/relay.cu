@@ -12,8 +12,10 @@
 //       keys per CTA through tensor-core tiles (mma.sync m16n8k16, online softmax over 32-key
 //       sub-tiles; 8 warps = 4 query blocks x 2 output halves); f32 inputs use SIMT tiles of 64
 //       keys (two partials per CTA).
-//   own CTAs (sequence n, head h, 512-key own block ob): one query against up to 512 keys,
-//       streamed with 16-byte coalesced loads, 8 in flight per lane (HBM-bound).
+//   own CTAs (sequence n, head h, 1024-key own block ob): one query against up to 1024 keys,
+//       streamed with 16-byte coalesced loads.  bf16: a single pass per warp with an online
+//       softmax, K and V rows of a key group loaded together (HBM-bound); f32: scores, then
+//       values, with the prefix path's exact arithmetic.
 // Each CTA writes its partials to the workspace and bumps a per-(n, h) arrival counter; the
 // CTA that completes a row merges its P partials (max of partial maxima, rescaled sums) and
 // writes o, max and sum.  The host clears the counters before each launch.
@@ -28,7 +30,7 @@ constexpr int BP = 64;        // prefix keys per tile
 constexpr int KSPLIT = 2;     // f32 path: partials per prefix CTA (key halves of 32)
 constexpr int TILES_BF16 = 8; // bf16 path: 64-key tiles streamed by one prefix CTA (512 keys)
 constexpr int NQ = 64;        // queries per prefix tile
-constexpr int BO = 512;       // own keys per own CTA
+constexpr int BO = 1024;      // own keys per own CTA
 constexpr int THREADS = 256;
 constexpr int MIN_BLOCKS = 3; // CTAs per SM the register budget is sized for
 constexpr int PAD = 8;        // bf16 row padding (row stride D+8 elements: conflict-free ldmatrix)

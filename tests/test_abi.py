@@ -86,8 +86,8 @@ def test_null_and_bad_arguments_return_status(native_lib):
 
 def test_relay_workspace_size_and_check(native_lib):
     need = native_lib.dbl_relay_merge_workspace_bytes(64, 16, 128, 4096, 1024)
-    # 64 * 16 rows x (2 * 64 prefix + 2 own partials, the f32 layout) x (128 + 2) floats + counters
-    assert need >= 64 * 16 * 130 * 130 * 4
+    # 64 * 16 rows x (2 * 64 prefix + 1 own partial, the f32 layout) x (128 + 2) floats + counters
+    assert need >= 64 * 16 * 129 * 130 * 4
     assert native_lib.dbl_relay_merge_workspace_bytes(0, 16, 128, 4096, 1024) == 0
     r = N.RelayMergeArgs(64, 16, 128, 4096, 1024, N.DBL_BF16, 0.088, 256, 256, 256, 256, 256, None, 256)
     assert native_lib.dbl_relay_merge_decode(ctypes.byref(r), None, need, None) == N.DBL_ERR_WORKSPACE
