@@ -63,6 +63,19 @@ class TrainingScanArgs(ctypes.Structure):
     ]
 
 
+class TrainingScanBackwardArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", _i64), ("time", _i64), ("heads", _i64), ("key_dim", _i64), ("value_dim", _i64),
+        ("chunk_size", _i32),
+        ("q", _vp), ("k", _vp), ("v", _vp),
+        ("alpha", _vp), ("erase", _vp), ("write", _vp),
+        ("valid", _vp), ("reset", _vp), ("initial_state", _vp),
+        ("grad_output", _vp), ("grad_final_state", _vp), ("grad_scores", _vp),
+        ("dq", _vp), ("dk", _vp), ("dv", _vp), ("dalpha", _vp), ("derase", _vp), ("dwrite", _vp),
+        ("dinitial", _vp),
+    ]
+
+
 class Gdn2ScanArgs(ctypes.Structure):
     _fields_ = [
         ("batch", _i64), ("time", _i64), ("heads", _i64), ("key_dim", _i64), ("value_dim", _i64),
@@ -93,6 +106,9 @@ EXPORTS = [
     ("dbl_gdn2_span_transition", ctypes.c_int, [ctypes.POINTER(PrefillArgs), _vp, _vp]),
     ("dbl_gdn2_decode_step", ctypes.c_int, [ctypes.POINTER(DecodeArgs), _vp]),
     ("dbl_gdn_training_scan", ctypes.c_int, [ctypes.POINTER(TrainingScanArgs), _vp]),
+    ("dbl_gdn_training_scan_backward_workspace_bytes", ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64, _i32]),
+    ("dbl_gdn_training_scan_backward", ctypes.c_int,
+     [ctypes.POINTER(TrainingScanBackwardArgs), _vp, ctypes.c_size_t, _vp]),
     ("dbl_gdn2_scan", ctypes.c_int, [ctypes.POINTER(Gdn2ScanArgs), _vp]),
     ("dbl_relay_merge_workspace_bytes", ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64]),
     ("dbl_relay_merge_decode", ctypes.c_int,

@@ -1,0 +1,321 @@
+// Backward of the stateful fused GDN-2 scan: dbl_gdn_training_scan_backward.
+//
+// Replaces delta_kernels' gdn_training_backward (crates/kernels/src/gdn_training_ops.rs:95-127,
+// kernel gdn_training.rs:117-284): the vector-Jacobian product of gdn_training_scan for the loss
+//     L = sum g_out . out + sum g_fin . final_state + sum g_score . scores.
+// The reference backward reads the checkpoints and per-token edits its forward saved; this entry
+// point recomputes them into the caller's workspace, so it needs only the forward's inputs.
+//
+// One CTA per (b, h); thread j owns value column j, as in the forward.
+//   pass 1  forward over all tokens, storing the state at every chunk start (checkpoints);
+//   pass 2  for each chunk from the last: replay it from its checkpoint, storing each token's
+//           previous state (workspace) and edit and |edit| (shared memory), then walk it in
+//           reverse with the adjoint column A[., j] in registers:
+//             dd_j = g_score |k| edit_j / |edit| + sum_i k_i A_ij     (after A += q dy^T)
+//             dq_i = sum_j (bar_ij + k_i edit_j) dy_j,   bar = reset ? 0 : alpha (.) S_prev
+//             dk_i = sum_j (A_ij edit_j - erase_i bar_ij dd_j) + g_score |edit| k_i / |k|
+//             de_i = -sum_j k_i bar_ij dd_j,   dv_j = dd_j write_j,   dw_j = dd_j v_j
+//             dbar = A - erase (.) k dd^T;  reset: A = 0;  else d alpha_i = sum_j dbar_ij S_prev_ij,
+//             A = alpha (.) dbar.
+// The sums over j use a warp butterfly reduce-scatter (lane L ends with the sum for index L of a
+// block of 32) and one shared-memory pass across warps.  f32 throughout, as the reference.
+#include "common.cuh"
+
+namespace dbl {
+namespace {
+
+constexpr unsigned FULL = 0xffffffffu;
+constexpr int MAXC = 16;  // largest checkpoint chunk (the reference's 1..=16)
+
+struct BwdParams {
+    int B, T, H, K, V, C, nch;
+    const float *q, *k, *v, *alpha, *erase, *write, *valid, *reset, *initial;
+    const float *g_out, *g_fin, *g_score;
+    float *dq, *dk, *dv, *dalpha, *derase, *dwrite, *dinitial;
+    float *ck;  // [B*H][nch][K][V] chunk-start states
+    float *rp;  // [B*H][C][K][V]   previous state of each token of the chunk being reversed
+};
+
+// Sum over the 32 lanes of vals[0..32): afterwards lane L's vals[0] holds the sum for index L.
+__device__ __forceinline__ void reduce_scatter32(float (&vals)[32], int lane) {
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        const bool upper = (lane & o) != 0;
+#pragma unroll
+        for (int x = 0; x < o; ++x) {
+            const float send = upper ? vals[x] : vals[x + o];
+            const float keep = upper ? vals[x + o] : vals[x];
+            vals[x] = keep + __shfl_xor_sync(FULL, send, o);
+        }
+    }
+}
+
+template <int KMAX>
+__global__ void __launch_bounds__(256) training_backward_kernel(const BwdParams p) {
+    constexpr int NKB = KMAX / 32;  // 32-wide blocks of key channels
+    __shared__ float sq[KMAX], sk[KMAX], sa[KMAX], se[KMAX];
+    __shared__ float sed[MAXC][256];   // edit_j of each token of the chunk
+    __shared__ float sen[MAXC][8];     // per-warp partial |edit|^2
+    __shared__ float red[8][4][KMAX];  // per-warp sums: dq, dk, dalpha, derase
+    __shared__ int sact, srst;
+
+    const int bh = blockIdx.x;
+    const int b = bh / p.H, h = bh - b * p.H;
+    const int j = threadIdx.x, nthr = blockDim.x;
+    const int warp = j >> 5, lane = j & 31, nwarps = nthr >> 5;
+    const bool col = j < p.V;
+    const int K = p.K, V = p.V, T = p.T, H = p.H;
+    const size_t sbase = ((size_t)b * H + h) * K * V;
+    auto tok = [&](int t) { return ((size_t)b * T + t) * H + h; };  // token row index
+
+    // stages k, alpha, erase (and q) of token t and its masks
+    auto stage = [&](int t, bool with_q) {
+        __syncthreads();
+        const size_t base = tok(t) * K;
+        for (int x = j; x < KMAX; x += nthr) {
+            const bool in = x < K;
+            sk[x] = in ? p.k[base + x] : 0.f;
+            sa[x] = in ? p.alpha[base + x] : 0.f;
+            se[x] = in ? p.erase[base + x] : 0.f;
+            if (with_q) sq[x] = in ? p.q[base + x] : 0.f;
+        }
+        if (j == 0) {
+            sact = p.valid[(size_t)b * T + t] != 0.f;
+            srst = p.reset[(size_t)b * T + t] != 0.f;
+        }
+        __syncthreads();
+    };
+
+    // ---------------------------------------------------------------- pass 1: checkpoints
+    float S[KMAX];
+#pragma unroll
+    for (int i = 0; i < KMAX; ++i) S[i] = (col && i < K && p.initial) ? p.initial[sbase + (size_t)i * V + j] : 0.f;
+    for (int t = 0; t < T; ++t) {
+        if (t % p.C == 0 && col) {
+            float* ckc = p.ck + ((size_t)bh * p.nch + t / p.C) * K * V;
+#pragma unroll
+            for (int i = 0; i < KMAX; ++i)
+                if (i < K) ckc[(size_t)i * V + j] = S[i];
+        }
+        stage(t, false);
+        if (!sact) continue;
+        const bool rst = srst;
+        float x = col ? p.write[tok(t) * V + j] * p.v[tok(t) * V + j] : 0.f;
+#pragma unroll
+        for (int i = 0; i < KMAX; ++i) {
+            const float bar = rst ? 0.f : sa[i] * S[i];
+            x -= se[i] * sk[i] * bar;
+            S[i] = bar;
+        }
+#pragma unroll
+        for (int i = 0; i < KMAX; ++i) S[i] = fmaf(sk[i], x, S[i]);
+    }
+
+    // ---------------------------------------------------------------- pass 2: reverse
+    float A[KMAX];
+#pragma unroll
+    for (int i = 0; i < KMAX; ++i) A[i] = (col && i < K && p.g_fin) ? p.g_fin[sbase + (size_t)i * V + j] : 0.f;
+    for (int c = p.nch - 1; c >= 0; --c) {
+        const int t0 = c * p.C, n = min(p.C, T - t0);
+        // replay the chunk: previous states to the workspace, edits to shared memory
+        const float* ckc = p.ck + ((size_t)bh * p.nch + c) * K * V;
+#pragma unroll
+        for (int i = 0; i < KMAX; ++i) S[i] = (col && i < K) ? ckc[(size_t)i * V + j] : 0.f;
+        for (int r = 0; r < n; ++r) {
+            const int t = t0 + r;
+            stage(t, false);
+            float* rpr = p.rp + ((size_t)bh * p.C + r) * K * V;
+            if (col) {
+#pragma unroll
+                for (int i = 0; i < KMAX; ++i)
+                    if (i < K) rpr[(size_t)i * V + j] = S[i];
+            }
+            float x = 0.f;
+            if (sact) {
+                const bool rst = srst;
+                x = col ? p.write[tok(t) * V + j] * p.v[tok(t) * V + j] : 0.f;
+#pragma unroll
+                for (int i = 0; i < KMAX; ++i) {
+                    const float bar = rst ? 0.f : sa[i] * S[i];
+                    x -= se[i] * sk[i] * bar;
+                    S[i] = bar;
+                }
+#pragma unroll
+                for (int i = 0; i < KMAX; ++i) S[i] = fmaf(sk[i], x, S[i]);
+            }
+            sed[r][j] = x;
+            float x2 = x * x;
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) x2 += __shfl_xor_sync(FULL, x2, o);
+            if (lane == 0) sen[r][warp] = x2;
+        }
+        for (int r = n - 1; r >= 0; --r) {
+            const int t = t0 + r;
+            stage(t, true);  // its leading barrier also orders the replay's shared writes
+            const size_t tk = tok(t) * K, tv = tok(t) * V;
+            if (!sact) {
+                for (int x = j; x < K; x += nthr) p.dq[tk + x] = p.dk[tk + x] = p.dalpha[tk + x] = p.derase[tk + x] = 0.f;
+                if (col) p.dv[tv + j] = p.dwrite[tv + j] = 0.f;
+                continue;
+            }
+            const bool rst = srst;
+            float en2 = 0.f;
+            for (int w = 0; w < nwarps; ++w) en2 += sen[r][w];
+            float kn2 = 0.f;
+#pragma unroll
+            for (int i = 0; i < KMAX; ++i) kn2 = fmaf(sk[i], sk[i], kn2);
+            const float enorm = sqrtf(en2), knorm = sqrtf(kn2);
+            const bool norms = knorm > 0.f && enorm > 0.f;
+            const float gs = p.g_score ? p.g_score[tok(t)] : 0.f;
+            const float key_scale = norms ? gs * enorm / knorm : 0.f;
+            const float xe = sed[r][j];  // this column's edit (0 beyond V)
+            const float dy = col ? p.g_out[tv + j] : 0.f;
+            float dd = (norms && col) ? gs * knorm * xe / enorm : 0.f;
+#pragma unroll
+            for (int i = 0; i < KMAX; ++i) {
+                A[i] = fmaf(sq[i], dy, A[i]);
+                dd = fmaf(sk[i], A[i], dd);
+            }
+            if (!col) dd = 0.f;
+            const float* rpr = p.rp + ((size_t)bh * p.C + r) * K * V;
+            float prev[KMAX];
+#pragma unroll
+            for (int i = 0; i < KMAX; ++i) prev[i] = (col && i < K) ? rpr[(size_t)i * V + j] : 0.f;
+            // the four per-channel sums, one 32-wide block at a time
+#pragma unroll
+            for (int kb = 0; kb < NKB; ++kb) {
+                float vals[32];
+#pragma unroll
+                for (int u = 0; u < 32; ++u) {
+                    const int i = 32 * kb + u;
+                    const float bar = rst ? 0.f : sa[i] * prev[i];
+                    vals[u] = (bar + sk[i] * xe) * dy;
+                }
+                reduce_scatter32(vals, lane);
+                red[warp][0][32 * kb + lane] = vals[0];
+#pragma unroll
+                for (int u = 0; u < 32; ++u) {
+                    const int i = 32 * kb + u;
+                    const float bar = rst ? 0.f : sa[i] * prev[i];
+                    vals[u] = A[i] * xe - se[i] * bar * dd;
+                }
+                reduce_scatter32(vals, lane);
+                red[warp][1][32 * kb + lane] = vals[0];
+#pragma unroll
+                for (int u = 0; u < 32; ++u) {
+                    const int i = 32 * kb + u;
+                    const float bar = rst ? 0.f : sa[i] * prev[i];
+                    vals[u] = -sk[i] * bar * dd;
+                }
+                reduce_scatter32(vals, lane);
+                red[warp][3][32 * kb + lane] = vals[0];
+#pragma unroll
+                for (int u = 0; u < 32; ++u) {
+                    const int i = 32 * kb + u;
+                    const float dbar = A[i] - se[i] * sk[i] * dd;
+                    vals[u] = rst ? 0.f : dbar * prev[i];
+                    A[i] = rst ? 0.f : sa[i] * dbar;
+                }
+                reduce_scatter32(vals, lane);
+                red[warp][2][32 * kb + lane] = vals[0];
+            }
+            if (col) {
+                p.dv[tv + j] = dd * p.write[tv + j];
+                p.dwrite[tv + j] = dd * p.v[tv + j];
+            }
+            __syncthreads();
+            for (int x = j; x < 4 * K; x += nthr) {
+                const int kind = x / K, i = x - kind * K;
+                float s = 0.f;
+                for (int w = 0; w < nwarps; ++w) s += red[w][kind][i];
+                if (kind == 0) p.dq[tk + i] = s;
+                else if (kind == 1) p.dk[tk + i] = s + key_scale * sk[i];
+                else if (kind == 2) p.dalpha[tk + i] = s;
+                else p.derase[tk + i] = s;
+            }
+        }
+    }
+    if (p.dinitial && col) {
+#pragma unroll
+        for (int i = 0; i < KMAX; ++i)
+            if (i < K) p.dinitial[sbase + (size_t)i * V + j] = A[i];
+    }
+}
+
+int nchunks_of(int64_t T, int C) { return (int)((T + C - 1) / C); }
+
+}  // namespace
+
+size_t training_backward_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t K, int64_t V, int chunk) {
+    if (B <= 0 || T <= 0 || H <= 0 || K <= 0 || V <= 0 || chunk < 1 || chunk > MAXC) return 0;
+    const size_t heads = (size_t)B * H, kv = (size_t)K * V;
+    return (heads * nchunks_of(T, chunk) * kv + heads * chunk * kv) * sizeof(float);
+}
+
+}  // namespace dbl
+
+extern "C" size_t dbl_gdn_training_scan_backward_workspace_bytes(int64_t batch, int64_t time, int64_t heads,
+                                                                 int64_t key_dim, int64_t value_dim,
+                                                                 int32_t chunk_size) {
+    return dbl::training_backward_workspace_bytes(batch, time, heads, key_dim, value_dim, chunk_size);
+}
+
+extern "C" int dbl_gdn_training_scan_backward(const dbl_training_scan_backward_args* a, void* workspace,
+                                              size_t workspace_bytes, dbl_stream_t stream) {
+    using namespace dbl;
+    if (!a) return fail(DBL_ERR_INVALID_ARGUMENT, "gdn_training_scan_backward: null args");
+    if (a->batch <= 0 || a->time <= 0 || a->heads <= 0 || a->key_dim <= 0 || a->value_dim <= 0)
+        return fail(DBL_ERR_INVALID_ARGUMENT, "GDN-2 requires nonempty axes");
+    if (a->chunk_size < 1 || a->chunk_size > MAXC)
+        return fail(DBL_ERR_INVALID_ARGUMENT, "GDN-2 checkpoint chunk must be 1..=16");
+    if (!a->q || !a->k || !a->v || !a->alpha || !a->erase || !a->write || !a->valid || !a->reset || !a->grad_output ||
+        !a->dq || !a->dk || !a->dv || !a->dalpha || !a->derase || !a->dwrite)
+        return fail(DBL_ERR_INVALID_ARGUMENT,
+                    "gdn_training_scan_backward: q, k, v, alpha, erase, write, valid, reset, grad_output and the "
+                    "six input gradients are required");
+    if (a->key_dim > 64 || a->value_dim > 256)
+        return fail(DBL_ERR_UNSUPPORTED, "gdn_training_scan_backward: key width up to 64 and value width up to 256");
+    if (a->batch * a->heads > 0x7fffffff || a->time > 0x7fffffff)
+        return fail(DBL_ERR_UNSUPPORTED, "GDN-2 axis exceeds 32-bit limits");
+    const size_t need = training_backward_workspace_bytes(a->batch, a->time, a->heads, a->key_dim, a->value_dim,
+                                                          a->chunk_size);
+    if (!workspace || workspace_bytes < need)
+        return fail(DBL_ERR_WORKSPACE, "gdn_training_scan_backward: workspace of %zu bytes required (got %zu)", need,
+                    workspace_bytes);
+    BwdParams p{};
+    p.B = (int)a->batch;
+    p.T = (int)a->time;
+    p.H = (int)a->heads;
+    p.K = (int)a->key_dim;
+    p.V = (int)a->value_dim;
+    p.C = a->chunk_size;
+    p.nch = nchunks_of(a->time, a->chunk_size);
+    p.q = a->q;
+    p.k = a->k;
+    p.v = a->v;
+    p.alpha = a->alpha;
+    p.erase = a->erase;
+    p.write = a->write;
+    p.valid = a->valid;
+    p.reset = a->reset;
+    p.initial = a->initial_state;
+    p.g_out = a->grad_output;
+    p.g_fin = a->grad_final_state;
+    p.g_score = a->grad_scores;
+    p.dq = a->dq;
+    p.dk = a->dk;
+    p.dv = a->dv;
+    p.dalpha = a->dalpha;
+    p.derase = a->derase;
+    p.dwrite = a->dwrite;
+    p.dinitial = a->dinitial;
+    const size_t heads = (size_t)a->batch * a->heads;
+    p.ck = static_cast<float*>(workspace);
+    p.rp = p.ck + heads * p.nch * (size_t)p.K * p.V;
+    const int threads = (p.V + 31) / 32 * 32;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (p.K <= 32) training_backward_kernel<32><<<(unsigned)heads, threads, 0, st>>>(p);
+    else training_backward_kernel<64><<<(unsigned)heads, threads, 0, st>>>(p);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? DBL_OK : cuda_status(e, "gdn_training_scan_backward launch");
+}

@@ -6,6 +6,7 @@ calls the C ABI of ``libdbl_gdn2.so`` on the current CUDA stream.  torch is only
 (device memory and streams); every kernel is this package's own CUDA code.
 
     gdn_training_scan  <- delta_kernels::gdn_training_scan  (crates/kernels/src/gdn_training_ops.rs:288-333)
+    gdn_training_backward <- GdnTrainingOps::gdn_training_backward (gdn_training_ops.rs:95-127)
     gdn2_scan          <- delta_kernels::gdn2_scan          (crates/kernels/src/ops.rs:251-276)
     gdn2_prefill       <- scalar-gate chunked forward (the BASELINE prefill; chunk.rs:129-250 semantics)
     gdn2_span_transition  hand-off matrix for time-sharded prefill (no reference counterpart)
@@ -104,6 +105,60 @@ def gdn_training_scan(q, k, v, alpha, erase, write, valid, reset, initial, chunk
                                _ptr(output), _ptr(final), _ptr(scores))
         N.check(N.lib().dbl_gdn_training_scan(ctypes.byref(a), _stream(dev)))
     return GdnTrainingOutput(output, final, scores)
+
+
+@dataclass
+class GdnTrainingGrads:
+    """Gradients of gdn_training_scan's inputs, in the order the reference's backward returns them
+    (gdn_training_ops.rs:95-127): q, k, v, alpha, erase, write, initial."""
+
+    dq: torch.Tensor
+    dk: torch.Tensor
+    dv: torch.Tensor
+    dalpha: torch.Tensor
+    derase: torch.Tensor
+    dwrite: torch.Tensor
+    dinitial: torch.Tensor
+
+
+def gdn_training_backward(q, k, v, alpha, erase, write, valid, reset, initial, grad_output,
+                          grad_final_state=None, grad_scores=None, chunk_size: int = 16
+                          ) -> GdnTrainingGrads:
+    """Backward of gdn_training_scan for L = sum grad_output.output + sum grad_final_state.final_state
+    + sum grad_scores.scores.  f32 as the reference's backward (K <= 64, V <= 256); the reference's
+    packed upstream tensor is passed as its three parts; checkpoints are recomputed (chunk_size
+    1..=16 is their spacing) instead of being read from the forward."""
+    dev = _require_cuda(q, k, v, alpha, erase, write, valid, reset, initial, grad_output)
+    B, T, H, K = q.shape
+    V = v.shape[3]
+    if B == 0 or T == 0 or H == 0:
+        raise ValueError("GDN-2 requires nonempty axes")
+    for name, t, shape in (("k", k, (B, T, H, K)), ("v", v, (B, T, H, V)),
+                           ("alpha", alpha, (B, T, H, K)), ("erase", erase, (B, T, H, K)),
+                           ("write", write, (B, T, H, V)), ("valid", valid, (B, T)),
+                           ("reset", reset, (B, T)), ("initial", initial, (B, H, K, V)),
+                           ("grad_output", grad_output, (B, T, H, V)),
+                           ("grad_final_state", grad_final_state, (B, H, K, V)),
+                           ("grad_scores", grad_scores, (B, T, H))):
+        if t is not None and tuple(t.shape) != shape and not (name == "grad_scores" and tuple(t.shape) == (B, T, H, 1)):
+            raise ValueError(f"{name} must have shape {list(shape)}, got {list(t.shape)}")
+    if not 1 <= chunk_size <= 16:
+        raise ValueError("GDN-2 checkpoint chunk must be 1..=16")
+    lib = N.lib()
+    with torch.cuda.device(dev):
+        f = [_f32c(x) for x in (q, k, v, alpha, erase, write, valid, reset, initial, grad_output)]
+        gf = None if grad_final_state is None else _f32c(grad_final_state)
+        gs = None if grad_scores is None else _f32c(grad_scores)
+        dq, dk, da, de = (torch.empty((B, T, H, K), device=dev, dtype=torch.float32) for _ in range(4))
+        dv, dw = (torch.empty((B, T, H, V), device=dev, dtype=torch.float32) for _ in range(2))
+        di = torch.empty((B, H, K, V), device=dev, dtype=torch.float32)
+        need = lib.dbl_gdn_training_scan_backward_workspace_bytes(B, T, H, K, V, chunk_size)
+        ws = torch.empty(max(need, 1), device=dev, dtype=torch.uint8)
+        a = N.TrainingScanBackwardArgs(B, T, H, K, V, chunk_size, *(_ptr(x) for x in f[:9]), _ptr(f[9]),
+                                       _ptr(gf), _ptr(gs), _ptr(dq), _ptr(dk), _ptr(dv), _ptr(da), _ptr(de),
+                                       _ptr(dw), _ptr(di))
+        N.check(lib.dbl_gdn_training_scan_backward(ctypes.byref(a), _ptr(ws), need, _stream(dev)))
+    return GdnTrainingGrads(dq, dk, dv, da, de, dw, di)
 
 
 def gdn2_scan(q, k, v, alpha, erase, write, doc_start, doc_end) -> torch.Tensor:

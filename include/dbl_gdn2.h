@@ -150,6 +150,36 @@ typedef struct {
 
 int dbl_gdn_training_scan(const dbl_training_scan_args *args, dbl_stream_t stream);
 
+/* Backward (vector-Jacobian product) of dbl_gdn_training_scan for the loss
+ *     L = sum grad_output . output + sum grad_final_state . final_state + sum grad_scores . scores.
+ * Replaces delta_kernels' gdn_training_backward (crates/kernels/src/gdn_training_ops.rs:95-127,
+ * kernel gdn_training.rs:117-284), whose upstream tensor packs the three gradients; here they are
+ * separate pointers.  The reference reads the checkpoints and per-token edits its forward saved;
+ * this call recomputes them into `workspace` (dbl_gdn_training_scan_backward_workspace_bytes()
+ * bytes), so it needs only the forward's inputs.  f32 throughout, as the reference; K <= 64,
+ * V <= 256; chunk_size (1..=16) is the checkpoint spacing.  All arrays contiguous.
+ * Outputs: dq, dk, dalpha, derase [B,T,H,K]; dv, dwrite [B,T,H,V]; dinitial [B,H,K,V] (optional).
+ * grad_final_state, grad_scores and initial_state may be NULL (zeros). */
+typedef struct {
+    int64_t batch, time, heads, key_dim, value_dim;
+    int32_t chunk_size;
+    const float *q, *k, *v;
+    const float *alpha, *erase, *write;
+    const float *valid, *reset;       /* required, [B,T]                                        */
+    const float *initial_state;       /* optional [B,H,K,V]                                     */
+    const float *grad_output;         /* required [B,T,H,V]                                     */
+    const float *grad_final_state;    /* optional [B,H,K,V]                                     */
+    const float *grad_scores;         /* optional [B,T,H]                                       */
+    float *dq, *dk, *dv, *dalpha, *derase, *dwrite;
+    float *dinitial;                  /* optional                                               */
+} dbl_training_scan_backward_args;
+
+size_t dbl_gdn_training_scan_backward_workspace_bytes(int64_t batch, int64_t time, int64_t heads,
+                                                      int64_t key_dim, int64_t value_dim,
+                                                      int32_t chunk_size);
+int dbl_gdn_training_scan_backward(const dbl_training_scan_backward_args *args, void *workspace,
+                                   size_t workspace_bytes, dbl_stream_t stream);
+
 /* Mirrors delta_kernels::gdn2_scan(q, k, v, alpha, erase, write, doc_start, doc_end) -> output
  * (crates/kernels/src/ops.rs:251-276, kernels gdn2.rs:23-283; oracle gdn2_reference.rs:87-105):
  * inclusive int32 document limits [B,T]; `end < start` marks padding (output 0, state kept),

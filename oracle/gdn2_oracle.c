@@ -19,6 +19,8 @@
  *                          (the online-softmax recurrence, in the kernel's f32 arithmetic)
  *   orc_relay_window_f64   relay_attention_kernel.rs:38-130 reference layout: +-radius
  *                          document window plus relay slots of the query's document
+ *   orc_gdn_training_backward_f64  crates/kernels/src/gdn_training.rs:117-284 (the backward of
+ *                          the stateful fused scan: gradients of q, k, v, gates and initial)
  *
  * Layouts (all contiguous, row-major):
  *   q, k, alpha, erase : [B,T,H,K]      v, write : [B,T,H,V]
@@ -516,5 +518,142 @@ int orc_relay_window_f64(int B, int H, int T, int D, int ndoc, int slots, int ra
             }
     free(sc);
     free(vs);
+    return 0;
+}
+
+/* ------------------------------------------------------------------------------------------
+ * Backward (vector-Jacobian product) of the stateful fused scan, restating the reference's
+ * backward kernel (crates/kernels/src/gdn_training.rs:117-284; op gdn_training_backward,
+ * gdn_training_ops.rs:95-127) for the loss
+ *     L = sum g_out . out + sum g_fin . final_state + sum g_score . scores.
+ * Per token t, in reverse, with A = dL/dS after the token (starting from g_fin):
+ *   padding: no gradient, A unchanged;
+ *   dd_j   = g_score |k| edit_j / |edit| + sum_i k_i A_ij   (after A += q dy^T, dy = g_out[t]);
+ *   bar    = reset ? 0 : alpha (.) S_prev;   dq_i = sum_j (bar + k_i edit_j) dy_j;
+ *   dk_i   = sum_j (A_ij edit_j - erase_i bar_ij dd_j) + g_score |edit| k_i / |k|;
+ *   de_i   = -sum_j k_i bar_ij dd_j;   dv_j = dd_j write_j;   dw_j = dd_j v_j;
+ *   dbar   = A - erase (.) k dd^T;  reset: A = 0, d alpha = 0;  else d alpha_i = sum_j dbar_ij
+ *            S_prev_ij and A = alpha (.) dbar.
+ * The score terms are taken only when |k| > 0 and |edit| > 0, as the reference does.  The
+ * reference replays each checkpoint chunk in f32; here every state is kept in f64, which the
+ * chunking does not change.  dinitial (optional) receives A after token 0.
+ * ---------------------------------------------------------------------------------------- */
+int orc_gdn_training_backward_f64(int B, int T, int H, int K, int V,
+                                  const double *q, const double *k, const double *v,
+                                  const double *alpha, const double *erase, const double *write,
+                                  const uint8_t *valid, const uint8_t *reset, const double *initial,
+                                  const double *g_out, const double *g_fin, const double *g_score,
+                                  double *dq, double *dk, double *dv, double *dalpha, double *derase,
+                                  double *dwrite, double *dinitial)
+{
+    double *S = (double *)malloc(sizeof(double) * (size_t)(T + 1) * K * V);
+    double *ed = (double *)malloc(sizeof(double) * (size_t)T * V);
+    double *kn = (double *)malloc(sizeof(double) * (size_t)T);
+    double *en = (double *)malloc(sizeof(double) * (size_t)T);
+    double *A = (double *)malloc(sizeof(double) * (size_t)K * V);
+    double *dd = (double *)malloc(sizeof(double) * (size_t)V);
+    if (!S || !ed || !kn || !en || !A || !dd) {
+        free(S); free(ed); free(kn); free(en); free(A); free(dd);
+        return -2;
+    }
+    for (int b = 0; b < B; ++b)
+        for (int h = 0; h < H; ++h) {
+            const size_t sbase = ((size_t)b * H + h) * K * V;
+            /* forward: every state S_t (before token t) and every token's edit and norms */
+            if (initial) memcpy(S, initial + sbase, sizeof(double) * K * V);
+            else memset(S, 0, sizeof(double) * K * V);
+            for (int t = 0; t < T; ++t) {
+                const double *St = S + (size_t)t * K * V;
+                double *Sn = S + (size_t)(t + 1) * K * V;
+                const int act = valid ? valid[(size_t)b * T + t] != 0 : 1;
+                const int rst = reset ? reset[(size_t)b * T + t] != 0 : 0;
+                const double *kt = k + IDX4(b, t, h, 0, T, H, K);
+                const double *at = alpha + IDX4(b, t, h, 0, T, H, K);
+                const double *et = erase + IDX4(b, t, h, 0, T, H, K);
+                const double *vt = v + IDX4(b, t, h, 0, T, H, V);
+                const double *wt = write + IDX4(b, t, h, 0, T, H, V);
+                double *edt = ed + (size_t)t * V;
+                if (!act) {
+                    memcpy(Sn, St, sizeof(double) * K * V);
+                    memset(edt, 0, sizeof(double) * V);
+                    kn[t] = en[t] = 0.0;
+                    continue;
+                }
+                double k2 = 0.0, e2 = 0.0;
+                for (int i = 0; i < K; ++i) k2 += kt[i] * kt[i];
+                for (int j = 0; j < V; ++j) {
+                    double x = wt[j] * vt[j];
+                    for (int i = 0; i < K; ++i) x -= et[i] * kt[i] * (rst ? 0.0 : at[i] * St[(size_t)i * V + j]);
+                    edt[j] = x;
+                    e2 += x * x;
+                }
+                for (int i = 0; i < K; ++i)
+                    for (int j = 0; j < V; ++j)
+                        Sn[(size_t)i * V + j] = (rst ? 0.0 : at[i] * St[(size_t)i * V + j]) + kt[i] * edt[j];
+                kn[t] = sqrt(k2);
+                en[t] = sqrt(e2);
+            }
+            /* reverse */
+            if (g_fin) memcpy(A, g_fin + sbase, sizeof(double) * K * V);
+            else memset(A, 0, sizeof(double) * K * V);
+            for (int t = T - 1; t >= 0; --t) {
+                double *dqt = dq + IDX4(b, t, h, 0, T, H, K), *dkt = dk + IDX4(b, t, h, 0, T, H, K);
+                double *dat = dalpha + IDX4(b, t, h, 0, T, H, K), *det = derase + IDX4(b, t, h, 0, T, H, K);
+                double *dvt = dv + IDX4(b, t, h, 0, T, H, V), *dwt = dwrite + IDX4(b, t, h, 0, T, H, V);
+                for (int i = 0; i < K; ++i) dqt[i] = dkt[i] = dat[i] = det[i] = 0.0;
+                for (int j = 0; j < V; ++j) dvt[j] = dwt[j] = 0.0;
+                const int act = valid ? valid[(size_t)b * T + t] != 0 : 1;
+                if (!act) continue;
+                const int rst = reset ? reset[(size_t)b * T + t] != 0 : 0;
+                const double *qt = q + IDX4(b, t, h, 0, T, H, K);
+                const double *kt = k + IDX4(b, t, h, 0, T, H, K);
+                const double *at = alpha + IDX4(b, t, h, 0, T, H, K);
+                const double *et = erase + IDX4(b, t, h, 0, T, H, K);
+                const double *vt = v + IDX4(b, t, h, 0, T, H, V);
+                const double *wt = write + IDX4(b, t, h, 0, T, H, V);
+                const double *dy = g_out + IDX4(b, t, h, 0, T, H, V);
+                const double gs = g_score ? g_score[((size_t)b * T + t) * H + h] : 0.0;
+                const double *St = S + (size_t)t * K * V;
+                const double *edt = ed + (size_t)t * V;
+                double key_scale = 0.0;
+                const int norms = kn[t] > 0.0 && en[t] > 0.0;
+                if (norms) key_scale = gs * en[t] / kn[t];
+                for (int i = 0; i < K; ++i)
+                    for (int j = 0; j < V; ++j) A[(size_t)i * V + j] += qt[i] * dy[j];
+                for (int j = 0; j < V; ++j) {
+                    double x = norms ? gs * kn[t] * edt[j] / en[t] : 0.0;
+                    for (int i = 0; i < K; ++i) x += kt[i] * A[(size_t)i * V + j];
+                    dd[j] = x;
+                }
+                for (int i = 0; i < K; ++i) {
+                    double gq = 0.0, gk = 0.0, ga = 0.0, ge = 0.0;
+                    for (int j = 0; j < V; ++j) {
+                        const double prev = St[(size_t)i * V + j];
+                        const double bar = rst ? 0.0 : at[i] * prev;
+                        double *a = A + (size_t)i * V + j;
+                        gq += (bar + kt[i] * edt[j]) * dy[j];
+                        gk += *a * edt[j] - et[i] * bar * dd[j];
+                        ge -= kt[i] * bar * dd[j];
+                        const double dbar = *a - et[i] * kt[i] * dd[j];
+                        if (rst) {
+                            *a = 0.0;
+                        } else {
+                            ga += dbar * prev;
+                            *a = at[i] * dbar;
+                        }
+                    }
+                    dqt[i] = gq;
+                    dkt[i] = gk + key_scale * kt[i];
+                    dat[i] = ga;
+                    det[i] = ge;
+                }
+                for (int j = 0; j < V; ++j) {
+                    dvt[j] = dd[j] * wt[j];
+                    dwt[j] = dd[j] * vt[j];
+                }
+            }
+            if (dinitial) memcpy(dinitial + sbase, A, sizeof(double) * K * V);
+        }
+    free(S); free(ed); free(kn); free(en); free(A); free(dd);
     return 0;
 }

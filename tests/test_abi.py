@@ -17,6 +17,7 @@ STRUCTS = {
     "dbl_prefill_args": N.PrefillArgs,
     "dbl_decode_args": N.DecodeArgs,
     "dbl_training_scan_args": N.TrainingScanArgs,
+    "dbl_training_scan_backward_args": N.TrainingScanBackwardArgs,
     "dbl_gdn2_scan_args": N.Gdn2ScanArgs,
     "dbl_relay_merge_args": N.RelayMergeArgs,
 }
@@ -99,3 +100,18 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(N, "_lib", None)
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         N.lib()
+
+
+def test_training_backward_workspace_and_checks(native_lib):
+    f = native_lib.dbl_gdn_training_scan_backward_workspace_bytes
+    # checkpoints (B*H*ceil(T/C)) plus one chunk of replayed states (B*H*C), K*V floats each
+    assert f(2, 40, 3, 32, 64, 16) == (2 * 3 * 3 + 2 * 3 * 16) * 32 * 64 * 4
+    assert f(2, 40, 3, 32, 64, 17) == 0 and f(0, 40, 3, 32, 64, 16) == 0
+    a = N.TrainingScanBackwardArgs(1, 8, 1, 32, 64, 0)
+    assert native_lib.dbl_gdn_training_scan_backward(ctypes.byref(a), None, 0, None) == N.DBL_ERR_INVALID_ARGUMENT
+    ptrs = {n: 256 for n, _ in N.TrainingScanBackwardArgs._fields_[6:] if n not in
+            ("initial_state", "grad_final_state", "grad_scores", "dinitial")}
+    a = N.TrainingScanBackwardArgs(1, 8, 1, 96, 64, 8, **ptrs)
+    assert native_lib.dbl_gdn_training_scan_backward(ctypes.byref(a), 256, 1 << 30, None) == N.DBL_ERR_UNSUPPORTED
+    a = N.TrainingScanBackwardArgs(1, 8, 1, 32, 64, 8, **ptrs)
+    assert native_lib.dbl_gdn_training_scan_backward(ctypes.byref(a), 256, 16, None) == N.DBL_ERR_WORKSPACE

@@ -287,3 +287,32 @@ def test_prefill_tc_span_transition(cuda, native_lib):
     assert _device_error_clear(native_lib) == (0, 0)
     comp = np.einsum("bhik,bhkj->bhij", A, S0) + host(Bs)
     assert rel_err(comp, ref_fin) < TOL_BF16
+
+
+# ----------------------------------------------------------------------- training-scan backward
+@pytest.mark.parametrize("K,V,chunk", [(32, 64, 16), (64, 128, 5), (20, 40, 1)])
+def test_training_backward_matches_oracle(cuda, native_lib, K, V, chunk):
+    # gdn_training_backward (gdn_training.rs:117-284) against the f64 oracle, which is itself
+    # pinned by finite differences (tests/test_oracle.py); padding, resets, an initial state and
+    # all three upstream gradients.
+    rng = np.random.default_rng(K + V)
+    B, T, H = 2, 37, 3
+    q, k = rng.standard_normal((B, T, H, K)) / np.sqrt(K), rng.standard_normal((B, T, H, K)) / np.sqrt(K)
+    v, w = rng.standard_normal((B, T, H, V)), rng.random((B, T, H, V))
+    a, e = rng.uniform(0.6, 1.0, (B, T, H, K)), rng.random((B, T, H, K))
+    valid = rng.random((B, T)) > 0.1
+    reset = rng.random((B, T)) > 0.93
+    init = 0.1 * rng.standard_normal((B, H, K, V))
+    go, gf, gs = rng.standard_normal((B, T, H, V)), rng.standard_normal((B, H, K, V)), rng.standard_normal((B, T, H))
+    d = lambda x: torch.as_tensor(np.asarray(x, np.float32), device=cuda)  # noqa: E731
+    got = dbl.gdn_training_backward(d(q), d(k), d(v), d(a), d(e), d(w), d(valid), d(reset), d(init), d(go),
+                                    d(gf), d(gs), chunk_size=chunk)
+    torch.cuda.synchronize()
+    ref = O.training_backward(*(np.asarray(x, np.float32) for x in (q, k, v, a, e, w, go, gf, gs)), valid, reset,
+                              np.asarray(init, np.float32))
+    names = ("dq", "dk", "dv", "dalpha", "derase", "dwrite", "dinitial")
+    for name, r in zip(names, ref):
+        g = getattr(got, name).cpu().numpy()
+        assert rel_err(g, r) < TOL_F32, (name, rel_err(g, r))
+    for name in names[:6]:
+        assert np.all(getattr(got, name).cpu().numpy()[~valid] == 0.0), name

@@ -244,3 +244,43 @@ def test_golden_fixtures_reproduce():
     assert set(stored.files) == set(fresh)
     for name in stored.files:
         np.testing.assert_allclose(fresh[name], stored[name], rtol=1e-12, atol=1e-14, err_msg=name)
+
+
+def test_training_backward_matches_finite_differences():
+    # The backward oracle (gdn_training.rs:117-284 restated) against central differences of the
+    # forward oracle, for L = sum g_out.out + sum g_fin.final + sum g_score.scores, with padding,
+    # a reset, an initial state and score gradients -- the finite-difference style of
+    # gdn2_reference.rs:237-268.
+    rng = np.random.default_rng(7)
+    B, T, H, K, V = 1, 9, 2, 3, 4
+    q, k = rng.standard_normal((B, T, H, K)), rng.standard_normal((B, T, H, K))
+    v, w = rng.standard_normal((B, T, H, V)), rng.random((B, T, H, V))
+    a, e = rng.uniform(0.5, 1.0, (B, T, H, K)), rng.random((B, T, H, K))
+    valid = np.ones((B, T), bool)
+    valid[0, 4] = False
+    reset = np.zeros((B, T), bool)
+    reset[0, 6] = True
+    init = 0.3 * rng.standard_normal((B, H, K, V))
+    go, gf, gs = rng.standard_normal((B, T, H, V)), rng.standard_normal((B, H, K, V)), rng.standard_normal((B, T, H))
+    inputs = [q, k, v, a, e, w, init]
+
+    def loss(xs):
+        o, f, s = O.scan(*xs[:6], valid, reset, xs[6])
+        return float(np.sum(go * o) + np.sum(gf * f) + np.sum(gs * s))
+    grads = O.training_backward(q, k, v, a, e, w, go, gf, gs, valid, reset, init)
+    # dq, dk, dv, dalpha, derase, dwrite, dinitial  <->  inputs q, k, v, alpha, erase, write, initial
+    for gi, xi in zip(grads, [0, 1, 2, 3, 4, 5, 6]):
+        x = inputs[xi]
+        num = np.zeros_like(x)
+        it = np.nditer(x, flags=["multi_index"])
+        for _ in it:
+            idx = it.multi_index
+            hi = [y.copy() for y in inputs]
+            lo = [y.copy() for y in inputs]
+            hi[xi][idx] += 1e-6
+            lo[xi][idx] -= 1e-6
+            num[idx] = (loss(hi) - loss(lo)) / 2e-6
+        assert np.max(np.abs(gi - num)) < 1e-6 * (1 + np.max(np.abs(num))), xi
+    # padding tokens get no gradient
+    for g in grads[:6]:
+        assert np.all(g[0, 4] == 0.0)
