@@ -492,6 +492,85 @@ def bench_relay(torch, args, dev):
             "gpu_launches": reps}
 
 
+def bench_backward(torch, args, dev):
+    """Training shape of the reference's fused scan (B8/T512/H4, K32/V64, f32, chunk 16): the
+    backward (gdn_training_backward) and, for context, the forward gdn_training_scan."""
+    import delta_block_lm_b200 as dbl
+
+    b, t, h, k_, v_ = 8, 512, 4, 32, 64
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+    rn = lambda *s: torch.randn(s, device=dev, generator=g)  # noqa: E731
+    q, k = rn(b, t, h, k_) / math.sqrt(k_), rn(b, t, h, k_) / math.sqrt(k_)
+    v, w = rn(b, t, h, v_), torch.sigmoid(rn(b, t, h, v_))
+    a, e = torch.sigmoid(3.0 + rn(b, t, h, k_)), torch.sigmoid(rn(b, t, h, k_))
+    valid, reset = torch.ones(b, t, device=dev), torch.zeros(b, t, device=dev)
+    init = torch.zeros(b, h, k_, v_, device=dev)
+    go, gf, gs = rn(b, t, h, v_), rn(b, h, k_, v_), rn(b, t, h)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn, reps=10):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / reps
+
+    ms_b = timed(lambda: dbl.gdn_training_backward(q, k, v, a, e, w, valid, reset, init, go, gf, gs, chunk_size=16))
+    ms_f = timed(lambda: dbl.gdn_training_scan(q, k, v, a, e, w, valid, reset, init, 16))
+    tokens = b * t
+    return {"metric": "GDN-2 training scan backward Mtok/s (gdn_training_backward)",
+            "value": tokens / (ms_b / 1e3) / 1e6, "unit": "Mtok/s", "ms_per_step": ms_b, "n_gpus": 1,
+            "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"B{b}/T{t}/H{h}/K{k_}/V{v_} f32 chunk 16 (the reference's training shape)",
+                       "forward_ms": ms_f, "forward_mtok_s": tokens / (ms_f / 1e3) / 1e6},
+            "gpu_launches": 10}
+
+
+def bench_prologue(torch, args, dev):
+    """The GDN-2 mixer prologue (conv + silu + l2 for q, k; conv + silu for v; decay and sigmoid
+    gates) at the config-1 shape: B8/T4096/H16, K = V = 128, bf16 projections in, bf16 q, k, v and
+    f32 gates out (HBM-bound)."""
+    import delta_block_lm_b200 as dbl
+
+    b, t, h, d = B, T, H, D
+    g = torch.Generator(device=dev)
+    g.manual_seed(13)
+    rn = lambda *s, dt=torch.float32: torch.randn(s, device=dev, generator=g).to(dt)  # noqa: E731
+    proj = [rn(b, t, h * d, dt=torch.bfloat16) for _ in range(6)]
+    conv = [0.3 * rn(4, h * d) for _ in range(3)]
+    bias, scale = rn(h * d), 0.3 * rn(h)
+    valid, reset = torch.ones(b, t, device=dev), (torch.rand(b, t, device=dev, generator=g) > 0.999).float()
+    stream = torch.cuda.current_stream(dev)
+    call = lambda: dbl.gdn2_prologue(*proj, *conv, bias, scale, valid, reset, heads=h, out_dtype=torch.bfloat16)  # noqa: E731
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize(dev)
+    reps = 20
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        call()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / reps
+    hbm, _, src = peaks()
+    # per token-head: 6 bf16 projection rows in; q, k, v bf16 and alpha, erase, write f32 out
+    alg = b * t * h * (6 * d * 2 + 3 * d * 2 + 3 * d * 4)
+    gbs = alg / (ms / 1e3) / 1e9
+    return {"metric": "GDN-2 mixer prologue Mtok/s", "value": b * t / (ms / 1e3) / 1e6, "unit": "Mtok/s",
+            "ms_per_step": ms, "n_gpus": 1, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"B{b}/T{t}/H{h}/K=V={d}, conv width 4, bf16 in/out, f32 gates"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                         "peak_source": src, "algorithmic_bytes_per_launch": alg},
+            "gpu_launches": reps}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -500,9 +579,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true", help="skip the decode / relay lines")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["prefill", "long", "decode", "relay"], default="prefill",
+    ap.add_argument("--workload", choices=["prefill", "long", "decode", "relay", "backward", "prologue"], default="prefill",
                     help="prefill: config 1 (the headline, weak-scaled); long: config 4 (time-sharded); "
-                         "decode: config 2 alone; relay: config 3 alone (1 GPU)")
+                         "decode: config 2 alone; relay: config 3 alone; backward: the fused scan's "
+                         "backward at the reference's training shape; prologue: the mixer prologue (1 GPU)")
     ap.add_argument("--long-tokens", type=int, default=131072)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -530,6 +610,16 @@ def main():
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()
+        return 0
+    if args.workload == "prologue":
+        if world > 1:
+            raise SystemExit("--workload prologue runs on one GPU")
+        print(json.dumps(bench_prologue(torch, args, dev)), flush=True)
+        return 0
+    if args.workload == "backward":
+        if world > 1:
+            raise SystemExit("--workload backward runs on one GPU")
+        print(json.dumps(bench_backward(torch, args, dev)), flush=True)
         return 0
     if args.workload in ("decode", "relay"):
         # single-kernel lines (the same measurements as the headline's `secondary` object)

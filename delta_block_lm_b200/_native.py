@@ -76,6 +76,18 @@ class TrainingScanBackwardArgs(ctypes.Structure):
     ]
 
 
+class Gdn2PrologueArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", _i64), ("time", _i64), ("heads", _i64), ("key_dim", _i64), ("value_dim", _i64),
+        ("conv_width", _i64), ("in_dtype", _i32), ("out_dtype", _i32),
+        ("proj_q", _vp), ("proj_k", _vp), ("proj_v", _vp),
+        ("proj_decay", _vp), ("proj_erase", _vp), ("proj_write", _vp),
+        ("conv_q", _vp), ("conv_k", _vp), ("conv_v", _vp),
+        ("decay_bias", _vp), ("decay_scale", _vp), ("valid", _vp), ("reset", _vp),
+        ("q", _vp), ("k", _vp), ("v", _vp), ("alpha", _vp), ("erase", _vp), ("write", _vp),
+    ]
+
+
 class Gdn2ScanArgs(ctypes.Structure):
     _fields_ = [
         ("batch", _i64), ("time", _i64), ("heads", _i64), ("key_dim", _i64), ("value_dim", _i64),
@@ -96,6 +108,16 @@ class RelayMergeArgs(ctypes.Structure):
     ]
 
 
+class RelayAttentionArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", _i64), ("heads", _i64), ("time", _i64), ("head_dim", _i64), ("documents", _i64),
+        ("dtype", _i32),
+        ("q", _vp), ("k", _vp), ("v", _vp), ("relay_k", _vp), ("relay_v", _vp),
+        ("doc_id", _vp), ("doc_start", _vp), ("doc_end", _vp),
+        ("o", _vp), ("normalization", _vp),
+    ]
+
+
 # (name, restype, argtypes) for every function in include/dbl_gdn2.h
 EXPORTS = [
     ("dbl_status_string", ctypes.c_char_p, [ctypes.c_int]),
@@ -109,11 +131,13 @@ EXPORTS = [
     ("dbl_gdn_training_scan_backward_workspace_bytes", ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64, _i32]),
     ("dbl_gdn_training_scan_backward", ctypes.c_int,
      [ctypes.POINTER(TrainingScanBackwardArgs), _vp, ctypes.c_size_t, _vp]),
+    ("dbl_gdn2_prologue", ctypes.c_int, [ctypes.POINTER(Gdn2PrologueArgs), _vp]),
     ("dbl_gdn2_scan", ctypes.c_int, [ctypes.POINTER(Gdn2ScanArgs), _vp]),
     ("dbl_relay_merge_workspace_bytes", ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64]),
     ("dbl_relay_merge_decode", ctypes.c_int,
      [ctypes.POINTER(RelayMergeArgs), _vp, ctypes.c_size_t, _vp]),
     ("dbl_relay_merge_decode_noalloc", ctypes.c_int, [ctypes.POINTER(RelayMergeArgs), _vp]),
+    ("dbl_relay_attention_forward", ctypes.c_int, [ctypes.POINTER(RelayAttentionArgs), _vp]),
 ]
 
 RELAY_NOALLOC_SCRATCH_BYTES = 16 << 20  # DBL_RELAY_NOALLOC_SCRATCH_BYTES

@@ -14,6 +14,8 @@ namespace dbl {
 
 // Records the reason for a failure in thread-local storage and returns `status`.
 int fail(int status, const char* fmt, ...);
+// Device address of the library's kernel error word (read and cleared by dbl_device_error).
+int device_error_record(int** out);
 
 // Converts a CUDA error into DBL_ERR_CUDA with a message naming the call site.
 inline int cuda_status(cudaError_t e, const char* what) {

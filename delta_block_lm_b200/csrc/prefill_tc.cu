@@ -864,6 +864,11 @@ int tc_prefill_launch(const dbl_prefill_args* a, const int64_t* qs, const int64_
     return launch_status("gdn2_prefill_tc_kernel");
 }
 
+int device_error_record(int** out) {
+    const cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(out), g_tc_error);
+    return e == cudaSuccess ? DBL_OK : cuda_status(e, "device error record");
+}
+
 }  // namespace dbl
 
 extern "C" int dbl_device_error(int* code) {
@@ -880,5 +885,9 @@ extern "C" int dbl_device_error(int* code) {
         return dbl::fail(DBL_ERR_UNSUPPORTED,
                          "tensor-core prefill: an fp16 MMA operand left fp16 range (inputs far outside unit-norm keys "
                          "and beta in [0, 1]); its outputs are not valid");
+    if (host == 101)
+        return dbl::fail(DBL_ERR_INVALID_ARGUMENT,
+                         "relay attention: a live row's document id lies outside [0, documents); its relay slots "
+                         "were skipped");
     return host ? dbl::fail(DBL_ERR_TIMEOUT, "a kernel gave up a bounded wait (site %d)", host) : DBL_OK;
 }

@@ -7,6 +7,7 @@ calls the C ABI of ``libdbl_gdn2.so`` on the current CUDA stream.  torch is only
 
     gdn_training_scan  <- delta_kernels::gdn_training_scan  (crates/kernels/src/gdn_training_ops.rs:288-333)
     gdn_training_backward <- GdnTrainingOps::gdn_training_backward (gdn_training_ops.rs:95-127)
+    gdn2_prologue      <- the GDN-2 gate and input producer of Mixer::forward_inner (crates/mixers/src/lib.rs:446-528)
     gdn2_scan          <- delta_kernels::gdn2_scan          (crates/kernels/src/ops.rs:251-276)
     gdn2_prefill       <- scalar-gate chunked forward (the BASELINE prefill; chunk.rs:129-250 semantics)
     gdn2_span_transition  hand-off matrix for time-sharded prefill (no reference counterpart)
@@ -159,6 +160,45 @@ def gdn_training_backward(q, k, v, alpha, erase, write, valid, reset, initial, g
                                        _ptr(dw), _ptr(di))
         N.check(lib.dbl_gdn_training_scan_backward(ctypes.byref(a), _ptr(ws), need, _stream(dev)))
     return GdnTrainingGrads(dq, dk, dv, da, de, dw, di)
+
+
+def gdn2_prologue(proj_q, proj_k, proj_v, proj_decay, proj_erase, proj_write, conv_q, conv_k, conv_v,
+                  decay_bias, decay_scale, valid, reset, heads: int, out_dtype=torch.float32):
+    """GDN-2 mixer prologue (lib.rs:446-528): returns (q, k, v, alpha, erase, write) shaped for the
+    scan -- q, k, alpha, erase [B,T,H,K], v, write [B,T,H,V]; q, k, v in ``out_dtype``, gates f32.
+    Projections [B,T,H*K] / [B,T,H*V] (f32 or bf16); conv weights [W,H*K] / [W,H*V]; decay_bias
+    [H*K] (or [H,K]); decay_scale [H]; valid, reset [B,T]."""
+    dev = _require_cuda(proj_q, proj_k, proj_v, proj_decay, proj_erase, proj_write, conv_q, conv_k, conv_v,
+                        decay_bias, decay_scale, valid, reset)
+    B, T, HK = proj_q.shape
+    HV = proj_v.shape[2]
+    if HK % heads or HV % heads:
+        raise ValueError("projection widths must be multiples of the head count")
+    K, V = HK // heads, HV // heads
+    W = conv_q.shape[0]
+    for name, t, shape in (("proj_k", proj_k, (B, T, HK)), ("proj_decay", proj_decay, (B, T, HK)),
+                           ("proj_erase", proj_erase, (B, T, HK)), ("proj_write", proj_write, (B, T, HV)),
+                           ("conv_q", conv_q, (W, HK)), ("conv_k", conv_k, (W, HK)), ("conv_v", conv_v, (W, HV)),
+                           ("valid", valid, (B, T)), ("reset", reset, (B, T))):
+        if tuple(t.shape) != shape:
+            raise ValueError(f"{name} must have shape {list(shape)}, got {list(t.shape)}")
+    if decay_bias.numel() != HK or decay_scale.numel() != heads:
+        raise ValueError("decay_bias needs H*K values and decay_scale H values")
+    in_code = _dtype_code(proj_q)
+    if any(x.dtype != proj_q.dtype for x in (proj_k, proj_v, proj_decay, proj_erase, proj_write)):
+        raise ValueError("the six projections must share a dtype")
+    out_code = N.DBL_BF16 if out_dtype == torch.bfloat16 else N.DBL_F32
+    with torch.cuda.device(dev):
+        pr = [x.contiguous() for x in (proj_q, proj_k, proj_v, proj_decay, proj_erase, proj_write)]
+        fl = [_f32c(x) for x in (conv_q, conv_k, conv_v, decay_bias, decay_scale, valid, reset)]
+        q, k = (torch.empty((B, T, heads, K), device=dev, dtype=out_dtype) for _ in range(2))
+        v = torch.empty((B, T, heads, V), device=dev, dtype=out_dtype)
+        alpha, erase = (torch.empty((B, T, heads, K), device=dev, dtype=torch.float32) for _ in range(2))
+        write = torch.empty((B, T, heads, V), device=dev, dtype=torch.float32)
+        a = N.Gdn2PrologueArgs(B, T, heads, K, V, W, in_code, out_code, *(_ptr(x) for x in pr), *(_ptr(x) for x in fl),
+                               _ptr(q), _ptr(k), _ptr(v), _ptr(alpha), _ptr(erase), _ptr(write))
+        N.check(N.lib().dbl_gdn2_prologue(ctypes.byref(a), _stream(dev)))
+    return q, k, v, alpha, erase, write
 
 
 def gdn2_scan(q, k, v, alpha, erase, write, doc_start, doc_end) -> torch.Tensor:

@@ -62,3 +62,45 @@ def relay_merge_decode(q, prefix_k, prefix_v, own_k, own_v, *, scale: Optional[f
                                                workspace.numel() * workspace.element_size(),
                                                _stream(dev)))
     return out, row_max, row_sum
+
+
+def relay_attention_forward(q, k, v, relay_k, relay_v, doc_id, doc_start, doc_end, *, out=None,
+                            normalization=None):
+    """Reference-layout relay attention (``relay_attention_forward`` / ``run_relay_windowed_attention``,
+    reuse/crates/dre-attention/src/relay_attention_kernel.rs:14-20, :38-130, :311-340).
+
+    q, k, v [B,H,T,64] and relay_k, relay_v [documents,H,16,64], f32 or bf16; doc_id, doc_start,
+    doc_end [B,T] integer (inclusive limits; doc_end < doc_start marks padding).  Query t attends to
+    the keys of [t - 128, t + 128] inside its document and to its document's 16 relay slots, with
+    scores q.k / 8.  Returns (o [B,H,T,64] in the input dtype, normalization [B,H,T,2] f32 =
+    (row maximum, sum of exp(score - maximum))); padding rows give o = 0 and (0, 1).
+    """
+    dev = _require_cuda(q, k, v, relay_k, relay_v, doc_id, doc_start, doc_end, out, normalization)
+    B, H, T, D = q.shape
+    if D != 64:
+        raise ValueError("relay attention: head width must be 64")
+    for name, t in (("k", k), ("v", v)):
+        if tuple(t.shape) != (B, H, T, D):
+            raise ValueError(f"relay attention: {name} must be [B,H,T,64], got {list(t.shape)}")
+    nd = relay_k.shape[0]
+    for name, t in (("relay_k", relay_k), ("relay_v", relay_v)):
+        if tuple(t.shape) != (nd, H, 16, D):
+            raise ValueError(f"relay attention: {name} must be [documents,H,16,64], got {list(t.shape)}")
+    for name, t in (("doc_id", doc_id), ("doc_start", doc_start), ("doc_end", doc_end)):
+        if tuple(t.shape) != (B, T):
+            raise ValueError(f"relay attention: {name} must be [B,T], got {list(t.shape)}")
+    for name, t in (("k", k), ("v", v), ("relay_k", relay_k), ("relay_v", relay_v)):
+        if t.dtype != q.dtype:
+            raise ValueError(f"relay attention: {name} must have the dtype of q")
+    with torch.cuda.device(dev):
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        relay_k, relay_v = relay_k.contiguous(), relay_v.contiguous()
+        di, ds, de = (x.to(torch.int32).contiguous() for x in (doc_id, doc_start, doc_end))
+        if out is None:
+            out = torch.empty((B, H, T, D), device=dev, dtype=q.dtype)
+        if normalization is None:
+            normalization = torch.empty((B, H, T, 2), device=dev, dtype=torch.float32)
+        a = N.RelayAttentionArgs(B, H, T, D, nd, _dtype_code(q), _ptr(q), _ptr(k), _ptr(v), _ptr(relay_k),
+                                 _ptr(relay_v), _ptr(di), _ptr(ds), _ptr(de), _ptr(out), _ptr(normalization))
+        N.check(N.lib().dbl_relay_attention_forward(ctypes.byref(a), _stream(dev)))
+    return out, normalization

@@ -54,10 +54,12 @@ int dbl_abi_version(void);
 /* Every wait inside the tensor-core kernels is bounded; one that gives up records a site code on
  * the current device and lets the kernel run to completion (its outputs are then undefined).  The
  * tensor-core prefill also records code 100 when one of its fp16 MMA operands left fp16 range
- * (inputs far outside unit-norm keys and beta in [0, 1]; its outputs are then not valid).
+ * (inputs far outside unit-norm keys and beta in [0, 1]; its outputs are then not valid), and
+ * relay attention records code 101 when a live row's document id lies outside [0, documents).
  * This call synchronises with the device, stores the code in *code (0 = none; code may be NULL),
- * clears the record and returns DBL_OK, DBL_ERR_UNSUPPORTED (code 100) or DBL_ERR_TIMEOUT.  No
- * counterpart in the reference, whose kernels have no bounded waits or range checks. */
+ * clears the record and returns DBL_OK, DBL_ERR_UNSUPPORTED (code 100), DBL_ERR_INVALID_ARGUMENT
+ * (code 101) or DBL_ERR_TIMEOUT.  No counterpart in the reference, whose kernels have no bounded
+ * waits or range checks. */
 int dbl_device_error(int *code);
 
 /* =============================================================================================
@@ -180,6 +182,32 @@ size_t dbl_gdn_training_scan_backward_workspace_bytes(int64_t batch, int64_t tim
 int dbl_gdn_training_scan_backward(const dbl_training_scan_backward_args *args, void *workspace,
                                    size_t workspace_bytes, dbl_stream_t stream);
 
+/* GDN-2 mixer prologue: what Mixer::forward_inner computes between the projections and the scan
+ * (crates/mixers/src/lib.rs:446-528, MixerKind::Gdn2), fused into one memory-bound pass:
+ *   q, k = l2(silu(conv(proj_q|proj_k))),  v = silu(conv(proj_v)),
+ *   alpha = exp(-softplus(proj_decay + decay_bias[h,k]) exp(decay_scale[h])),
+ *   erase = sigmoid(proj_erase),  write = sigmoid(proj_write).
+ * conv is the depthwise causal convolution kept inside one document (conv.rs:7-45; documents =
+ * cumsum(reset * valid) over time), l2 is x / sqrt(sum x^2 + 1e-6) per head row (norm.rs mode 0),
+ * softplus switches to x above 20 (decay.rs:13-20).  Projections [B,T,H*K] (q, k, decay, erase)
+ * and [B,T,H*V] (v, write) in in_dtype; conv weights [W,H*K] / [W,H*V] f32 (W <= 8);
+ * decay_bias [H*K], decay_scale [H], valid / reset [B,T] f32.  Outputs q, k [B,T,H,K] and
+ * v [B,T,H,V] in out_dtype; alpha, erase [B,T,H,K] and write [B,T,H,V] f32.  K, V <= 256; all
+ * arrays contiguous. */
+typedef struct {
+    int64_t batch, time, heads, key_dim, value_dim, conv_width;
+    int32_t in_dtype, out_dtype;
+    const void *proj_q, *proj_k, *proj_v;
+    const void *proj_decay, *proj_erase, *proj_write;
+    const float *conv_q, *conv_k, *conv_v;
+    const float *decay_bias, *decay_scale;
+    const float *valid, *reset;
+    void *q, *k, *v;
+    float *alpha, *erase, *write;
+} dbl_gdn2_prologue_args;
+
+int dbl_gdn2_prologue(const dbl_gdn2_prologue_args *args, dbl_stream_t stream);
+
 /* Mirrors delta_kernels::gdn2_scan(q, k, v, alpha, erase, write, doc_start, doc_end) -> output
  * (crates/kernels/src/ops.rs:251-276, kernels gdn2.rs:23-283; oracle gdn2_reference.rs:87-105):
  * inclusive int32 document limits [B,T]; `end < start` marks padding (output 0, state kept),
@@ -244,6 +272,32 @@ int dbl_relay_merge_decode(const dbl_relay_merge_args *args, void *workspace,
  *     e.g. on two streams, race on it. */
 #define DBL_RELAY_NOALLOC_SCRATCH_BYTES (16u << 20)
 int dbl_relay_merge_decode_noalloc(const dbl_relay_merge_args *args, dbl_stream_t stream);
+
+/* =============================================================================================
+ * 5. Relay attention in the reference layout (training / prefill forward).
+ *
+ * Replaces RelayAttentionKernelOps::relay_attention_forward and run_relay_windowed_attention
+ * (reuse/crates/dre-attention/src/relay_attention_kernel.rs:14-20, :311-340; kernel
+ * relay_forward_kernel :38-130): query t of row b attends, in one softmax, to the keys of [t - 128,
+ * t + 128] inside its inclusive document limits [doc_start, doc_end] and to the 16 relay slots of
+ * its document doc_id; scores are q.k / 8.  q, k, v [B,H,T,64] and relay_k, relay_v
+ * [documents,H,16,64] in dtype (f32 or bf16); doc_* [B,T] int32; o [B,H,T,64] in dtype;
+ * normalization [B,H,T,2] f32 = (row maximum, sum of exp(score - maximum)).  A padding row
+ * (doc_end < doc_start) writes o = 0 and (0, 1), as the reference.  head_dim must be 64 (the
+ * reference asserts it).  All arrays contiguous and 16-byte aligned.  The forward's unused layout
+ * tensors (doc_row, relay_start, relay_end) are not taken.  A live row whose doc_id is outside
+ * [0, documents) gets no relay slots and records device error 101 (dbl_device_error). */
+typedef struct {
+    int64_t batch, heads, time, head_dim, documents;
+    int32_t dtype;
+    const void *q, *k, *v;
+    const void *relay_k, *relay_v;
+    const int32_t *doc_id, *doc_start, *doc_end;
+    void *o;
+    float *normalization;
+} dbl_relay_attention_args;
+
+int dbl_relay_attention_forward(const dbl_relay_attention_args *args, dbl_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -18,8 +18,10 @@ STRUCTS = {
     "dbl_decode_args": N.DecodeArgs,
     "dbl_training_scan_args": N.TrainingScanArgs,
     "dbl_training_scan_backward_args": N.TrainingScanBackwardArgs,
+    "dbl_gdn2_prologue_args": N.Gdn2PrologueArgs,
     "dbl_gdn2_scan_args": N.Gdn2ScanArgs,
     "dbl_relay_merge_args": N.RelayMergeArgs,
+    "dbl_relay_attention_args": N.RelayAttentionArgs,
 }
 
 

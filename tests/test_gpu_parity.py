@@ -4,6 +4,7 @@ Tolerances: f32 paths at the reference's 2e-5 + 3e-4|ref| (checks.rs:73-74) wher
 checks f32 against f64, and the north-star bounds elsewhere (``rel_err``: 2e-3 for f32, 2e-2 for
 bf16 inputs; inputs are rounded to bf16 before the oracle runs, so only kernel rounding counts).
 """
+import ctypes
 import os
 
 import numpy as np
@@ -11,6 +12,7 @@ import pytest
 import torch
 
 import delta_block_lm_b200 as dbl
+from delta_block_lm_b200 import _native as N
 from fixtures import (TOL_BF16, TOL_F32, baseline_inputs, bf16_round, chunk_test_fixture, edge_edits,
                       edge_initial, ref_close, rel_err, sinusoid_fixture, splitmix_tokens)
 from oracle import oracle as O
@@ -316,3 +318,152 @@ def test_training_backward_matches_oracle(cuda, native_lib, K, V, chunk):
         assert rel_err(g, r) < TOL_F32, (name, rel_err(g, r))
     for name in names[:6]:
         assert np.all(getattr(got, name).cpu().numpy()[~valid] == 0.0), name
+
+
+# ----------------------------------------------------------------------- mixer prologue
+@pytest.mark.parametrize("B,T,H,K,V,W,dtype", [(2, 37, 3, 32, 64, 4, torch.float32),
+                                                (1, 50, 2, 128, 128, 4, torch.bfloat16),
+                                                (2, 9, 2, 40, 72, 1, torch.float32),
+                                                (1, 20, 2, 36, 20, 3, torch.bfloat16),
+                                                (1, 70, 1, 256, 256, 8, torch.float32)])
+def test_gdn2_prologue_matches_oracle(cuda, native_lib, B, T, H, K, V, W, dtype):
+    # lib.rs:446-528 (MixerKind::Gdn2): conv + silu + l2 for q, k; conv + silu for v; decay and
+    # sigmoid gates -- against the f64 prologue oracle, with padding and resets in the documents.
+    rng = np.random.default_rng(T + K)
+    r = lambda *s: rng.standard_normal(s)  # noqa: E731
+    proj = [r(B, T, H * K), r(B, T, H * K), r(B, T, H * V), 3 * r(B, T, H * K), r(B, T, H * K), r(B, T, H * V)]
+    proj[3][0, 0, :3] = [30.0, 21.0, -25.0]  # both sides of the softplus threshold
+    conv = [0.3 * r(W, H * K), 0.3 * r(W, H * K), 0.3 * r(W, H * V)]
+    bias, scale = 0.5 * r(H * K), 0.3 * r(H)
+    valid = (rng.random((B, T)) > 0.15).astype(np.float32)
+    reset = (rng.random((B, T)) > 0.8).astype(np.float32)
+    if dtype == torch.bfloat16:
+        proj = [bf16_round(x) for x in proj]
+    d = lambda x, dt=torch.float32: torch.as_tensor(np.asarray(x, np.float32), device=cuda).to(dt)  # noqa: E731
+    got = dbl.gdn2_prologue(*(d(x, dtype) for x in proj), *(d(x) for x in conv), d(bias), d(scale), d(valid),
+                            d(reset), heads=H, out_dtype=dtype)
+    torch.cuda.synchronize()
+    ref = O.gdn2_prologue(*proj, *conv, bias, scale, valid, reset, heads=H)
+    # gates (f32, in [0, 1]): within 2e-6 absolute of the f64 oracle; q, k, v within 2e-5 relative
+    # (elementwise, against |e| + rms) in f32, within bf16 rounding otherwise
+    for name, g, e in zip(("q", "k", "v", "alpha", "erase", "write"), got, ref):
+        g = g.float().cpu().numpy()
+        if name in ("alpha", "erase", "write"):
+            assert np.abs(g - e).max() < 2e-6, (name, np.abs(g - e).max())
+        else:
+            tol = TOL_BF16 if dtype == torch.bfloat16 else 2e-5
+            assert rel_err(g, e) < tol, (name, rel_err(g, e))
+
+
+# ----------------------------------------------------------------- reference-layout relay attention
+def _packed_layout(docs_per_row, tokens):
+    """Packed documents (dre-core lib.rs:105-175): ids across rows, inclusive limits; padding
+    tokens have start = position, end = position - 1, id -1."""
+    B = len(docs_per_row)
+    di = np.full((B, tokens), -1, np.int32)
+    ds = np.tile(np.arange(tokens, dtype=np.int32), (B, 1))
+    de = ds - 1
+    doc = 0
+    for b, docs in enumerate(docs_per_row):
+        first = 0
+        for n in docs:
+            di[b, first:first + n], ds[b, first:first + n], de[b, first:first + n] = doc, first, first + n - 1
+            first += n
+            doc += 1
+    return di, ds, de, doc
+
+
+def _relay_inputs(docs_per_row, tokens, heads, seed, dtype):
+    rng = np.random.default_rng(seed)
+    di, ds, de, nd = _packed_layout(docs_per_row, tokens)
+    B = len(docs_per_row)
+    q, k, v = (rng.standard_normal((B, heads, tokens, 64)) for _ in range(3))
+    rk, rv = (rng.standard_normal((nd, heads, 16, 64)) for _ in range(2))
+    if dtype == torch.bfloat16:
+        q, k, v, rk, rv = (bf16_round(x) for x in (q, k, v, rk, rv))
+    return q, k, v, rk, rv, di, ds, de
+
+
+def _relay_run(cuda, dtype, q, k, v, rk, rv, di, ds, de):
+    d = lambda x: torch.as_tensor(np.asarray(x, np.float32), device=cuda).to(dtype)  # noqa: E731
+    i = lambda x: torch.as_tensor(x, device=cuda)  # noqa: E731
+    o, norm = dbl.relay_attention_forward(d(q), d(k), d(v), d(rk), d(rv), i(di), i(ds), i(de))
+    torch.cuda.synchronize()
+    assert native_device_ok()
+    return o.float().cpu().numpy(), norm.cpu().numpy()
+
+
+def native_device_ok():
+    code = ctypes.c_int(0)
+    return N.lib().dbl_device_error(ctypes.byref(code)) == 0 and code.value == 0
+
+
+def _relay_check(o, norm, eo, en, dtype):
+    # f32: the reference's own tolerance, 2e-5 + 1e-4 |e| (relay.rs:166-171); bf16: P enters the
+    # tensor cores as bf16, so o is within bf16 rounding of the f64 oracle
+    if dtype == torch.float32:
+        np.testing.assert_allclose(o, eo, rtol=1e-4, atol=2e-5)
+        np.testing.assert_allclose(norm, en, rtol=1e-4, atol=2e-5)
+    else:
+        assert rel_err(o, eo) < 1e-2, rel_err(o, eo)
+        np.testing.assert_allclose(norm[..., 0], en[..., 0], rtol=1e-5, atol=1e-4)
+        np.testing.assert_allclose(norm[..., 1], en[..., 1], rtol=1e-4)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("docs,tokens,heads", [([[2, 3]], 6, 1),               # relay_tests.rs:94-140 layout
+                                               ([[100, 57, 80], [300]], 300, 3),  # padding tails, 3 tiles
+                                               ([[258]], 258, 2),               # window edges at radius 128
+                                               ([[2] * 512], 1024, 2)])         # relay_tests.rs:244: 512 documents
+def test_relay_attention_matches_oracle(cuda, native_lib, dtype, docs, tokens, heads):
+    q, k, v, rk, rv, di, ds, de = _relay_inputs(docs, tokens, heads, tokens + heads, dtype)
+    o, norm = _relay_run(cuda, dtype, q, k, v, rk, rv, di, ds, de)
+    eo, en = O.relay_window(q, k, v, rk, rv, di, ds, de)
+    _relay_check(o, norm, eo, en, dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_relay_attention_extreme_scores(cuda, native_lib, dtype):
+    # relay_tests.rs:12-93: scores near -8e32; one effective key gives exactly its value and (m, 1);
+    # eighteen equal keys give the sum 18
+    di, ds, de, _ = _packed_layout([[1]], 2)
+    q = np.full((1, 1, 2, 64), 1e16)
+    k = np.full((1, 1, 2, 64), -1e16)
+    v = np.array([i - 32.0 if i < 64 else 17.0 for i in range(128)]).reshape(1, 1, 2, 64)
+    o, norm = _relay_run(cuda, dtype, q, k, v, np.full((1, 1, 16, 64), -2e16), np.full((1, 1, 16, 64), 23.0),
+                         di, ds, de)
+    assert np.isfinite(norm[0, 0, 0, 0]) and norm[0, 0, 0, 0] < -1e30 and norm[0, 0, 0, 1] == 1.0
+    assert list(norm[0, 0, 1]) == [0.0, 1.0]
+    assert np.array_equal(o[0, 0, 0], v[0, 0, 0]) and np.all(o[0, 0, 1] == 0.0)
+    di, ds, de, _ = _packed_layout([[2]], 2)
+    o, norm = _relay_run(cuda, dtype, q, k, np.zeros_like(v), np.full((1, 1, 16, 64), -1e16),
+                         np.zeros((1, 1, 16, 64)), di, ds, de)
+    assert np.all(np.isfinite(norm[..., 0])) and np.all(norm[..., 0] < -1e30) and np.all(norm[..., 1] == 18.0)
+    assert np.all(o == 0.0)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_relay_attention_ignores_nan_padding(cuda, native_lib, dtype):
+    # relay.rs:173-210: NaN in padding tokens (and in padding documents' relay slots) leaves the
+    # live outputs unchanged and finite
+    docs, tokens = [[90, 60], [200]], 260
+    q, k, v, rk, rv, di, ds, de = _relay_inputs(docs, tokens, 2, 5, dtype)
+    clean = _relay_run(cuda, dtype, q, k, v, rk, rv, di, ds, de)
+    pad = de < ds
+    q2, k2, v2 = (x.copy() for x in (q, k, v))
+    for x in (q2, k2, v2):
+        x.transpose(0, 2, 1, 3)[pad] = np.nan
+    rk2 = np.concatenate([rk, np.full((2,) + rk.shape[1:], np.nan)])
+    rv2 = np.concatenate([rv, np.full((2,) + rv.shape[1:], np.nan)])
+    dirty = _relay_run(cuda, dtype, q2, k2, v2, rk2, rv2, di, ds, de)
+    assert np.all(np.isfinite(dirty[0])) and np.all(np.isfinite(dirty[1]))
+    np.testing.assert_array_equal(dirty[0], clean[0])
+    np.testing.assert_array_equal(dirty[1], clean[1])
+
+
+def test_relay_attention_rejects_bad_shapes(cuda, native_lib):
+    q = torch.zeros(1, 1, 4, 32, device=cuda)
+    ids = torch.zeros(1, 4, dtype=torch.int32, device=cuda)
+    with pytest.raises(ValueError):
+        dbl.relay_attention_forward(q, q, q, torch.zeros(1, 1, 16, 32, device=cuda), torch.zeros(1, 1, 16, 32, device=cuda),
+                                    ids, ids, ids)

@@ -284,3 +284,110 @@ def test_training_backward_matches_finite_differences():
     # padding tokens get no gradient
     for g in grads[:6]:
         assert np.all(g[0, 4] == 0.0)
+
+
+@pytest.mark.parametrize("t,c,width", [(1, 3, 4), (2, 35, 4), (7, 3, 4), (17, 128, 4), (19, 256, 4), (7, 35, 1)])
+def test_causal_conv_matches_reference_fixture(t, c, width):
+    # The reference's convolution check (crates/mixers/src/convolution_checks.rs:55-175) restated:
+    # its sin fixtures, padding/reset pattern and explicit f64 loop over lags and document masks.
+    b = 2
+    x = np.array([np.sin((i * 17 + 3) * 0.013) for i in range(b * t * c)], np.float32).reshape(b, t, c)
+    w = np.array([0.0 if i % 7 == 0 else np.sin((i + 3) * np.float32(0.17)) * 0.1 for i in range(width * c)],
+                 np.float32).reshape(width, c)
+    valid = np.array([0.0 if (i % 7 == 3 or i % t == t - 1) else 1.0 for i in range(b * t)], np.float32).reshape(b, t)
+    reset = np.array([1.0 if (i % t in (0, 2, 5)) else 0.0 for i in range(b * t)], np.float32).reshape(b, t)
+    docs = np.cumsum(valid * reset, axis=1)
+    y = np.zeros((b, t, c))
+    for row in range(b):
+        for dest in range(t):
+            for lag in range(min(width, dest + 1)):
+                src = dest - lag
+                m = float(valid[row, src]) * float(valid[row, dest]) if docs[row, src] == docs[row, dest] else 0.0
+                y[row, dest] += x[row, src].astype(np.float64) * w[lag].astype(np.float64) * m
+    assert np.max(np.abs(O.causal_conv(x, w, valid, reset) - y)) < 1e-12
+
+
+def test_prologue_gate_and_norm_known_values():
+    # softplus threshold 20 (decay.rs:13-20): above it alpha = exp(-(x + b) e^s) exactly
+    z = np.array([25.0, 20.5, -3.0, 0.0])
+    sp = O.softplus20(z)
+    assert sp[0] == 25.0 and sp[1] == 20.5
+    assert abs(sp[2] - np.log1p(np.exp(-3.0))) < 1e-15 and abs(sp[3] - np.log(2.0)) < 1e-15
+    # L2 rows (normalization.rs:21-25): unit norm up to eps, a zero row stays zero
+    x = np.array([[3.0, 4.0], [0.0, 0.0]])
+    n = O.l2_rows(x)
+    assert abs(np.linalg.norm(n[0]) - 5.0 / np.sqrt(25.0 + 1e-6)) < 1e-15 and np.all(n[1] == 0.0)
+
+
+def packed_layout(docs_per_row, tokens):
+    """doc_id / doc_start / doc_end [B,T] of a packed batch (dre-core lib.rs:105-113, 145-175):
+    documents numbered across rows, inclusive limits; a padding token has start = position,
+    end = position - 1 and document id -1."""
+    B = len(docs_per_row)
+    di = np.full((B, tokens), -1, np.int32)
+    ds = np.tile(np.arange(tokens, dtype=np.int32), (B, 1))
+    de = ds - 1
+    doc = 0
+    for b, docs in enumerate(docs_per_row):
+        first = 0
+        for n in docs:
+            di[b, first:first + n], ds[b, first:first + n], de[b, first:first + n] = doc, first, first + n - 1
+            first += n
+            doc += 1
+    return di, ds, de
+
+
+def test_relay_window_extreme_single_effective_key():
+    # relay_tests.rs:12-47: q = 1e16, k = -1e16 (source score -8e32), relay keys -2e16 (-1.6e33):
+    # every relay weight underflows, the output is exactly the one source value and the statistic
+    # is (a finite maximum below -1e30, 1); the padding row gives (0, 1) and zeros.
+    di, ds, de = packed_layout([[1]], 2)
+    q = np.full((1, 1, 2, 64), 1e16)
+    k = np.full((1, 1, 2, 64), -1e16)
+    v = np.array([i - 32.0 if i < 64 else 17.0 for i in range(128)]).reshape(1, 1, 2, 64)
+    rk, rv = np.full((1, 1, 16, 64), -2e16), np.full((1, 1, 16, 64), 23.0)
+    o, norm = O.relay_window(q, k, v, rk, rv, di, ds, de)
+    assert np.isfinite(norm[0, 0, 0, 0]) and norm[0, 0, 0, 0] < -1e30
+    assert norm[0, 0, 0, 1] == 1.0
+    assert list(norm[0, 0, 1]) == [0.0, 1.0]
+    assert np.array_equal(o[0, 0, 0], v[0, 0, 0]) and np.all(o[0, 0, 1] == 0.0)
+
+
+def test_relay_window_extreme_equal_keys():
+    # relay_tests.rs:51-93: two source keys and sixteen relay keys with identical scores near -8e32:
+    # the sum is exactly 18 and the output 0 for zero values.
+    di, ds, de = packed_layout([[2]], 2)
+    q = np.full((1, 1, 2, 64), 1e16)
+    k = np.full((1, 1, 2, 64), -1e16)
+    rk = np.full((1, 1, 16, 64), -1e16)
+    z = np.zeros((1, 1, 2, 64))
+    o, norm = O.relay_window(q, k, z, rk, np.zeros((1, 1, 16, 64)), di, ds, de)
+    for row in norm[0, 0]:
+        assert np.isfinite(row[0]) and row[0] < -1e30 and row[1] == 18.0
+    assert np.all(o == 0.0)
+
+
+def test_relay_window_matches_dense_masked_attention():
+    # relay_tests.rs:94-140: tokens 6, documents [2, 3] packed; a dense softmax over
+    # [window keys ; all relay slots] with the reference test's mask (other document or more than
+    # 128 tokens away; relay slot of another document) equals the windowed relay attention.
+    tokens, documents = 6, 2
+    make = lambda n, seed: np.sin(((np.arange(n) * 31 + seed).astype(np.float32) * np.float32(0.0021))  # noqa: E731
+                                  .astype(np.float32)).astype(np.float64)
+    q, k, v = (make(tokens * 64, s).reshape(1, 1, tokens, 64) for s in (1, 2, 3))
+    rk, rv = (make(documents * 16 * 64, s).reshape(documents, 1, 16, 64) for s in (4, 5))
+    di, ds, de = packed_layout([[2, 3]], tokens)
+    o, norm = O.relay_window(q, k, v, rk, rv, di, ds, de)
+    docs = [0, 0, 1, 1, 1, -1]
+    dk = np.concatenate([k[0, 0], rk.reshape(documents * 16, 64)])
+    dv = np.concatenate([v[0, 0], rv.reshape(documents * 16, 64)])
+    for t in range(tokens):
+        if docs[t] < 0:
+            assert np.all(o[0, 0, t] == 0.0) and list(norm[0, 0, t]) == [0.0, 1.0]
+            continue
+        keep = np.array([(docs[j] == docs[t] and abs(t - j) <= 128) if j < tokens else (j - tokens) // 16 == docs[t]
+                         for j in range(tokens + documents * 16)])
+        s = dk[keep] @ q[0, 0, t] * 0.125
+        w = np.exp(s - s.max())
+        np.testing.assert_allclose(o[0, 0, t], w @ dv[keep] / w.sum(), rtol=1e-12, atol=1e-14)
+        np.testing.assert_allclose(norm[0, 0, t], [s.max(), w.sum()], rtol=1e-12)
