@@ -571,6 +571,71 @@ def bench_prologue(torch, args, dev):
             "gpu_launches": reps}
 
 
+def bench_relay_attn(torch, args, dev, with_cpu=True):
+    """Reference-layout relay attention (relay_attention_kernel.rs:38-130: +-128 document window
+    plus 16 relay slots, head width 64) at B8/H16/T4096 with 1024-token documents, bf16 on the
+    tensor cores; the f32 CUDA-core path and the f64 CPU oracle on a bounded sample for context."""
+    import delta_block_lm_b200 as dbl
+
+    b, h, t, dl = 8, 16, 4096, 1024
+    nd = b * t // dl
+    g = torch.Generator(device=dev)
+    g.manual_seed(17)
+    rn = lambda *s: torch.randn(s, device=dev, generator=g)  # noqa: E731
+    pos = torch.arange(t, device=dev, dtype=torch.int32)
+    ds = (pos // dl * dl).expand(b, t).contiguous()
+    de = (ds + dl - 1).contiguous()
+    di = (torch.arange(b, device=dev, dtype=torch.int32)[:, None] * (t // dl) + pos // dl).contiguous()
+    x32 = [rn(b, h, t, 64) for _ in range(3)] + [rn(nd, h, 16, 64) for _ in range(2)]
+    x16 = [x.to(torch.bfloat16) for x in x32]
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn, reps=20):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / reps
+
+    ms = timed(lambda: dbl.relay_attention_forward(*x16, di, ds, de))
+    ms32 = timed(lambda: dbl.relay_attention_forward(*x32, di, ds, de), reps=5)
+    hbm, _, src = peaks()
+    # per query row: q, k, v read and o written (64 bf16 each) and the f32 statistic pair;
+    # plus the relay slots once per (document, head)
+    alg = b * h * t * (4 * 64 * 2 + 8) + 2 * nd * h * 16 * 64 * 2
+    gbs = alg / (ms / 1e3) / 1e9
+    # in-window keys per query (document edges clip the +-128 window) for the FLOP count
+    win = sum(min(i + 128, dl - 1) - max(i - 128, 0) + 1 for i in range(dl)) / dl
+    flops = b * h * t * (win + 16) * 64 * 4
+    line = {"metric": "relay attention (reference layout) Mtok/s", "value": b * t / (ms / 1e3) / 1e6,
+            "unit": "Mtok/s", "ms_per_step": ms, "n_gpus": 1, "higher_is_better": True, "dtype": "bf16",
+            "data": "synthetic (seeded normal q, k, v and relay slots)",
+            "config": {"workload": f"B{b}/H{h}/T{t}/hd64, documents of {dl} tokens, 16 relay slots, radius 128",
+                       "f32_ms": ms32, "tflops_bf16": flops / (ms / 1e3) / 1e12},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                         "peak_source": src, "algorithmic_bytes_per_launch": alg},
+            "gpu_launches": 20 + 5}
+    if with_cpu:
+        sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+        from oracle import oracle as O
+        import numpy as np
+        ts = 1024
+        sel = [x[:1, :1, :ts].float().cpu().numpy().astype(np.float64) for x in x32[:3]]
+        rel = [x[:1, :1].float().cpu().numpy().astype(np.float64) for x in x32[3:]]
+        c0 = time.perf_counter()
+        O.relay_window(*sel, *rel, di[:1, :ts].cpu().numpy(), ds[:1, :ts].cpu().numpy(), de[:1, :ts].cpu().numpy())
+        sec = time.perf_counter() - c0
+        line["cpu_baseline"] = {"value": ts / sec / 1e6, "unit": "Mtok/s (one head)", "cores": 1, "kind": "port",
+                                "sample": f"B1/H1/T{ts}, one document, f64 C restatement of relay_forward_kernel, "
+                                          f"{sec:.2f} s"}
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -579,10 +644,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true", help="skip the decode / relay lines")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["prefill", "long", "decode", "relay", "backward", "prologue"], default="prefill",
+    ap.add_argument("--workload", choices=["prefill", "long", "decode", "relay", "backward", "prologue", "relay_attn"],
+                    default="prefill",
                     help="prefill: config 1 (the headline, weak-scaled); long: config 4 (time-sharded); "
                          "decode: config 2 alone; relay: config 3 alone; backward: the fused scan's "
-                         "backward at the reference's training shape; prologue: the mixer prologue (1 GPU)")
+                         "backward at the reference's training shape; prologue: the mixer prologue; "
+                         "relay_attn: reference-layout relay attention (1 GPU)")
     ap.add_argument("--long-tokens", type=int, default=131072)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -615,6 +682,11 @@ def main():
         if world > 1:
             raise SystemExit("--workload prologue runs on one GPU")
         print(json.dumps(bench_prologue(torch, args, dev)), flush=True)
+        return 0
+    if args.workload == "relay_attn":
+        if world > 1:
+            raise SystemExit("--workload relay_attn runs on one GPU")
+        print(json.dumps(bench_relay_attn(torch, args, dev, with_cpu=not args.no_cpu_baseline)), flush=True)
         return 0
     if args.workload == "backward":
         if world > 1:

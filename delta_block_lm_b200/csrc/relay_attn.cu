@@ -14,13 +14,17 @@
 //     zero-filled by the copy, and the K / V rows of padding tokens are zeroed before use (the
 //     reference never reads them, and a NaN there must not reach 0 * NaN in the P V product);
 //   * S = Q K^T (M 128, N 3 x 128, K 64) accumulates in TMEM columns [0, 384);
-//   * thread i owns query row i (TMEM lane i): it reads its row's 257 window columns twice (the
-//     exact row maximum, then p = exp(s - max) and the sum), adds its 16 relay scores (computed on
-//     the CUDA cores while the copies land: a row's relay slots depend on its own document, so
-//     the tile has no common relay operand), and writes P [128 x 384] as bf16 in the swizzled
-//     K-major layout, zero outside the window;
-//   * O = P V (M 128, N 64, K 384, V read MN-major) accumulates in TMEM columns [384, 448);
-//   * the epilogue adds the relay values sum_s p_s rv_s, divides by the sum and stores.
+//   * the relay slots of the tile's documents (up to 8 distinct documents, gathered by TMA) give
+//     S_relay = Q RK^T (N = 16 per document) in TMEM columns [384, 384 + 16 J);
+//   * the four warps that share TMEM lane quarter qd (rows 32 qd ..) split the 288 band columns
+//     their rows can reach into chunks of 16 and take the exact row maximum and then p = exp(s -
+//     max) and the sum in two passes, exchanging per-row partials through shared memory; column
+//     group 0 adds the row's own document's relay scores;
+//   * after a barrier that closes every read of S, P (bf16 pairs, zero outside the window and
+//     outside the row's document group) overwrites S in TMEM, and O = P V + P_relay RV (A from
+//     TMEM, V read MN-major) accumulates in TMEM columns [192, 256);
+//   * the epilogue divides by the sum and stores, each column group 16 output channels.
+// A tile with more than 8 documents computes its relay scores and values on the CUDA cores.
 // f32 runs on the CUDA cores with the reference's online-softmax order: four lanes per query,
 // 16 channels each, scores reduced by two shuffles.
 #include <cuda_bf16.h>
@@ -37,14 +41,23 @@ constexpr float SCALE = 0.125f;
 // ------------------------------------------------------------------------------ tensor cores
 constexpr int TQ = 128;                 // queries per CTA = TMEM lanes
 constexpr int KB = TQ + 2 * RADIUS;     // 384 band keys
-constexpr int NTH = 128;
-constexpr uint32_t OFF_Q = 0;           // [128][128 B]
-constexpr uint32_t OFF_K = 16384;       // 3 x [128][128 B]
-constexpr uint32_t OFF_V = OFF_K + 49152;
-constexpr uint32_t OFF_P = OFF_V + 49152;  // 6 x [128 rows][128 B]: keys 64 a .. 64 a + 63
-constexpr uint32_t OFF_BAR = OFF_P + 98304;
+constexpr int NTH = 512;                // 16 warps: lane quarter = warp % 4, column group = warp / 4
+constexpr int JMAX = 8;                 // relay documents per tile on the tensor cores
+constexpr int EMPTY_DOC = -1;
+constexpr uint32_t OFF_Q = 0;                 // [128][128 B]
+constexpr uint32_t OFF_K = 16384;             // 3 x [128][128 B]
+constexpr uint32_t OFF_V = OFF_K + 49152;     // 3 x [128][128 B]
+constexpr uint32_t OFF_RK = OFF_V + 49152;    // JMAX x [16][128 B]: relay keys of the tile's documents
+constexpr uint32_t OFF_RV = OFF_RK + 16384;   // JMAX x [16][128 B]
+constexpr uint32_t OFF_RED = OFF_RV + 16384;  // f32 [2][4][128]: per-group row maxima and sums
+constexpr uint32_t OFF_ROW = OFF_RED + 4096;  // int4 [128]: window columns, relay group, document
+constexpr uint32_t OFF_PR = OFF_ROW + 2048;   // f32 [128][16]: relay weights (CUDA-core relay)
+constexpr uint32_t OFF_DOC = OFF_PR + 8192;   // int [JMAX] documents, int overflow
+constexpr uint32_t OFF_BAR = OFF_DOC + 64;
 constexpr uint32_t SMEM_TC = OFF_BAR + 64 + 1024;  // + alignment slack
-constexpr uint32_t TM_O = 384;
+// TMEM columns: S of the band [0, 384) and of the relay slots [384, 384 + 16 J); once the softmax
+// has read them, P of the band (bf16 pairs) [0, 192), O [192, 256), P of the relay slots [256, 256 + 8 J)
+constexpr uint32_t TM_SR = 384, TM_O = 192, TM_PR = 256;
 constexpr uint32_t IDESC_S = umma_idesc_bf16(128, 128, false);
 constexpr uint32_t IDESC_O = umma_idesc_bf16(128, 64, true);
 constexpr int kRelayDocError = 101;  // a live row's doc_id outside [0, documents)
@@ -59,18 +72,48 @@ struct RelayParams {
 };
 
 __device__ __forceinline__ uint64_t kdesc(uint32_t saddr) { return umma_sdesc_sw128(saddr, 16, 1024); }
+__device__ __forceinline__ uint64_t mndesc(uint32_t saddr) { return umma_sdesc_sw128(saddr, 16384, 1024); }
+
+// dot of a bf16 row of 64 (eight 16-byte words already in registers) with a bf16 row in memory
+__device__ __forceinline__ float dot64(const uint4 (&qv)[8], const __nv_bfloat16* row) {
+    const uint4* kg = reinterpret_cast<const uint4*>(row);
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint4 kv = __ldg(kg + i);
+        acc = fmaf(bf16_lo(qv[i].x), bf16_lo(kv.x), acc);
+        acc = fmaf(bf16_hi(qv[i].x), bf16_hi(kv.x), acc);
+        acc = fmaf(bf16_lo(qv[i].y), bf16_lo(kv.y), acc);
+        acc = fmaf(bf16_hi(qv[i].y), bf16_hi(kv.y), acc);
+        acc = fmaf(bf16_lo(qv[i].z), bf16_lo(kv.z), acc);
+        acc = fmaf(bf16_hi(qv[i].z), bf16_hi(kv.z), acc);
+        acc = fmaf(bf16_lo(qv[i].w), bf16_lo(kv.w), acc);
+        acc = fmaf(bf16_hi(qv[i].w), bf16_hi(kv.w), acc);
+    }
+    return acc;
+}
 
 __global__ void __launch_bounds__(NTH, 1)
     relay_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                         const __grid_constant__ CUtensorMap tm_v, const RelayParams p) {
+                         const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_rk,
+                         const __grid_constant__ CUtensorMap tm_rv, const RelayParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float* smax = reinterpret_cast<float*>(sm + OFF_RED);  // [4][128]
+    float* ssum = smax + 512;                              // [4][128]
+    int4* srow = reinterpret_cast<int4*>(sm + OFF_ROW);
+    float* spr = reinterpret_cast<float*>(sm + OFF_PR);
+    int* sdocs = reinterpret_cast<int*>(sm + OFF_DOC);
+    int* sover = sdocs + JMAX;
     uint64_t* bar_ld = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
-    uint64_t* bar_s = bar_ld + 1;
-    uint64_t* bar_o = bar_ld + 2;
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_ld + 3);
+    uint64_t* bar_rl = bar_ld + 1;
+    uint64_t* bar_s = bar_ld + 2;
+    uint64_t* bar_o = bar_ld + 3;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_ld + 4);
     int* serr = reinterpret_cast<int*>(tslot + 1);
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int qd = warp & 3, g = warp >> 2;     // TMEM lane quarter, column group
+    const int r = 32 * qd + lane;               // the row (query) this thread works on
     const int T = p.T, tiles = (T + TQ - 1) / TQ;
     const int tile = blockIdx.x % tiles, bh = blockIdx.x / tiles, b = bh / p.H, h = bh % p.H;
     const int q0 = tile * TQ, kb0 = q0 - RADIUS;
@@ -80,11 +123,14 @@ __global__ void __launch_bounds__(NTH, 1)
         prefetch_tmap(&tm_k);
         prefetch_tmap(&tm_v);
         mbar_init(bar_ld, 1);
+        mbar_init(bar_rl, 1);
         mbar_init(bar_s, 1);
         mbar_init(bar_o, 1);
         *serr = 0;
+        *sover = 0;
         fence_mbar_init();
     }
+    if (tid < JMAX) sdocs[tid] = EMPTY_DOC;
     if (warp == 0) {
         tmem_alloc(tslot, 512);
         tmem_relinquish();
@@ -102,62 +148,72 @@ __global__ void __launch_bounds__(NTH, 1)
             tma_load_4d(sm + OFF_V + 16384 * j, &tm_v, bar_ld, 0, kb0 + 128 * j, h, b);
         }
     }
-
-    // the row: query t = q0 + tid
-    const int t = q0 + tid;
-    const bool in_t = t < T;
-    int st = 0, en = -1, doc = 0;
-    if (in_t) {
-        st = p.doc_start[(size_t)b * T + t];
-        en = p.doc_end[(size_t)b * T + t];
-        doc = p.doc_id[(size_t)b * T + t];
-    }
-    const bool live = in_t && en >= st;
-    const bool relay_ok = live && doc >= 0 && doc < p.ndoc;
-    if (live && !relay_ok) atomicExch(p.err, kRelayDocError);
-    // window columns (band index = key - kb0), inclusive
-    const int lo = max(max(t - RADIUS, st), 0), hi = min(min(t + RADIUS, en), T - 1);
-    const int clo = live ? lo - kb0 : 1, chi = live ? hi - kb0 : 0;
-
-    // relay scores on the CUDA cores while the copies land
-    float rs[SLOTS];
-    const size_t rbase = ((size_t)doc * p.H + h) * SLOTS * D;
-    {
-        uint4 qv[8];
-        const uint4* qg = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.q) +
-                                                         (((size_t)b * p.H + h) * T + (in_t ? t : 0)) * D);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) qv[i] = in_t ? qg[i] : make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-        for (int s = 0; s < SLOTS; ++s) {
-            float acc = 0.f;
-            if (relay_ok) {
-                const uint4* kg = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.rk) + rbase + s * D);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const uint4 kv = __ldg(kg + i);
-                    acc = fmaf(bf16_lo(qv[i].x), bf16_lo(kv.x), acc);
-                    acc = fmaf(bf16_hi(qv[i].x), bf16_hi(kv.x), acc);
-                    acc = fmaf(bf16_lo(qv[i].y), bf16_lo(kv.y), acc);
-                    acc = fmaf(bf16_hi(qv[i].y), bf16_hi(kv.y), acc);
-                    acc = fmaf(bf16_lo(qv[i].z), bf16_lo(kv.z), acc);
-                    acc = fmaf(bf16_hi(qv[i].z), bf16_hi(kv.z), acc);
-                    acc = fmaf(bf16_lo(qv[i].w), bf16_lo(kv.w), acc);
-                    acc = fmaf(bf16_hi(qv[i].w), bf16_hi(kv.w), acc);
+    // row set-up (column group 0): window columns (band index = key - kb0) and the relay group
+    if (g == 0) {
+        const int t = q0 + r;
+        int st = 0, en = -1, doc = 0;
+        if (t < T) {
+            st = p.doc_start[(size_t)b * T + t];
+            en = p.doc_end[(size_t)b * T + t];
+            doc = p.doc_id[(size_t)b * T + t];
+        }
+        const bool live = t < T && en >= st;
+        const bool relay_ok = live && doc >= 0 && doc < p.ndoc;
+        if (live && !relay_ok) atomicExch(p.err, kRelayDocError);
+        int jr = -1;
+        if (relay_ok) {
+            for (int k = 0; k < JMAX; ++k) {
+                const int prev = atomicCAS(&sdocs[k], EMPTY_DOC, doc);
+                if (prev == EMPTY_DOC || prev == doc) {
+                    jr = k;
+                    break;
                 }
             }
-            rs[s] = acc * SCALE;
+            if (jr < 0) atomicOr(sover, 1);
         }
+        const int lo = max(max(t - RADIUS, st), 0), hi = min(min(t + RADIUS, en), T - 1);
+        srow[r] = make_int4(live ? lo - kb0 : 1, live ? hi - kb0 : 0, jr, live ? (relay_ok ? doc : -2) : -1);
+    }
+    __syncthreads();
+    // slots are filled in order, so the documents form a prefix of sdocs
+    int J = 0;
+#pragma unroll
+    for (int k = 0; k < JMAX; ++k) J += sdocs[k] != EMPTY_DOC;
+    const bool tc_relay = *sover == 0;
+    if (tid == 0 && tc_relay && J > 0) {
+        prefetch_tmap(&tm_rk);
+        prefetch_tmap(&tm_rv);
+        mbar_arrive_expect_tx(bar_rl, 2u * 2048u * (uint32_t)J);
+        for (int j = 0; j < J; ++j) {
+            tma_load_4d(sm + OFF_RK + 2048 * j, &tm_rk, bar_rl, 0, 0, h, sdocs[j]);
+            tma_load_4d(sm + OFF_RV + 2048 * j, &tm_rv, bar_rl, 0, 0, h, sdocs[j]);
+        }
+    }
+    const int4 ri = srow[r];
+    const int clo = ri.x, chi = ri.y, jr = ri.z, rdoc = ri.w;
+    const size_t rbase = ((size_t)(rdoc >= 0 ? rdoc : 0) * p.H + h) * SLOTS * D;
+    // more documents than the tensor-core relay holds: relay scores on the CUDA cores
+    float rs[SLOTS];
+#pragma unroll
+    for (int s = 0; s < SLOTS; ++s) rs[s] = 0.f;
+    if (!tc_relay && g == 0 && rdoc >= 0) {
+        uint4 qv[8];
+        const uint4* qg = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.q) +
+                                                         (((size_t)b * p.H + h) * T + q0 + r) * D);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) qv[i] = qg[i];
+#pragma unroll
+        for (int s = 0; s < SLOTS; ++s)
+            rs[s] = dot64(qv, static_cast<const __nv_bfloat16*>(p.rk) + rbase + s * D) * SCALE;
     }
 
     // padding keys: zero their K and V rows once they have landed
     mbar_wait(bar_ld, 0, serr, 1);
-#pragma unroll
-    for (int j = 0; j < 3; ++j) {
-        const int r = tid + 128 * j, key = kb0 + r;
+    if (tid < KB) {
+        const int key = kb0 + tid;
         if (key >= 0 && key < T && p.doc_end[(size_t)b * T + key] < p.doc_start[(size_t)b * T + key]) {
-            uint4* kr = reinterpret_cast<uint4*>(sm + OFF_K + r * 128);
-            uint4* vr = reinterpret_cast<uint4*>(sm + OFF_V + r * 128);
+            uint4* kr = reinterpret_cast<uint4*>(sm + OFF_K + tid * 128);
+            uint4* vr = reinterpret_cast<uint4*>(sm + OFF_V + tid * 128);
 #pragma unroll
             for (int i = 0; i < 8; ++i) kr[i] = vr[i] = make_uint4(0u, 0u, 0u, 0u);
         }
@@ -172,116 +228,165 @@ __global__ void __launch_bounds__(NTH, 1)
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
                 umma_ss(tmem + 128 * j, kdesc(qa + 32 * kk), kdesc(ka + 16384 * j + 32 * kk), IDESC_S, kk > 0 ? 1u : 0u);
+        if (tc_relay && J > 0) {
+            mbar_wait(bar_rl, 0, serr, 2);
+            tc_fence_after();
+            const uint32_t ra = smem_u32addr(sm + OFF_RK), idesc = umma_idesc_bf16(128, 16 * J, false);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+                umma_ss(tmem + TM_SR, kdesc(qa + 32 * kk), kdesc(ra + 32 * kk), idesc, kk > 0 ? 1u : 0u);
+        }
         umma_commit(bar_s);
     }
 
-    // softmax over the row: the warp's rows need band columns [32 w, 32 w + 288)
-    mbar_wait(bar_s, 0, serr, 2);
+    // softmax: this warp reads columns [cb + 16 c0, cb + 16 c1) of its lane quarter's band span
+    mbar_wait(bar_s, 0, serr, 3);
     tc_fence_after();
-    const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
-    const int cb = 32 * warp;
+    const uint32_t trow = tmem + ((uint32_t)(32 * qd) << 16);
+    const int cb = 32 * qd, c0 = (18 * g) / 4, c1 = (18 * (g + 1)) / 4;
     float m = -INFINITY;
-#pragma unroll 1
-    for (int c = 0; c < 18; ++c) {
-        uint32_t r[16];
-        tmem_ld16(trow + cb + 16 * c, r);
+    for (int c = c0; c < c1; ++c) {
+        uint32_t v[16];
+        tmem_ld16(trow + cb + 16 * c, v);
         tmem_ld_wait();
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
             const int col = cb + 16 * c + e;
-            if (col >= clo && col <= chi) m = fmaxf(m, __uint_as_float(r[e]) * SCALE);
+            if (col >= clo && col <= chi) m = fmaxf(m, __uint_as_float(v[e]) * SCALE);
         }
     }
-    if (relay_ok) {
+    // relay scores (column group 0): this row's document group of the relay columns
+    if (g == 0) {
+        if (tc_relay) {
+            for (int j = 0; j < J; ++j) {
+                uint32_t v[16];
+                tmem_ld16(trow + TM_SR + 16 * j, v);
+                tmem_ld_wait();
+                if (j == jr) {
 #pragma unroll
-        for (int s = 0; s < SLOTS; ++s) m = fmaxf(m, rs[s]);
+                    for (int s = 0; s < SLOTS; ++s) rs[s] = __uint_as_float(v[s]) * SCALE;
+                }
+            }
+        }
+        if (rdoc >= 0) {
+#pragma unroll
+            for (int s = 0; s < SLOTS; ++s) m = fmaxf(m, rs[s]);
+        }
     }
+    smax[g * 128 + r] = m;
+    __syncthreads();
+    m = fmaxf(fmaxf(smax[r], smax[128 + r]), fmaxf(smax[256 + r], smax[384 + r]));
     float total = 0.f;
-    uint8_t* P = sm + OFF_P;
-    const int prow = tid * 128, sw = tid & 7;
-#pragma unroll 1
-    for (int c = 0; c < 18; ++c) {
-        uint32_t r[16];
-        tmem_ld16(trow + cb + 16 * c, r);
-        tmem_ld_wait();
-        uint32_t pk[8];
+    uint32_t pk[5][8];
 #pragma unroll
-        for (int e = 0; e < 16; e += 2) {
-            const int col = cb + 16 * c + e;
-            const float p0 = (col >= clo && col <= chi) ? __expf(__uint_as_float(r[e]) * SCALE - m) : 0.f;
-            const float p1 = (col + 1 >= clo && col + 1 <= chi) ? __expf(__uint_as_float(r[e + 1]) * SCALE - m) : 0.f;
-            total += p0 + p1;
-            pk[e / 2] = pack_bf16x2(p0, p1);
+    for (int i = 0; i < 5; ++i) {
+        const int c = c0 + i;
+        if (c < c1) {
+            uint32_t v[16];
+            tmem_ld16(trow + cb + 16 * c, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+                const int col = cb + 16 * c + e;
+                // s - m is formed exactly before the exponential (scores far below zero stay exact)
+                const float p0 = (col >= clo && col <= chi) ? __expf(fmaf(__uint_as_float(v[e]), SCALE, -m)) : 0.f;
+                const float p1 =
+                    (col + 1 >= clo && col + 1 <= chi) ? __expf(fmaf(__uint_as_float(v[e + 1]), SCALE, -m)) : 0.f;
+                total += p0 + p1;
+                pk[i][e / 2] = pack_bf16x2(p0, p1);
+            }
         }
-        // columns cb + 16 c .. + 15: atom a, 16-byte chunks cc and cc + 1
-        const int kc = cb + 16 * c, a = kc >> 6, cc = (kc & 63) >> 3;
-        uint8_t* base = P + a * 16384 + prow;
-        *reinterpret_cast<uint4*>(base + ((cc ^ sw) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        *reinterpret_cast<uint4*>(base + (((cc + 1) ^ sw) << 4)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
     }
-    // the columns outside the warp's range hold zeros
-    for (int kc = 0; kc < KB; kc += 8) {
-        if (kc >= cb && kc < cb + 288) continue;
-        *reinterpret_cast<uint4*>(P + (kc >> 6) * 16384 + prow + ((((kc & 63) >> 3) ^ sw) << 4)) =
-            make_uint4(0u, 0u, 0u, 0u);
-    }
-    float pr[SLOTS];
+    uint32_t prk[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+    if (g == 0 && rdoc >= 0) {
+        float pr[SLOTS];
 #pragma unroll
-    for (int s = 0; s < SLOTS; ++s) {
-        pr[s] = relay_ok ? __expf(rs[s] - m) : 0.f;
-        total += pr[s];
+        for (int s = 0; s < SLOTS; ++s) {
+            pr[s] = __expf(rs[s] - m);
+            total += pr[s];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) prk[u] = pack_bf16x2(pr[2 * u], pr[2 * u + 1]);
+        if (!tc_relay) {
+#pragma unroll
+            for (int s = 0; s < SLOTS; ++s) spr[r * SLOTS + s] = pr[s];
+        }
     }
-    fence_proxy_async_smem();
+    ssum[g * 128 + r] = total;
+    tc_fence_before();
+    __syncthreads();  // every read of S is complete: P may now overwrite it
+    tc_fence_after();
+#pragma unroll
+    for (int i = 0; i < 5; ++i)
+        if (c0 + i < c1) tmem_st8(trow + (uint32_t)(16 * qd + 8 * (c0 + i)), pk[i]);
+    {
+        // P columns outside the lane quarter's span [16 qd, 16 qd + 144) are zero: six groups of 8
+        const uint32_t zero[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+        for (int zc = g; zc < 6; zc += 4) {
+            const int col = zc < 2 * qd ? 8 * zc : 16 * qd + 144 + 8 * (zc - 2 * qd);
+            tmem_st8(trow + (uint32_t)col, zero);
+        }
+        if (g == 0 && tc_relay) {
+            // one warp-wide store per document group; each lane supplies its row's values
+            for (int j = 0; j < J; ++j) {
+                uint32_t val[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) val[u] = j == jr ? prk[u] : 0u;
+                tmem_st8(trow + TM_PR + 8 * j, val);
+            }
+        }
+    }
+    tmem_st_wait();
     tc_fence_before();
     __syncthreads();
     if (tid == 0) {
         tc_fence_after();
-        const uint32_t pa = smem_u32addr(P), va = smem_u32addr(sm + OFF_V);
+        const uint32_t va = smem_u32addr(sm + OFF_V), rva = smem_u32addr(sm + OFF_RV);
 #pragma unroll
         for (int kk = 0; kk < KB / 16; ++kk)
-            umma_ss(tmem + TM_O, kdesc(pa + 16384 * (kk >> 2) + 32 * (kk & 3)), umma_sdesc_sw128(va + 2048 * kk, 16384, 1024),
-                    IDESC_O, kk > 0 ? 1u : 0u);
+            umma_ts(tmem + TM_O, tmem + 8 * kk, mndesc(va + 2048 * kk), IDESC_O, kk > 0 ? 1u : 0u);
+        if (tc_relay)
+            for (int j = 0; j < J; ++j) umma_ts(tmem + TM_O, tmem + TM_PR + 8 * j, mndesc(rva + 2048 * j), IDESC_O, 1u);
         umma_commit(bar_o);
     }
-    mbar_wait(bar_o, 0, serr, 3);
+    mbar_wait(bar_o, 0, serr, 4);
     tc_fence_after();
-    float o[D];
+    // epilogue: column group g stores output channels 16 g .. 16 g + 15 of its row
+    uint32_t v[16];
+    tmem_ld16(trow + TM_O + 16 * g, v);
+    tmem_ld_wait();
+    const int t = q0 + r;
+    if (t < T) {
+        const bool live = rdoc != -1;
+        const float tot = ssum[r] + ssum[128 + r] + ssum[256 + r] + ssum[384 + r];
+        float o[16];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-        uint32_t r[16];
-        tmem_ld16(trow + TM_O + 16 * c, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 16; ++e) o[16 * c + e] = __uint_as_float(r[e]);
-    }
-    if (relay_ok) {
-#pragma unroll 1
-        for (int s = 0; s < SLOTS; ++s) {
-            const uint4* vg = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.rv) + rbase + s * D);
-            const float w = pr[s];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const uint4 vv = __ldg(vg + i);
-                o[8 * i + 0] = fmaf(w, bf16_lo(vv.x), o[8 * i + 0]);
-                o[8 * i + 1] = fmaf(w, bf16_hi(vv.x), o[8 * i + 1]);
-                o[8 * i + 2] = fmaf(w, bf16_lo(vv.y), o[8 * i + 2]);
-                o[8 * i + 3] = fmaf(w, bf16_hi(vv.y), o[8 * i + 3]);
-                o[8 * i + 4] = fmaf(w, bf16_lo(vv.z), o[8 * i + 4]);
-                o[8 * i + 5] = fmaf(w, bf16_hi(vv.z), o[8 * i + 5]);
-                o[8 * i + 6] = fmaf(w, bf16_lo(vv.w), o[8 * i + 6]);
-                o[8 * i + 7] = fmaf(w, bf16_hi(vv.w), o[8 * i + 7]);
+        for (int e = 0; e < 16; ++e) o[e] = __uint_as_float(v[e]);
+        if (!tc_relay && rdoc >= 0) {
+            const __nv_bfloat16* rv = static_cast<const __nv_bfloat16*>(p.rv) + rbase + 16 * g;
+#pragma unroll 4
+            for (int s = 0; s < SLOTS; ++s) {
+                const float w = spr[r * SLOTS + s];
+                const uint4* vg = reinterpret_cast<const uint4*>(rv + s * D);
+                const uint4 a = __ldg(vg), c = __ldg(vg + 1);
+                o[0] = fmaf(w, bf16_lo(a.x), o[0]);   o[1] = fmaf(w, bf16_hi(a.x), o[1]);
+                o[2] = fmaf(w, bf16_lo(a.y), o[2]);   o[3] = fmaf(w, bf16_hi(a.y), o[3]);
+                o[4] = fmaf(w, bf16_lo(a.z), o[4]);   o[5] = fmaf(w, bf16_hi(a.z), o[5]);
+                o[6] = fmaf(w, bf16_lo(a.w), o[6]);   o[7] = fmaf(w, bf16_hi(a.w), o[7]);
+                o[8] = fmaf(w, bf16_lo(c.x), o[8]);   o[9] = fmaf(w, bf16_hi(c.x), o[9]);
+                o[10] = fmaf(w, bf16_lo(c.y), o[10]); o[11] = fmaf(w, bf16_hi(c.y), o[11]);
+                o[12] = fmaf(w, bf16_lo(c.z), o[12]); o[13] = fmaf(w, bf16_hi(c.z), o[13]);
+                o[14] = fmaf(w, bf16_lo(c.w), o[14]); o[15] = fmaf(w, bf16_hi(c.w), o[15]);
             }
         }
-    }
-    if (in_t) {
         const size_t row = ((size_t)b * p.H + h) * T + t;
-        uint4* og = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.o) + row * D);
-        const float inv = live ? 1.f / total : 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-            og[i] = make_uint4(pack_bf16x2(o[8 * i] * inv, o[8 * i + 1] * inv), pack_bf16x2(o[8 * i + 2] * inv, o[8 * i + 3] * inv),
-                               pack_bf16x2(o[8 * i + 4] * inv, o[8 * i + 5] * inv), pack_bf16x2(o[8 * i + 6] * inv, o[8 * i + 7] * inv));
-        reinterpret_cast<float2*>(p.norm)[row] = live ? make_float2(m, total) : make_float2(0.f, 1.f);
+        const float inv = live ? 1.f / tot : 0.f;
+        uint4* og = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.o) + row * D + 16 * g);
+        og[0] = make_uint4(pack_bf16x2(o[0] * inv, o[1] * inv), pack_bf16x2(o[2] * inv, o[3] * inv),
+                           pack_bf16x2(o[4] * inv, o[5] * inv), pack_bf16x2(o[6] * inv, o[7] * inv));
+        og[1] = make_uint4(pack_bf16x2(o[8] * inv, o[9] * inv), pack_bf16x2(o[10] * inv, o[11] * inv),
+                           pack_bf16x2(o[12] * inv, o[13] * inv), pack_bf16x2(o[14] * inv, o[15] * inv));
+        if (g == 0) reinterpret_cast<float2*>(p.norm)[row] = live ? make_float2(m, tot) : make_float2(0.f, 1.f);
     }
     tc_fence_before();
     __syncthreads();
@@ -388,8 +493,8 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-// 4-D bf16 map over a contiguous [B][H][T][64] array; box {64, 128, 1, 1}, 128-byte swizzle
-int make_band_map(CUtensorMap* m, const void* base, int64_t B, int64_t H, int64_t T) {
+// 4-D bf16 map over a contiguous [outer][H][rows][64] array; box {64, box_rows, 1, 1}, 128-byte swizzle
+int make_map64(CUtensorMap* m, const void* base, int64_t outer, int64_t H, int64_t rows, uint32_t box_rows) {
     static EncodeTiledFn enc = nullptr;
     if (!enc) {
         void* ptr = nullptr;
@@ -399,9 +504,9 @@ int make_band_map(CUtensorMap* m, const void* base, int64_t B, int64_t H, int64_
             enc = reinterpret_cast<EncodeTiledFn>(ptr);
     }
     if (!enc) return fail(DBL_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-    cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)T, (cuuint64_t)H, (cuuint64_t)B};
-    cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)(T * D * 2), (cuuint64_t)(H * T * D * 2)};
-    cuuint32_t box[4] = {(cuuint32_t)D, 128, 1, 1};
+    cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)rows, (cuuint64_t)H, (cuuint64_t)outer};
+    cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)(rows * D * 2), (cuuint64_t)(H * rows * D * 2)};
+    cuuint32_t box[4] = {(cuuint32_t)D, box_rows, 1, 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
     CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -454,10 +559,12 @@ extern "C" int dbl_relay_attention_forward(const dbl_relay_attention_args* a, db
         relay_attn_f32_kernel<<<(unsigned)(tiles * p.B * p.H), 128, 0, st>>>(p);
         return launch_status("relay_attn_f32_kernel");
     }
-    CUtensorMap mq, mk, mv;
-    rc = make_band_map(&mq, a->q, a->batch, a->heads, a->time);
-    if (rc == DBL_OK) rc = make_band_map(&mk, a->k, a->batch, a->heads, a->time);
-    if (rc == DBL_OK) rc = make_band_map(&mv, a->v, a->batch, a->heads, a->time);
+    CUtensorMap mq, mk, mv, mrk, mrv;
+    rc = make_map64(&mq, a->q, a->batch, a->heads, a->time, 128);
+    if (rc == DBL_OK) rc = make_map64(&mk, a->k, a->batch, a->heads, a->time, 128);
+    if (rc == DBL_OK) rc = make_map64(&mv, a->v, a->batch, a->heads, a->time, 128);
+    if (rc == DBL_OK) rc = make_map64(&mrk, a->relay_k, a->documents, a->heads, SLOTS, SLOTS);
+    if (rc == DBL_OK) rc = make_map64(&mrv, a->relay_v, a->documents, a->heads, SLOTS, SLOTS);
     if (rc != DBL_OK) return rc;
     static bool attr_set = false;
     if (!attr_set) {
@@ -467,6 +574,6 @@ extern "C" int dbl_relay_attention_forward(const dbl_relay_attention_args* a, db
         attr_set = true;
     }
     const size_t tiles = (size_t)(p.T + TQ - 1) / TQ;
-    relay_attn_tc_kernel<<<(unsigned)(tiles * p.B * p.H), NTH, SMEM_TC, st>>>(mq, mk, mv, p);
+    relay_attn_tc_kernel<<<(unsigned)(tiles * p.B * p.H), NTH, SMEM_TC, st>>>(mq, mk, mv, mrk, mrv, p);
     return launch_status("relay_attn_tc_kernel");
 }
