@@ -56,9 +56,12 @@ constexpr uint32_t OFF_DOC = OFF_PR + 8192;   // int [JMAX] documents, int overf
 constexpr uint32_t OFF_BAR = OFF_DOC + 64;
 constexpr uint32_t SMEM_TC = OFF_BAR + 64 + 1024;  // + alignment slack
 // TMEM columns: S of the band [0, 384) and of the relay slots [384, 384 + 16 J); once the softmax
-// has read them, P of the band (bf16 pairs) [0, 192), O [192, 256), P of the relay slots [256, 256 + 8 J)
-constexpr uint32_t TM_SR = 384, TM_O = 192, TM_PR = 256;
+// has read them, P of the band (bf16 pairs) [0, 192), O in two partial sums [192, 256) and
+// [320, 384), P of the relay slots [256, 256 + 8 J)
+constexpr uint32_t TM_SR = 384, TM_O = 192, TM_PR = 256, TM_O2 = 320;
 constexpr uint32_t IDESC_S = umma_idesc_bf16(128, 128, false);
+constexpr uint32_t IDESC_S256 = umma_idesc_bf16(128, 256, false);
+constexpr int ISSUER2 = 128;  // the second MMA-issuing thread (warp 4): the product chains are split in two
 constexpr uint32_t IDESC_O = umma_idesc_bf16(128, 64, true);
 constexpr int kRelayDocError = 101;  // a live row's doc_id outside [0, documents)
 
@@ -117,6 +120,17 @@ __global__ void __launch_bounds__(NTH, 1)
     const int T = p.T, tiles = (T + TQ - 1) / TQ;
     const int tile = blockIdx.x % tiles, bh = blockIdx.x / tiles, b = bh / p.H, h = bh % p.H;
     const int q0 = tile * TQ, kb0 = q0 - RADIUS;
+    // the metadata loads go out first, so that their latency overlaps the TMEM allocation and the
+    // tile copies: the row's document (column group 0) and whether band key tid is padding
+    int st = 0, en = -1, doc = 0;
+    if (g == 0 && q0 + r < T) {
+        st = p.doc_start[(size_t)b * T + q0 + r];
+        en = p.doc_end[(size_t)b * T + q0 + r];
+        doc = p.doc_id[(size_t)b * T + q0 + r];
+    }
+    bool pad_key = false;
+    if (tid < KB && kb0 + tid >= 0 && kb0 + tid < T)
+        pad_key = p.doc_end[(size_t)b * T + kb0 + tid] < p.doc_start[(size_t)b * T + kb0 + tid];
 
     if (tid == 0) {
         prefetch_tmap(&tm_q);
@@ -124,8 +138,8 @@ __global__ void __launch_bounds__(NTH, 1)
         prefetch_tmap(&tm_v);
         mbar_init(bar_ld, 1);
         mbar_init(bar_rl, 1);
-        mbar_init(bar_s, 1);
-        mbar_init(bar_o, 1);
+        mbar_init(bar_s, 2);
+        mbar_init(bar_o, 2);
         *serr = 0;
         *sover = 0;
         fence_mbar_init();
@@ -151,12 +165,6 @@ __global__ void __launch_bounds__(NTH, 1)
     // row set-up (column group 0): window columns (band index = key - kb0) and the relay group
     if (g == 0) {
         const int t = q0 + r;
-        int st = 0, en = -1, doc = 0;
-        if (t < T) {
-            st = p.doc_start[(size_t)b * T + t];
-            en = p.doc_end[(size_t)b * T + t];
-            doc = p.doc_id[(size_t)b * T + t];
-        }
         const bool live = t < T && en >= st;
         const bool relay_ok = live && doc >= 0 && doc < p.ndoc;
         if (live && !relay_ok) atomicExch(p.err, kRelayDocError);
@@ -209,9 +217,8 @@ __global__ void __launch_bounds__(NTH, 1)
 
     // padding keys: zero their K and V rows once they have landed
     mbar_wait(bar_ld, 0, serr, 1);
-    if (tid < KB) {
-        const int key = kb0 + tid;
-        if (key >= 0 && key < T && p.doc_end[(size_t)b * T + key] < p.doc_start[(size_t)b * T + key]) {
+    if (pad_key) {
+        {
             uint4* kr = reinterpret_cast<uint4*>(sm + OFF_K + tid * 128);
             uint4* vr = reinterpret_cast<uint4*>(sm + OFF_V + tid * 128);
 #pragma unroll
@@ -220,21 +227,26 @@ __global__ void __launch_bounds__(NTH, 1)
     }
     fence_proxy_async_smem();
     __syncthreads();
-    if (tid == 0) {
+    if (tid == 0 || tid == ISSUER2) {
+        // two issuers: band keys [0, 256) as one N = 256 chain; keys [256, 384) and the relay slots
         tc_fence_after();
         const uint32_t qa = smem_u32addr(sm + OFF_Q), ka = smem_u32addr(sm + OFF_K);
-#pragma unroll
-        for (int j = 0; j < 3; ++j)
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-                umma_ss(tmem + 128 * j, kdesc(qa + 32 * kk), kdesc(ka + 16384 * j + 32 * kk), IDESC_S, kk > 0 ? 1u : 0u);
-        if (tc_relay && J > 0) {
-            mbar_wait(bar_rl, 0, serr, 2);
-            tc_fence_after();
-            const uint32_t ra = smem_u32addr(sm + OFF_RK), idesc = umma_idesc_bf16(128, 16 * J, false);
+        if (tid == 0) {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-                umma_ss(tmem + TM_SR, kdesc(qa + 32 * kk), kdesc(ra + 32 * kk), idesc, kk > 0 ? 1u : 0u);
+                umma_ss(tmem, kdesc(qa + 32 * kk), kdesc(ka + 32 * kk), IDESC_S256, kk > 0 ? 1u : 0u);
+        } else {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+                umma_ss(tmem + 256, kdesc(qa + 32 * kk), kdesc(ka + 32768 + 32 * kk), IDESC_S, kk > 0 ? 1u : 0u);
+            if (tc_relay && J > 0) {
+                mbar_wait(bar_rl, 0, serr, 2);
+                tc_fence_after();
+                const uint32_t ra = smem_u32addr(sm + OFF_RK), idesc = umma_idesc_bf16(128, 16 * J, false);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_ss(tmem + TM_SR, kdesc(qa + 32 * kk), kdesc(ra + 32 * kk), idesc, kk > 0 ? 1u : 0u);
+            }
         }
         umma_commit(bar_s);
     }
@@ -244,17 +256,29 @@ __global__ void __launch_bounds__(NTH, 1)
     tc_fence_after();
     const uint32_t trow = tmem + ((uint32_t)(32 * qd) << 16);
     const int cb = 32 * qd, c0 = (18 * g) / 4, c1 = (18 * (g + 1)) / 4;
-    float m = -INFINITY;
-    for (int c = c0; c < c1; ++c) {
-        uint32_t v[16];
-        tmem_ld16(trow + cb + 16 * c, v);
-        tmem_ld_wait();
+    // raw scores: max(s) / 8 is max(s / 8) exactly.  A chunk inside every lane's window (most of
+    // them) takes the unmasked loop.
+    float mraw = -INFINITY;
+    auto max_chunk = [&](const uint32_t (&v)[16], int cs) {
+        if (__all_sync(0xffffffffu, cs >= clo && cs + 15 <= chi)) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-            const int col = cb + 16 * c + e;
-            if (col >= clo && col <= chi) m = fmaxf(m, __uint_as_float(v[e]) * SCALE);
+            for (int e = 0; e < 16; ++e) mraw = fmaxf(mraw, __uint_as_float(v[e]));
+        } else if (!__all_sync(0xffffffffu, cs > chi || cs + 15 < clo)) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+                if (cs + e >= clo && cs + e <= chi) mraw = fmaxf(mraw, __uint_as_float(v[e]));
         }
+    };
+    // two chunks per TMEM wait
+    for (int c = c0; c < c1; c += 2) {
+        uint32_t v0[16], v1[16];
+        tmem_ld16(trow + cb + 16 * c, v0);
+        if (c + 1 < c1) tmem_ld16(trow + cb + 16 * (c + 1), v1);
+        tmem_ld_wait();
+        max_chunk(v0, cb + 16 * c);
+        if (c + 1 < c1) max_chunk(v1, cb + 16 * (c + 1));
     }
+    float m = mraw * SCALE;
     // relay scores (column group 0): this row's document group of the relay columns
     if (g == 0) {
         if (tc_relay) {
@@ -278,23 +302,42 @@ __global__ void __launch_bounds__(NTH, 1)
     m = fmaxf(fmaxf(smax[r], smax[128 + r]), fmaxf(smax[256 + r], smax[384 + r]));
     float total = 0.f;
     uint32_t pk[5][8];
-#pragma unroll
-    for (int i = 0; i < 5; ++i) {
-        const int c = c0 + i;
-        if (c < c1) {
-            uint32_t v[16];
-            tmem_ld16(trow + cb + 16 * c, v);
-            tmem_ld_wait();
+    // p = exp(s / 8 - m) packed to bf16 pairs; s / 8 - m is formed exactly before the exponential
+    // (scores far below zero stay exact)
+    auto exp_chunk = [&](const uint32_t (&v)[16], int cs, uint32_t (&out)[8]) {
+        if (__all_sync(0xffffffffu, cs >= clo && cs + 15 <= chi)) {
 #pragma unroll
             for (int e = 0; e < 16; e += 2) {
-                const int col = cb + 16 * c + e;
-                // s - m is formed exactly before the exponential (scores far below zero stay exact)
+                const float p0 = __expf(fmaf(__uint_as_float(v[e]), SCALE, -m));
+                const float p1 = __expf(fmaf(__uint_as_float(v[e + 1]), SCALE, -m));
+                total += p0 + p1;
+                out[e / 2] = pack_bf16x2(p0, p1);
+            }
+        } else if (__all_sync(0xffffffffu, cs > chi || cs + 15 < clo)) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) out[e] = 0u;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+                const int col = cs + e;
                 const float p0 = (col >= clo && col <= chi) ? __expf(fmaf(__uint_as_float(v[e]), SCALE, -m)) : 0.f;
                 const float p1 =
                     (col + 1 >= clo && col + 1 <= chi) ? __expf(fmaf(__uint_as_float(v[e + 1]), SCALE, -m)) : 0.f;
                 total += p0 + p1;
-                pk[i][e / 2] = pack_bf16x2(p0, p1);
+                out[e / 2] = pack_bf16x2(p0, p1);
             }
+        }
+    };
+#pragma unroll
+    for (int i = 0; i < 5; i += 2) {
+        const int c = c0 + i;
+        if (c < c1) {
+            uint32_t v0[16], v1[16];
+            tmem_ld16(trow + cb + 16 * c, v0);
+            if (c + 1 < c1) tmem_ld16(trow + cb + 16 * (c + 1), v1);
+            tmem_ld_wait();
+            exp_chunk(v0, cb + 16 * c, pk[i]);
+            if (i + 1 < 5 && c + 1 < c1) exp_chunk(v1, cb + 16 * (c + 1), pk[i + 1]);
         }
     }
     uint32_t prk[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
@@ -339,21 +382,26 @@ __global__ void __launch_bounds__(NTH, 1)
     tmem_st_wait();
     tc_fence_before();
     __syncthreads();
-    if (tid == 0) {
+    if (tid == 0 || tid == ISSUER2) {
+        // two partial sums: band keys [0, 192) and the relay slots into [192, 256), keys [192, 384)
+        // into [320, 384)
         tc_fence_after();
         const uint32_t va = smem_u32addr(sm + OFF_V), rva = smem_u32addr(sm + OFF_RV);
+        const int k0 = tid == 0 ? 0 : KB / 32;
+        const uint32_t dst = tmem + (tid == 0 ? TM_O : TM_O2);
 #pragma unroll
-        for (int kk = 0; kk < KB / 16; ++kk)
-            umma_ts(tmem + TM_O, tmem + 8 * kk, mndesc(va + 2048 * kk), IDESC_O, kk > 0 ? 1u : 0u);
-        if (tc_relay)
-            for (int j = 0; j < J; ++j) umma_ts(tmem + TM_O, tmem + TM_PR + 8 * j, mndesc(rva + 2048 * j), IDESC_O, 1u);
+        for (int i = 0; i < KB / 32; ++i)
+            umma_ts(dst, tmem + 8 * (k0 + i), mndesc(va + 2048 * (k0 + i)), IDESC_O, i > 0 ? 1u : 0u);
+        if (tid == 0 && tc_relay)
+            for (int j = 0; j < J; ++j) umma_ts(dst, tmem + TM_PR + 8 * j, mndesc(rva + 2048 * j), IDESC_O, 1u);
         umma_commit(bar_o);
     }
     mbar_wait(bar_o, 0, serr, 4);
     tc_fence_after();
     // epilogue: column group g stores output channels 16 g .. 16 g + 15 of its row
-    uint32_t v[16];
+    uint32_t v[16], v2[16];
     tmem_ld16(trow + TM_O + 16 * g, v);
+    tmem_ld16(trow + TM_O2 + 16 * g, v2);
     tmem_ld_wait();
     const int t = q0 + r;
     if (t < T) {
@@ -361,7 +409,7 @@ __global__ void __launch_bounds__(NTH, 1)
         const float tot = ssum[r] + ssum[128 + r] + ssum[256 + r] + ssum[384 + r];
         float o[16];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) o[e] = __uint_as_float(v[e]);
+        for (int e = 0; e < 16; ++e) o[e] = __uint_as_float(v[e]) + __uint_as_float(v2[e]);
         if (!tc_relay && rdoc >= 0) {
             const __nv_bfloat16* rv = static_cast<const __nv_bfloat16*>(p.rv) + rbase + 16 * g;
 #pragma unroll 4
