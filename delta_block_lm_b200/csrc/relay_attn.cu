@@ -29,6 +29,8 @@
 // 16 channels each, scores reduced by two shuffles.
 #include <cuda_bf16.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "tc_ptx.cuh"
 
@@ -39,30 +41,36 @@ constexpr int D = 64, RADIUS = 128, SLOTS = 16;
 constexpr float SCALE = 0.125f;
 
 // ------------------------------------------------------------------------------ tensor cores
-constexpr int TQ = 128;                 // queries per CTA = TMEM lanes
-constexpr int KB = TQ + 2 * RADIUS;     // 384 band keys
+constexpr int TQ = 128;                 // queries per tile = TMEM lanes
+constexpr int KB = TQ + 2 * RADIUS;     // 384 band keys: blocks t - 1, t, t + 1 of 128 keys
 constexpr int NTH = 512;                // 16 warps: lane quarter = warp % 4, column group = warp / 4
-constexpr int JMAX = 8;                 // relay documents per tile on the tensor cores
+constexpr int JMAX = 4;                 // relay documents per tile on the tensor cores
 constexpr int EMPTY_DOC = -1;
-constexpr uint32_t OFF_Q = 0;                 // [128][128 B]
-constexpr uint32_t OFF_K = 16384;             // 3 x [128][128 B]
-constexpr uint32_t OFF_V = OFF_K + 49152;     // 3 x [128][128 B]
-constexpr uint32_t OFF_RK = OFF_V + 49152;    // JMAX x [16][128 B]: relay keys of the tile's documents
-constexpr uint32_t OFF_RV = OFF_RK + 16384;   // JMAX x [16][128 B]
+// shared memory: Q double-buffered, key and value blocks in rings of 4 (block j in slot j % 4), the
+// relay slots double-buffered, then the per-tile bookkeeping (double-buffered where tile u + 1 is
+// prepared while tile u runs)
+constexpr uint32_t OFF_Q = 0;                 // 2 x [128][128 B]
+constexpr uint32_t OFF_K = 32768;             // 4 x [128][128 B]
+constexpr uint32_t OFF_V = OFF_K + 65536;     // 4 x [128][128 B]
+constexpr uint32_t OFF_RK = OFF_V + 65536;    // 2 x JMAX x [16][128 B]
+constexpr uint32_t OFF_RV = OFF_RK + 16384;   // 2 x JMAX x [16][128 B]
 constexpr uint32_t OFF_RED = OFF_RV + 16384;  // f32 [2][4][128]: per-group row maxima and sums
-constexpr uint32_t OFF_ROW = OFF_RED + 4096;  // int4 [128]: window columns, relay group, document
-constexpr uint32_t OFF_PR = OFF_ROW + 2048;   // f32 [128][16]: relay weights (CUDA-core relay)
-constexpr uint32_t OFF_DOC = OFF_PR + 8192;   // int [JMAX] documents, int overflow
-constexpr uint32_t OFF_BAR = OFF_DOC + 64;
-constexpr uint32_t SMEM_TC = OFF_BAR + 64 + 1024;  // + alignment slack
+constexpr uint32_t OFF_ROW = OFF_RED + 4096;  // int4 [2][128]: window columns, relay group, document
+constexpr uint32_t OFF_PR = OFF_ROW + 4096;   // f32 [128][16]: relay weights (CUDA-core relay)
+constexpr uint32_t OFF_DOC = OFF_PR + 8192;   // int [2][8]: JMAX documents, overflow flag
+constexpr uint32_t OFF_PAD = OFF_DOC + 64;    // u32 [2][12]: padding bits of the band keys to load
+constexpr uint32_t OFF_META = OFF_PAD + 128;  // int [3][128] rows (start, end, id), [2][384] keys (start, end)
+constexpr uint32_t OFF_BAR = OFF_META + 4608;
+constexpr uint32_t SMEM_TC = OFF_BAR + 128 + 1024;  // + alignment slack
 // TMEM columns: S of the band [0, 384) and of the relay slots [384, 384 + 16 J); once the softmax
 // has read them, P of the band (bf16 pairs) [0, 192), O in two partial sums [192, 256) and
 // [320, 384), P of the relay slots [256, 256 + 8 J)
 constexpr uint32_t TM_SR = 384, TM_O = 192, TM_PR = 256, TM_O2 = 320;
 constexpr uint32_t IDESC_S = umma_idesc_bf16(128, 128, false);
 constexpr uint32_t IDESC_S256 = umma_idesc_bf16(128, 256, false);
-constexpr int ISSUER2 = 128;  // the second MMA-issuing thread (warp 4): the product chains are split in two
 constexpr uint32_t IDESC_O = umma_idesc_bf16(128, 64, true);
+constexpr int ISSUER2 = 128;  // the second MMA-issuing thread (warp 4): the product chains are split in two
+constexpr int LOADER = 256;   // the thread (warp 8) that issues the next tile's copies
 constexpr int kRelayDocError = 101;  // a live row's doc_id outside [0, documents)
 
 struct RelayParams {
@@ -75,6 +83,10 @@ struct RelayParams {
 };
 
 __device__ __forceinline__ uint64_t kdesc(uint32_t saddr) { return umma_sdesc_sw128(saddr, 16, 1024); }
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_u32addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 __device__ __forceinline__ uint64_t mndesc(uint32_t saddr) { return umma_sdesc_sw128(saddr, 16384, 1024); }
 
 // dot of a bf16 row of 64 (eight 16-byte words already in registers) with a bf16 row in memory
@@ -96,6 +108,10 @@ __device__ __forceinline__ float dot64(const uint4 (&qv)[8], const __nv_bfloat16
     return acc;
 }
 
+// The persistent kernel: CTA c takes the tiles [c NT / G, (c + 1) NT / G) of the (b, h)-major tile
+// order, NT = B H ceil(T / 128), G = gridDim.x.  Consecutive tiles of one (b, h) share two of their
+// three key blocks, so a tile loads Q and one new key / value block, issued while the previous tile
+// computes; a change of (b, h) loads all three blocks once the previous tile's products are done.
 __global__ void __launch_bounds__(NTH, 1)
     relay_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_rk,
@@ -104,47 +120,41 @@ __global__ void __launch_bounds__(NTH, 1)
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float* smax = reinterpret_cast<float*>(sm + OFF_RED);  // [4][128]
     float* ssum = smax + 512;                              // [4][128]
-    int4* srow = reinterpret_cast<int4*>(sm + OFF_ROW);
+    int4* srow = reinterpret_cast<int4*>(sm + OFF_ROW);    // [2][128]
     float* spr = reinterpret_cast<float*>(sm + OFF_PR);
-    int* sdocs = reinterpret_cast<int*>(sm + OFF_DOC);
-    int* sover = sdocs + JMAX;
-    uint64_t* bar_ld = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
-    uint64_t* bar_rl = bar_ld + 1;
-    uint64_t* bar_s = bar_ld + 2;
-    uint64_t* bar_o = bar_ld + 3;
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_ld + 4);
+    int* sdoc = reinterpret_cast<int*>(sm + OFF_DOC);      // [2][8]: [0, JMAX) documents, [JMAX] overflow
+    uint32_t* spad = reinterpret_cast<uint32_t*>(sm + OFF_PAD);  // [2][12]
+    uint64_t* bar_ld = reinterpret_cast<uint64_t*>(sm + OFF_BAR);  // [2]
+    uint64_t* bar_rl = bar_ld + 2;                                 // [2]
+    uint64_t* bar_s = bar_ld + 4;
+    uint64_t* bar_o = bar_ld + 5;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_ld + 6);
     int* serr = reinterpret_cast<int*>(tslot + 1);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int qd = warp & 3, g = warp >> 2;     // TMEM lane quarter, column group
-    const int r = 32 * qd + lane;               // the row (query) this thread works on
-    const int T = p.T, tiles = (T + TQ - 1) / TQ;
-    const int tile = blockIdx.x % tiles, bh = blockIdx.x / tiles, b = bh / p.H, h = bh % p.H;
-    const int q0 = tile * TQ, kb0 = q0 - RADIUS;
-    // the metadata loads go out first, so that their latency overlaps the TMEM allocation and the
-    // tile copies: the row's document (column group 0) and whether band key tid is padding
-    int st = 0, en = -1, doc = 0;
-    if (g == 0 && q0 + r < T) {
-        st = p.doc_start[(size_t)b * T + q0 + r];
-        en = p.doc_end[(size_t)b * T + q0 + r];
-        doc = p.doc_id[(size_t)b * T + q0 + r];
-    }
-    bool pad_key = false;
-    if (tid < KB && kb0 + tid >= 0 && kb0 + tid < T)
-        pad_key = p.doc_end[(size_t)b * T + kb0 + tid] < p.doc_start[(size_t)b * T + kb0 + tid];
+    const int r = 32 * qd + lane;               // the row (query of the tile) this thread works on
+    const int T = p.T, tps = (T + TQ - 1) / TQ;
+    const int64_t NT = (int64_t)p.B * p.H * tps;
+    const int64_t ubeg = NT * blockIdx.x / gridDim.x, uend = NT * (blockIdx.x + 1) / gridDim.x;
+    if (ubeg >= uend) return;
 
     if (tid == 0) {
         prefetch_tmap(&tm_q);
         prefetch_tmap(&tm_k);
         prefetch_tmap(&tm_v);
-        mbar_init(bar_ld, 1);
-        mbar_init(bar_rl, 1);
+        prefetch_tmap(&tm_rk);
+        prefetch_tmap(&tm_rv);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&bar_ld[i], 1);
+            mbar_init(&bar_rl[i], 1);
+        }
         mbar_init(bar_s, 2);
         mbar_init(bar_o, 2);
         *serr = 0;
-        *sover = 0;
         fence_mbar_init();
     }
-    if (tid < JMAX) sdocs[tid] = EMPTY_DOC;
+    if (tid < 16) sdoc[tid] = (tid & 7) < JMAX ? EMPTY_DOC : 0;
+    if (tid < 24) spad[tid] = 0u;
     if (warp == 0) {
         tmem_alloc(tslot, 512);
         tmem_relinquish();
@@ -153,290 +163,379 @@ __global__ void __launch_bounds__(NTH, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
-    if (tid == 0) {
-        mbar_arrive_expect_tx(bar_ld, 16384 + 2 * 49152);
-        tma_load_4d(sm + OFF_Q, &tm_q, bar_ld, 0, q0, h, b);
-#pragma unroll
-        for (int j = 0; j < 3; ++j) {
-            tma_load_4d(sm + OFF_K + 16384 * j, &tm_k, bar_ld, 0, kb0 + 128 * j, h, b);
-            tma_load_4d(sm + OFF_V + 16384 * j, &tm_v, bar_ld, 0, kb0 + 128 * j, h, b);
+    const uint32_t trow = tmem + ((uint32_t)(32 * qd) << 16);
+
+    // ---- per-tile preparation, run by column group 0 (thread = row r): the row's window columns and
+    // relay group into srow[buf], its document into sdoc[buf] (deduplicated), and the padding bits of
+    // the band keys this tile loads into spad[buf] (all three blocks, or only the third).  The
+    // metadata arrives by cp.async into shared memory (no register waits on it), each thread
+    // copying and later reading only its own row and keys.
+    int* mrow = reinterpret_cast<int*>(sm + OFF_META);  // [3][128]
+    int* mkey = mrow + 384;                             // [2][384]
+    auto fetch_meta = [&](int bh, int t, bool full) {
+        const int b = bh / p.H, q0 = t * TQ, kb0 = q0 - RADIUS;
+        if (q0 + r < T) {
+            cp_async4(&mrow[r], p.doc_start + (size_t)b * T + q0 + r);
+            cp_async4(&mrow[128 + r], p.doc_end + (size_t)b * T + q0 + r);
+            cp_async4(&mrow[256 + r], p.doc_id + (size_t)b * T + q0 + r);
+        } else {
+            mrow[r] = 0;
+            mrow[128 + r] = -1;
+            mrow[256 + r] = 0;
         }
-    }
-    // row set-up (column group 0): window columns (band index = key - kb0) and the relay group
-    if (g == 0) {
-        const int t = q0 + r;
-        const bool live = t < T && en >= st;
+#pragma unroll
+        for (int jb = 0; jb < 3; ++jb) {
+            const int key = kb0 + 128 * jb + r, kk = 128 * jb + r;
+            if ((full || jb == 2) && key >= 0 && key < T) {
+                cp_async4(&mkey[kk], p.doc_start + (size_t)b * T + key);
+                cp_async4(&mkey[384 + kk], p.doc_end + (size_t)b * T + key);
+            } else {
+                mkey[kk] = 0;
+                mkey[384 + kk] = 0;
+            }
+        }
+    };
+    auto prepare = [&](int t, int buf) {
+        cp_async_wait_all();
+        const int st = mrow[r], en = mrow[128 + r], doc = mrow[256 + r];
+        const int q0 = t * TQ, kb0 = q0 - RADIUS, tq = q0 + r;
+        const bool live = tq < T && en >= st;
         const bool relay_ok = live && doc >= 0 && doc < p.ndoc;
         if (live && !relay_ok) atomicExch(p.err, kRelayDocError);
+        // deduplicate within the warp first: one leader per distinct document takes a slot
+        const unsigned peers = __match_any_sync(0xffffffffu, relay_ok ? doc : -2 - lane);
+        const int leader = __ffs(peers) - 1;
         int jr = -1;
-        if (relay_ok) {
+        if (relay_ok && lane == leader) {
             for (int k = 0; k < JMAX; ++k) {
-                const int prev = atomicCAS(&sdocs[k], EMPTY_DOC, doc);
+                const int prev = atomicCAS(&sdoc[buf * 8 + k], EMPTY_DOC, doc);
                 if (prev == EMPTY_DOC || prev == doc) {
                     jr = k;
                     break;
                 }
             }
-            if (jr < 0) atomicOr(sover, 1);
+            if (jr < 0) atomicOr(&sdoc[buf * 8 + JMAX], 1);
         }
-        const int lo = max(max(t - RADIUS, st), 0), hi = min(min(t + RADIUS, en), T - 1);
-        srow[r] = make_int4(live ? lo - kb0 : 1, live ? hi - kb0 : 0, jr, live ? (relay_ok ? doc : -2) : -1);
-    }
-    __syncthreads();
-    // slots are filled in order, so the documents form a prefix of sdocs
-    int J = 0;
+        jr = __shfl_sync(0xffffffffu, jr, leader);
+        if (!relay_ok) jr = -1;
+        const int lo = max(max(tq - RADIUS, st), 0), hi = min(min(tq + RADIUS, en), T - 1);
+        srow[buf * 128 + r] = make_int4(live ? lo - kb0 : 1, live ? hi - kb0 : 0, jr, live ? (relay_ok ? doc : -2) : -1);
+        unsigned bits[3];
 #pragma unroll
-    for (int k = 0; k < JMAX; ++k) J += sdocs[k] != EMPTY_DOC;
-    const bool tc_relay = *sover == 0;
-    if (tid == 0 && tc_relay && J > 0) {
-        prefetch_tmap(&tm_rk);
-        prefetch_tmap(&tm_rv);
-        mbar_arrive_expect_tx(bar_rl, 2u * 2048u * (uint32_t)J);
-        for (int j = 0; j < J; ++j) {
-            tma_load_4d(sm + OFF_RK + 2048 * j, &tm_rk, bar_rl, 0, 0, h, sdocs[j]);
-            tma_load_4d(sm + OFF_RV + 2048 * j, &tm_rv, bar_rl, 0, 0, h, sdocs[j]);
-        }
-    }
-    const int4 ri = srow[r];
-    const int clo = ri.x, chi = ri.y, jr = ri.z, rdoc = ri.w;
-    const size_t rbase = ((size_t)(rdoc >= 0 ? rdoc : 0) * p.H + h) * SLOTS * D;
-    // more documents than the tensor-core relay holds: relay scores on the CUDA cores
-    float rs[SLOTS];
+        for (int jb = 0; jb < 3; ++jb) bits[jb] = __ballot_sync(0xffffffffu, mkey[384 + 128 * jb + r] < mkey[128 * jb + r]);
+        if (lane == 0) {
 #pragma unroll
-    for (int s = 0; s < SLOTS; ++s) rs[s] = 0.f;
-    if (!tc_relay && g == 0 && rdoc >= 0) {
-        uint4 qv[8];
-        const uint4* qg = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.q) +
-                                                         (((size_t)b * p.H + h) * T + q0 + r) * D);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) qv[i] = qg[i];
-#pragma unroll
-        for (int s = 0; s < SLOTS; ++s)
-            rs[s] = dot64(qv, static_cast<const __nv_bfloat16*>(p.rk) + rbase + s * D) * SCALE;
-    }
-
-    // padding keys: zero their K and V rows once they have landed
-    mbar_wait(bar_ld, 0, serr, 1);
-    if (pad_key) {
-        {
-            uint4* kr = reinterpret_cast<uint4*>(sm + OFF_K + tid * 128);
-            uint4* vr = reinterpret_cast<uint4*>(sm + OFF_V + tid * 128);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) kr[i] = vr[i] = make_uint4(0u, 0u, 0u, 0u);
-        }
-    }
-    fence_proxy_async_smem();
-    __syncthreads();
-    if (tid == 0 || tid == ISSUER2) {
-        // two issuers: band keys [0, 256) as one N = 256 chain; keys [256, 384) and the relay slots
-        tc_fence_after();
-        const uint32_t qa = smem_u32addr(sm + OFF_Q), ka = smem_u32addr(sm + OFF_K);
-        if (tid == 0) {
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-                umma_ss(tmem, kdesc(qa + 32 * kk), kdesc(ka + 32 * kk), IDESC_S256, kk > 0 ? 1u : 0u);
-        } else {
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-                umma_ss(tmem + 256, kdesc(qa + 32 * kk), kdesc(ka + 32768 + 32 * kk), IDESC_S, kk > 0 ? 1u : 0u);
-            if (tc_relay && J > 0) {
-                mbar_wait(bar_rl, 0, serr, 2);
-                tc_fence_after();
-                const uint32_t ra = smem_u32addr(sm + OFF_RK), idesc = umma_idesc_bf16(128, 16 * J, false);
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    umma_ss(tmem + TM_SR, kdesc(qa + 32 * kk), kdesc(ra + 32 * kk), idesc, kk > 0 ? 1u : 0u);
-            }
-        }
-        umma_commit(bar_s);
-    }
-
-    // softmax: this warp reads columns [cb + 16 c0, cb + 16 c1) of its lane quarter's band span
-    mbar_wait(bar_s, 0, serr, 3);
-    tc_fence_after();
-    const uint32_t trow = tmem + ((uint32_t)(32 * qd) << 16);
-    const int cb = 32 * qd, c0 = (18 * g) / 4, c1 = (18 * (g + 1)) / 4;
-    // raw scores: max(s) / 8 is max(s / 8) exactly.  A chunk inside every lane's window (most of
-    // them) takes the unmasked loop.
-    float mraw = -INFINITY;
-    auto max_chunk = [&](const uint32_t (&v)[16], int cs) {
-        if (__all_sync(0xffffffffu, cs >= clo && cs + 15 <= chi)) {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) mraw = fmaxf(mraw, __uint_as_float(v[e]));
-        } else if (!__all_sync(0xffffffffu, cs > chi || cs + 15 < clo)) {
-#pragma unroll
-            for (int e = 0; e < 16; ++e)
-                if (cs + e >= clo && cs + e <= chi) mraw = fmaxf(mraw, __uint_as_float(v[e]));
+            for (int jb = 0; jb < 3; ++jb) spad[buf * 12 + 4 * jb + qd] = bits[jb];
         }
     };
-    // two chunks per TMEM wait
-    for (int c = c0; c < c1; c += 2) {
-        uint32_t v0[16], v1[16];
-        tmem_ld16(trow + cb + 16 * c, v0);
-        if (c + 1 < c1) tmem_ld16(trow + cb + 16 * (c + 1), v1);
-        tmem_ld_wait();
-        max_chunk(v0, cb + 16 * c);
-        if (c + 1 < c1) max_chunk(v1, cb + 16 * (c + 1));
-    }
-    float m = mraw * SCALE;
-    // relay scores (column group 0): this row's document group of the relay columns
-    if (g == 0) {
-        if (tc_relay) {
+    // TMA of tile (bh, t)'s Q and its new key / value blocks
+    auto load_tile = [&](int bh, int t, int buf, bool full) {
+        const int b = bh / p.H, h = bh % p.H;
+        mbar_arrive_expect_tx(&bar_ld[buf], 16384u + (full ? 3u : 1u) * 32768u);
+        tma_load_4d(sm + OFF_Q + 16384 * buf, &tm_q, &bar_ld[buf], 0, t * TQ, h, b);
+        for (int jb = full ? 0 : 2; jb < 3; ++jb) {
+            const int blk = t - 1 + jb, slot = blk & 3;
+            tma_load_4d(sm + OFF_K + 16384 * slot, &tm_k, &bar_ld[buf], 0, 128 * blk, h, b);
+            tma_load_4d(sm + OFF_V + 16384 * slot, &tm_v, &bar_ld[buf], 0, 128 * blk, h, b);
+        }
+    };
+    // TMA of tile (bh, t)'s relay slots; armed with zero bytes when the tile has none, so that every
+    // tile completes one phase of bar_rl[buf]
+    auto load_relay = [&](int bh, int buf) {
+        const int h = bh % p.H;
+        int J = 0;
+        for (int k = 0; k < JMAX; ++k) J += sdoc[buf * 8 + k] != EMPTY_DOC;
+        const bool tc = sdoc[buf * 8 + JMAX] == 0;
+        mbar_arrive_expect_tx(&bar_rl[buf], tc ? 4096u * (uint32_t)J : 0u);
+        if (tc)
             for (int j = 0; j < J; ++j) {
-                uint32_t v[16];
-                tmem_ld16(trow + TM_SR + 16 * j, v);
-                tmem_ld_wait();
-                if (j == jr) {
+                tma_load_4d(sm + OFF_RK + 8192 * buf + 2048 * j, &tm_rk, &bar_rl[buf], 0, 0, h, sdoc[buf * 8 + j]);
+                tma_load_4d(sm + OFF_RV + 8192 * buf + 2048 * j, &tm_rv, &bar_rl[buf], 0, 0, h, sdoc[buf * 8 + j]);
+            }
+    };
+
+    int cur_bh = (int)(ubeg / tps), cur_t = (int)(ubeg % tps);
+    if (g == 0) {
+        fetch_meta(cur_bh, cur_t, true);
+        prepare(cur_t, 0);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        load_tile(cur_bh, cur_t, 0, true);
+        load_relay(cur_bh, 0);
+    }
+
+    const int ntile = (int)(uend - ubeg);
+    for (int i = 0; i < ntile; ++i) {
+        const int buf = i & 1;
+        const uint32_t ph2 = (uint32_t)(i >> 1) & 1u, ph1 = (uint32_t)i & 1u;
+        const int bh = cur_bh, t = cur_t, b = bh / p.H, h = bh % p.H;
+        const int q0 = t * TQ;
+        const bool has_next = i + 1 < ntile, next_same = has_next && t + 1 < tps;
+        const int nbh = next_same ? bh : bh + 1, nt = next_same ? t + 1 : 0;
+        int J = 0;
 #pragma unroll
-                    for (int s = 0; s < SLOTS; ++s) rs[s] = __uint_as_float(v[s]) * SCALE;
+        for (int k = 0; k < JMAX; ++k) J += sdoc[buf * 8 + k] != EMPTY_DOC;
+        const bool tc_relay = sdoc[buf * 8 + JMAX] == 0;
+        const int4 ri = srow[buf * 128 + r];
+        const int clo = ri.x, chi = ri.y, jr = ri.z, rdoc = ri.w;
+        const size_t rbase = ((size_t)(rdoc >= 0 ? rdoc : 0) * p.H + h) * SLOTS * D;
+        // the next tile's metadata copies go out now; they are used while this tile's O products run
+        if (g == 0 && has_next) fetch_meta(nbh, nt, !next_same);
+
+        // the tile's copies have landed: zero the rows of padding keys among the new blocks
+        mbar_wait(&bar_ld[buf], ph2, serr, 1);
+        if (tid < KB && (spad[buf * 12 + tid / 32] >> (tid & 31) & 1u)) {
+            const int slot = (t - 1 + tid / 128) & 3;
+            uint4* kr = reinterpret_cast<uint4*>(sm + OFF_K + 16384 * slot + (tid & 127) * 128);
+            uint4* vr = reinterpret_cast<uint4*>(sm + OFF_V + 16384 * slot + (tid & 127) * 128);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) kr[e] = vr[e] = make_uint4(0u, 0u, 0u, 0u);
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        // the other buffer's bookkeeping is free (tile u - 1 is complete): clear it for tile u + 1
+        if (tid < 8) sdoc[(buf ^ 1) * 8 + tid] = tid < JMAX ? EMPTY_DOC : 0;
+        if (tid >= 32 && tid < 44) spad[(buf ^ 1) * 12 + tid - 32] = 0u;
+        if (tid == 0 || tid == ISSUER2) {
+            // two chains over the three band blocks: the two blocks that sit in adjacent ring slots
+            // go as one N = 256 product (blocks t - 1, t unless block t - 1 is in the last slot)
+            const uint32_t qa = smem_u32addr(sm + OFF_Q + 16384 * buf), ka = smem_u32addr(sm + OFF_K);
+            const bool lead_pair = ((t - 1) & 3) != 3;
+            const bool mine_wide = (tid == 0) == lead_pair;  // this issuer takes the N = 256 chain
+            const int jb0 = tid == 0 ? 0 : (lead_pair ? 2 : 1);
+            const uint32_t idesc = mine_wide ? IDESC_S256 : IDESC_S;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+                umma_ss(tmem + 128 * jb0, kdesc(qa + 32 * kk), kdesc(ka + 16384 * ((t - 1 + jb0) & 3) + 32 * kk), idesc,
+                        kk > 0 ? 1u : 0u);
+            if (tid == ISSUER2) {
+                mbar_wait(&bar_rl[buf], ph2, serr, 2);
+                if (tc_relay && J > 0) {
+                    tc_fence_after();
+                    const uint32_t ra = smem_u32addr(sm + OFF_RK + 8192 * buf), idesc = umma_idesc_bf16(128, 16 * J, false);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma_ss(tmem + TM_SR, kdesc(qa + 32 * kk), kdesc(ra + 32 * kk), idesc, kk > 0 ? 1u : 0u);
                 }
             }
+            umma_commit(bar_s);
         }
-        if (rdoc >= 0) {
+        // the next tile of this (b, h) needs Q and one new block, whose slots tile u - 1 has released
+        if (tid == LOADER && next_same) load_tile(nbh, nt, buf ^ 1, false);
+        // more documents than the tensor-core relay holds: relay scores on the CUDA cores
+        float rs[SLOTS];
 #pragma unroll
-            for (int s = 0; s < SLOTS; ++s) m = fmaxf(m, rs[s]);
+        for (int s = 0; s < SLOTS; ++s) rs[s] = 0.f;
+        if (!tc_relay && g == 0 && rdoc >= 0) {
+            uint4 qv[8];
+            const uint4* qg = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.q) +
+                                                             (((size_t)b * p.H + h) * T + q0 + r) * D);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) qv[e] = qg[e];
+#pragma unroll
+            for (int s = 0; s < SLOTS; ++s)
+                rs[s] = dot64(qv, static_cast<const __nv_bfloat16*>(p.rk) + rbase + s * D) * SCALE;
         }
-    }
-    smax[g * 128 + r] = m;
-    __syncthreads();
-    m = fmaxf(fmaxf(smax[r], smax[128 + r]), fmaxf(smax[256 + r], smax[384 + r]));
-    float total = 0.f;
-    uint32_t pk[5][8];
-    // p = exp(s / 8 - m) packed to bf16 pairs; s / 8 - m is formed exactly before the exponential
-    // (scores far below zero stay exact)
-    auto exp_chunk = [&](const uint32_t (&v)[16], int cs, uint32_t (&out)[8]) {
-        if (__all_sync(0xffffffffu, cs >= clo && cs + 15 <= chi)) {
+
+        // ---- softmax: this warp reads columns [cb + 16 c0, cb + 16 c1) of its lane quarter's band span
+        mbar_wait(bar_s, ph1, serr, 3);
+        tc_fence_after();
+        const int cb = 32 * qd, c0 = (18 * g) / 4, c1 = (18 * (g + 1)) / 4;
+        // raw scores: max(s) / 8 is max(s / 8) exactly.  A chunk inside every lane's window (most of
+        // them) takes the unmasked loop; one outside every window is skipped.
+        float mraw = -INFINITY;
+        auto max_chunk = [&](const uint32_t (&v)[16], int cs) {
+            if (__all_sync(0xffffffffu, cs >= clo && cs + 15 <= chi)) {
 #pragma unroll
-            for (int e = 0; e < 16; e += 2) {
-                const float p0 = __expf(fmaf(__uint_as_float(v[e]), SCALE, -m));
-                const float p1 = __expf(fmaf(__uint_as_float(v[e + 1]), SCALE, -m));
-                total += p0 + p1;
-                out[e / 2] = pack_bf16x2(p0, p1);
+                for (int e = 0; e < 16; ++e) mraw = fmaxf(mraw, __uint_as_float(v[e]));
+            } else if (!__all_sync(0xffffffffu, cs > chi || cs + 15 < clo)) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                    if (cs + e >= clo && cs + e <= chi) mraw = fmaxf(mraw, __uint_as_float(v[e]));
             }
-        } else if (__all_sync(0xffffffffu, cs > chi || cs + 15 < clo)) {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) out[e] = 0u;
-        } else {
-#pragma unroll
-            for (int e = 0; e < 16; e += 2) {
-                const int col = cs + e;
-                const float p0 = (col >= clo && col <= chi) ? __expf(fmaf(__uint_as_float(v[e]), SCALE, -m)) : 0.f;
-                const float p1 =
-                    (col + 1 >= clo && col + 1 <= chi) ? __expf(fmaf(__uint_as_float(v[e + 1]), SCALE, -m)) : 0.f;
-                total += p0 + p1;
-                out[e / 2] = pack_bf16x2(p0, p1);
-            }
-        }
-    };
-#pragma unroll
-    for (int i = 0; i < 5; i += 2) {
-        const int c = c0 + i;
-        if (c < c1) {
+        };
+        for (int c = c0; c < c1; c += 2) {  // two chunks per TMEM wait
             uint32_t v0[16], v1[16];
             tmem_ld16(trow + cb + 16 * c, v0);
             if (c + 1 < c1) tmem_ld16(trow + cb + 16 * (c + 1), v1);
             tmem_ld_wait();
-            exp_chunk(v0, cb + 16 * c, pk[i]);
-            if (i + 1 < 5 && c + 1 < c1) exp_chunk(v1, cb + 16 * (c + 1), pk[i + 1]);
+            max_chunk(v0, cb + 16 * c);
+            if (c + 1 < c1) max_chunk(v1, cb + 16 * (c + 1));
         }
-    }
-    uint32_t prk[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-    if (g == 0 && rdoc >= 0) {
-        float pr[SLOTS];
+        float m = mraw * SCALE;
+        // relay scores (column group 0): this row's document group of the relay columns
+        if (g == 0) {
+            if (tc_relay) {
+                for (int j = 0; j < J; ++j) {
+                    uint32_t v[16];
+                    tmem_ld16(trow + TM_SR + 16 * j, v);
+                    tmem_ld_wait();
+                    if (j == jr) {
 #pragma unroll
-        for (int s = 0; s < SLOTS; ++s) {
-            pr[s] = __expf(rs[s] - m);
-            total += pr[s];
-        }
+                        for (int s = 0; s < SLOTS; ++s) rs[s] = __uint_as_float(v[s]) * SCALE;
+                    }
+                }
+            }
+            if (rdoc >= 0) {
 #pragma unroll
-        for (int u = 0; u < 8; ++u) prk[u] = pack_bf16x2(pr[2 * u], pr[2 * u + 1]);
-        if (!tc_relay) {
-#pragma unroll
-            for (int s = 0; s < SLOTS; ++s) spr[r * SLOTS + s] = pr[s];
-        }
-    }
-    ssum[g * 128 + r] = total;
-    tc_fence_before();
-    __syncthreads();  // every read of S is complete: P may now overwrite it
-    tc_fence_after();
-#pragma unroll
-    for (int i = 0; i < 5; ++i)
-        if (c0 + i < c1) tmem_st8(trow + (uint32_t)(16 * qd + 8 * (c0 + i)), pk[i]);
-    {
-        // P columns outside the lane quarter's span [16 qd, 16 qd + 144) are zero: six groups of 8
-        const uint32_t zero[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-        for (int zc = g; zc < 6; zc += 4) {
-            const int col = zc < 2 * qd ? 8 * zc : 16 * qd + 144 + 8 * (zc - 2 * qd);
-            tmem_st8(trow + (uint32_t)col, zero);
-        }
-        if (g == 0 && tc_relay) {
-            // one warp-wide store per document group; each lane supplies its row's values
-            for (int j = 0; j < J; ++j) {
-                uint32_t val[8];
-#pragma unroll
-                for (int u = 0; u < 8; ++u) val[u] = j == jr ? prk[u] : 0u;
-                tmem_st8(trow + TM_PR + 8 * j, val);
+                for (int s = 0; s < SLOTS; ++s) m = fmaxf(m, rs[s]);
             }
         }
-    }
-    tmem_st_wait();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0 || tid == ISSUER2) {
-        // two partial sums: band keys [0, 192) and the relay slots into [192, 256), keys [192, 384)
-        // into [320, 384)
-        tc_fence_after();
-        const uint32_t va = smem_u32addr(sm + OFF_V), rva = smem_u32addr(sm + OFF_RV);
-        const int k0 = tid == 0 ? 0 : KB / 32;
-        const uint32_t dst = tmem + (tid == 0 ? TM_O : TM_O2);
+        smax[g * 128 + r] = m;
+        __syncthreads();
+        m = fmaxf(fmaxf(smax[r], smax[128 + r]), fmaxf(smax[256 + r], smax[384 + r]));
+        float total = 0.f;
+        uint32_t pk[5][8];
+        // p = exp(s / 8 - m) packed to bf16 pairs; s / 8 - m is formed exactly before the
+        // exponential (scores far below zero stay exact)
+        auto exp_chunk = [&](const uint32_t (&v)[16], int cs, uint32_t (&out)[8]) {
+            if (__all_sync(0xffffffffu, cs >= clo && cs + 15 <= chi)) {
 #pragma unroll
-        for (int i = 0; i < KB / 32; ++i)
-            umma_ts(dst, tmem + 8 * (k0 + i), mndesc(va + 2048 * (k0 + i)), IDESC_O, i > 0 ? 1u : 0u);
-        if (tid == 0 && tc_relay)
-            for (int j = 0; j < J; ++j) umma_ts(dst, tmem + TM_PR + 8 * j, mndesc(rva + 2048 * j), IDESC_O, 1u);
-        umma_commit(bar_o);
-    }
-    mbar_wait(bar_o, 0, serr, 4);
-    tc_fence_after();
-    // epilogue: column group g stores output channels 16 g .. 16 g + 15 of its row
-    uint32_t v[16], v2[16];
-    tmem_ld16(trow + TM_O + 16 * g, v);
-    tmem_ld16(trow + TM_O2 + 16 * g, v2);
-    tmem_ld_wait();
-    const int t = q0 + r;
-    if (t < T) {
-        const bool live = rdoc != -1;
-        const float tot = ssum[r] + ssum[128 + r] + ssum[256 + r] + ssum[384 + r];
-        float o[16];
+                for (int e = 0; e < 16; e += 2) {
+                    const float p0 = __expf(fmaf(__uint_as_float(v[e]), SCALE, -m));
+                    const float p1 = __expf(fmaf(__uint_as_float(v[e + 1]), SCALE, -m));
+                    total += p0 + p1;
+                    out[e / 2] = pack_bf16x2(p0, p1);
+                }
+            } else if (__all_sync(0xffffffffu, cs > chi || cs + 15 < clo)) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) o[e] = __uint_as_float(v[e]) + __uint_as_float(v2[e]);
-        if (!tc_relay && rdoc >= 0) {
-            const __nv_bfloat16* rv = static_cast<const __nv_bfloat16*>(p.rv) + rbase + 16 * g;
-#pragma unroll 4
+                for (int e = 0; e < 8; ++e) out[e] = 0u;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 16; e += 2) {
+                    const int col = cs + e;
+                    const float p0 = (col >= clo && col <= chi) ? __expf(fmaf(__uint_as_float(v[e]), SCALE, -m)) : 0.f;
+                    const float p1 =
+                        (col + 1 >= clo && col + 1 <= chi) ? __expf(fmaf(__uint_as_float(v[e + 1]), SCALE, -m)) : 0.f;
+                    total += p0 + p1;
+                    out[e / 2] = pack_bf16x2(p0, p1);
+                }
+            }
+        };
+#pragma unroll
+        for (int k = 0; k < 5; k += 2) {
+            const int c = c0 + k;
+            if (c < c1) {
+                uint32_t v0[16], v1[16];
+                tmem_ld16(trow + cb + 16 * c, v0);
+                if (c + 1 < c1) tmem_ld16(trow + cb + 16 * (c + 1), v1);
+                tmem_ld_wait();
+                exp_chunk(v0, cb + 16 * c, pk[k]);
+                if (k + 1 < 5 && c + 1 < c1) exp_chunk(v1, cb + 16 * (c + 1), pk[k + 1]);
+            }
+        }
+        uint32_t prk[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+        if (g == 0 && rdoc >= 0) {
+            float pr[SLOTS];
+#pragma unroll
             for (int s = 0; s < SLOTS; ++s) {
-                const float w = spr[r * SLOTS + s];
-                const uint4* vg = reinterpret_cast<const uint4*>(rv + s * D);
-                const uint4 a = __ldg(vg), c = __ldg(vg + 1);
-                o[0] = fmaf(w, bf16_lo(a.x), o[0]);   o[1] = fmaf(w, bf16_hi(a.x), o[1]);
-                o[2] = fmaf(w, bf16_lo(a.y), o[2]);   o[3] = fmaf(w, bf16_hi(a.y), o[3]);
-                o[4] = fmaf(w, bf16_lo(a.z), o[4]);   o[5] = fmaf(w, bf16_hi(a.z), o[5]);
-                o[6] = fmaf(w, bf16_lo(a.w), o[6]);   o[7] = fmaf(w, bf16_hi(a.w), o[7]);
-                o[8] = fmaf(w, bf16_lo(c.x), o[8]);   o[9] = fmaf(w, bf16_hi(c.x), o[9]);
-                o[10] = fmaf(w, bf16_lo(c.y), o[10]); o[11] = fmaf(w, bf16_hi(c.y), o[11]);
-                o[12] = fmaf(w, bf16_lo(c.z), o[12]); o[13] = fmaf(w, bf16_hi(c.z), o[13]);
-                o[14] = fmaf(w, bf16_lo(c.w), o[14]); o[15] = fmaf(w, bf16_hi(c.w), o[15]);
+                pr[s] = __expf(rs[s] - m);
+                total += pr[s];
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) prk[e] = pack_bf16x2(pr[2 * e], pr[2 * e + 1]);
+            if (!tc_relay) {
+#pragma unroll
+                for (int s = 0; s < SLOTS; ++s) spr[r * SLOTS + s] = pr[s];
             }
         }
-        const size_t row = ((size_t)b * p.H + h) * T + t;
-        const float inv = live ? 1.f / tot : 0.f;
-        uint4* og = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.o) + row * D + 16 * g);
-        og[0] = make_uint4(pack_bf16x2(o[0] * inv, o[1] * inv), pack_bf16x2(o[2] * inv, o[3] * inv),
-                           pack_bf16x2(o[4] * inv, o[5] * inv), pack_bf16x2(o[6] * inv, o[7] * inv));
-        og[1] = make_uint4(pack_bf16x2(o[8] * inv, o[9] * inv), pack_bf16x2(o[10] * inv, o[11] * inv),
-                           pack_bf16x2(o[12] * inv, o[13] * inv), pack_bf16x2(o[14] * inv, o[15] * inv));
-        if (g == 0) reinterpret_cast<float2*>(p.norm)[row] = live ? make_float2(m, tot) : make_float2(0.f, 1.f);
+        ssum[g * 128 + r] = total;
+        tc_fence_before();
+        __syncthreads();  // every read of S is complete: P may now overwrite it
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 5; ++k)
+            if (c0 + k < c1) tmem_st8(trow + (uint32_t)(16 * qd + 8 * (c0 + k)), pk[k]);
+        {
+            // P columns outside the lane quarter's span [16 qd, 16 qd + 144) are zero: six groups of 8
+            const uint32_t zero[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+            for (int zc = g; zc < 6; zc += 4) {
+                const int col = zc < 2 * qd ? 8 * zc : 16 * qd + 144 + 8 * (zc - 2 * qd);
+                tmem_st8(trow + (uint32_t)col, zero);
+            }
+            if (g == 0 && tc_relay) {
+                // one warp-wide store per document group; each lane supplies its row's values
+                for (int j = 0; j < J; ++j) {
+                    uint32_t val[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) val[e] = j == jr ? prk[e] : 0u;
+                    tmem_st8(trow + TM_PR + 8 * j, val);
+                }
+            }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0 || tid == ISSUER2) {
+            // two partial sums: band keys [0, 192) and the relay slots into [192, 256), keys
+            // [192, 384) into [320, 384)
+            tc_fence_after();
+            const uint32_t va = smem_u32addr(sm + OFF_V), rva = smem_u32addr(sm + OFF_RV + 8192 * buf);
+            const int k0 = tid == 0 ? 0 : KB / 32;
+            const uint32_t dst = tmem + (tid == 0 ? TM_O : TM_O2);
+#pragma unroll
+            for (int k = 0; k < KB / 32; ++k) {
+                const int kk = k0 + k;  // 16 band keys: block kk / 8, rows 16 (kk % 8) ..
+                umma_ts(dst, tmem + 8 * kk, mndesc(va + 16384 * ((t - 1 + kk / 8) & 3) + 2048 * (kk & 7)), IDESC_O,
+                        k > 0 ? 1u : 0u);
+            }
+            if (tid == 0 && tc_relay)
+                for (int j = 0; j < J; ++j) umma_ts(dst, tmem + TM_PR + 8 * j, mndesc(rva + 2048 * j), IDESC_O, 1u);
+            umma_commit(bar_o);
+        }
+        // while the products run: the next tile's preparation, then its relay copies
+        if (g == 0 && has_next) prepare(nt, buf ^ 1);
+        __syncthreads();
+        if (tid == LOADER && has_next) load_relay(nbh, buf ^ 1);
+        mbar_wait(bar_o, ph1, serr, 4);
+        tc_fence_after();
+        // epilogue: column group g stores output channels 16 g .. 16 g + 15 of its row
+        uint32_t v[16], v2[16];
+        tmem_ld16(trow + TM_O + 16 * g, v);
+        tmem_ld16(trow + TM_O2 + 16 * g, v2);
+        tmem_ld_wait();
+        // a new (b, h): every ring slot is free now that this tile's products are done
+        if (tid == 0 && has_next && !next_same) load_tile(nbh, nt, buf ^ 1, true);
+        const int tq = q0 + r;
+        if (tq < T) {
+            const bool live = rdoc != -1;
+            const float tot = ssum[r] + ssum[128 + r] + ssum[256 + r] + ssum[384 + r];
+            float o[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) o[e] = __uint_as_float(v[e]) + __uint_as_float(v2[e]);
+            if (!tc_relay && rdoc >= 0) {
+                const __nv_bfloat16* rv = static_cast<const __nv_bfloat16*>(p.rv) + rbase + 16 * g;
+#pragma unroll 4
+                for (int s = 0; s < SLOTS; ++s) {
+                    const float w = spr[r * SLOTS + s];
+                    const uint4* vg = reinterpret_cast<const uint4*>(rv + s * D);
+                    const uint4 a = __ldg(vg), c = __ldg(vg + 1);
+                    o[0] = fmaf(w, bf16_lo(a.x), o[0]);   o[1] = fmaf(w, bf16_hi(a.x), o[1]);
+                    o[2] = fmaf(w, bf16_lo(a.y), o[2]);   o[3] = fmaf(w, bf16_hi(a.y), o[3]);
+                    o[4] = fmaf(w, bf16_lo(a.z), o[4]);   o[5] = fmaf(w, bf16_hi(a.z), o[5]);
+                    o[6] = fmaf(w, bf16_lo(a.w), o[6]);   o[7] = fmaf(w, bf16_hi(a.w), o[7]);
+                    o[8] = fmaf(w, bf16_lo(c.x), o[8]);   o[9] = fmaf(w, bf16_hi(c.x), o[9]);
+                    o[10] = fmaf(w, bf16_lo(c.y), o[10]); o[11] = fmaf(w, bf16_hi(c.y), o[11]);
+                    o[12] = fmaf(w, bf16_lo(c.z), o[12]); o[13] = fmaf(w, bf16_hi(c.z), o[13]);
+                    o[14] = fmaf(w, bf16_lo(c.w), o[14]); o[15] = fmaf(w, bf16_hi(c.w), o[15]);
+                }
+            }
+            const size_t row = ((size_t)b * p.H + h) * T + tq;
+            const float inv = live ? 1.f / tot : 0.f;
+            uint4* og = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.o) + row * D + 16 * g);
+            og[0] = make_uint4(pack_bf16x2(o[0] * inv, o[1] * inv), pack_bf16x2(o[2] * inv, o[3] * inv),
+                               pack_bf16x2(o[4] * inv, o[5] * inv), pack_bf16x2(o[6] * inv, o[7] * inv));
+            og[1] = make_uint4(pack_bf16x2(o[8] * inv, o[9] * inv), pack_bf16x2(o[10] * inv, o[11] * inv),
+                               pack_bf16x2(o[12] * inv, o[13] * inv), pack_bf16x2(o[14] * inv, o[15] * inv));
+            if (g == 0) reinterpret_cast<float2*>(p.norm)[row] = live ? make_float2(m, tot) : make_float2(0.f, 1.f);
+        }
+        tc_fence_before();
+        cur_bh = nbh;
+        cur_t = nt;
     }
-    tc_fence_before();
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
@@ -621,7 +720,13 @@ extern "C" int dbl_relay_attention_forward(const dbl_relay_attention_args* a, db
         if (e != cudaSuccess) return cuda_status(e, "relay_attention_forward: cudaFuncSetAttribute");
         attr_set = true;
     }
-    const size_t tiles = (size_t)(p.T + TQ - 1) / TQ;
-    relay_attn_tc_kernel<<<(unsigned)(tiles * p.B * p.H), NTH, SMEM_TC, st>>>(mq, mk, mv, mrk, mrv, p);
+    // persistent: one CTA per SM (or per tile when there are fewer tiles)
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_status(e, "relay_attention_forward: device query");
+    const int64_t ntiles = (int64_t)p.B * p.H * ((p.T + TQ - 1) / TQ);
+    const unsigned grid = (unsigned)std::min<int64_t>(ntiles, (int64_t)sms);
+    relay_attn_tc_kernel<<<grid, NTH, SMEM_TC, st>>>(mq, mk, mv, mrk, mrv, p);
     return launch_status("relay_attn_tc_kernel");
 }
