@@ -70,6 +70,14 @@ __host__ __device__ __forceinline__ Layout layout(int K, int V, int W, int es) {
 
 // e^-x overflows to +inf below x = -88.7; __fdividef(., inf) is 0, the correct limit of both
 __device__ __forceinline__ float siluf(float x) { return __fdividef(x, 1.f + __expf(-x)); }
+// silu(x) = x/2 (1 + tanh(x/2)) on the hardware tanh (one MUFU operation; relative error about
+// 2^-11), used only where the result is rounded to bf16 (relative step 2^-8)
+__device__ __forceinline__ float silu_bf16out(float x) {
+    float th;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(th) : "f"(0.5f * x));
+    const float hx = 0.5f * x;
+    return fmaf(hx, th, hx);
+}
 __device__ __forceinline__ float sigmoidf(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 
 // log1p(v) for v in [0, 1] by log1p(v) = log((1 + s) / (1 - s)) = 2 atanh(s), s = v / (2 + v) in
@@ -264,7 +272,8 @@ __device__ __forceinline__ void conv_row(const TI* xs, const float* ws, int C, i
             }
 #pragma unroll
             for (int e = 0; e < E; ++e) {
-                y[u][e] = siluf(y[u][e]);
+                if constexpr (sizeof(TO) == 2) y[u][e] = silu_bf16out(y[u][e]);
+                else y[u][e] = siluf(y[u][e]);
                 ss = fmaf(y[u][e], y[u][e], ss);
             }
         }
@@ -278,11 +287,13 @@ __device__ __forceinline__ void conv_row(const TI* xs, const float* ws, int C, i
     }
 }
 
-template <typename TI, typename TO, bool VEC, int WT>
+// WT > 0 fixes the conv width and CT > 0 the key and value widths (K = V = CT) at compile time, so
+// that the index arithmetic of the common shape folds to shifts; 0 reads them from p.
+template <typename TI, typename TO, bool VEC, int WT, int CT>
 __global__ void __launch_bounds__(THREADS, sizeof(TI) == 2 ? 4 : 3) prologue_kernel(const ProParams p) {
     extern __shared__ __align__(16) unsigned char smraw[];
     constexpr int E = VEC ? 4 : 1;
-    const int K = p.K, V = p.V, W = p.W, T = p.T;
+    const int K = CT > 0 ? CT : p.K, V = CT > 0 ? CT : p.V, W = WT > 0 ? WT : p.W, T = p.T;
     const Layout L = layout(K, V, W, (int)sizeof(TI));
     TI* xq = reinterpret_cast<TI*>(smraw + L.xq);
     TI* xk = reinterpret_cast<TI*>(smraw + L.xk);
@@ -427,16 +438,16 @@ __global__ void __launch_bounds__(THREADS, sizeof(TI) == 2 ? 4 : 3) prologue_ker
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
-template <typename TI, typename TO, bool VEC, int WT>
+template <typename TI, typename TO, bool VEC, int WT, int CT = 0>
 cudaError_t launch_v(const ProParams& p, cudaStream_t st) {
     const size_t smem = layout(p.K, p.V, p.W, (int)sizeof(TI)).total;
     if (smem > 48 * 1024) {
-        const cudaError_t e = cudaFuncSetAttribute(prologue_kernel<TI, TO, VEC, WT>,
+        const cudaError_t e = cudaFuncSetAttribute(prologue_kernel<TI, TO, VEC, WT, CT>,
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
     const size_t tiles = (size_t)(p.T + TT - 1) / TT;
-    prologue_kernel<TI, TO, VEC, WT><<<(unsigned)(tiles * p.B * p.H), THREADS, smem, st>>>(p);
+    prologue_kernel<TI, TO, VEC, WT, CT><<<(unsigned)(tiles * p.B * p.H), THREADS, smem, st>>>(p);
     return cudaGetLastError();
 }
 
@@ -447,6 +458,7 @@ cudaError_t launch(const ProParams& p, cudaStream_t st) {
                      aligned16(p.cv) && aligned16(p.bias) && aligned16(p.q) && aligned16(p.k) && aligned16(p.v) &&
                      aligned16(p.alpha) && aligned16(p.erase) && aligned16(p.write);
     if (!vec) return launch_v<TI, TO, false, 0>(p, st);
+    if (p.W == 4 && p.K == 128 && p.V == 128) return launch_v<TI, TO, true, 4, 128>(p, st);
     return p.W == 4 ? launch_v<TI, TO, true, 4>(p, st) : launch_v<TI, TO, true, 0>(p, st);
 }
 
