@@ -108,6 +108,16 @@ class RelayMergeArgs(ctypes.Structure):
     ]
 
 
+class Gdn2ScanBackwardArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", _i64), ("time", _i64), ("heads", _i64), ("key_dim", _i64), ("value_dim", _i64),
+        ("dtype", _i32),
+        ("q", _vp), ("k", _vp), ("v", _vp), ("alpha", _vp), ("erase", _vp), ("write", _vp),
+        ("doc_start", _vp), ("doc_end", _vp), ("grad_output", _vp),
+        ("dq", _vp), ("dk", _vp), ("dv", _vp), ("dalpha", _vp), ("derase", _vp), ("dwrite", _vp),
+    ]
+
+
 class RelayAttentionArgs(ctypes.Structure):
     _fields_ = [
         ("batch", _i64), ("heads", _i64), ("time", _i64), ("head_dim", _i64), ("documents", _i64),
@@ -131,6 +141,8 @@ EXPORTS = [
     ("dbl_gdn_training_scan_backward_workspace_bytes", ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64, _i32]),
     ("dbl_gdn_training_scan_backward", ctypes.c_int,
      [ctypes.POINTER(TrainingScanBackwardArgs), _vp, ctypes.c_size_t, _vp]),
+    ("dbl_gdn2_scan_backward_workspace_bytes", ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64, _i32]),
+    ("dbl_gdn2_scan_backward", ctypes.c_int, [ctypes.POINTER(Gdn2ScanBackwardArgs), _vp, ctypes.c_size_t, _vp]),
     ("dbl_gdn2_prologue", ctypes.c_int, [ctypes.POINTER(Gdn2PrologueArgs), _vp]),
     ("dbl_gdn2_scan", ctypes.c_int, [ctypes.POINTER(Gdn2ScanArgs), _vp]),
     ("dbl_relay_merge_workspace_bytes", ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64]),

@@ -19,6 +19,10 @@
 //             A = alpha (.) dbar.
 // The sums over j use a warp butterfly reduce-scatter (lane L ends with the sum for index L of a
 // block of 32) and one shared-memory pass across warps.  f32 throughout, as the reference.
+#include <cuda_bf16.h>
+
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace dbl {
@@ -318,4 +322,136 @@ extern "C" int dbl_gdn_training_scan_backward(const dbl_training_scan_backward_a
     else training_backward_kernel<64><<<(unsigned)heads, threads, 0, st>>>(p);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? DBL_OK : cuda_status(e, "gdn_training_scan_backward launch");
+}
+
+// ------------------------------------------------------------------------------ gdn2_scan backward
+// The output-only scan with inclusive document limits (dbl_gdn2_scan) is the stateful scan with
+// valid = (doc_end >= doc_start), reset = (doc_start == t), a zero initial state and no final state
+// or scores, so its backward (gdn2_backward, crates/kernels/src/gdn2.rs:285-519, wired at
+// ops.rs:106-160) is the kernel above on those masks, with zero final-state and score gradients.
+namespace dbl {
+namespace {
+
+__global__ void limits_to_masks_kernel(const int32_t* start, const int32_t* end, int64_t B, int64_t T, float* valid,
+                                       float* reset) {
+    const int64_t x = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (x >= B * T) return;
+    const int t = (int)(x % T);
+    valid[x] = end[x] >= start[x] ? 1.f : 0.f;
+    reset[x] = start[x] == t ? 1.f : 0.f;
+}
+__global__ void widen_bf16_kernel(const __nv_bfloat16* in, float* out, int64_t n) {
+    for (int64_t x = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; x < n; x += (int64_t)gridDim.x * blockDim.x)
+        out[x] = __bfloat162float(in[x]);
+}
+__global__ void narrow_bf16_kernel(const float* in, __nv_bfloat16* out, int64_t n) {
+    for (int64_t x = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; x < n; x += (int64_t)gridDim.x * blockDim.x)
+        out[x] = __float2bfloat16_rn(in[x]);
+}
+
+constexpr int GDN2_CHUNK = 16;  // gdn2.rs: C = 16
+size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct Gdn2BwdLayout {
+    size_t valid, reset, q, k, v, go, dq, dk, dv, train, total;
+};
+Gdn2BwdLayout gdn2_bwd_layout(int64_t B, int64_t T, int64_t H, int64_t K, int64_t V, int dtype) {
+    Gdn2BwdLayout L{};
+    const size_t bt = (size_t)(B * T), nk = (size_t)(B * T * H * K) * 4, nv = (size_t)(B * T * H * V) * 4;
+    const bool wide = dtype == DBL_BF16;
+    size_t o = 0;
+    L.valid = o; o += al256(bt * 4);
+    L.reset = o; o += al256(bt * 4);
+    L.q = o; o += wide ? al256(nk) : 0;
+    L.k = o; o += wide ? al256(nk) : 0;
+    L.v = o; o += wide ? al256(nv) : 0;
+    L.go = o; o += wide ? al256(nv) : 0;
+    L.dq = o; o += wide ? al256(nk) : 0;
+    L.dk = o; o += wide ? al256(nk) : 0;
+    L.dv = o; o += wide ? al256(nv) : 0;
+    L.train = o; o += training_backward_workspace_bytes(B, T, H, K, V, GDN2_CHUNK);
+    L.total = o;
+    return L;
+}
+
+unsigned grid_for(int64_t n) { return (unsigned)std::min<int64_t>((n + 255) / 256, 148 * 16); }
+
+}  // namespace
+}  // namespace dbl
+
+extern "C" size_t dbl_gdn2_scan_backward_workspace_bytes(int64_t batch, int64_t time, int64_t heads, int64_t key_dim,
+                                                         int64_t value_dim, int32_t dtype) {
+    if (batch <= 0 || time <= 0 || heads <= 0 || key_dim <= 0 || value_dim <= 0) return 0;
+    return dbl::gdn2_bwd_layout(batch, time, heads, key_dim, value_dim, dtype).total;
+}
+
+extern "C" int dbl_gdn2_scan_backward(const dbl_gdn2_scan_backward_args* a, void* workspace, size_t workspace_bytes,
+                                      dbl_stream_t stream) {
+    using namespace dbl;
+    if (!a) return fail(DBL_ERR_INVALID_ARGUMENT, "gdn2_scan_backward: null args");
+    if (a->batch <= 0 || a->time <= 0 || a->heads <= 0 || a->key_dim <= 0 || a->value_dim <= 0)
+        return fail(DBL_ERR_INVALID_ARGUMENT, "GDN-2 requires nonempty axes");
+    if (a->dtype != DBL_F32 && a->dtype != DBL_BF16)
+        return fail(DBL_ERR_INVALID_ARGUMENT, "gdn2_scan_backward: dtype must be f32 or bf16");
+    if (!a->q || !a->k || !a->v || !a->alpha || !a->erase || !a->write || !a->doc_start || !a->doc_end ||
+        !a->grad_output || !a->dq || !a->dk || !a->dv || !a->dalpha || !a->derase || !a->dwrite)
+        return fail(DBL_ERR_INVALID_ARGUMENT, "gdn2_scan_backward: every pointer is required");
+    const Gdn2BwdLayout L = gdn2_bwd_layout(a->batch, a->time, a->heads, a->key_dim, a->value_dim, a->dtype);
+    if (!workspace || workspace_bytes < L.total)
+        return fail(DBL_ERR_WORKSPACE, "gdn2_scan_backward: workspace of %zu bytes required (got %zu)", L.total,
+                    workspace_bytes);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const int64_t bt = a->batch * a->time, nk = bt * a->heads * a->key_dim, nv = bt * a->heads * a->value_dim;
+    float* valid = reinterpret_cast<float*>(ws + L.valid);
+    float* reset = reinterpret_cast<float*>(ws + L.reset);
+    limits_to_masks_kernel<<<(unsigned)((bt + 255) / 256), 256, 0, st>>>(a->doc_start, a->doc_end, a->batch, a->time,
+                                                                         valid, reset);
+    const bool wide = a->dtype == DBL_BF16;
+    dbl_training_scan_backward_args t{};
+    t.batch = a->batch;
+    t.time = a->time;
+    t.heads = a->heads;
+    t.key_dim = a->key_dim;
+    t.value_dim = a->value_dim;
+    t.chunk_size = GDN2_CHUNK;
+    if (wide) {
+        float *q = reinterpret_cast<float*>(ws + L.q), *k = reinterpret_cast<float*>(ws + L.k);
+        float *v = reinterpret_cast<float*>(ws + L.v), *go = reinterpret_cast<float*>(ws + L.go);
+        widen_bf16_kernel<<<grid_for(nk), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(a->q), q, nk);
+        widen_bf16_kernel<<<grid_for(nk), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(a->k), k, nk);
+        widen_bf16_kernel<<<grid_for(nv), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(a->v), v, nv);
+        widen_bf16_kernel<<<grid_for(nv), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(a->grad_output), go, nv);
+        t.q = q;
+        t.k = k;
+        t.v = v;
+        t.grad_output = go;
+        t.dq = reinterpret_cast<float*>(ws + L.dq);
+        t.dk = reinterpret_cast<float*>(ws + L.dk);
+        t.dv = reinterpret_cast<float*>(ws + L.dv);
+    } else {
+        t.q = static_cast<const float*>(a->q);
+        t.k = static_cast<const float*>(a->k);
+        t.v = static_cast<const float*>(a->v);
+        t.grad_output = static_cast<const float*>(a->grad_output);
+        t.dq = static_cast<float*>(a->dq);
+        t.dk = static_cast<float*>(a->dk);
+        t.dv = static_cast<float*>(a->dv);
+    }
+    t.alpha = a->alpha;
+    t.erase = a->erase;
+    t.write = a->write;
+    t.valid = valid;
+    t.reset = reset;
+    t.dalpha = a->dalpha;
+    t.derase = a->derase;
+    t.dwrite = a->dwrite;
+    const int rc = dbl_gdn_training_scan_backward(&t, ws + L.train, L.total - L.train, stream);
+    if (rc != DBL_OK) return rc;
+    if (wide) {
+        narrow_bf16_kernel<<<grid_for(nk), 256, 0, st>>>(t.dq, static_cast<__nv_bfloat16*>(a->dq), nk);
+        narrow_bf16_kernel<<<grid_for(nk), 256, 0, st>>>(t.dk, static_cast<__nv_bfloat16*>(a->dk), nk);
+        narrow_bf16_kernel<<<grid_for(nv), 256, 0, st>>>(t.dv, static_cast<__nv_bfloat16*>(a->dv), nv);
+    }
+    return launch_status("gdn2_scan_backward");
 }

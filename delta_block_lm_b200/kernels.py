@@ -9,6 +9,7 @@ calls the C ABI of ``libdbl_gdn2.so`` on the current CUDA stream.  torch is only
     gdn_training_backward <- GdnTrainingOps::gdn_training_backward (gdn_training_ops.rs:95-127)
     gdn2_prologue      <- the GDN-2 gate and input producer of Mixer::forward_inner (crates/mixers/src/lib.rs:446-528)
     gdn2_scan          <- delta_kernels::gdn2_scan          (crates/kernels/src/ops.rs:251-276)
+    gdn2_scan_backward <- Gdn2Ops::gdn2_backward            (ops.rs:106-160; kernels gdn2.rs:285-519)
     gdn2_prefill       <- scalar-gate chunked forward (the BASELINE prefill; chunk.rs:129-250 semantics)
     gdn2_span_transition  hand-off matrix for time-sharded prefill (no reference counterpart)
     gdn2_decode_step   <- the T = 1 continuation scan (crates/mixers/src/lib.rs:544-556), in place
@@ -228,6 +229,36 @@ def gdn2_scan(q, k, v, alpha, erase, write, doc_start, doc_end) -> torch.Tensor:
                            _ptr(write), _ptr(ds), _ptr(de), _ptr(out))
         N.check(N.lib().dbl_gdn2_scan(ctypes.byref(a), _stream(dev)))
     return out
+
+
+def gdn2_scan_backward(q, k, v, alpha, erase, write, doc_start, doc_end, grad_output):
+    """Backward of ``gdn2_scan`` (``Gdn2Ops::gdn2_backward``, crates/kernels/src/ops.rs:106-160;
+    kernels gdn2.rs:285-519): returns (dq, dk, dv, dalpha, derase, dwrite), dq/dk/dv in the q dtype,
+    the gate gradients f32.  The chunk states are recomputed; no forward checkpoint is needed."""
+    dev = _require_cuda(q, k, v, alpha, erase, write, doc_start, doc_end, grad_output)
+    B, T, H, K = q.shape
+    V = v.shape[3]
+    for name, t, shape in (("k", k, (B, T, H, K)), ("v", v, (B, T, H, V)), ("alpha", alpha, (B, T, H, K)),
+                           ("erase", erase, (B, T, H, K)), ("write", write, (B, T, H, V)),
+                           ("doc_start", doc_start, (B, T)), ("doc_end", doc_end, (B, T)),
+                           ("grad_output", grad_output, (B, T, H, V))):
+        if tuple(t.shape) != shape:
+            raise ValueError(f"{name} must have shape {list(shape)}, got {list(t.shape)}")
+    dt = _dtype_code(q)
+    with torch.cuda.device(dev):
+        q, k, v = q.contiguous(), k.to(q.dtype).contiguous(), v.to(q.dtype).contiguous()
+        go = grad_output.to(q.dtype).contiguous()
+        alpha, erase, write = _f32c(alpha), _f32c(erase), _f32c(write)
+        ds, de = doc_start.to(torch.int32).contiguous(), doc_end.to(torch.int32).contiguous()
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        da, dE, dw = torch.empty_like(alpha), torch.empty_like(erase), torch.empty_like(write)
+        need = int(N.lib().dbl_gdn2_scan_backward_workspace_bytes(B, T, H, K, V, dt))
+        ws = torch.empty(max(need, 1), device=dev, dtype=torch.uint8)
+        a = N.Gdn2ScanBackwardArgs(B, T, H, K, V, dt, _ptr(q), _ptr(k), _ptr(v), _ptr(alpha), _ptr(erase),
+                                   _ptr(write), _ptr(ds), _ptr(de), _ptr(go), _ptr(dq), _ptr(dk), _ptr(dv),
+                                   _ptr(da), _ptr(dE), _ptr(dw))
+        N.check(N.lib().dbl_gdn2_scan_backward(ctypes.byref(a), _ptr(ws), need, _stream(dev)))
+    return dq, dk, dv, da, dE, dw
 
 
 def _strides(t: torch.Tensor, n: int):

@@ -182,6 +182,28 @@ size_t dbl_gdn_training_scan_backward_workspace_bytes(int64_t batch, int64_t tim
 int dbl_gdn_training_scan_backward(const dbl_training_scan_backward_args *args, void *workspace,
                                    size_t workspace_bytes, dbl_stream_t stream);
 
+/* Backward of dbl_gdn2_scan: replaces Gdn2Ops::gdn2_backward(q, k, v, alpha, erase, write,
+ * output_grad, checkpoint, doc_start, doc_end) -> (dq, dk, dv, dalpha, derase, dwrite)
+ * (crates/kernels/src/ops.rs:106-160; kernels gdn2.rs:285-519).  Layouts as dbl_gdn2_scan; q, k,
+ * v, grad_output and dq, dk, dv in dtype (f32 or bf16), the gates and their gradients f32.  The
+ * forward's checkpoint tensor is not taken: the chunk states are recomputed in the workspace
+ * (dbl_gdn2_scan_backward_workspace_bytes).  K <= 64, V <= 256. */
+typedef struct {
+    int64_t batch, time, heads, key_dim, value_dim;
+    int32_t dtype;
+    const void *q, *k, *v;
+    const float *alpha, *erase, *write;
+    const int32_t *doc_start, *doc_end;
+    const void *grad_output;
+    void *dq, *dk, *dv;
+    float *dalpha, *derase, *dwrite;
+} dbl_gdn2_scan_backward_args;
+
+size_t dbl_gdn2_scan_backward_workspace_bytes(int64_t batch, int64_t time, int64_t heads, int64_t key_dim,
+                                              int64_t value_dim, int32_t dtype);
+int dbl_gdn2_scan_backward(const dbl_gdn2_scan_backward_args *args, void *workspace, size_t workspace_bytes,
+                           dbl_stream_t stream);
+
 /* GDN-2 mixer prologue: what Mixer::forward_inner computes between the projections and the scan
  * (crates/mixers/src/lib.rs:446-528, MixerKind::Gdn2), fused into one memory-bound pass:
  *   q, k = l2(silu(conv(proj_q|proj_k))),  v = silu(conv(proj_v)),

@@ -20,6 +20,7 @@ STRUCTS = {
     "dbl_training_scan_backward_args": N.TrainingScanBackwardArgs,
     "dbl_gdn2_prologue_args": N.Gdn2PrologueArgs,
     "dbl_gdn2_scan_args": N.Gdn2ScanArgs,
+    "dbl_gdn2_scan_backward_args": N.Gdn2ScanBackwardArgs,
     "dbl_relay_merge_args": N.RelayMergeArgs,
     "dbl_relay_attention_args": N.RelayAttentionArgs,
 }

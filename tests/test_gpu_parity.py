@@ -467,3 +467,34 @@ def test_relay_attention_rejects_bad_shapes(cuda, native_lib):
     with pytest.raises(ValueError):
         dbl.relay_attention_forward(q, q, q, torch.zeros(1, 1, 16, 32, device=cuda), torch.zeros(1, 1, 16, 32, device=cuda),
                                     ids, ids, ids)
+
+
+# ------------------------------------------------------------------------- gdn2_scan backward
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("B,T,H", [(2, 45, 2), (1, 130, 3)])
+def test_gdn2_scan_backward_matches_oracle(cuda, native_lib, dtype, B, T, H):
+    # gdn2_backward (ops.rs:106-160, gdn2.rs:285-519) at the reference's widths K32 / V64, documents
+    # with resets and a padding tail, against the f64 backward oracle on the same (rounded) inputs
+    K, V = 32, 64
+    rng = np.random.default_rng(T + H)
+    q, k = rng.standard_normal((B, T, H, K)) / 6, rng.standard_normal((B, T, H, K)) / 6
+    v, w = rng.standard_normal((B, T, H, V)), 1 / (1 + np.exp(-rng.standard_normal((B, T, H, V))))
+    a = 1 / (1 + np.exp(-(3 + rng.standard_normal((B, T, H, K)))))
+    e = 1 / (1 + np.exp(-rng.standard_normal((B, T, H, K))))
+    go = rng.standard_normal((B, T, H, V))
+    lengths = [[T // 3, T // 3], [T - 5]] if B == 2 else [[T // 2, T // 4]]
+    di, ds, de, _ = _packed_layout(lengths, T)
+    if dtype == torch.bfloat16:
+        q, k, v, go = (bf16_round(x) for x in (q, k, v, go))
+    d = lambda x, dt=torch.float32: torch.as_tensor(np.asarray(x, np.float32), device=cuda).to(dt)  # noqa: E731
+    got = dbl.gdn2_scan_backward(d(q, dtype), d(k, dtype), d(v, dtype), d(a), d(e), d(w),
+                                 torch.as_tensor(ds, device=cuda), torch.as_tensor(de, device=cuda), d(go, dtype))
+    torch.cuda.synchronize()
+    ref = O.doc_backward(q, k, v, a, e, w, ds, de, go)
+    for name, g, r in zip(("dq", "dk", "dv", "dalpha", "derase", "dwrite"), got, ref):
+        tol = TOL_BF16 if (dtype == torch.bfloat16 and name in ("dq", "dk", "dv")) else TOL_F32
+        assert rel_err(g.float().cpu().numpy(), r) < tol, (name, rel_err(g.float().cpu().numpy(), r))
+    # padding tokens get no gradient
+    pad = (de < ds)
+    for g in got:
+        assert torch.all(g.float().cpu()[torch.as_tensor(pad)] == 0.0)

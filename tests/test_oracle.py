@@ -391,3 +391,34 @@ def test_relay_window_matches_dense_masked_attention():
         w = np.exp(s - s.max())
         np.testing.assert_allclose(o[0, 0, t], w @ dv[keep] / w.sum(), rtol=1e-12, atol=1e-14)
         np.testing.assert_allclose(norm[0, 0, t], [s.max(), w.sum()], rtol=1e-12)
+
+
+def test_doc_scan_backward_matches_finite_differences():
+    # gdn2_backward (gdn2.rs:285-519) restated as the stateful backward on the document masks: its
+    # gradients equal central differences of the doc-limit forward oracle (gdn2_reference.rs:87-105)
+    rng = np.random.default_rng(3)
+    B, T, H, K, V = 1, 10, 1, 3, 4
+    q, k = rng.standard_normal((B, T, H, K)), rng.standard_normal((B, T, H, K))
+    v, w = rng.standard_normal((B, T, H, V)), rng.random((B, T, H, V))
+    a, e = rng.uniform(0.5, 1.0, (B, T, H, K)), rng.random((B, T, H, K))
+    # documents [0, 4), [4, 8), then padding at 8 and 9
+    ds = np.array([[0, 0, 0, 0, 4, 4, 4, 4, 8, 9]], np.int32)
+    de = np.array([[3, 3, 3, 3, 7, 7, 7, 7, 7, 8]], np.int32)
+    go = rng.standard_normal((B, T, H, V))
+    inputs = [q, k, v, a, e, w]
+
+    def loss(xs):
+        return float(np.sum(go * O.doc_scan(*xs, ds, de)))
+    grads = O.doc_backward(q, k, v, a, e, w, ds, de, go)
+    for xi, gi in enumerate(grads):
+        x = inputs[xi]
+        num = np.zeros_like(x)
+        it = np.nditer(x, flags=["multi_index"])
+        for _ in it:
+            idx = it.multi_index
+            hi = [y.copy() for y in inputs]
+            lo = [y.copy() for y in inputs]
+            hi[xi][idx] += 1e-6
+            lo[xi][idx] -= 1e-6
+            num[idx] = (loss(hi) - loss(lo)) / 2e-6
+        assert np.max(np.abs(gi - num)) < 1e-6 * (1 + np.max(np.abs(num))), xi
