@@ -57,11 +57,16 @@ __device__ __forceinline__ void reduce_scatter32(float (&vals)[32], int lane) {
 template <int KMAX>
 __global__ void __launch_bounds__(256) training_backward_kernel(const BwdParams p) {
     constexpr int NKB = KMAX / 32;  // 32-wide blocks of key channels
-    __shared__ float sq[KMAX], sk[KMAX], sa[KMAX], se[KMAX];
-    __shared__ float sed[MAXC][256];   // edit_j of each token of the chunk
-    __shared__ float sen[MAXC][8];     // per-warp partial |edit|^2
-    __shared__ float red[8][4][KMAX];  // per-warp sums: dq, dk, dalpha, derase
-    __shared__ int sact, srst;
+    // the staged chunk: k, alpha, erase, q of its tokens and their masks; per-warp partials
+    __shared__ float sk[MAXC][KMAX], sa[MAXC][KMAX], se[MAXC][KMAX], sq[MAXC][KMAX];
+    __shared__ float sen[MAXC][8];        // per-warp partial |edit|^2
+    __shared__ float red[2][8][4][KMAX];  // per-warp sums dq, dk, dalpha, derase (double-buffered)
+    __shared__ int sact[MAXC], srst[MAXC];
+    // per column: write * v and the edit of each token of the chunk, [MAXC][blockDim] (dynamic);
+    // thread j reads and writes only column j
+    extern __shared__ float dyn[];
+    float* swv = dyn;
+    float* sxe = dyn + MAXC * blockDim.x;
 
     const int bh = blockIdx.x;
     const int b = bh / p.H, h = bh - b * p.H;
@@ -72,119 +77,136 @@ __global__ void __launch_bounds__(256) training_backward_kernel(const BwdParams 
     const size_t sbase = ((size_t)b * H + h) * K * V;
     auto tok = [&](int t) { return ((size_t)b * T + t) * H + h; };  // token row index
 
-    // stages k, alpha, erase (and q) of token t and its masks
-    auto stage = [&](int t, bool with_q) {
+    // stages the n tokens from t0 (k, alpha, erase and, for the reverse, q) with one pair of
+    // barriers: every load of the chunk is in flight at once
+    auto stage = [&](int t0, int n, bool with_q) {
         __syncthreads();
-        const size_t base = tok(t) * K;
-        for (int x = j; x < KMAX; x += nthr) {
-            const bool in = x < K;
-            sk[x] = in ? p.k[base + x] : 0.f;
-            sa[x] = in ? p.alpha[base + x] : 0.f;
-            se[x] = in ? p.erase[base + x] : 0.f;
-            if (with_q) sq[x] = in ? p.q[base + x] : 0.f;
+        for (int x = j; x < n * KMAX; x += nthr) {
+            const int r = x / KMAX, i = x - r * KMAX;
+            const bool in = i < K;
+            const size_t g = tok(t0 + r) * K + i;
+            sk[r][i] = in ? p.k[g] : 0.f;
+            sa[r][i] = in ? p.alpha[g] : 0.f;
+            se[r][i] = in ? p.erase[g] : 0.f;
+            if (with_q) sq[r][i] = in ? p.q[g] : 0.f;
         }
-        if (j == 0) {
-            sact = p.valid[(size_t)b * T + t] != 0.f;
-            srst = p.reset[(size_t)b * T + t] != 0.f;
+        if (j < n) {
+            sact[j] = p.valid[(size_t)b * T + t0 + j] != 0.f;
+            srst[j] = p.reset[(size_t)b * T + t0 + j] != 0.f;
         }
         __syncthreads();
+    };
+    // write * v of this column for the chunk's tokens into swv: all loads issued, then stored
+    auto load_wv = [&](int t0, int n) {
+        float w[MAXC], x[MAXC];
+#pragma unroll
+        for (int r = 0; r < MAXC; ++r) {
+            w[r] = (col && r < n) ? p.write[tok(t0 + r) * V + j] : 0.f;
+            x[r] = (col && r < n) ? p.v[tok(t0 + r) * V + j] : 0.f;
+        }
+#pragma unroll
+        for (int r = 0; r < MAXC; ++r) swv[r * nthr + j] = w[r] * x[r];
+    };
+    // one forward step of this column; returns the edit x
+    auto step = [&](float (&S)[KMAX], int r, float wv) {
+        if (!sact[r]) return 0.f;
+        const bool rst = srst[r];
+        float x = wv;
+#pragma unroll
+        for (int i = 0; i < KMAX; ++i) {
+            const float bar = rst ? 0.f : sa[r][i] * S[i];
+            x -= se[r][i] * sk[r][i] * bar;
+            S[i] = bar;
+        }
+#pragma unroll
+        for (int i = 0; i < KMAX; ++i) S[i] = fmaf(sk[r][i], x, S[i]);
+        return x;
     };
 
     // ---------------------------------------------------------------- pass 1: checkpoints
     float S[KMAX];
 #pragma unroll
     for (int i = 0; i < KMAX; ++i) S[i] = (col && i < K && p.initial) ? p.initial[sbase + (size_t)i * V + j] : 0.f;
-    for (int t = 0; t < T; ++t) {
-        if (t % p.C == 0 && col) {
-            float* ckc = p.ck + ((size_t)bh * p.nch + t / p.C) * K * V;
+    for (int c = 0; c < p.nch; ++c) {
+        const int t0 = c * p.C, n = min(p.C, T - t0);
+        if (col) {
+            float* ckc = p.ck + ((size_t)bh * p.nch + c) * K * V;
 #pragma unroll
             for (int i = 0; i < KMAX; ++i)
                 if (i < K) ckc[(size_t)i * V + j] = S[i];
         }
-        stage(t, false);
-        if (!sact) continue;
-        const bool rst = srst;
-        float x = col ? p.write[tok(t) * V + j] * p.v[tok(t) * V + j] : 0.f;
-#pragma unroll
-        for (int i = 0; i < KMAX; ++i) {
-            const float bar = rst ? 0.f : sa[i] * S[i];
-            x -= se[i] * sk[i] * bar;
-            S[i] = bar;
-        }
-#pragma unroll
-        for (int i = 0; i < KMAX; ++i) S[i] = fmaf(sk[i], x, S[i]);
+        load_wv(t0, n);
+        stage(t0, n, false);
+#pragma unroll 1
+        for (int r = 0; r < n; ++r) step(S, r, swv[r * nthr + j]);
     }
 
     // ---------------------------------------------------------------- pass 2: reverse
     float A[KMAX];
 #pragma unroll
     for (int i = 0; i < KMAX; ++i) A[i] = (col && i < K && p.g_fin) ? p.g_fin[sbase + (size_t)i * V + j] : 0.f;
+    int rb = 0;  // red[] buffer of the next reverse token
     for (int c = p.nch - 1; c >= 0; --c) {
         const int t0 = c * p.C, n = min(p.C, T - t0);
-        // replay the chunk: previous states to the workspace, edits to shared memory
+        // replay the chunk: previous states to the workspace, edits to registers
         const float* ckc = p.ck + ((size_t)bh * p.nch + c) * K * V;
 #pragma unroll
         for (int i = 0; i < KMAX; ++i) S[i] = (col && i < K) ? ckc[(size_t)i * V + j] : 0.f;
+        load_wv(t0, n);
+        stage(t0, n, true);
+#pragma unroll 1
         for (int r = 0; r < n; ++r) {
-            const int t = t0 + r;
-            stage(t, false);
             float* rpr = p.rp + ((size_t)bh * p.C + r) * K * V;
             if (col) {
 #pragma unroll
                 for (int i = 0; i < KMAX; ++i)
                     if (i < K) rpr[(size_t)i * V + j] = S[i];
             }
-            float x = 0.f;
-            if (sact) {
-                const bool rst = srst;
-                x = col ? p.write[tok(t) * V + j] * p.v[tok(t) * V + j] : 0.f;
-#pragma unroll
-                for (int i = 0; i < KMAX; ++i) {
-                    const float bar = rst ? 0.f : sa[i] * S[i];
-                    x -= se[i] * sk[i] * bar;
-                    S[i] = bar;
-                }
-#pragma unroll
-                for (int i = 0; i < KMAX; ++i) S[i] = fmaf(sk[i], x, S[i]);
-            }
-            sed[r][j] = x;
+            float x = step(S, r, swv[r * nthr + j]);
+            x = col ? x : 0.f;
+            sxe[r * nthr + j] = x;
             float x2 = x * x;
 #pragma unroll
             for (int o = 16; o >= 1; o >>= 1) x2 += __shfl_xor_sync(FULL, x2, o);
             if (lane == 0) sen[r][warp] = x2;
         }
+        __syncthreads();  // sen complete; the previous states are in the workspace (same thread)
+        // walk the chunk backwards; the upstream gradient of the next token is fetched one step ahead
+        float dy_next = (col && n > 0) ? p.g_out[tok(t0 + n - 1) * V + j] : 0.f;
+#pragma unroll 1
         for (int r = n - 1; r >= 0; --r) {
             const int t = t0 + r;
-            stage(t, true);  // its leading barrier also orders the replay's shared writes
             const size_t tk = tok(t) * K, tv = tok(t) * V;
-            if (!sact) {
+            const float dy = dy_next;
+            if (r > 0) dy_next = col ? p.g_out[tok(t - 1) * V + j] : 0.f;
+            if (!sact[r]) {
                 for (int x = j; x < K; x += nthr) p.dq[tk + x] = p.dk[tk + x] = p.dalpha[tk + x] = p.derase[tk + x] = 0.f;
                 if (col) p.dv[tv + j] = p.dwrite[tv + j] = 0.f;
                 continue;
             }
-            const bool rst = srst;
-            float en2 = 0.f;
-            for (int w = 0; w < nwarps; ++w) en2 += sen[r][w];
-            float kn2 = 0.f;
-#pragma unroll
-            for (int i = 0; i < KMAX; ++i) kn2 = fmaf(sk[i], sk[i], kn2);
-            const float enorm = sqrtf(en2), knorm = sqrtf(kn2);
-            const bool norms = knorm > 0.f && enorm > 0.f;
-            const float gs = p.g_score ? p.g_score[tok(t)] : 0.f;
-            const float key_scale = norms ? gs * enorm / knorm : 0.f;
-            const float xe = sed[r][j];  // this column's edit (0 beyond V)
-            const float dy = col ? p.g_out[tv + j] : 0.f;
-            float dd = (norms && col) ? gs * knorm * xe / enorm : 0.f;
-#pragma unroll
-            for (int i = 0; i < KMAX; ++i) {
-                A[i] = fmaf(sq[i], dy, A[i]);
-                dd = fmaf(sk[i], A[i], dd);
-            }
-            if (!col) dd = 0.f;
+            const float wr = col ? p.write[tv + j] : 0.f, vr = col ? p.v[tv + j] : 0.f;
             const float* rpr = p.rp + ((size_t)bh * p.C + r) * K * V;
             float prev[KMAX];
 #pragma unroll
             for (int i = 0; i < KMAX; ++i) prev[i] = (col && i < K) ? rpr[(size_t)i * V + j] : 0.f;
+            const bool rst = srst[r];
+            float en2 = 0.f;
+            for (int w = 0; w < nwarps; ++w) en2 += sen[r][w];
+            float kn2 = 0.f;
+#pragma unroll
+            for (int i = 0; i < KMAX; ++i) kn2 = fmaf(sk[r][i], sk[r][i], kn2);
+            const float enorm = sqrtf(en2), knorm = sqrtf(kn2);
+            const bool norms = knorm > 0.f && enorm > 0.f;
+            const float gs = p.g_score ? p.g_score[tok(t)] : 0.f;
+            const float key_scale = norms ? gs * enorm / knorm : 0.f;
+            const float x_e = sxe[r * nthr + j];  // this column's edit (0 beyond V)
+            float dd = (norms && col) ? gs * knorm * x_e / enorm : 0.f;
+#pragma unroll
+            for (int i = 0; i < KMAX; ++i) {
+                A[i] = fmaf(sq[r][i], dy, A[i]);
+                dd = fmaf(sk[r][i], A[i], dd);
+            }
+            if (!col) dd = 0.f;
             // the four per-channel sums, one 32-wide block at a time
 #pragma unroll
             for (int kb = 0; kb < NKB; ++kb) {
@@ -192,57 +214,59 @@ __global__ void __launch_bounds__(256) training_backward_kernel(const BwdParams 
 #pragma unroll
                 for (int u = 0; u < 32; ++u) {
                     const int i = 32 * kb + u;
-                    const float bar = rst ? 0.f : sa[i] * prev[i];
-                    vals[u] = (bar + sk[i] * xe) * dy;
+                    const float bar = rst ? 0.f : sa[r][i] * prev[i];
+                    vals[u] = (bar + sk[r][i] * x_e) * dy;
                 }
                 reduce_scatter32(vals, lane);
-                red[warp][0][32 * kb + lane] = vals[0];
+                red[rb][warp][0][32 * kb + lane] = vals[0];
 #pragma unroll
                 for (int u = 0; u < 32; ++u) {
                     const int i = 32 * kb + u;
-                    const float bar = rst ? 0.f : sa[i] * prev[i];
-                    vals[u] = A[i] * xe - se[i] * bar * dd;
+                    const float bar = rst ? 0.f : sa[r][i] * prev[i];
+                    vals[u] = A[i] * x_e - se[r][i] * bar * dd;
                 }
                 reduce_scatter32(vals, lane);
-                red[warp][1][32 * kb + lane] = vals[0];
+                red[rb][warp][1][32 * kb + lane] = vals[0];
 #pragma unroll
                 for (int u = 0; u < 32; ++u) {
                     const int i = 32 * kb + u;
-                    const float bar = rst ? 0.f : sa[i] * prev[i];
-                    vals[u] = -sk[i] * bar * dd;
+                    const float bar = rst ? 0.f : sa[r][i] * prev[i];
+                    vals[u] = -sk[r][i] * bar * dd;
                 }
                 reduce_scatter32(vals, lane);
-                red[warp][3][32 * kb + lane] = vals[0];
+                red[rb][warp][3][32 * kb + lane] = vals[0];
 #pragma unroll
                 for (int u = 0; u < 32; ++u) {
                     const int i = 32 * kb + u;
-                    const float dbar = A[i] - se[i] * sk[i] * dd;
+                    const float dbar = A[i] - se[r][i] * sk[r][i] * dd;
                     vals[u] = rst ? 0.f : dbar * prev[i];
-                    A[i] = rst ? 0.f : sa[i] * dbar;
+                    A[i] = rst ? 0.f : sa[r][i] * dbar;
                 }
                 reduce_scatter32(vals, lane);
-                red[warp][2][32 * kb + lane] = vals[0];
+                red[rb][warp][2][32 * kb + lane] = vals[0];
             }
             if (col) {
-                p.dv[tv + j] = dd * p.write[tv + j];
-                p.dwrite[tv + j] = dd * p.v[tv + j];
+                p.dv[tv + j] = dd * wr;
+                p.dwrite[tv + j] = dd * vr;
             }
-            __syncthreads();
+            __syncthreads();  // red[rb] complete; the other buffer takes the next token
             for (int x = j; x < 4 * K; x += nthr) {
                 const int kind = x / K, i = x - kind * K;
                 float s = 0.f;
-                for (int w = 0; w < nwarps; ++w) s += red[w][kind][i];
+                for (int w = 0; w < nwarps; ++w) s += red[rb][w][kind][i];
                 if (kind == 0) p.dq[tk + i] = s;
-                else if (kind == 1) p.dk[tk + i] = s + key_scale * sk[i];
+                else if (kind == 1) p.dk[tk + i] = s + key_scale * sk[r][i];
                 else if (kind == 2) p.dalpha[tk + i] = s;
                 else p.derase[tk + i] = s;
             }
+            rb ^= 1;
         }
     }
     if (p.dinitial && col) {
 #pragma unroll
         for (int i = 0; i < KMAX; ++i)
             if (i < K) p.dinitial[sbase + (size_t)i * V + j] = A[i];
+
     }
 }
 
@@ -317,9 +341,20 @@ extern "C" int dbl_gdn_training_scan_backward(const dbl_training_scan_backward_a
     p.ck = static_cast<float*>(workspace);
     p.rp = p.ck + heads * p.nch * (size_t)p.K * p.V;
     const int threads = (p.V + 31) / 32 * 32;
+    const size_t dyn = 2 * (size_t)MAXC * threads * sizeof(float);  // swv, sxe
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    if (p.K <= 32) training_backward_kernel<32><<<(unsigned)heads, threads, 0, st>>>(p);
-    else training_backward_kernel<64><<<(unsigned)heads, threads, 0, st>>>(p);
+    static bool attr_set = false;  // the dynamic part may take the static part past 48 KB
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(training_backward_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             2 * MAXC * 256 * (int)sizeof(float));
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(training_backward_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     2 * MAXC * 256 * (int)sizeof(float));
+        if (e != cudaSuccess) return cuda_status(e, "gdn_training_scan_backward: cudaFuncSetAttribute");
+        attr_set = true;
+    }
+    if (p.K <= 32) training_backward_kernel<32><<<(unsigned)heads, threads, dyn, st>>>(p);
+    else training_backward_kernel<64><<<(unsigned)heads, threads, dyn, st>>>(p);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? DBL_OK : cuda_status(e, "gdn_training_scan_backward launch");
 }
