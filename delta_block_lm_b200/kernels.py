@@ -11,6 +11,7 @@ calls the C ABI of ``libdbl_gdn2.so`` on the current CUDA stream.  torch is only
     gdn2_scan          <- delta_kernels::gdn2_scan          (crates/kernels/src/ops.rs:251-276)
     gdn2_scan_backward <- Gdn2Ops::gdn2_backward            (ops.rs:106-160; kernels gdn2.rs:285-519)
     gdn2_prefill       <- scalar-gate chunked forward (the BASELINE prefill; chunk.rs:129-250 semantics)
+    gdn2_prefill_host     the same from host buffers, copies and kernels pipelined over batch slices
     gdn2_span_transition  hand-off matrix for time-sharded prefill (no reference counterpart)
     gdn2_decode_step   <- the T = 1 continuation scan (crates/mixers/src/lib.rs:544-556), in place
 """
@@ -340,6 +341,55 @@ def gdn2_prefill(q, k, v, alpha, beta, *, scale: Optional[float] = None, valid=N
         a = _prefill_args(q, k, v, alpha, beta, scale, valid, reset, initial_state, out,
                           final_state, chunk_size)
         N.check(N.lib().dbl_gdn2_prefill(ctypes.byref(a), _stream(dev)))
+    return out, final_state
+
+
+_host_streams: dict = {}
+
+
+def gdn2_prefill_host(q, k, v, alpha, beta, *, device=None, scale: Optional[float] = None, out=None,
+                      final_state=None, pieces: int = 8):
+    """``gdn2_prefill`` from host buffers: copies the inputs to ``device``, runs the prefill and
+    copies the output and the final state back, pipelined over ``pieces`` slices of the batch on
+    separate CUDA streams, so that one slice's kernel and read-back overlap the next slices'
+    host-to-device copies (the sequences of a batch are independent).  q, k, v, alpha, beta are
+    host tensors (pinned, for asynchronous copies); ``out`` [B,T,H,V] and ``final_state`` [B,H,K,V]
+    are host tensors (allocated pinned when not given).  The work is ordered before later work on
+    the device's current stream; the host results are complete once that stream is synchronised.
+    Returns (out, final_state)."""
+    if q.is_cuda:
+        raise ValueError("gdn2_prefill_host takes host tensors; use gdn2_prefill for device tensors")
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    B, T, H, K = q.shape
+    V = v.shape[3]
+    pieces = max(1, min(int(pieces), B))
+    if out is None:
+        out = torch.empty((B, T, H, V), dtype=q.dtype, pin_memory=True)
+    if final_state is None:
+        final_state = torch.empty((B, H, K, V), dtype=torch.float32, pin_memory=True)
+    key = (dev.index, pieces)
+    if key not in _host_streams:
+        with torch.cuda.device(dev):
+            _host_streams[key] = [torch.cuda.Stream(dev) for _ in range(pieces)]
+    streams = _host_streams[key]
+    main = torch.cuda.current_stream(dev)
+    start = torch.cuda.Event()
+    start.record(main)
+    with torch.cuda.device(dev):
+        for i, st in enumerate(streams):
+            lo, hi = B * i // pieces, B * (i + 1) // pieces
+            if lo == hi:
+                continue
+            st.wait_event(start)
+            with torch.cuda.stream(st):
+                dq, dk, dv = (x[lo:hi].to(dev, non_blocking=True) for x in (q, k, v))
+                da, db = (x[lo:hi].to(dev, non_blocking=True) for x in (alpha, beta))
+                o, f = gdn2_prefill(dq, dk, dv, da, db, scale=scale)
+                out[lo:hi].copy_(o, non_blocking=True)
+                final_state[lo:hi].copy_(f, non_blocking=True)
+                done = torch.cuda.Event()
+                done.record(st)
+            main.wait_event(done)
     return out, final_state
 
 

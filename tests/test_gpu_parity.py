@@ -498,3 +498,21 @@ def test_gdn2_scan_backward_matches_oracle(cuda, native_lib, dtype, B, T, H):
     pad = (de < ds)
     for g in got:
         assert torch.all(g.float().cpu()[torch.as_tensor(pad)] == 0.0)
+
+
+def test_prefill_from_host_matches_device(cuda, native_lib):
+    # the host-buffer entry point (copies and kernels pipelined over batch slices on side streams)
+    # gives the device path's results exactly: the sequences of a batch are independent
+    B, T, H, D = 5, 192, 2, 128
+    g = torch.Generator().manual_seed(21)
+    q = torch.nn.functional.normalize(torch.randn(B, T, H, D, generator=g), dim=-1).bfloat16()
+    k = torch.nn.functional.normalize(torch.randn(B, T, H, D, generator=g), dim=-1).bfloat16()
+    v = torch.randn(B, T, H, D, generator=g).bfloat16()
+    alpha = torch.sigmoid(3 + torch.randn(B, T, H, generator=g))
+    beta = torch.sigmoid(torch.randn(B, T, H, generator=g))
+    ref_o, ref_f = dbl.gdn2_prefill(*(x.to(cuda) for x in (q, k, v, alpha, beta)))
+    ho, hf = dbl.gdn2_prefill_host(*(x.pin_memory() for x in (q, k, v, alpha, beta)), device=cuda, pieces=3)
+    torch.cuda.synchronize()
+    assert torch.equal(ho, ref_o.cpu()) and torch.equal(hf, ref_f.cpu())
+    with pytest.raises(ValueError):
+        dbl.gdn2_prefill_host(q.to(cuda), k, v, alpha, beta)
