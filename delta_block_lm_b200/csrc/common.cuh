@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 
@@ -25,6 +26,20 @@ inline int cuda_status(cudaError_t e, const char* what) {
 
 // Checks the last launch on this thread.
 inline int launch_status(const char* what) { return cuda_status(cudaGetLastError(), what); }
+
+// Runs `set` (returning a DBL status) once per device for one call site, e.g. a kernel attribute,
+// which the runtime keeps per device; `done` is the site's static set of devices already handled.
+template <typename F>
+inline int once_per_device(std::atomic<uint64_t>& done, F&& set) {
+    int dev = 0;
+    const cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+    const uint64_t bit = dev >= 0 && dev < 64 ? uint64_t(1) << dev : 0;
+    if (bit && (done.load(std::memory_order_acquire) & bit)) return DBL_OK;
+    const int rc = set();
+    if (rc == DBL_OK && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+    return rc;
+}
 
 template <typename T>
 __device__ __forceinline__ float to_f32(T x);

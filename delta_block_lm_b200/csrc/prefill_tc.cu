@@ -854,12 +854,13 @@ int tc_prefill_launch(const dbl_prefill_args* a, const int64_t* qs, const int64_
     cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_tc_error);
     if (e != cudaSuccess) return cuda_status(e, "prefill_tc: error record");
     p.err = err;
-    static bool attr_set = false;  // per process; the attribute is per device function
-    if (!attr_set) {
-        e = cudaFuncSetAttribute(gdn2_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
-        if (e != cudaSuccess) return cuda_status(e, "prefill_tc: cudaFuncSetAttribute");
-        attr_set = true;
-    }
+    static std::atomic<uint64_t> attr_done{0};
+    rc = once_per_device(attr_done, [] {
+        return cuda_status(cudaFuncSetAttribute(gdn2_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                (int)SMEM_BYTES),
+                           "prefill_tc: cudaFuncSetAttribute");
+    });
+    if (rc != DBL_OK) return rc;
     gdn2_prefill_tc_kernel<<<(unsigned)(a->batch * a->heads), NTHREADS, SMEM_BYTES, st>>>(mq, mk, mv, mo, p);
     return launch_status("gdn2_prefill_tc_kernel");
 }

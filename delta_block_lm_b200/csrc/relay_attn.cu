@@ -713,13 +713,13 @@ extern "C" int dbl_relay_attention_forward(const dbl_relay_attention_args* a, db
     if (rc == DBL_OK) rc = make_map64(&mrk, a->relay_k, a->documents, a->heads, SLOTS, SLOTS);
     if (rc == DBL_OK) rc = make_map64(&mrv, a->relay_v, a->documents, a->heads, SLOTS, SLOTS);
     if (rc != DBL_OK) return rc;
-    static bool attr_set = false;
-    if (!attr_set) {
-        const cudaError_t e =
-            cudaFuncSetAttribute(relay_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_TC);
-        if (e != cudaSuccess) return cuda_status(e, "relay_attention_forward: cudaFuncSetAttribute");
-        attr_set = true;
-    }
+    static std::atomic<uint64_t> attr_done{0};
+    rc = once_per_device(attr_done, [] {
+        return cuda_status(
+            cudaFuncSetAttribute(relay_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_TC),
+            "relay_attention_forward: cudaFuncSetAttribute");
+    });
+    if (rc != DBL_OK) return rc;
     // persistent: one CTA per SM (or per tile when there are fewer tiles)
     int dev = 0, sms = 0;
     cudaError_t e = cudaGetDevice(&dev);

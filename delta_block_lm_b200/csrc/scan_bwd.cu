@@ -343,16 +343,16 @@ extern "C" int dbl_gdn_training_scan_backward(const dbl_training_scan_backward_a
     const int threads = (p.V + 31) / 32 * 32;
     const size_t dyn = 2 * (size_t)MAXC * threads * sizeof(float);  // swv, sxe
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    static bool attr_set = false;  // the dynamic part may take the static part past 48 KB
-    if (!attr_set) {
+    static std::atomic<uint64_t> attr_done{0};  // the dynamic part may take the static part past 48 KB
+    const int rc = once_per_device(attr_done, [] {
         cudaError_t e = cudaFuncSetAttribute(training_backward_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              2 * MAXC * 256 * (int)sizeof(float));
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(training_backward_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      2 * MAXC * 256 * (int)sizeof(float));
-        if (e != cudaSuccess) return cuda_status(e, "gdn_training_scan_backward: cudaFuncSetAttribute");
-        attr_set = true;
-    }
+        return cuda_status(e, "gdn_training_scan_backward: cudaFuncSetAttribute");
+    });
+    if (rc != DBL_OK) return rc;
     if (p.K <= 32) training_backward_kernel<32><<<(unsigned)heads, threads, dyn, st>>>(p);
     else training_backward_kernel<64><<<(unsigned)heads, threads, dyn, st>>>(p);
     const cudaError_t e = cudaGetLastError();
