@@ -29,6 +29,7 @@ __global__ void __launch_bounds__(256) seq_scan_kernel(const SeqParams p) {
     __shared__ int sact[TOK], srst[TOK];
     __shared__ float sd2[TOK][8];         // per-warp partial |edit|^2
     __shared__ float skk[TOK];
+    __shared__ float svw[TOK][256];       // write_j v_j of the staged tokens (column j: thread j)
 
     const int bh = blockIdx.x;
     const int b = bh / p.H, h = bh - b * p.H;
@@ -77,6 +78,20 @@ __global__ void __launch_bounds__(256) seq_scan_kernel(const SeqParams p) {
                 se[u][i] = ev;
             }
         }
+        {
+            // this column's write * v for the group: every load in flight before the stores
+            float vv[TOK], ww[TOK];
+#pragma unroll
+            for (int u = 0; u < TOK; ++u) {
+                const int t = t0 + u;
+                vv[u] = (col && u < nt && !p.v_zero) ? to_f32(vb[t * p.vs[1] + j * p.vs[3]]) : 0.f;
+                ww[u] = (col && u < nt && !SCALAR)
+                            ? p.write[(size_t)b * p.ws[0] + (size_t)t * p.ws[1] + (size_t)h * p.ws[2] + (size_t)j * p.ws[3]]
+                            : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < TOK; ++u) svw[u][j] = SCALAR ? vv[u] : ww[u] * vv[u];
+        }
         if (j < TOK) {
             const int u = j, t = t0 + u;
             int act = 0, rst = 0;
@@ -109,14 +124,9 @@ __global__ void __launch_bounds__(256) seq_scan_kernel(const SeqParams p) {
             const bool act = sact[u] != 0;
             float delta = 0.f, o = 0.f;
             if (act) {
-                float vj = 0.f, wj = 0.f;
-                if (col) {
-                    if (!p.v_zero) vj = to_f32(vb[t * p.vs[1] + j * p.vs[3]]);
-                    wj = SCALAR ? sgb[u]
-                                : p.write[(size_t)b * p.ws[0] + (size_t)t * p.ws[1] + (size_t)h * p.ws[2] + (size_t)j * p.ws[3]];
-                }
                 const bool rst = srst[u] != 0;
-                delta = wj * vj;
+                // write v for the channel-wise gates; beta v for the scalar ones
+                delta = col ? (SCALAR ? sgb[u] * svw[u][j] : svw[u][j]) : 0.f;
                 if (SCALAR) {
                     const float a = rst ? 0.f : sga[u];
                     float kS = 0.f;
