@@ -6,9 +6,11 @@
 // and the scalar-gate prefill at shapes the tensor-core kernel does not take (f32 inputs,
 // K or V other than 128), e.g. BASELINE config 0.
 //
-// One CTA per (b, h); thread j owns state column j (K f32 registers), as the reference kernel's
-// lane-per-value-column layout (gdn_training.rs:28-49).  Tokens are staged TOK at a time in
-// shared memory so a CTA synchronises twice per TOK tokens, not per token.  Step order is the
+// One CTA per (b, h); four lanes (two when V > 128) share state column j, each holding every
+// fourth row (the reference kernel gives a lane a whole value column, gdn_training.rs:28-49), so
+// that a step's row sums are short chains plus two shuffles.  Tokens are staged TOK at a time in
+// shared memory (k, q, gates and each column's write v) so a CTA synchronises twice per TOK tokens,
+// not per token.  Step order is the
 // reference's (reference.rs:62-108): padding -> o = 0, state kept; reset -> S = 0; decay;
 // edit = write v - sum_i erase_i k_i S_i; score = |k||edit|; S += k edit; o = q^T S.
 #include "scan_seq_params.cuh"
@@ -21,33 +23,46 @@ namespace {
 
 constexpr int TOK = 8;
 
-template <int KMAX, typename T, bool SCALAR>
-__global__ void __launch_bounds__(256) seq_scan_kernel(const SeqParams p) {
+// TPC lanes share value column j (lane / TPC within the warp's group of 32 / TPC columns); lane g =
+// lane % TPC owns state rows i = g, g + TPC, g + 2 TPC, ... (strided, so that the TPC lanes read
+// adjacent shared-memory words), KMAX / TPC of them.  The two row sums of a step (k^T bar erase and
+// q^T S) are reduced over the TPC lanes with shuffles.
+template <int TPC>
+__device__ __forceinline__ float row_sum(float x) {
+#pragma unroll
+    for (int o = 1; o < TPC; o <<= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    return x;
+}
+
+template <int KMAX, typename T, bool SCALAR, int TPC>
+__global__ void __launch_bounds__(512) seq_scan_kernel(const SeqParams p) {
+    constexpr int R = KMAX / TPC;
     __shared__ float sk[TOK][KMAX], sq[TOK][KMAX];
-    __shared__ float sa[SCALAR ? 1 : TOK][KMAX], se[SCALAR ? 1 : TOK][KMAX];
+    __shared__ float sa[SCALAR ? 1 : TOK][KMAX], se[SCALAR ? 1 : TOK][KMAX];  // se: erase_i k_i
     __shared__ float sga[TOK], sgb[TOK];  // scalar gates
     __shared__ int sact[TOK], srst[TOK];
-    __shared__ float sd2[TOK][8];         // per-warp partial |edit|^2
-    __shared__ float skk[TOK];
-    __shared__ float svw[TOK][256];       // write_j v_j of the staged tokens (column j: thread j)
+    __shared__ float sdl[TOK][256];       // each column's edit, for the scores after the group
+    __shared__ float svw[TOK][256];       // write_j v_j (beta: v_j) of the staged tokens
 
     const int bh = blockIdx.x;
     const int b = bh / p.H, h = bh - b * p.H;
-    const int j = threadIdx.x;
-    const int nthr = blockDim.x;
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    const int warp = tid >> 5, lane = tid & 31, nwarps = nthr >> 5;
+    const int g = lane % TPC;
+    const int j = warp * (32 / TPC) + lane / TPC;  // value column
     const bool col = j < p.V;
-    const int warp = j >> 5, lane = j & 31, nwarps = nthr >> 5;
 
-    float S[KMAX];
+    float S[R];
     const size_t sbase = ((size_t)b * p.H + h) * p.K * p.V;
 #pragma unroll
-    for (int i = 0; i < KMAX; ++i) {
+    for (int r = 0; r < R; ++r) {
+        const int i = g + TPC * r;
         float x = 0.f;
         if (col && i < p.K) {
             if (p.init_mode == 1) x = p.initial[sbase + (size_t)i * p.V + j];
             else if (p.init_mode == 2) x = (i == j) ? 1.f : 0.f;
         }
-        S[i] = x;
+        S[r] = x;
     }
 
     const T* qb = static_cast<const T*>(p.q) + b * p.qs[0] + h * p.qs[2];
@@ -57,7 +72,7 @@ __global__ void __launch_bounds__(256) seq_scan_kernel(const SeqParams p) {
     for (int t0 = 0; t0 < p.T; t0 += TOK) {
         const int nt = min(TOK, p.T - t0);
         __syncthreads();  // previous group's shared reads are complete
-        for (int x = j; x < TOK * KMAX; x += nthr) {
+        for (int x = tid; x < TOK * KMAX; x += nthr) {
             const int u = x / KMAX, i = x - u * KMAX;
             float kv = 0.f, qv = 0.f, av = 1.f, ev = 0.f;
             if (u < nt && i < p.K) {
@@ -75,25 +90,25 @@ __global__ void __launch_bounds__(256) seq_scan_kernel(const SeqParams p) {
             sq[u][i] = qv;
             if (!SCALAR) {
                 sa[u][i] = av;
-                se[u][i] = ev;
+                se[u][i] = ev * kv;
             }
         }
-        {
+        if (g == 0 && col) {
             // this column's write * v for the group: every load in flight before the stores
             float vv[TOK], ww[TOK];
 #pragma unroll
             for (int u = 0; u < TOK; ++u) {
                 const int t = t0 + u;
-                vv[u] = (col && u < nt && !p.v_zero) ? to_f32(vb[t * p.vs[1] + j * p.vs[3]]) : 0.f;
-                ww[u] = (col && u < nt && !SCALAR)
+                vv[u] = (u < nt && !p.v_zero) ? to_f32(vb[t * p.vs[1] + j * p.vs[3]]) : 0.f;
+                ww[u] = (u < nt && !SCALAR)
                             ? p.write[(size_t)b * p.ws[0] + (size_t)t * p.ws[1] + (size_t)h * p.ws[2] + (size_t)j * p.ws[3]]
                             : 0.f;
             }
 #pragma unroll
             for (int u = 0; u < TOK; ++u) svw[u][j] = SCALAR ? vv[u] : ww[u] * vv[u];
         }
-        if (j < TOK) {
-            const int u = j, t = t0 + u;
+        if (tid < TOK) {
+            const int u = tid, t = t0 + u;
             int act = 0, rst = 0;
             float ga = 1.f, gb = 0.f;
             if (u < nt) {
@@ -125,72 +140,82 @@ __global__ void __launch_bounds__(256) seq_scan_kernel(const SeqParams p) {
             float delta = 0.f, o = 0.f;
             if (act) {
                 const bool rst = srst[u] != 0;
-                // write v for the channel-wise gates; beta v for the scalar ones
-                delta = col ? (SCALAR ? sgb[u] * svw[u][j] : svw[u][j]) : 0.f;
+                const float wv = col ? svw[u][j] : 0.f;
+                float part = 0.f;
                 if (SCALAR) {
                     const float a = rst ? 0.f : sga[u];
-                    float kS = 0.f;
 #pragma unroll
-                    for (int i = 0; i < KMAX; ++i) {
-                        S[i] *= a;
-                        kS = fmaf(sk[u][i], S[i], kS);
+                    for (int r = 0; r < R; ++r) {
+                        const int i = g + TPC * r;
+                        S[r] *= a;
+                        part = fmaf(sk[u][i], S[r], part);
                     }
-                    delta -= sgb[u] * kS;
+                    // beta v - beta k^T S
+                    delta = sgb[u] * (wv - row_sum<TPC>(part));
                 } else {
 #pragma unroll
-                    for (int i = 0; i < KMAX; ++i) {
-                        S[i] = rst ? 0.f : S[i] * sa[u][i];
-                        delta -= se[u][i] * sk[u][i] * S[i];
+                    for (int r = 0; r < R; ++r) {
+                        const int i = g + TPC * r;
+                        S[r] = rst ? 0.f : S[r] * sa[u][i];
+                        part = fmaf(se[u][i], S[r], part);
                     }
+                    delta = wv - row_sum<TPC>(part);
                 }
+                float op = 0.f;
 #pragma unroll
-                for (int i = 0; i < KMAX; ++i) {
-                    S[i] = fmaf(sk[u][i], delta, S[i]);
-                    o = fmaf(sq[u][i], S[i], o);
+                for (int r = 0; r < R; ++r) {
+                    const int i = g + TPC * r;
+                    S[r] = fmaf(sk[u][i], delta, S[r]);
+                    op = fmaf(sq[u][i], S[r], op);
                 }
+                o = row_sum<TPC>(op);
             }
-            if (p.out && col) {
+            if (p.out && col && g == 0) {
                 const size_t oi = (size_t)b * p.os[0] + (size_t)t * p.os[1] + (size_t)h * p.os[2] + (size_t)j * p.os[3];
                 if (p.out_dtype == DBL_BF16) static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(o);
                 else static_cast<float*>(p.out)[oi] = o;
             }
-            if (p.scores) {
-                float d2 = col ? delta * delta : 0.f;
-#pragma unroll
-                for (int off = 16; off > 0; off >>= 1) d2 += __shfl_xor_sync(0xffffffffu, d2, off);
-                if (lane == 0) sd2[u][warp] = d2;
-            }
+            if (p.scores && g == 0 && col) sdl[u][j] = delta;
         }
         if (p.scores) {
-            if (warp == 0 && lane < TOK) {
-                // |k|^2 for the TOK staged tokens (lane = token).
-                float kk = 0.f;
-                for (int i = 0; i < p.K; ++i) kk = fmaf(sk[lane][i], sk[lane][i], kk);
-                skk[lane] = kk;
-            }
+            // score = |k| |edit| per token of the group: one warp per token
             __syncthreads();
-            if (j < nt) {
-                const int u = j, t = t0 + u;
-                float d2 = 0.f;
-                for (int w = 0; w < nwarps; ++w) d2 += sd2[u][w];
-                const float sc = sact[u] ? sqrtf(skk[u]) * sqrtf(d2) : 0.f;
-                p.scores[((size_t)b * p.T + t) * p.H + h] = sc;
+            for (int u = warp; u < nt; u += nwarps) {
+                const int t = t0 + u;
+                float kk = 0.f, d2 = 0.f;
+                for (int i = lane; i < p.K; i += 32) kk = fmaf(sk[u][i], sk[u][i], kk);
+                for (int c = lane; c < p.V; c += 32) d2 = fmaf(sdl[u][c], sdl[u][c], d2);
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) {
+                    kk += __shfl_xor_sync(0xffffffffu, kk, off);
+                    d2 += __shfl_xor_sync(0xffffffffu, d2, off);
+                }
+                if (lane == 0) p.scores[((size_t)b * p.T + t) * p.H + h] = sact[u] ? sqrtf(kk) * sqrtf(d2) : 0.f;
             }
         }
     }
     if (p.final_state && col) {
 #pragma unroll
-        for (int i = 0; i < KMAX; ++i)
-            if (i < p.K) p.final_state[sbase + (size_t)i * p.V + j] = S[i];
+        for (int r = 0; r < R; ++r) {
+            const int i = g + TPC * r;
+            if (i < p.K) p.final_state[sbase + (size_t)i * p.V + j] = S[r];
+        }
     }
 }
 
 template <int KMAX, typename T>
 int launch_seq_t(const SeqParams& p, cudaStream_t st) {
-    const int threads = ((p.V + 31) / 32) * 32;
     const unsigned grid = (unsigned)(p.B * p.H);
-    if (p.gate_mode == 1) seq_scan_kernel<KMAX, T, true><<<grid, threads, 0, st>>>(p);
-    else seq_scan_kernel<KMAX, T, false><<<grid, threads, 0, st>>>(p);
+    // four lanes per value column up to 128 columns, two beyond (at most 512 threads)
+    if (p.V <= 128) {
+        const int threads = ((p.V * 4 + 31) / 32) * 32;
+        if (p.gate_mode == 1) seq_scan_kernel<KMAX, T, true, 4><<<grid, threads, 0, st>>>(p);
+        else seq_scan_kernel<KMAX, T, false, 4><<<grid, threads, 0, st>>>(p);
+    } else {
+        const int threads = ((p.V * 2 + 31) / 32) * 32;
+        if (p.gate_mode == 1) seq_scan_kernel<KMAX, T, true, 2><<<grid, threads, 0, st>>>(p);
+        else seq_scan_kernel<KMAX, T, false, 2><<<grid, threads, 0, st>>>(p);
+    }
     return launch_status("seq_scan_kernel");
 }
 
