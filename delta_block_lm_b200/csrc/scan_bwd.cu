@@ -40,38 +40,89 @@ struct BwdParams {
     float *rp;  // [B*H][C][K][V]   previous state of each token of the chunk being reversed
 };
 
-// Sum over the 32 lanes of vals[0..32): afterwards lane L's vals[0] holds the sum for index L.
-__device__ __forceinline__ void reduce_scatter32(float (&vals)[32], int lane) {
+// One level of a reduce-scatter over the lanes that differ in lane bit `o`: the lower lane keeps
+// (and sums) the first `half` values, the upper lane the next `half`, moved to the front.
+template <int N>
+__device__ __forceinline__ void rs_level(float (&v)[N], int half, int o, int lane) {
+    const bool upper = (lane & o) != 0;
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) {
-        const bool upper = (lane & o) != 0;
-#pragma unroll
-        for (int x = 0; x < o; ++x) {
-            const float send = upper ? vals[x] : vals[x + o];
-            const float keep = upper ? vals[x + o] : vals[x];
-            vals[x] = keep + __shfl_xor_sync(FULL, send, o);
+    for (int x = 0; x < N / 2; ++x) {
+        if (x < half) {
+            const float send = upper ? v[x] : v[x + half];
+            const float keep = upper ? v[x + half] : v[x];
+            v[x] = keep + __shfl_xor_sync(FULL, send, o);
         }
     }
 }
+// Sums v over the 32 / TPC lanes that share lane % TPC (the columns of the warp at one row group):
+// afterwards v[0 .. M), M = N TPC / 32, holds the sums of indices [M s, M (s + 1)), s = lane / TPC.
+template <int N, int TPC>
+__device__ __forceinline__ void reduce_scatter_cols(float (&v)[N], int lane) {
+    int half = N / 2;
+#pragma unroll
+    for (int o = 16; o >= TPC; o >>= 1) {
+        rs_level(v, half, o, lane);
+        half >>= 1;
+    }
+}
+template <int TPC>
+__device__ __forceinline__ float row_sum(float x) {
+#pragma unroll
+    for (int o = 1; o < TPC; o <<= 1) x += __shfl_xor_sync(FULL, x, o);
+    return x;
+}
 
-template <int KMAX>
-__global__ void __launch_bounds__(256) training_backward_kernel(const BwdParams p) {
-    constexpr int NKB = KMAX / 32;  // 32-wide blocks of key channels
-    // the staged chunk: k, alpha, erase, q of its tokens and their masks; per-warp partials
-    __shared__ float sk[MAXC][KMAX], sa[MAXC][KMAX], se[MAXC][KMAX], sq[MAXC][KMAX];
-    __shared__ float sen[MAXC][8];        // per-warp partial |edit|^2
-    __shared__ float red[2][8][4][KMAX];  // per-warp sums dq, dk, dalpha, derase (double-buffered)
-    __shared__ int sact[MAXC], srst[MAXC];
-    // per column: write * v and the edit of each token of the chunk, [MAXC][blockDim] (dynamic);
-    // thread j reads and writes only column j
-    extern __shared__ float dyn[];
-    float* swv = dyn;
-    float* sxe = dyn + MAXC * blockDim.x;
+// Shared memory of the backward kernel (dynamic; the same carve-up on host and device).
+struct BwdSmem {
+    size_t k, a, e, q, wv, xe, en, kn, red, act, rst, total;
+};
+__host__ __device__ inline BwdSmem bwd_smem(int kmax, int cols, int nwarps) {
+    BwdSmem L{};
+    size_t o = 0;
+    const size_t tk = (size_t)MAXC * kmax * 4, tc = (size_t)MAXC * cols * 4;
+    L.k = o; o += tk;
+    L.a = o; o += tk;
+    L.e = o; o += tk;
+    L.q = o; o += tk;
+    L.wv = o; o += tc;
+    L.xe = o; o += tc;
+    L.en = o; o += MAXC * 4;
+    L.kn = o; o += MAXC * 4;
+    L.red = o; o += (size_t)2 * nwarps * 4 * kmax * 4;
+    L.act = o; o += MAXC * 4;
+    L.rst = o; o += MAXC * 4;
+    L.total = o;
+    return L;
+}
+
+// TPC lanes share value column j (as the forward kernel): lane g = lane % TPC holds state, adjoint
+// and replayed rows i = g, g + TPC, ... (R = KMAX / TPC of them).
+template <int KMAX, int TPC>
+__global__ void __launch_bounds__(512) training_backward_kernel(const BwdParams p) {
+    constexpr int R = KMAX / TPC;
+    constexpr int NV = 4 * R;            // per-lane contributions to the four channel sums
+    constexpr int M = NV * TPC / 32;     // sums a lane holds after the column reduce-scatter
+    extern __shared__ __align__(16) uint8_t dyn_raw[];
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    const int warp = tid >> 5, lane = tid & 31, nwarps = nthr >> 5;
+    const int g = lane % TPC;
+    const int j = warp * (32 / TPC) + lane / TPC;  // value column
+    const int cols = nwarps * (32 / TPC);
+    const BwdSmem L = bwd_smem(KMAX, cols, nwarps);
+    float(*sk)[KMAX] = reinterpret_cast<float(*)[KMAX]>(dyn_raw + L.k);
+    float(*sa)[KMAX] = reinterpret_cast<float(*)[KMAX]>(dyn_raw + L.a);
+    float(*se)[KMAX] = reinterpret_cast<float(*)[KMAX]>(dyn_raw + L.e);
+    float(*sq)[KMAX] = reinterpret_cast<float(*)[KMAX]>(dyn_raw + L.q);
+    float* swv = reinterpret_cast<float*>(dyn_raw + L.wv);  // [MAXC][cols]
+    float* sxe = reinterpret_cast<float*>(dyn_raw + L.xe);  // [MAXC][cols]
+    float* sen = reinterpret_cast<float*>(dyn_raw + L.en);  // |edit|^2 per token
+    float* skn = reinterpret_cast<float*>(dyn_raw + L.kn);  // |k|^2 per token
+    float* red = reinterpret_cast<float*>(dyn_raw + L.red); // [2][nwarps][4][KMAX]
+    int* sact = reinterpret_cast<int*>(dyn_raw + L.act);
+    int* srst = reinterpret_cast<int*>(dyn_raw + L.rst);
 
     const int bh = blockIdx.x;
     const int b = bh / p.H, h = bh - b * p.H;
-    const int j = threadIdx.x, nthr = blockDim.x;
-    const int warp = j >> 5, lane = j & 31, nwarps = nthr >> 5;
     const bool col = j < p.V;
     const int K = p.K, V = p.V, T = p.T, H = p.H;
     const size_t sbase = ((size_t)b * H + h) * K * V;
@@ -81,96 +132,104 @@ __global__ void __launch_bounds__(256) training_backward_kernel(const BwdParams 
     // barriers: every load of the chunk is in flight at once
     auto stage = [&](int t0, int n, bool with_q) {
         __syncthreads();
-        for (int x = j; x < n * KMAX; x += nthr) {
+        for (int x = tid; x < n * KMAX; x += nthr) {
             const int r = x / KMAX, i = x - r * KMAX;
             const bool in = i < K;
-            const size_t g = tok(t0 + r) * K + i;
-            sk[r][i] = in ? p.k[g] : 0.f;
-            sa[r][i] = in ? p.alpha[g] : 0.f;
-            se[r][i] = in ? p.erase[g] : 0.f;
-            if (with_q) sq[r][i] = in ? p.q[g] : 0.f;
+            const size_t gi = tok(t0 + r) * K + i;
+            sk[r][i] = in ? p.k[gi] : 0.f;
+            sa[r][i] = in ? p.alpha[gi] : 0.f;
+            se[r][i] = in ? p.erase[gi] : 0.f;
+            if (with_q) sq[r][i] = in ? p.q[gi] : 0.f;
         }
-        if (j < n) {
-            sact[j] = p.valid[(size_t)b * T + t0 + j] != 0.f;
-            srst[j] = p.reset[(size_t)b * T + t0 + j] != 0.f;
+        if (tid < n) {
+            sact[tid] = p.valid[(size_t)b * T + t0 + tid] != 0.f;
+            srst[tid] = p.reset[(size_t)b * T + t0 + tid] != 0.f;
+        }
+        if (g == 0) {
+            // this column's write * v for the chunk: all loads issued, then stored
+            float w[MAXC], x[MAXC];
+#pragma unroll
+            for (int r = 0; r < MAXC; ++r) {
+                w[r] = (col && r < n) ? p.write[tok(t0 + r) * V + j] : 0.f;
+                x[r] = (col && r < n) ? p.v[tok(t0 + r) * V + j] : 0.f;
+            }
+#pragma unroll
+            for (int r = 0; r < MAXC; ++r) swv[r * cols + j] = w[r] * x[r];
         }
         __syncthreads();
     };
-    // write * v of this column for the chunk's tokens into swv: all loads issued, then stored
-    auto load_wv = [&](int t0, int n) {
-        float w[MAXC], x[MAXC];
-#pragma unroll
-        for (int r = 0; r < MAXC; ++r) {
-            w[r] = (col && r < n) ? p.write[tok(t0 + r) * V + j] : 0.f;
-            x[r] = (col && r < n) ? p.v[tok(t0 + r) * V + j] : 0.f;
-        }
-#pragma unroll
-        for (int r = 0; r < MAXC; ++r) swv[r * nthr + j] = w[r] * x[r];
-    };
-    // one forward step of this column; returns the edit x
-    auto step = [&](float (&S)[KMAX], int r, float wv) {
+    // one forward step of this lane's rows; returns the column's edit x
+    auto step = [&](float (&S)[R], int r) {
         if (!sact[r]) return 0.f;
         const bool rst = srst[r];
-        float x = wv;
+        float part = 0.f;
 #pragma unroll
-        for (int i = 0; i < KMAX; ++i) {
-            const float bar = rst ? 0.f : sa[r][i] * S[i];
-            x -= se[r][i] * sk[r][i] * bar;
-            S[i] = bar;
+        for (int u = 0; u < R; ++u) {
+            const int i = g + TPC * u;
+            const float bar = rst ? 0.f : sa[r][i] * S[u];
+            part = fmaf(se[r][i] * sk[r][i], bar, part);
+            S[u] = bar;
         }
+        const float x = (col ? swv[r * cols + j] : 0.f) - row_sum<TPC>(part);
 #pragma unroll
-        for (int i = 0; i < KMAX; ++i) S[i] = fmaf(sk[r][i], x, S[i]);
+        for (int u = 0; u < R; ++u) S[u] = fmaf(sk[r][g + TPC * u], x, S[u]);
         return x;
     };
+    auto row_ok = [&](int u) { return col && g + TPC * u < K; };
 
     // ---------------------------------------------------------------- pass 1: checkpoints
-    float S[KMAX];
+    float S[R];
 #pragma unroll
-    for (int i = 0; i < KMAX; ++i) S[i] = (col && i < K && p.initial) ? p.initial[sbase + (size_t)i * V + j] : 0.f;
+    for (int u = 0; u < R; ++u) S[u] = (row_ok(u) && p.initial) ? p.initial[sbase + (size_t)(g + TPC * u) * V + j] : 0.f;
     for (int c = 0; c < p.nch; ++c) {
         const int t0 = c * p.C, n = min(p.C, T - t0);
-        if (col) {
-            float* ckc = p.ck + ((size_t)bh * p.nch + c) * K * V;
+        float* ckc = p.ck + ((size_t)bh * p.nch + c) * K * V;
 #pragma unroll
-            for (int i = 0; i < KMAX; ++i)
-                if (i < K) ckc[(size_t)i * V + j] = S[i];
-        }
-        load_wv(t0, n);
+        for (int u = 0; u < R; ++u)
+            if (row_ok(u)) ckc[(size_t)(g + TPC * u) * V + j] = S[u];
         stage(t0, n, false);
 #pragma unroll 1
-        for (int r = 0; r < n; ++r) step(S, r, swv[r * nthr + j]);
+        for (int r = 0; r < n; ++r) step(S, r);
     }
 
     // ---------------------------------------------------------------- pass 2: reverse
-    float A[KMAX];
+    float A[R];
 #pragma unroll
-    for (int i = 0; i < KMAX; ++i) A[i] = (col && i < K && p.g_fin) ? p.g_fin[sbase + (size_t)i * V + j] : 0.f;
-    int rb = 0;  // red[] buffer of the next reverse token
+    for (int u = 0; u < R; ++u) A[u] = (row_ok(u) && p.g_fin) ? p.g_fin[sbase + (size_t)(g + TPC * u) * V + j] : 0.f;
+    int rb = 0;  // red buffer of the next reverse token
     for (int c = p.nch - 1; c >= 0; --c) {
         const int t0 = c * p.C, n = min(p.C, T - t0);
-        // replay the chunk: previous states to the workspace, edits to registers
+        // replay the chunk: previous states to the workspace, edits to shared memory
         const float* ckc = p.ck + ((size_t)bh * p.nch + c) * K * V;
 #pragma unroll
-        for (int i = 0; i < KMAX; ++i) S[i] = (col && i < K) ? ckc[(size_t)i * V + j] : 0.f;
-        load_wv(t0, n);
+        for (int u = 0; u < R; ++u) S[u] = row_ok(u) ? ckc[(size_t)(g + TPC * u) * V + j] : 0.f;
         stage(t0, n, true);
 #pragma unroll 1
         for (int r = 0; r < n; ++r) {
             float* rpr = p.rp + ((size_t)bh * p.C + r) * K * V;
-            if (col) {
 #pragma unroll
-                for (int i = 0; i < KMAX; ++i)
-                    if (i < K) rpr[(size_t)i * V + j] = S[i];
-            }
-            float x = step(S, r, swv[r * nthr + j]);
-            x = col ? x : 0.f;
-            sxe[r * nthr + j] = x;
-            float x2 = x * x;
-#pragma unroll
-            for (int o = 16; o >= 1; o >>= 1) x2 += __shfl_xor_sync(FULL, x2, o);
-            if (lane == 0) sen[r][warp] = x2;
+            for (int u = 0; u < R; ++u)
+                if (row_ok(u)) rpr[(size_t)(g + TPC * u) * V + j] = S[u];
+            const float x = step(S, r);
+            if (g == 0 && col) sxe[r * cols + j] = x;
         }
-        __syncthreads();  // sen complete; the previous states are in the workspace (same thread)
+        __syncthreads();
+        // |edit|^2 and |k|^2 of each token of the chunk: one warp per token
+        for (int r = warp; r < n; r += nwarps) {
+            float e2 = 0.f, k2 = 0.f;
+            for (int cc = lane; cc < V; cc += 32) e2 = fmaf(sxe[r * cols + cc], sxe[r * cols + cc], e2);
+            for (int i = lane; i < K; i += 32) k2 = fmaf(sk[r][i], sk[r][i], k2);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                e2 += __shfl_xor_sync(FULL, e2, o);
+                k2 += __shfl_xor_sync(FULL, k2, o);
+            }
+            if (lane == 0) {
+                sen[r] = e2;
+                skn[r] = k2;
+            }
+        }
+        __syncthreads();
         // walk the chunk backwards; the upstream gradient of the next token is fetched one step ahead
         float dy_next = (col && n > 0) ? p.g_out[tok(t0 + n - 1) * V + j] : 0.f;
 #pragma unroll 1
@@ -180,93 +239,74 @@ __global__ void __launch_bounds__(256) training_backward_kernel(const BwdParams 
             const float dy = dy_next;
             if (r > 0) dy_next = col ? p.g_out[tok(t - 1) * V + j] : 0.f;
             if (!sact[r]) {
-                for (int x = j; x < K; x += nthr) p.dq[tk + x] = p.dk[tk + x] = p.dalpha[tk + x] = p.derase[tk + x] = 0.f;
-                if (col) p.dv[tv + j] = p.dwrite[tv + j] = 0.f;
+                for (int x = tid; x < K; x += nthr) p.dq[tk + x] = p.dk[tk + x] = p.dalpha[tk + x] = p.derase[tk + x] = 0.f;
+                if (col && g == 0) p.dv[tv + j] = p.dwrite[tv + j] = 0.f;
                 continue;
             }
-            const float wr = col ? p.write[tv + j] : 0.f, vr = col ? p.v[tv + j] : 0.f;
+            const float wr = (col && g == 0) ? p.write[tv + j] : 0.f, vr = (col && g == 0) ? p.v[tv + j] : 0.f;
             const float* rpr = p.rp + ((size_t)bh * p.C + r) * K * V;
-            float prev[KMAX];
+            float prev[R];
 #pragma unroll
-            for (int i = 0; i < KMAX; ++i) prev[i] = (col && i < K) ? rpr[(size_t)i * V + j] : 0.f;
+            for (int u = 0; u < R; ++u) prev[u] = row_ok(u) ? rpr[(size_t)(g + TPC * u) * V + j] : 0.f;
             const bool rst = srst[r];
-            float en2 = 0.f;
-            for (int w = 0; w < nwarps; ++w) en2 += sen[r][w];
-            float kn2 = 0.f;
-#pragma unroll
-            for (int i = 0; i < KMAX; ++i) kn2 = fmaf(sk[r][i], sk[r][i], kn2);
-            const float enorm = sqrtf(en2), knorm = sqrtf(kn2);
+            const float enorm = sqrtf(sen[r]), knorm = sqrtf(skn[r]);
             const bool norms = knorm > 0.f && enorm > 0.f;
             const float gs = p.g_score ? p.g_score[tok(t)] : 0.f;
             const float key_scale = norms ? gs * enorm / knorm : 0.f;
-            const float x_e = sxe[r * nthr + j];  // this column's edit (0 beyond V)
-            float dd = (norms && col) ? gs * knorm * x_e / enorm : 0.f;
+            const float x_e = col ? sxe[r * cols + j] : 0.f;  // this column's edit
+            float part = 0.f;
 #pragma unroll
-            for (int i = 0; i < KMAX; ++i) {
-                A[i] = fmaf(sq[r][i], dy, A[i]);
-                dd = fmaf(sk[r][i], A[i], dd);
+            for (int u = 0; u < R; ++u) {
+                const int i = g + TPC * u;
+                A[u] = fmaf(sq[r][i], dy, A[u]);
+                part = fmaf(sk[r][i], A[u], part);
             }
+            float dd = row_sum<TPC>(part) + ((norms && col) ? gs * knorm * x_e / enorm : 0.f);
             if (!col) dd = 0.f;
-            // the four per-channel sums, one 32-wide block at a time
+            // the four per-channel contributions of this lane's rows: [q][u], q = dq, dk, dalpha, derase
+            float vals[NV];
 #pragma unroll
-            for (int kb = 0; kb < NKB; ++kb) {
-                float vals[32];
-#pragma unroll
-                for (int u = 0; u < 32; ++u) {
-                    const int i = 32 * kb + u;
-                    const float bar = rst ? 0.f : sa[r][i] * prev[i];
-                    vals[u] = (bar + sk[r][i] * x_e) * dy;
-                }
-                reduce_scatter32(vals, lane);
-                red[rb][warp][0][32 * kb + lane] = vals[0];
-#pragma unroll
-                for (int u = 0; u < 32; ++u) {
-                    const int i = 32 * kb + u;
-                    const float bar = rst ? 0.f : sa[r][i] * prev[i];
-                    vals[u] = A[i] * x_e - se[r][i] * bar * dd;
-                }
-                reduce_scatter32(vals, lane);
-                red[rb][warp][1][32 * kb + lane] = vals[0];
-#pragma unroll
-                for (int u = 0; u < 32; ++u) {
-                    const int i = 32 * kb + u;
-                    const float bar = rst ? 0.f : sa[r][i] * prev[i];
-                    vals[u] = -sk[r][i] * bar * dd;
-                }
-                reduce_scatter32(vals, lane);
-                red[rb][warp][3][32 * kb + lane] = vals[0];
-#pragma unroll
-                for (int u = 0; u < 32; ++u) {
-                    const int i = 32 * kb + u;
-                    const float dbar = A[i] - se[r][i] * sk[r][i] * dd;
-                    vals[u] = rst ? 0.f : dbar * prev[i];
-                    A[i] = rst ? 0.f : sa[r][i] * dbar;
-                }
-                reduce_scatter32(vals, lane);
-                red[rb][warp][2][32 * kb + lane] = vals[0];
+            for (int u = 0; u < R; ++u) {
+                const int i = g + TPC * u;
+                const float bar = rst ? 0.f : sa[r][i] * prev[u];
+                const float dbar = A[u] - se[r][i] * sk[r][i] * dd;
+                vals[u] = (bar + sk[r][i] * x_e) * dy;
+                vals[R + u] = A[u] * x_e - se[r][i] * bar * dd;
+                vals[2 * R + u] = rst ? 0.f : dbar * prev[u];
+                vals[3 * R + u] = -sk[r][i] * bar * dd;
+                A[u] = rst ? 0.f : sa[r][i] * dbar;
             }
-            if (col) {
+            reduce_scatter_cols<NV, TPC>(vals, lane);
+            {
+                const int s = lane / TPC;
+                float* rw = red + ((size_t)(rb * nwarps + warp) * 4) * KMAX;
+#pragma unroll
+                for (int m = 0; m < M; ++m) {
+                    const int idx = M * s + m, q = idx / R, u = idx - q * R;
+                    rw[q * KMAX + g + TPC * u] = vals[m];
+                }
+            }
+            if (col && g == 0) {
                 p.dv[tv + j] = dd * wr;
                 p.dwrite[tv + j] = dd * vr;
             }
             __syncthreads();  // red[rb] complete; the other buffer takes the next token
-            for (int x = j; x < 4 * K; x += nthr) {
-                const int kind = x / K, i = x - kind * K;
-                float s = 0.f;
-                for (int w = 0; w < nwarps; ++w) s += red[rb][w][kind][i];
-                if (kind == 0) p.dq[tk + i] = s;
-                else if (kind == 1) p.dk[tk + i] = s + key_scale * sk[r][i];
-                else if (kind == 2) p.dalpha[tk + i] = s;
-                else p.derase[tk + i] = s;
+            for (int x = tid; x < 4 * K; x += nthr) {
+                const int q = x / K, i = x - q * K;
+                float sum = 0.f;
+                for (int w = 0; w < nwarps; ++w) sum += red[((size_t)(rb * nwarps + w) * 4 + q) * KMAX + i];
+                if (q == 0) p.dq[tk + i] = sum;
+                else if (q == 1) p.dk[tk + i] = sum + key_scale * sk[r][i];
+                else if (q == 2) p.dalpha[tk + i] = sum;
+                else p.derase[tk + i] = sum;
             }
             rb ^= 1;
         }
     }
-    if (p.dinitial && col) {
+    if (p.dinitial) {
 #pragma unroll
-        for (int i = 0; i < KMAX; ++i)
-            if (i < K) p.dinitial[sbase + (size_t)i * V + j] = A[i];
-
+        for (int u = 0; u < R; ++u)
+            if (row_ok(u)) p.dinitial[sbase + (size_t)(g + TPC * u) * V + j] = A[u];
     }
 }
 
@@ -340,22 +380,22 @@ extern "C" int dbl_gdn_training_scan_backward(const dbl_training_scan_backward_a
     const size_t heads = (size_t)a->batch * a->heads;
     p.ck = static_cast<float*>(workspace);
     p.rp = p.ck + heads * p.nch * (size_t)p.K * p.V;
-    const int threads = (p.V + 31) / 32 * 32;
-    const size_t dyn = 2 * (size_t)MAXC * threads * sizeof(float);  // swv, sxe
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    static std::atomic<uint64_t> attr_done{0};  // the dynamic part may take the static part past 48 KB
-    const int rc = once_per_device(attr_done, [] {
-        cudaError_t e = cudaFuncSetAttribute(training_backward_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             2 * MAXC * 256 * (int)sizeof(float));
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(training_backward_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     2 * MAXC * 256 * (int)sizeof(float));
-        return cuda_status(e, "gdn_training_scan_backward: cudaFuncSetAttribute");
-    });
-    if (rc != DBL_OK) return rc;
-    if (p.K <= 32) training_backward_kernel<32><<<(unsigned)heads, threads, dyn, st>>>(p);
-    else training_backward_kernel<64><<<(unsigned)heads, threads, dyn, st>>>(p);
-    const cudaError_t e = cudaGetLastError();
+    // four lanes per value column up to 128 columns, two beyond (at most 512 threads)
+    const int tpc = p.V <= 128 ? 4 : 2;
+    const int threads = (p.V * tpc + 31) / 32 * 32, nwarps = threads / 32;
+    const size_t dyn = bwd_smem(p.K <= 32 ? 32 : 64, nwarps * (32 / tpc), nwarps).total;
+    auto go = [&](auto kernel) {
+        if (dyn > 48 * 1024) {
+            const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+            if (e != cudaSuccess) return e;
+        }
+        kernel<<<(unsigned)heads, threads, dyn, st>>>(p);
+        return cudaGetLastError();
+    };
+    cudaError_t e;
+    if (p.K <= 32) e = tpc == 4 ? go(training_backward_kernel<32, 4>) : go(training_backward_kernel<32, 2>);
+    else e = tpc == 4 ? go(training_backward_kernel<64, 4>) : go(training_backward_kernel<64, 2>);
     return e == cudaSuccess ? DBL_OK : cuda_status(e, "gdn_training_scan_backward launch");
 }
 

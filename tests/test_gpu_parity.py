@@ -57,6 +57,25 @@ def test_training_scan_chunk_fixture_and_padding_zero(cuda, native_lib):
     assert ok, err
 
 
+@pytest.mark.parametrize("K,V", [(48, 200), (100, 96), (7, 9)])
+def test_training_scan_lane_layouts(cuda, native_lib, K, V):
+    # widths that take each lane layout of the sequential kernel (two lanes per column above 128
+    # columns, four below; rows not a multiple of the lane count), with padding, a reset and an
+    # initial state, against the f64 oracle
+    f = splitmix_tokens(91 + K, 2, 33, 2, K, V)
+    q, k, v = (x.astype(np.float32) for x in f[:3])
+    valid = np.ones((2, 33), bool)
+    valid[1, 25:] = False
+    reset = np.zeros((2, 33), bool)
+    reset[0, 11] = True
+    init = (0.1 * np.random.default_rng(K).standard_normal((2, 2, K, V))).astype(np.float32)
+    out, fin, sco = O.scan(q, k, v, *f[3:], valid, reset, init)
+    r = dbl.gdn_training_scan(*(dev_t(x, cuda) for x in (q, k, v, *f[3:], valid, reset, init)), 16)
+    assert rel_err(host(r.output), out) < TOL_F32
+    assert rel_err(host(r.final_state), fin) < TOL_F32
+    assert rel_err(host(r.scores[..., 0]), sco) < TOL_F32
+
+
 def test_training_scan_bf16_inputs(cuda, native_lib):
     f = splitmix_tokens(77, 2, 40, 3, 32, 64)
     q, k, v = (bf16_round(x.astype(np.float32)) for x in f[:3])
@@ -292,7 +311,7 @@ def test_prefill_tc_span_transition(cuda, native_lib):
 
 
 # ----------------------------------------------------------------------- training-scan backward
-@pytest.mark.parametrize("K,V,chunk", [(32, 64, 16), (64, 128, 5), (20, 40, 1)])
+@pytest.mark.parametrize("K,V,chunk", [(32, 64, 16), (64, 128, 5), (20, 40, 1), (48, 160, 7), (24, 200, 16)])
 def test_training_backward_matches_oracle(cuda, native_lib, K, V, chunk):
     # gdn_training_backward (gdn_training.rs:117-284) against the f64 oracle, which is itself
     # pinned by finite differences (tests/test_oracle.py); padding, resets, an initial state and
