@@ -668,14 +668,17 @@ int make_map64(CUtensorMap* m, const void* base, int64_t outer, int64_t H, int64
 extern "C" int dbl_relay_attention_forward(const dbl_relay_attention_args* a, dbl_stream_t stream) {
     using namespace dbl;
     if (!a) return fail(DBL_ERR_INVALID_ARGUMENT, "relay_attention_forward: null args");
-    if (a->batch <= 0 || a->heads <= 0 || a->time <= 0 || a->documents <= 0)
-        return fail(DBL_ERR_INVALID_ARGUMENT, "relay_attention_forward: batch, heads, tokens and documents must be positive");
+    if (a->batch <= 0 || a->heads <= 0 || a->time <= 0 || a->documents < 0)
+        return fail(DBL_ERR_INVALID_ARGUMENT,
+                    "relay_attention_forward: batch, heads and tokens must be positive, documents non-negative");
     if (a->head_dim != D)
         return fail(DBL_ERR_UNSUPPORTED, "relay_attention_forward: head width must be 64 (relay_attention_kernel.rs asserts it)");
     if (a->dtype != DBL_F32 && a->dtype != DBL_BF16)
         return fail(DBL_ERR_INVALID_ARGUMENT, "relay_attention_forward: dtype must be f32 or bf16");
-    if (!a->q || !a->k || !a->v || !a->relay_k || !a->relay_v || !a->doc_id || !a->doc_start || !a->doc_end || !a->o ||
-        !a->normalization)
+    // with no documents (a batch of padding) the relay slots are empty and may be null
+    const bool has_docs = a->documents > 0;
+    if (!a->q || !a->k || !a->v || (has_docs && (!a->relay_k || !a->relay_v)) || !a->doc_id || !a->doc_start ||
+        !a->doc_end || !a->o || !a->normalization)
         return fail(DBL_ERR_INVALID_ARGUMENT, "relay_attention_forward: every pointer is required");
     if (!aligned(a->q, 16) || !aligned(a->k, 16) || !aligned(a->v, 16) || !aligned(a->relay_k, 16) ||
         !aligned(a->relay_v, 16) || !aligned(a->o, 16) || !aligned(a->normalization, 8))
@@ -710,8 +713,14 @@ extern "C" int dbl_relay_attention_forward(const dbl_relay_attention_args* a, db
     rc = make_map64(&mq, a->q, a->batch, a->heads, a->time, 128);
     if (rc == DBL_OK) rc = make_map64(&mk, a->k, a->batch, a->heads, a->time, 128);
     if (rc == DBL_OK) rc = make_map64(&mv, a->v, a->batch, a->heads, a->time, 128);
-    if (rc == DBL_OK) rc = make_map64(&mrk, a->relay_k, a->documents, a->heads, SLOTS, SLOTS);
-    if (rc == DBL_OK) rc = make_map64(&mrv, a->relay_v, a->documents, a->heads, SLOTS, SLOTS);
+    // no documents: no row can reach a relay slot (its document id is out of range), so the relay
+    // maps only need to be valid descriptors; they cover q
+    if (rc == DBL_OK)
+        rc = has_docs ? make_map64(&mrk, a->relay_k, a->documents, a->heads, SLOTS, SLOTS)
+                      : make_map64(&mrk, a->q, a->batch, a->heads, a->time, SLOTS);
+    if (rc == DBL_OK)
+        rc = has_docs ? make_map64(&mrv, a->relay_v, a->documents, a->heads, SLOTS, SLOTS)
+                      : make_map64(&mrv, a->q, a->batch, a->heads, a->time, SLOTS);
     if (rc != DBL_OK) return rc;
     static std::atomic<uint64_t> attr_done{0};
     rc = once_per_device(attr_done, [] {

@@ -308,7 +308,8 @@ int dbl_relay_merge_decode_noalloc(const dbl_relay_merge_args *args, dbl_stream_
  * (doc_end < doc_start) writes o = 0 and (0, 1), as the reference.  head_dim must be 64 (the
  * reference asserts it).  All arrays contiguous and 16-byte aligned.  The forward's unused layout
  * tensors (doc_row, relay_start, relay_end) are not taken.  A live row whose doc_id is outside
- * [0, documents) gets no relay slots and records device error 101 (dbl_device_error). */
+ * [0, documents) gets no relay slots and records device error 101 (dbl_device_error).  documents
+ * may be 0 (a batch of padding; relay_k and relay_v may then be NULL). */
 typedef struct {
     int64_t batch, heads, time, head_dim, documents;
     int32_t dtype;

@@ -480,6 +480,21 @@ def test_relay_attention_ignores_nan_padding(cuda, native_lib, dtype):
     np.testing.assert_array_equal(dirty[1], clean[1])
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_relay_attention_all_padding_no_documents(cuda, native_lib, dtype):
+    # a batch without documents (document capacity 0, relay tensors [0, H, 16, 64]): every row is
+    # padding and gives o = 0 and (0, 1), as relay_attention_kernel.rs:113-123
+    B, H, T = 2, 3, 150
+    di, ds, de, nd = _packed_layout([[], []], T)
+    assert nd == 0
+    x = [torch.randn(B, H, T, 64, device=cuda).to(dtype) for _ in range(3)]
+    r = [torch.zeros(0, H, 16, 64, device=cuda, dtype=dtype) for _ in range(2)]
+    o, norm = dbl.relay_attention_forward(*x, *r, *(torch.as_tensor(a, device=cuda) for a in (di, ds, de)))
+    torch.cuda.synchronize()
+    assert native_device_ok()
+    assert torch.all(o == 0) and torch.all(norm[..., 0] == 0) and torch.all(norm[..., 1] == 1)
+
+
 def test_relay_attention_rejects_bad_shapes(cuda, native_lib):
     q = torch.zeros(1, 1, 4, 32, device=cuda)
     ids = torch.zeros(1, 4, dtype=torch.int32, device=cuda)
