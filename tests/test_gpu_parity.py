@@ -550,3 +550,37 @@ def test_prefill_from_host_matches_device(cuda, native_lib):
     assert torch.equal(ho, ref_o.cpu()) and torch.equal(hf, ref_f.cpu())
     with pytest.raises(ValueError):
         dbl.gdn2_prefill_host(q.to(cuda), k, v, alpha, beta)
+
+
+# ------------------------------------------------------------------------- single-token inputs
+def test_single_token_inputs(cuda, native_lib):
+    # T = 1 through the prologue (no conv history), relay attention (a window of one key plus the
+    # relay slots) and the gdn2_scan backward (one token, one document), against the oracles
+    rng = np.random.default_rng(5)
+    H, K, V, W = 2, 32, 64, 4
+    proj = [rng.standard_normal((1, 1, H * K)), rng.standard_normal((1, 1, H * K)), rng.standard_normal((1, 1, H * V)),
+            rng.standard_normal((1, 1, H * K)), rng.standard_normal((1, 1, H * K)), rng.standard_normal((1, 1, H * V))]
+    conv = [0.3 * rng.standard_normal((W, H * K)), 0.3 * rng.standard_normal((W, H * K)),
+            0.3 * rng.standard_normal((W, H * V))]
+    bias, scale = 0.5 * rng.standard_normal(H * K), 0.3 * rng.standard_normal(H)
+    one, zero = np.ones((1, 1)), np.zeros((1, 1))
+    d = lambda x: torch.as_tensor(np.asarray(x, np.float32), device=cuda)  # noqa: E731
+    got = dbl.gdn2_prologue(*(d(x) for x in proj), *(d(x) for x in conv), d(bias), d(scale), d(one), d(zero), heads=H)
+    ref = O.gdn2_prologue(*proj, *conv, bias, scale, one, zero, heads=H)
+    for g, r in zip(got, ref):
+        assert rel_err(g.cpu().numpy(), r) < 2e-5
+    for dtype in (torch.float32, torch.bfloat16):
+        q, k, v, rk, rv, di, ds, de = _relay_inputs([[1]], 1, H, 7, dtype)
+        o, norm = _relay_run(cuda, dtype, q, k, v, rk, rv, di, ds, de)
+        eo, en = O.relay_window(q, k, v, rk, rv, di, ds, de)
+        _relay_check(o, norm, eo, en, dtype)
+    q, k = rng.standard_normal((1, 1, H, K)) / 6, rng.standard_normal((1, 1, H, K)) / 6
+    v, w = rng.standard_normal((1, 1, H, V)), rng.random((1, 1, H, V))
+    a, e = rng.uniform(0.5, 1.0, (1, 1, H, K)), rng.random((1, 1, H, K))
+    go = rng.standard_normal((1, 1, H, V))
+    ds1, de1 = np.zeros((1, 1), np.int32), np.zeros((1, 1), np.int32)
+    got = dbl.gdn2_scan_backward(*(d(x) for x in (q, k, v, a, e, w)), torch.as_tensor(ds1, device=cuda),
+                                 torch.as_tensor(de1, device=cuda), d(go))
+    ref = O.doc_backward(q, k, v, a, e, w, ds1, de1, go)
+    for g, r in zip(got, ref):
+        assert rel_err(g.cpu().numpy(), r) < TOL_F32
