@@ -522,12 +522,25 @@ def bench_backward(torch, args, dev):
     ms_b = timed(lambda: dbl.gdn_training_backward(q, k, v, a, e, w, valid, reset, init, go, gf, gs, chunk_size=16))
     ms_f = timed(lambda: dbl.gdn_training_scan(q, k, v, a, e, w, valid, reset, init, 16))
     tokens = b * t
-    return {"metric": "GDN-2 training scan backward Mtok/s (gdn_training_backward)",
+    line = {"metric": "GDN-2 training scan backward Mtok/s (gdn_training_backward)",
             "value": tokens / (ms_b / 1e3) / 1e6, "unit": "Mtok/s", "ms_per_step": ms_b, "n_gpus": 1,
             "higher_is_better": True, "dtype": "f32", "data": "synthetic",
             "config": {"workload": f"B{b}/T{t}/H{h}/K{k_}/V{v_} f32 chunk 16 (the reference's training shape)",
                        "forward_ms": ms_f, "forward_mtok_s": tokens / (ms_f / 1e3) / 1e6},
-            "gpu_launches": 10}
+            "gpu_launches": 10 + 10}
+    if not args.no_cpu_baseline:
+        # the f64 C restatement of the reference's backward on one (b) row of the workload
+        sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+        from oracle import oracle as O
+        host = [x[:1].double().cpu().numpy() for x in (q, k, v, a, e, w, go, gf, gs)]
+        c0 = time.perf_counter()
+        O.training_backward(*host[:7], host[7], host[8], valid[:1].cpu().numpy() > 0, reset[:1].cpu().numpy() > 0,
+                            init[:1].double().cpu().numpy())
+        sec = time.perf_counter() - c0
+        line["cpu_baseline"] = {"value": t / sec / 1e6, "unit": "Mtok/s", "cores": 1, "kind": "port",
+                                "sample": f"B1/T{t}/H{h}/K{k_}/V{v_}, f64 C restatement of gdn_training.rs:117-284, "
+                                          f"{sec:.2f} s"}
+    return line
 
 
 def bench_prologue(torch, args, dev):
@@ -561,12 +574,25 @@ def bench_prologue(torch, args, dev):
     # per token-head: 6 bf16 projection rows in; q, k, v bf16 and alpha, erase, write f32 out
     alg = b * t * h * (6 * d * 2 + 3 * d * 2 + 3 * d * 4)
     gbs = alg / (ms / 1e3) / 1e9
-    return {"metric": "GDN-2 mixer prologue Mtok/s", "value": b * t / (ms / 1e3) / 1e6, "unit": "Mtok/s",
+    line = {"metric": "GDN-2 mixer prologue Mtok/s", "value": b * t / (ms / 1e3) / 1e6, "unit": "Mtok/s",
             "ms_per_step": ms, "n_gpus": 1, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": f"B{b}/T{t}/H{h}/K=V={d}, conv width 4, bf16 in/out, f32 gates"},
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
                          "peak_source": src, "algorithmic_bytes_per_launch": alg},
             "gpu_launches": reps}
+    if not args.no_cpu_baseline:
+        # the numpy restatement of the prologue (f64) on the first 1024 tokens of one row
+        sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+        from oracle import oracle as O
+        ts = 1024
+        host = [x[:1, :ts].float().cpu().numpy() for x in proj]
+        c0 = time.perf_counter()
+        O.gdn2_prologue(*host, *(x.cpu().numpy() for x in conv), bias.cpu().numpy(), scale.cpu().numpy(),
+                        valid[:1, :ts].cpu().numpy(), reset[:1, :ts].cpu().numpy(), heads=h)
+        sec = time.perf_counter() - c0
+        line["cpu_baseline"] = {"value": ts / sec / 1e6, "unit": "Mtok/s", "cores": 1, "kind": "port",
+                                "sample": f"B1/T{ts}/H{h}/K=V={d}, numpy f64 restatement of lib.rs:446-528, {sec:.2f} s"}
+    return line
 
 
 def bench_relay_attn(torch, args, dev, with_cpu=True):
