@@ -584,3 +584,77 @@ def test_single_token_inputs(cuda, native_lib):
     ref = O.doc_backward(q, k, v, a, e, w, ds1, de1, go)
     for g, r in zip(got, ref):
         assert rel_err(g.cpu().numpy(), r) < TOL_F32
+
+
+# --------------------------------------------------------------- full-size, size-independent checks
+def test_prefill_full_size_linear_in_values_and_permutation(cuda, native_lib):
+    # BASELINE config 1 (B8/H16/T4096/d128 bf16) for every head: the output and final state are
+    # linear in v for a zero initial state, so doubling v doubles them (to 1e-3: doubling is exact in
+    # floating point except where the kernel's fp16 operands are subnormal); permuting the batch
+    # permutes them bit for bit (each (b, h) is computed on its own, so no pair leaks into another).
+    import bench
+    q, k, v, alpha, beta = bench.make_prefill_inputs(torch, cuda, 4321)
+    o1, f1 = dbl.gdn2_prefill(q, k, v, alpha, beta)
+    o2, f2 = dbl.gdn2_prefill(q, k, v * 2, alpha, beta)
+    perm = torch.tensor([3, 0, 7, 1, 6, 2, 5, 4], device=cuda)
+    o3, f3 = dbl.gdn2_prefill(q[perm], k[perm], v[perm], alpha[perm], beta[perm])
+    torch.cuda.synchronize()
+    assert _device_error_clear(native_lib) == (0, 0)
+    assert torch.isfinite(o1.float()).all() and torch.isfinite(f1).all()
+    assert rel_err(host(o2.float()), 2 * host(o1.float())) < 1e-3 and rel_err(host(f2), 2 * host(f1)) < 1e-3
+    assert torch.equal(o3, o1[perm]) and torch.equal(f3, f1[perm])
+
+
+def test_prologue_full_size_sampled(cuda, native_lib):
+    # the prologue at the config-1 shape (B8/T4096/H16, K = V = 128, bf16), three (b, head, token
+    # window) slices against the oracle, each window with its conv history
+    b_, t_, h_, d = 8, 4096, 16, 128
+    g = torch.Generator(device=cuda)
+    g.manual_seed(13)
+    proj = [torch.randn(b_, t_, h_ * d, device=cuda, generator=g).bfloat16() for _ in range(6)]
+    conv = [0.3 * torch.randn(4, h_ * d, device=cuda, generator=g) for _ in range(3)]
+    bias, scale = torch.randn(h_ * d, device=cuda, generator=g), 0.3 * torch.randn(h_, device=cuda, generator=g)
+    valid = torch.ones(b_, t_, device=cuda)
+    reset = (torch.rand(b_, t_, device=cuda, generator=g) > 0.99).float()
+    got = dbl.gdn2_prologue(*proj, *conv, bias, scale, valid, reset, heads=h_, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    for b, h, t0 in ((0, 0, 0), (5, 11, 2000), (7, 15, 4096 - 200)):
+        lo, hi = max(0, t0 - 8), min(t_, t0 + 200)
+        cols = slice(h * d, (h + 1) * d)
+        ref = O.gdn2_prologue(*(host(x[b:b + 1, lo:hi, cols]) for x in proj), *(host(c[:, cols]) for c in conv),
+                              host(bias[cols]), host(scale[h:h + 1]), host(valid[b:b + 1, lo:hi]),
+                              host(reset[b:b + 1, lo:hi]), heads=1)
+        # the first rows of the window lack their conv history unless the window starts at t = 0
+        skip = 0 if lo == 0 else 8
+        for gi, r in zip(got, ref):
+            g_slice = host(gi[b:b + 1, lo:hi, h:h + 1].float())
+            tol = 2e-6 if gi.dtype == torch.float32 else TOL_BF16
+            if gi.dtype == torch.float32:
+                assert np.abs(g_slice[:, skip:] - r[:, skip:]).max() < tol
+            else:
+                assert rel_err(g_slice[:, skip:], r[:, skip:]) < tol
+
+
+def test_relay_attention_full_size_sampled(cuda, native_lib):
+    # reference-layout relay attention at the bench shape (B8/H16/T4096, 1024-token documents,
+    # bf16): three (b, h) heads against the oracle, and every row finite
+    b_, h_, t_, dl = 8, 16, 4096, 1024
+    nd = b_ * t_ // dl
+    g = torch.Generator(device=cuda)
+    g.manual_seed(17)
+    x = [torch.randn(b_, h_, t_, 64, device=cuda, generator=g).bfloat16() for _ in range(3)]
+    r = [torch.randn(nd, h_, 16, 64, device=cuda, generator=g).bfloat16() for _ in range(2)]
+    pos = torch.arange(t_, device=cuda, dtype=torch.int32)
+    ds = (pos // dl * dl).expand(b_, t_).contiguous()
+    de = (ds + dl - 1).contiguous()
+    di = (torch.arange(b_, device=cuda, dtype=torch.int32)[:, None] * (t_ // dl) + pos // dl).contiguous()
+    o, norm = dbl.relay_attention_forward(*x, *r, di, ds, de)
+    torch.cuda.synchronize()
+    assert native_device_ok()
+    assert torch.isfinite(o.float()).all() and torch.isfinite(norm).all()
+    for b, h in ((0, 0), (3, 9), (7, 15)):
+        # the head's documents are b * 4 .. b * 4 + 3 (relay slots of this head only)
+        eo, en = O.relay_window(*(host(t[b:b + 1, h:h + 1].float()) for t in x),
+                                *(host(t[4 * b:4 * b + 4, h:h + 1].float()) for t in r),
+                                host(di[b:b + 1]) - 4 * b, host(ds[b:b + 1]), host(de[b:b + 1]))
+        _relay_check(host(o[b:b + 1, h:h + 1].float()), host(norm[b:b + 1, h:h + 1]), eo, en, torch.bfloat16)
