@@ -38,6 +38,7 @@ struct BwdParams {
     float *dq, *dk, *dv, *dalpha, *derase, *dwrite, *dinitial;
     float *ck;  // [B*H][nch][K][V] chunk-start states
     float *rp;  // [B*H][C][K][V]   previous state of each token of the chunk being reversed
+    int rp_shared;  // 1: those states live in shared memory ([C][K][cols + 8]) instead of rp
 };
 
 // One level of a reduce-scatter over the lanes that differ in lane bit `o`: the lower lane keeps
@@ -120,6 +121,11 @@ __global__ void __launch_bounds__(512) training_backward_kernel(const BwdParams 
     float* red = reinterpret_cast<float*>(dyn_raw + L.red); // [2][nwarps][4][KMAX]
     int* sact = reinterpret_cast<int*>(dyn_raw + L.act);
     int* srst = reinterpret_cast<int*>(dyn_raw + L.rst);
+    // the replayed previous states of the chunk: shared memory when they fit (row stride cols + 8
+    // puts the four row-group lanes of a column on different banks), else this CTA's workspace rows
+    const int rstride = p.rp_shared ? cols + 8 : p.V;
+    float* rpb = p.rp_shared ? reinterpret_cast<float*>(dyn_raw + L.total)
+                             : p.rp + (size_t)blockIdx.x * p.C * p.K * p.V;
 
     const int bh = blockIdx.x;
     const int b = bh / p.H, h = bh - b * p.H;
@@ -206,10 +212,10 @@ __global__ void __launch_bounds__(512) training_backward_kernel(const BwdParams 
         stage(t0, n, true);
 #pragma unroll 1
         for (int r = 0; r < n; ++r) {
-            float* rpr = p.rp + ((size_t)bh * p.C + r) * K * V;
+            float* rpr = rpb + (size_t)r * K * rstride;
 #pragma unroll
             for (int u = 0; u < R; ++u)
-                if (row_ok(u)) rpr[(size_t)(g + TPC * u) * V + j] = S[u];
+                if (row_ok(u)) rpr[(size_t)(g + TPC * u) * rstride + j] = S[u];
             const float x = step(S, r);
             if (g == 0 && col) sxe[r * cols + j] = x;
         }
@@ -244,10 +250,10 @@ __global__ void __launch_bounds__(512) training_backward_kernel(const BwdParams 
                 continue;
             }
             const float wr = (col && g == 0) ? p.write[tv + j] : 0.f, vr = (col && g == 0) ? p.v[tv + j] : 0.f;
-            const float* rpr = p.rp + ((size_t)bh * p.C + r) * K * V;
+            const float* rpr = rpb + (size_t)r * K * rstride;
             float prev[R];
 #pragma unroll
-            for (int u = 0; u < R; ++u) prev[u] = row_ok(u) ? rpr[(size_t)(g + TPC * u) * V + j] : 0.f;
+            for (int u = 0; u < R; ++u) prev[u] = row_ok(u) ? rpr[(size_t)(g + TPC * u) * rstride + j] : 0.f;
             const bool rst = srst[r];
             const float enorm = sqrtf(sen[r]), knorm = sqrtf(skn[r]);
             const bool norms = knorm > 0.f && enorm > 0.f;
@@ -384,7 +390,11 @@ extern "C" int dbl_gdn_training_scan_backward(const dbl_training_scan_backward_a
     // four lanes per value column up to 128 columns, two beyond (at most 512 threads)
     const int tpc = p.V <= 128 ? 4 : 2;
     const int threads = (p.V * tpc + 31) / 32 * 32, nwarps = threads / 32;
-    const size_t dyn = bwd_smem(p.K <= 32 ? 32 : 64, nwarps * (32 / tpc), nwarps).total;
+    const int cols = nwarps * (32 / tpc);
+    const size_t base_smem = bwd_smem(p.K <= 32 ? 32 : 64, cols, nwarps).total;
+    const size_t rp_smem = (size_t)p.C * p.K * (cols + 8) * sizeof(float);
+    p.rp_shared = base_smem + rp_smem <= 200 * 1024 ? 1 : 0;  // a chunk's replayed states fit on chip
+    const size_t dyn = base_smem + (p.rp_shared ? rp_smem : 0);
     auto go = [&](auto kernel) {
         if (dyn > 48 * 1024) {
             const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
