@@ -363,7 +363,7 @@ def bench_long(torch, dist, args, dev, rank, world):
     q, k, v, alpha, beta = make_prefill_inputs(torch, dev, 777 + rank, b=1, t=hi - lo)
     stream = torch.cuda.current_stream(dev)
 
-    segs = shard.pick_segments(hi - lo, H)
+    segs = shard.pick_segments(hi - lo, H, shard.sm_count(dev))
 
     def step():
         return shard.time_sharded_prefill(q, k, v, alpha, beta, segments=segs)

@@ -69,9 +69,18 @@ def exchange_span_states(first_or_transition: torch.Tensor, offset: Optional[tor
     return As, Bs
 
 
+def sm_count(device: Optional[torch.device] = None) -> int:
+    """Streaming multiprocessors of `device` (the current CUDA device by default; 148 on a B200)."""
+    if not torch.cuda.is_available():
+        return 148
+    return torch.cuda.get_device_properties(device if device is not None else torch.cuda.current_device()
+                                            ).multi_processor_count
+
+
 def pick_segments(t_span: int, heads: int, sms: int = 148) -> int:
     """Segments per span: the largest power of two with segments x heads <= sms whose segments are
-    whole 64-token chunks (1 when the span is short or heads alone fill the GPU)."""
+    whole 64-token chunks (1 when the span is short or heads alone fill the GPU).  `sms` is the
+    device's SM count (``sm_count``)."""
     s = 1
     while (s * 2) * heads <= sms and t_span % (s * 2 * CHUNK) == 0:
         s *= 2
@@ -125,7 +134,7 @@ def segmented_prefill(q, k, v, alpha, beta, *, segments: Optional[int] = None, s
     if q.shape[0] != 1:
         raise ValueError("segmented_prefill handles one sequence (batch 1)")
     T, H = q.shape[1], q.shape[2]
-    S = segments or pick_segments(T, H)
+    S = segments or pick_segments(T, H, sm_count(q.device))
     if S == 1 or T % S:
         return kernels.gdn2_prefill(q, k, v, alpha, beta, scale=scale,
                                     initial_state=start if start is not None else initial_state,
@@ -160,7 +169,7 @@ def time_sharded_prefill(q, k, v, alpha, beta, *, group=None, scale: Optional[fl
         return segmented_prefill(q, k, v, alpha, beta, segments=segments, scale=scale,
                                  initial_state=initial_state, chunk_size=chunk_size)
     T, H = q.shape[1], q.shape[2]
-    S = segments or pick_segments(T, H)
+    S = segments or pick_segments(T, H, sm_count(q.device))
     if S == 1 or T % S:
         # unsegmented span: rank 0 scans from the initial state, the others hand off (A_g, B_g)
         if rank == 0:
