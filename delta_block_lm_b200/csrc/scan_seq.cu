@@ -21,7 +21,7 @@ namespace dbl {
 
 namespace {
 
-constexpr int TOK = 8;
+constexpr int TOKB = 8;  // tokens staged per group (doubled for small key widths)
 
 // TPC lanes share value column j (lane / TPC within the warp's group of 32 / TPC columns); lane g =
 // lane % TPC owns state rows i = g, g + TPC, g + 2 TPC, ... (strided, so that the TPC lanes read
@@ -37,6 +37,8 @@ __device__ __forceinline__ float row_sum(float x) {
 template <int KMAX, typename T, bool SCALAR, int TPC>
 __global__ void __launch_bounds__(512) seq_scan_kernel(const SeqParams p) {
     constexpr int R = KMAX / TPC;
+    // tokens staged per group: 16 where the group's arrays still fit the static shared memory
+    constexpr int TOK = KMAX <= 32 ? 2 * TOKB : TOKB;
     __shared__ float sk[TOK][KMAX], sq[TOK][KMAX];
     __shared__ float sa[SCALAR ? 1 : TOK][KMAX], se[SCALAR ? 1 : TOK][KMAX];  // se: erase_i k_i
     __shared__ float sga[TOK], sgb[TOK];  // scalar gates
