@@ -357,14 +357,15 @@ __global__ void __launch_bounds__(NTH, 1)
                     if (cs + e >= clo && cs + e <= chi) mraw = fmaxf(mraw, __uint_as_float(v[e]));
             }
         };
-        for (int c = c0; c < c1; c += 2) {  // two chunks per TMEM wait
-            uint32_t v0[16], v1[16];
-            tmem_ld16(trow + cb + 16 * c, v0);
-            if (c + 1 < c1) tmem_ld16(trow + cb + 16 * (c + 1), v1);
-            tmem_ld_wait();
-            max_chunk(v0, cb + 16 * c);
-            if (c + 1 < c1) max_chunk(v1, cb + 16 * (c + 1));
-        }
+        // the warp's 4 or 5 chunks stay in registers for both passes: one TMEM wait
+        uint32_t sv[80];
+        tmem_ld32(trow + cb + 16 * c0, &sv[0]);
+        tmem_ld32(trow + cb + 16 * (c0 + 2), &sv[32]);
+        if (c0 + 4 < c1) tmem_ld16(trow + cb + 16 * (c0 + 4), *reinterpret_cast<uint32_t(*)[16]>(&sv[64]));
+        tmem_ld_wait();
+#pragma unroll
+        for (int k = 0; k < 5; ++k)
+            if (c0 + k < c1) max_chunk(*reinterpret_cast<const uint32_t(*)[16]>(&sv[16 * k]), cb + 16 * (c0 + k));
         float m = mraw * SCALE;
         // relay scores (column group 0): this row's document group of the relay columns
         if (g == 0) {
@@ -388,10 +389,11 @@ __global__ void __launch_bounds__(NTH, 1)
         __syncthreads();
         m = fmaxf(fmaxf(smax[r], smax[128 + r]), fmaxf(smax[256 + r], smax[384 + r]));
         float total = 0.f;
-        uint32_t pk[5][8];
         // p = exp(s / 8 - m) packed to bf16 pairs; s / 8 - m is formed exactly before the
-        // exponential (scores far below zero stay exact)
-        auto exp_chunk = [&](const uint32_t (&v)[16], int cs, uint32_t (&out)[8]) {
+        // exponential (scores far below zero stay exact).  The pairs of a chunk overwrite the
+        // first half of its registers (pair e / 2 is written after scores e, e + 1 are read).
+        auto exp_chunk = [&](uint32_t (&v)[16], int cs) {
+            uint32_t (&out)[16] = v;
             if (__all_sync(0xffffffffu, cs >= clo && cs + 15 <= chi)) {
 #pragma unroll
                 for (int e = 0; e < 16; e += 2) {
@@ -416,17 +418,8 @@ __global__ void __launch_bounds__(NTH, 1)
             }
         };
 #pragma unroll
-        for (int k = 0; k < 5; k += 2) {
-            const int c = c0 + k;
-            if (c < c1) {
-                uint32_t v0[16], v1[16];
-                tmem_ld16(trow + cb + 16 * c, v0);
-                if (c + 1 < c1) tmem_ld16(trow + cb + 16 * (c + 1), v1);
-                tmem_ld_wait();
-                exp_chunk(v0, cb + 16 * c, pk[k]);
-                if (k + 1 < 5 && c + 1 < c1) exp_chunk(v1, cb + 16 * (c + 1), pk[k + 1]);
-            }
-        }
+        for (int k = 0; k < 5; ++k)
+            if (c0 + k < c1) exp_chunk(*reinterpret_cast<uint32_t(*)[16]>(&sv[16 * k]), cb + 16 * (c0 + k));
         uint32_t prk[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
         if (g == 0 && rdoc >= 0) {
             float pr[SLOTS];
@@ -448,7 +441,8 @@ __global__ void __launch_bounds__(NTH, 1)
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < 5; ++k)
-            if (c0 + k < c1) tmem_st8(trow + (uint32_t)(16 * qd + 8 * (c0 + k)), pk[k]);
+            if (c0 + k < c1)
+                tmem_st8(trow + (uint32_t)(16 * qd + 8 * (c0 + k)), *reinterpret_cast<const uint32_t(*)[8]>(&sv[16 * k]));
         {
             // P columns outside the lane quarter's span [16 qd, 16 qd + 144) are zero: six groups of 8
             const uint32_t zero[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
