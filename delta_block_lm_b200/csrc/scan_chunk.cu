@@ -1,0 +1,458 @@
+// Chunked GDN-2 scan for the reference's training widths: the stateful recurrence of
+// scan_seq.cu (gdn_training.rs:12-115; gdn2.rs:23-283 for document limits) rewritten so that the
+// work between chunk boundaries is state-independent and runs for every chunk at once.
+//
+// Within a chunk of C tokens, with per-channel step factors f_t = 0 at a reset, alpha_t for
+// other valid tokens and 1 for padding, the cumulative decays P_t = f_0 ... f_t and the pairwise
+// products d[t][s] = f_{s+1} ... f_t (formed directly, never as ratios of cumulative products),
+// the state after token t is S_t = P_t (.) S_0 + sum_{s <= t} d[t][s] (.) k_s edit_s^T.  The edits
+// solve the unit lower-triangular system (I + A) edit = WV - B S_0 with
+//   A[t][s] = sum_i (erase k)_t,i d[t][s]_i k_s,i (s < t),   B[t] = (erase k)_t (.) P_t,
+// so with Ti = (I + A)^-1, U0 = Ti WV and B' = Ti B, edit = U0 - B' S_0, and
+//   o   = (Q' - M B') S_0 + M U0,   Q'[t] = q_t (.) P_t,  M[t][s] = sum_i q_t,i d[t][s]_i k_s,i (s <= t)
+//   S_C = (diag(P_last) - Wd^T B') S_0 + Wd^T U0,   Wd[s] = d[last][s] (.) k_s.
+// Padding tokens have no edit and no output (their rows of WV, B and the output maps are zero).
+//
+// chunk_prep_kernel: one CTA per (b, h, chunk) builds the chunk's maps Qe = Q' - M B', O0 = M U0,
+//   B', U0, G = diag(P_last) - Wd^T B', H = Wd^T U0 and |k_t|.
+// chunk_main_kernel: one CTA per (b, h, column group) walks the chunks with its state columns in
+//   shared memory (the columns of S evolve independently): o = Qe S + O0, edit = U0 - B' S (for
+//   the scores |k| |edit|), S <- G S + H.
+#include "scan_seq_params.cuh"
+
+#include <algorithm>
+
+namespace dbl {
+namespace {
+
+constexpr int CC = 16;      // tokens per chunk
+constexpr int CVMAX = 128;  // value width limit of the chunked path
+constexpr int CTH = 256;
+
+// Per-chunk block of the workspace, in floats.  The part every column group reads (Qe, B', G with
+// rows padded to KP = K rounded up to 4, plus 4, so that two rows read by one warp fall in different
+// banks; |k_t|) comes first, then the column-sliced part (O0, U0, H as rows of V).
+struct ChunkBlock {
+    int kp, qe, bp, g, kn, sh, o0, u0, hh, total;
+};
+__host__ __device__ inline ChunkBlock chunk_block(int K, int V) {
+    ChunkBlock L{};
+    L.kp = ((K + 3) & ~3) + 4;
+    int o = 0;
+    L.qe = o; o += CC * L.kp;
+    L.bp = o; o += CC * L.kp;
+    L.g = o; o += K * L.kp;
+    L.kn = o; o += CC;
+    L.sh = o;
+    L.o0 = o; o += CC * V;
+    L.u0 = o; o += CC * V;
+    L.hh = o; o += K * V;
+    L.total = (o + 3) & ~3;  // 16-byte aligned blocks
+    return L;
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    return x;
+}
+
+template <int KMAX, typename T>
+__global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, float* ws) {
+    constexpr int KPL = KMAX / 32;  // key channels per lane in the running products
+    __shared__ float sk[CC][KMAX], sq[CC][KMAX], sek[CC][KMAX], sf[CC][KMAX];
+    __shared__ float sP[CC][KMAX], sWd[CC][KMAX], sBp[CC][KMAX];
+    __shared__ float swv[CC][CVMAX], sU0[CC][CVMAX];
+    __shared__ float sA[CC][CC], sM[CC][CC], sTi[CC][CC];
+    __shared__ int sact[CC];
+    const int K = p.K, V = p.V;
+    const int nch = (p.T + CC - 1) / CC;
+    const int c = blockIdx.x % nch, bh = blockIdx.x / nch, b = bh / p.H, h = bh - (bh / p.H) * p.H;
+    const int t0 = c * CC, n = min(CC, p.T - t0);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const T* qb = static_cast<const T*>(p.q) + b * p.qs[0] + h * p.qs[2];
+    const T* kb = static_cast<const T*>(p.k) + b * p.ks[0] + h * p.ks[2];
+    const T* vb = static_cast<const T*>(p.v) + b * p.vs[0] + h * p.vs[2];
+    const bool scalar = p.gate_mode == 1;
+
+    // token masks: act (valid, in range), rst (reset)
+    if (tid < CC) {
+        const int t = t0 + tid;
+        int act = 0, rst = 0;
+        if (tid < n) {
+            if (p.mask_mode == 1) {
+                act = p.valid[(size_t)b * p.T + t] != 0.f;
+                rst = p.reset[(size_t)b * p.T + t] != 0.f;
+            } else if (p.mask_mode == 2) {
+                const int32_t st = p.doc_start[(size_t)b * p.T + t], en = p.doc_end[(size_t)b * p.T + t];
+                act = en >= st;
+                rst = st == t;
+            } else {
+                act = 1;
+            }
+        }
+        sact[tid] = act | (rst << 1);
+    }
+    __syncthreads();
+    // inputs: k, q (scaled), step factors f, erase k (zero for padding), write v (zero for padding)
+    for (int x = tid; x < CC * KMAX; x += CTH) {
+        const int u = x / KMAX, i = x - u * KMAX;
+        const int t = t0 + u;
+        const bool act = sact[u] & 1, rst = sact[u] & 2;
+        float kv = 0.f, qv = 0.f, f = 1.f, ek = 0.f;
+        if (u < n && i < K) {
+            kv = to_f32(kb[t * p.ks[1] + i * p.ks[3]]);
+            qv = to_f32(qb[t * p.qs[1] + i * p.qs[3]]) * p.scale;
+            if (act) {
+                float a, e;
+                if (scalar) {
+                    a = p.alpha[(size_t)b * p.as[0] + (size_t)t * p.as[1] + (size_t)h * p.as[2]];
+                    e = p.erase[(size_t)b * p.es[0] + (size_t)t * p.es[1] + (size_t)h * p.es[2]];
+                } else {
+                    a = p.alpha[(size_t)b * p.as[0] + (size_t)t * p.as[1] + (size_t)h * p.as[2] + (size_t)i * p.as[3]];
+                    e = p.erase[(size_t)b * p.es[0] + (size_t)t * p.es[1] + (size_t)h * p.es[2] + (size_t)i * p.es[3]];
+                }
+                f = rst ? 0.f : a;
+                ek = e * kv;
+            }
+        }
+        sk[u][i] = kv;
+        sq[u][i] = qv;
+        sf[u][i] = f;
+        sek[u][i] = ek;
+    }
+    for (int x = tid; x < CC * V; x += CTH) {
+        const int u = x / V, j = x - u * V;
+        const int t = t0 + u;
+        float wv = 0.f;
+        if (u < n && (sact[u] & 1)) {
+            const float vv = p.v_zero ? 0.f : to_f32(vb[t * p.vs[1] + j * p.vs[3]]);
+            const float w = scalar ? p.erase[(size_t)b * p.es[0] + (size_t)t * p.es[1] + (size_t)h * p.es[2]]
+                                   : p.write[(size_t)b * p.ws[0] + (size_t)t * p.ws[1] + (size_t)h * p.ws[2] +
+                                             (size_t)j * p.ws[3]];
+            wv = w * vv;
+        }
+        swv[u][j] = wv;
+    }
+    __syncthreads();
+
+    // running products: source s = -1 (the chunk start: P) and s = 0 .. C-1 (A, M, Wd); warp w takes
+    // the sources w - 1, w + 7, ... (lane l: channels l, l + 32)
+    for (int s = warp - 1; s < CC; s += CTH / 32) {
+        float prod[KPL];
+#pragma unroll
+        for (int e = 0; e < KPL; ++e) prod[e] = 1.f;
+        if (s >= 0) {
+            // the diagonal of M: d[s][s] = 1
+            float mq = 0.f;
+#pragma unroll
+            for (int e = 0; e < KPL; ++e) {
+                const int i = lane + 32 * e;
+                mq = fmaf(sq[s][i], sk[s][i], mq);
+            }
+            mq = warp_sum(mq);
+            if (lane == 0) {
+                sM[s][s] = mq;
+                sA[s][s] = 0.f;
+            }
+        }
+        for (int t = s + 1; t < CC; ++t) {
+            float aa = 0.f, mm = 0.f;
+#pragma unroll
+            for (int e = 0; e < KPL; ++e) {
+                const int i = lane + 32 * e;
+                prod[e] *= sf[t][i];
+                if (s < 0) {
+                    sP[t][i] = prod[e];
+                } else {
+                    const float dk = prod[e] * sk[s][i];
+                    aa = fmaf(sek[t][i], dk, aa);
+                    mm = fmaf(sq[t][i], dk, mm);
+                }
+            }
+            if (s >= 0) {
+                aa = warp_sum(aa);
+                mm = warp_sum(mm);
+                if (lane == 0) {
+                    sA[t][s] = aa;
+                    sM[t][s] = mm;
+                    sA[s][t] = 0.f;  // strictly lower triangular
+                    sM[s][t] = 0.f;
+                }
+            }
+        }
+        if (s >= 0) {
+#pragma unroll
+            for (int e = 0; e < KPL; ++e) sWd[s][lane + 32 * e] = prod[e] * sk[s][lane + 32 * e];
+        }
+    }
+    __syncthreads();
+    // Ti = (I + A)^-1: row t = e_t - sum_{s < t} A[t][s] Ti[s]  (warp 0, lane = column)
+    if (warp == 0) {
+        for (int t = 0; t < CC; ++t) {
+            if (lane < CC) {
+                float x = lane == t ? 1.f : 0.f;
+                for (int s = 0; s < t; ++s) x = fmaf(-sA[t][s], sTi[s][lane], x);
+                sTi[t][lane] = x;
+            }
+            __syncwarp();
+        }
+    }
+    __syncthreads();
+    // B' = Ti B (B[s] = (erase k)_s (.) P_s),  U0 = Ti WV
+    for (int x = tid; x < CC * KMAX; x += CTH) {
+        const int t = x / KMAX, i = x - t * KMAX;
+        float acc = 0.f;
+        for (int s = 0; s <= t; ++s) acc = fmaf(sTi[t][s], sek[s][i] * sP[s][i], acc);
+        sBp[t][i] = acc;
+    }
+    for (int x = tid; x < CC * V; x += CTH) {
+        const int t = x / V, j = x - t * V;
+        float acc = 0.f;
+        for (int s = 0; s <= t; ++s) acc = fmaf(sTi[t][s], swv[s][j], acc);
+        sU0[t][j] = acc;
+    }
+    __syncthreads();
+    // the chunk's maps, to the workspace
+    const ChunkBlock L = chunk_block(K, V);
+    const int KP = L.kp;
+    float* blk = ws + ((size_t)bh * nch + c) * L.total;
+    for (int x = tid; x < CC * K; x += CTH) {
+        const int t = x / K, i = x - t * K;
+        float qe = (sact[t] & 1) ? sq[t][i] * sP[t][i] : 0.f;
+        if (sact[t] & 1)
+            for (int s = 0; s <= t; ++s) qe = fmaf(-sM[t][s], sBp[s][i], qe);
+        blk[L.qe + t * KP + i] = qe;
+        blk[L.bp + t * KP + i] = sBp[t][i];
+    }
+    for (int x = tid; x < CC * V; x += CTH) {
+        const int t = x / V, j = x - t * V;
+        float o0 = 0.f;
+        if (sact[t] & 1)
+            for (int s = 0; s <= t; ++s) o0 = fmaf(sM[t][s], sU0[s][j], o0);
+        blk[L.o0 + x] = o0;
+        blk[L.u0 + x] = sU0[t][j];
+    }
+    for (int x = tid; x < K * K; x += CTH) {
+        const int i = x / K, i2 = x - i * K;
+        float g = i == i2 ? sP[CC - 1][i] : 0.f;
+        for (int s = 0; s < CC; ++s) g = fmaf(-sWd[s][i], sBp[s][i2], g);
+        blk[L.g + i * KP + i2] = g;
+    }
+    for (int x = tid; x < K * V; x += CTH) {
+        const int i = x / V, j = x - i * V;
+        float hv = 0.f;
+        for (int s = 0; s < CC; ++s) hv = fmaf(sWd[s][i], sU0[s][j], hv);
+        blk[L.hh + x] = hv;
+    }
+    if (warp == 0) {
+        for (int t = 0; t < CC; ++t) {
+            float kk = 0.f;
+            for (int i = lane; i < K; i += 32) kk = fmaf(sk[t][i], sk[t][i], kk);
+            kk = warp_sum(kk);
+            if (lane == 0) blk[L.kn + t] = (sact[t] & 1) ? sqrtf(kk) : 0.f;
+        }
+    }
+}
+
+// The sequential pass: one CTA per (b, h, column group of VG <= 64 columns), the group's state
+// columns S [K][VG] in shared memory (double-buffered), the chunk maps double-buffered by cp.async
+// so that chunk c + 1 loads while chunk c computes.  With one group the scores are written here;
+// with several, each group writes its partial sum of edit^2 per token to `part`.
+__global__ void __launch_bounds__(CTH) chunk_main_kernel(const SeqParams p, const float* ws, float* part,
+                                                         int VG, int ngroups) {
+    extern __shared__ __align__(16) float smain[];
+    const int K = p.K, V = p.V;
+    const int nch = (p.T + CC - 1) / CC;
+    const int grp = blockIdx.x % ngroups, bh = blockIdx.x / ngroups;
+    const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
+    const int c0 = grp * VG, vg = min(VG, V - c0);
+    const int tid = threadIdx.x;
+    const ChunkBlock L = chunk_block(K, V);
+    const int KP = L.kp;
+    const int rows = 2 * CC + K;                 // O0, U0, H rows
+    const int bfl = L.sh + rows * VG;            // floats per buffered chunk
+    float* Sb0 = smain;
+    float* Sb1 = smain + K * VG;
+    float* bb0 = smain + 2 * K * VG;
+    float* bb1 = bb0 + bfl;
+    float* ssq = bb1 + bfl;
+    const bool vec = (V & 3) == 0;
+    const size_t sbase = ((size_t)b * p.H + h) * K * V;
+    for (int x = tid; x < K * vg; x += CTH) {
+        const int i = x / vg, j = x - i * vg;
+        Sb0[i * VG + j] = p.init_mode == 1 ? p.initial[sbase + (size_t)i * V + c0 + j] : 0.f;
+    }
+    if (tid < CC) ssq[tid] = 0.f;
+    auto prefetch = [&](int c) {
+        const float* src = ws + ((size_t)bh * nch + c) * L.total;
+        float* dst = (c & 1) ? bb1 : bb0;
+        for (int x = tid; x < L.sh / 4; x += CTH) cp_async16(dst + 4 * x, src + 4 * x);
+        if (vec) {
+            const int q4 = vg >> 2;
+            for (int x = tid; x < rows * q4; x += CTH) {
+                const int r = x / q4, u = x - r * q4;
+                cp_async16(dst + L.sh + r * VG + 4 * u, src + L.sh + (size_t)r * V + c0 + 4 * u);
+            }
+        } else {
+            for (int x = tid; x < rows * vg; x += CTH) {
+                const int r = x / vg, u = x - r * vg;
+                cp_async4(dst + L.sh + r * VG + u, src + L.sh + (size_t)r * V + c0 + u);
+            }
+        }
+    };
+    prefetch(0);
+    cp_async_commit();
+    for (int c = 0; c < nch; ++c) {
+        const int t0 = c * CC, n = min(CC, p.T - t0);
+        if (c + 1 < nch) prefetch(c + 1);
+        cp_async_commit();
+        cp_async_wait1();
+        __syncthreads();  // chunk c's maps and the state are in place
+        const float* blk = (c & 1) ? bb1 : bb0;
+        const float* S = (c & 1) ? Sb1 : Sb0;
+        float* Sn = (c & 1) ? Sb0 : Sb1;
+        const float* qe = blk + L.qe;
+        const float* bp = blk + L.bp;
+        const float* o0 = blk + L.sh;
+        const float* u0 = o0 + CC * VG;
+        const float* hh = u0 + CC * VG;
+        const float* g = blk + L.g;
+        // o = Qe S + O0 and edit = U0 - B' S for (token, column) pairs
+        for (int x = tid; x < CC * vg; x += CTH) {
+            const int t = x / vg, j = x - t * vg;
+            float o = o0[t * VG + j], u = u0[t * VG + j];
+#pragma unroll 8
+            for (int i = 0; i < K; ++i) {
+                const float sv = S[i * VG + j];
+                o = fmaf(qe[t * KP + i], sv, o);
+                u = fmaf(-bp[t * KP + i], sv, u);
+            }
+            if (t < n) {
+                if (p.out) {
+                    const size_t oi = (size_t)b * p.os[0] + (size_t)(t0 + t) * p.os[1] + (size_t)h * p.os[2] +
+                                      (size_t)(c0 + j) * p.os[3];
+                    if (p.out_dtype == DBL_BF16) static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(o);
+                    else static_cast<float*>(p.out)[oi] = o;
+                }
+                if (p.scores) atomicAdd(&ssq[t], u * u);
+            }
+        }
+        // S <- G S + H into the other state buffer
+        for (int x = tid; x < K * vg; x += CTH) {
+            const int i = x / vg, j = x - i * vg;
+            float acc = hh[i * VG + j];
+#pragma unroll 8
+            for (int i2 = 0; i2 < K; ++i2) acc = fmaf(g[i * KP + i2], S[i2 * VG + j], acc);
+            Sn[i * VG + j] = acc;
+        }
+        // |k_t| is read before the barrier: the next prefetch into this buffer may start right after it
+        const float kn = (p.scores && tid < n) ? blk[L.kn + tid] : 0.f;
+        __syncthreads();
+        if (p.scores && tid < n) {
+            const size_t si = ((size_t)b * p.T + t0 + tid) * p.H + h;
+            if (ngroups == 1) p.scores[si] = kn * sqrtf(ssq[tid]);
+            else part[(size_t)grp * p.B * p.T * p.H + si] = ssq[tid];
+            ssq[tid] = 0.f;
+        }
+    }
+    if (p.final_state) {
+        const float* S = (nch & 1) ? Sb1 : Sb0;
+        for (int x = tid; x < K * vg; x += CTH) {
+            const int i = x / vg, j = x - i * vg;
+            p.final_state[sbase + (size_t)i * V + c0 + j] = S[i * VG + j];
+        }
+    }
+}
+
+// scores = |k_t| sqrt(sum over column groups of the partial edit^2 sums)
+__global__ void chunk_scores_kernel(const SeqParams p, const float* ws, const float* part, int ngroups) {
+    const size_t n = (size_t)p.B * p.T * p.H;
+    const size_t si = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (si >= n) return;
+    const int h = (int)(si % p.H), t = (int)((si / p.H) % p.T), b = (int)(si / ((size_t)p.H * p.T));
+    const int nch = (p.T + CC - 1) / CC;
+    const ChunkBlock L = chunk_block(p.K, p.V);
+    const float kn = ws[(((size_t)b * p.H + h) * nch + t / CC) * L.total + L.kn + t % CC];
+    float s = 0.f;
+    for (int g = 0; g < ngroups; ++g) s += part[(size_t)g * n + si];
+    p.scores[si] = kn * sqrtf(s);
+}
+}  // namespace
+
+// Whether the chunked path takes these shapes: key width <= 64, value width <= 128, a zero or given
+// initial state (not the identity of span transitions) and at least two chunks.
+bool chunk_scan_supported(const SeqParams& p) {
+    return p.K <= 64 && p.V <= CVMAX && p.init_mode != 2 && p.T >= 2 * CC;
+}
+
+// Runs the chunked scan; its workspace comes from the stream-ordered allocator and is released on
+// the stream after the last kernel.
+int launch_chunk_scan(const SeqParams& p, int in_dtype, cudaStream_t st) {
+    const int nch = (p.T + CC - 1) / CC;
+    const ChunkBlock L = chunk_block(p.K, p.V);
+    const int64_t bh = (int64_t)p.B * p.H;
+    // column groups: the widest of 64 / 32 / 16 columns that still gives a full wave of CTAs
+    int VG = 16;
+    for (int cand : {64, 32}) {
+        if (bh * ((p.V + cand - 1) / cand) >= 148) {
+            VG = cand;
+            break;
+        }
+    }
+    const int ngroups = (p.V + VG - 1) / VG;
+    if ((int64_t)bh * nch > 0x7fffffffLL || bh * ngroups > 0x7fffffffLL)
+        return fail(DBL_ERR_UNSUPPORTED, "chunk scan: grid exceeds 32-bit limits");
+    const size_t ws_floats = (size_t)bh * nch * L.total;
+    const size_t part_floats = (p.scores && ngroups > 1) ? (size_t)ngroups * bh * p.T : 0;
+    float* ws = nullptr;
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&ws), (ws_floats + part_floats) * sizeof(float), st);
+    if (e != cudaSuccess) return cuda_status(e, "chunk scan: workspace");
+    float* part = ws + ws_floats;
+    const bool bf = in_dtype == DBL_BF16;
+    const unsigned gprep = (unsigned)(bh * nch);
+    if (p.K <= 32) {
+        if (bf) chunk_prep_kernel<32, __nv_bfloat16><<<gprep, CTH, 0, st>>>(p, ws);
+        else chunk_prep_kernel<32, float><<<gprep, CTH, 0, st>>>(p, ws);
+    } else {
+        if (bf) chunk_prep_kernel<64, __nv_bfloat16><<<gprep, CTH, 0, st>>>(p, ws);
+        else chunk_prep_kernel<64, float><<<gprep, CTH, 0, st>>>(p, ws);
+    }
+    e = cudaGetLastError();
+    if (e == cudaSuccess) {
+        const size_t smem = ((size_t)2 * p.K * VG + 2 * ((size_t)L.sh + (2 * CC + p.K) * VG) + CC) * sizeof(float);
+        static std::atomic<uint64_t> attr_done{0};
+        const int rc = once_per_device(attr_done, [] {
+            return cuda_status(cudaFuncSetAttribute(chunk_main_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                    227 * 1024),
+                               "chunk scan: shared memory attribute");
+        });
+        if (rc != DBL_OK) {
+            cudaFreeAsync(ws, st);
+            return rc;
+        }
+        chunk_main_kernel<<<(unsigned)(bh * ngroups), CTH, smem, st>>>(p, ws, part, VG, ngroups);
+        e = cudaGetLastError();
+        if (e == cudaSuccess && part_floats) {
+            const size_t n = (size_t)bh * p.T;
+            chunk_scores_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p, ws, part, ngroups);
+            e = cudaGetLastError();
+        }
+    }
+    const cudaError_t ef = cudaFreeAsync(ws, st);
+    if (e != cudaSuccess) return cuda_status(e, "chunk scan launch");
+    return cuda_status(ef, "chunk scan: workspace release");
+}
+
+}  // namespace dbl

@@ -230,6 +230,7 @@ int launch_seq_scan(const SeqParams& p, int in_dtype, cudaStream_t st) {
     if (p.K > 128) return fail(DBL_ERR_UNSUPPORTED, "sequential scan supports key_dim <= 128 (got %d)", p.K);
     if (p.V > 256) return fail(DBL_ERR_UNSUPPORTED, "sequential scan supports value_dim <= 256 (got %d)", p.V);
     if ((int64_t)p.B * p.H > 0x7fffffffLL) return fail(DBL_ERR_UNSUPPORTED, "batch*heads exceeds the grid limit");
+    if (chunk_scan_supported(p)) return launch_chunk_scan(p, in_dtype, st);
     const bool bf = in_dtype == DBL_BF16;
     if (p.K <= 32) return bf ? launch_seq_t<32, __nv_bfloat16>(p, st) : launch_seq_t<32, float>(p, st);
     if (p.K <= 64) return bf ? launch_seq_t<64, __nv_bfloat16>(p, st) : launch_seq_t<64, float>(p, st);

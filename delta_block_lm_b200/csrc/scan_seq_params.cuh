@@ -32,4 +32,8 @@ struct SeqParams {
 // Validates the shape limits of the sequential kernel and launches it on `st`.
 int launch_seq_scan(const SeqParams& p, int in_dtype, cudaStream_t st);
 
+// The chunked form of the same scan (scan_chunk.cu): whether it takes `p`, and its launcher.
+bool chunk_scan_supported(const SeqParams& p);
+int launch_chunk_scan(const SeqParams& p, int in_dtype, cudaStream_t st);
+
 }  // namespace dbl

@@ -93,6 +93,56 @@ def test_training_scan_bf16_inputs(cuda, native_lib):
     assert rel_err(host(r.scores[..., 0]), sco) < TOL_F32
 
 
+@pytest.mark.parametrize("B,T,H,K,V", [(2, 200, 3, 64, 128), (4, 70, 40, 32, 64), (1, 97, 2, 7, 9),
+                                       (3, 64, 2, 20, 36)])
+def test_training_scan_chunked_form(cuda, native_lib, B, T, H, K, V):
+    # sequences of two or more 16-token chunks with key width <= 64 and value width <= 128 take the
+    # chunked form: several column groups with partial score sums (few heads), one group (B*H >= 148),
+    # widths that are not multiples of 4 (4-byte staging) and a ragged last chunk; padding runs,
+    # resets (one on padding) and an initial state
+    f = splitmix_tokens(300 + T + K, B, T, H, K, V)
+    f[1] = f[1] / np.linalg.norm(f[1], axis=-1, keepdims=True)
+    q, k, v = (x.astype(np.float32) for x in f[:3])
+    rng = np.random.default_rng(T + K)
+    valid = rng.random((B, T)) > 0.1
+    valid[0, 40:60] = False
+    reset = rng.random((B, T)) > 0.93
+    reset[0, 45] = True
+    init = (0.1 * rng.standard_normal((B, H, K, V))).astype(np.float32)
+    out, fin, sco = O.scan(q, k, v, *f[3:], valid, reset, init)
+    r = dbl.gdn_training_scan(*(dev_t(x, cuda) for x in (q, k, v, *f[3:], valid, reset, init)), 16)
+    ok, err = ref_close(host(r.output), out)
+    assert ok, ("out", err)
+    ok, err = ref_close(host(r.final_state), fin)
+    assert ok, ("final", err)
+    ok, err = ref_close(host(r.scores[..., 0]), sco)
+    assert ok, ("scores", err)
+    assert np.all(host(r.output)[~valid] == 0.0)
+
+
+def test_gdn2_scan_chunked_bf16_documents(cuda, native_lib):
+    # bf16 in and out through the document-limit entry on the chunked form: documents that start
+    # and end inside chunks, a padding gap and one-token documents
+    B, T, H, K, V = 2, 150, 3, 32, 64
+    f = splitmix_tokens(4242, B, T, H, K, V)
+    f[1] = f[1] / np.linalg.norm(f[1], axis=-1, keepdims=True)
+    f[:3] = [bf16_round(x.astype(np.float32)) for x in f[:3]]
+    bounds = [0, 23, 24, 61, 90, 131, 150]
+    starts = np.zeros((B, T), np.int32)
+    ends = np.zeros((B, T), np.int32)
+    for lo, hi in zip(bounds[:-1], bounds[1:]):
+        starts[:, lo:hi] = lo
+        ends[:, lo:hi] = hi - 1
+    starts[1, 70:80], ends[1, 70:80] = 80, 79  # padding: end < start
+    ref = O.doc_scan(*f, starts, ends)
+    out = dbl.gdn2_scan(*[dev_t(x, cuda, torch.bfloat16 if i < 3 else torch.float32) for i, x in enumerate(f)],
+                        torch.as_tensor(starts, device=cuda), torch.as_tensor(ends, device=cuda))
+    got = host(out)
+    assert out.dtype == torch.bfloat16
+    assert rel_err(got, ref) < TOL_BF16
+    assert np.all(got[1, 70:80] == 0.0)
+
+
 def test_gdn2_scan_doc_limits(cuda, native_lib):
     g = np.load(GOLDEN)
     f = splitmix_tokens(2024, 1, 33, 2, 32, 64)
