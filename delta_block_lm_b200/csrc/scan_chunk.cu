@@ -21,6 +21,7 @@
 #include "scan_seq_params.cuh"
 
 #include <algorithm>
+#include <mutex>
 
 namespace dbl {
 namespace {
@@ -60,7 +61,12 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
+// waits until at most `pending` (0..2) of this thread's most recent cp.async groups are in flight
+__device__ __forceinline__ void cp_async_wait_pending(int pending) {
+    if (pending <= 0) asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    else if (pending == 1) asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+    else asm volatile("cp.async.wait_group 2;\n" ::: "memory");
+}
 
 __device__ __forceinline__ float warp_sum(float x) {
 #pragma unroll
@@ -147,74 +153,84 @@ __global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, floa
     }
     __syncthreads();
 
-    // running products: source s = -1 (the chunk start: P) and s = 0 .. C-1 (A, M, Wd); warp w takes
-    // the sources w - 1, w + 7, ... (lane l: channels l, l + 32)
+    // Running products, one source per warp step: s = -1 gives the chunk-start decays P_t, a token
+    // s >= 0 gives column s of A and M (and Wd[s]).  Lane l holds channels l, l + 32; the 32 sums of a
+    // source (A[t][s] and M[t][s] for t = 0..15) leave the lanes by one reduce-scatter (31 shuffles)
+    // after which lane l holds sum l.
     for (int s = warp - 1; s < CC; s += CTH / 32) {
         float prod[KPL];
 #pragma unroll
         for (int e = 0; e < KPL; ++e) prod[e] = 1.f;
-        if (s >= 0) {
-            // the diagonal of M: d[s][s] = 1
-            float mq = 0.f;
+        float r[2 * CC];
 #pragma unroll
-            for (int e = 0; e < KPL; ++e) {
-                const int i = lane + 32 * e;
-                mq = fmaf(sq[s][i], sk[s][i], mq);
-            }
-            mq = warp_sum(mq);
-            if (lane == 0) {
-                sM[s][s] = mq;
-                sA[s][s] = 0.f;
-            }
-        }
-        for (int t = s + 1; t < CC; ++t) {
+        for (int t = 0; t < CC; ++t) {
             float aa = 0.f, mm = 0.f;
+            if (t > s) {
 #pragma unroll
-            for (int e = 0; e < KPL; ++e) {
-                const int i = lane + 32 * e;
-                prod[e] *= sf[t][i];
-                if (s < 0) {
-                    sP[t][i] = prod[e];
-                } else {
-                    const float dk = prod[e] * sk[s][i];
-                    aa = fmaf(sek[t][i], dk, aa);
-                    mm = fmaf(sq[t][i], dk, mm);
+                for (int e = 0; e < KPL; ++e) {
+                    const int i = lane + 32 * e;
+                    prod[e] *= sf[t][i];
+                    if (s < 0) {
+                        sP[t][i] = prod[e];
+                    } else {
+                        const float dk = prod[e] * sk[s][i];
+                        aa = fmaf(sek[t][i], dk, aa);
+                        mm = fmaf(sq[t][i], dk, mm);
+                    }
                 }
+            } else if (t == s) {
+#pragma unroll
+                for (int e = 0; e < KPL; ++e) mm = fmaf(sq[t][lane + 32 * e], sk[t][lane + 32 * e], mm);
             }
-            if (s >= 0) {
-                aa = warp_sum(aa);
-                mm = warp_sum(mm);
-                if (lane == 0) {
-                    sA[t][s] = aa;
-                    sM[t][s] = mm;
-                    sA[s][t] = 0.f;  // strictly lower triangular
-                    sM[s][t] = 0.f;
-                }
-            }
+            r[t] = aa;
+            r[CC + t] = mm;
         }
         if (s >= 0) {
 #pragma unroll
             for (int e = 0; e < KPL; ++e) sWd[s][lane + 32 * e] = prod[e] * sk[s][lane + 32 * e];
-        }
-    }
-    __syncthreads();
-    // Ti = (I + A)^-1: row t = e_t - sum_{s < t} A[t][s] Ti[s]  (warp 0, lane = column)
-    if (warp == 0) {
-        for (int t = 0; t < CC; ++t) {
-            if (lane < CC) {
-                float x = lane == t ? 1.f : 0.f;
-                for (int s = 0; s < t; ++s) x = fmaf(-sA[t][s], sTi[s][lane], x);
-                sTi[t][lane] = x;
+#pragma unroll
+            for (int o = 16, half = CC; o > 0; o >>= 1, half >>= 1) {
+                const bool up = lane & o;
+#pragma unroll
+                for (int x = 0; x < half; ++x) {
+                    const float send = up ? r[x] : r[x + half];
+                    const float keep = up ? r[x + half] : r[x];
+                    r[x] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                }
             }
-            __syncwarp();
+            if (lane < CC) sA[lane][s] = r[0];
+            else sM[lane - CC][s] = r[0];
         }
     }
     __syncthreads();
-    // B' = Ti B (B[s] = (erase k)_s (.) P_s),  U0 = Ti WV
+    if (warp == 0) {
+        // Ti = (I + A)^-1 by right-looking substitution, lane = column: once row s is final it is
+        // subtracted from every later row, so the dependent chain is 16 steps long
+        float x[CC];
+#pragma unroll
+        for (int t = 0; t < CC; ++t) x[t] = t == lane ? 1.f : 0.f;
+#pragma unroll
+        for (int s = 0; s < CC; ++s) {
+#pragma unroll
+            for (int t = s + 1; t < CC; ++t) x[t] = fmaf(-sA[t][s], x[s], x[t]);
+        }
+        if (lane < CC) {
+#pragma unroll
+            for (int t = 0; t < CC; ++t) sTi[t][lane] = x[t];
+        }
+    } else {
+        // B[t] = (erase k)_t (.) P_t, in place
+        for (int x = tid - 32; x < CC * KMAX; x += CTH - 32) {
+            const int t = x / KMAX, i = x - t * KMAX;
+            sek[t][i] *= sP[t][i];
+        }
+    }
+    __syncthreads();
+    // B' = Ti B,  U0 = Ti WV
     for (int x = tid; x < CC * KMAX; x += CTH) {
         const int t = x / KMAX, i = x - t * KMAX;
         float acc = 0.f;
-        for (int s = 0; s <= t; ++s) acc = fmaf(sTi[t][s], sek[s][i] * sP[s][i], acc);
+        for (int s = 0; s <= t; ++s) acc = fmaf(sTi[t][s], sek[s][i], acc);
         sBp[t][i] = acc;
     }
     for (int x = tid; x < CC * V; x += CTH) {
@@ -228,13 +244,19 @@ __global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, floa
     const ChunkBlock L = chunk_block(K, V);
     const int KP = L.kp;
     float* blk = ws + ((size_t)bh * nch + c) * L.total;
-    for (int x = tid; x < CC * K; x += CTH) {
-        const int t = x / K, i = x - t * K;
-        float qe = (sact[t] & 1) ? sq[t][i] * sP[t][i] : 0.f;
-        if (sact[t] & 1)
-            for (int s = 0; s <= t; ++s) qe = fmaf(-sM[t][s], sBp[s][i], qe);
-        blk[L.qe + t * KP + i] = qe;
-        blk[L.bp + t * KP + i] = sBp[t][i];
+    // rows padded to KP with zeros: the sequential pass reads them four channels at a time
+    for (int x = tid; x < CC * KP; x += CTH) {
+        const int t = x / KP, i = x - t * KP;
+        float qe = 0.f, bpv = 0.f;
+        if (i < K) {
+            bpv = sBp[t][i];
+            if (sact[t] & 1) {
+                qe = sq[t][i] * sP[t][i];
+                for (int s = 0; s <= t; ++s) qe = fmaf(-sM[t][s], sBp[s][i], qe);
+            }
+        }
+        blk[L.qe + x] = qe;
+        blk[L.bp + x] = bpv;
     }
     for (int x = tid; x < CC * V; x += CTH) {
         const int t = x / V, j = x - t * V;
@@ -244,11 +266,14 @@ __global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, floa
         blk[L.o0 + x] = o0;
         blk[L.u0 + x] = sU0[t][j];
     }
-    for (int x = tid; x < K * K; x += CTH) {
-        const int i = x / K, i2 = x - i * K;
-        float g = i == i2 ? sP[CC - 1][i] : 0.f;
-        for (int s = 0; s < CC; ++s) g = fmaf(-sWd[s][i], sBp[s][i2], g);
-        blk[L.g + i * KP + i2] = g;
+    for (int x = tid; x < K * KP; x += CTH) {
+        const int i = x / KP, i2 = x - i * KP;
+        float g = 0.f;
+        if (i2 < K) {
+            g = i == i2 ? sP[CC - 1][i] : 0.f;
+            for (int s = 0; s < CC; ++s) g = fmaf(-sWd[s][i], sBp[s][i2], g);
+        }
+        blk[L.g + x] = g;
     }
     for (int x = tid; x < K * V; x += CTH) {
         const int i = x / V, j = x - i * V;
@@ -266,112 +291,151 @@ __global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, floa
     }
 }
 
-// The sequential pass: one CTA per (b, h, column group of VG <= 64 columns), the group's state
-// columns S [K][VG] in shared memory (double-buffered), the chunk maps double-buffered by cp.async
-// so that chunk c + 1 loads while chunk c computes.  With one group the scores are written here;
-// with several, each group writes its partial sum of edit^2 per token to `part`.
+// The sequential pass: one CTA per (b, h, column group of VG columns), the group's state columns
+// S [K4][VG] in shared memory (double-buffered; K4 = K rounded up to 4, the extra rows zero), the
+// chunk maps in a ring of NB buffers filled by cp.async NB - 1 chunks ahead, so that a chunk's
+// L2 latency hides behind the compute of the chunks before it.  Thread
+// (rr, j) owns column j, tokens rr + m RP and state rows rr + m RP: one pass over the key channels,
+// four at a time, accumulates o, the edit and the new state from the same state loads.  One barrier
+// per chunk; the scores of a chunk are written after the next chunk's barrier.  With one group the
+// scores are final here; with several, each group writes its partial sums of edit^2 to `part`.
+template <int KMAX, int VG>
 __global__ void __launch_bounds__(CTH) chunk_main_kernel(const SeqParams p, const float* ws, float* part,
-                                                         int VG, int ngroups) {
+                                                         int ngroups, int NB) {
+    constexpr int RP = CTH / VG;               // token (and state) rows per pass
+    constexpr int NT = CC / RP;                // tokens per thread
+    constexpr int NS = KMAX / RP;              // state rows per thread
+    constexpr int NP = VG > 32 ? VG / 32 : 1;  // warps sharing one token
+    constexpr int RW = VG < 32 ? VG : 32;      // lanes sharing one token within a warp
     extern __shared__ __align__(16) float smain[];
-    const int K = p.K, V = p.V;
+    const int K = p.K, V = p.V, K4 = (K + 3) & ~3;
     const int nch = (p.T + CC - 1) / CC;
     const int grp = blockIdx.x % ngroups, bh = blockIdx.x / ngroups;
     const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
     const int c0 = grp * VG, vg = min(VG, V - c0);
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, j = tid % VG, rr = tid / VG;
     const ChunkBlock L = chunk_block(K, V);
     const int KP = L.kp;
-    const int rows = 2 * CC + K;                 // O0, U0, H rows
-    const int bfl = L.sh + rows * VG;            // floats per buffered chunk
+    const int rows = 2 * CC + K;  // O0, U0, H rows
+    const int bfl = L.sh + rows * VG;
     float* Sb0 = smain;
-    float* Sb1 = smain + K * VG;
-    float* bb0 = smain + 2 * K * VG;
-    float* bb1 = bb0 + bfl;
-    float* ssq = bb1 + bfl;
+    float* Sb1 = smain + K4 * VG;
+    float* bb0 = smain + 2 * K4 * VG;  // NB buffers of bfl floats
+    float* ssqp = bb0 + NB * bfl;      // [2][CC][NP]
     const bool vec = (V & 3) == 0;
     const size_t sbase = ((size_t)b * p.H + h) * K * V;
-    for (int x = tid; x < K * vg; x += CTH) {
-        const int i = x / vg, j = x - i * vg;
-        Sb0[i * VG + j] = p.init_mode == 1 ? p.initial[sbase + (size_t)i * V + c0 + j] : 0.f;
+    for (int x = tid; x < K4 * VG; x += CTH) {
+        const int i = x / VG, jj = x - i * VG;
+        Sb0[x] = (p.init_mode == 1 && i < K && jj < vg) ? p.initial[sbase + (size_t)i * V + c0 + jj] : 0.f;
+        Sb1[x] = 0.f;
     }
-    if (tid < CC) ssq[tid] = 0.f;
+    // stages chunk c into buffer c % NB and commits one group (an empty one past the last chunk)
     auto prefetch = [&](int c) {
+        if (c >= nch) {
+            cp_async_commit();
+            return;
+        }
         const float* src = ws + ((size_t)bh * nch + c) * L.total;
-        float* dst = (c & 1) ? bb1 : bb0;
+        float* dst = bb0 + (c % NB) * bfl;
         for (int x = tid; x < L.sh / 4; x += CTH) cp_async16(dst + 4 * x, src + 4 * x);
         if (vec) {
             const int q4 = vg >> 2;
             for (int x = tid; x < rows * q4; x += CTH) {
-                const int r = x / q4, u = x - r * q4;
-                cp_async16(dst + L.sh + r * VG + 4 * u, src + L.sh + (size_t)r * V + c0 + 4 * u);
+                const int r = x / q4, w = x - r * q4;
+                cp_async16(dst + L.sh + r * VG + 4 * w, src + L.sh + (size_t)r * V + c0 + 4 * w);
             }
         } else {
             for (int x = tid; x < rows * vg; x += CTH) {
-                const int r = x / vg, u = x - r * vg;
-                cp_async4(dst + L.sh + r * VG + u, src + L.sh + (size_t)r * V + c0 + u);
+                const int r = x / vg, w = x - r * vg;
+                cp_async4(dst + L.sh + r * VG + w, src + L.sh + (size_t)r * V + c0 + w);
             }
         }
+        cp_async_commit();
     };
-    prefetch(0);
-    cp_async_commit();
+    auto write_scores = [&](int c, float kn) {
+        const int t0 = c * CC, n = min(CC, p.T - t0);
+        if (tid < n) {
+            const float* sp = ssqp + (c & 1) * CC * NP + tid * NP;
+            float s = 0.f;
+#pragma unroll
+            for (int w = 0; w < NP; ++w) s += sp[w];
+            const size_t si = ((size_t)b * p.T + t0 + tid) * p.H + h;
+            if (ngroups == 1) p.scores[si] = kn * sqrtf(s);
+            else part[(size_t)grp * p.B * p.T * p.H + si] = s;
+        }
+    };
+    for (int c = 0; c < NB - 1; ++c) prefetch(c);
+    float kn_prev = 0.f;
     for (int c = 0; c < nch; ++c) {
         const int t0 = c * CC, n = min(CC, p.T - t0);
-        if (c + 1 < nch) prefetch(c + 1);
-        cp_async_commit();
-        cp_async_wait1();
-        __syncthreads();  // chunk c's maps and the state are in place
-        const float* blk = (c & 1) ? bb1 : bb0;
+        cp_async_wait_pending(NB - 2);
+        __syncthreads();  // chunk c's maps, the state and the previous chunk's edit sums are in place
+        prefetch(c + NB - 1);  // into the buffer of chunk c - 1, which every thread has finished
+        const float* blk = bb0 + (c % NB) * bfl;
+        if (p.scores && c > 0) write_scores(c - 1, kn_prev);
+        kn_prev = (p.scores && tid < n) ? blk[L.kn + tid] : 0.f;
         const float* S = (c & 1) ? Sb1 : Sb0;
         float* Sn = (c & 1) ? Sb0 : Sb1;
         const float* qe = blk + L.qe;
         const float* bp = blk + L.bp;
+        const float* g = blk + L.g;
         const float* o0 = blk + L.sh;
         const float* u0 = o0 + CC * VG;
         const float* hh = u0 + CC * VG;
-        const float* g = blk + L.g;
-        // o = Qe S + O0 and edit = U0 - B' S for (token, column) pairs
-        for (int x = tid; x < CC * vg; x += CTH) {
-            const int t = x / vg, j = x - t * vg;
-            float o = o0[t * VG + j], u = u0[t * VG + j];
-#pragma unroll 8
-            for (int i = 0; i < K; ++i) {
-                const float sv = S[i * VG + j];
-                o = fmaf(qe[t * KP + i], sv, o);
-                u = fmaf(-bp[t * KP + i], sv, u);
+        float o[NT], u[NT], acc[NS];
+#pragma unroll
+        for (int m = 0; m < NT; ++m) {
+            o[m] = o0[(rr + m * RP) * VG + j];
+            u[m] = u0[(rr + m * RP) * VG + j];
+        }
+#pragma unroll
+        for (int m = 0; m < NS; ++m) acc[m] = (rr + m * RP < K) ? hh[(rr + m * RP) * VG + j] : 0.f;
+#pragma unroll 2
+        for (int i = 0; i < K4; i += 4) {
+            const float s0 = S[(i + 0) * VG + j], s1 = S[(i + 1) * VG + j];
+            const float s2 = S[(i + 2) * VG + j], s3 = S[(i + 3) * VG + j];
+#pragma unroll
+            for (int m = 0; m < NT; ++m) {
+                const float4 qv = *reinterpret_cast<const float4*>(qe + (rr + m * RP) * KP + i);
+                const float4 bv = *reinterpret_cast<const float4*>(bp + (rr + m * RP) * KP + i);
+                o[m] = fmaf(qv.x, s0, fmaf(qv.y, s1, fmaf(qv.z, s2, fmaf(qv.w, s3, o[m]))));
+                u[m] = fmaf(-bv.x, s0, fmaf(-bv.y, s1, fmaf(-bv.z, s2, fmaf(-bv.w, s3, u[m]))));
             }
-            if (t < n) {
-                if (p.out) {
-                    const size_t oi = (size_t)b * p.os[0] + (size_t)(t0 + t) * p.os[1] + (size_t)h * p.os[2] +
-                                      (size_t)(c0 + j) * p.os[3];
-                    if (p.out_dtype == DBL_BF16) static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(o);
-                    else static_cast<float*>(p.out)[oi] = o;
+#pragma unroll
+            for (int m = 0; m < NS; ++m) {
+                if (rr + m * RP < K) {
+                    const float4 gv = *reinterpret_cast<const float4*>(g + (rr + m * RP) * KP + i);
+                    acc[m] = fmaf(gv.x, s0, fmaf(gv.y, s1, fmaf(gv.z, s2, fmaf(gv.w, s3, acc[m]))));
                 }
-                if (p.scores) atomicAdd(&ssq[t], u * u);
             }
         }
-        // S <- G S + H into the other state buffer
-        for (int x = tid; x < K * vg; x += CTH) {
-            const int i = x / vg, j = x - i * vg;
-            float acc = hh[i * VG + j];
-#pragma unroll 8
-            for (int i2 = 0; i2 < K; ++i2) acc = fmaf(g[i * KP + i2], S[i2 * VG + j], acc);
-            Sn[i * VG + j] = acc;
-        }
-        // |k_t| is read before the barrier: the next prefetch into this buffer may start right after it
-        const float kn = (p.scores && tid < n) ? blk[L.kn + tid] : 0.f;
-        __syncthreads();
-        if (p.scores && tid < n) {
-            const size_t si = ((size_t)b * p.T + t0 + tid) * p.H + h;
-            if (ngroups == 1) p.scores[si] = kn * sqrtf(ssq[tid]);
-            else part[(size_t)grp * p.B * p.T * p.H + si] = ssq[tid];
-            ssq[tid] = 0.f;
+#pragma unroll
+        for (int m = 0; m < NS; ++m)
+            if (rr + m * RP < K) Sn[(rr + m * RP) * VG + j] = acc[m];
+#pragma unroll
+        for (int m = 0; m < NT; ++m) {
+            const int t = rr + m * RP;
+            if (t < n && j < vg && p.out) {
+                const size_t oi = (size_t)b * p.os[0] + (size_t)(t0 + t) * p.os[1] + (size_t)h * p.os[2] +
+                                  (size_t)(c0 + j) * p.os[3];
+                if (p.out_dtype == DBL_BF16) static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(o[m]);
+                else static_cast<float*>(p.out)[oi] = o[m];
+            }
+            if (p.scores) {
+                float e2 = j < vg ? u[m] * u[m] : 0.f;
+#pragma unroll
+                for (int w = RW / 2; w > 0; w >>= 1) e2 += __shfl_xor_sync(0xffffffffu, e2, w);
+                if ((j & (RW - 1)) == 0) ssqp[(c & 1) * CC * NP + t * NP + j / 32] = e2;
+            }
         }
     }
+    __syncthreads();
+    if (p.scores) write_scores(nch - 1, kn_prev);
     if (p.final_state) {
         const float* S = (nch & 1) ? Sb1 : Sb0;
         for (int x = tid; x < K * vg; x += CTH) {
-            const int i = x / vg, j = x - i * vg;
-            p.final_state[sbase + (size_t)i * V + c0 + j] = S[i * VG + j];
+            const int i = x / vg, jj = x - i * vg;
+            p.final_state[sbase + (size_t)i * V + c0 + jj] = S[i * VG + jj];
         }
     }
 }
@@ -397,8 +461,61 @@ bool chunk_scan_supported(const SeqParams& p) {
     return p.K <= 64 && p.V <= CVMAX && p.init_mode != 2 && p.T >= 2 * CC;
 }
 
-// Runs the chunked scan; its workspace comes from the stream-ordered allocator and is released on
-// the stream after the last kernel.
+namespace {
+
+// A stream-ordered pool per device for the chunk maps, created on first use; freed blocks stay in the
+// pool (release threshold: never) so that repeated calls reuse them without driver allocations.
+int scratch_pool(cudaMemPool_t* out) {
+    static std::mutex mu;
+    static cudaMemPool_t pools[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 64) return fail(DBL_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!pools[dev]) {
+        cudaMemPoolProps props{};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = dev;
+        cudaMemPool_t pool = nullptr;
+        e = cudaMemPoolCreate(&pool, &props);
+        if (e != cudaSuccess) return cuda_status(e, "chunk scan: cudaMemPoolCreate");
+        uint64_t keep = ~uint64_t(0);
+        e = cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+        if (e != cudaSuccess) return cuda_status(e, "chunk scan: pool release threshold");
+        pools[dev] = pool;
+    }
+    *out = pools[dev];
+    return DBL_OK;
+}
+
+template <int KMAX, int VG>
+int launch_main(const SeqParams& p, const float* ws, float* part, int ngroups, int NB, size_t smem,
+                cudaStream_t st) {
+    static std::atomic<uint64_t> attr_done{0};
+    const int rc = once_per_device(attr_done, [] {
+        return cuda_status(cudaFuncSetAttribute(chunk_main_kernel<KMAX, VG>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024),
+                           "chunk scan: shared memory attribute");
+    });
+    if (rc != DBL_OK) return rc;
+    chunk_main_kernel<KMAX, VG><<<(unsigned)((int64_t)p.B * p.H * ngroups), CTH, smem, st>>>(p, ws, part, ngroups, NB);
+    return launch_status("chunk_main_kernel");
+}
+
+template <int KMAX>
+int launch_main_vg(const SeqParams& p, const float* ws, float* part, int VG, int ngroups, int NB, size_t smem,
+                   cudaStream_t st) {
+    if (VG == 16) return launch_main<KMAX, 16>(p, ws, part, ngroups, NB, smem, st);
+    if (VG == 32) return launch_main<KMAX, 32>(p, ws, part, ngroups, NB, smem, st);
+    return launch_main<KMAX, 64>(p, ws, part, ngroups, NB, smem, st);
+}
+
+}  // namespace
+
+// Runs the chunked scan: chunk maps (and partial score sums) in a workspace from the library's
+// stream-ordered pool, released on the stream after the last kernel.
 int launch_chunk_scan(const SeqParams& p, int in_dtype, cudaStream_t st) {
     const int nch = (p.T + CC - 1) / CC;
     const ChunkBlock L = chunk_block(p.K, p.V);
@@ -412,12 +529,16 @@ int launch_chunk_scan(const SeqParams& p, int in_dtype, cudaStream_t st) {
         }
     }
     const int ngroups = (p.V + VG - 1) / VG;
-    if ((int64_t)bh * nch > 0x7fffffffLL || bh * ngroups > 0x7fffffffLL)
+    if (bh * nch > 0x7fffffffLL || bh * ngroups > 0x7fffffffLL)
         return fail(DBL_ERR_UNSUPPORTED, "chunk scan: grid exceeds 32-bit limits");
     const size_t ws_floats = (size_t)bh * nch * L.total;
     const size_t part_floats = (p.scores && ngroups > 1) ? (size_t)ngroups * bh * p.T : 0;
+    cudaMemPool_t pool = nullptr;
+    int rc = scratch_pool(&pool);
+    if (rc != DBL_OK) return rc;
     float* ws = nullptr;
-    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&ws), (ws_floats + part_floats) * sizeof(float), st);
+    cudaError_t e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&ws), (ws_floats + part_floats) * sizeof(float),
+                                            pool, st);
     if (e != cudaSuccess) return cuda_status(e, "chunk scan: workspace");
     float* part = ws + ws_floats;
     const bool bf = in_dtype == DBL_BF16;
@@ -429,29 +550,25 @@ int launch_chunk_scan(const SeqParams& p, int in_dtype, cudaStream_t st) {
         if (bf) chunk_prep_kernel<64, __nv_bfloat16><<<gprep, CTH, 0, st>>>(p, ws);
         else chunk_prep_kernel<64, float><<<gprep, CTH, 0, st>>>(p, ws);
     }
-    e = cudaGetLastError();
-    if (e == cudaSuccess) {
-        const size_t smem = ((size_t)2 * p.K * VG + 2 * ((size_t)L.sh + (2 * CC + p.K) * VG) + CC) * sizeof(float);
-        static std::atomic<uint64_t> attr_done{0};
-        const int rc = once_per_device(attr_done, [] {
-            return cuda_status(cudaFuncSetAttribute(chunk_main_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                    227 * 1024),
-                               "chunk scan: shared memory attribute");
-        });
-        if (rc != DBL_OK) {
-            cudaFreeAsync(ws, st);
-            return rc;
-        }
-        chunk_main_kernel<<<(unsigned)(bh * ngroups), CTH, smem, st>>>(p, ws, part, VG, ngroups);
-        e = cudaGetLastError();
-        if (e == cudaSuccess && part_floats) {
-            const size_t n = (size_t)bh * p.T;
-            chunk_scores_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p, ws, part, ngroups);
-            e = cudaGetLastError();
-        }
+    rc = launch_status("chunk_prep_kernel");
+    if (rc == DBL_OK) {
+        const int K4 = (p.K + 3) & ~3;
+        const int np = VG > 32 ? VG / 32 : 1;
+        const size_t bfl = (size_t)L.sh + (2 * CC + p.K) * VG;
+        // the deepest ring of 4, 3 or 2 chunk buffers that fits in 227 KB
+        int NB = 4;
+        while (NB > 2 && ((size_t)2 * K4 * VG + NB * bfl + 2 * CC * np) * sizeof(float) > 227 * 1024) --NB;
+        const size_t smem = ((size_t)2 * K4 * VG + NB * bfl + 2 * CC * np) * sizeof(float);
+        rc = p.K <= 32 ? launch_main_vg<32>(p, ws, part, VG, ngroups, NB, smem, st)
+                       : launch_main_vg<64>(p, ws, part, VG, ngroups, NB, smem, st);
+    }
+    if (rc == DBL_OK && part_floats) {
+        const size_t n = (size_t)bh * p.T;
+        chunk_scores_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p, ws, part, ngroups);
+        rc = launch_status("chunk_scores_kernel");
     }
     const cudaError_t ef = cudaFreeAsync(ws, st);
-    if (e != cudaSuccess) return cuda_status(e, "chunk scan launch");
+    if (rc != DBL_OK) return rc;
     return cuda_status(ef, "chunk scan: workspace release");
 }
 
