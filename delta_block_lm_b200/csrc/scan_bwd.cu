@@ -24,6 +24,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "scan_seq_params.cuh"
 
 namespace dbl {
 namespace {
@@ -39,6 +40,7 @@ struct BwdParams {
     float *ck;  // [B*H][nch][K][V] chunk-start states
     float *rp;  // [B*H][C][K][V]   previous state of each token of the chunk being reversed
     int rp_shared;  // 1: those states live in shared memory ([C][K][cols + 8]) instead of rp
+    int ck_ready;   // 1: ck already holds the chunk-start states (pass 1 is skipped)
 };
 
 // One level of a reduce-scatter over the lanes that differ in lane bit `o`: the lower lane keeps
@@ -75,7 +77,7 @@ __device__ __forceinline__ float row_sum(float x) {
 
 // Shared memory of the backward kernel (dynamic; the same carve-up on host and device).
 struct BwdSmem {
-    size_t k, a, e, q, wv, xe, en, kn, red, act, rst, total;
+    size_t k, a, e, q, wv, xe, en, kn, gs, red, act, rst, total;
 };
 __host__ __device__ inline BwdSmem bwd_smem(int kmax, int cols, int nwarps) {
     BwdSmem L{};
@@ -89,6 +91,7 @@ __host__ __device__ inline BwdSmem bwd_smem(int kmax, int cols, int nwarps) {
     L.xe = o; o += tc;
     L.en = o; o += MAXC * 4;
     L.kn = o; o += MAXC * 4;
+    L.gs = o; o += MAXC * 4;
     L.red = o; o += (size_t)2 * nwarps * 4 * kmax * 4;
     L.act = o; o += MAXC * 4;
     L.rst = o; o += MAXC * 4;
@@ -118,6 +121,7 @@ __global__ void __launch_bounds__(512) training_backward_kernel(const BwdParams 
     float* sxe = reinterpret_cast<float*>(dyn_raw + L.xe);  // [MAXC][cols]
     float* sen = reinterpret_cast<float*>(dyn_raw + L.en);  // |edit|^2 per token
     float* skn = reinterpret_cast<float*>(dyn_raw + L.kn);  // |k|^2 per token
+    float* sgs = reinterpret_cast<float*>(dyn_raw + L.gs);  // g_score per token
     float* red = reinterpret_cast<float*>(dyn_raw + L.red); // [2][nwarps][4][KMAX]
     int* sact = reinterpret_cast<int*>(dyn_raw + L.act);
     int* srst = reinterpret_cast<int*>(dyn_raw + L.rst);
@@ -150,6 +154,7 @@ __global__ void __launch_bounds__(512) training_backward_kernel(const BwdParams 
         if (tid < n) {
             sact[tid] = p.valid[(size_t)b * T + t0 + tid] != 0.f;
             srst[tid] = p.reset[(size_t)b * T + t0 + tid] != 0.f;
+            if (with_q) sgs[tid] = p.g_score ? p.g_score[tok(t0 + tid)] : 0.f;
         }
         if (g == 0) {
             // this column's write * v for the chunk: all loads issued, then stored
@@ -187,7 +192,7 @@ __global__ void __launch_bounds__(512) training_backward_kernel(const BwdParams 
     float S[R];
 #pragma unroll
     for (int u = 0; u < R; ++u) S[u] = (row_ok(u) && p.initial) ? p.initial[sbase + (size_t)(g + TPC * u) * V + j] : 0.f;
-    for (int c = 0; c < p.nch; ++c) {
+    for (int c = 0; c < (p.ck_ready ? 0 : p.nch); ++c) {
         const int t0 = c * p.C, n = min(p.C, T - t0);
         float* ckc = p.ck + ((size_t)bh * p.nch + c) * K * V;
 #pragma unroll
@@ -257,7 +262,7 @@ __global__ void __launch_bounds__(512) training_backward_kernel(const BwdParams 
             const bool rst = srst[r];
             const float enorm = sqrtf(sen[r]), knorm = sqrtf(skn[r]);
             const bool norms = knorm > 0.f && enorm > 0.f;
-            const float gs = p.g_score ? p.g_score[tok(t)] : 0.f;
+            const float gs = sgs[r];
             const float key_scale = norms ? gs * enorm / knorm : 0.f;
             const float x_e = col ? sxe[r * cols + j] : 0.f;  // this column's edit
             float part = 0.f;
@@ -387,6 +392,44 @@ extern "C" int dbl_gdn_training_scan_backward(const dbl_training_scan_backward_a
     p.ck = static_cast<float*>(workspace);
     p.rp = p.ck + heads * p.nch * (size_t)p.K * p.V;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    // with 16-token checkpoints the chunked forward (scan_chunk.cu) writes them, several chunks in
+    // parallel, instead of the kernel's own token-sequential first pass
+    {
+        SeqParams sp{};
+        sp.B = p.B;
+        sp.T = p.T;
+        sp.H = p.H;
+        sp.K = p.K;
+        sp.V = p.V;
+        const int64_t dk[4] = {a->batch, a->time, a->heads, a->key_dim};
+        const int64_t dv[4] = {a->batch, a->time, a->heads, a->value_dim};
+        const int64_t z[4] = {0, 0, 0, 0};
+        sp.q = p.q;
+        sp.k = p.k;
+        sp.v = p.v;
+        resolve_strides(z, dk, 4, sp.qs);
+        resolve_strides(z, dk, 4, sp.ks);
+        resolve_strides(z, dv, 4, sp.vs);
+        sp.gate_mode = 0;
+        sp.alpha = p.alpha;
+        sp.erase = p.erase;
+        sp.write = p.write;
+        resolve_strides(z, dk, 4, sp.as);
+        resolve_strides(z, dk, 4, sp.es);
+        resolve_strides(z, dv, 4, sp.ws);
+        sp.scale = 1.f;
+        sp.mask_mode = 1;
+        sp.valid = p.valid;
+        sp.reset = p.reset;
+        sp.init_mode = p.initial ? 1 : 0;
+        sp.initial = p.initial;
+        sp.chunk_states = p.ck;
+        if (p.C == 16 && chunk_scan_supported(sp)) {
+            const int rc = launch_chunk_scan(sp, DBL_F32, st);
+            if (rc != DBL_OK) return rc;
+            p.ck_ready = 1;
+        }
+    }
     // four lanes per value column up to 128 columns, two beyond (at most 512 threads)
     const int tpc = p.V <= 128 ? 4 : 2;
     const int threads = (p.V * tpc + 31) / 32 * 32, nwarps = threads / 32;

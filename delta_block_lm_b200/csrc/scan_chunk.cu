@@ -74,15 +74,40 @@ __device__ __forceinline__ float warp_sum(float x) {
     return x;
 }
 
+__device__ __forceinline__ float4 lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+// acc[r][c] += sum_{s < CC} A[(r0 + r) lda + s] Bm[s ldb + n0 + c] for a 2 x 4 tile: A rows are
+// contiguous in s, Bm rows contiguous in n; every operand is read four at a time (16-byte aligned).
+__device__ __forceinline__ void tile_mm(float (&acc)[2][4], const float* A, int lda, int r0, const float* Bm,
+                                        int ldb, int n0) {
+#pragma unroll
+    for (int s = 0; s < CC; s += 4) {
+        const float4 b0 = lds4(Bm + (s + 0) * ldb + n0), b1 = lds4(Bm + (s + 1) * ldb + n0);
+        const float4 b2 = lds4(Bm + (s + 2) * ldb + n0), b3 = lds4(Bm + (s + 3) * ldb + n0);
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const float4 a = lds4(A + (r0 + r) * lda + s);
+            acc[r][0] = fmaf(a.x, b0.x, fmaf(a.y, b1.x, fmaf(a.z, b2.x, fmaf(a.w, b3.x, acc[r][0]))));
+            acc[r][1] = fmaf(a.x, b0.y, fmaf(a.y, b1.y, fmaf(a.z, b2.y, fmaf(a.w, b3.y, acc[r][1]))));
+            acc[r][2] = fmaf(a.x, b0.z, fmaf(a.y, b1.z, fmaf(a.z, b2.z, fmaf(a.w, b3.z, acc[r][2]))));
+            acc[r][3] = fmaf(a.x, b0.w, fmaf(a.y, b1.w, fmaf(a.z, b2.w, fmaf(a.w, b3.w, acc[r][3]))));
+        }
+    }
+}
+
 template <int KMAX, typename T>
 __global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, float* ws) {
     constexpr int KPL = KMAX / 32;  // key channels per lane in the running products
-    __shared__ float sk[CC][KMAX], sq[CC][KMAX], sek[CC][KMAX], sf[CC][KMAX];
-    __shared__ float sP[CC][KMAX], sWd[CC][KMAX], sBp[CC][KMAX];
-    __shared__ float swv[CC][CVMAX], sU0[CC][CVMAX];
-    __shared__ float sA[CC][CC], sM[CC][CC], sTi[CC][CC];
+    constexpr int WS = CC + 4;      // row stride of Wd^T (16-byte rows on distinct banks)
+    __shared__ __align__(16) float sk[CC][KMAX], sq[CC][KMAX], sek[CC][KMAX], sf[CC][KMAX];
+    __shared__ __align__(16) float sPB[CC][KMAX];  // P_t, then (once P is folded into B and Q) B'
+    __shared__ __align__(16) float sWdT[KMAX][WS];
+    __shared__ __align__(16) float swv[CC][CVMAX], sU0[CC][CVMAX];
+    __shared__ __align__(16) float sA[CC][CC], sM[CC][CC], sTi[CC][CC];
+    __shared__ float sPl[KMAX];
     __shared__ int sact[CC];
     const int K = p.K, V = p.V;
+    const int K4 = (K + 3) & ~3, V4 = (V + 3) & ~3;
     const int nch = (p.T + CC - 1) / CC;
     const int c = blockIdx.x % nch, bh = blockIdx.x / nch, b = bh / p.H, h = bh - (bh / p.H) * p.H;
     const int t0 = c * CC, n = min(CC, p.T - t0);
@@ -111,7 +136,8 @@ __global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, floa
         sact[tid] = act | (rst << 1);
     }
     __syncthreads();
-    // inputs: k, q (scaled), step factors f, erase k (zero for padding), write v (zero for padding)
+    // inputs: k, q (scaled; zero for padding, whose outputs are zero), step factors f, erase k (zero
+    // for padding), write v (zero for padding)
     for (int x = tid; x < CC * KMAX; x += CTH) {
         const int u = x / KMAX, i = x - u * KMAX;
         const int t = t0 + u;
@@ -119,8 +145,8 @@ __global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, floa
         float kv = 0.f, qv = 0.f, f = 1.f, ek = 0.f;
         if (u < n && i < K) {
             kv = to_f32(kb[t * p.ks[1] + i * p.ks[3]]);
-            qv = to_f32(qb[t * p.qs[1] + i * p.qs[3]]) * p.scale;
             if (act) {
+                qv = to_f32(qb[t * p.qs[1] + i * p.qs[3]]) * p.scale;
                 float a, e;
                 if (scalar) {
                     a = p.alpha[(size_t)b * p.as[0] + (size_t)t * p.as[1] + (size_t)h * p.as[2]];
@@ -138,11 +164,11 @@ __global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, floa
         sf[u][i] = f;
         sek[u][i] = ek;
     }
-    for (int x = tid; x < CC * V; x += CTH) {
-        const int u = x / V, j = x - u * V;
+    for (int x = tid; x < CC * CVMAX; x += CTH) {
+        const int u = x / CVMAX, j = x - u * CVMAX;
         const int t = t0 + u;
         float wv = 0.f;
-        if (u < n && (sact[u] & 1)) {
+        if (j < V && u < n && (sact[u] & 1)) {
             const float vv = p.v_zero ? 0.f : to_f32(vb[t * p.vs[1] + j * p.vs[3]]);
             const float w = scalar ? p.erase[(size_t)b * p.es[0] + (size_t)t * p.es[1] + (size_t)h * p.es[2]]
                                    : p.write[(size_t)b * p.ws[0] + (size_t)t * p.ws[1] + (size_t)h * p.ws[2] +
@@ -154,9 +180,9 @@ __global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, floa
     __syncthreads();
 
     // Running products, one source per warp step: s = -1 gives the chunk-start decays P_t, a token
-    // s >= 0 gives column s of A and M (and Wd[s]).  Lane l holds channels l, l + 32; the 32 sums of a
-    // source (A[t][s] and M[t][s] for t = 0..15) leave the lanes by one reduce-scatter (31 shuffles)
-    // after which lane l holds sum l.
+    // s >= 0 gives column s of A and M and row s of Wd.  Lane l holds channels l, l + 32; the 32 sums
+    // of a source (A[t][s] and M[t][s] for t = 0..15) leave the lanes by one reduce-scatter (31
+    // shuffles) after which lane l holds sum l.
     for (int s = warp - 1; s < CC; s += CTH / 32) {
         float prod[KPL];
 #pragma unroll
@@ -171,7 +197,7 @@ __global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, floa
                     const int i = lane + 32 * e;
                     prod[e] *= sf[t][i];
                     if (s < 0) {
-                        sP[t][i] = prod[e];
+                        sPB[t][i] = prod[e];
                     } else {
                         const float dk = prod[e] * sk[s][i];
                         aa = fmaf(sek[t][i], dk, aa);
@@ -187,7 +213,7 @@ __global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, floa
         }
         if (s >= 0) {
 #pragma unroll
-            for (int e = 0; e < KPL; ++e) sWd[s][lane + 32 * e] = prod[e] * sk[s][lane + 32 * e];
+            for (int e = 0; e < KPL; ++e) sWdT[lane + 32 * e][s] = prod[e] * sk[s][lane + 32 * e];
 #pragma unroll
             for (int o = 16, half = CC; o > 0; o >>= 1, half >>= 1) {
                 const bool up = lane & o;
@@ -219,67 +245,99 @@ __global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, floa
             for (int t = 0; t < CC; ++t) sTi[t][lane] = x[t];
         }
     } else {
-        // B[t] = (erase k)_t (.) P_t, in place
+        // fold the decays in: B[t] = (erase k)_t (.) P_t and Q'[t] = q_t (.) P_t, in place
         for (int x = tid - 32; x < CC * KMAX; x += CTH - 32) {
             const int t = x / KMAX, i = x - t * KMAX;
-            sek[t][i] *= sP[t][i];
+            const float pt = sPB[t][i];
+            sek[t][i] *= pt;
+            sq[t][i] *= pt;
+            if (t == CC - 1) sPl[i] = pt;
         }
     }
     __syncthreads();
-    // B' = Ti B,  U0 = Ti WV
-    for (int x = tid; x < CC * KMAX; x += CTH) {
-        const int t = x / KMAX, i = x - t * KMAX;
-        float acc = 0.f;
-        for (int s = 0; s <= t; ++s) acc = fmaf(sTi[t][s], sek[s][i], acc);
-        sBp[t][i] = acc;
-    }
-    for (int x = tid; x < CC * V; x += CTH) {
-        const int t = x / V, j = x - t * V;
-        float acc = 0.f;
-        for (int s = 0; s <= t; ++s) acc = fmaf(sTi[t][s], swv[s][j], acc);
-        sU0[t][j] = acc;
+    // B' = Ti B and U0 = Ti WV (2 x 4 tiles; B' overwrites P, which is no longer read)
+    {
+        const int nb = K4 / 4, nu = V4 / 4;
+        const int tb = (CC / 2) * nb, tu = (CC / 2) * nu;
+        for (int x = tid; x < tb + tu; x += CTH) {
+            float acc[2][4] = {};
+            const bool isb = x < tb;
+            const int y = isb ? x : x - tb, nn = isb ? nb : nu;
+            const int r0 = 2 * (y / nn), n0 = 4 * (y - (y / nn) * nn);
+            if (isb) tile_mm(acc, &sTi[0][0], CC, r0, &sek[0][0], KMAX, n0);
+            else tile_mm(acc, &sTi[0][0], CC, r0, &swv[0][0], CVMAX, n0);
+            float* dst = isb ? &sPB[0][0] : &sU0[0][0];
+            const int ld = isb ? KMAX : CVMAX;
+#pragma unroll
+            for (int r = 0; r < 2; ++r)
+                *reinterpret_cast<float4*>(dst + (r0 + r) * ld + n0) =
+                    make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+        }
     }
     __syncthreads();
-    // the chunk's maps, to the workspace
+    // the chunk's maps, to the workspace: Qe = Q' - M B', O0 = M U0, G = diag(P_last) - Wd^T B',
+    // H = Wd^T U0 (2 x 4 tiles), B' and U0 as computed, zero padding columns K4 .. KP of the rows
+    // of Qe, B' and G, and |k_t|
     const ChunkBlock L = chunk_block(K, V);
     const int KP = L.kp;
     float* blk = ws + ((size_t)bh * nch + c) * L.total;
-    // rows padded to KP with zeros: the sequential pass reads them four channels at a time
-    for (int x = tid; x < CC * KP; x += CTH) {
-        const int t = x / KP, i = x - t * KP;
-        float qe = 0.f, bpv = 0.f;
-        if (i < K) {
-            bpv = sBp[t][i];
-            if (sact[t] & 1) {
-                qe = sq[t][i] * sP[t][i];
-                for (int s = 0; s <= t; ++s) qe = fmaf(-sM[t][s], sBp[s][i], qe);
+    {
+        const int nk = K4 / 4, nv = V4 / 4, rk = (K + 1) / 2;
+        const int tq = (CC / 2) * nk, to = (CC / 2) * nv, tg = rk * nk, th = rk * nv;
+        const int tbp = CC * nk, tu0 = CC * nv, tpad = 2 * CC + K;
+        const int total = tq + to + tg + th + tbp + tu0 + tpad;
+        for (int x = tid; x < total; x += CTH) {
+            int y = x;
+            if (y < tq + to + tg + th) {
+                // a product tile
+                int kind, nn;
+                if (y < tq) { kind = 0; nn = nk; }
+                else if ((y -= tq) < to) { kind = 1; nn = nv; }
+                else if ((y -= to) < tg) { kind = 2; nn = nk; }
+                else { y -= tg; kind = 3; nn = nv; }
+                const int r0 = 2 * (y / nn), n0 = 4 * (y - (y / nn) * nn);
+                float acc[2][4] = {};
+                if (kind == 0) tile_mm(acc, &sM[0][0], CC, r0, &sPB[0][0], KMAX, n0);
+                else if (kind == 1) tile_mm(acc, &sM[0][0], CC, r0, &sU0[0][0], CVMAX, n0);
+                else if (kind == 2) tile_mm(acc, &sWdT[0][0], WS, r0, &sPB[0][0], KMAX, n0);
+                else tile_mm(acc, &sWdT[0][0], WS, r0, &sU0[0][0], CVMAX, n0);
+#pragma unroll
+                for (int r = 0; r < 2; ++r) {
+                    const int row = r0 + r;
+#pragma unroll
+                    for (int cc = 0; cc < 4; ++cc) {
+                        const int col = n0 + cc;
+                        if (kind == 0) {
+                            if (col < K4) blk[L.qe + row * KP + col] = sq[row][col] - acc[r][cc];
+                        } else if (kind == 1) {
+                            if (col < V) blk[L.o0 + row * V + col] = acc[r][cc];
+                        } else if (kind == 2) {
+                            if (row < K && col < K4)
+                                blk[L.g + row * KP + col] = (row == col ? sPl[row] : 0.f) - acc[r][cc];
+                        } else {
+                            if (row < K && col < V) blk[L.hh + row * V + col] = acc[r][cc];
+                        }
+                    }
+                }
+            } else if ((y -= tq + to + tg + th) < tbp + tu0) {
+                // copies of B' and U0
+                if (y < tbp) {
+                    const int t = y / nk, n0 = 4 * (y - t * nk);
+                    *reinterpret_cast<float4*>(blk + L.bp + t * KP + n0) = lds4(&sPB[t][n0]);
+                } else {
+                    y -= tbp;
+                    const int t = y / nv, n0 = 4 * (y - t * nv);
+#pragma unroll
+                    for (int cc = 0; cc < 4; ++cc)
+                        if (n0 + cc < V) blk[L.u0 + t * V + n0 + cc] = sU0[t][n0 + cc];
+                }
+            } else {
+                // zero columns K4 .. KP of a row of Qe, B' or G
+                y -= tbp + tu0;
+                const int off = y < CC ? L.qe + y * KP : y < 2 * CC ? L.bp + (y - CC) * KP : L.g + (y - 2 * CC) * KP;
+                *reinterpret_cast<float4*>(blk + off + K4) = make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }
-        blk[L.qe + x] = qe;
-        blk[L.bp + x] = bpv;
-    }
-    for (int x = tid; x < CC * V; x += CTH) {
-        const int t = x / V, j = x - t * V;
-        float o0 = 0.f;
-        if (sact[t] & 1)
-            for (int s = 0; s <= t; ++s) o0 = fmaf(sM[t][s], sU0[s][j], o0);
-        blk[L.o0 + x] = o0;
-        blk[L.u0 + x] = sU0[t][j];
-    }
-    for (int x = tid; x < K * KP; x += CTH) {
-        const int i = x / KP, i2 = x - i * KP;
-        float g = 0.f;
-        if (i2 < K) {
-            g = i == i2 ? sP[CC - 1][i] : 0.f;
-            for (int s = 0; s < CC; ++s) g = fmaf(-sWd[s][i], sBp[s][i2], g);
-        }
-        blk[L.g + x] = g;
-    }
-    for (int x = tid; x < K * V; x += CTH) {
-        const int i = x / V, j = x - i * V;
-        float hv = 0.f;
-        for (int s = 0; s < CC; ++s) hv = fmaf(sWd[s][i], sU0[s][j], hv);
-        blk[L.hh + x] = hv;
     }
     if (warp == 0) {
         for (int t = 0; t < CC; ++t) {
@@ -291,7 +349,7 @@ __global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, floa
     }
 }
 
-// The sequential pass: one CTA per (b, h, column group of VG columns), the group's state columns
+// The sequential pass: one CTA per (b, h, column group of VG = 16 or 32 columns), the group's state columns
 // S [K4][VG] in shared memory (double-buffered; K4 = K rounded up to 4, the extra rows zero), the
 // chunk maps in a ring of NB buffers filled by cp.async NB - 1 chunks ahead, so that a chunk's
 // L2 latency hides behind the compute of the chunks before it.  Thread
@@ -373,6 +431,15 @@ __global__ void __launch_bounds__(CTH) chunk_main_kernel(const SeqParams p, cons
         prefetch(c + NB - 1);  // into the buffer of chunk c - 1, which every thread has finished
         const float* blk = bb0 + (c % NB) * bfl;
         if (p.scores && c > 0) write_scores(c - 1, kn_prev);
+        if (p.chunk_states) {
+            float* cs = p.chunk_states + ((size_t)bh * nch + c) * K * V + c0 + j;
+            const float* S = (c & 1) ? Sb1 : Sb0;
+            if (j < vg) {
+#pragma unroll
+                for (int m = 0; m < NS; ++m)
+                    if (rr + m * RP < K) cs[(size_t)(rr + m * RP) * V] = S[(rr + m * RP) * VG + j];
+            }
+        }
         kn_prev = (p.scores && tid < n) ? blk[L.kn + tid] : 0.f;
         const float* S = (c & 1) ? Sb1 : Sb0;
         float* Sn = (c & 1) ? Sb0 : Sb1;
@@ -456,9 +523,12 @@ __global__ void chunk_scores_kernel(const SeqParams p, const float* ws, const fl
 }  // namespace
 
 // Whether the chunked path takes these shapes: key width <= 64, value width <= 128, a zero or given
-// initial state (not the identity of span transitions) and at least two chunks.
+// initial state (not the identity of span transitions), at least two chunks, and at most 64
+// sequences x heads.  Beyond that the token-sequential kernel has enough (b, h) rows to fill the GPU
+// and does less work per token (measured at T512/K32/V64: 32 rows 0.31 vs 0.10 ms chunked, 128 rows
+// 0.42 vs 0.53 ms, 512 rows 0.69 vs 1.06 ms).
 bool chunk_scan_supported(const SeqParams& p) {
-    return p.K <= 64 && p.V <= CVMAX && p.init_mode != 2 && p.T >= 2 * CC;
+    return p.K <= 64 && p.V <= CVMAX && p.init_mode != 2 && p.T >= 2 * CC && (int64_t)p.B * p.H <= 64;
 }
 
 namespace {
@@ -508,8 +578,7 @@ template <int KMAX>
 int launch_main_vg(const SeqParams& p, const float* ws, float* part, int VG, int ngroups, int NB, size_t smem,
                    cudaStream_t st) {
     if (VG == 16) return launch_main<KMAX, 16>(p, ws, part, ngroups, NB, smem, st);
-    if (VG == 32) return launch_main<KMAX, 32>(p, ws, part, ngroups, NB, smem, st);
-    return launch_main<KMAX, 64>(p, ws, part, ngroups, NB, smem, st);
+    return launch_main<KMAX, 32>(p, ws, part, ngroups, NB, smem, st);
 }
 
 }  // namespace
@@ -520,14 +589,8 @@ int launch_chunk_scan(const SeqParams& p, int in_dtype, cudaStream_t st) {
     const int nch = (p.T + CC - 1) / CC;
     const ChunkBlock L = chunk_block(p.K, p.V);
     const int64_t bh = (int64_t)p.B * p.H;
-    // column groups: the widest of 64 / 32 / 16 columns that still gives a full wave of CTAs
-    int VG = 16;
-    for (int cand : {64, 32}) {
-        if (bh * ((p.V + cand - 1) / cand) >= 148) {
-            VG = cand;
-            break;
-        }
-    }
+    // column groups of 32 columns when that still gives a full wave of CTAs, else of 16
+    const int VG = bh * ((p.V + 31) / 32) >= 148 ? 32 : 16;
     const int ngroups = (p.V + VG - 1) / VG;
     if (bh * nch > 0x7fffffffLL || bh * ngroups > 0x7fffffffLL)
         return fail(DBL_ERR_UNSUPPORTED, "chunk scan: grid exceeds 32-bit limits");

@@ -27,6 +27,8 @@ struct SeqParams {
     int64_t os[4];
     float* final_state;  // optional, [B,H,K,V]
     float* scores;       // optional, [B,T,H]
+    float* chunk_states; // optional, chunked form only: the state at every 16-token chunk start,
+                         // [B*H][ceil(T/16)][K][V]
 };
 
 // Validates the shape limits of the sequential kernel and launches it on `st`.

@@ -93,13 +93,14 @@ def test_training_scan_bf16_inputs(cuda, native_lib):
     assert rel_err(host(r.scores[..., 0]), sco) < TOL_F32
 
 
-@pytest.mark.parametrize("B,T,H,K,V", [(2, 200, 3, 64, 128), (4, 70, 40, 32, 64), (1, 97, 2, 7, 9),
-                                       (3, 64, 2, 20, 36)])
+@pytest.mark.parametrize("B,T,H,K,V", [(2, 200, 3, 64, 128), (4, 70, 16, 32, 128), (1, 97, 2, 7, 9),
+                                       (3, 64, 2, 20, 36), (8, 48, 16, 32, 64)])
 def test_training_scan_chunked_form(cuda, native_lib, B, T, H, K, V):
-    # sequences of two or more 16-token chunks with key width <= 64 and value width <= 128 take the
-    # chunked form: several column groups with partial score sums (few heads), one group (B*H >= 148),
-    # widths that are not multiples of 4 (4-byte staging) and a ragged last chunk; padding runs,
-    # resets (one on padding) and an initial state
+    # sequences of two or more 16-token chunks with key width <= 64, value width <= 128 and at most 64
+    # sequences x heads take the chunked form: 16-column groups with partial score sums, 32-column
+    # groups (64 rows of 128 columns), one group (V <= 16), widths that are not multiples of 4 (4-byte
+    # staging) and a ragged last chunk; padding runs, resets (one on padding) and an initial state.
+    # 128 rows take the token-sequential kernel
     f = splitmix_tokens(300 + T + K, B, T, H, K, V)
     f[1] = f[1] / np.linalg.norm(f[1], axis=-1, keepdims=True)
     q, k, v = (x.astype(np.float32) for x in f[:3])
