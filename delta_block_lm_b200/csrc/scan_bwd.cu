@@ -40,7 +40,6 @@ struct BwdParams {
     float *ck;  // [B*H][nch][K][V] chunk-start states
     float *rp;  // [B*H][C][K][V]   previous state of each token of the chunk being reversed
     int rp_shared;  // 1: those states live in shared memory ([C][K][cols + 8]) instead of rp
-    int ck_ready;   // 1: ck already holds the chunk-start states (pass 1 is skipped)
 };
 
 // One level of a reduce-scatter over the lanes that differ in lane bit `o`: the lower lane keeps
@@ -192,7 +191,7 @@ __global__ void __launch_bounds__(512) training_backward_kernel(const BwdParams 
     float S[R];
 #pragma unroll
     for (int u = 0; u < R; ++u) S[u] = (row_ok(u) && p.initial) ? p.initial[sbase + (size_t)(g + TPC * u) * V + j] : 0.f;
-    for (int c = 0; c < (p.ck_ready ? 0 : p.nch); ++c) {
+    for (int c = 0; c < p.nch; ++c) {
         const int t0 = c * p.C, n = min(p.C, T - t0);
         float* ckc = p.ck + ((size_t)bh * p.nch + c) * K * V;
 #pragma unroll
@@ -325,10 +324,26 @@ int nchunks_of(int64_t T, int C) { return (int)((T + C - 1) / C); }
 
 }  // namespace
 
+// Whether the backward of these shapes runs in the chunked form (scan_chunk_bwd.cu): 16-token
+// checkpoints and the shapes the chunked forward takes.
+bool chunked_backward(int64_t B, int64_t T, int64_t H, int64_t K, int64_t V, int chunk) {
+    if (chunk != 16 || B > 0x7fffffff || T > 0x7fffffff || H > 0x7fffffff || K > 64 || V > 256) return false;
+    const SeqParams sp = chunk_backward_forward_params((int)B, (int)T, (int)H, (int)K, (int)V, nullptr, nullptr,
+                                                       nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr);
+    return chunk_scan_supported(sp);
+}
+
 size_t training_backward_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t K, int64_t V, int chunk) {
     if (B <= 0 || T <= 0 || H <= 0 || K <= 0 || V <= 0 || chunk < 1 || chunk > MAXC) return 0;
     const size_t heads = (size_t)B * H, kv = (size_t)K * V;
-    return (heads * nchunks_of(T, chunk) * kv + heads * chunk * kv) * sizeof(float);
+    size_t bytes = (heads * nchunks_of(T, chunk) * kv + heads * chunk * kv) * sizeof(float);
+    if (chunked_backward(B, T, H, K, V, chunk)) {
+        const SeqParams sp = chunk_backward_forward_params((int)B, (int)T, (int)H, (int)K, (int)V, nullptr, nullptr,
+                                                           nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                                                           nullptr);
+        bytes = std::max(bytes, chunk_backward_workspace_floats(sp) * sizeof(float));
+    }
+    return bytes;
 }
 
 }  // namespace dbl
@@ -392,43 +407,14 @@ extern "C" int dbl_gdn_training_scan_backward(const dbl_training_scan_backward_a
     p.ck = static_cast<float*>(workspace);
     p.rp = p.ck + heads * p.nch * (size_t)p.K * p.V;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    // with 16-token checkpoints the chunked forward (scan_chunk.cu) writes them, several chunks in
-    // parallel, instead of the kernel's own token-sequential first pass
-    {
-        SeqParams sp{};
-        sp.B = p.B;
-        sp.T = p.T;
-        sp.H = p.H;
-        sp.K = p.K;
-        sp.V = p.V;
-        const int64_t dk[4] = {a->batch, a->time, a->heads, a->key_dim};
-        const int64_t dv[4] = {a->batch, a->time, a->heads, a->value_dim};
-        const int64_t z[4] = {0, 0, 0, 0};
-        sp.q = p.q;
-        sp.k = p.k;
-        sp.v = p.v;
-        resolve_strides(z, dk, 4, sp.qs);
-        resolve_strides(z, dk, 4, sp.ks);
-        resolve_strides(z, dv, 4, sp.vs);
-        sp.gate_mode = 0;
-        sp.alpha = p.alpha;
-        sp.erase = p.erase;
-        sp.write = p.write;
-        resolve_strides(z, dk, 4, sp.as);
-        resolve_strides(z, dk, 4, sp.es);
-        resolve_strides(z, dv, 4, sp.ws);
-        sp.scale = 1.f;
-        sp.mask_mode = 1;
-        sp.valid = p.valid;
-        sp.reset = p.reset;
-        sp.init_mode = p.initial ? 1 : 0;
-        sp.initial = p.initial;
-        sp.chunk_states = p.ck;
-        if (p.C == 16 && chunk_scan_supported(sp)) {
-            const int rc = launch_chunk_scan(sp, DBL_F32, st);
-            if (rc != DBL_OK) return rc;
-            p.ck_ready = 1;
-        }
+    // 16-token checkpoints at the shapes of the chunked forward: the chunked backward
+    // (scan_chunk_bwd.cu), given a 16-byte aligned workspace
+    if (chunked_backward(a->batch, a->time, a->heads, a->key_dim, a->value_dim, a->chunk_size) &&
+        (reinterpret_cast<uintptr_t>(workspace) & 15) == 0) {
+        const SeqParams sp = chunk_backward_forward_params(p.B, p.T, p.H, p.K, p.V, p.q, p.k, p.v, p.alpha, p.erase,
+                                                           p.write, p.valid, p.reset, p.initial);
+        return launch_chunk_backward(sp, p.g_out, p.g_fin, p.g_score, p.dq, p.dk, p.dv, p.dalpha, p.derase, p.dwrite,
+                                     p.dinitial, static_cast<float*>(workspace), st);
     }
     // four lanes per value column up to 128 columns, two beyond (at most 512 threads)
     const int tpc = p.V <= 128 ? 4 : 2;

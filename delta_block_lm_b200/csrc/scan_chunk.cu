@@ -18,6 +18,7 @@
 // chunk_main_kernel: one CTA per (b, h, column group) walks the chunks with its state columns in
 //   shared memory (the columns of S evolve independently): o = Qe S + O0, edit = U0 - B' S (for
 //   the scores |k| |edit|), S <- G S + H.
+#include "scan_chunk.cuh"
 #include "scan_seq_params.cuh"
 
 #include <algorithm>
@@ -26,77 +27,10 @@
 namespace dbl {
 namespace {
 
-constexpr int CC = 16;      // tokens per chunk
-constexpr int CVMAX = 128;  // value width limit of the chunked path
-constexpr int CTH = 256;
-
-// Per-chunk block of the workspace, in floats.  The part every column group reads (Qe, B', G with
-// rows padded to KP = K rounded up to 4, plus 4, so that two rows read by one warp fall in different
-// banks; |k_t|) comes first, then the column-sliced part (O0, U0, H as rows of V).
-struct ChunkBlock {
-    int kp, qe, bp, g, kn, sh, o0, u0, hh, total;
-};
-__host__ __device__ inline ChunkBlock chunk_block(int K, int V) {
-    ChunkBlock L{};
-    L.kp = ((K + 3) & ~3) + 4;
-    int o = 0;
-    L.qe = o; o += CC * L.kp;
-    L.bp = o; o += CC * L.kp;
-    L.g = o; o += K * L.kp;
-    L.kn = o; o += CC;
-    L.sh = o;
-    L.o0 = o; o += CC * V;
-    L.u0 = o; o += CC * V;
-    L.hh = o; o += K * V;
-    L.total = (o + 3) & ~3;  // 16-byte aligned blocks
-    return L;
-}
-
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    const unsigned s = (unsigned)__cvta_generic_to_shared(dst);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
-    const unsigned s = (unsigned)__cvta_generic_to_shared(dst);
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-// waits until at most `pending` (0..2) of this thread's most recent cp.async groups are in flight
-__device__ __forceinline__ void cp_async_wait_pending(int pending) {
-    if (pending <= 0) asm volatile("cp.async.wait_group 0;\n" ::: "memory");
-    else if (pending == 1) asm volatile("cp.async.wait_group 1;\n" ::: "memory");
-    else asm volatile("cp.async.wait_group 2;\n" ::: "memory");
-}
-
-__device__ __forceinline__ float warp_sum(float x) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-    return x;
-}
-
-__device__ __forceinline__ float4 lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
-
-// acc[r][c] += sum_{s < CC} A[(r0 + r) lda + s] Bm[s ldb + n0 + c] for a 2 x 4 tile: A rows are
-// contiguous in s, Bm rows contiguous in n; every operand is read four at a time (16-byte aligned).
-__device__ __forceinline__ void tile_mm(float (&acc)[2][4], const float* A, int lda, int r0, const float* Bm,
-                                        int ldb, int n0) {
-#pragma unroll
-    for (int s = 0; s < CC; s += 4) {
-        const float4 b0 = lds4(Bm + (s + 0) * ldb + n0), b1 = lds4(Bm + (s + 1) * ldb + n0);
-        const float4 b2 = lds4(Bm + (s + 2) * ldb + n0), b3 = lds4(Bm + (s + 3) * ldb + n0);
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const float4 a = lds4(A + (r0 + r) * lda + s);
-            acc[r][0] = fmaf(a.x, b0.x, fmaf(a.y, b1.x, fmaf(a.z, b2.x, fmaf(a.w, b3.x, acc[r][0]))));
-            acc[r][1] = fmaf(a.x, b0.y, fmaf(a.y, b1.y, fmaf(a.z, b2.y, fmaf(a.w, b3.y, acc[r][1]))));
-            acc[r][2] = fmaf(a.x, b0.z, fmaf(a.y, b1.z, fmaf(a.z, b2.z, fmaf(a.w, b3.z, acc[r][2]))));
-            acc[r][3] = fmaf(a.x, b0.w, fmaf(a.y, b1.w, fmaf(a.z, b2.w, fmaf(a.w, b3.w, acc[r][3]))));
-        }
-    }
-}
+using namespace chunk;
 
 template <int KMAX, typename T>
-__global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, float* ws) {
+__global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, float* ws, int extra) {
     constexpr int KPL = KMAX / 32;  // key channels per lane in the running products
     constexpr int WS = CC + 4;      // row stride of Wd^T (16-byte rows on distinct banks)
     __shared__ __align__(16) float sk[CC][KMAX], sq[CC][KMAX], sek[CC][KMAX], sf[CC][KMAX];
@@ -254,6 +188,18 @@ __global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, floa
             if (t == CC - 1) sPl[i] = pt;
         }
     }
+    const ChunkBlock L = chunk_block(K, V, extra != 0);
+    const int KP = L.kp;
+    float* blk = ws + ((size_t)bh * nch + c) * L.total;
+    if (extra) {
+        // P, Wd (rows of KP, zero beyond K) and M for the backward; Q' and Ti follow below
+        for (int x = tid; x < CC * KP; x += CTH) {
+            const int t = x / KP, i = x - t * KP;
+            blk[L.pp + x] = i < K ? sPB[t][i] : 0.f;
+            blk[L.wd + x] = i < K ? sWdT[i][t] : 0.f;
+        }
+        for (int x = tid; x < CC * CC; x += CTH) blk[L.mm + x] = sM[x / CC][x % CC];
+    }
     __syncthreads();
     // B' = Ti B and U0 = Ti WV (2 x 4 tiles; B' overwrites P, which is no longer read)
     {
@@ -278,9 +224,13 @@ __global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, floa
     // the chunk's maps, to the workspace: Qe = Q' - M B', O0 = M U0, G = diag(P_last) - Wd^T B',
     // H = Wd^T U0 (2 x 4 tiles), B' and U0 as computed, zero padding columns K4 .. KP of the rows
     // of Qe, B' and G, and |k_t|
-    const ChunkBlock L = chunk_block(K, V);
-    const int KP = L.kp;
-    float* blk = ws + ((size_t)bh * nch + c) * L.total;
+    if (extra) {
+        for (int x = tid; x < CC * KP; x += CTH) {
+            const int t = x / KP, i = x - t * KP;
+            blk[L.qp + x] = i < K ? sq[t][i] : 0.f;
+        }
+        for (int x = tid; x < CC * CC; x += CTH) blk[L.ti + x] = sTi[x / CC][x % CC];
+    }
     {
         const int nk = K4 / 4, nv = V4 / 4, rk = (K + 1) / 2;
         const int tq = (CC / 2) * nk, to = (CC / 2) * nv, tg = rk * nk, th = rk * nv;
@@ -359,7 +309,7 @@ __global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, floa
 // scores are final here; with several, each group writes its partial sums of edit^2 to `part`.
 template <int KMAX, int VG>
 __global__ void __launch_bounds__(CTH) chunk_main_kernel(const SeqParams p, const float* ws, float* part,
-                                                         int ngroups, int NB) {
+                                                         int ngroups, int NB, int extra) {
     constexpr int RP = CTH / VG;               // token (and state) rows per pass
     constexpr int NT = CC / RP;                // tokens per thread
     constexpr int NS = KMAX / RP;              // state rows per thread
@@ -372,7 +322,7 @@ __global__ void __launch_bounds__(CTH) chunk_main_kernel(const SeqParams p, cons
     const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
     const int c0 = grp * VG, vg = min(VG, V - c0);
     const int tid = threadIdx.x, j = tid % VG, rr = tid / VG;
-    const ChunkBlock L = chunk_block(K, V);
+    const ChunkBlock L = chunk_block(K, V, extra != 0);
     const int KP = L.kp;
     const int rows = 2 * CC + K;  // O0, U0, H rows
     const int bfl = L.sh + rows * VG;
@@ -482,6 +432,8 @@ __global__ void __launch_bounds__(CTH) chunk_main_kernel(const SeqParams p, cons
 #pragma unroll
         for (int m = 0; m < NT; ++m) {
             const int t = rr + m * RP;
+            if (t < n && j < vg && p.edits)
+                p.edits[(((size_t)b * p.T + t0 + t) * p.H + h) * V + c0 + j] = u[m];
             if (t < n && j < vg && p.out) {
                 const size_t oi = (size_t)b * p.os[0] + (size_t)(t0 + t) * p.os[1] + (size_t)h * p.os[2] +
                                   (size_t)(c0 + j) * p.os[3];
@@ -508,13 +460,13 @@ __global__ void __launch_bounds__(CTH) chunk_main_kernel(const SeqParams p, cons
 }
 
 // scores = |k_t| sqrt(sum over column groups of the partial edit^2 sums)
-__global__ void chunk_scores_kernel(const SeqParams p, const float* ws, const float* part, int ngroups) {
+__global__ void chunk_scores_kernel(const SeqParams p, const float* ws, const float* part, int ngroups, int extra) {
     const size_t n = (size_t)p.B * p.T * p.H;
     const size_t si = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (si >= n) return;
     const int h = (int)(si % p.H), t = (int)((si / p.H) % p.T), b = (int)(si / ((size_t)p.H * p.T));
     const int nch = (p.T + CC - 1) / CC;
-    const ChunkBlock L = chunk_block(p.K, p.V);
+    const ChunkBlock L = chunk_block(p.K, p.V, extra != 0);
     const float kn = ws[(((size_t)b * p.H + h) * nch + t / CC) * L.total + L.kn + t % CC];
     float s = 0.f;
     for (int g = 0; g < ngroups; ++g) s += part[(size_t)g * n + si];
@@ -561,7 +513,7 @@ int scratch_pool(cudaMemPool_t* out) {
 }
 
 template <int KMAX, int VG>
-int launch_main(const SeqParams& p, const float* ws, float* part, int ngroups, int NB, size_t smem,
+int launch_main(const SeqParams& p, const float* ws, float* part, int ngroups, int NB, int extra, size_t smem,
                 cudaStream_t st) {
     static std::atomic<uint64_t> attr_done{0};
     const int rc = once_per_device(attr_done, [] {
@@ -570,24 +522,36 @@ int launch_main(const SeqParams& p, const float* ws, float* part, int ngroups, i
                            "chunk scan: shared memory attribute");
     });
     if (rc != DBL_OK) return rc;
-    chunk_main_kernel<KMAX, VG><<<(unsigned)((int64_t)p.B * p.H * ngroups), CTH, smem, st>>>(p, ws, part, ngroups, NB);
+    chunk_main_kernel<KMAX, VG><<<(unsigned)((int64_t)p.B * p.H * ngroups), CTH, smem, st>>>(p, ws, part, ngroups, NB, extra);
     return launch_status("chunk_main_kernel");
 }
 
 template <int KMAX>
-int launch_main_vg(const SeqParams& p, const float* ws, float* part, int VG, int ngroups, int NB, size_t smem,
-                   cudaStream_t st) {
-    if (VG == 16) return launch_main<KMAX, 16>(p, ws, part, ngroups, NB, smem, st);
-    return launch_main<KMAX, 32>(p, ws, part, ngroups, NB, smem, st);
+int launch_main_vg(const SeqParams& p, const float* ws, float* part, int VG, int ngroups, int NB, int extra,
+                   size_t smem, cudaStream_t st) {
+    if (VG == 16) return launch_main<KMAX, 16>(p, ws, part, ngroups, NB, extra, smem, st);
+    return launch_main<KMAX, 32>(p, ws, part, ngroups, NB, extra, smem, st);
 }
 
 }  // namespace
 
-// Runs the chunked scan: chunk maps (and partial score sums) in a workspace from the library's
-// stream-ordered pool, released on the stream after the last kernel.
-int launch_chunk_scan(const SeqParams& p, int in_dtype, cudaStream_t st) {
+// Floats of the chunk maps (and partial score sums) a chunked scan of `p` uses; with `extra` the
+// maps the backward keeps as well.
+size_t chunk_scan_workspace_floats(const SeqParams& p, bool extra) {
     const int nch = (p.T + CC - 1) / CC;
-    const ChunkBlock L = chunk_block(p.K, p.V);
+    const int64_t bh = (int64_t)p.B * p.H;
+    const int VG = bh * ((p.V + 31) / 32) >= 148 ? 32 : 16;
+    const int ngroups = (p.V + VG - 1) / VG;
+    const size_t part = (p.scores && ngroups > 1) ? (size_t)ngroups * bh * p.T : 0;
+    return (size_t)bh * nch * chunk_block(p.K, p.V, extra).total + part;
+}
+
+// Runs the chunked scan: chunk maps (and partial score sums) in `ext_ws` when given (it must hold
+// chunk_scan_workspace_floats(p, extra) floats and outlive the launches), else in a workspace from
+// the library's stream-ordered pool, released on the stream after the last kernel.
+int launch_chunk_scan(const SeqParams& p, int in_dtype, cudaStream_t st, float* ext_ws, bool extra) {
+    const int nch = (p.T + CC - 1) / CC;
+    const ChunkBlock L = chunk_block(p.K, p.V, extra);
     const int64_t bh = (int64_t)p.B * p.H;
     // column groups of 32 columns when that still gives a full wave of CTAs, else of 16
     const int VG = bh * ((p.V + 31) / 32) >= 148 ? 32 : 16;
@@ -596,22 +560,26 @@ int launch_chunk_scan(const SeqParams& p, int in_dtype, cudaStream_t st) {
         return fail(DBL_ERR_UNSUPPORTED, "chunk scan: grid exceeds 32-bit limits");
     const size_t ws_floats = (size_t)bh * nch * L.total;
     const size_t part_floats = (p.scores && ngroups > 1) ? (size_t)ngroups * bh * p.T : 0;
-    cudaMemPool_t pool = nullptr;
-    int rc = scratch_pool(&pool);
-    if (rc != DBL_OK) return rc;
-    float* ws = nullptr;
-    cudaError_t e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&ws), (ws_floats + part_floats) * sizeof(float),
-                                            pool, st);
-    if (e != cudaSuccess) return cuda_status(e, "chunk scan: workspace");
+    float* ws = ext_ws;
+    int rc = DBL_OK;
+    if (!ws) {
+        cudaMemPool_t pool = nullptr;
+        rc = scratch_pool(&pool);
+        if (rc != DBL_OK) return rc;
+        const cudaError_t e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&ws),
+                                                      (ws_floats + part_floats) * sizeof(float), pool, st);
+        if (e != cudaSuccess) return cuda_status(e, "chunk scan: workspace");
+    }
     float* part = ws + ws_floats;
     const bool bf = in_dtype == DBL_BF16;
     const unsigned gprep = (unsigned)(bh * nch);
+    const int ex = extra ? 1 : 0;
     if (p.K <= 32) {
-        if (bf) chunk_prep_kernel<32, __nv_bfloat16><<<gprep, CTH, 0, st>>>(p, ws);
-        else chunk_prep_kernel<32, float><<<gprep, CTH, 0, st>>>(p, ws);
+        if (bf) chunk_prep_kernel<32, __nv_bfloat16><<<gprep, CTH, 0, st>>>(p, ws, ex);
+        else chunk_prep_kernel<32, float><<<gprep, CTH, 0, st>>>(p, ws, ex);
     } else {
-        if (bf) chunk_prep_kernel<64, __nv_bfloat16><<<gprep, CTH, 0, st>>>(p, ws);
-        else chunk_prep_kernel<64, float><<<gprep, CTH, 0, st>>>(p, ws);
+        if (bf) chunk_prep_kernel<64, __nv_bfloat16><<<gprep, CTH, 0, st>>>(p, ws, ex);
+        else chunk_prep_kernel<64, float><<<gprep, CTH, 0, st>>>(p, ws, ex);
     }
     rc = launch_status("chunk_prep_kernel");
     if (rc == DBL_OK) {
@@ -622,17 +590,19 @@ int launch_chunk_scan(const SeqParams& p, int in_dtype, cudaStream_t st) {
         int NB = 4;
         while (NB > 2 && ((size_t)2 * K4 * VG + NB * bfl + 2 * CC * np) * sizeof(float) > 227 * 1024) --NB;
         const size_t smem = ((size_t)2 * K4 * VG + NB * bfl + 2 * CC * np) * sizeof(float);
-        rc = p.K <= 32 ? launch_main_vg<32>(p, ws, part, VG, ngroups, NB, smem, st)
-                       : launch_main_vg<64>(p, ws, part, VG, ngroups, NB, smem, st);
+        rc = p.K <= 32 ? launch_main_vg<32>(p, ws, part, VG, ngroups, NB, ex, smem, st)
+                       : launch_main_vg<64>(p, ws, part, VG, ngroups, NB, ex, smem, st);
     }
     if (rc == DBL_OK && part_floats) {
         const size_t n = (size_t)bh * p.T;
-        chunk_scores_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p, ws, part, ngroups);
+        chunk_scores_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p, ws, part, ngroups, ex);
         rc = launch_status("chunk_scores_kernel");
     }
-    const cudaError_t ef = cudaFreeAsync(ws, st);
-    if (rc != DBL_OK) return rc;
-    return cuda_status(ef, "chunk scan: workspace release");
+    if (!ext_ws) {
+        const cudaError_t ef = cudaFreeAsync(ws, st);
+        if (rc == DBL_OK) rc = cuda_status(ef, "chunk scan: workspace release");
+    }
+    return rc;
 }
 
 }  // namespace dbl

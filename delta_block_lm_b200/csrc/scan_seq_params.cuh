@@ -29,13 +29,28 @@ struct SeqParams {
     float* scores;       // optional, [B,T,H]
     float* chunk_states; // optional, chunked form only: the state at every 16-token chunk start,
                          // [B*H][ceil(T/16)][K][V]
+    float* edits;        // optional, chunked form only: every token's edit, [B,T,H,V] f32
 };
 
 // Validates the shape limits of the sequential kernel and launches it on `st`.
 int launch_seq_scan(const SeqParams& p, int in_dtype, cudaStream_t st);
 
-// The chunked form of the same scan (scan_chunk.cu): whether it takes `p`, and its launcher.
+// The chunked form of the same scan (scan_chunk.cu): whether it takes `p`, its workspace and its
+// launcher (maps in `ext_ws` when given, else in the library's pool; `extra` keeps the maps the
+// chunked backward reads).
 bool chunk_scan_supported(const SeqParams& p);
-int launch_chunk_scan(const SeqParams& p, int in_dtype, cudaStream_t st);
+size_t chunk_scan_workspace_floats(const SeqParams& p, bool extra);
+int launch_chunk_scan(const SeqParams& p, int in_dtype, cudaStream_t st, float* ext_ws = nullptr, bool extra = false);
+
+// The chunked backward of the training scan for 16-token checkpoints (scan_chunk_bwd.cu): the
+// forward parameters it runs (f32 [B,T,H,W] inputs, valid/reset masks, no outputs), its workspace
+// and its launcher (`ws` 16-byte aligned).
+SeqParams chunk_backward_forward_params(int B, int T, int H, int K, int V, const float* q, const float* k,
+                                        const float* v, const float* alpha, const float* erase, const float* write,
+                                        const float* valid, const float* reset, const float* initial);
+size_t chunk_backward_workspace_floats(const SeqParams& sp);
+int launch_chunk_backward(const SeqParams& sp, const float* g_out, const float* g_fin, const float* g_score,
+                          float* dq, float* dk, float* dv, float* dalpha, float* derase, float* dwrite,
+                          float* dinitial, float* ws, cudaStream_t st);
 
 }  // namespace dbl

@@ -107,8 +107,14 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
 
 def test_training_backward_workspace_and_checks(native_lib):
     f = native_lib.dbl_gdn_training_scan_backward_workspace_bytes
-    # checkpoints (B*H*ceil(T/C)) plus one chunk of replayed states (B*H*C), K*V floats each
-    assert f(2, 40, 3, 32, 64, 16) == (2 * 3 * 3 + 2 * 3 * 16) * 32 * 64 * 4
+    # token-sequential backward: checkpoints (B*H*ceil(T/C)) plus one chunk of replayed states
+    # (B*H*C), K*V floats each
+    assert f(2, 40, 3, 32, 64, 8) == (2 * 3 * 5 + 2 * 3 * 8) * 32 * 64 * 4
+    assert f(2, 40, 3, 32, 200, 16) == (2 * 3 * 3 + 2 * 3 * 16) * 32 * 200 * 4
+    # chunked backward (16-token checkpoints, K <= 64, V <= 128, B*H <= 64): at least the chunk-start
+    # states, every token's edit and its gradient, and each chunk end's state gradient
+    assert f(2, 40, 3, 32, 64, 16) >= (2 * 3 * 3 * 32 * 64 * 2 + 2 * 40 * 3 * 64 * 2) * 4
+    assert f(2, 40, 3, 32, 17, 16) % 16 == 0
     assert f(2, 40, 3, 32, 64, 17) == 0 and f(0, 40, 3, 32, 64, 16) == 0
     a = N.TrainingScanBackwardArgs(1, 8, 1, 32, 64, 0)
     assert native_lib.dbl_gdn_training_scan_backward(ctypes.byref(a), None, 0, None) == N.DBL_ERR_INVALID_ARGUMENT

@@ -390,6 +390,41 @@ def test_training_backward_matches_oracle(cuda, native_lib, K, V, chunk):
         assert np.all(getattr(got, name).cpu().numpy()[~valid] == 0.0), name
 
 
+@pytest.mark.parametrize("B,T,H,K,V,opt", [(2, 70, 3, 32, 64, True), (1, 50, 2, 64, 128, True),
+                                           (2, 37, 2, 7, 9, True), (3, 64, 2, 20, 36, False),
+                                           (4, 96, 16, 32, 64, True)])
+def test_training_backward_chunked_form(cuda, native_lib, B, T, H, K, V, opt):
+    # 16-token checkpoints with key width <= 64, value width <= 128 and at most 64 sequence-heads take
+    # the chunked backward: ragged last chunks, widths that are not multiples of 4, padding runs,
+    # resets (one on padding), a zero gate in one channel, and with / without an initial state and
+    # the final-state and score gradients, against the f64 oracle
+    rng = np.random.default_rng(K * 7 + T)
+    q, k = rng.standard_normal((B, T, H, K)) / np.sqrt(K), rng.standard_normal((B, T, H, K)) / np.sqrt(K)
+    v, w = rng.standard_normal((B, T, H, V)), rng.random((B, T, H, V))
+    a, e = rng.uniform(0.6, 1.0, (B, T, H, K)), rng.random((B, T, H, K))
+    a[0, 5, 0, 1] = 0.0
+    valid = rng.random((B, T)) > 0.1
+    valid[0, 20:34] = False
+    reset = rng.random((B, T)) > 0.93
+    reset[0, 25] = True
+    init = 0.1 * rng.standard_normal((B, H, K, V)) if opt else np.zeros((B, H, K, V))
+    go = rng.standard_normal((B, T, H, V))
+    gf = rng.standard_normal((B, H, K, V)) if opt else np.zeros((B, H, K, V))
+    gs = rng.standard_normal((B, T, H)) if opt else np.zeros((B, T, H))
+    d = lambda x: torch.as_tensor(np.asarray(x, np.float32), device=cuda)  # noqa: E731
+    got = dbl.gdn_training_backward(d(q), d(k), d(v), d(a), d(e), d(w), d(valid), d(reset), d(init), d(go),
+                                    d(gf) if opt else None, d(gs) if opt else None, chunk_size=16)
+    torch.cuda.synchronize()
+    ref = O.training_backward(*(np.asarray(x, np.float32) for x in (q, k, v, a, e, w, go, gf, gs)), valid, reset,
+                              np.asarray(init, np.float32))
+    names = ("dq", "dk", "dv", "dalpha", "derase", "dwrite", "dinitial")
+    for name, r in zip(names, ref):
+        g = getattr(got, name).cpu().numpy()
+        assert rel_err(g, r) < TOL_F32, (name, rel_err(g, r))
+    for name in names[:6]:
+        assert np.all(getattr(got, name).cpu().numpy()[~valid] == 0.0), name
+
+
 # ----------------------------------------------------------------------- mixer prologue
 @pytest.mark.parametrize("B,T,H,K,V,W,dtype", [(2, 37, 3, 32, 64, 4, torch.float32),
                                                 (1, 50, 2, 128, 128, 4, torch.bfloat16),
