@@ -527,7 +527,9 @@ def bench_backward(torch, args, dev):
             "higher_is_better": True, "dtype": "f32", "data": "synthetic",
             "config": {"workload": f"B{b}/T{t}/H{h}/K{k_}/V{v_} f32 chunk 16 (the reference's training shape)",
                        "forward_ms": ms_f, "forward_mtok_s": tokens / (ms_f / 1e3) / 1e6},
-            "gpu_launches": 10 + 10}
+            # chunked forms at this shape: the backward launches the chunk-map, main, reverse-map,
+            # reverse and gradient kernels; the forward the chunk-map, main and score kernels
+            "gpu_launches": 10 * 5 + 10 * 3}
     if not args.no_cpu_baseline:
         # the f64 C restatement of the reference's backward on one (b) row of the workload
         sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))

@@ -325,12 +325,12 @@ int nchunks_of(int64_t T, int C) { return (int)((T + C - 1) / C); }
 }  // namespace
 
 // Whether the backward of these shapes runs in the chunked form (scan_chunk_bwd.cu): 16-token
-// checkpoints and the shapes the chunked forward takes.
+// checkpoints and the shapes chunk_backward_supported takes.
 bool chunked_backward(int64_t B, int64_t T, int64_t H, int64_t K, int64_t V, int chunk) {
     if (chunk != 16 || B > 0x7fffffff || T > 0x7fffffff || H > 0x7fffffff || K > 64 || V > 256) return false;
     const SeqParams sp = chunk_backward_forward_params((int)B, (int)T, (int)H, (int)K, (int)V, nullptr, nullptr,
                                                        nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr);
-    return chunk_scan_supported(sp);
+    return chunk_backward_supported(sp);
 }
 
 size_t training_backward_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t K, int64_t V, int chunk) {

@@ -335,8 +335,11 @@ __host__ __device__ inline GradSmem grad_smem(int kmax, int V) {
     return L;
 }
 
+// 512 threads: each phase's work items (up to 320 tiles, 16 x K channel walks) fit in one round
+constexpr int GTH = 512;
+
 template <int KMAX>
-__global__ void __launch_bounds__(CTH) chunk_bwd_grad_kernel(const CBwdParams p) {
+__global__ void __launch_bounds__(GTH, 2) chunk_bwd_grad_kernel(const CBwdParams p) {
     constexpr int SR = CC + 4;
     extern __shared__ __align__(16) float smem_g[];
     const int K = p.K, V = p.V, K4 = (K + 3) & ~3, V4 = (V + 3) & ~3;
@@ -386,12 +389,12 @@ __global__ void __launch_bounds__(CTH) chunk_bwd_grad_kernel(const CBwdParams p)
         skn[tid] = fb[F.kn + tid];
         sgs[tid] = (in && p.g_score) ? p.g_score[tok(p, b, t, h)] : 0.f;
     }
-    for (int x = tid; x < CC * SR; x += CTH) {
+    for (int x = tid; x < CC * SR; x += GTH) {
         const int t = x / SR, s = x - t * SR;
         sTiT[x] = s < CC ? fb[F.ti + s * CC + t] : 0.f;
     }
     __syncthreads();
-    for (int x = tid; x < CC * KMAX; x += CTH) {
+    for (int x = tid; x < CC * KMAX; x += GTH) {
         const int u = x / KMAX, i = x - u * KMAX;
         const int t = t0 + u;
         const bool act = sact[u], rst = srst[u];
@@ -413,14 +416,14 @@ __global__ void __launch_bounds__(CTH) chunk_bwd_grad_kernel(const CBwdParams p)
         sek[u][i] = e * kv;
         sP[u][i] = pv;
     }
-    for (int x = tid; x < CC * CV; x += CTH) {
+    for (int x = tid; x < CC * CV; x += GTH) {
         const int t = x / CV, j = x - t * CV;
         const bool in = t < n && j < V;
         sE[x] = in ? p.edits[tok(p, b, t0 + t, h) * V + j] : 0.f;
         sdE[x] = in ? p.dE[(((size_t)bh * nch + c) * CC + t) * V + j] : 0.f;
         sdO[x] = (in && sact[t]) ? p.g_out[tok(p, b, t0 + t, h) * V + j] : 0.f;
     }
-    for (int x = tid; x < KMAX * CV; x += CTH) {
+    for (int x = tid; x < KMAX * CV; x += GTH) {
         const int i = x / CV, j = x - i * CV;
         const bool in = i < K && j < V;
         sS0[x] = in ? p.ck[((size_t)bh * nch + c) * K * V + (size_t)i * V + j] : 0.f;
@@ -431,7 +434,7 @@ __global__ void __launch_bounds__(CTH) chunk_bwd_grad_kernel(const CBwdParams p)
     {
         const int nv = V4 / 4, nk = K4 / 4;
         const int t1 = (CC / 2) * nv, t2 = (CC / 2) * nk, t3 = (CC / 2) * (CC / 4), t4 = (CC / 2) * nk;
-        for (int x = tid; x < t1 + t2 + t3 + t4 + K; x += CTH) {
+        for (int x = tid; x < t1 + t2 + t3 + t4 + K; x += GTH) {
             float acc[2][4] = {};
             int y = x;
             if (y < t1) {
@@ -478,7 +481,7 @@ __global__ void __launch_bounds__(CTH) chunk_bwd_grad_kernel(const CBwdParams p)
     {
         const int nk = K4 / 4;
         const int t1 = (CC / 2) * nk, t2 = (CC / 2) * (CC / 4);
-        for (int x = tid; x < t1 + t2; x += CTH) {
+        for (int x = tid; x < t1 + t2; x += GTH) {
             float acc[2][4] = {};
             if (x < t1) {
                 const int r0 = 2 * (x / nk), n0 = 4 * (x - (x / nk) * nk);
@@ -496,7 +499,7 @@ __global__ void __launch_bounds__(CTH) chunk_bwd_grad_kernel(const CBwdParams p)
                     for (int cc = 0; cc < 4; ++cc) sdA[r0 + r][n0 + cc] = n0 + cc < r0 + r ? -acc[r][cc] : 0.f;
             }
         }
-        for (int x = tid; x < n * V; x += CTH) {
+        for (int x = tid; x < n * V; x += GTH) {
             const int t = x / V, j = x - t * V;
             const size_t gi = tok(p, b, t0 + t, h) * V + j;
             const float dwv = sact[t] ? sdWV[t * CV + j] : 0.f;
@@ -506,7 +509,7 @@ __global__ void __launch_bounds__(CTH) chunk_bwd_grad_kernel(const CBwdParams p)
     }
     __syncthreads();
     // phase 3, per (token t, key channel i): dq, d(ek), dk from A, M, Wd; dP
-    for (int x = tid; x < CC * K; x += CTH) {
+    for (int x = tid; x < CC * K; x += GTH) {
         const int t = x / K, i = x - t * K;
         const float pt = sP[t][i];
         float gq = sdQp[t][i] * pt, dek = sdB[t][i] * pt;
@@ -539,7 +542,7 @@ __global__ void __launch_bounds__(CTH) chunk_bwd_grad_kernel(const CBwdParams p)
     }
     __syncthreads();
     // phase 4, per (token u, key channel i): d alpha
-    for (int x = tid; x < n * K; x += CTH) {
+    for (int x = tid; x < n * K; x += GTH) {
         const int u = x / K, i = x - u * K;
         const float pm1 = u > 0 ? sP[u - 1][i] : 1.f;
         float df = 0.f, dtu = 1.f;  // d[t][u]
@@ -582,7 +585,7 @@ int launch_grad(const CBwdParams& p, cudaStream_t st) {
     });
     if (rc != DBL_OK) return rc;
     const size_t smem = (size_t)grad_smem(KMAX, p.V).total * sizeof(float);
-    chunk_bwd_grad_kernel<KMAX><<<(unsigned)((int64_t)p.B * p.H * p.nch), CTH, smem, st>>>(p);
+    chunk_bwd_grad_kernel<KMAX><<<(unsigned)((int64_t)p.B * p.H * p.nch), GTH, smem, st>>>(p);
     return launch_status("chunk_bwd_grad_kernel");
 }
 
@@ -645,7 +648,17 @@ SeqParams chunk_backward_forward_params(int B, int T, int H, int K, int V, const
 
 size_t chunk_backward_workspace_floats(const SeqParams& sp) { return cbwd_ws(sp).total; }
 
-// Runs the chunked backward for 16-token checkpoints (the caller checked chunk_scan_supported on
+// Whether the backward of `sp` runs in chunked form: the chunked forward's widths (K <= 64,
+// V <= 128, T >= 32, a zero or given initial state) and B*H ceil(K/32) ceil(V/64) <= 512.  Unlike
+// the forward it replaces a token-sequential kernel that is slow at every size (measured at
+// T512/K32/V64: 64 rows 1.21 vs 0.45 ms chunked, 512 rows 5.14 vs 2.86 ms; K64/V128 at 128 rows
+// even, 3.20 vs 3.10 ms).
+bool chunk_backward_supported(const SeqParams& sp) {
+    return sp.K <= 64 && sp.V <= CVMAX && sp.init_mode != 2 && sp.T >= 2 * CC &&
+           (int64_t)sp.B * sp.H * ((sp.K + 31) / 32) * ((sp.V + 63) / 64) <= 512;
+}
+
+// Runs the chunked backward for 16-token checkpoints (the caller checked chunk_backward_supported on
 // `sp`); `ws` holds chunk_backward_workspace_floats(sp) floats.
 int launch_chunk_backward(const SeqParams& sp, const float* g_out, const float* g_fin, const float* g_score,
                           float* dq, float* dk, float* dv, float* dalpha, float* derase, float* dwrite,

@@ -49,6 +49,7 @@ SeqParams chunk_backward_forward_params(int B, int T, int H, int K, int V, const
                                         const float* v, const float* alpha, const float* erase, const float* write,
                                         const float* valid, const float* reset, const float* initial);
 size_t chunk_backward_workspace_floats(const SeqParams& sp);
+bool chunk_backward_supported(const SeqParams& sp);
 int launch_chunk_backward(const SeqParams& sp, const float* g_out, const float* g_fin, const float* g_score,
                           float* dq, float* dk, float* dv, float* dalpha, float* derase, float* dwrite,
                           float* dinitial, float* ws, cudaStream_t st);
