@@ -65,18 +65,21 @@ __host__ __device__ inline RevBlock rev_block(int K, int V) {
     return L;
 }
 
-// acc[r][c] += sum_{x < n4} A[(r0 + r) lda + x] Bm[(n0 + c) ldb + x] (both operands contiguous in x,
-// read four at a time; n4 a multiple of 4)
-__device__ __forceinline__ void tile_nt(float (&acc)[2][4], const float* A, int lda, int r0, const float* Bm, int ldb,
-                                        int n0, int n4) {
+// acc[r][c] += sum_{s < kd} A[(r0 + r) lda + s] Bm[s ldb + n0 + c] for a 2 x 4 tile (tile_mm with a
+// contraction length kd, a multiple of 4)
+__device__ __forceinline__ void tile_mmk(float (&acc)[2][4], const float* A, int lda, int r0, const float* Bm,
+                                         int ldb, int n0, int kd) {
 #pragma unroll 2
-    for (int x = 0; x < n4; x += 4) {
-        const float4 a0 = lds4(A + r0 * lda + x), a1 = lds4(A + (r0 + 1) * lda + x);
+    for (int s = 0; s < kd; s += 4) {
+        const float4 b0 = lds4(Bm + (s + 0) * ldb + n0), b1 = lds4(Bm + (s + 1) * ldb + n0);
+        const float4 b2 = lds4(Bm + (s + 2) * ldb + n0), b3 = lds4(Bm + (s + 3) * ldb + n0);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const float4 bv = lds4(Bm + (n0 + c) * ldb + x);
-            acc[0][c] = fmaf(a0.x, bv.x, fmaf(a0.y, bv.y, fmaf(a0.z, bv.z, fmaf(a0.w, bv.w, acc[0][c]))));
-            acc[1][c] = fmaf(a1.x, bv.x, fmaf(a1.y, bv.y, fmaf(a1.z, bv.z, fmaf(a1.w, bv.w, acc[1][c]))));
+        for (int r = 0; r < 2; ++r) {
+            const float4 a = lds4(A + (r0 + r) * lda + s);
+            acc[r][0] = fmaf(a.x, b0.x, fmaf(a.y, b1.x, fmaf(a.z, b2.x, fmaf(a.w, b3.x, acc[r][0]))));
+            acc[r][1] = fmaf(a.x, b0.y, fmaf(a.y, b1.y, fmaf(a.z, b2.y, fmaf(a.w, b3.y, acc[r][1]))));
+            acc[r][2] = fmaf(a.x, b0.z, fmaf(a.y, b1.z, fmaf(a.z, b2.z, fmaf(a.w, b3.z, acc[r][2]))));
+            acc[r][3] = fmaf(a.x, b0.w, fmaf(a.y, b1.w, fmaf(a.z, b2.w, fmaf(a.w, b3.w, acc[r][3]))));
         }
     }
 }
@@ -296,14 +299,18 @@ __global__ void __launch_bounds__(CTH) chunk_bwd_rev_kernel(const CBwdParams p, 
 // ------------------------------------------------------------------------------------------------
 // Per chunk: every input gradient (see the top of the file).  Shared memory carve-up, in floats;
 // rows of value width use the stride CV = V4 + 4.
+// S0, dS_end and E are also kept transposed (contraction index as the row: S0T [V4][KT],
+// dST [V4][KT], ET [V4][CC + 4]) so that every product is a tile_mm whose consecutive lanes read
+// consecutive float4s of the B operand.
 struct GradSmem {
-    int cv, k, q, ek, f, er, P, tit, E, dE, dO, dWV, S0, dS, dQp, dB, dWd, dP, dM, dA, dPl, en, kn, gs, act, rst,
-        total;
+    int cv, kt, k, q, ek, f, er, P, tit, E, dE, dO, dWV, S0T, dST, ET, dQp, dB, dWd, dP, dM, dA, dPl, en, kn, gs,
+        act, rst, total;
 };
 __host__ __device__ inline GradSmem grad_smem(int kmax, int V) {
     GradSmem L{};
     const int V4 = (V + 3) & ~3;
     L.cv = V4 + 4;
+    L.kt = kmax + 4;
     const int tk = CC * kmax, tv = CC * L.cv, sr = CC * (CC + 4);
     int o = 0;
     L.k = o; o += tk;
@@ -317,8 +324,9 @@ __host__ __device__ inline GradSmem grad_smem(int kmax, int V) {
     L.dE = o; o += tv;
     L.dO = o; o += tv;
     L.dWV = o; o += tv;
-    L.S0 = o; o += kmax * L.cv;
-    L.dS = o; o += kmax * L.cv;
+    L.S0T = o; o += V4 * L.kt;
+    L.dST = o; o += V4 * L.kt;
+    L.ET = o; o += V4 * (CC + 4);
     L.dQp = o; o += tk;
     L.dB = o; o += tk;
     L.dWd = o; o += tk;
@@ -366,8 +374,10 @@ __global__ void __launch_bounds__(GTH, 2) chunk_bwd_grad_kernel(const CBwdParams
     float* sdE = smem_g + L.dE;
     float* sdO = smem_g + L.dO;
     float* sdWV = smem_g + L.dWV;
-    float* sS0 = smem_g + L.S0;
-    float* sdS = smem_g + L.dS;
+    float* sS0T = smem_g + L.S0T;
+    float* sdST = smem_g + L.dST;
+    float* sET = smem_g + L.ET;
+    const int KT = L.kt;
     float* sdPl = smem_g + L.dPl;
     float* sen = smem_g + L.en;
     float* skn = smem_g + L.kn;
@@ -419,15 +429,18 @@ __global__ void __launch_bounds__(GTH, 2) chunk_bwd_grad_kernel(const CBwdParams
     for (int x = tid; x < CC * CV; x += GTH) {
         const int t = x / CV, j = x - t * CV;
         const bool in = t < n && j < V;
-        sE[x] = in ? p.edits[tok(p, b, t0 + t, h) * V + j] : 0.f;
+        const float ev = in ? p.edits[tok(p, b, t0 + t, h) * V + j] : 0.f;
+        sE[x] = ev;
+        if (j < V4) sET[j * SR + t] = ev;
         sdE[x] = in ? p.dE[(((size_t)bh * nch + c) * CC + t) * V + j] : 0.f;
         sdO[x] = (in && sact[t]) ? p.g_out[tok(p, b, t0 + t, h) * V + j] : 0.f;
     }
-    for (int x = tid; x < KMAX * CV; x += GTH) {
-        const int i = x / CV, j = x - i * CV;
+    // transposed: consecutive threads read consecutive j of one state row
+    for (int x = tid; x < KT * V4; x += GTH) {
+        const int i = x / V4, j = x - i * V4;
         const bool in = i < K && j < V;
-        sS0[x] = in ? p.ck[((size_t)bh * nch + c) * K * V + (size_t)i * V + j] : 0.f;
-        sdS[x] = in ? p.dSe[((size_t)bh * nch + c) * K * V + (size_t)i * V + j] : 0.f;
+        sS0T[j * KT + i] = in ? p.ck[((size_t)bh * nch + c) * K * V + (size_t)i * V + j] : 0.f;
+        sdST[j * KT + i] = in ? p.dSe[((size_t)bh * nch + c) * K * V + (size_t)i * V + j] : 0.f;
     }
     __syncthreads();
     // phase 1: dWV = Ti^T dE, dQ' = dO S0^T, dM = lower(dO E^T), dWd = E dS^T, dP_last
@@ -446,21 +459,21 @@ __global__ void __launch_bounds__(GTH, 2) chunk_bwd_grad_kernel(const CBwdParams
                         make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
             } else if ((y -= t1) < t2) {
                 const int r0 = 2 * (y / nk), n0 = 4 * (y - (y / nk) * nk);
-                tile_nt(acc, sdO, CV, r0, sS0, CV, n0, V4);
+                tile_mmk(acc, sdO, CV, r0, sS0T, KT, n0, V4);
 #pragma unroll
                 for (int r = 0; r < 2; ++r)
 #pragma unroll
                     for (int cc = 0; cc < 4; ++cc) sdQp[r0 + r][n0 + cc] = acc[r][cc];
             } else if ((y -= t2) < t3) {
                 const int r0 = 2 * (y / 4), n0 = 4 * (y % 4);
-                tile_nt(acc, sdO, CV, r0, sE, CV, n0, V4);
+                tile_mmk(acc, sdO, CV, r0, sET, SR, n0, V4);
 #pragma unroll
                 for (int r = 0; r < 2; ++r)
 #pragma unroll
                     for (int cc = 0; cc < 4; ++cc) sdM[r0 + r][n0 + cc] = n0 + cc <= r0 + r ? acc[r][cc] : 0.f;
             } else if ((y -= t3) < t4) {
                 const int r0 = 2 * (y / nk), n0 = 4 * (y - (y / nk) * nk);
-                tile_nt(acc, sE, CV, r0, sdS, CV, n0, V4);
+                tile_mmk(acc, sE, CV, r0, sdST, KT, n0, V4);
 #pragma unroll
                 for (int r = 0; r < 2; ++r)
 #pragma unroll
@@ -468,10 +481,7 @@ __global__ void __launch_bounds__(GTH, 2) chunk_bwd_grad_kernel(const CBwdParams
             } else {
                 const int i = y - t4;
                 float sacc = 0.f;
-                for (int jj = 0; jj < V4; jj += 4) {
-                    const float4 a = lds4(sS0 + i * CV + jj), g = lds4(sdS + i * CV + jj);
-                    sacc = fmaf(a.x, g.x, fmaf(a.y, g.y, fmaf(a.z, g.z, fmaf(a.w, g.w, sacc))));
-                }
+                for (int jj = 0; jj < V; ++jj) sacc = fmaf(sS0T[jj * KT + i], sdST[jj * KT + i], sacc);
                 sdPl[i] = sacc;
             }
         }
@@ -485,14 +495,14 @@ __global__ void __launch_bounds__(GTH, 2) chunk_bwd_grad_kernel(const CBwdParams
             float acc[2][4] = {};
             if (x < t1) {
                 const int r0 = 2 * (x / nk), n0 = 4 * (x - (x / nk) * nk);
-                tile_nt(acc, sdWV, CV, r0, sS0, CV, n0, V4);
+                tile_mmk(acc, sdWV, CV, r0, sS0T, KT, n0, V4);
 #pragma unroll
                 for (int r = 0; r < 2; ++r)
 #pragma unroll
                     for (int cc = 0; cc < 4; ++cc) sdB[r0 + r][n0 + cc] = -acc[r][cc];
             } else {
                 const int y = x - t1, r0 = 2 * (y / 4), n0 = 4 * (y % 4);
-                tile_nt(acc, sdWV, CV, r0, sE, CV, n0, V4);
+                tile_mmk(acc, sdWV, CV, r0, sET, SR, n0, V4);
 #pragma unroll
                 for (int r = 0; r < 2; ++r)
 #pragma unroll
