@@ -299,63 +299,76 @@ __global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, floa
     }
 }
 
-// The sequential pass: one CTA per (b, h, column group of VG = 16 or 32 columns), the group's state columns
-// S [K4][VG] in shared memory (double-buffered; K4 = K rounded up to 4, the extra rows zero), the
-// chunk maps in a ring of NB buffers filled by cp.async NB - 1 chunks ahead, so that a chunk's
-// L2 latency hides behind the compute of the chunks before it.  Thread
-// (rr, j) owns column j, tokens rr + m RP and state rows rr + m RP: one pass over the key channels,
-// four at a time, accumulates o, the edit and the new state from the same state loads.  One barrier
-// per chunk; the scores of a chunk are written after the next chunk's barrier.  With one group the
-// scores are final here; with several, each group writes its partial sums of edit^2 to `part`.
-template <int KMAX, int VG>
-__global__ void __launch_bounds__(CTH) chunk_main_kernel(const SeqParams p, const float* ws, float* part,
+// The sequential pass: one CTA per (b, h, column group of VG = 16 or 32 columns), the group's state
+// columns S [K4][VG + 4] in shared memory (double-buffered; K4 = K rounded up to 4, the extra rows
+// zero), the chunk maps in a ring of NB buffers filled by cp.async NB - 1 chunks ahead, so that a
+// chunk's L2 latency hides behind the compute of the chunks before it.  The 256 slots (rr, j) own
+// column j, tokens rr + m RP and state rows rr + m RP.  With NTH = 512 threads (grids of one wave)
+// the two 16-lane halves of a warp take the same slots and alternate blocks of four key channels
+// (one shuffle joins them; the state row stride VG + 4 puts the halves' rows on different banks);
+// with 256 (more CTAs than SMs at key widths up to 32, where two CTAs share an SM) each slot is one
+// thread.  One pass over the key channels
+// accumulates o, the edit and the new state from the same state loads; one barrier per chunk; the
+// scores of a chunk are written after the next chunk's barrier.  With one group the scores are final
+// here; with several, each group writes its partial sums of edit^2 to `part`.
+template <int KMAX, int VG, int NTH>
+__global__ void __launch_bounds__(NTH) chunk_main_kernel(const SeqParams p, const float* ws, float* part,
                                                          int ngroups, int NB, int extra) {
-    constexpr int RP = CTH / VG;               // token (and state) rows per pass
-    constexpr int NT = CC / RP;                // tokens per thread
-    constexpr int NS = KMAX / RP;              // state rows per thread
-    constexpr int NP = VG > 32 ? VG / 32 : 1;  // warps sharing one token
-    constexpr int RW = VG < 32 ? VG : 32;      // lanes sharing one token within a warp
+    constexpr int MTH = NTH;
+    constexpr int HALVES = NTH / 256;  // threads per slot
+    constexpr int RP = 256 / VG;  // token (and state) rows per pass
+    constexpr int NT = CC / RP;   // tokens per thread
+    constexpr int NS = KMAX / RP; // state rows per thread
+    constexpr int NP = VG / 16;   // 16-lane groups sharing one token
+    constexpr int SST = VG + 4;   // state row stride
+    constexpr int MAXCOL = 8;     // column-part copies per thread and chunk (at most 96 rows x 32 columns)
     extern __shared__ __align__(16) float smain[];
     const int K = p.K, V = p.V, K4 = (K + 3) & ~3;
     const int nch = (p.T + CC - 1) / CC;
     const int grp = blockIdx.x % ngroups, bh = blockIdx.x / ngroups;
     const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
     const int c0 = grp * VG, vg = min(VG, V - c0);
-    const int tid = threadIdx.x, j = tid % VG, rr = tid / VG;
+    const int tid = threadIdx.x, lane = tid & 31, half = HALVES == 2 ? lane >> 4 : 0;
+    const int slot = HALVES == 2 ? (tid >> 5) * 16 + (lane & 15) : tid;
+    const int j = slot % VG, rr = slot / VG;
     const ChunkBlock L = chunk_block(K, V, extra != 0);
     const int KP = L.kp;
     const int rows = 2 * CC + K;  // O0, U0, H rows
     const int bfl = L.sh + rows * VG;
     float* Sb0 = smain;
-    float* Sb1 = smain + K4 * VG;
-    float* bb0 = smain + 2 * K4 * VG;  // NB buffers of bfl floats
-    float* ssqp = bb0 + NB * bfl;      // [2][CC][NP]
+    float* Sb1 = smain + K4 * SST;
+    float* bb0 = smain + 2 * K4 * SST;  // NB buffers of bfl floats
+    float* ssqp = bb0 + NB * bfl;       // [2][CC][NP]
     const bool vec = (V & 3) == 0;
     const size_t sbase = ((size_t)b * p.H + h) * K * V;
-    for (int x = tid; x < K4 * VG; x += CTH) {
-        const int i = x / VG, jj = x - i * VG;
+    for (int x = tid; x < K4 * SST; x += MTH) {
+        const int i = x / SST, jj = x - i * SST;
         Sb0[x] = (p.init_mode == 1 && i < K && jj < vg) ? p.initial[sbase + (size_t)i * V + c0 + jj] : 0.f;
         Sb1[x] = 0.f;
     }
-    // stages chunk c into buffer c % NB and commits one group (an empty one past the last chunk)
-    auto prefetch = [&](int c) {
-        if (c >= nch) {
-            cp_async_commit();
-            return;
-        }
-        const float* src = ws + ((size_t)bh * nch + c) * L.total;
-        float* dst = bb0 + (c % NB) * bfl;
-        for (int x = tid; x < L.sh / 4; x += CTH) cp_async16(dst + 4 * x, src + 4 * x);
-        if (vec) {
-            const int q4 = vg >> 2;
-            for (int x = tid; x < rows * q4; x += CTH) {
-                const int r = x / q4, w = x - r * q4;
-                cp_async16(dst + L.sh + r * VG + 4 * w, src + L.sh + (size_t)r * V + c0 + 4 * w);
-            }
-        } else {
-            for (int x = tid; x < rows * vg; x += CTH) {
-                const int r = x / vg, w = x - r * vg;
-                cp_async4(dst + L.sh + r * VG + w, src + L.sh + (size_t)r * V + c0 + w);
+    // this thread's copies of the column-sliced part (O0, U0, H rows), the same every chunk:
+    // shared-memory and block offsets in floats (16-byte copies when V is a multiple of 4)
+    int soff[MAXCOL], goff[MAXCOL];
+    const int per = vec ? vg >> 2 : vg, ncopy = rows * per;
+#pragma unroll
+    for (int k = 0; k < MAXCOL; ++k) {
+        const int x = tid + k * MTH;
+        const int r = x / per, w = x - r * per;
+        soff[k] = L.sh + r * VG + (vec ? 4 * w : w);
+        goff[k] = L.sh + r * V + c0 + (vec ? 4 * w : w);
+    }
+    // stages chunk c into buffer `buf` and commits one group (an empty one past the last chunk)
+    auto prefetch = [&](int c, int buf) {
+        if (c < nch) {
+            const float* src = ws + ((size_t)bh * nch + c) * L.total;
+            float* dst = bb0 + buf * bfl;
+            for (int x = tid; x < L.sh / 4; x += MTH) cp_async16(dst + 4 * x, src + 4 * x);
+#pragma unroll
+            for (int k = 0; k < MAXCOL; ++k) {
+                if (tid + k * MTH < ncopy) {
+                    if (vec) cp_async16(dst + soff[k], src + goff[k]);
+                    else cp_async4(dst + soff[k], src + goff[k]);
+                }
             }
         }
         cp_async_commit();
@@ -372,79 +385,91 @@ __global__ void __launch_bounds__(CTH) chunk_main_kernel(const SeqParams p, cons
             else part[(size_t)grp * p.B * p.T * p.H + si] = s;
         }
     };
-    for (int c = 0; c < NB - 1; ++c) prefetch(c);
+    for (int c = 0; c < NB - 1; ++c) prefetch(c, c);
     float kn_prev = 0.f;
+    int cur = 0;  // buffer of chunk c; chunk c + NB - 1 goes to the buffer before it
     for (int c = 0; c < nch; ++c) {
         const int t0 = c * CC, n = min(CC, p.T - t0);
         cp_async_wait_pending(NB - 2);
         __syncthreads();  // chunk c's maps, the state and the previous chunk's edit sums are in place
-        prefetch(c + NB - 1);  // into the buffer of chunk c - 1, which every thread has finished
-        const float* blk = bb0 + (c % NB) * bfl;
+        prefetch(c + NB - 1, cur == 0 ? NB - 1 : cur - 1);  // the buffer of chunk c - 1, finished by all
+        const float* blk = bb0 + cur * bfl;
+        cur = cur + 1 == NB ? 0 : cur + 1;
         if (p.scores && c > 0) write_scores(c - 1, kn_prev);
-        if (p.chunk_states) {
-            float* cs = p.chunk_states + ((size_t)bh * nch + c) * K * V + c0 + j;
-            const float* S = (c & 1) ? Sb1 : Sb0;
-            if (j < vg) {
-#pragma unroll
-                for (int m = 0; m < NS; ++m)
-                    if (rr + m * RP < K) cs[(size_t)(rr + m * RP) * V] = S[(rr + m * RP) * VG + j];
-            }
-        }
-        kn_prev = (p.scores && tid < n) ? blk[L.kn + tid] : 0.f;
         const float* S = (c & 1) ? Sb1 : Sb0;
         float* Sn = (c & 1) ? Sb0 : Sb1;
+        if (p.chunk_states && half == HALVES - 1 && j < vg) {
+            float* cs = p.chunk_states + ((size_t)bh * nch + c) * K * V + c0 + j;
+#pragma unroll
+            for (int m = 0; m < NS; ++m)
+                if (rr + m * RP < K) cs[(size_t)(rr + m * RP) * V] = S[(rr + m * RP) * SST + j];
+        }
+        kn_prev = (p.scores && tid < n) ? blk[L.kn + tid] : 0.f;
         const float* qe = blk + L.qe;
         const float* bp = blk + L.bp;
         const float* g = blk + L.g;
         const float* o0 = blk + L.sh;
         const float* u0 = o0 + CC * VG;
         const float* hh = u0 + CC * VG;
+        // half 0 starts from the chunk's constant terms, half 1 from zero
         float o[NT], u[NT], acc[NS];
 #pragma unroll
         for (int m = 0; m < NT; ++m) {
-            o[m] = o0[(rr + m * RP) * VG + j];
-            u[m] = u0[(rr + m * RP) * VG + j];
+            o[m] = half ? 0.f : o0[(rr + m * RP) * VG + j];
+            u[m] = half ? 0.f : u0[(rr + m * RP) * VG + j];
         }
 #pragma unroll
-        for (int m = 0; m < NS; ++m) acc[m] = (rr + m * RP < K) ? hh[(rr + m * RP) * VG + j] : 0.f;
+        for (int m = 0; m < NS; ++m) acc[m] = (half == 0 && rr + m * RP < K) ? hh[(rr + m * RP) * VG + j] : 0.f;
 #pragma unroll 2
-        for (int i = 0; i < K4; i += 4) {
-            const float s0 = S[(i + 0) * VG + j], s1 = S[(i + 1) * VG + j];
-            const float s2 = S[(i + 2) * VG + j], s3 = S[(i + 3) * VG + j];
+        for (int i = 4 * half; i < K4; i += 4 * HALVES) {
+            const float s0 = S[(i + 0) * SST + j], s1 = S[(i + 1) * SST + j];
+            const float s2 = S[(i + 2) * SST + j], s3 = S[(i + 3) * SST + j];
 #pragma unroll
             for (int m = 0; m < NT; ++m) {
-                const float4 qv = *reinterpret_cast<const float4*>(qe + (rr + m * RP) * KP + i);
-                const float4 bv = *reinterpret_cast<const float4*>(bp + (rr + m * RP) * KP + i);
+                const float4 qv = lds4(qe + (rr + m * RP) * KP + i);
+                const float4 bv = lds4(bp + (rr + m * RP) * KP + i);
                 o[m] = fmaf(qv.x, s0, fmaf(qv.y, s1, fmaf(qv.z, s2, fmaf(qv.w, s3, o[m]))));
                 u[m] = fmaf(-bv.x, s0, fmaf(-bv.y, s1, fmaf(-bv.z, s2, fmaf(-bv.w, s3, u[m]))));
             }
 #pragma unroll
             for (int m = 0; m < NS; ++m) {
                 if (rr + m * RP < K) {
-                    const float4 gv = *reinterpret_cast<const float4*>(g + (rr + m * RP) * KP + i);
+                    const float4 gv = lds4(g + (rr + m * RP) * KP + i);
                     acc[m] = fmaf(gv.x, s0, fmaf(gv.y, s1, fmaf(gv.z, s2, fmaf(gv.w, s3, acc[m]))));
                 }
             }
         }
+        if constexpr (HALVES == 2) {
 #pragma unroll
-        for (int m = 0; m < NS; ++m)
-            if (rr + m * RP < K) Sn[(rr + m * RP) * VG + j] = acc[m];
+            for (int m = 0; m < NT; ++m) {
+                o[m] += __shfl_xor_sync(0xffffffffu, o[m], 16);
+                u[m] += __shfl_xor_sync(0xffffffffu, u[m], 16);
+            }
+#pragma unroll
+            for (int m = 0; m < NS; ++m) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], 16);
+        }
+        if (half == HALVES - 1) {
+#pragma unroll
+            for (int m = 0; m < NS; ++m)
+                if (rr + m * RP < K) Sn[(rr + m * RP) * SST + j] = acc[m];
+        }
 #pragma unroll
         for (int m = 0; m < NT; ++m) {
             const int t = rr + m * RP;
-            if (t < n && j < vg && p.edits)
-                p.edits[(((size_t)b * p.T + t0 + t) * p.H + h) * V + c0 + j] = u[m];
-            if (t < n && j < vg && p.out) {
-                const size_t oi = (size_t)b * p.os[0] + (size_t)(t0 + t) * p.os[1] + (size_t)h * p.os[2] +
-                                  (size_t)(c0 + j) * p.os[3];
-                if (p.out_dtype == DBL_BF16) static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(o[m]);
-                else static_cast<float*>(p.out)[oi] = o[m];
+            if (half == 0 && t < n && j < vg) {
+                if (p.edits) p.edits[(((size_t)b * p.T + t0 + t) * p.H + h) * V + c0 + j] = u[m];
+                if (p.out) {
+                    const size_t oi = (size_t)b * p.os[0] + (size_t)(t0 + t) * p.os[1] + (size_t)h * p.os[2] +
+                                      (size_t)(c0 + j) * p.os[3];
+                    if (p.out_dtype == DBL_BF16) static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(o[m]);
+                    else static_cast<float*>(p.out)[oi] = o[m];
+                }
             }
             if (p.scores) {
                 float e2 = j < vg ? u[m] * u[m] : 0.f;
 #pragma unroll
-                for (int w = RW / 2; w > 0; w >>= 1) e2 += __shfl_xor_sync(0xffffffffu, e2, w);
-                if ((j & (RW - 1)) == 0) ssqp[(c & 1) * CC * NP + t * NP + j / 32] = e2;
+                for (int w = 8; w > 0; w >>= 1) e2 += __shfl_xor_sync(0xffffffffu, e2, w);
+                if (half == 0 && (lane & 15) == 0) ssqp[(c & 1) * CC * NP + t * NP + j / 16] = e2;
             }
         }
     }
@@ -452,9 +477,9 @@ __global__ void __launch_bounds__(CTH) chunk_main_kernel(const SeqParams p, cons
     if (p.scores) write_scores(nch - 1, kn_prev);
     if (p.final_state) {
         const float* S = (nch & 1) ? Sb1 : Sb0;
-        for (int x = tid; x < K * vg; x += CTH) {
+        for (int x = tid; x < K * vg; x += MTH) {
             const int i = x / vg, jj = x - i * vg;
-            p.final_state[sbase + (size_t)i * V + c0 + jj] = S[i * VG + jj];
+            p.final_state[sbase + (size_t)i * V + c0 + jj] = S[i * SST + jj];
         }
     }
 }
@@ -512,18 +537,29 @@ int scratch_pool(cudaMemPool_t* out) {
     return DBL_OK;
 }
 
-template <int KMAX, int VG>
-int launch_main(const SeqParams& p, const float* ws, float* part, int ngroups, int NB, int extra, size_t smem,
-                cudaStream_t st) {
+template <int KMAX, int VG, int NTH>
+int launch_main_t(const SeqParams& p, const float* ws, float* part, int ngroups, int NB, int extra, size_t smem,
+                  cudaStream_t st) {
     static std::atomic<uint64_t> attr_done{0};
     const int rc = once_per_device(attr_done, [] {
-        return cuda_status(cudaFuncSetAttribute(chunk_main_kernel<KMAX, VG>,
+        return cuda_status(cudaFuncSetAttribute(chunk_main_kernel<KMAX, VG, NTH>,
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024),
                            "chunk scan: shared memory attribute");
     });
     if (rc != DBL_OK) return rc;
-    chunk_main_kernel<KMAX, VG><<<(unsigned)((int64_t)p.B * p.H * ngroups), CTH, smem, st>>>(p, ws, part, ngroups, NB, extra);
+    chunk_main_kernel<KMAX, VG, NTH><<<(unsigned)((int64_t)p.B * p.H * ngroups), NTH, smem, st>>>(p, ws, part, ngroups, NB, extra);
     return launch_status("chunk_main_kernel");
+}
+
+// 512 threads when the grid is one wave of one CTA per SM or the key width is above 32 (the split
+// of the key channels pays for the second wave: B8/T512/H4/K64/V128, 256 CTAs, 0.246 vs 0.270 ms),
+// else 256 (two CTAs share an SM: B4/T512/H16/K32/V128, 256 CTAs, 0.215 vs 0.264 ms)
+template <int KMAX, int VG>
+int launch_main(const SeqParams& p, const float* ws, float* part, int ngroups, int NB, int extra, size_t smem,
+                cudaStream_t st) {
+    if ((int64_t)p.B * p.H * ngroups <= 148 || p.K > 32)
+        return launch_main_t<KMAX, VG, 512>(p, ws, part, ngroups, NB, extra, smem, st);
+    return launch_main_t<KMAX, VG, 256>(p, ws, part, ngroups, NB, extra, smem, st);
 }
 
 template <int KMAX>
@@ -584,12 +620,13 @@ int launch_chunk_scan(const SeqParams& p, int in_dtype, cudaStream_t st, float* 
     rc = launch_status("chunk_prep_kernel");
     if (rc == DBL_OK) {
         const int K4 = (p.K + 3) & ~3;
-        const int np = VG > 32 ? VG / 32 : 1;
+        const int np = VG / 16;
+        const size_t sfl = (size_t)2 * K4 * (VG + 4);  // the two state buffers
         const size_t bfl = (size_t)L.sh + (2 * CC + p.K) * VG;
         // the deepest ring of 4, 3 or 2 chunk buffers that fits in 227 KB
         int NB = 4;
-        while (NB > 2 && ((size_t)2 * K4 * VG + NB * bfl + 2 * CC * np) * sizeof(float) > 227 * 1024) --NB;
-        const size_t smem = ((size_t)2 * K4 * VG + NB * bfl + 2 * CC * np) * sizeof(float);
+        while (NB > 2 && (sfl + NB * bfl + 2 * CC * np) * sizeof(float) > 227 * 1024) --NB;
+        const size_t smem = (sfl + NB * bfl + 2 * CC * np) * sizeof(float);
         rc = p.K <= 32 ? launch_main_vg<32>(p, ws, part, VG, ngroups, NB, ex, smem, st)
                        : launch_main_vg<64>(p, ws, part, VG, ngroups, NB, ex, smem, st);
     }
