@@ -141,6 +141,10 @@ EXPORTS = [
     ("dbl_gdn_training_scan_backward_workspace_bytes", ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64, _i32]),
     ("dbl_gdn_training_scan_backward", ctypes.c_int,
      [ctypes.POINTER(TrainingScanBackwardArgs), _vp, ctypes.c_size_t, _vp]),
+    ("dbl_gdn_training_scan_context_bytes", ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64, _i32]),
+    ("dbl_gdn_training_scan_save", ctypes.c_int, [ctypes.POINTER(TrainingScanArgs), _vp, ctypes.c_size_t, _vp]),
+    ("dbl_gdn_training_scan_backward_saved", ctypes.c_int,
+     [ctypes.POINTER(TrainingScanBackwardArgs), _vp, ctypes.c_size_t, _vp, ctypes.c_size_t, _vp]),
     ("dbl_gdn2_scan_backward_workspace_bytes", ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64, _i32]),
     ("dbl_gdn2_scan_backward", ctypes.c_int, [ctypes.POINTER(Gdn2ScanBackwardArgs), _vp, ctypes.c_size_t, _vp]),
     ("dbl_gdn2_prologue", ctypes.c_int, [ctypes.POINTER(Gdn2PrologueArgs), _vp]),

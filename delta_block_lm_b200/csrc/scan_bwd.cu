@@ -354,9 +354,12 @@ extern "C" size_t dbl_gdn_training_scan_backward_workspace_bytes(int64_t batch, 
     return dbl::training_backward_workspace_bytes(batch, time, heads, key_dim, value_dim, chunk_size);
 }
 
-extern "C" int dbl_gdn_training_scan_backward(const dbl_training_scan_backward_args* a, void* workspace,
-                                              size_t workspace_bytes, dbl_stream_t stream) {
-    using namespace dbl;
+namespace dbl {
+
+// The backward entry, recomputing the forward (ctx null) or reading a saved context at the shapes
+// that keep one (chunked_backward).
+int training_backward_entry(const dbl_training_scan_backward_args* a, void* workspace, size_t workspace_bytes,
+                            const void* ctx, size_t ctx_bytes, dbl_stream_t stream) {
     if (!a) return fail(DBL_ERR_INVALID_ARGUMENT, "gdn_training_scan_backward: null args");
     if (a->batch <= 0 || a->time <= 0 || a->heads <= 0 || a->key_dim <= 0 || a->value_dim <= 0)
         return fail(DBL_ERR_INVALID_ARGUMENT, "GDN-2 requires nonempty axes");
@@ -409,8 +412,21 @@ extern "C" int dbl_gdn_training_scan_backward(const dbl_training_scan_backward_a
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     // 16-token checkpoints at the shapes of the chunked forward: the chunked backward
     // (scan_chunk_bwd.cu), given a 16-byte aligned workspace
-    if (chunked_backward(a->batch, a->time, a->heads, a->key_dim, a->value_dim, a->chunk_size) &&
-        (reinterpret_cast<uintptr_t>(workspace) & 15) == 0) {
+    const bool chunked = chunked_backward(a->batch, a->time, a->heads, a->key_dim, a->value_dim, a->chunk_size);
+    if (chunked && ctx) {
+        // the saved context of dbl_gdn_training_scan_save (16-byte aligned, checked by the caller)
+        const SeqParams sp = chunk_backward_forward_params(p.B, p.T, p.H, p.K, p.V, p.q, p.k, p.v, p.alpha, p.erase,
+                                                           p.write, p.valid, p.reset, p.initial);
+        if (ctx_bytes < chunk_context_floats(sp) * sizeof(float))
+            return fail(DBL_ERR_WORKSPACE, "gdn_training_scan_backward_saved: context of %zu bytes required (got %zu)",
+                        chunk_context_floats(sp) * sizeof(float), ctx_bytes);
+        if ((reinterpret_cast<uintptr_t>(workspace) & 15) != 0)
+            return fail(DBL_ERR_INVALID_ARGUMENT, "gdn_training_scan_backward_saved: workspace must be 16-byte aligned");
+        return launch_chunk_backward_saved(sp, p.g_out, p.g_fin, p.g_score, p.dq, p.dk, p.dv, p.dalpha, p.derase,
+                                           p.dwrite, p.dinitial, static_cast<const float*>(ctx),
+                                           static_cast<float*>(workspace), st);
+    }
+    if (chunked && (reinterpret_cast<uintptr_t>(workspace) & 15) == 0) {
         const SeqParams sp = chunk_backward_forward_params(p.B, p.T, p.H, p.K, p.V, p.q, p.k, p.v, p.alpha, p.erase,
                                                            p.write, p.valid, p.reset, p.initial);
         return launch_chunk_backward(sp, p.g_out, p.g_fin, p.g_score, p.dq, p.dk, p.dv, p.dalpha, p.derase, p.dwrite,
@@ -436,6 +452,61 @@ extern "C" int dbl_gdn_training_scan_backward(const dbl_training_scan_backward_a
     if (p.K <= 32) e = tpc == 4 ? go(training_backward_kernel<32, 4>) : go(training_backward_kernel<32, 2>);
     else e = tpc == 4 ? go(training_backward_kernel<64, 4>) : go(training_backward_kernel<64, 2>);
     return e == cudaSuccess ? DBL_OK : cuda_status(e, "gdn_training_scan_backward launch");
+}
+
+}  // namespace dbl
+
+extern "C" int dbl_gdn_training_scan_backward(const dbl_training_scan_backward_args* a, void* workspace,
+                                              size_t workspace_bytes, dbl_stream_t stream) {
+    return dbl::training_backward_entry(a, workspace, workspace_bytes, nullptr, 0, stream);
+}
+
+// The reference's forward returns checkpoint and auxiliary tensors beside its outputs and its
+// backward consumes them (gdn_training_ops.rs:201-224, :87-112).  These three calls do the same:
+// at the shapes of the chunked backward the context holds the chunk-start states, the chunk maps and
+// every token's edit; elsewhere it is empty (0 bytes) and the two calls are the plain forward and the
+// recomputing backward.
+extern "C" size_t dbl_gdn_training_scan_context_bytes(int64_t batch, int64_t time, int64_t heads, int64_t key_dim,
+                                                      int64_t value_dim, int32_t chunk_size) {
+    using namespace dbl;
+    if (batch <= 0 || time <= 0 || heads <= 0 || key_dim <= 0 || value_dim <= 0 || chunk_size < 1 ||
+        chunk_size > MAXC)
+        return 0;
+    if (!chunked_backward(batch, time, heads, key_dim, value_dim, chunk_size)) return 0;
+    const SeqParams sp = chunk_backward_forward_params((int)batch, (int)time, (int)heads, (int)key_dim, (int)value_dim,
+                                                       nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                                                       nullptr, nullptr);
+    return chunk_context_floats(sp) * sizeof(float);
+}
+
+extern "C" int dbl_gdn_training_scan_save(const dbl_training_scan_args* a, void* context, size_t context_bytes,
+                                          dbl_stream_t stream) {
+    using namespace dbl;
+    SeqParams p{};
+    int rc = training_scan_params(a, &p);
+    if (rc != DBL_OK) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const size_t need =
+        dbl_gdn_training_scan_context_bytes(a->batch, a->time, a->heads, a->key_dim, a->value_dim, a->chunk_size);
+    if (need == 0) return launch_seq_scan(p, a->dtype, st);
+    if (!context || context_bytes < need)
+        return fail(DBL_ERR_WORKSPACE, "gdn_training_scan_save: context of %zu bytes required (got %zu)", need,
+                    context_bytes);
+    if ((reinterpret_cast<uintptr_t>(context) & 15) != 0)
+        return fail(DBL_ERR_INVALID_ARGUMENT, "gdn_training_scan_save: context must be 16-byte aligned");
+    return launch_chunk_forward_saved(p, a->dtype, static_cast<float*>(context), st);
+}
+
+extern "C" int dbl_gdn_training_scan_backward_saved(const dbl_training_scan_backward_args* a, const void* context,
+                                                    size_t context_bytes, void* workspace, size_t workspace_bytes,
+                                                    dbl_stream_t stream) {
+    using namespace dbl;
+    if (a && context && (reinterpret_cast<uintptr_t>(context) & 15) != 0)
+        return fail(DBL_ERR_INVALID_ARGUMENT, "gdn_training_scan_backward_saved: context must be 16-byte aligned");
+    if (a && !context &&
+        dbl_gdn_training_scan_context_bytes(a->batch, a->time, a->heads, a->key_dim, a->value_dim, a->chunk_size) > 0)
+        return fail(DBL_ERR_WORKSPACE, "gdn_training_scan_backward_saved: these shapes keep a context; pass it");
+    return training_backward_entry(a, workspace, workspace_bytes, context, context_bytes, stream);
 }
 
 // ------------------------------------------------------------------------------ gdn2_scan backward

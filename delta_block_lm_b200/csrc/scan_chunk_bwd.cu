@@ -668,17 +668,15 @@ bool chunk_backward_supported(const SeqParams& sp) {
            (int64_t)sp.B * sp.H * ((sp.K + 31) / 32) * ((sp.V + 63) / 64) <= 512;
 }
 
-// Runs the chunked backward for 16-token checkpoints (the caller checked chunk_backward_supported on
-// `sp`); `ws` holds chunk_backward_workspace_floats(sp) floats.
-int launch_chunk_backward(const SeqParams& sp, const float* g_out, const float* g_fin, const float* g_score,
-                          float* dq, float* dk, float* dv, float* dalpha, float* derase, float* dwrite,
-                          float* dinitial, float* ws, cudaStream_t st) {
+namespace {
+
+// The backward proper (pre, reverse, gradient kernels) given the forward's chunk-start states `ck`,
+// chunk maps `fwd` and edits; its own buffers from `ws` (the carve-up of cbwd_ws).
+int chunk_backward_core(const SeqParams& sp, const float* g_out, const float* g_fin, const float* g_score,
+                        float* dq, float* dk, float* dv, float* dalpha, float* derase, float* dwrite,
+                        float* dinitial, const float* ck, const float* fwd, const float* edits, float* ws,
+                        cudaStream_t st) {
     const CBwdWs W = cbwd_ws(sp);
-    SeqParams fp = sp;
-    fp.chunk_states = ws + W.ck;
-    fp.edits = ws + W.edits;
-    int rc = launch_chunk_scan(fp, DBL_F32, st, ws + W.fwd, true);
-    if (rc != DBL_OK) return rc;
     CBwdParams p{};
     p.B = sp.B;
     p.T = sp.T;
@@ -704,9 +702,9 @@ int launch_chunk_backward(const SeqParams& sp, const float* g_out, const float* 
     p.derase = derase;
     p.dwrite = dwrite;
     p.dinitial = dinitial;
-    p.fwd = ws + W.fwd;
-    p.ck = ws + W.ck;
-    p.edits = ws + W.edits;
+    p.fwd = fwd;
+    p.ck = ck;
+    p.edits = edits;
     p.rev = ws + W.rev;
     p.dE = ws + W.dE;
     p.dSe = ws + W.dSe;
@@ -714,7 +712,7 @@ int launch_chunk_backward(const SeqParams& sp, const float* g_out, const float* 
     const unsigned gchunks = (unsigned)(bh * p.nch);
     if (p.K <= 32) chunk_bwd_pre_kernel<32><<<gchunks, CTH, 0, st>>>(p);
     else chunk_bwd_pre_kernel<64><<<gchunks, CTH, 0, st>>>(p);
-    rc = launch_status("chunk_bwd_pre_kernel");
+    int rc = launch_status("chunk_bwd_pre_kernel");
     if (rc != DBL_OK) return rc;
     const int VG = bh * ((p.V + 31) / 32) >= 148 ? 32 : 16;
     const int ngroups = (p.V + VG - 1) / VG;
@@ -727,6 +725,65 @@ int launch_chunk_backward(const SeqParams& sp, const float* g_out, const float* 
     else rc = VG == 16 ? launch_rev<64, 16>(p, ngroups, NB, smem, st) : launch_rev<64, 32>(p, ngroups, NB, smem, st);
     if (rc != DBL_OK) return rc;
     return p.K <= 32 ? launch_grad<32>(p, st) : launch_grad<64>(p, st);
+}
+
+// The saved context: chunk-start states, chunk maps (laid out as if scores were requested, so the
+// size does not depend on the forward's optional outputs), every token's edit; each segment on
+// 16 bytes.
+struct CtxLayout {
+    size_t ck, fwd, edits, total;
+};
+CtxLayout ctx_layout(const SeqParams& sp) {
+    auto up4 = [](size_t x) { return (x + 3) & ~(size_t)3; };
+    SeqParams with_scores = sp;
+    float dummy = 0.f;
+    with_scores.scores = &dummy;
+    const size_t bh = (size_t)sp.B * sp.H, nch = (size_t)(sp.T + CC - 1) / CC;
+    CtxLayout C{};
+    size_t o = 0;
+    C.ck = o; o += up4(bh * nch * sp.K * sp.V);
+    C.fwd = o; o += up4(chunk_scan_workspace_floats(with_scores, true));
+    C.edits = o; o += up4((size_t)sp.B * sp.T * sp.H * sp.V);
+    C.total = o;
+    return C;
+}
+
+}  // namespace
+
+// Runs the chunked backward for 16-token checkpoints (the caller checked chunk_backward_supported on
+// `sp`); `ws` holds chunk_backward_workspace_floats(sp) floats.  The forward runs first, into `ws`.
+int launch_chunk_backward(const SeqParams& sp, const float* g_out, const float* g_fin, const float* g_score,
+                          float* dq, float* dk, float* dv, float* dalpha, float* derase, float* dwrite,
+                          float* dinitial, float* ws, cudaStream_t st) {
+    const CBwdWs W = cbwd_ws(sp);
+    SeqParams fp = sp;
+    fp.chunk_states = ws + W.ck;
+    fp.edits = ws + W.edits;
+    const int rc = launch_chunk_scan(fp, DBL_F32, st, ws + W.fwd, true);
+    if (rc != DBL_OK) return rc;
+    return chunk_backward_core(sp, g_out, g_fin, g_score, dq, dk, dv, dalpha, derase, dwrite, dinitial, ws + W.ck,
+                               ws + W.fwd, ws + W.edits, ws, st);
+}
+
+size_t chunk_context_floats(const SeqParams& sp) { return ctx_layout(sp).total; }
+
+// The forward of `sp` (outputs as requested) in chunked form, keeping its chunk-start states, maps
+// and edits in `ctx`.
+int launch_chunk_forward_saved(const SeqParams& sp, int in_dtype, float* ctx, cudaStream_t st) {
+    const CtxLayout C = ctx_layout(sp);
+    SeqParams fp = sp;
+    fp.chunk_states = ctx + C.ck;
+    fp.edits = ctx + C.edits;
+    return launch_chunk_scan(fp, in_dtype, st, ctx + C.fwd, true);
+}
+
+// The backward from a context launch_chunk_forward_saved wrote for the same inputs.
+int launch_chunk_backward_saved(const SeqParams& sp, const float* g_out, const float* g_fin, const float* g_score,
+                                float* dq, float* dk, float* dv, float* dalpha, float* derase, float* dwrite,
+                                float* dinitial, const float* ctx, float* ws, cudaStream_t st) {
+    const CtxLayout C = ctx_layout(sp);
+    return chunk_backward_core(sp, g_out, g_fin, g_score, dq, dk, dv, dalpha, derase, dwrite, dinitial, ctx + C.ck,
+                               ctx + C.fwd, ctx + C.edits, ws, st);
 }
 
 }  // namespace dbl

@@ -240,9 +240,10 @@ int launch_seq_scan(const SeqParams& p, int in_dtype, cudaStream_t st) {
 }  // namespace dbl
 
 // --------------------------------------------------------------------------------------------
-// delta_kernels::gdn_training_scan (crates/kernels/src/gdn_training_ops.rs:288-333) forward.
-extern "C" int dbl_gdn_training_scan(const dbl_training_scan_args* a, dbl_stream_t stream) {
-    using namespace dbl;
+namespace dbl {
+
+// Checks the arguments of the training-scan forward and fills the scan parameters.
+int training_scan_params(const dbl_training_scan_args* a, SeqParams* out) {
     if (!a) return fail(DBL_ERR_INVALID_ARGUMENT, "gdn_training_scan: null args");
     if (a->batch <= 0 || a->time <= 0 || a->heads <= 0)
         return fail(DBL_ERR_INVALID_ARGUMENT, "GDN-2 requires nonempty axes");
@@ -291,6 +292,18 @@ extern "C" int dbl_gdn_training_scan(const dbl_training_scan_args* a, dbl_stream
     resolve_strides(z, dv, 4, p.os);
     p.final_state = a->final_state;
     p.scores = a->scores;
+    *out = p;
+    return DBL_OK;
+}
+
+}  // namespace dbl
+
+// delta_kernels::gdn_training_scan (crates/kernels/src/gdn_training_ops.rs:288-333) forward.
+extern "C" int dbl_gdn_training_scan(const dbl_training_scan_args* a, dbl_stream_t stream) {
+    using namespace dbl;
+    SeqParams p{};
+    const int rc = training_scan_params(a, &p);
+    if (rc != DBL_OK) return rc;
     return launch_seq_scan(p, a->dtype, reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -32,6 +32,9 @@ struct SeqParams {
     float* edits;        // optional, chunked form only: every token's edit, [B,T,H,V] f32
 };
 
+// Checks the arguments of the training-scan forward (dbl_gdn_training_scan) and fills `out`.
+int training_scan_params(const dbl_training_scan_args* a, SeqParams* out);
+
 // Validates the shape limits of the sequential kernel and launches it on `st`.
 int launch_seq_scan(const SeqParams& p, int in_dtype, cudaStream_t st);
 
@@ -53,5 +56,15 @@ bool chunk_backward_supported(const SeqParams& sp);
 int launch_chunk_backward(const SeqParams& sp, const float* g_out, const float* g_fin, const float* g_score,
                           float* dq, float* dk, float* dv, float* dalpha, float* derase, float* dwrite,
                           float* dinitial, float* ws, cudaStream_t st);
+
+// The saved forward context of the chunked backward (chunk-start states, chunk maps, every token's
+// edit): its size for the shapes of `sp`, the forward that writes it beside the outputs (`ctx`
+// 16-byte aligned), and the backward that reads it instead of recomputing the forward (`ws` as for
+// launch_chunk_backward).
+size_t chunk_context_floats(const SeqParams& sp);
+int launch_chunk_forward_saved(const SeqParams& sp, int in_dtype, float* ctx, cudaStream_t st);
+int launch_chunk_backward_saved(const SeqParams& sp, const float* g_out, const float* g_fin, const float* g_score,
+                                float* dq, float* dk, float* dv, float* dalpha, float* derase, float* dwrite,
+                                float* dinitial, const float* ctx, float* ws, cudaStream_t st);
 
 }  // namespace dbl

@@ -80,6 +80,19 @@ def gdn_training_scan(q, k, v, alpha, erase, write, valid, reset, initial, chunk
     {0,1}; initial [B,H,K,V].  chunk_size 1..=16 (it bounds the reference's backward
     checkpoints; this forward-only build validates it and otherwise ignores it).
     """
+    return _training_scan(q, k, v, alpha, erase, write, valid, reset, initial, chunk_size, False)[0]
+
+
+def gdn_training_scan_saved(q, k, v, alpha, erase, write, valid, reset, initial, chunk_size: int):
+    """gdn_training_scan that also returns the context its backward reads, as the reference's
+    forward returns checkpoint and auxiliary tensors beside its outputs
+    (gdn_training_ops.rs:201-224).  Returns (GdnTrainingOutput, context): context is a uint8 tensor,
+    empty at shapes where the backward recomputes instead (chunk_size other than 16, wider keys or
+    values, many sequence-heads); pass it to gdn_training_backward_saved with the same inputs."""
+    return _training_scan(q, k, v, alpha, erase, write, valid, reset, initial, chunk_size, True)
+
+
+def _training_scan(q, k, v, alpha, erase, write, valid, reset, initial, chunk_size, save):
     dev = _require_cuda(q, k, v, alpha, erase, write, valid, reset, initial)
     B, T, H, K = q.shape
     V = v.shape[3]
@@ -106,8 +119,15 @@ def gdn_training_scan(q, k, v, alpha, erase, write, valid, reset, initial, chunk
         a = N.TrainingScanArgs(B, T, H, K, V, dt, chunk_size, _ptr(q), _ptr(k), _ptr(v), _ptr(alpha),
                                _ptr(erase), _ptr(write), _ptr(valid), _ptr(reset), _ptr(initial),
                                _ptr(output), _ptr(final), _ptr(scores))
-        N.check(N.lib().dbl_gdn_training_scan(ctypes.byref(a), _stream(dev)))
-    return GdnTrainingOutput(output, final, scores)
+        ctx = None
+        if save:
+            need = N.lib().dbl_gdn_training_scan_context_bytes(B, T, H, K, V, chunk_size)
+            ctx = torch.empty(need, device=dev, dtype=torch.uint8)
+            N.check(N.lib().dbl_gdn_training_scan_save(ctypes.byref(a), _ptr(ctx) if need else None, need,
+                                                       _stream(dev)))
+        else:
+            N.check(N.lib().dbl_gdn_training_scan(ctypes.byref(a), _stream(dev)))
+    return GdnTrainingOutput(output, final, scores), ctx
 
 
 @dataclass
@@ -131,6 +151,24 @@ def gdn_training_backward(q, k, v, alpha, erase, write, valid, reset, initial, g
     + sum grad_scores.scores.  f32 as the reference's backward (K <= 64, V <= 256); the reference's
     packed upstream tensor is passed as its three parts; checkpoints are recomputed (chunk_size
     1..=16 is their spacing) instead of being read from the forward."""
+    return _training_backward(q, k, v, alpha, erase, write, valid, reset, initial, grad_output, grad_final_state,
+                              grad_scores, chunk_size, None)
+
+
+def gdn_training_backward_saved(q, k, v, alpha, erase, write, valid, reset, initial, grad_output, context,
+                                grad_final_state=None, grad_scores=None, chunk_size: int = 16
+                                ) -> GdnTrainingGrads:
+    """gdn_training_backward from the context gdn_training_scan_saved returned for the same inputs
+    (the reference's backward consumes its forward's checkpoint and auxiliary tensors,
+    gdn_training_ops.rs:87-112): the forward is not run again."""
+    if context is None or not context.is_cuda or context.dtype != torch.uint8:
+        raise ValueError("context must be the uint8 CUDA tensor gdn_training_scan_saved returned")
+    return _training_backward(q, k, v, alpha, erase, write, valid, reset, initial, grad_output, grad_final_state,
+                              grad_scores, chunk_size, context)
+
+
+def _training_backward(q, k, v, alpha, erase, write, valid, reset, initial, grad_output, grad_final_state,
+                       grad_scores, chunk_size, context):
     dev = _require_cuda(q, k, v, alpha, erase, write, valid, reset, initial, grad_output)
     B, T, H, K = q.shape
     V = v.shape[3]
@@ -160,7 +198,11 @@ def gdn_training_backward(q, k, v, alpha, erase, write, valid, reset, initial, g
         a = N.TrainingScanBackwardArgs(B, T, H, K, V, chunk_size, *(_ptr(x) for x in f[:9]), _ptr(f[9]),
                                        _ptr(gf), _ptr(gs), _ptr(dq), _ptr(dk), _ptr(dv), _ptr(da), _ptr(de),
                                        _ptr(dw), _ptr(di))
-        N.check(lib.dbl_gdn_training_scan_backward(ctypes.byref(a), _ptr(ws), need, _stream(dev)))
+        if context is None:
+            N.check(lib.dbl_gdn_training_scan_backward(ctypes.byref(a), _ptr(ws), need, _stream(dev)))
+        else:
+            N.check(lib.dbl_gdn_training_scan_backward_saved(ctypes.byref(a), _ptr(context) if context.numel() else None,
+                                                             context.numel(), _ptr(ws), need, _stream(dev)))
     return GdnTrainingGrads(dq, dk, dv, da, de, dw, di)
 
 

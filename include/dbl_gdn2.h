@@ -182,6 +182,24 @@ size_t dbl_gdn_training_scan_backward_workspace_bytes(int64_t batch, int64_t tim
 int dbl_gdn_training_scan_backward(const dbl_training_scan_backward_args *args, void *workspace,
                                    size_t workspace_bytes, dbl_stream_t stream);
 
+/* The forward -> backward hand-off of the reference: its gdn_training_scan returns checkpoint and
+ * auxiliary tensors beside the packed outputs and its gdn_training_backward consumes them
+ * (crates/kernels/src/gdn_training_ops.rs:201-224 and :87-112).  At the shapes of the chunked
+ * backward (chunk_size 16, key width <= 64, value width <= 128, B*H*ceil(K/32)*ceil(V/64) <= 512,
+ * T >= 32) the saved context holds the chunk-start states, the chunk maps and every token's edit,
+ * and the backward skips the forward it would otherwise rerun; elsewhere the context is empty
+ * (0 bytes) and these calls are dbl_gdn_training_scan and dbl_gdn_training_scan_backward.
+ * The context must be 16-byte aligned and hold dbl_gdn_training_scan_context_bytes() bytes; the
+ * backward takes the same inputs as the forward that wrote it and a workspace of
+ * dbl_gdn_training_scan_backward_workspace_bytes() bytes (16-byte aligned). */
+size_t dbl_gdn_training_scan_context_bytes(int64_t batch, int64_t time, int64_t heads, int64_t key_dim,
+                                           int64_t value_dim, int32_t chunk_size);
+int dbl_gdn_training_scan_save(const dbl_training_scan_args *args, void *context, size_t context_bytes,
+                               dbl_stream_t stream);
+int dbl_gdn_training_scan_backward_saved(const dbl_training_scan_backward_args *args, const void *context,
+                                         size_t context_bytes, void *workspace, size_t workspace_bytes,
+                                         dbl_stream_t stream);
+
 /* Backward of dbl_gdn2_scan: replaces Gdn2Ops::gdn2_backward(q, k, v, alpha, erase, write,
  * output_grad, checkpoint, doc_start, doc_end) -> (dq, dk, dv, dalpha, derase, dwrite)
  * (crates/kernels/src/ops.rs:106-160; kernels gdn2.rs:285-519).  Layouts as dbl_gdn2_scan; q, k,

@@ -111,8 +111,8 @@ def test_training_backward_workspace_and_checks(native_lib):
     # (B*H*C), K*V floats each
     assert f(2, 40, 3, 32, 64, 8) == (2 * 3 * 5 + 2 * 3 * 8) * 32 * 64 * 4
     assert f(2, 40, 3, 32, 200, 16) == (2 * 3 * 3 + 2 * 3 * 16) * 32 * 200 * 4
-    # chunked backward (16-token checkpoints, K <= 64, V <= 128, B*H <= 64): at least the chunk-start
-    # states, every token's edit and its gradient, and each chunk end's state gradient
+    # chunked backward (16-token checkpoints, K <= 64, V <= 128, B*H*ceil(K/32)*ceil(V/64) <= 512): the chunk-start
+    # states, every token's edit and its gradient, and each chunk end's state gradient at least
     assert f(2, 40, 3, 32, 64, 16) >= (2 * 3 * 3 * 32 * 64 * 2 + 2 * 40 * 3 * 64 * 2) * 4
     assert f(2, 40, 3, 32, 17, 16) % 16 == 0
     assert f(2, 40, 3, 32, 64, 17) == 0 and f(0, 40, 3, 32, 64, 16) == 0
@@ -124,3 +124,32 @@ def test_training_backward_workspace_and_checks(native_lib):
     assert native_lib.dbl_gdn_training_scan_backward(ctypes.byref(a), 256, 1 << 30, None) == N.DBL_ERR_UNSUPPORTED
     a = N.TrainingScanBackwardArgs(1, 8, 1, 32, 64, 8, **ptrs)
     assert native_lib.dbl_gdn_training_scan_backward(ctypes.byref(a), 256, 16, None) == N.DBL_ERR_WORKSPACE
+
+
+def test_training_context_sizes_and_checks(native_lib):
+    # the saved forward context exists only at the chunked backward's shapes (chunk 16, K <= 64,
+    # V <= 128, B*H*ceil(K/32)*ceil(V/64) <= 512, T >= 32); elsewhere it is empty
+    f = native_lib.dbl_gdn_training_scan_context_bytes
+    n = f(2, 40, 3, 32, 64, 16)
+    assert n > 0 and n % 16 == 0
+    # at least the chunk-start states and every token's edit
+    assert n >= (2 * 3 * 3 * 32 * 64 + 2 * 40 * 3 * 64) * 4
+    assert f(2, 40, 3, 32, 64, 8) == 0 and f(2, 40, 3, 32, 200, 16) == 0 and f(2, 20, 3, 32, 64, 16) == 0
+    assert f(64, 40, 16, 32, 64, 16) == 0 and f(0, 40, 3, 32, 64, 16) == 0
+    # argument checks, before anything is launched
+    ptrs = {nm: 256 for nm, _ in N.TrainingScanArgs._fields_[7:] if nm not in
+            ("initial_state", "final_state", "scores")}
+    a = N.TrainingScanArgs(2, 40, 3, 32, 64, N.DBL_F32, 16, **ptrs)
+    assert native_lib.dbl_gdn_training_scan_save(ctypes.byref(a), None, 0, None) == N.DBL_ERR_WORKSPACE
+    assert native_lib.dbl_gdn_training_scan_save(ctypes.byref(a), 256, n - 1, None) == N.DBL_ERR_WORKSPACE
+    assert native_lib.dbl_gdn_training_scan_save(ctypes.byref(a), 260, n, None) == N.DBL_ERR_INVALID_ARGUMENT
+    bptrs = {nm: 256 for nm, _ in N.TrainingScanBackwardArgs._fields_[6:] if nm not in
+             ("initial_state", "grad_final_state", "grad_scores", "dinitial")}
+    b = N.TrainingScanBackwardArgs(2, 40, 3, 32, 64, 16, **bptrs)
+    ws = native_lib.dbl_gdn_training_scan_backward_workspace_bytes(2, 40, 3, 32, 64, 16)
+    assert native_lib.dbl_gdn_training_scan_backward_saved(ctypes.byref(b), None, 0, 256, ws, None) == \
+        N.DBL_ERR_WORKSPACE
+    assert native_lib.dbl_gdn_training_scan_backward_saved(ctypes.byref(b), 260, n, 256, ws, None) == \
+        N.DBL_ERR_INVALID_ARGUMENT
+    assert native_lib.dbl_gdn_training_scan_backward_saved(ctypes.byref(b), 256, n - 16, 256, ws, None) == \
+        N.DBL_ERR_WORKSPACE

@@ -426,6 +426,46 @@ def test_training_backward_chunked_form(cuda, native_lib, B, T, H, K, V, opt):
         assert np.all(getattr(got, name).cpu().numpy()[~valid] == 0.0), name
 
 
+@pytest.mark.parametrize("B,T,H,K,V,chunk", [(2, 70, 3, 32, 64, 16), (8, 40, 16, 32, 64, 16), (1, 50, 2, 64, 128, 16),
+                                             (2, 37, 2, 32, 64, 8)])
+def test_training_saved_context(cuda, native_lib, B, T, H, K, V, chunk):
+    # the forward -> backward hand-off (the reference's checkpoint and auxiliary tensors): the saved
+    # forward gives the plain forward's outputs, and the backward from its context gives exactly the
+    # recomputing backward's gradients (the same kernels on the same maps), within the f32 bound of
+    # the f64 oracle; 128 sequence-heads (beyond the plain forward's chunked form) and a shape with
+    # no context (chunk 8)
+    rng = np.random.default_rng(K + T + chunk)
+    q, k = rng.standard_normal((B, T, H, K)) / np.sqrt(K), rng.standard_normal((B, T, H, K)) / np.sqrt(K)
+    v, w = rng.standard_normal((B, T, H, V)), rng.random((B, T, H, V))
+    a, e = rng.uniform(0.6, 1.0, (B, T, H, K)), rng.random((B, T, H, K))
+    valid = rng.random((B, T)) > 0.1
+    reset = rng.random((B, T)) > 0.93
+    init = 0.1 * rng.standard_normal((B, H, K, V))
+    go, gf, gs = rng.standard_normal((B, T, H, V)), rng.standard_normal((B, H, K, V)), rng.standard_normal((B, T, H))
+    d = lambda x: torch.as_tensor(np.asarray(x, np.float32), device=cuda)  # noqa: E731
+    args = [d(x) for x in (q, k, v, a, e, w, valid, reset, init)]
+    plain = dbl.gdn_training_scan(*args, chunk)
+    saved, ctx = dbl.gdn_training_scan_saved(*args, chunk)
+    torch.cuda.synchronize()
+    assert (ctx.numel() > 0) == (chunk == 16)
+    f64 = [np.asarray(x, np.float32) for x in (q, k, v, a, e, w)]
+    out, fin, sco = O.scan(*f64, valid, reset, np.asarray(init, np.float32))
+    for got, ref_plain, ref in ((saved.output, plain.output, out), (saved.final_state, plain.final_state, fin),
+                                (saved.scores[..., 0], plain.scores[..., 0], sco)):
+        assert rel_err(host(got), ref) < TOL_F32
+        assert rel_err(host(got), host(ref_plain)) < TOL_F32
+    g0 = dbl.gdn_training_backward(*args, d(go), d(gf), d(gs), chunk_size=chunk)
+    g1 = dbl.gdn_training_backward_saved(*args, d(go), ctx, d(gf), d(gs), chunk_size=chunk)
+    torch.cuda.synchronize()
+    ref = O.training_backward(*f64, *(np.asarray(x, np.float32) for x in (go, gf, gs)), valid, reset,
+                              np.asarray(init, np.float32))
+    names = ("dq", "dk", "dv", "dalpha", "derase", "dwrite", "dinitial")
+    for name, r in zip(names, ref):
+        x0, x1 = getattr(g0, name).cpu().numpy(), getattr(g1, name).cpu().numpy()
+        assert np.array_equal(x0, x1), name
+        assert rel_err(x1, r) < TOL_F32, (name, rel_err(x1, r))
+
+
 # ----------------------------------------------------------------------- mixer prologue
 @pytest.mark.parametrize("B,T,H,K,V,W,dtype", [(2, 37, 3, 32, 64, 4, torch.float32),
                                                 (1, 50, 2, 128, 128, 4, torch.bfloat16),
