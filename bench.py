@@ -521,15 +521,26 @@ def bench_backward(torch, args, dev):
 
     ms_b = timed(lambda: dbl.gdn_training_backward(q, k, v, a, e, w, valid, reset, init, go, gf, gs, chunk_size=16))
     ms_f = timed(lambda: dbl.gdn_training_scan(q, k, v, a, e, w, valid, reset, init, 16))
+    # the reference's pairing: the forward saves its context, the backward reads it (a full step)
+    args_ = (q, k, v, a, e, w, valid, reset, init)
+
+    def step_saved():
+        _, ctx = dbl.gdn_training_scan_saved(*args_, 16)
+        dbl.gdn_training_backward_saved(*args_, go, ctx, gf, gs, chunk_size=16)
+
+    ms_step = timed(step_saved)
     tokens = b * t
     line = {"metric": "GDN-2 training scan backward Mtok/s (gdn_training_backward)",
             "value": tokens / (ms_b / 1e3) / 1e6, "unit": "Mtok/s", "ms_per_step": ms_b, "n_gpus": 1,
             "higher_is_better": True, "dtype": "f32", "data": "synthetic",
             "config": {"workload": f"B{b}/T{t}/H{h}/K{k_}/V{v_} f32 chunk 16 (the reference's training shape)",
-                       "forward_ms": ms_f, "forward_mtok_s": tokens / (ms_f / 1e3) / 1e6},
-            # chunked forms at this shape: the backward launches the chunk-map, main, reverse-map,
-            # reverse and gradient kernels; the forward the chunk-map, main and score kernels
-            "gpu_launches": 10 * 5 + 10 * 3}
+                       "forward_ms": ms_f, "forward_mtok_s": tokens / (ms_f / 1e3) / 1e6,
+                       "training_step_saved_context_ms": ms_step,
+                       "training_step_recomputing_ms": ms_f + ms_b},
+            # chunked forms at this shape: the recomputing backward launches the chunk-map, main,
+            # reverse-map, reverse and gradient kernels; the forward the chunk-map, main and score
+            # kernels; a saved-context step the forward's three and the backward's last three
+            "gpu_launches": 10 * 5 + 10 * 3 + 10 * 6}
     if not args.no_cpu_baseline:
         # the f64 C restatement of the reference's backward on one (b) row of the workload
         sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
