@@ -108,7 +108,16 @@ __global__ void __launch_bounds__(CTH) chunk_bwd_pre_kernel(const CBwdParams p) 
     float* rb = p.rev + ((size_t)bh * nch + c) * R.total;
     const int KP = F.kp;
 
-    if (tid < CC) sact[tid] = tid < n && p.valid[(size_t)b * p.T + t0 + tid] != 0.f;
+    // every global load of the kernel is issued before the first barrier: the token flags, score
+    // gradients and |k_t|, the maps (M, Q', B' transposed), dO and the edits; the Wd and G^T rows of
+    // the reverse block are plain copies
+    __shared__ float sgs[CC], skn[CC];
+    if (tid < CC) {
+        const bool act = tid < n && p.valid[(size_t)b * p.T + t0 + tid] != 0.f;
+        sact[tid] = act;
+        sgs[tid] = (p.g_score && act) ? p.g_score[tok(p, b, t0 + tid, h)] : 0.f;
+        skn[tid] = fb[F.kn + tid];
+    }
     for (int x = tid; x < CC * CC; x += CTH) {
         const int t = x / CC, s = x - t * CC;
         sMT[s][t] = fb[F.mm + x];
@@ -118,12 +127,18 @@ __global__ void __launch_bounds__(CTH) chunk_bwd_pre_kernel(const CBwdParams p) 
         sQpT[i][t] = i < K ? fb[F.qp + t * KP + i] : 0.f;
         sBpT[i][t] = i < K ? fb[F.bp + t * KP + i] : 0.f;
     }
-    __syncthreads();
     for (int x = tid; x < CC * CVMAX; x += CTH) {
         const int t = x / CVMAX, j = x - t * CVMAX;
         const bool in = t < n && j < V;
-        sdO[t][j] = (in && sact[t]) ? p.g_out[tok(p, b, t0 + t, h) * V + j] : 0.f;
+        const bool act = in && p.valid[(size_t)b * p.T + t0 + t] != 0.f;
+        sdO[t][j] = act ? p.g_out[tok(p, b, t0 + t, h) * V + j] : 0.f;
         sE[t][j] = in ? p.edits[tok(p, b, t0 + t, h) * V + j] : 0.f;
+    }
+    for (int x = tid; x < CC * KP / 4; x += CTH)
+        reinterpret_cast<float4*>(rb + R.wd)[x] = reinterpret_cast<const float4*>(fb + F.wd)[x];
+    for (int x = tid; x < K * KP; x += CTH) {
+        const int i = x / KP, i2 = x - i * KP;
+        rb[R.gt + x] = i2 < K ? fb[F.g + i2 * KP + i] : 0.f;
     }
     __syncthreads();
     for (int t = warp; t < CC; t += CTH / 32) {
@@ -131,10 +146,9 @@ __global__ void __launch_bounds__(CTH) chunk_bwd_pre_kernel(const CBwdParams p) 
         for (int j = lane; j < V; j += 32) e2 = fmaf(sE[t][j], sE[t][j], e2);
         e2 = warp_sum(e2);
         if (lane == 0) {
-            const float en = sqrtf(e2), kn = fb[F.kn + t];
-            const float gs = (p.g_score && sact[t]) ? p.g_score[tok(p, b, t0 + t, h)] : 0.f;
+            const float en = sqrtf(e2), kn = skn[t];
             sen[t] = en;
-            sgE[t] = (sact[t] && en > 0.f && kn > 0.f) ? gs * kn / en : 0.f;
+            sgE[t] = (sact[t] && en > 0.f && kn > 0.f) ? sgs[t] * kn / en : 0.f;
         }
     }
     __syncthreads();
@@ -168,13 +182,7 @@ __global__ void __launch_bounds__(CTH) chunk_bwd_pre_kernel(const CBwdParams p) 
             for (int cc = 0; cc < 4; ++cc)
                 if (r0 + r < K && n0 + cc < V) rb[R.hb + (r0 + r) * V + n0 + cc] = a1[r][cc] - a2[r][cc];
     }
-    // Wd rows (already zero beyond K), G^T rows (zero beyond K), |E_t|
-    for (int x = tid; x < CC * KP / 4; x += CTH)
-        reinterpret_cast<float4*>(rb + R.wd)[x] = reinterpret_cast<const float4*>(fb + F.wd)[x];
-    for (int x = tid; x < K * KP; x += CTH) {
-        const int i = x / KP, i2 = x - i * KP;
-        rb[R.gt + x] = i2 < K ? fb[F.g + i2 * KP + i] : 0.f;
-    }
+    // |E_t|
     if (tid < CC) rb[R.en + tid] = sen[tid];
     (void)K4;
 }
