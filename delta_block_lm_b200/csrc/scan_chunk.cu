@@ -386,6 +386,9 @@ __global__ void __launch_bounds__(NTH) chunk_main_kernel(const SeqParams p, cons
         }
     };
     for (int c = 0; c < NB - 1; ++c) prefetch(c, c);
+    // this thread's output and edit offsets at token 0
+    const size_t out_base = (size_t)b * p.os[0] + (size_t)h * p.os[2] + (size_t)(c0 + j) * p.os[3];
+    const size_t edit_base = ((size_t)b * p.T * p.H + h) * V + c0 + j;
     float kn_prev = 0.f;
     int cur = 0;  // buffer of chunk c; chunk c + NB - 1 goes to the buffer before it
     for (int c = 0; c < nch; ++c) {
@@ -420,8 +423,11 @@ __global__ void __launch_bounds__(NTH) chunk_main_kernel(const SeqParams p, cons
         }
 #pragma unroll
         for (int m = 0; m < NS; ++m) acc[m] = (half == 0 && rr + m * RP < K) ? hh[(rr + m * RP) * VG + j] : 0.f;
-#pragma unroll 2
-        for (int i = 4 * half; i < K4; i += 4 * HALVES) {
+        // unrolled over the compile-time key bound (K4 <= KMAX) so that the loads issue early
+#pragma unroll
+        for (int i0 = 0; i0 < KMAX; i0 += 4 * HALVES) {
+            const int i = i0 + 4 * half;
+            if (i >= K4) break;
             const float s0 = S[(i + 0) * SST + j], s1 = S[(i + 1) * SST + j];
             const float s2 = S[(i + 2) * SST + j], s3 = S[(i + 3) * SST + j];
 #pragma unroll
@@ -457,10 +463,9 @@ __global__ void __launch_bounds__(NTH) chunk_main_kernel(const SeqParams p, cons
         for (int m = 0; m < NT; ++m) {
             const int t = rr + m * RP;
             if (half == 0 && t < n && j < vg) {
-                if (p.edits) p.edits[(((size_t)b * p.T + t0 + t) * p.H + h) * V + c0 + j] = u[m];
+                if (p.edits) p.edits[edit_base + (size_t)(t0 + t) * p.H * V] = u[m];
                 if (p.out) {
-                    const size_t oi = (size_t)b * p.os[0] + (size_t)(t0 + t) * p.os[1] + (size_t)h * p.os[2] +
-                                      (size_t)(c0 + j) * p.os[3];
+                    const size_t oi = out_base + (size_t)(t0 + t) * p.os[1];
                     if (p.out_dtype == DBL_BF16) static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(o[m]);
                     else static_cast<float*>(p.out)[oi] = o[m];
                 }
