@@ -268,8 +268,10 @@ __global__ void __launch_bounds__(CTH) chunk_bwd_rev_kernel(const CBwdParams p, 
         for (int m = 0; m < NT; ++m) o[m] = dep[(rr + m * RP) * VG + j];
 #pragma unroll
         for (int m = 0; m < NS; ++m) acc[m] = (rr + m * RP < K) ? hb[(rr + m * RP) * VG + j] : 0.f;
-#pragma unroll 2
-        for (int i = 0; i < K4; i += 4) {
+        // unrolled over the compile-time key bound (K4 <= KMAX) so that the loads issue early
+#pragma unroll
+        for (int i = 0; i < KMAX; i += 4) {
+            if (i >= K4) break;
             const float s0 = S[(i + 0) * VG + j], s1 = S[(i + 1) * VG + j];
             const float s2 = S[(i + 2) * VG + j], s3 = S[(i + 3) * VG + j];
 #pragma unroll
