@@ -413,11 +413,12 @@ __global__ void __launch_bounds__(GTH, 2) chunk_bwd_grad_kernel(const CBwdParams
         const int t = x / SR, s = x - t * SR;
         sTiT[x] = s < CC ? fb[F.ti + s * CC + t] : 0.f;
     }
-    __syncthreads();
+    // no barrier yet: the token flags are read again where needed, so every load is in flight at once
     for (int x = tid; x < CC * KMAX; x += GTH) {
         const int u = x / KMAX, i = x - u * KMAX;
         const int t = t0 + u;
-        const bool act = sact[u], rst = srst[u];
+        const bool act = u < n && p.valid[(size_t)b * p.T + t] != 0.f;
+        const bool rst = u < n && p.reset[(size_t)b * p.T + t] != 0.f;
         float kv = 0.f, qv = 0.f, f = 1.f, e = 0.f, pv = 0.f;
         if (u < n && i < K) {
             const size_t gi = tok(p, b, t, h) * K + i;
@@ -443,7 +444,7 @@ __global__ void __launch_bounds__(GTH, 2) chunk_bwd_grad_kernel(const CBwdParams
         sE[x] = ev;
         if (j < V4) sET[j * SR + t] = ev;
         sdE[x] = in ? p.dE[(((size_t)bh * nch + c) * CC + t) * V + j] : 0.f;
-        sdO[x] = (in && sact[t]) ? p.g_out[tok(p, b, t0 + t, h) * V + j] : 0.f;
+        sdO[x] = (in && p.valid[(size_t)b * p.T + t0 + t] != 0.f) ? p.g_out[tok(p, b, t0 + t, h) * V + j] : 0.f;
     }
     // transposed: consecutive threads read consecutive j of one state row
     for (int x = tid; x < KT * V4; x += GTH) {
