@@ -251,21 +251,33 @@ __global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, floa
                 else if (kind == 1) tile_mm(acc, &sM[0][0], CC, r0, &sU0[0][0], CVMAX, n0);
                 else if (kind == 2) tile_mm(acc, &sWdT[0][0], WS, r0, &sPB[0][0], KMAX, n0);
                 else tile_mm(acc, &sWdT[0][0], WS, r0, &sU0[0][0], CVMAX, n0);
+                // rows of Qe and G (stride KP) are 16-byte aligned, rows of O0 and H (stride V) when
+                // V is a multiple of 4: one float4 store per tile row there
+                const bool v4 = (V & 3) == 0;
 #pragma unroll
                 for (int r = 0; r < 2; ++r) {
                     const int row = r0 + r;
-#pragma unroll
-                    for (int cc = 0; cc < 4; ++cc) {
-                        const int col = n0 + cc;
-                        if (kind == 0) {
-                            if (col < K4) blk[L.qe + row * KP + col] = sq[row][col] - acc[r][cc];
-                        } else if (kind == 1) {
-                            if (col < V) blk[L.o0 + row * V + col] = acc[r][cc];
-                        } else if (kind == 2) {
-                            if (row < K && col < K4)
-                                blk[L.g + row * KP + col] = (row == col ? sPl[row] : 0.f) - acc[r][cc];
+                    float4 w;
+                    if (kind == 0) {
+                        w = make_float4(sq[row][n0] - acc[r][0], sq[row][n0 + 1] - acc[r][1],
+                                        sq[row][n0 + 2] - acc[r][2], sq[row][n0 + 3] - acc[r][3]);
+                        *reinterpret_cast<float4*>(blk + L.qe + row * KP + n0) = w;
+                    } else if (kind == 2) {
+                        if (row < K) {
+                            w = make_float4((row == n0 ? sPl[row] : 0.f) - acc[r][0],
+                                            (row == n0 + 1 ? sPl[row] : 0.f) - acc[r][1],
+                                            (row == n0 + 2 ? sPl[row] : 0.f) - acc[r][2],
+                                            (row == n0 + 3 ? sPl[row] : 0.f) - acc[r][3]);
+                            *reinterpret_cast<float4*>(blk + L.g + row * KP + n0) = w;
+                        }
+                    } else if (kind == 1 || row < K) {
+                        float* dst = blk + (kind == 1 ? L.o0 : L.hh) + row * V;
+                        if (v4) {
+                            *reinterpret_cast<float4*>(dst + n0) = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
                         } else {
-                            if (row < K && col < V) blk[L.hh + row * V + col] = acc[r][cc];
+#pragma unroll
+                            for (int cc = 0; cc < 4; ++cc)
+                                if (n0 + cc < V) dst[n0 + cc] = acc[r][cc];
                         }
                     }
                 }
@@ -277,9 +289,13 @@ __global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, floa
                 } else {
                     y -= tbp;
                     const int t = y / nv, n0 = 4 * (y - t * nv);
+                    if ((V & 3) == 0) {
+                        *reinterpret_cast<float4*>(blk + L.u0 + t * V + n0) = lds4(&sU0[t][n0]);
+                    } else {
 #pragma unroll
-                    for (int cc = 0; cc < 4; ++cc)
-                        if (n0 + cc < V) blk[L.u0 + t * V + n0 + cc] = sU0[t][n0 + cc];
+                        for (int cc = 0; cc < 4; ++cc)
+                            if (n0 + cc < V) blk[L.u0 + t * V + n0 + cc] = sU0[t][n0 + cc];
+                    }
                 }
             } else {
                 // zero columns K4 .. KP of a row of Qe, B' or G
