@@ -160,11 +160,19 @@ __global__ void __launch_bounds__(CTH) chunk_bwd_pre_kernel(const CBwdParams p) 
         tile_mm(acc, &sMT[0][0], SR, r0, &sdO[0][0], CVMAX, n0);
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
+            float d[4];
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) {
-                const float d = fmaf(sgE[r0 + r], sE[r0 + r][n0 + cc], acc[r][cc]);
-                sdep[r0 + r][n0 + cc] = d;
-                if (n0 + cc < V) rb[R.dep + (r0 + r) * V + n0 + cc] = d;
+                d[cc] = fmaf(sgE[r0 + r], sE[r0 + r][n0 + cc], acc[r][cc]);
+                sdep[r0 + r][n0 + cc] = d[cc];
+            }
+            float* dst = rb + R.dep + (r0 + r) * V + n0;
+            if ((V & 3) == 0) {
+                *reinterpret_cast<float4*>(dst) = make_float4(d[0], d[1], d[2], d[3]);
+            } else {
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc)
+                    if (n0 + cc < V) dst[cc] = d[cc];
             }
         }
     }
@@ -177,10 +185,18 @@ __global__ void __launch_bounds__(CTH) chunk_bwd_pre_kernel(const CBwdParams p) 
         tile_mm(a1, &sQpT[0][0], SR, r0, &sdO[0][0], CVMAX, n0);
         tile_mm(a2, &sBpT[0][0], SR, r0, &sdep[0][0], CVMAX, n0);
 #pragma unroll
-        for (int r = 0; r < 2; ++r)
+        for (int r = 0; r < 2; ++r) {
+            if (r0 + r >= K) continue;
+            float* dst = rb + R.hb + (r0 + r) * V + n0;
+            if ((V & 3) == 0) {
+                *reinterpret_cast<float4*>(dst) = make_float4(a1[r][0] - a2[r][0], a1[r][1] - a2[r][1],
+                                                              a1[r][2] - a2[r][2], a1[r][3] - a2[r][3]);
+            } else {
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc)
-                if (r0 + r < K && n0 + cc < V) rb[R.hb + (r0 + r) * V + n0 + cc] = a1[r][cc] - a2[r][cc];
+                for (int cc = 0; cc < 4; ++cc)
+                    if (n0 + cc < V) dst[cc] = a1[r][cc] - a2[r][cc];
+            }
+        }
     }
     // |E_t|
     if (tid < CC) rb[R.en + tid] = sen[tid];
