@@ -330,7 +330,7 @@ __global__ void __launch_bounds__(CTH) chunk_bwd_rev_kernel(const CBwdParams p, 
 // consecutive float4s of the B operand.
 struct GradSmem {
     int cv, kt, k, q, ek, f, er, P, tit, E, dE, dO, dWV, S0T, dST, ET, dQp, dB, dWd, dP, dM, dA, dPl, en, kn, gs,
-        act, rst, total;
+        act, rst, C, total;
 };
 __host__ __device__ inline GradSmem grad_smem(int kmax, int V) {
     GradSmem L{};
@@ -365,6 +365,13 @@ __host__ __device__ inline GradSmem grad_smem(int kmax, int V) {
     L.gs = o; o += CC;
     L.act = o; o += CC;
     L.rst = o; o += CC;
+    // phase 4's terms C [CC][CC][kmax] reuse E .. dS_end when those are large enough
+    if (L.ET - L.E >= CC * CC * kmax) {
+        L.C = L.E;
+    } else {
+        o = (o + 3) & ~3;
+        L.C = o; o += CC * CC * kmax;
+    }
     L.total = o;
     return L;
 }
@@ -578,23 +585,40 @@ __global__ void __launch_bounds__(GTH, 2) chunk_bwd_grad_kernel(const CBwdParams
         }
     }
     __syncthreads();
-    // phase 4, per (token u, key channel i): d alpha
+    // phase 4: d alpha.  Y[t][u] = dP_t P_{u-1} + sum_{s<u} DD[t][s] d[u-1][s] obeys
+    // Y[t][u + 1] = f_u Y[t][u] + DD[t][u] (Y[t][0] = dP_t), so the thread of (token t, channel i)
+    // walks u upwards for Y and back down for the terms d[t][u] Y[t][u], which it leaves in
+    // C[t][u][i] (in the shared memory of E .. dS_end, no longer read, where it fits); then
+    // df_u = sum_{t>=u} C[t][u].
+    float* sC = smem_g + L.C;  // [CC][CC][KMAX]
+    for (int x = tid; x < CC * K; x += GTH) {
+        const int t = x / K, i = x - t * K;
+        const float ekt = sek[t][i], qt = sq[t][i];
+        const float wl = t == CC - 1 ? 1.f : 0.f;
+        float y[CC];
+        y[0] = sdP[t][i];
+#pragma unroll
+        for (int u = 1; u < CC; ++u) {
+            if (u <= t) {
+                const int s0 = u - 1;
+                const float dd = fmaf(sdA[t][s0], ekt, fmaf(sdM[t][s0], qt, wl * sdWd[s0][i])) * sk[s0][i];
+                y[u] = fmaf(sf[s0][i], y[u - 1], dd);
+            }
+        }
+        float dtu = 1.f;  // d[t][u]
+#pragma unroll
+        for (int u = CC - 1; u >= 0; --u) {
+            if (u <= t) {
+                sC[(t * CC + u) * KMAX + i] = dtu * y[u];
+                dtu *= sf[u][i];
+            }
+        }
+    }
+    __syncthreads();
     for (int x = tid; x < n * K; x += GTH) {
         const int u = x / K, i = x - u * K;
-        const float pm1 = u > 0 ? sP[u - 1][i] : 1.f;
-        float df = 0.f, dtu = 1.f;  // d[t][u]
-        for (int t = u; t < CC; ++t) {
-            if (t > u) dtu *= sf[t][i];
-            const float wl = t == CC - 1 ? 1.f : 0.f;
-            float y = sdP[t][i] * pm1, z = 1.f;  // z = d[u-1][s]
-            for (int s = u - 1; s >= 0; --s) {
-                const float dd =
-                    fmaf(sdA[t][s], sek[t][i], fmaf(sdM[t][s], sq[t][i], wl * sdWd[s][i])) * sk[s][i];
-                y = fmaf(dd, z, y);
-                z *= sf[s][i];
-            }
-            df = fmaf(dtu, y, df);
-        }
+        float df = 0.f;
+        for (int t = u; t < CC; ++t) df += sC[(t * CC + u) * KMAX + i];
         p.dalpha[tok(p, b, t0 + u, h) * K + i] = (sact[u] && !srst[u]) ? df : 0.f;
     }
 }
