@@ -71,8 +71,42 @@ __global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, floa
     }
     __syncthreads();
     // inputs: k, q (scaled; zero for padding, whose outputs are zero), step factors f, erase k (zero
-    // for padding), write v (zero for padding)
-    for (int x = tid; x < CC * KMAX; x += CTH) {
+    // for padding), write v (zero for padding).  f32 rows with unit channel stride, 16-byte aligned
+    // (the training entry's contiguous tensors at K, V multiples of 4) are read four at a time.
+    auto al16 = [](const void* ptr, int64_t s0, int64_t s1, int64_t s2) {
+        return ((reinterpret_cast<uintptr_t>(ptr) & 15) | (s0 & 3) | (s1 & 3) | (s2 & 3)) == 0;
+    };
+    const bool vec_k = sizeof(T) == 4 && !scalar && (K & 3) == 0 && p.ks[3] == 1 && p.qs[3] == 1 && p.as[3] == 1 &&
+                       p.es[3] == 1 && al16(p.k, p.ks[0], p.ks[1], p.ks[2]) && al16(p.q, p.qs[0], p.qs[1], p.qs[2]) &&
+                       al16(p.alpha, p.as[0], p.as[1], p.as[2]) && al16(p.erase, p.es[0], p.es[1], p.es[2]);
+    const bool vec_v = sizeof(T) == 4 && !scalar && !p.v_zero && (V & 3) == 0 && p.vs[3] == 1 && p.ws[3] == 1 &&
+                       al16(p.v, p.vs[0], p.vs[1], p.vs[2]) && al16(p.write, p.ws[0], p.ws[1], p.ws[2]);
+    if (vec_k) {
+        for (int x = tid; x < CC * (KMAX / 4); x += CTH) {
+            const int u = x / (KMAX / 4), i = 4 * (x - u * (KMAX / 4));
+            const int t = t0 + u;
+            const bool act = sact[u] & 1, rst = sact[u] & 2;
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), qv = kv, f = make_float4(1.f, 1.f, 1.f, 1.f), ek = kv;
+            if (u < n && i < K) {
+                kv = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(kb) + t * p.ks[1] + i);
+                if (act) {
+                    const float4 q4 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(qb) + t * p.qs[1] + i);
+                    const float4 a4 = *reinterpret_cast<const float4*>(
+                        p.alpha + (size_t)b * p.as[0] + (size_t)t * p.as[1] + (size_t)h * p.as[2] + i);
+                    const float4 e4 = *reinterpret_cast<const float4*>(
+                        p.erase + (size_t)b * p.es[0] + (size_t)t * p.es[1] + (size_t)h * p.es[2] + i);
+                    qv = make_float4(q4.x * p.scale, q4.y * p.scale, q4.z * p.scale, q4.w * p.scale);
+                    f = rst ? make_float4(0.f, 0.f, 0.f, 0.f) : a4;
+                    ek = make_float4(e4.x * kv.x, e4.y * kv.y, e4.z * kv.z, e4.w * kv.w);
+                }
+            }
+            *reinterpret_cast<float4*>(&sk[u][i]) = kv;
+            *reinterpret_cast<float4*>(&sq[u][i]) = qv;
+            *reinterpret_cast<float4*>(&sf[u][i]) = f;
+            *reinterpret_cast<float4*>(&sek[u][i]) = ek;
+        }
+    }
+    for (int x = tid; x < (vec_k ? 0 : CC * KMAX); x += CTH) {
         const int u = x / KMAX, i = x - u * KMAX;
         const int t = t0 + u;
         const bool act = sact[u] & 1, rst = sact[u] & 2;
@@ -98,7 +132,21 @@ __global__ void __launch_bounds__(CTH) chunk_prep_kernel(const SeqParams p, floa
         sf[u][i] = f;
         sek[u][i] = ek;
     }
-    for (int x = tid; x < CC * CVMAX; x += CTH) {
+    if (vec_v) {
+        for (int x = tid; x < CC * (CVMAX / 4); x += CTH) {
+            const int u = x / (CVMAX / 4), j = 4 * (x - u * (CVMAX / 4));
+            const int t = t0 + u;
+            float4 wv = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (j < V && u < n && (sact[u] & 1)) {
+                const float4 v4 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(vb) + t * p.vs[1] + j);
+                const float4 w4 = *reinterpret_cast<const float4*>(
+                    p.write + (size_t)b * p.ws[0] + (size_t)t * p.ws[1] + (size_t)h * p.ws[2] + j);
+                wv = make_float4(w4.x * v4.x, w4.y * v4.y, w4.z * v4.z, w4.w * v4.w);
+            }
+            *reinterpret_cast<float4*>(&swv[u][j]) = wv;
+        }
+    }
+    for (int x = tid; x < (vec_v ? 0 : CC * CVMAX); x += CTH) {
         const int u = x / CVMAX, j = x - u * CVMAX;
         const int t = t0 + u;
         float wv = 0.f;
