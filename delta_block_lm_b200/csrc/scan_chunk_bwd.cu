@@ -436,8 +436,38 @@ __global__ void __launch_bounds__(GTH, 2) chunk_bwd_grad_kernel(const CBwdParams
         const int t = x / SR, s = x - t * SR;
         sTiT[x] = s < CC ? fb[F.ti + s * CC + t] : 0.f;
     }
-    // no barrier yet: the token flags are read again where needed, so every load is in flight at once
-    for (int x = tid; x < CC * KMAX; x += GTH) {
+    // no barrier yet: the token flags are read again where needed, so every load is in flight at once.
+    // Rows are read four floats at a time where widths and pointers allow (K, V multiples of 4).
+    auto a16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+    const bool vk = (K & 3) == 0 && a16(p.k) && a16(p.q) && a16(p.erase) && a16(p.alpha);
+    const bool vv = (V & 3) == 0 && a16(p.g_out);
+    if (vk) {
+        for (int x = tid; x < CC * (KMAX / 4); x += GTH) {
+            const int u = x / (KMAX / 4), i = 4 * (x - u * (KMAX / 4));
+            const int t = t0 + u;
+            const bool act = u < n && p.valid[(size_t)b * p.T + t] != 0.f;
+            const bool rst = u < n && p.reset[(size_t)b * p.T + t] != 0.f;
+            const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 kv = z4, qv = z4, f = make_float4(1.f, 1.f, 1.f, 1.f), e = z4, pv = z4;
+            if (u < n && i < K) {
+                const size_t gi = tok(p, b, t, h) * K + i;
+                kv = *reinterpret_cast<const float4*>(p.k + gi);
+                if (act) {
+                    qv = *reinterpret_cast<const float4*>(p.q + gi);
+                    e = *reinterpret_cast<const float4*>(p.erase + gi);
+                    f = rst ? z4 : *reinterpret_cast<const float4*>(p.alpha + gi);
+                }
+            }
+            if (i < K) pv = *reinterpret_cast<const float4*>(fb + F.pp + u * KP + i);
+            *reinterpret_cast<float4*>(&sk[u][i]) = kv;
+            *reinterpret_cast<float4*>(&sq[u][i]) = qv;
+            *reinterpret_cast<float4*>(&sf[u][i]) = f;
+            *reinterpret_cast<float4*>(&ser[u][i]) = e;
+            *reinterpret_cast<float4*>(&sek[u][i]) = make_float4(e.x * kv.x, e.y * kv.y, e.z * kv.z, e.w * kv.w);
+            *reinterpret_cast<float4*>(&sP[u][i]) = pv;
+        }
+    }
+    for (int x = tid; x < (vk ? 0 : CC * KMAX); x += GTH) {
         const int u = x / KMAX, i = x - u * KMAX;
         const int t = t0 + u;
         const bool act = u < n && p.valid[(size_t)b * p.T + t] != 0.f;
@@ -460,7 +490,49 @@ __global__ void __launch_bounds__(GTH, 2) chunk_bwd_grad_kernel(const CBwdParams
         sek[u][i] = e * kv;
         sP[u][i] = pv;
     }
-    for (int x = tid; x < CC * CV; x += GTH) {
+    if (vv) {
+        for (int x = tid; x < CC * (CV / 4); x += GTH) {
+            const int t = x / (CV / 4), j = 4 * (x - t * (CV / 4));
+            const bool in = t < n && j < V;
+            const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 ev = z4, de = z4, dov = z4;
+            if (in) {
+                ev = *reinterpret_cast<const float4*>(p.edits + tok(p, b, t0 + t, h) * V + j);
+                de = *reinterpret_cast<const float4*>(p.dE + (((size_t)bh * nch + c) * CC + t) * V + j);
+                if (p.valid[(size_t)b * p.T + t0 + t] != 0.f)
+                    dov = *reinterpret_cast<const float4*>(p.g_out + tok(p, b, t0 + t, h) * V + j);
+            }
+            *reinterpret_cast<float4*>(sE + t * CV + j) = ev;
+            *reinterpret_cast<float4*>(sdE + t * CV + j) = de;
+            *reinterpret_cast<float4*>(sdO + t * CV + j) = dov;
+            if (j < V4) {
+                sET[(j + 0) * SR + t] = ev.x;
+                sET[(j + 1) * SR + t] = ev.y;
+                sET[(j + 2) * SR + t] = ev.z;
+                sET[(j + 3) * SR + t] = ev.w;
+            }
+        }
+        // transposed: consecutive threads read consecutive columns of one state row
+        for (int x = tid; x < KT * (V4 / 4); x += GTH) {
+            const int i = x / (V4 / 4), j = 4 * (x - i * (V4 / 4));
+            const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 a = z4, g = z4;
+            if (i < K) {
+                const size_t gi = ((size_t)bh * nch + c) * K * V + (size_t)i * V + j;
+                a = *reinterpret_cast<const float4*>(p.ck + gi);
+                g = *reinterpret_cast<const float4*>(p.dSe + gi);
+            }
+            sS0T[(j + 0) * KT + i] = a.x;
+            sS0T[(j + 1) * KT + i] = a.y;
+            sS0T[(j + 2) * KT + i] = a.z;
+            sS0T[(j + 3) * KT + i] = a.w;
+            sdST[(j + 0) * KT + i] = g.x;
+            sdST[(j + 1) * KT + i] = g.y;
+            sdST[(j + 2) * KT + i] = g.z;
+            sdST[(j + 3) * KT + i] = g.w;
+        }
+    }
+    for (int x = tid; x < (vv ? 0 : CC * CV); x += GTH) {
         const int t = x / CV, j = x - t * CV;
         const bool in = t < n && j < V;
         const float ev = in ? p.edits[tok(p, b, t0 + t, h) * V + j] : 0.f;
@@ -470,7 +542,7 @@ __global__ void __launch_bounds__(GTH, 2) chunk_bwd_grad_kernel(const CBwdParams
         sdO[x] = (in && p.valid[(size_t)b * p.T + t0 + t] != 0.f) ? p.g_out[tok(p, b, t0 + t, h) * V + j] : 0.f;
     }
     // transposed: consecutive threads read consecutive j of one state row
-    for (int x = tid; x < KT * V4; x += GTH) {
+    for (int x = tid; x < (vv ? 0 : KT * V4); x += GTH) {
         const int i = x / V4, j = x - i * V4;
         const bool in = i < K && j < V;
         sS0T[j * KT + i] = in ? p.ck[((size_t)bh * nch + c) * K * V + (size_t)i * V + j] : 0.f;
