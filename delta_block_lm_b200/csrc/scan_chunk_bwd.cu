@@ -122,17 +122,43 @@ __global__ void __launch_bounds__(CTH) chunk_bwd_pre_kernel(const CBwdParams p) 
         const int t = x / CC, s = x - t * CC;
         sMT[s][t] = fb[F.mm + x];
     }
-    for (int x = tid; x < CC * KMAX; x += CTH) {
-        const int t = x / KMAX, i = x - t * KMAX;
-        sQpT[i][t] = i < K ? fb[F.qp + t * KP + i] : 0.f;
-        sBpT[i][t] = i < K ? fb[F.bp + t * KP + i] : 0.f;
+    // Q' and B' rows (KP floats, zero beyond K, 16-byte aligned) four floats at a time, stored transposed
+    for (int x = tid; x < CC * (KMAX / 4); x += CTH) {
+        const int t = x / (KMAX / 4), i = 4 * (x - t * (KMAX / 4));
+        const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 qv = i < KP ? *reinterpret_cast<const float4*>(fb + F.qp + t * KP + i) : z4;
+        const float4 bv = i < KP ? *reinterpret_cast<const float4*>(fb + F.bp + t * KP + i) : z4;
+        sQpT[i][t] = qv.x;
+        sQpT[i + 1][t] = qv.y;
+        sQpT[i + 2][t] = qv.z;
+        sQpT[i + 3][t] = qv.w;
+        sBpT[i][t] = bv.x;
+        sBpT[i + 1][t] = bv.y;
+        sBpT[i + 2][t] = bv.z;
+        sBpT[i + 3][t] = bv.w;
     }
-    for (int x = tid; x < CC * CVMAX; x += CTH) {
-        const int t = x / CVMAX, j = x - t * CVMAX;
-        const bool in = t < n && j < V;
-        const bool act = in && p.valid[(size_t)b * p.T + t0 + t] != 0.f;
-        sdO[t][j] = act ? p.g_out[tok(p, b, t0 + t, h) * V + j] : 0.f;
-        sE[t][j] = in ? p.edits[tok(p, b, t0 + t, h) * V + j] : 0.f;
+    if ((V & 3) == 0 && (reinterpret_cast<uintptr_t>(p.g_out) & 15) == 0) {
+        for (int x = tid; x < CC * (CVMAX / 4); x += CTH) {
+            const int t = x / (CVMAX / 4), j = 4 * (x - t * (CVMAX / 4));
+            const bool in = t < n && j < V;
+            const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 dov = z4, ev = z4;
+            if (in) {
+                ev = *reinterpret_cast<const float4*>(p.edits + tok(p, b, t0 + t, h) * V + j);
+                if (p.valid[(size_t)b * p.T + t0 + t] != 0.f)
+                    dov = *reinterpret_cast<const float4*>(p.g_out + tok(p, b, t0 + t, h) * V + j);
+            }
+            *reinterpret_cast<float4*>(&sdO[t][j]) = dov;
+            *reinterpret_cast<float4*>(&sE[t][j]) = ev;
+        }
+    } else {
+        for (int x = tid; x < CC * CVMAX; x += CTH) {
+            const int t = x / CVMAX, j = x - t * CVMAX;
+            const bool in = t < n && j < V;
+            const bool act = in && p.valid[(size_t)b * p.T + t0 + t] != 0.f;
+            sdO[t][j] = act ? p.g_out[tok(p, b, t0 + t, h) * V + j] : 0.f;
+            sE[t][j] = in ? p.edits[tok(p, b, t0 + t, h) * V + j] : 0.f;
+        }
     }
     for (int x = tid; x < CC * KP / 4; x += CTH)
         reinterpret_cast<float4*>(rb + R.wd)[x] = reinterpret_cast<const float4*>(fb + F.wd)[x];
