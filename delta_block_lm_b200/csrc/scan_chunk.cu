@@ -569,12 +569,14 @@ __global__ void chunk_scores_kernel(const SeqParams p, const float* ws, const fl
 }  // namespace
 
 // Whether the chunked path takes these shapes: key width <= 64, value width <= 128, a zero or given
-// initial state (not the identity of span transitions), at least two chunks, and at most 64
-// sequences x heads.  Beyond that the token-sequential kernel has enough (b, h) rows to fill the GPU
-// and does less work per token (measured at T512/K32/V64: 32 rows 0.31 vs 0.10 ms chunked, 128 rows
-// 0.42 vs 0.53 ms, 512 rows 0.69 vs 1.06 ms).
+// initial state (not the identity of span transitions), at least two chunks, and
+// B*H*ceil(K/32)*ceil(V/64) <= 384.  Beyond that the token-sequential kernel has enough (b, h) rows
+// to fill the GPU and does less work per token (measured at T512: K32/V64 96 rows 0.31 ms sequential
+// vs 0.20 ms chunked, 128 rows 0.34 vs 0.22, 256 rows 0.42 vs 0.43; K64/V128 96 rows 0.60 vs 0.53;
+// 512 rows 0.69 ms sequential).
 bool chunk_scan_supported(const SeqParams& p) {
-    return p.K <= 64 && p.V <= CVMAX && p.init_mode != 2 && p.T >= 2 * CC && (int64_t)p.B * p.H <= 64;
+    return p.K <= 64 && p.V <= CVMAX && p.init_mode != 2 && p.T >= 2 * CC &&
+           (int64_t)p.B * p.H * ((p.K + 31) / 32) * ((p.V + 63) / 64) <= 384;
 }
 
 namespace {

@@ -94,13 +94,13 @@ def test_training_scan_bf16_inputs(cuda, native_lib):
 
 
 @pytest.mark.parametrize("B,T,H,K,V", [(2, 200, 3, 64, 128), (4, 70, 16, 32, 128), (1, 97, 2, 7, 9),
-                                       (3, 64, 2, 20, 36), (8, 48, 16, 32, 64)])
+                                       (3, 64, 2, 20, 36), (8, 48, 16, 32, 64), (32, 48, 16, 32, 64)])
 def test_training_scan_chunked_form(cuda, native_lib, B, T, H, K, V):
-    # sequences of two or more 16-token chunks with key width <= 64, value width <= 128 and at most 64
-    # sequences x heads take the chunked form: 16-column groups with partial score sums, 32-column
-    # groups (64 rows of 128 columns), one group (V <= 16), widths that are not multiples of 4 (4-byte
-    # staging) and a ragged last chunk; padding runs, resets (one on padding) and an initial state.
-    # 128 rows take the token-sequential kernel
+    # sequences of two or more 16-token chunks with key width <= 64, value width <= 128 and
+    # B*H*ceil(K/32)*ceil(V/64) <= 384 take the chunked form: 16-column groups with partial score
+    # sums, 32-column groups, one group (V <= 16), widths that are not multiples of 4 (4-byte staging),
+    # 128 sequence-heads (256 CTAs, two per SM) and a ragged last chunk; padding runs, resets (one on
+    # padding) and an initial state.  512 sequence-heads take the token-sequential kernel
     f = splitmix_tokens(300 + T + K, B, T, H, K, V)
     f[1] = f[1] / np.linalg.norm(f[1], axis=-1, keepdims=True)
     q, k, v = (x.astype(np.float32) for x in f[:3])
