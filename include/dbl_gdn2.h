@@ -185,8 +185,7 @@ int dbl_gdn_training_scan_backward(const dbl_training_scan_backward_args *args, 
 /* The forward -> backward hand-off of the reference: its gdn_training_scan returns checkpoint and
  * auxiliary tensors beside the packed outputs and its gdn_training_backward consumes them
  * (crates/kernels/src/gdn_training_ops.rs:201-224 and :87-112).  At the shapes of the chunked
- * backward (chunk_size 16, key width <= 64, value width <= 128, B*H*ceil(K/32)*ceil(V/64) <= 512,
- * T >= 32) the saved context holds the chunk-start states, the chunk maps and every token's edit,
+ * backward (chunk_size 16, key width <= 64, value width <= 128, T >= 32) the saved context holds the chunk-start states, the chunk maps and every token's edit,
  * and the backward skips the forward it would otherwise rerun; elsewhere the context is empty
  * (0 bytes) and these calls are dbl_gdn_training_scan and dbl_gdn_training_scan_backward.
  * The context must be 16-byte aligned and hold dbl_gdn_training_scan_context_bytes() bytes; the

@@ -394,8 +394,8 @@ def test_training_backward_matches_oracle(cuda, native_lib, K, V, chunk):
                                            (2, 37, 2, 7, 9, True), (3, 64, 2, 20, 36, False),
                                            (4, 96, 16, 32, 64, True), (8, 40, 16, 32, 64, True)])
 def test_training_backward_chunked_form(cuda, native_lib, B, T, H, K, V, opt):
-    # 16-token checkpoints with key width <= 64, value width <= 128 and B*H ceil(K/32) ceil(V/64) <= 512
-    # take the chunked backward (128 sequence-heads here, beyond the chunked forward's 64): ragged last
+    # 16-token checkpoints with key width <= 64, value width <= 128 and T >= 32 take the chunked
+    # backward (128 sequence-heads here, 256 CTAs of the reverse pass): ragged last
     # chunks, widths that are not multiples of 4, padding runs,
     # resets (one on padding), a zero gate in one channel, and with / without an initial state and
     # the final-state and score gradients, against the f64 oracle
