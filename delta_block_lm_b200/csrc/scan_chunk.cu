@@ -670,11 +670,20 @@ int launch_chunk_scan(const SeqParams& p, int in_dtype, cudaStream_t st, float* 
     float* ws = ext_ws;
     int rc = DBL_OK;
     if (!ws) {
-        cudaMemPool_t pool = nullptr;
-        rc = scratch_pool(&pool);
-        if (rc != DBL_OK) return rc;
-        const cudaError_t e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&ws),
-                                                      (ws_floats + part_floats) * sizeof(float), pool, st);
+        // while `st` is being captured into a CUDA graph the allocation becomes a graph memory node
+        // (cudaMallocAsync); otherwise it comes from the library's pool
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        cudaError_t e = cudaStreamIsCapturing(st, &cap);
+        if (e != cudaSuccess) return cuda_status(e, "chunk scan: cudaStreamIsCapturing");
+        const size_t bytes = (ws_floats + part_floats) * sizeof(float);
+        if (cap == cudaStreamCaptureStatusActive) {
+            e = cudaMallocAsync(reinterpret_cast<void**>(&ws), bytes, st);
+        } else {
+            cudaMemPool_t pool = nullptr;
+            rc = scratch_pool(&pool);
+            if (rc != DBL_OK) return rc;
+            e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&ws), bytes, pool, st);
+        }
         if (e != cudaSuccess) return cuda_status(e, "chunk scan: workspace");
     }
     float* part = ws + ws_floats;

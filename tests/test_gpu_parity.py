@@ -466,6 +466,47 @@ def test_training_saved_context(cuda, native_lib, B, T, H, K, V, chunk):
         assert rel_err(x1, r) < TOL_F32, (name, rel_err(x1, r))
 
 
+def test_training_scan_and_backward_in_a_cuda_graph(cuda, native_lib):
+    # the chunked forward (its workspace a graph memory node while the stream is captured) and the
+    # saved-context backward captured into one CUDA graph and replayed: the same outputs and
+    # gradients as eager calls
+    B, T, H, K, V = 2, 64, 3, 32, 64
+    rng = np.random.default_rng(5)
+    q, k = rng.standard_normal((B, T, H, K)) / np.sqrt(K), rng.standard_normal((B, T, H, K)) / np.sqrt(K)
+    v, w = rng.standard_normal((B, T, H, V)), rng.random((B, T, H, V))
+    a, e = rng.uniform(0.6, 1.0, (B, T, H, K)), rng.random((B, T, H, K))
+    valid, reset = rng.random((B, T)) > 0.1, rng.random((B, T)) > 0.93
+    init = 0.1 * rng.standard_normal((B, H, K, V))
+    go, gf, gs = rng.standard_normal((B, T, H, V)), rng.standard_normal((B, H, K, V)), rng.standard_normal((B, T, H))
+    d = lambda x: torch.as_tensor(np.asarray(x, np.float32), device=cuda)  # noqa: E731
+    args = [d(x) for x in (q, k, v, a, e, w, valid, reset, init)]
+    ups = [d(go), d(gf), d(gs)]
+
+    def step():
+        fwd = dbl.gdn_training_scan(*args, 16)
+        res, ctx = dbl.gdn_training_scan_saved(*args, 16)
+        grads = dbl.gdn_training_backward_saved(*args, ups[0], ctx, ups[1], ups[2], chunk_size=16)
+        return fwd, res, grads
+
+    eager = step()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        captured = step()
+    graph.replay()
+    graph.replay()
+    torch.cuda.synchronize()
+    for x, y in ((eager[0].output, captured[0].output), (eager[0].scores, captured[0].scores),
+                 (eager[1].output, captured[1].output), (eager[1].final_state, captured[1].final_state)):
+        assert torch.equal(x, y)
+    for name in ("dq", "dk", "dv", "dalpha", "derase", "dwrite", "dinitial"):
+        assert torch.equal(getattr(eager[2], name), getattr(captured[2], name)), name
+
+
 # ----------------------------------------------------------------------- mixer prologue
 @pytest.mark.parametrize("B,T,H,K,V,W,dtype", [(2, 37, 3, 32, 64, 4, torch.float32),
                                                 (1, 50, 2, 128, 128, 4, torch.bfloat16),
