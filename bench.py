@@ -759,6 +759,15 @@ def main():
     if world == 1 and rank == 0:
         if not args.no_secondary:
             line["secondary"] = {"decode": bench_decode(torch, args, dev), "relay": bench_relay(torch, args, dev)}
+            # the training scan at the reference's training shape (the backward workload's line,
+            # without its CPU sample)
+            tr = bench_backward(torch, argparse.Namespace(**{**vars(args), "no_cpu_baseline": True}), dev)
+            line["secondary"]["training_scan"] = {
+                "workload": tr["config"]["workload"], "backward_ms": tr["ms_per_step"],
+                "backward_mtok_s": tr["value"], "forward_ms": tr["config"]["forward_ms"],
+                "training_step_saved_context_ms": tr["config"]["training_step_saved_context_ms"],
+                "training_step_recomputing_ms": tr["config"]["training_step_recomputing_ms"],
+                "gpu_launches": tr["gpu_launches"]}
         if not args.no_cpu_baseline:
             cores = host_cores()
             v, t_s, secs = cpu_chunk_sample(target_s=4.0, nthreads=cores, reps=3)
