@@ -94,7 +94,8 @@ def test_training_scan_bf16_inputs(cuda, native_lib):
 
 
 @pytest.mark.parametrize("B,T,H,K,V", [(2, 200, 3, 64, 128), (4, 70, 16, 32, 128), (1, 97, 2, 7, 9),
-                                       (3, 64, 2, 20, 36), (8, 48, 16, 32, 64), (32, 48, 16, 32, 64)])
+                                       (3, 64, 2, 20, 36), (2, 61, 2, 37, 50), (8, 48, 16, 32, 64),
+                                       (32, 48, 16, 32, 64)])
 def test_training_scan_chunked_form(cuda, native_lib, B, T, H, K, V):
     # sequences of two or more 16-token chunks with key width <= 64, value width <= 128 and
     # B*H*ceil(K/32)*ceil(V/64) <= 384 take the chunked form: 16-column groups with partial score
@@ -392,7 +393,8 @@ def test_training_backward_matches_oracle(cuda, native_lib, K, V, chunk):
 
 @pytest.mark.parametrize("B,T,H,K,V,opt", [(2, 70, 3, 32, 64, True), (1, 50, 2, 64, 128, True),
                                            (2, 37, 2, 7, 9, True), (3, 64, 2, 20, 36, False),
-                                           (4, 96, 16, 32, 64, True), (8, 40, 16, 32, 64, True)])
+                                           (2, 45, 2, 37, 50, True), (4, 96, 16, 32, 64, True),
+                                           (8, 40, 16, 32, 64, True)])
 def test_training_backward_chunked_form(cuda, native_lib, B, T, H, K, V, opt):
     # 16-token checkpoints with key width <= 64, value width <= 128 and T >= 32 take the chunked
     # backward (128 sequence-heads here, 256 CTAs of the reverse pass): ragged last
