@@ -290,7 +290,7 @@ __device__ __forceinline__ void conv_row(const TI* xs, const float* ws, int C, i
 // WT > 0 fixes the conv width and CT > 0 the key and value widths (K = V = CT) at compile time, so
 // that the index arithmetic of the common shape folds to shifts; 0 reads them from p.
 template <typename TI, typename TO, bool VEC, int WT, int CT>
-__global__ void __launch_bounds__(THREADS, sizeof(TI) == 2 ? 4 : 3) prologue_kernel(const ProParams p) {
+__global__ void __launch_bounds__(THREADS, sizeof(TI) == 2 ? 5 : 3) prologue_kernel(const ProParams p) {
     extern __shared__ __align__(16) unsigned char smraw[];
     constexpr int E = VEC ? 4 : 1;
     const int K = CT > 0 ? CT : p.K, V = CT > 0 ? CT : p.V, W = WT > 0 ? WT : p.W, T = p.T;
