@@ -429,10 +429,9 @@ __global__ void __launch_bounds__(NTH) chunk_main_kernel(const SeqParams p, cons
             for (int x = tid; x < L.sh / 4; x += MTH) cp_async16(dst + 4 * x, src + 4 * x);
 #pragma unroll
             for (int k = 0; k < MAXCOL; ++k) {
-                if (tid + k * MTH < ncopy) {
-                    if (vec) cp_async16(dst + soff[k], src + goff[k]);
-                    else cp_async4(dst + soff[k], src + goff[k]);
-                }
+                if (tid + k * MTH >= ncopy) break;  // a thread's copies are a prefix of the slots
+                if (vec) cp_async16(dst + soff[k], src + goff[k]);
+                else cp_async4(dst + soff[k], src + goff[k]);
             }
         }
         cp_async_commit();
