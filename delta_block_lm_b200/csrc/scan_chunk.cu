@@ -385,7 +385,7 @@ __global__ void __launch_bounds__(NTH) chunk_main_kernel(const SeqParams p, cons
     constexpr int NS = KMAX / RP; // state rows per thread
     constexpr int NP = VG / 16;   // 16-lane groups sharing one token
     constexpr int SST = VG + 4;   // state row stride
-    constexpr int MAXCOL = 8;     // column-part copies per thread and chunk (at most 96 rows x 32 columns)
+    constexpr int MAXCOL = ((2 * CC + KMAX) * VG + NTH - 1) / NTH;  // column-part copies per thread
     extern __shared__ __align__(16) float smain[];
     const int K = p.K, V = p.V, K4 = (K + 3) & ~3;
     const int nch = (p.T + CC - 1) / CC;

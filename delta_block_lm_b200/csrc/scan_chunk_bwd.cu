@@ -260,26 +260,31 @@ __global__ void __launch_bounds__(CTH) chunk_bwd_rev_kernel(const CBwdParams p, 
         Sb0[x] = (p.g_fin && i < K && jj < vg) ? p.g_fin[sbase + (size_t)i * V + c0 + jj] : 0.f;
         Sb1[x] = 0.f;
     }
+    // this thread's copies of the column-sliced part (dE_pre, Hb rows), the same every chunk:
+    // shared-memory and block offsets (16-byte copies when V is a multiple of 4); a thread's copies
+    // are a prefix of its slots
+    constexpr int MAXCOL = ((CC + KMAX) * VG + CTH - 1) / CTH;  // rows x columns over the threads
+    int soff[MAXCOL], goff[MAXCOL];
+    const int per = vec ? vg >> 2 : vg, ncopy = rows * per;
+#pragma unroll
+    for (int k = 0; k < MAXCOL; ++k) {
+        const int x = tid + k * CTH;
+        const int r = x / per, w = x - r * per;
+        soff[k] = L.sh + r * VG + (vec ? 4 * w : w);
+        goff[k] = L.sh + r * V + c0 + (vec ? 4 * w : w);
+    }
     // stages the maps of reverse step `it` (chunk nch - 1 - it) into buffer it % NB, one group each
     auto prefetch = [&](int it) {
-        if (it >= nch) {
-            cp_async_commit();
-            return;
-        }
-        const int c = nch - 1 - it;
-        const float* src = p.rev + ((size_t)bh * nch + c) * L.total;
-        float* dst = bb0 + (it % NB) * bfl;
-        for (int x = tid; x < L.sh / 4; x += CTH) cp_async16(dst + 4 * x, src + 4 * x);
-        if (vec) {
-            const int q4 = vg >> 2;
-            for (int x = tid; x < rows * q4; x += CTH) {
-                const int r = x / q4, w = x - r * q4;
-                cp_async16(dst + L.sh + r * VG + 4 * w, src + L.sh + (size_t)r * V + c0 + 4 * w);
-            }
-        } else {
-            for (int x = tid; x < rows * vg; x += CTH) {
-                const int r = x / vg, w = x - r * vg;
-                cp_async4(dst + L.sh + r * VG + w, src + L.sh + (size_t)r * V + c0 + w);
+        if (it < nch) {
+            const int c = nch - 1 - it;
+            const float* src = p.rev + ((size_t)bh * nch + c) * L.total;
+            float* dst = bb0 + (it % NB) * bfl;
+            for (int x = tid; x < L.sh / 4; x += CTH) cp_async16(dst + 4 * x, src + 4 * x);
+#pragma unroll
+            for (int k = 0; k < MAXCOL; ++k) {
+                if (tid + k * CTH >= ncopy) break;
+                if (vec) cp_async16(dst + soff[k], src + goff[k]);
+                else cp_async4(dst + soff[k], src + goff[k]);
             }
         }
         cp_async_commit();
