@@ -153,6 +153,7 @@ EXPORTS = [
     ("dbl_relay_merge_decode", ctypes.c_int,
      [ctypes.POINTER(RelayMergeArgs), _vp, ctypes.c_size_t, _vp]),
     ("dbl_relay_merge_decode_noalloc", ctypes.c_int, [ctypes.POINTER(RelayMergeArgs), _vp]),
+    ("dbl_relay_merge_call_workspace_bytes", ctypes.c_size_t, [ctypes.POINTER(RelayMergeArgs)]),
     ("dbl_relay_attention_forward", ctypes.c_int, [ctypes.POINTER(RelayAttentionArgs), _vp]),
 ]
 

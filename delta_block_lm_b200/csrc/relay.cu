@@ -685,8 +685,9 @@ size_t relay_workspace_bytes(int64_t N, int64_t H, int64_t D, int64_t Lp, int64_
     return a > b ? a : b;
 }
 
-// Launches the merge with its partials placed in `ws` (>= relay_workspace_bytes bytes).  The
-// arrival counters are cleared first on the same stream.
+// Launches the merge with its partials placed in `ws`, which must hold at least
+// relay_call_workspace_bytes(a) bytes (the layout of the call's own dtype).  The arrival counters
+// are cleared first on the same stream.
 int relay_launch(const dbl_relay_merge_args* a, void* ws, cudaStream_t st) {
     const Layout L = layout(a->n_seq, a->heads, a->head_dim, a->prefix_len, a->own_cap, a->dtype == DBL_BF16);
     RelayParams p{};
@@ -727,6 +728,11 @@ extern "C" size_t dbl_relay_merge_workspace_bytes(int64_t n_seq, int64_t heads, 
                                                   int64_t own_cap) {
     if (n_seq <= 0 || heads <= 0 || head_dim <= 0 || prefix_len < 0 || own_cap < 0) return 0;
     return dbl::relay_workspace_bytes(n_seq, heads, head_dim, prefix_len, own_cap);
+}
+
+extern "C" size_t dbl_relay_merge_call_workspace_bytes(const dbl_relay_merge_args* a) {
+    if (!a || a->n_seq <= 0 || a->heads <= 0 || a->head_dim <= 0 || a->prefix_len < 0 || a->own_cap < 0) return 0;
+    return dbl::relay_call_workspace_bytes(a);
 }
 
 extern "C" int dbl_relay_merge_decode(const dbl_relay_merge_args* a, void* workspace, size_t workspace_bytes,

@@ -8,6 +8,8 @@
 // memory is fragmented.  For them this variant keeps the scratch in a fixed array in device
 // memory that is part of the library image: it is reserved when the library's module loads on a
 // device and stays reserved on every device that loaded it until the process exits.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -29,20 +31,54 @@ static __device__ __align__(256) unsigned char g_relay_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mutex;
+// Per device: the address resolved for the context whose id is g_scratch_ctx[dev].  Context ids
+// (cuCtxGetId) are never reused within a process, so an address resolved in a context that was
+// since destroyed (cudaDeviceReset) or in another context of the same device is never handed out.
 void* g_scratch_ptr[kMaxDevices] = {};
+unsigned long long g_scratch_ctx[kMaxDevices] = {};
 
-// Resolves (once per device, with that device current) the device address of the scratch array.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+// Id of the calling thread's current context, or 0 when it cannot be read.
+unsigned long long current_context_id() {
+    static CtxGetCurrentFn get_current = nullptr;
+    static CtxGetIdFn get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult qr;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &qr) == cudaSuccess &&
+            qr == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+        p = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &qr) == cudaSuccess &&
+            qr == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<CtxGetIdFn>(p);
+    });
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS)
+        return 0;
+    return id;
+}
+
+// The device address of the scratch array in the current context, resolved with
+// cudaGetSymbolAddress the first time a context of this device calls (and again whenever the
+// current context changes).
 int scratch_for_current_device(void** out) {
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_status(e, "relay_noalloc: cudaGetDevice");
     if (dev < 0 || dev >= kMaxDevices) return fail(DBL_ERR_UNSUPPORTED, "relay_noalloc: device ordinal %d out of range", dev);
+    const unsigned long long ctx = current_context_id();  // 0 until the runtime's context exists
     std::lock_guard<std::mutex> lock(g_mutex);
-    if (!g_scratch_ptr[dev]) {
+    if (!g_scratch_ptr[dev] || ctx == 0 || g_scratch_ctx[dev] != ctx) {
         void* ptr = nullptr;
-        e = cudaGetSymbolAddress(&ptr, g_relay_scratch);
+        e = cudaGetSymbolAddress(&ptr, g_relay_scratch);  // also makes the device's context current
         if (e != cudaSuccess) return cuda_status(e, "relay_noalloc: cudaGetSymbolAddress");
         g_scratch_ptr[dev] = ptr;
+        g_scratch_ctx[dev] = current_context_id();
     }
     *out = g_scratch_ptr[dev];
     return DBL_OK;

@@ -58,9 +58,15 @@ def assert_fused_device(device: torch.device) -> None:
 
 
 def scan_selected(backend: ScanBackend, kind: MixerKind, input: ScanInput, valid: torch.Tensor,
-                  reset: torch.Tensor, chunk_size: int, initial: Optional[torch.Tensor] = None
-                  ) -> ScanOutput:
-    """Explicit dispatch; requesting fused execution never falls back to tensor operations."""
+                  reset: torch.Tensor, chunk_size: int, initial: Optional[torch.Tensor] = None,
+                  *, check_gates: bool = False) -> ScanOutput:
+    """Explicit dispatch; requesting fused execution never falls back to tensor operations.
+
+    ``CHUNKED_GDN2`` takes ``erase`` as the scalar beta of the delta rule and requires
+    ``write == erase``; that equality is the caller's contract and is not checked by default,
+    because checking it reads both tensors back to the host (a device synchronisation per call).
+    ``check_gates=True`` checks it and raises ``ValueError`` on a mismatch.  The decode step is
+    this call with T = 1 and ``initial`` set (crates/mixers/src/lib.rs:544-556)."""
     if backend == ScanBackend.TENSOR_SOLVER:
         raise NotImplementedError(
             "tensor_solver is the reference's Burn tensor-op path; this build provides "
@@ -80,7 +86,7 @@ def scan_selected(backend: ScanBackend, kind: MixerKind, input: ScanInput, valid
     if input.alpha.shape[3] != 1 or input.erase.shape[3] != 1 or input.write.shape[3] != 1:
         raise ValueError("chunked_gdn2 requires scalar gates (alpha, erase, write of width 1)")
     beta = input.erase[..., 0].to(torch.float32)
-    if not torch.equal(beta, input.write[..., 0].to(torch.float32)):
+    if check_gates and not torch.equal(beta, input.write[..., 0].to(torch.float32)):
         raise ValueError("chunked_gdn2 requires erase == write (the scalar beta of the delta rule)")
     out, final = kernels.gdn2_prefill(input.q, input.k, input.v,
                                       input.alpha[..., 0].to(torch.float32).contiguous(),

@@ -293,6 +293,9 @@ typedef struct {
 
 size_t dbl_relay_merge_workspace_bytes(int64_t n_seq, int64_t heads, int64_t head_dim,
                                        int64_t prefix_len, int64_t own_cap);
+/* Scratch bytes of one call's own layout (its dtype's): at most dbl_relay_merge_workspace_bytes,
+ * which bounds both dtypes.  0 for an invalid shape.  Host-only; needs no device. */
+size_t dbl_relay_merge_call_workspace_bytes(const dbl_relay_merge_args *args);
 int dbl_relay_merge_decode(const dbl_relay_merge_args *args, void *workspace,
                            size_t workspace_bytes, dbl_stream_t stream);
 
@@ -302,10 +305,13 @@ int dbl_relay_merge_decode(const dbl_relay_merge_args *args, void *workspace,
  * as dbl_relay_merge_decode; the split-softmax partials go to a fixed array of
  * DBL_RELAY_NOALLOC_SCRATCH_BYTES that the library keeps in device memory (reserved on every
  * device that loads the library, until the process exits), so the call allocates nothing.
- *   - A call whose partials need more than that (see dbl_relay_merge_workspace_bytes) returns
- *     DBL_ERR_WORKSPACE and launches nothing.
- *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress) with
- *     that device current; make that first call before any stream capture.
+ *   - The limit is checked against the scratch of the call's own dtype, which
+ *     dbl_relay_merge_call_workspace_bytes(args) returns: a call needing more than the array
+ *     returns DBL_ERR_WORKSPACE and launches nothing.
+ *   - The first call in a CUDA context looks up the array's device address in that context
+ *     (cudaGetSymbolAddress) and keeps it for later calls in the same context; a call from another
+ *     context of the device (a driver-API host, or after cudaDeviceReset) looks it up again.
+ *     Make the first call of each context before any stream capture.
  *   - Every call on a device shares the one array and the array keeps the last call's partials
  *     (the arrival counters are cleared at the start of each call): calls that overlap on the GPU,
  *     e.g. on two streams, race on it. */

@@ -46,69 +46,84 @@
  * Returns 0, or -1 on a non-finite input (reference.rs:58-61 panics there).
  * states_out (optional) receives the state after every token: [B,H,T,K,V].
  * ---------------------------------------------------------------------------------------- */
+/* One (b, h) row of orc_gdn2_scan_f64; S and edit are K*V and V scratch doubles. */
+static int scan_row_f64(int b, int h, int T, int H, int K, int V,
+                        const double *q, const double *k, const double *v,
+                        const double *alpha, const double *erase, const double *write,
+                        const uint8_t *valid, const uint8_t *reset, const double *initial,
+                        double *out, double *final_state, double *scores, double *states_out,
+                        double *S, double *edit)
+{
+    const size_t sbase = ((size_t)b * H + h) * K * V;
+    if (initial) memcpy(S, initial + sbase, sizeof(double) * K * V);
+    else memset(S, 0, sizeof(double) * K * V);
+    for (int t = 0; t < T; ++t) {
+        const double *qt = q + IDX4(b, t, h, 0, T, H, K);
+        const double *kt = k + IDX4(b, t, h, 0, T, H, K);
+        const double *vt = v + IDX4(b, t, h, 0, T, H, V);
+        const double *at = alpha + IDX4(b, t, h, 0, T, H, K);
+        const double *et = erase + IDX4(b, t, h, 0, T, H, K);
+        const double *wt = write + IDX4(b, t, h, 0, T, H, V);
+        double *ot = out ? out + IDX4(b, t, h, 0, T, H, V) : NULL;
+        for (int i = 0; i < K; ++i)
+            if (!isfinite(qt[i]) || !isfinite(kt[i]) || !isfinite(at[i]) || !isfinite(et[i])) return -1;
+        for (int j = 0; j < V; ++j)
+            if (!isfinite(vt[j]) || !isfinite(wt[j])) return -1;
+        const int act = valid ? valid[(size_t)b * T + t] != 0 : 1;
+        const int rst = reset ? reset[(size_t)b * T + t] != 0 : 0;
+        if (!act) {
+            if (ot) memset(ot, 0, sizeof(double) * V);
+            if (scores) scores[((size_t)b * T + t) * H + h] = 0.0;
+        } else {
+            if (rst) memset(S, 0, sizeof(double) * K * V);
+            for (int i = 0; i < K; ++i)
+                for (int j = 0; j < V; ++j) S[(size_t)i * V + j] *= at[i];
+            for (int j = 0; j < V; ++j) {
+                double e = wt[j] * vt[j];
+                for (int i = 0; i < K; ++i) e -= et[i] * kt[i] * S[(size_t)i * V + j];
+                edit[j] = e;
+            }
+            double kk = 0.0, ee = 0.0;
+            for (int i = 0; i < K; ++i) kk += kt[i] * kt[i];
+            for (int j = 0; j < V; ++j) ee += edit[j] * edit[j];
+            if (scores) scores[((size_t)b * T + t) * H + h] = sqrt(kk * ee);
+            if (ot) memset(ot, 0, sizeof(double) * V);
+            for (int i = 0; i < K; ++i)
+                for (int j = 0; j < V; ++j) {
+                    S[(size_t)i * V + j] += kt[i] * edit[j];
+                    if (ot) ot[j] += qt[i] * S[(size_t)i * V + j];
+                }
+        }
+        if (states_out)
+            memcpy(states_out + ((((size_t)b * H + h) * T + t) * K * V), S, sizeof(double) * K * V);
+    }
+    if (final_state) memcpy(final_state + sbase, S, sizeof(double) * K * V);
+    return 0;
+}
+
 int orc_gdn2_scan_f64(int B, int T, int H, int K, int V,
                       const double *q, const double *k, const double *v,
                       const double *alpha, const double *erase, const double *write,
                       const uint8_t *valid, const uint8_t *reset, const double *initial,
                       double *out, double *final_state, double *scores, double *states_out)
 {
-    double *edit = (double *)malloc(sizeof(double) * (size_t)V);
-    double *S = (double *)malloc(sizeof(double) * (size_t)K * V);
-    if (!edit || !S) { free(edit); free(S); return -2; }
-    for (int b = 0; b < B; ++b) {
-        for (int h = 0; h < H; ++h) {
-            const size_t sbase = ((size_t)b * H + h) * K * V;
-            if (initial) memcpy(S, initial + sbase, sizeof(double) * K * V);
-            else memset(S, 0, sizeof(double) * K * V);
-            for (int t = 0; t < T; ++t) {
-                const double *qt = q + IDX4(b, t, h, 0, T, H, K);
-                const double *kt = k + IDX4(b, t, h, 0, T, H, K);
-                const double *vt = v + IDX4(b, t, h, 0, T, H, V);
-                const double *at = alpha + IDX4(b, t, h, 0, T, H, K);
-                const double *et = erase + IDX4(b, t, h, 0, T, H, K);
-                const double *wt = write + IDX4(b, t, h, 0, T, H, V);
-                double *ot = out ? out + IDX4(b, t, h, 0, T, H, V) : NULL;
-                for (int i = 0; i < K; ++i)
-                    if (!isfinite(qt[i]) || !isfinite(kt[i]) || !isfinite(at[i]) || !isfinite(et[i])) {
-                        free(edit); free(S); return -1;
-                    }
-                for (int j = 0; j < V; ++j)
-                    if (!isfinite(vt[j]) || !isfinite(wt[j])) { free(edit); free(S); return -1; }
-                const int act = valid ? valid[(size_t)b * T + t] != 0 : 1;
-                const int rst = reset ? reset[(size_t)b * T + t] != 0 : 0;
-                if (!act) {
-                    if (ot) memset(ot, 0, sizeof(double) * V);
-                    if (scores) scores[((size_t)b * T + t) * H + h] = 0.0;
-                } else {
-                    if (rst) memset(S, 0, sizeof(double) * K * V);
-                    for (int i = 0; i < K; ++i)
-                        for (int j = 0; j < V; ++j) S[(size_t)i * V + j] *= at[i];
-                    for (int j = 0; j < V; ++j) {
-                        double e = wt[j] * vt[j];
-                        for (int i = 0; i < K; ++i) e -= et[i] * kt[i] * S[(size_t)i * V + j];
-                        edit[j] = e;
-                    }
-                    double kk = 0.0, ee = 0.0;
-                    for (int i = 0; i < K; ++i) kk += kt[i] * kt[i];
-                    for (int j = 0; j < V; ++j) ee += edit[j] * edit[j];
-                    if (scores) scores[((size_t)b * T + t) * H + h] = sqrt(kk * ee);
-                    if (ot) memset(ot, 0, sizeof(double) * V);
-                    for (int i = 0; i < K; ++i)
-                        for (int j = 0; j < V; ++j) {
-                            S[(size_t)i * V + j] += kt[i] * edit[j];
-                            if (ot) ot[j] += qt[i] * S[(size_t)i * V + j];
-                        }
-                }
-                if (states_out)
-                    memcpy(states_out + ((((size_t)b * H + h) * T + t) * K * V), S,
-                           sizeof(double) * K * V);
-            }
-            if (final_state) memcpy(final_state + sbase, S, sizeof(double) * K * V);
+    int status = 0;
+    /* the (b, h) rows are independent: one row per OpenMP task, each with its own scratch */
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int bh = 0; bh < B * H; ++bh) {
+        double *edit = (double *)malloc(sizeof(double) * (size_t)V);
+        double *S = (double *)malloc(sizeof(double) * (size_t)K * V);
+        int rc = (!edit || !S) ? -2
+                               : scan_row_f64(bh / H, bh % H, T, H, K, V, q, k, v, alpha, erase, write, valid,
+                                              reset, initial, out, final_state, scores, states_out, S, edit);
+        if (rc != 0) {
+#pragma omp critical
+            if (status == 0 || rc == -1) status = rc;
         }
+        free(edit);
+        free(S);
     }
-    free(edit);
-    free(S);
-    return 0;
+    return status;
 }
 
 /* ------------------------------------------------------------------------------------------

@@ -48,6 +48,42 @@ def rel_err(actual, expected) -> float:
     return float((np.abs(a - e) / (np.abs(e) + rms)).max(initial=0.0))
 
 
+def strict_metrics(actual, expected, floor=1e-3, atol=ATOL, rtol=RTOL) -> dict:
+    """The three parity numbers reported beside every kernel-vs-oracle comparison:
+    ``rel_err`` (above), ``max_rel`` = max |a - e| / |e| over the elements with |e| > floor * rms(e)
+    (the north star's plain max relative error, with near-zero elements left out), and
+    ``ref_pass`` = the fraction of elements inside the reference's |a - e| <= atol + rtol |e|
+    (checks.rs:73-101, reuse/crates/dre-gdn2/src/tests.rs:109-122)."""
+    a = np.asarray(actual, np.float64).ravel()
+    e = np.asarray(expected, np.float64).ravel()
+    assert a.shape == e.shape, (a.shape, e.shape)
+    if not np.isfinite(a).all():
+        return {"rel_err": float("inf"), "max_rel": float("inf"), "ref_pass": 0.0}
+    rms = float(np.sqrt(np.mean(e * e))) if e.size else 0.0
+    big = np.abs(e) > floor * rms
+    d = np.abs(a - e)
+    max_rel = float((d[big] / np.abs(e[big])).max(initial=0.0)) if big.any() else 0.0
+    ref_pass = float(np.mean(d <= atol + rtol * np.abs(e))) if e.size else 1.0
+    return {"rel_err": rel_err(a, e), "max_rel": max_rel, "ref_pass": ref_pass}
+
+
+def report(case: str, **named) -> dict:
+    """Strict metrics of each (actual, expected) pair in ``named``, printed and, when the
+    environment variable DBL_PARITY_REPORT names a file, appended to it as one JSON line."""
+    import json
+    import os
+
+    out = {"case": case}
+    for name, (a, e) in named.items():
+        out[name] = strict_metrics(a, e)
+    print(json.dumps(out))
+    path = os.environ.get("DBL_PARITY_REPORT")
+    if path:
+        with open(path, "a") as f:
+            f.write(json.dumps(out) + "\n")
+    return out
+
+
 # ------------------------------------------------------------------------------ reference formulas
 def sinusoid_fixture(t: int, b: int = 2, h: int = 4, k: int = 32, v: int = 64):
     """checks.rs:119-180 for GDN-2: returns (fields list of [B,T,H,W] f32, valid, reset)."""

@@ -1,0 +1,144 @@
+"""GPU parity at every BASELINE config's stated shape, against the CPU oracle.
+
+Each test runs the kernel on the whole config (the code path the bench times) and compares a
+seeded sample (or all) of its heads / rows with the f64 oracle on the same bf16-rounded inputs.
+Every comparison reports three numbers (``fixtures.report``): ``rel_err`` (asserted against the
+north star's bound), ``max_rel`` (plain max relative error over elements above 1e-3 rms) and
+``ref_pass`` (fraction inside the reference's 2e-5 + 3e-4|e|).  Set DBL_PARITY_REPORT=<file> to
+collect them as JSON lines.
+
+  config 0  B2/H4/T512/d64 f32               all heads
+  config 1  B8/H16/T4096/d128 bf16            32 of 128 (b, h) heads, seeded
+  config 2  256 seq x H16 x 128^2, 64 steps    64 of 4096 (n, h) heads, seeded, every step
+  config 3  64 x H16, prefix 4096 + own 1024   all 1024 rows (9 partials merged per row)
+  config 4  B1/H16/T131072/d128, segmented     2 of 16 heads over the whole sequence
+"""
+import numpy as np
+import pytest
+import torch
+
+import delta_block_lm_b200 as dbl
+from fixtures import TOL_BF16, TOL_F32, report
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def host(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _no_device_error(lib):
+    import ctypes
+    code = ctypes.c_int(0)
+    assert lib.dbl_device_error(ctypes.byref(code)) == 0 and code.value == 0, code.value
+
+
+def test_config0_full(cuda, native_lib):
+    g = torch.Generator(device=cuda)
+    g.manual_seed(5)
+    B, T, H, D = 2, 512, 4, 64
+    q = torch.randn((B, T, H, D), device=cuda, generator=g)
+    k = torch.randn((B, T, H, D), device=cuda, generator=g)
+    q, k = q / q.norm(dim=-1, keepdim=True), k / k.norm(dim=-1, keepdim=True)
+    v = torch.randn((B, T, H, D), device=cuda, generator=g)
+    beta = torch.sigmoid(torch.randn((B, T, H), device=cuda, generator=g))
+    alpha = torch.exp(torch.nn.functional.logsigmoid(3.0 + torch.randn((B, T, H), device=cuda, generator=g)))
+    out, fin = dbl.gdn2_prefill(q, k, v, alpha, beta)
+    torch.cuda.synchronize()
+    ro, rf, _ = O.scan_scalar(host(q), host(k), host(v), host(alpha), host(beta))
+    r = report("config0 B2/H4/T512/d64 f32", out=(host(out), ro), final_state=(host(fin), rf))
+    assert r["out"]["rel_err"] < TOL_F32 and r["final_state"]["rel_err"] < TOL_F32
+
+
+def test_config1_full_sampled_heads(cuda, native_lib):
+    import bench
+    q, k, v, alpha, beta = bench.make_prefill_inputs(torch, cuda, 1234)
+    out, fin = dbl.gdn2_prefill(q, k, v, alpha, beta)
+    torch.cuda.synchronize()
+    _no_device_error(native_lib)
+    rng = np.random.default_rng(1)
+    pick = rng.choice(8 * 16, size=32, replace=False)
+    bs, hs = torch.as_tensor(pick // 16, device=cuda), torch.as_tensor(pick % 16, device=cuda)
+    # the sampled heads as a batch of 32 single-head sequences [32, T, 1, D]
+    sel = lambda t: host(t[bs, :, hs].unsqueeze(2))  # noqa: E731
+    ro, rf, _ = O.scan_scalar(sel(q), sel(k), sel(v), host(alpha[bs, :, hs].unsqueeze(2)),
+                              host(beta[bs, :, hs].unsqueeze(2)))
+    r = report("config1 B8/H16/T4096/d128 bf16, 32 sampled heads", out=(sel(out), ro),
+               final_state=(host(fin[bs, hs].unsqueeze(1)), rf))
+    assert r["out"]["rel_err"] < TOL_BF16 and r["final_state"]["rel_err"] < TOL_BF16
+
+
+def test_config2_full_64_steps(cuda, native_lib):
+    n, H, D, steps = 256, 16, 128, 64
+    g = torch.Generator(device=cuda)
+    g.manual_seed(7)
+    state = 0.02 * torch.randn((n, H, D, D), device=cuda, generator=g)
+    q = torch.randn((steps, n, H, D), device=cuda, generator=g)
+    k = torch.randn((steps, n, H, D), device=cuda, generator=g)
+    q = (q / q.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    k = (k / k.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    v = torch.randn((steps, n, H, D), device=cuda, generator=g).to(torch.bfloat16)
+    beta = torch.sigmoid(torch.randn((steps, n, H), device=cuda, generator=g))
+    alpha = torch.exp(torch.nn.functional.logsigmoid(3.0 + torch.randn((steps, n, H), device=cuda, generator=g)))
+    rng = np.random.default_rng(2)
+    pick = rng.choice(n * H, size=64, replace=False)
+    Sref = host(state).reshape(n * H, D, D)[pick].astype(np.float64)
+    scale = 1.0 / np.sqrt(D)
+    outs, refs = [], []
+    for s in range(steps):
+        o = dbl.gdn2_decode_step(q[s], k[s], v[s], alpha[s], beta[s], state)
+        fl = lambda t, w: host(t).reshape(n * H, w)[pick]  # noqa: E731
+        a = np.repeat(host(alpha[s]).reshape(-1, 1)[pick], D, 1)
+        b_ = np.repeat(host(beta[s]).reshape(-1, 1)[pick], D, 1)
+        ro, Sref = O.step(fl(q[s], D) * scale, fl(k[s], D), fl(v[s], D), a, b_, b_, Sref)
+        outs.append(fl(o, D))
+        refs.append(ro)
+    torch.cuda.synchronize()
+    r = report("config2 decode 256x16x128^2, 64 steps, 64 sampled heads",
+               out=(np.stack(outs), np.stack(refs)), state=(host(state).reshape(n * H, D, D)[pick], Sref))
+    assert r["out"]["rel_err"] < TOL_BF16 and r["state"]["rel_err"] < TOL_BF16
+
+
+def test_config3_full_all_rows(cuda, native_lib):
+    n, H, D, lp, lo = 64, 16, 128, 4096, 1024
+    g = torch.Generator(device=cuda)
+    g.manual_seed(9)
+    mk = lambda *s: torch.randn(s, device=cuda, generator=g).to(torch.bfloat16)  # noqa: E731
+    q, kp, vp, ko, vo = mk(n, H, D), mk(H, lp, D), mk(H, lp, D), mk(n, H, lo, D), mk(n, H, lo, D)
+    o, m, s = dbl.relay_merge_decode(q, kp, vp, ko, vo)
+    torch.cuda.synchronize()
+    ro, rm, rs = O.relay_merge(host(q), host(kp), host(vp), host(ko), host(vo), 1.0 / np.sqrt(D))
+    r = report("config3 relay 64x16, prefix 4096 + own 1024, all rows", out=(host(o), ro),
+               row_max=(host(m), rm), row_sum=(host(s), rs))
+    assert r["out"]["rel_err"] < TOL_BF16
+    assert r["row_max"]["rel_err"] < TOL_BF16 and r["row_sum"]["rel_err"] < TOL_BF16
+
+
+def _config4_inputs(dev, t=131072):
+    import bench
+    return bench.make_prefill_inputs(torch, dev, 777, b=1, t=t)
+
+
+def _config4_oracle(q, k, v, alpha, beta, heads):
+    """The oracle over the whole sequence for the given heads, run as a batch of single-head
+    sequences: returns (out [h, T, 1, D], final_state [h, 1, D, D], scores)."""
+    hs = list(heads)
+    seq = lambda t: host(t[0, :, hs].transpose(0, 1).unsqueeze(2))  # [T,h,D] -> [h,T,1,D]  # noqa: E731
+    gate = lambda t: host(t[0, :, hs].transpose(0, 1).unsqueeze(2))  # [T,h] -> [h,T,1]  # noqa: E731
+    return O.scan_scalar(seq(q), seq(k), seq(v), gate(alpha), gate(beta))
+
+
+def test_config4_full_segmented_two_heads(cuda, native_lib):
+    from delta_block_lm_b200 import shard
+    q, k, v, alpha, beta = _config4_inputs(cuda)
+    out, fin = shard.segmented_prefill(q, k, v, alpha, beta)
+    torch.cuda.synchronize()
+    _no_device_error(native_lib)
+    heads = (0, 15)
+    ro, rf, _ = _config4_oracle(q, k, v, alpha, beta, heads)
+    got_o = np.stack([host(out[0, :, h]) for h in heads])
+    got_f = np.stack([host(fin[0, h]) for h in heads])
+    r = report("config4 B1/H16/T131072/d128 bf16, 1 GPU segmented, heads 0 and 15",
+               out=(got_o, ro[:, :, 0]), final_state=(got_f, rf[:, 0]))
+    assert r["out"]["rel_err"] < TOL_BF16 and r["final_state"]["rel_err"] < TOL_BF16
