@@ -225,7 +225,9 @@ def run_reference(args, rank: int, world: int):
         "config": {"workload": f"c1 prefill sample B{B}/H{H}/T{t_s}/d{D} (chunk 16, the reference's maximum)",
                    "batch_per_gpu": B, "heads": H, "seq_len_sample": t_s, "d_k": D, "d_v": D},
         "cpu_baseline": {"value": value, "unit": "Mtok/s", "cores": cores, "kind": "port",
-                         "sample": f"B{B}/H{H}/T{t_s}/d{D} per step, chunk::scan restated in C (OpenMP)"},
+                         "sample": f"B{B}/H{H}/T{t_s}/d{D} per step, chunk::scan restated in C (OpenMP)",
+                         "scope": "the whole host: every core of the node that holds the GPUs (rank 0 alone runs "
+                                  "it at any N; the ours arm at N GPUs shares this one host)"},
         "e2e": {"value": value, "unit": "Mtok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -325,8 +327,25 @@ def bench_prefill(torch, dist, args, dev, rank, world):
         e2e_ms = tt.item()
     h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv, ha, hb))
     d2h = ho.numel() * ho.element_size() + hf.numel() * hf.element_size()
+    # the copy path alone on this rank: the same host buffers in and out, no kernel
+    dq_, dk_, dv_ = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    c0, c1, c2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    c0.record(stream)
+    for x, y in ((dq_, hq), (dk_, hk), (dv_, hv)):
+        x.copy_(y, non_blocking=True)
+    c1.record(stream)
+    ho.copy_(out, non_blocking=True)
+    hf.copy_(fin, non_blocking=True)
+    c2.record(stream)
+    torch.cuda.synchronize(dev)
+    h2d_gbs = (h2d - sum(x.numel() * x.element_size() for x in (ha, hb))) / (c0.elapsed_time(c1) / 1e3) / 1e9
+    d2h_gbs = d2h / (c1.elapsed_time(c2) / 1e3) / 1e9
+    del dq_, dk_, dv_
     e2e = {"value": B * T * world * e2e_steps / (e2e_ms / 1e3) / 1e6, "unit": "Mtok/s",
-           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps}
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+           "copy_rate_rank0_gbs": {"h2d": h2d_gbs, "d2h": d2h_gbs,
+                                   "note": "pinned host <-> this rank's GPU, copies alone on one stream; every "
+                                           "rank of a node shares the host's memory bandwidth"}}
 
     hbm, tflops, src = peaks()
     token_heads = B * T * H
@@ -336,6 +355,8 @@ def bench_prefill(torch, dist, args, dev, rank, world):
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                 "frac": achieved / hbm, "peak_source": src,
                 "traffic": ncu_traffic("gdn2_prefill_c1"),
+                "traffic_source": "profiles/ncu_traffic.json: dram bytes of one launch of this kernel at this "
+                                  "workload from an ncu capture, not measured in this run",
                 "algorithmic_bytes_per_launch": alg_bytes,
                 "tensor_tflops": alg_flops / (launch_ms / 1e3) / 1e12,
                 "tensor_frac": alg_flops / (launch_ms / 1e3) / 1e12 / tflops,
@@ -354,52 +375,100 @@ def bench_prefill(torch, dist, args, dev, rank, world):
 
 
 def bench_long(torch, dist, args, dev, rank, world):
-    """Config 4: one sequence B1/H16/T131072/d128 bf16, sharded along time over the ranks
-    (strong scaling); the hand-off is one all_gather of the span boundary objects."""
-    from delta_block_lm_b200 import shard
+    """Config 4: one sequence B1/H16/T131072/d128 bf16, sharded along time over the ranks (strong
+    scaling).  Phases, each max over ranks: pass 1 (the segment maps of this rank's span), the
+    hand-off (the span map composed by the fold kernel, one all_gather of the span boundary objects
+    -- the only collective -- and the fold of the earlier ranks' maps), pass 2 (the fold of this
+    rank's segment starts and the rescan).  At one GPU the same work is also timed as the single
+    C-ABI call dbl_gdn2_prefill_segmented."""
+    from delta_block_lm_b200 import kernels, shard
 
     t_total = args.long_tokens
     lo, hi = shard.shard_bounds(t_total, world, rank, align=CHUNK)
     q, k, v, alpha, beta = make_prefill_inputs(torch, dev, 777 + rank, b=1, t=hi - lo)
     stream = torch.cuda.current_stream(dev)
-
     segs = shard.pick_segments(hi - lo, H, shard.sm_count(dev))
+    K = V = D
 
-    def step():
-        return shard.time_sharded_prefill(q, k, v, alpha, beta, segments=segs)
+    def step(ev=None):
+        rec = (lambda i: ev[i].record(stream)) if ev else (lambda i: None)
+        rec(0)
+        maps = shard.segment_maps(q, k, v, alpha, beta, segs)
+        rec(1)
+        if rank == 0:
+            s0 = torch.zeros((1, H, K, V), device=dev, dtype=torch.float32)
+            _, e0, _ = kernels.gdn2_span_fold(maps[0], maps[1], s0[0])
+            if world > 1:
+                shard.exchange_span_states(e0.unsqueeze(0), None, rank, world)
+            start = s0
+        else:
+            At, Bt = shard.compose_maps(*maps)
+            As, Bs = shard.exchange_span_states(At, Bt, rank, world)
+            start = shard.fold_span_states(Bs[0], As, Bs, rank)
+        rec(2)
+        out = shard.segmented_prefill(q, k, v, alpha, beta, segments=segs, maps=maps, start=start)
+        rec(3)
+        return out
 
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
-        step()
+    for i in range(args.steps):
+        step(evs[i])
     e1.record(stream)
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1)
+    phases = [statistics.mean(ev[j].elapsed_time(ev[j + 1]) for ev in evs) for j in range(3)]
     if world > 1:
-        tt = torch.tensor([ms], device=dev)
+        tt = torch.tensor([ms] + phases, device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms = tt.item()
+        ms, *phases = tt.tolist()
     ms_step = ms / args.steps
+    one_call_ms = None
+    if world == 1:
+        kernels.gdn2_prefill_segmented(q, k, v, alpha, beta, segments=segs)
+        torch.cuda.synchronize(dev)
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        for _ in range(args.steps):
+            kernels.gdn2_prefill_segmented(q, k, v, alpha, beta, segments=segs)
+        c1.record(stream)
+        torch.cuda.synchronize(dev)
+        one_call_ms = c0.elapsed_time(c1) / args.steps
     hbm, _, src = peaks()
     alg = t_total * H * BYTES_PER_TOKEN_HEAD + H * D * D * 4
-    return {"metric": "GDN-2 long-context prefill Mtok/s (config 4, time-sharded)",
-            "value": t_total / (ms_step / 1e3) / 1e6, "unit": "Mtok/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-            "higher_is_better": True, "scaling": "strong", "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"c4 B1/H{H}/T{t_total}/d{D} bf16 chunk {CHUNK}, time-sharded over {world} GPU(s)",
-                       "span_tokens": hi - lo, "segments_per_gpu": segs,
-                       "handoff": "all_gather of (A_g [H,K,K], B_g [H,K,V]) f32"},
-            "roofline": {"bound": "hbm", "algorithmic_bytes": alg, "achieved_gbs_aggregate": alg / (ms_step / 1e3) / 1e9,
-                         "peak_per_gpu": hbm, "peak_source": src}}
+    handoff_bytes = world * H * D * (D + D) * 4 if world > 1 else 0
+    return {"workload": f"c4 B1/H{H}/T{t_total}/d{D} bf16 chunk {CHUNK}, time-sharded over {world} GPU(s)",
+            "value": t_total / (ms_step / 1e3) / 1e6, "unit": "Mtok/s", "ms_per_step": ms_step,
+            "scaling": "strong", "span_tokens": hi - lo, "segments_per_gpu": segs,
+            "phases_ms": {"pass1_segment_maps": phases[0], "handoff_compose_allgather_fold": phases[1],
+                          "pass2_fold_and_rescan": phases[2]},
+            "handoff": "all_gather of (A_g [H,K,K], B_g [H,K,V]) f32 per rank",
+            "handoff_bytes_gathered_per_rank": handoff_bytes,
+            "one_call_ms": one_call_ms,
+            "roofline": {"bound": "hbm", "algorithmic_bytes": alg,
+                         "achieved_gbs_aggregate": alg / (ms_step / 1e3) / 1e9, "peak_per_gpu": hbm,
+                         "frac_of_aggregate_peak": alg / (ms_step / 1e3) / 1e9 / (hbm * world),
+                         "peak_source": src}}
 
 
-def bench_decode(torch, args, dev):
-    """Config 2: 256 sequences x 16 heads x 128^2 f32 state, 64 consecutive in-place steps."""
+def _max_over_ranks(torch, dist, world, dev, x):
+    if world > 1:
+        t = torch.tensor([x], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+    return x
+
+
+def bench_decode(torch, args, dev, dist=None, world=1):
+    """Config 2: 256 sequences x 16 heads x 128^2 f32 state, 64 consecutive in-place steps.  With N
+    ranks every rank decodes its own 256 sequences (sequence sharding, no communication): the time
+    is the max over ranks and the rate counts every rank's sequences."""
     import ctypes
 
     from delta_block_lm_b200 import _native as N
@@ -444,20 +513,23 @@ def bench_decode(torch, args, dev):
         run64()
     e1.record(stream)
     torch.cuda.synchronize(dev)
-    ms_step = e0.elapsed_time(e1) / (reps * steps)
+    ms_step = _max_over_ranks(torch, dist, world, dev, e0.elapsed_time(e1) / (reps * steps))
     hbm, _, src = peaks()
     alg = n * H * (2 * D * D * 4 + 3 * D * 2 + D * 2 + 8)
     gbs = alg / (ms_step / 1e3) / 1e9
-    return {"workload": f"c2 decode {n} seq x H{H} x {D}x{D} f32 state, {steps} steps (x{reps})",
-            "tok_per_s": n / (ms_step / 1e3), "us_per_step": ms_step * 1e3,
+    return {"workload": f"c2 decode {n} seq x H{H} x {D}x{D} f32 state per GPU, {steps} steps (x{reps}), "
+                        f"{world} GPU(s) sharded by sequence",
+            "tok_per_s": world * n / (ms_step / 1e3), "us_per_step": ms_step * 1e3, "scaling": "weak",
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
                          "peak_source": src, "algorithmic_bytes_per_launch": alg,
                          "traffic": ncu_traffic("gdn2_decode_c2")},
             "gpu_launches": reps * steps}
 
 
-def bench_relay(torch, args, dev):
-    """Config 3: shared 4096-token prefix + 64 x 1024 own tokens, H16, hd128, bf16, 1 query/seq."""
+def bench_relay(torch, args, dev, dist=None, world=1):
+    """Config 3: shared 4096-token prefix + 64 x 1024 own tokens, H16, hd128, bf16, 1 query/seq.
+    With N ranks every rank serves its own 64 sequences with a replica of the prefix (no
+    communication): the time is the max over ranks and the rate counts every rank's queries."""
     import delta_block_lm_b200 as dbl
 
     n, lp, lo = 64, 4096, 1024
@@ -478,16 +550,67 @@ def bench_relay(torch, args, dev):
         dbl.relay_merge_decode(q, kp, vp, ko, vo, out=out, workspace=ws, return_stats=False)
     e1.record(stream)
     torch.cuda.synchronize(dev)
-    ms = e0.elapsed_time(e1) / reps
+    ms = _max_over_ranks(torch, dist, world, dev, e0.elapsed_time(e1) / reps)
     hbm, _, src = peaks()
     alg = (2 * H * lp * D + 2 * n * H * lo * D + 2 * n * H * D) * 2
     gbs = alg / (ms / 1e3) / 1e9
-    return {"workload": f"c3 relay decode prefix {lp} + {n} x {lo} own, H{H}, hd{D}, bf16",
-            "queries_per_s": n * H / (ms / 1e3), "us_per_call": ms * 1e3,
+    return {"workload": f"c3 relay decode prefix {lp} + {n} x {lo} own per GPU, H{H}, hd{D}, bf16, "
+                        f"{world} GPU(s) sharded by sequence",
+            "queries_per_s": world * n * H / (ms / 1e3), "us_per_call": ms * 1e3, "scaling": "weak",
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
                          "peak_source": src, "algorithmic_bytes_per_launch": alg,
                          "traffic": ncu_traffic("relay_merge_c3")},
             "gpu_launches": reps}
+
+
+def _timed(torch, dev, fn, reps, warm=3):
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1) / reps
+
+
+def bench_config0(torch, dev):
+    """Config 0 (the reference's CPU-runnable case): B2/H4/T512/d64 f32, chunked prefill on the GPU.
+    Latency-bound (4.4 MB of traffic); reported as time and tokens/s, with no roofline claim."""
+    import delta_block_lm_b200 as dbl
+    b, t, h, d = 2, 512, 4, 64
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    q = torch.randn((b, t, h, d), device=dev, generator=g)
+    k = torch.randn((b, t, h, d), device=dev, generator=g)
+    q, k = q / q.norm(dim=-1, keepdim=True), k / k.norm(dim=-1, keepdim=True)
+    v = torch.randn((b, t, h, d), device=dev, generator=g)
+    beta = torch.sigmoid(torch.randn((b, t, h), device=dev, generator=g))
+    alpha = torch.exp(torch.nn.functional.logsigmoid(3.0 + torch.randn((b, t, h), device=dev, generator=g)))
+    ms = _timed(torch, dev, lambda: dbl.gdn2_prefill(q, k, v, alpha, beta), 50)
+    return {"workload": f"c0 B{b}/H{h}/T{t}/d{d} f32", "ms": ms, "mtok_s": b * t / (ms / 1e3) / 1e6,
+            "gpu_launches": 50}
+
+
+def bench_dropin_c1(torch, dev):
+    """The reference's own drop-in call, delta_kernels::gdn_training_scan (crates/kernels/src/
+    gdn_training_ops.rs:288-333, what scan_selected(FusedGdn2) calls), at the config-1 shape
+    B8/H16/T4096/K=V=128 bf16: channel-wise gate tensors (here the scalar gates broadcast over the
+    channels), valid / reset, initial state, f32 outputs and scores."""
+    import delta_block_lm_b200 as dbl
+    q, k, v, alpha, beta = make_prefill_inputs(torch, dev, 1234)
+    a = alpha[..., None].expand(B, T, H, D).contiguous()
+    e = beta[..., None].expand(B, T, H, D).contiguous()
+    valid, reset = torch.ones((B, T), device=dev), torch.zeros((B, T), device=dev)
+    init = torch.zeros((B, H, D, D), device=dev)
+    ms = _timed(torch, dev, lambda: dbl.gdn_training_scan(q / math.sqrt(D), k, v, a, e, e, valid, reset, init, 16),
+                reps=3, warm=1)
+    del a, e
+    return {"workload": f"gdn_training_scan B{B}/H{H}/T{T}/K=V={D} bf16, channel-wise gates, f32 outputs + scores",
+            "ms": ms, "mtok_s": B * T / (ms / 1e3) / 1e6, "gpu_launches": 4}
 
 
 def bench_backward(torch, args, dev):
@@ -708,7 +831,11 @@ def main():
     from delta_block_lm_b200 import _native
     _native.lib()
     if args.workload == "long":
-        line = bench_long(torch, dist, args, dev, rank, world)
+        r = bench_long(torch, dist, args, dev, rank, world)
+        line = {"metric": "GDN-2 long-context prefill Mtok/s (config 4, time-sharded)", "value": r["value"],
+                "unit": "Mtok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "strong", "dtype": "bf16",
+                "data": "synthetic", "config": {k_: v_ for k_, v_ in r.items() if k_ not in ("value", "ms_per_step")}}
         if rank == 0:
             print(json.dumps(line), flush=True)
         if world > 1:
@@ -756,9 +883,18 @@ def main():
             "config": res["config"], "clocks": res["clocks"], "e2e": res["e2e"],
             "gpu_launches": res["gpu_launches"], "roofline": res["roofline"],
             "kernel_ms_per_launch": res["launch_ms"]}
+    if not args.no_secondary:
+        # every rank takes part: decode and relay as sequence-sharded replicas, config 4 through the
+        # time-sharded hand-off (the only collective)
+        sec = {"decode": bench_decode(torch, args, dev, dist, world), "relay": bench_relay(torch, args, dev, dist, world),
+               "long": bench_long(torch, dist, argparse.Namespace(**{**vars(args), "steps": 5, "warmup": 3}), dev,
+                                  rank, world)}
+        if rank == 0:
+            line["secondary"] = sec
     if world == 1 and rank == 0:
         if not args.no_secondary:
-            line["secondary"] = {"decode": bench_decode(torch, args, dev), "relay": bench_relay(torch, args, dev)}
+            line["secondary"]["config0"] = bench_config0(torch, dev)
+            line["secondary"]["training_scan_c1_dropin"] = bench_dropin_c1(torch, dev)
             # the training scan at the reference's training shape (the backward workload's line,
             # without its CPU sample)
             tr = bench_backward(torch, argparse.Namespace(**{**vars(args), "no_cpu_baseline": True}), dev)

@@ -155,6 +155,14 @@ EXPORTS = [
     ("dbl_relay_merge_decode_noalloc", ctypes.c_int, [ctypes.POINTER(RelayMergeArgs), _vp]),
     ("dbl_relay_merge_call_workspace_bytes", ctypes.c_size_t, [ctypes.POINTER(RelayMergeArgs)]),
     ("dbl_relay_attention_forward", ctypes.c_int, [ctypes.POINTER(RelayAttentionArgs), _vp]),
+    ("dbl_gdn2_span_fold", ctypes.c_int, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp]),
+    ("dbl_gdn2_prefill_segmented_workspace_bytes", ctypes.c_size_t, [ctypes.POINTER(PrefillArgs), _i64]),
+    ("dbl_gdn2_prefill_segmented", ctypes.c_int, [ctypes.POINTER(PrefillArgs), _i64, _vp, ctypes.c_size_t, _vp]),
+    ("dbl_gdn2_prefill_time_sharded_workspace_bytes", ctypes.c_size_t,
+     [ctypes.POINTER(PrefillArgs), ctypes.c_int, _i64]),
+    ("dbl_gdn2_prefill_time_sharded", ctypes.c_int,
+     [ctypes.POINTER(PrefillArgs), ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(_vp), _i64,
+      ctypes.POINTER(_vp), ctypes.POINTER(ctypes.c_size_t)]),
 ]
 
 RELAY_NOALLOC_SCRATCH_BYTES = 16 << 20  # DBL_RELAY_NOALLOC_SCRATCH_BYTES

@@ -1,0 +1,448 @@
+// Long-sequence prefill by time segments: the span-map fold, the one-device
+// segmented prefill and the multi-device time-sharded prefill driven from one host thread.
+//
+// Over a token span the GDN-2 state map is affine: S_end = A S_start + B, with A the K x K span
+// transition (dbl_gdn2_span_transition: the scan of the span from S = I with zero values) and B
+// the scan of the span from a zero state.  A span of T tokens is cut into `segments` equal
+// segments that run as a batch (a strided [segments, T/segments, H, D] view of the same memory),
+// so segments x H CTAs of the tensor-core prefill share the GPU instead of H:
+//   pass 1  the maps (A_s, B_s) of every segment (two batched launches);
+//   fold    the start state of every segment, X_{s+1} = A_s X_s + B_s (span_fold_kernel);
+//   pass 2  every segment rescanned from its start state (one batched launch).
+// Across devices, device g holds time span g.  Each device composes its span's map
+// (A_g, B_g) = fold of its segment maps; device 0 instead folds its maps from the sequence's initial
+// state to its end state E_0.  Device g pulls E_0 and the maps of devices 1 .. g-1 with one
+// cudaMemcpyPeerAsync each (ordered after the producing device's event), folds them into its start
+// state and runs its own fold and pass 2.  Peer memory is only read by copies, never by a kernel.
+// The reference has no time-parallel or multi-device code; this file is the B200 build's own.
+#include <vector>
+
+#include "common.cuh"
+
+namespace dbl {
+
+int prefill_dispatch(const dbl_prefill_args* a, int mode, float* transition, cudaStream_t st);
+
+namespace {
+
+constexpr int kFoldCols = 16;    // value columns per CTA
+constexpr int kFoldThreads = 256;  // thread t: state row t / 2, columns 8 (t % 2) .. + 8
+constexpr int kChunk = 64;
+
+struct FoldParams {
+    int S, H, K, V;
+    const float* A;    // [S][H][K][K]
+    const float* B;    // [S][H][K][V] or null (zero offsets)
+    const float* X0;   // [H][K][V] or null (zeros); ignored when x0_identity
+    int x0_identity;   // X_0 = I (V == K)
+    float* starts;     // [S][H][K][V] or null: X_0 .. X_{S-1}
+    float* end;        // [H][K][V] or null: X_S
+};
+
+// X_{s+1} = A_s X_s + B_s for s = 0 .. S-1, one CTA per (16 value columns, head).  f32 FMAs: the
+// fold is short (S <= a few dozen steps of a K x K by K x 16 product) and its errors would reach
+// every later state, so it stays in full f32.
+__global__ void __launch_bounds__(kFoldThreads) span_fold_kernel(const FoldParams p) {
+    __shared__ __align__(16) float sX[128 * kFoldCols];
+    const int h = blockIdx.y, c0 = blockIdx.x * kFoldCols;
+    const int t = threadIdx.x, i = t >> 1, half = (t & 1) * 8;
+    const bool row = i < p.K;
+    const size_t xb = (size_t)h * p.K * p.V;
+    for (int e = t; e < p.K * kFoldCols; e += kFoldThreads) {
+        const int r = e / kFoldCols, c = e % kFoldCols;
+        float x = 0.f;
+        if (p.x0_identity) x = (r == c0 + c) ? 1.f : 0.f;
+        else if (p.X0) x = p.X0[xb + (size_t)r * p.V + c0 + c];
+        sX[e] = x;
+    }
+    __syncthreads();
+    for (int s = 0; s < p.S; ++s) {
+        const size_t sb = ((size_t)s * p.H + h) * p.K * p.V;
+        float acc[8];
+        if (row) {
+            const float4* xr = reinterpret_cast<const float4*>(sX + i * kFoldCols + half);
+            if (p.starts) {
+                float4* dst = reinterpret_cast<float4*>(p.starts + sb + (size_t)i * p.V + c0 + half);
+                dst[0] = xr[0];
+                dst[1] = xr[1];
+            }
+            if (p.B) {
+                const float4* b4 = reinterpret_cast<const float4*>(p.B + sb + (size_t)i * p.V + c0 + half);
+                const float4 u = b4[0], w = b4[1];
+                acc[0] = u.x, acc[1] = u.y, acc[2] = u.z, acc[3] = u.w;
+                acc[4] = w.x, acc[5] = w.y, acc[6] = w.z, acc[7] = w.w;
+            } else {
+#pragma unroll
+                for (int c = 0; c < 8; ++c) acc[c] = 0.f;
+            }
+            const float4* ar = reinterpret_cast<const float4*>(p.A + (((size_t)s * p.H + h) * p.K + i) * p.K);
+            for (int k4 = 0; k4 < p.K / 4; ++k4) {
+                const float4 a = ar[k4];
+                const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const float4* xk = reinterpret_cast<const float4*>(sX + (4 * k4 + kk) * kFoldCols + half);
+                    const float4 x0 = xk[0], x1 = xk[1];
+                    acc[0] = fmaf(av[kk], x0.x, acc[0]);
+                    acc[1] = fmaf(av[kk], x0.y, acc[1]);
+                    acc[2] = fmaf(av[kk], x0.z, acc[2]);
+                    acc[3] = fmaf(av[kk], x0.w, acc[3]);
+                    acc[4] = fmaf(av[kk], x1.x, acc[4]);
+                    acc[5] = fmaf(av[kk], x1.y, acc[5]);
+                    acc[6] = fmaf(av[kk], x1.z, acc[6]);
+                    acc[7] = fmaf(av[kk], x1.w, acc[7]);
+                }
+            }
+        }
+        __syncthreads();
+        if (row) {
+            float4* xw = reinterpret_cast<float4*>(sX + i * kFoldCols + half);
+            xw[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            xw[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        }
+        __syncthreads();
+    }
+    if (p.end && row) {
+        const float4* xr = reinterpret_cast<const float4*>(sX + i * kFoldCols + half);
+        float4* dst = reinterpret_cast<float4*>(p.end + xb + (size_t)i * p.V + c0 + half);
+        dst[0] = xr[0];
+        dst[1] = xr[1];
+    }
+}
+
+int fold_launch(const FoldParams& p, cudaStream_t st) {
+    if (p.K <= 0 || p.K > 128 || p.K % 4 != 0 || p.V <= 0 || p.V % kFoldCols != 0 || p.H <= 0 || p.S < 0)
+        return fail(DBL_ERR_UNSUPPORTED, "span fold: key width must be a multiple of 4 up to 128 and value width a multiple of 16");
+    if (p.x0_identity && p.V != p.K) return fail(DBL_ERR_INVALID_ARGUMENT, "span fold: identity start needs V == K");
+    for (const void* ptr : {static_cast<const void*>(p.A), static_cast<const void*>(p.B), static_cast<const void*>(p.X0),
+                            static_cast<const void*>(p.starts), static_cast<const void*>(p.end)})
+        if (ptr && !aligned(ptr, 16)) return fail(DBL_ERR_INVALID_ARGUMENT, "span fold: arrays must be 16-byte aligned");
+    if (p.S > 0 && !p.A) return fail(DBL_ERR_INVALID_ARGUMENT, "span fold: transitions are required");
+    if (p.H > 65535) return fail(DBL_ERR_UNSUPPORTED, "span fold: at most 65535 heads");
+    const dim3 grid((unsigned)(p.V / kFoldCols), (unsigned)p.H);
+    span_fold_kernel<<<grid, kFoldThreads, 0, st>>>(p);
+    return launch_status("span_fold_kernel");
+}
+
+// Segment maps and fold scratch of one span: A [S,H,K,K], B [S,H,K,V] (reused for the rescan's
+// final states), starts [S,H,K,V].
+struct SegLayout {
+    size_t off_a, off_b, off_starts, total;
+};
+
+SegLayout seg_layout(int64_t S, int64_t H, int64_t K, int64_t V) {
+    auto up = [](size_t x) { return (x + 255) / 256 * 256; };
+    SegLayout L{};
+    L.off_a = 0;
+    L.off_b = up(L.off_a + (size_t)S * H * K * K * 4);
+    L.off_starts = up(L.off_b + (size_t)S * H * K * V * 4);
+    L.total = up(L.off_starts + (size_t)S * H * K * V * 4);
+    return L;
+}
+
+int sm_count_current(int* out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(out, cudaDevAttrMultiProcessorCount, dev);
+    return cuda_status(e, "SM count");
+}
+
+// Segments of a span: the largest power of two S with S x heads <= SMs and whole 64-token chunks
+// per segment (1 when the span is short or the heads alone fill the device).
+int64_t pick_segments(int64_t T, int64_t H, int sms) {
+    int64_t s = 1;
+    while ((s * 2) * H <= sms && T % (s * 2 * kChunk) == 0) s *= 2;
+    return s;
+}
+
+int check_span(const dbl_prefill_args* a, const char* who) {
+    if (!a) return fail(DBL_ERR_INVALID_ARGUMENT, "%s: null args", who);
+    if (a->batch != 1) return fail(DBL_ERR_UNSUPPORTED, "%s: one sequence (batch 1) per span", who);
+    if (a->time <= 0 || a->heads <= 0 || a->key_dim <= 0 || a->value_dim <= 0)
+        return fail(DBL_ERR_INVALID_ARGUMENT, "%s: GDN-2 requires nonempty axes", who);
+    if (!a->q || !a->k || !a->v || !a->alpha || !a->beta)
+        return fail(DBL_ERR_INVALID_ARGUMENT, "%s: q, k, v, alpha and beta are required", who);
+    return DBL_OK;
+}
+
+// `a` viewed as S equal segments of its one sequence: batch S, time T / S, the same memory.
+dbl_prefill_args segment_view(const dbl_prefill_args* a, int64_t S) {
+    dbl_prefill_args v = *a;
+    const int64_t Ts = a->time / S;
+    const int64_t dk[4] = {a->batch, a->time, a->heads, a->key_dim};
+    const int64_t dv[4] = {a->batch, a->time, a->heads, a->value_dim};
+    const int64_t dg[3] = {a->batch, a->time, a->heads};
+    int64_t st[4];
+    resolve_strides(a->q_stride, dk, 4, st);
+    v.q_stride[0] = Ts * st[1], v.q_stride[1] = st[1], v.q_stride[2] = st[2], v.q_stride[3] = st[3];
+    resolve_strides(a->k_stride, dk, 4, st);
+    v.k_stride[0] = Ts * st[1], v.k_stride[1] = st[1], v.k_stride[2] = st[2], v.k_stride[3] = st[3];
+    resolve_strides(a->v_stride, dv, 4, st);
+    v.v_stride[0] = Ts * st[1], v.v_stride[1] = st[1], v.v_stride[2] = st[2], v.v_stride[3] = st[3];
+    resolve_strides(a->out_stride, dv, 4, st);
+    v.out_stride[0] = Ts * st[1], v.out_stride[1] = st[1], v.out_stride[2] = st[2], v.out_stride[3] = st[3];
+    resolve_strides(a->alpha_stride, dg, 3, st);
+    v.alpha_stride[0] = Ts * st[1], v.alpha_stride[1] = st[1], v.alpha_stride[2] = st[2];
+    resolve_strides(a->beta_stride, dg, 3, st);
+    v.beta_stride[0] = Ts * st[1], v.beta_stride[1] = st[1], v.beta_stride[2] = st[2];
+    v.batch = S;
+    v.time = Ts;
+    // valid / reset are [1, T] contiguous, i.e. already [S, T / S] contiguous
+    v.initial_state = nullptr;
+    v.final_state = nullptr;
+    v.out = nullptr;
+    return v;
+}
+
+// Pass 1: the maps of every segment into the workspace.
+int segment_maps(const dbl_prefill_args* a, int64_t S, unsigned char* ws, const SegLayout& L, cudaStream_t st) {
+    dbl_prefill_args v = segment_view(a, S);
+    float* A = reinterpret_cast<float*>(ws + L.off_a);
+    float* Bm = reinterpret_cast<float*>(ws + L.off_b);
+    int rc = prefill_dispatch(&v, 1, A, st);
+    if (rc != DBL_OK) return rc;
+    v.final_state = Bm;
+    return prefill_dispatch(&v, 0, nullptr, st);
+}
+
+// Fold of the segment maps from `start` (null = zeros) into the segment starts; `end` (optional)
+// receives the state after the last segment.
+int segment_starts(const dbl_prefill_args* a, int64_t S, unsigned char* ws, const SegLayout& L, const float* start,
+                   float* end, cudaStream_t st) {
+    FoldParams f{};
+    f.S = (int)S, f.H = (int)a->heads, f.K = (int)a->key_dim, f.V = (int)a->value_dim;
+    f.A = reinterpret_cast<const float*>(ws + L.off_a);
+    f.B = reinterpret_cast<const float*>(ws + L.off_b);
+    f.X0 = start;
+    f.starts = reinterpret_cast<float*>(ws + L.off_starts);
+    f.end = end;
+    return fold_launch(f, st);
+}
+
+// Pass 2: every segment rescanned from its start state; the last segment's final state goes to
+// a->final_state.
+int segment_rescan(const dbl_prefill_args* a, int64_t S, unsigned char* ws, const SegLayout& L, cudaStream_t st) {
+    dbl_prefill_args v = segment_view(a, S);
+    v.initial_state = reinterpret_cast<const float*>(ws + L.off_starts);
+    v.out = a->out;
+    float* fin = reinterpret_cast<float*>(ws + L.off_b);  // the offsets are consumed by the fold
+    v.final_state = a->final_state ? fin : nullptr;
+    int rc = prefill_dispatch(&v, 0, nullptr, st);
+    if (rc != DBL_OK || !a->final_state) return rc;
+    const size_t state = (size_t)a->heads * a->key_dim * a->value_dim;
+    return cuda_status(cudaMemcpyAsync(a->final_state, fin + (size_t)(S - 1) * state, state * sizeof(float),
+                                       cudaMemcpyDeviceToDevice, st),
+                       "segmented prefill: final state");
+}
+
+int resolve_segments(const dbl_prefill_args* a, int64_t segments, int64_t* out) {
+    int64_t S = segments;
+    if (S == 0) {
+        int sms = 0;
+        int rc = sm_count_current(&sms);
+        if (rc != DBL_OK) return rc;
+        S = pick_segments(a->time, a->heads, sms);
+    }
+    if (S < 1 || a->time % S != 0)
+        return fail(DBL_ERR_INVALID_ARGUMENT, "segmented prefill: %lld segments do not divide %lld tokens",
+                    (long long)S, (long long)a->time);
+    *out = S;
+    return DBL_OK;
+}
+
+}  // namespace
+}  // namespace dbl
+
+extern "C" int dbl_gdn2_span_fold(const float* transition, const float* offset, int64_t segments, int64_t heads,
+                                  int64_t key_dim, int64_t value_dim, const float* start, float* starts, float* end,
+                                  float* composed_transition, dbl_stream_t stream) {
+    using namespace dbl;
+    if (segments < 0 || heads <= 0 || key_dim <= 0 || value_dim <= 0)
+        return fail(DBL_ERR_INVALID_ARGUMENT, "span fold: nonempty heads and widths, segments >= 0");
+    if (segments > 0x7fffffff || heads > 0x7fffffff)
+        return fail(DBL_ERR_UNSUPPORTED, "span fold: axis exceeds 32-bit limits");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    FoldParams f{};
+    f.S = (int)segments, f.H = (int)heads, f.K = (int)key_dim;
+    f.A = transition;
+    int rc = DBL_OK;
+    if (composed_transition) {
+        f.V = (int)key_dim;
+        f.x0_identity = 1;
+        f.end = composed_transition;
+        rc = fold_launch(f, st);
+        if (rc != DBL_OK) return rc;
+    }
+    if (starts || end) {
+        f.V = (int)value_dim;
+        f.x0_identity = 0;
+        f.B = offset;
+        f.X0 = start;
+        f.starts = starts;
+        f.end = end;
+        rc = fold_launch(f, st);
+    }
+    return rc;
+}
+
+extern "C" size_t dbl_gdn2_prefill_segmented_workspace_bytes(const dbl_prefill_args* a, int64_t segments) {
+    using namespace dbl;
+    if (check_span(a, "segmented prefill") != DBL_OK) return 0;
+    int64_t S = 0;
+    if (resolve_segments(a, segments, &S) != DBL_OK) return 0;
+    return seg_layout(S, a->heads, a->key_dim, a->value_dim).total;
+}
+
+extern "C" int dbl_gdn2_prefill_segmented(const dbl_prefill_args* a, int64_t segments, void* workspace,
+                                          size_t workspace_bytes, dbl_stream_t stream) {
+    using namespace dbl;
+    int rc = check_span(a, "segmented prefill");
+    if (rc != DBL_OK) return rc;
+    int64_t S = 0;
+    rc = resolve_segments(a, segments, &S);
+    if (rc != DBL_OK) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (S == 1) return dbl_gdn2_prefill(a, stream);
+    const SegLayout L = seg_layout(S, a->heads, a->key_dim, a->value_dim);
+    if (!workspace || workspace_bytes < L.total)
+        return fail(DBL_ERR_WORKSPACE, "segmented prefill: workspace of %zu bytes required (got %zu)", L.total,
+                    workspace_bytes);
+    if (!aligned(workspace, 256)) return fail(DBL_ERR_INVALID_ARGUMENT, "segmented prefill: workspace must be 256-byte aligned");
+    unsigned char* ws = static_cast<unsigned char*>(workspace);
+    rc = segment_maps(a, S, ws, L, st);
+    if (rc == DBL_OK) rc = segment_starts(a, S, ws, L, a->initial_state, nullptr, st);
+    if (rc == DBL_OK) rc = segment_rescan(a, S, ws, L, st);
+    return rc;
+}
+
+// ------------------------------------------------------------------------------ multi-device
+namespace dbl {
+namespace {
+
+// Per-device workspace: the segment layout, then the span map slots of every device
+// (transition [n][H][K][K], offset [n][H][K][V]; slot 0's offset is device 0's end state) and the
+// device's start state [H][K][V].
+struct ShardLayout {
+    SegLayout seg;
+    size_t off_ga, off_gb, off_sin, total;
+};
+
+ShardLayout shard_layout(int64_t S, int n, int64_t H, int64_t K, int64_t V) {
+    auto up = [](size_t x) { return (x + 255) / 256 * 256; };
+    ShardLayout L{};
+    L.seg = seg_layout(S, H, K, V);
+    L.off_ga = L.seg.total;
+    L.off_gb = up(L.off_ga + (size_t)n * H * K * K * 4);
+    L.off_sin = up(L.off_gb + (size_t)n * H * K * V * 4);
+    L.total = up(L.off_sin + (size_t)H * K * V * 4);
+    return L;
+}
+
+// Restores the calling thread's device when the multi-device call returns.
+struct DeviceGuard {
+    int saved = -1;
+    DeviceGuard() { cudaGetDevice(&saved); }
+    ~DeviceGuard() {
+        if (saved >= 0) cudaSetDevice(saved);
+    }
+};
+
+}  // namespace
+}  // namespace dbl
+
+extern "C" size_t dbl_gdn2_prefill_time_sharded_workspace_bytes(const dbl_prefill_args* span, int n_gpus,
+                                                                 int64_t segments) {
+    using namespace dbl;
+    if (n_gpus < 1 || check_span(span, "time-sharded prefill") != DBL_OK) return 0;
+    int64_t S = 0;
+    if (resolve_segments(span, segments, &S) != DBL_OK) return 0;
+    return shard_layout(S, n_gpus, span->heads, span->key_dim, span->value_dim).total;
+}
+
+extern "C" int dbl_gdn2_prefill_time_sharded(const dbl_prefill_args* spans, int n_gpus, const int* devices,
+                                             dbl_stream_t const* streams, int64_t segments, void* const* workspaces,
+                                             const size_t* workspace_bytes) {
+    using namespace dbl;
+    if (!spans || !devices || !streams || !workspaces || !workspace_bytes || n_gpus < 1)
+        return fail(DBL_ERR_INVALID_ARGUMENT, "time-sharded prefill: spans, devices, streams and workspaces are required");
+    const int64_t H = spans[0].heads, K = spans[0].key_dim, V = spans[0].value_dim;
+    for (int g = 0; g < n_gpus; ++g) {
+        int rc = check_span(&spans[g], "time-sharded prefill");
+        if (rc != DBL_OK) return rc;
+        if (spans[g].heads != H || spans[g].key_dim != K || spans[g].value_dim != V || spans[g].dtype != spans[0].dtype)
+            return fail(DBL_ERR_INVALID_ARGUMENT, "time-sharded prefill: every span needs the same heads, widths and dtype");
+    }
+    std::vector<int64_t> S(n_gpus);
+    std::vector<ShardLayout> L(n_gpus);
+    DeviceGuard guard;
+    for (int g = 0; g < n_gpus; ++g) {
+        int rc = cuda_status(cudaSetDevice(devices[g]), "time-sharded prefill: cudaSetDevice");
+        if (rc == DBL_OK) rc = resolve_segments(&spans[g], segments, &S[g]);
+        if (rc != DBL_OK) return rc;
+        L[g] = shard_layout(S[g], n_gpus, H, K, V);
+        if (!workspaces[g] || workspace_bytes[g] < L[g].total)
+            return fail(DBL_ERR_WORKSPACE, "time-sharded prefill: device %d needs a workspace of %zu bytes (got %zu)", g,
+                        L[g].total, workspace_bytes[g]);
+        if (!aligned(workspaces[g], 256))
+            return fail(DBL_ERR_INVALID_ARGUMENT, "time-sharded prefill: workspaces must be 256-byte aligned");
+    }
+    const size_t tbytes = (size_t)H * K * K * 4, obytes = (size_t)H * K * V * 4;
+    std::vector<cudaEvent_t> ready(n_gpus, nullptr);
+    auto cleanup = [&](int rc) {
+        for (cudaEvent_t e : ready)
+            if (e) cudaEventDestroy(e);
+        return rc;
+    };
+    // pass 1 and the span maps (device 0: its end state) on every device
+    for (int g = 0; g < n_gpus; ++g) {
+        unsigned char* ws = static_cast<unsigned char*>(workspaces[g]);
+        cudaStream_t st = reinterpret_cast<cudaStream_t>(streams[g]);
+        int rc = cuda_status(cudaSetDevice(devices[g]), "time-sharded prefill: cudaSetDevice");
+        if (rc == DBL_OK) rc = segment_maps(&spans[g], S[g], ws, L[g].seg, st);
+        float* ga = reinterpret_cast<float*>(ws + L[g].off_ga) + (size_t)g * H * K * K;
+        float* gb = reinterpret_cast<float*>(ws + L[g].off_gb) + (size_t)g * H * K * V;
+        if (rc == DBL_OK && g == 0) {
+            rc = segment_starts(&spans[0], S[0], ws, L[0].seg, spans[0].initial_state, gb, st);
+        } else if (rc == DBL_OK) {
+            rc = dbl_gdn2_span_fold(reinterpret_cast<const float*>(ws + L[g].seg.off_a),
+                                    reinterpret_cast<const float*>(ws + L[g].seg.off_b), S[g], H, K, V, nullptr, nullptr,
+                                    gb, ga, streams[g]);
+        }
+        if (rc == DBL_OK) rc = cuda_status(cudaEventCreateWithFlags(&ready[g], cudaEventDisableTiming), "event");
+        if (rc == DBL_OK) rc = cuda_status(cudaEventRecord(ready[g], st), "event record");
+        if (rc != DBL_OK) return cleanup(rc);
+    }
+    // hand-off: device g pulls the map slots of devices 0 .. g-1, folds its start state, then runs
+    // its own fold and the rescan
+    for (int g = 0; g < n_gpus; ++g) {
+        unsigned char* ws = static_cast<unsigned char*>(workspaces[g]);
+        cudaStream_t st = reinterpret_cast<cudaStream_t>(streams[g]);
+        int rc = cuda_status(cudaSetDevice(devices[g]), "time-sharded prefill: cudaSetDevice");
+        float* ga = reinterpret_cast<float*>(ws + L[g].off_ga);
+        float* gb = reinterpret_cast<float*>(ws + L[g].off_gb);
+        for (int r = 0; r < g && rc == DBL_OK; ++r) {
+            const unsigned char* src = static_cast<const unsigned char*>(workspaces[r]);
+            rc = cuda_status(cudaStreamWaitEvent(st, ready[r], 0), "time-sharded prefill: wait for device");
+            if (rc == DBL_OK && r > 0)
+                rc = cuda_status(cudaMemcpyPeerAsync(ga + (size_t)r * H * K * K, devices[g],
+                                                     src + L[r].off_ga + (size_t)r * tbytes, devices[r], tbytes, st),
+                                 "time-sharded prefill: transition hand-off");
+            if (rc == DBL_OK)
+                rc = cuda_status(cudaMemcpyPeerAsync(gb + (size_t)r * H * K * V, devices[g],
+                                                     src + L[r].off_gb + (size_t)r * obytes, devices[r], obytes, st),
+                                 "time-sharded prefill: state hand-off");
+        }
+        if (rc != DBL_OK) return cleanup(rc);
+        if (g > 0) {
+            // S_in(g) = fold of the maps of devices 1 .. g-1 from device 0's end state
+            float* sin = reinterpret_cast<float*>(ws + L[g].off_sin);
+            rc = dbl_gdn2_span_fold(ga + (size_t)H * K * K, gb + (size_t)H * K * V, g - 1, H, K, V, gb, nullptr, sin,
+                                    nullptr, streams[g]);
+            if (rc == DBL_OK) rc = segment_starts(&spans[g], S[g], ws, L[g].seg, sin, nullptr, st);
+            if (rc != DBL_OK) return cleanup(rc);
+        }
+        rc = segment_rescan(&spans[g], S[g], ws, L[g].seg, st);
+        if (rc != DBL_OK) return cleanup(rc);
+    }
+    return cleanup(DBL_OK);
+}

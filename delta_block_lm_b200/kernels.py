@@ -454,6 +454,111 @@ def gdn2_span_transition(k, alpha, beta, *, valid=None, reset=None, transition=N
     return transition
 
 
+def gdn2_span_fold(transition, offset=None, start=None, *, want_starts=False, want_end=True,
+                   want_composed=False):
+    """Fold of consecutive span maps: X_{s+1} = transition[s] X_s + offset[s], X_0 = start.
+
+    transition [S,H,K,K], offset [S,H,K,V] (None = zeros), start [H,K,V] (None = zeros), f32.
+    Returns (starts [S,H,K,V] or None, end [H,K,V] or None, composed [H,K,K] or None): the start
+    state of every span, the state after the last span and the composed transition
+    transition[S-1] ... transition[0]."""
+    dev = _require_cuda(transition, offset, start)
+    S, H, K, _ = transition.shape
+    V = offset.shape[3] if offset is not None else (start.shape[2] if start is not None else K)
+    with torch.cuda.device(dev):
+        transition = _f32c(transition)
+        offset = None if offset is None else _f32c(offset)
+        start = None if start is None else _f32c(start).reshape(H, K, V)
+        starts = torch.empty((S, H, K, V), device=dev, dtype=torch.float32) if want_starts else None
+        end = torch.empty((H, K, V), device=dev, dtype=torch.float32) if want_end else None
+        comp = torch.empty((H, K, K), device=dev, dtype=torch.float32) if want_composed else None
+        N.check(N.lib().dbl_gdn2_span_fold(_ptr(transition), _ptr(offset), S, H, K, V, _ptr(start), _ptr(starts),
+                                           _ptr(end), _ptr(comp), _stream(dev)))
+    return starts, end, comp
+
+
+def gdn2_prefill_segmented(q, k, v, alpha, beta, *, segments: int = 0, scale: Optional[float] = None,
+                           valid=None, reset=None, initial_state=None, out=None, final_state=None):
+    """``gdn2_prefill`` of ONE long sequence (batch 1) on one device by time segments (pass 1 the
+    segment maps, a fold of their start states, pass 2 the rescan), in one C-ABI call
+    (dbl_gdn2_prefill_segmented).  segments = 0 picks the largest power of two with segments x H
+    <= the device's SM count.  Returns (out [1,T,H,V], final_state [1,H,K,V])."""
+    dev = _require_cuda(q, k, v, alpha, beta, valid, reset, initial_state, out, final_state)
+    _check_prefill_inputs(q, k, v, alpha, beta, valid, reset)
+    B, T, H, K = q.shape
+    V = v.shape[3]
+    if B != 1:
+        raise ValueError("gdn2_prefill_segmented handles one sequence (batch 1)")
+    if scale is None:
+        scale = 1.0 / math.sqrt(K)
+    with torch.cuda.device(dev):
+        if valid is not None:
+            valid, reset = _f32c(valid), _f32c(reset)
+        if initial_state is not None:
+            initial_state = _f32c(initial_state)
+        if out is None:
+            out = torch.empty((B, T, H, V), device=dev, dtype=q.dtype)
+        if final_state is None:
+            final_state = torch.empty((B, H, K, V), device=dev, dtype=torch.float32)
+        a = _prefill_args(q, k, v, alpha, beta, scale, valid, reset, initial_state, out, final_state, 64)
+        L = N.lib()
+        need = int(L.dbl_gdn2_prefill_segmented_workspace_bytes(ctypes.byref(a), segments))
+        ws = torch.empty(max(need, 256), device=dev, dtype=torch.uint8)
+        N.check(L.dbl_gdn2_prefill_segmented(ctypes.byref(a), segments, _ptr(ws), need, _stream(dev)))
+    return out, final_state
+
+
+def gdn2_prefill_time_sharded_devices(spans, *, segments: int = 0, scale: Optional[float] = None,
+                                      initial_state=None):
+    """ONE long sequence sharded along time over several devices of this process, through the
+    C-ABI's multi-device entry point (dbl_gdn2_prefill_time_sharded): ``spans`` is a list of
+    (q, k, v, alpha, beta) tuples, the consecutive time spans of the sequence, each on its own
+    device (batch 1).  Each device runs on its current stream; the span maps cross devices by peer
+    copies.  Returns ([out_g per span], final_state on the last span's device)."""
+    n = len(spans)
+    args, devs, streams, wss, sizes, outs, keep = [], [], [], [], [], [], []
+    fin = None
+    for g, (q, k, v, alpha, beta) in enumerate(spans):
+        dev = _require_cuda(q, k, v, alpha, beta)
+        _check_prefill_inputs(q, k, v, alpha, beta, None, None)
+        _, T, H, K = q.shape
+        V = v.shape[3]
+        sc = 1.0 / math.sqrt(K) if scale is None else scale
+        with torch.cuda.device(dev):
+            out = torch.empty((1, T, H, V), device=dev, dtype=q.dtype)
+            init = _f32c(initial_state) if (g == 0 and initial_state is not None) else None
+            if g == n - 1:
+                fin = torch.empty((1, H, K, V), device=dev, dtype=torch.float32)
+            a = _prefill_args(q, k, v, alpha, beta, sc, None, None, init, out, fin if g == n - 1 else None, 64)
+            need = int(N.lib().dbl_gdn2_prefill_time_sharded_workspace_bytes(ctypes.byref(a), n, segments))
+            ws = torch.empty(max(need, 256), device=dev, dtype=torch.uint8)
+            stream = torch.cuda.current_stream(dev)
+        args.append(a)
+        devs.append(dev.index)
+        streams.append(stream.cuda_stream)
+        wss.append(ws.data_ptr())
+        sizes.append(need)
+        outs.append(out)
+        keep += [ws, init]
+    arr = (N.PrefillArgs * n)(*args)
+    N.check(N.lib().dbl_gdn2_prefill_time_sharded(
+        arr, n, (ctypes.c_int * n)(*devs), (ctypes.c_void_p * n)(*streams), segments,
+        (ctypes.c_void_p * n)(*wss), (ctypes.c_size_t * n)(*sizes)))
+    # device g's stream reads the workspaces of devices 0 .. g-1 (peer copies): every device's
+    # stream waits for every other one, so a workspace freed below is not reused before those reads
+    done = []
+    for q, *_rest in spans:
+        with torch.cuda.device(q.device):
+            e = torch.cuda.Event()
+            e.record(torch.cuda.current_stream(q.device))
+            done.append(e)
+    for q, *_rest in spans:
+        for e in done:
+            torch.cuda.current_stream(q.device).wait_event(e)
+    del keep
+    return outs, fin
+
+
 def gdn2_decode_step(q, k, v, alpha, beta, state, *, scale: Optional[float] = None, out=None):
     """One recurrent step for N sequences; ``state`` [N,H,K,V] f32 is updated IN PLACE.
 

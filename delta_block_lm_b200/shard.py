@@ -7,8 +7,10 @@
   and B the scan of the span from a zero state.  A long span is cut into S segments that run as a
   batch (a strided [S, T/S, H, D] view of the same memory, so S x H CTAs fill the GPU):
       pass 1  all segment maps (A_s, B_s) in two batched launches;
-      fold    the start state of every segment by composing the maps before it (tiny);
+      fold    the start state of every segment by composing the maps before it (one small
+              kernel, dbl_gdn2_span_fold);
       pass 2  every segment rescanned from its exact start state in one batched launch.
+  On one device the three steps are one C-ABI call (dbl_gdn2_prefill_segmented).
   Across GPUs, rank g holds the contiguous span g; the ranks exchange their composed span maps
   with one ``all_gather`` (the only collective) and each rank folds the maps of the ranks before it
   into its own start state before the local fold.
@@ -42,7 +44,16 @@ def shard_batch(q, k, v, alpha, beta, *, group=None, **kw):
 def fold_span_states(first_state: torch.Tensor, transitions: Sequence[torch.Tensor],
                      offsets: Sequence[torch.Tensor], upto: int) -> torch.Tensor:
     """S_in(upto) from S_in(1) = first_state and the spans 1 .. upto-1:
-    S_in(g + 1) = A_g S_in(g) + B_g  (A_g [B,H,K,K], B_g / states [B,H,K,V], f32)."""
+    S_in(g + 1) = A_g S_in(g) + B_g  (A_g [B,H,K,K], B_g / states [B,H,K,V], f32).  On CUDA
+    tensors this is one fold kernel (kernels.gdn2_span_fold); on CPU tensors (the gloo tests) the
+    same recurrence in torch."""
+    if upto <= 1:
+        return first_state
+    if first_state.is_cuda:
+        A = torch.stack([transitions[g][0] for g in range(1, upto)])
+        Bm = torch.stack([offsets[g][0] for g in range(1, upto)])
+        _, end, _ = kernels.gdn2_span_fold(A, Bm, first_state[0])
+        return end.unsqueeze(0)
     s = first_state
     for g in range(1, upto):
         s = torch.matmul(transitions[g], s) + offsets[g]
@@ -104,6 +115,9 @@ def segment_maps(q, k, v, alpha, beta, S: int, *, scale=None, chunk_size=CHUNK):
 
 def compose_maps(A: torch.Tensor, Bm: torch.Tensor):
     """The map of the whole span from its segment maps: (A_{S-1} ... A_0, fold of the B's)."""
+    if A.is_cuda:
+        _, Bt, At = kernels.gdn2_span_fold(A, Bm, None, want_composed=True)
+        return At.unsqueeze(0), Bt.unsqueeze(0)
     At, Bt = A[0], Bm[0]
     for s in range(1, A.shape[0]):
         At = torch.matmul(A[s], At)
@@ -113,6 +127,9 @@ def compose_maps(A: torch.Tensor, Bm: torch.Tensor):
 
 def segment_starts(A: torch.Tensor, Bm: torch.Tensor, start: torch.Tensor) -> torch.Tensor:
     """Start states [S,H,K,V] of the S segments given the span's start state [1,H,K,V]."""
+    if A.is_cuda:
+        starts, _, _ = kernels.gdn2_span_fold(A, Bm, start[0], want_starts=True, want_end=False)
+        return starts
     S = A.shape[0]
     out = torch.empty_like(Bm)
     s_cur = start[0]
@@ -128,8 +145,10 @@ def segmented_prefill(q, k, v, alpha, beta, *, segments: Optional[int] = None, s
                       maps=None, start: Optional[torch.Tensor] = None):
     """Prefill of one long sequence [1, T, H, D] on one GPU through time segmentation.
 
-    Returns (out [1, T, H, V], final_state [1, H, K, V]).  `maps` reuses pass-1 results and
-    `start` overrides the span's start state (used by the multi-GPU driver).
+    Returns (out [1, T, H, V], final_state [1, H, K, V]).  Without ``maps`` this is one C-ABI call
+    (kernels.gdn2_prefill_segmented: pass 1, fold and rescan in the library); ``maps`` reuses
+    pass-1 results computed by the caller and ``start`` overrides the span's start state (the
+    multi-GPU driver, which has already computed the maps to hand them off).
     """
     if q.shape[0] != 1:
         raise ValueError("segmented_prefill handles one sequence (batch 1)")
@@ -139,8 +158,10 @@ def segmented_prefill(q, k, v, alpha, beta, *, segments: Optional[int] = None, s
         return kernels.gdn2_prefill(q, k, v, alpha, beta, scale=scale,
                                     initial_state=start if start is not None else initial_state,
                                     chunk_size=chunk_size)
-    A, Bm = maps if maps is not None else segment_maps(q, k, v, alpha, beta, S, scale=scale,
-                                                       chunk_size=chunk_size)
+    if maps is None:
+        return kernels.gdn2_prefill_segmented(q, k, v, alpha, beta, segments=S, scale=scale,
+                                              initial_state=start if start is not None else initial_state)
+    A, Bm = maps
     K, V = q.shape[3], v.shape[3]
     if start is None:
         start = initial_state if initial_state is not None else torch.zeros(
@@ -186,13 +207,14 @@ def time_sharded_prefill(q, k, v, alpha, beta, *, group=None, scale: Optional[fl
                                     chunk_size=chunk_size)
     maps = segment_maps(q, k, v, alpha, beta, S, scale=scale, chunk_size=chunk_size)
     K, V = q.shape[3], v.shape[3]
-    At, Bt = compose_maps(*maps)
     if rank == 0:
         s0 = initial_state.to(torch.float32) if initial_state is not None else torch.zeros(
             (1, H, K, V), device=q.device, dtype=torch.float32)
-        exchange_span_states(torch.matmul(At, s0) + Bt, None, rank, world, group)
+        _, end, _ = kernels.gdn2_span_fold(maps[0], maps[1], s0[0])
+        exchange_span_states(end.unsqueeze(0), None, rank, world, group)
         start = s0
     else:
+        At, Bt = compose_maps(*maps)
         As, Bs = exchange_span_states(At, Bt, rank, world, group)
         start = fold_span_states(Bs[0], As, Bs, rank)
     return segmented_prefill(q, k, v, alpha, beta, segments=S, scale=scale, chunk_size=chunk_size,

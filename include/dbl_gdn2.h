@@ -102,6 +102,51 @@ int dbl_gdn2_prefill(const dbl_prefill_args *args, dbl_stream_t stream);
 int dbl_gdn2_span_transition(const dbl_prefill_args *args, float *transition,
                              dbl_stream_t stream);
 
+/* Fold of span maps (the time-sharding hand-off).  For s = 0 .. segments-1,
+ *     X_{s+1} = transition[s] X_s + offset[s],   X_0 = start (NULL = zeros),
+ * per head, in f32.  transition [S,H,K,K] and offset [S,H,K,V] are the maps of consecutive token
+ * spans (dbl_gdn2_span_transition and dbl_gdn2_prefill from a zero state); starts [S,H,K,V]
+ * (optional) receives X_0 .. X_{S-1}, the start state of every span, end [H,K,V] (optional) X_S,
+ * and composed_transition [H,K,K] (optional) transition[S-1] ... transition[0], the transition of
+ * the whole run of spans.  K a multiple of 4 up to 128, V a multiple of 16; arrays contiguous and
+ * 16-byte aligned.  No counterpart in the reference, which has no time sharding. */
+int dbl_gdn2_span_fold(const float *transition, const float *offset, int64_t segments, int64_t heads,
+                       int64_t key_dim, int64_t value_dim, const float *start, float *starts, float *end,
+                       float *composed_transition, dbl_stream_t stream);
+
+/* Prefill of ONE long sequence (batch 1, config 4) on one device by time segments: the span is cut
+ * into `segments` equal segments (0 = the largest power of two with segments x heads <= the
+ * device's SM count and whole 64-token chunks per segment) that run side by side -- pass 1 the
+ * segment maps, a fold of their start states from initial_state, pass 2 every segment rescanned
+ * from its start.  Same arguments and results as dbl_gdn2_prefill (out, final_state); the result
+ * agrees with the one-pass scan to the rounding of the maps.  workspace: device memory of
+ * dbl_gdn2_prefill_segmented_workspace_bytes() bytes, 256-byte aligned.  Replaces, for one long
+ * sequence, the chunk-boundary carry of chunk::scan (crates/mixers/src/chunk.rs:147-244), whose
+ * chunk loop runs the whole sequence in order. */
+size_t dbl_gdn2_prefill_segmented_workspace_bytes(const dbl_prefill_args *args, int64_t segments);
+int dbl_gdn2_prefill_segmented(const dbl_prefill_args *args, int64_t segments, void *workspace,
+                               size_t workspace_bytes, dbl_stream_t stream);
+
+/* Prefill of ONE long sequence sharded along time over n_gpus devices, driven from one host thread
+ * (config 4 for a host that owns several GPUs in one process).  spans[g] describes the g-th
+ * consecutive time span (batch 1; device pointers on devices[g]; same heads, widths and dtype);
+ * spans[0].initial_state is the sequence's initial state (the other spans' initial_state is
+ * ignored) and the last span's final_state receives the sequence's final state.  Each device scans
+ * its span's segment maps (as dbl_gdn2_prefill_segmented); device g then pulls the span maps of
+ * devices 0 .. g-1 -- 2 x H x K x (K + V) x 4 bytes each, one cudaMemcpyPeerAsync per array on
+ * streams[g] after an event of the producing device -- folds them into its start state and
+ * rescans its span.  Peer memory is only read by those copies.  Work is enqueued on streams[g];
+ * the call returns without waiting.  workspaces[g]: device memory on devices[g] of
+ * dbl_gdn2_prefill_time_sharded_workspace_bytes(&spans[g], n_gpus, segments) bytes (the segment
+ * count 0 = automatic follows the SM count of the device current at the query).  The calling
+ * thread's current device is restored on return.  No counterpart in the reference, which runs on
+ * one device; its sequence-scaling contract is the chunk-boundary carry of chunk.rs:147-244. */
+size_t dbl_gdn2_prefill_time_sharded_workspace_bytes(const dbl_prefill_args *span, int n_gpus,
+                                                     int64_t segments);
+int dbl_gdn2_prefill_time_sharded(const dbl_prefill_args *spans, int n_gpus, const int *devices,
+                                  dbl_stream_t const *streams, int64_t segments, void *const *workspaces,
+                                  const size_t *workspace_bytes);
+
 /* =============================================================================================
  * 2. Single-token recurrent decode step, state updated IN PLACE (config 2).
  *

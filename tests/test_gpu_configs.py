@@ -142,3 +142,69 @@ def test_config4_full_segmented_two_heads(cuda, native_lib):
     r = report("config4 B1/H16/T131072/d128 bf16, 1 GPU segmented, heads 0 and 15",
                out=(got_o, ro[:, :, 0]), final_state=(got_f, rf[:, 0]))
     assert r["out"]["rel_err"] < TOL_BF16 and r["final_state"]["rel_err"] < TOL_BF16
+
+
+def test_config4_full_time_sharded_devices(cuda, native_lib):
+    # the C-ABI multi-device entry (dbl_gdn2_prefill_time_sharded) at full size: two spans on two
+    # GPUs when there are two, else both on cuda:0 (the hand-off then copies within one device)
+    q, k, v, alpha, beta = _config4_inputs(cuda)
+    devs = [torch.device("cuda", 0), torch.device("cuda", 1 if torch.cuda.device_count() > 1 else 0)]
+    T = q.shape[1]
+    half = T // 2
+    spans = []
+    for g, dev in enumerate(devs):
+        sl = slice(g * half, (g + 1) * half)
+        spans.append(tuple(x[:, sl].to(dev).contiguous() for x in (q, k, v, alpha, beta)))
+    outs, fin = dbl.gdn2_prefill_time_sharded_devices(spans)
+    for d in devs:
+        torch.cuda.synchronize(d)
+    _no_device_error(native_lib)
+    heads = (0, 15)
+    ro, rf, _ = _config4_oracle(q, k, v, alpha, beta, heads)
+    got_o = np.stack([np.concatenate([host(o[0, :, h]) for o in outs]) for h in heads])
+    got_f = np.stack([host(fin[0, h]) for h in heads])
+    r = report(f"config4 B1/H16/T131072/d128 bf16, time-sharded over devices {[d.index for d in devs]}, heads 0 and 15",
+               out=(got_o, ro[:, :, 0]), final_state=(got_f, rf[:, 0]))
+    assert r["out"]["rel_err"] < TOL_BF16 and r["final_state"]["rel_err"] < TOL_BF16
+
+
+def test_span_fold_matches_f64(cuda, native_lib):
+    rng = np.random.default_rng(3)
+    S, H, K, V = 5, 3, 128, 64
+    A = (rng.standard_normal((S, H, K, K)) / np.sqrt(K) * 0.9).astype(np.float32)
+    Bm = rng.standard_normal((S, H, K, V)).astype(np.float32)
+    x0 = rng.standard_normal((H, K, V)).astype(np.float32)
+    t = lambda x: torch.as_tensor(x, device=cuda)  # noqa: E731
+    starts, end, comp = dbl.gdn2_span_fold(t(A), t(Bm), t(x0), want_starts=True, want_composed=True)
+    torch.cuda.synchronize()
+    x = x0.astype(np.float64)
+    c = np.broadcast_to(np.eye(K), (H, K, K)).astype(np.float64)
+    ref_starts = []
+    for s in range(S):
+        ref_starts.append(x)
+        x = np.einsum("hik,hkv->hiv", A[s].astype(np.float64), x) + Bm[s]
+        c = np.einsum("hik,hkj->hij", A[s].astype(np.float64), c)
+    r = report("span fold S5/H3/K128/V64 f32", starts=(host(starts), np.stack(ref_starts)), end=(host(end), x),
+               composed=(host(comp), c))
+    for name in ("starts", "end", "composed"):
+        assert r[name]["rel_err"] < 1e-5, name
+
+
+def test_segmented_prefill_with_masks_and_initial(cuda, native_lib):
+    import bench
+    q, k, v, alpha, beta = bench.make_prefill_inputs(torch, cuda, 41, b=1, t=8192, h=4)
+    g = torch.Generator(device=cuda)
+    g.manual_seed(2)
+    valid = (torch.rand((1, 8192), device=cuda, generator=g) > 0.05).float()
+    reset = (torch.rand((1, 8192), device=cuda, generator=g) > 0.998).float()
+    init = 0.02 * torch.randn((1, 4, 128, 128), device=cuda, generator=g)
+    out, fin = dbl.gdn2_prefill_segmented(q, k, v, alpha, beta, segments=8, valid=valid, reset=reset,
+                                          initial_state=init)
+    torch.cuda.synchronize()
+    _no_device_error(native_lib)
+    ro, rf, _ = O.scan_scalar(host(q), host(k), host(v), host(alpha), host(beta), host(valid) > 0,
+                              host(reset) > 0, host(init))
+    r = report("segmented prefill B1/H4/T8192 d128 bf16, 8 segments, masks + initial state",
+               out=(host(out), ro), final_state=(host(fin), rf))
+    assert r["out"]["rel_err"] < TOL_BF16 and r["final_state"]["rel_err"] < TOL_BF16
+    assert np.all(host(out)[0][host(valid)[0] == 0] == 0.0)
