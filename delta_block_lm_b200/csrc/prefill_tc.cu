@@ -61,7 +61,7 @@ constexpr int NPREP = 256;   // warps 0-7, 112 registers each after setmaxnreg
 constexpr int NCHAIN = 256;  // warps 8-15, 144 registers each (the f32 state lives in registers)
 constexpr int PREP_REGS = 112, CHAIN_REGS = 144;
 static_assert(NPREP * PREP_REGS + NCHAIN * CHAIN_REGS <= 65536, "register split exceeds the launch budget");
-constexpr int BAR_PREP = 1, BAR_CHAIN = 2;
+constexpr int BAR_PREP = 1, BAR_CHAIN = 2, BAR_SCAN = 3;  // BAR_SCAN: the gate-scan warps 0-1
 
 // TMEM column map (512 columns, f32 accumulators unless noted).  Two 128-column regions alternate
 // by chunk parity p = c & 1: region p holds [D1 | DO] of chunk c (K S, then the output accumulator
@@ -72,7 +72,6 @@ constexpr uint32_t TM_S = 0;      // S^T bf16 A operand: 64 cols (128 keys, 2 pe
 constexpr uint32_t TM_KK = 64;    // prep: [K;Q] K^T, 64 cols
 constexpr uint32_t TM_D2 = 128;   // Delta^T (64 cols) -> scaled / plain bf16 in place
 constexpr uint32_t TM_R0 = 192;   // regions 0 and 1, 128 cols each (192..447)
-constexpr uint32_t TM_PD = 448;   // P Delta half of the output, 64 cols
 
 // Shared memory (offsets from a 1024-aligned base).  The K/Q tiles and the gates have three stages,
 // so the loads of chunk c + 3 go out as soon as the chain is done with chunk c; V, T and P have
@@ -100,27 +99,35 @@ constexpr uint32_t OFF_SG = OFF_SX + 1280 * 4;
 constexpr uint32_t OFF_SEM = OFF_SG + 64 * 4;   // 2^-g_s (fast decay path), 16-byte aligned
 constexpr uint32_t OFF_SCNT = OFF_SEM + 64 * 4;
 constexpr uint32_t OFF_SWT = OFF_SCNT + 64 * 4;
-constexpr uint32_t OFF_COM = OFF_SWT + 64;        // chain copy of the output multipliers [2][2][64] (16-B aligned)
-constexpr uint32_t OFF_BAR = (OFF_COM + 2 * 128 * 4 + 7) / 8 * 8;
-constexpr uint32_t NBARS = 13;
+constexpr uint32_t OFF_SGT = OFF_SWT + 64;        // gate staging [2][valid, reset, alpha, beta, write][64]
+constexpr uint32_t OFF_SDD = OFF_SGT + 2 * 5 * 64 * 4;  // edit-norm partials [4][64] (scores)
+constexpr uint32_t OFF_BAR = (OFF_SDD + 4 * 64 * 4 + 7) / 8 * 8;
+constexpr uint32_t NBARS = 19;
 constexpr uint32_t OFF_TSLOT = OFF_BAR + NBARS * 8;
 constexpr uint32_t SMEM_BYTES = OFF_TSLOT + 16 + 1024;  // + alignment slack
 static_assert(SMEM_BYTES <= 232448, "shared memory beyond the 227 KB a block can have");
 static_assert(OFF_T % 1024 == 0 && OFF_P % 1024 == 0 && T_BYTES % 1024 == 0, "swizzled tiles need 1024-B alignment");
 // gate arrays inside a stage's G region (floats)
-constexpr int G_CB = 0, G_CG = 64, G_CD = 128, G_OM = 192, G_VAL = 256, G_GC = 320;
+constexpr int G_CB = 0, G_CG = 64, G_CD = 128, G_OM = 192, G_VAL = 256, G_GC = 320, G_CE = 384, G_KK = 448;
 constexpr float kF16Max = 65504.f;
 
-constexpr uint32_t IDESC_M128_N64 = umma_idesc_bf16(128, 64, false);
-constexpr uint32_t IDESC_M128_N128_BMN = umma_idesc_bf16(128, 128, true);
-constexpr uint32_t IDESC_M128_N128 = umma_idesc_bf16(128, 128, false);
+constexpr uint32_t IDESC_M128_N64 = umma_idesc_bf16(128, 64, false);        // [K;Q] K^T on the raw bf16 tiles
+constexpr uint32_t IDESC_F16_M128_N128_BMN = umma_idesc_f16(128, 128, true);  // MMA3: B = K (fp16) MN-major
+constexpr uint32_t IDESC_F16_M128_N128 = umma_idesc_f16(128, 128, false);     // MMA1: B = [K; Q~] (fp16)
 constexpr uint32_t IDESC_F16_M128_N64 = umma_idesc_f16(128, 64, false);
 
 struct TcParams {
     int B, T, H, nchunks;
     float scale;
-    const float *alpha, *beta;
+    const float *alpha, *beta;  // beta: the erase gate (and the write gate unless `write` is set)
     int64_t as[3], bs[3];
+    const float* write;         // optional separate write gate (strides ws)
+    int64_t ws[3];
+    float* out_f32;             // f32 output written directly (instead of the bf16 TMA store), strides os
+    int64_t os[3];
+    float* scores;              // optional [B,T,H]: |k_t| |edit_t| (0 for padding)
+    const int* route;           // optional per-(b,h) flags: the CTA runs only where (route != 0) == route_want
+    int route_want;
     const float *valid, *reset;
     const float* initial;
     int init_mode;  // 0 zeros, 1 initial pointer, 2 identity
@@ -167,11 +174,16 @@ __device__ __forceinline__ void zero_tile_16(uint8_t* Tt, int row0, int chunk, i
     *reinterpret_cast<uint32_t*>(Tt + (row0 + g + 8) * 128 + sw + 4 * t4) = 0u;
 }
 
+// TRAIN: the training-scan instance (separate write gate, f32 output, scores, route flags); the
+// prefill instance compiles without those paths.
+template <bool TRAIN>
 __global__ void __launch_bounds__(NTHREADS, 1)
     gdn2_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                            const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
                            const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
+    // routed launches: this (b, h) is served by the other kernel of the call
+    if (TRAIN && p.route && ((p.route[blockIdx.x] != 0) != (p.route_want != 0))) return;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
     uint64_t* bar_x = bars + 0;      // [3] K/Q tiles landed
@@ -182,6 +194,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint64_t* bar_m1 = bars + 10;
     uint64_t* bar_m2 = bars + 11;
     uint64_t* bar_m3 = bars + 12;
+    uint64_t* bar_kkx = bars + 13;  // [3] the [K;Q] K^T MMA of the stage's chunk is complete (its tiles are free)
+    uint64_t* bar_gt = bars + 16;   // [3] the stage's gate arrays are written
     uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + OFF_TSLOT);
     int* serr = reinterpret_cast<int*>(smem + OFF_TSLOT + 8);  // the block's wait-error word
     float* sA = reinterpret_cast<float*>(smem + OFF_SA);
@@ -192,7 +206,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     int* scnt = reinterpret_cast<int*>(smem + OFF_SCNT);
     float* swt = reinterpret_cast<float*>(smem + OFF_SWT);
     int* swc = reinterpret_cast<int*>(smem + OFF_SWT + 32);
-    float* com = reinterpret_cast<float*>(smem + OFF_COM);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int bh = blockIdx.x;
@@ -207,7 +220,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
     if (tid == 0) {
         *serr = 0;
-        for (int i = 0; i < (int)NBARS; ++i) mbar_init(bars + i, 1);
+        for (int i = 0; i < (int)NBARS; ++i) mbar_init(bars + i, i == 12 ? 2 : 1);  // bar_m3: two issuers
         fence_mbar_init();
         prefetch_tmap(&tm_q);
         prefetch_tmap(&tm_k);
@@ -251,28 +264,40 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             load_v(0);
             if (nchunks > 1) load_v(1);
         }
-        // gates of the next chunk are fetched one iteration ahead (their load latency is hidden)
-        float nx_a = 1.f, nx_b = 0.f, nx_v = 0.f;
+        // gates of the next chunk are fetched one iteration ahead by asynchronous copies into shared
+        // memory, issued by warp 3 (idle during the gate scan; two tokens per lane) and waited for by it
+        // before the barrier that ends the iteration, so no scanning warp stalls on them
+        float* sgt = reinterpret_cast<float*>(smem + OFF_SGT);
         auto fetch_gates = [&](int c) {
-            nx_a = 1.f;
-            nx_b = 0.f;
-            nx_v = 0.f;
-            const int t = c * C + tid;
-            if (tid < C && t < p.T) {
-                nx_v = p.valid ? (p.valid[(size_t)b * p.T + t] != 0.f ? 1.f : 0.f) : 1.f;
-                const bool rs = p.reset ? p.reset[(size_t)b * p.T + t] != 0.f : false;
-                if (nx_v != 0.f) {
-                    nx_a = rs ? 0.f : p.alpha[(size_t)b * p.as[0] + (size_t)t * p.as[1] + (size_t)h * p.as[2]];
-                    nx_b = p.beta[(size_t)b * p.bs[0] + (size_t)t * p.bs[1] + (size_t)h * p.bs[2]];
+            if (warp != 3) return;
+            float* st = sgt + (c & 1) * 320;
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int r = lane + 32 * u, t = c * C + r;
+                if (t < p.T) {
+                    if (p.valid) cpa_4(st + r, p.valid + (size_t)b * p.T + t);
+                    else st[r] = 1.f;
+                    if (p.reset) cpa_4(st + 64 + r, p.reset + (size_t)b * p.T + t);
+                    else st[64 + r] = 0.f;
+                    cpa_4(st + 128 + r, p.alpha + (size_t)b * p.as[0] + (size_t)t * p.as[1] + (size_t)h * p.as[2]);
+                    cpa_4(st + 192 + r, p.beta + (size_t)b * p.bs[0] + (size_t)t * p.bs[1] + (size_t)h * p.bs[2]);
+                    if (TRAIN && p.write)
+                        cpa_4(st + 256 + r, p.write + (size_t)b * p.ws[0] + (size_t)t * p.ws[1] + (size_t)h * p.ws[2]);
+                } else {
+                    st[r] = 0.f;  // past the end: padding
                 }
             }
+            cpa_commit();
         };
         fetch_gates(0);
+        if (warp == 3) cpa_wait_all();
+        named_bar_sync(BAR_PREP, NPREP);
         // P = (scale Gamma o Q K^T, s <= r) in fp16 into stage s, from the Q rows of [K;Q] K^T in TMEM
         // (lanes 64..127, so warps with q = 2, 3): row r = 32 (q - 2) + lane, columns [32 half, 32 half
         // + 32).  Fast path: P[r][s] = (scale 2^g_r) 2^-g_s (q_r . k_s), every factor finite in f32.
-        auto write_p = [&](int s, bool fast) {
+        auto write_p = [&](int s, bool fast, const float* G) {
             const int r = 32 * (q - 2) + lane;
+            const float vr = G[G_VAL + r];  // a padding row's P row is zero (its output is zero)
             const float gr = sg[r];
             const int cr = scnt[r];
             const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + TM_KK + 32 * half;
@@ -284,7 +309,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const int s0 = 32 * half;
             float big = 0.f;
             if (fast) {
-                const float er = p.scale * exp2f(gr);
+                const float er = vr * p.scale * exp2f(gr);
 #pragma unroll
                 for (int e4 = 0; e4 < 8; ++e4) {
                     const float4 m = sem4[e4];
@@ -297,7 +322,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             } else {
 #pragma unroll
                 for (int e = 0; e < 32; ++e)
-                    gl[e] = __float_as_uint((s0 + e <= r && scnt[s0 + e] == cr) ? p.scale * exp2f(gr - sg[s0 + e]) * __uint_as_float(gl[e]) : 0.f);
+                    gl[e] = __float_as_uint((s0 + e <= r && scnt[s0 + e] == cr) ? vr * p.scale * exp2f(gr - sg[s0 + e]) * __uint_as_float(gl[e]) : 0.f);
             }
             uint8_t* P = stP(s);
 #pragma unroll
@@ -318,7 +343,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const int s = c & 1, xs = c % NXS;
             const uint32_t xpar = (uint32_t)(c / NXS) & 1u;
             // ---- gates: threads 0..63, token r = tid
-            const float a = nx_a, be = nx_b, vf = nx_v;
+            // this chunk's gates (padding: alpha 1, beta 0; a reset zeroes alpha)
+            float a = 1.f, be = 0.f, wr = 0.f, vf = 0.f;
+            if (tid < C) {
+                const float* st = sgt + (c & 1) * 320;
+                if (st[tid] != 0.f) {
+                    vf = 1.f;
+                    a = st[64 + tid] != 0.f ? 0.f : st[128 + tid];
+                    be = st[192 + tid];
+                    wr = (TRAIN && p.write) ? st[256 + tid] : be;
+                }
+            }
             if (c + 1 < nchunks) fetch_gates(c + 1);
             if (warp == 2) {
                 // [K;Q] K^T on the tensor cores needs only the TMA tiles: warp 2 (outside the gate scan)
@@ -333,11 +368,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         umma_ss(tmem + TM_KK, kdesc(xa), kdesc(xa), IDESC_M128_N64, kk > 0 ? 1u : 0u);
                     }
                     umma_commit(bar_kk);
+                    umma_commit(&bar_kkx[xs]);
                 }
                 __syncwarp();
             }
+            // ---- gates: warps 0-1, token r = tid.  They synchronise among themselves only, so warp 2's
+            //      MMA issue above and the idle warps do not hold up the scan.
             float lg = 0.f;
             int z = 0;
+            float* G = stG(xs);
             if (tid < C) {
                 z = a <= 0.f;
                 lg = z ? 0.f : __log2f(a);  // log2 domain: every decay product is one exp2
@@ -354,27 +393,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     swt[warp] = lg;
                     swc[warp] = z;
                 }
-            }
-            named_bar_sync(BAR_PREP, NPREP);
-            if (tid >= 32 && tid < C) {
-                lg += swt[0];
-                z += swc[0];
-            }
-            // the chunk's K/Q tiles have landed.  The gate stage c % 3 was last read by the chain in
-            // chunk c - 3, which finished before this block's wait on bar_tfree for chunk c - 3.
-            mbar_wait(&bar_x[xs], xpar, serr, 1);
-            float* G = stG(xs);
-            if (tid < C) {
+                named_bar_sync(BAR_SCAN, C);
+                if (tid >= 32) {
+                    lg += swt[0];
+                    z += swc[0];
+                }
+                // the chunk's K/Q tiles have landed.  The gate stage c % 3 was last read by the chain
+                // in chunk c - 3, which finished before the chain reloaded the stage for chunk c.
+                mbar_wait(&bar_x[xs], xpar, serr, 1);
                 sg[tid] = lg;
                 scnt[tid] = z;
                 sem[tid] = exp2f(-lg);
-            }
-            named_bar_sync(BAR_PREP, NPREP);
-            if (tid < C) {
+                named_bar_sync(BAR_SCAN, C);
                 const float gC = sg[C - 1];
                 const int cC = scnt[C - 1];
                 const float gamma = (z == 0) ? exp2f(lg) : 0.f;
-                G[G_CB + tid] = be;
+                G[G_CB + tid] = wr;                // write gate: R = write V - ...
+                if (TRAIN) G[G_CE + tid] = be;     // erase gate: rows of A (the prefill's is beta)
                 G[G_CG + tid] = be * gamma;
                 G[G_CD + tid] = (cC == z) ? exp2f(gC - lg) : 0.f;
                 // output: O_r = om_r (Q S)_r + (P Delta)_r with om_r = scale gamma_r
@@ -383,6 +418,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if (tid == C - 1) G[G_GC] = gamma;
             }
             named_bar_sync(BAR_PREP, NPREP);
+            if (tid == 0) mbar_arrive(&bar_gt[xs]);
             mbar_wait(bar_kk, c & 1, serr, 2);
             tc_fence_after();
             // Fast path: no zero decay in the chunk and a bounded total decay, so
@@ -401,7 +437,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 tmem_ld_wait();
                 const float4* sem4 = reinterpret_cast<const float4*>(sem + 32 * half);
                 const int s0 = 32 * half;
-                const float br = G[G_CB + r];
+                const float br = TRAIN ? G[G_CE + r] : G[G_CB + r];
+                if (TRAIN && p.scores && (r >> 5) == half) {
+                    float kk = 0.f;
+#pragma unroll
+                    for (int e = 0; e < 32; ++e)
+                        if (e == (r & 31)) kk = __uint_as_float(gl[e]);
+                    G[G_KK + r] = kk;
+                }
                 if (fast) {
                     const float brer = br * exp2f(gr);
                     float4* Arow = reinterpret_cast<float4*>(sA + r * LDA + s0);
@@ -496,7 +539,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                    pack_f16x2(w.z, w.w));
                 } else {
                     // warps 2, 3, 6, 7 meanwhile: P from the Q rows of [K;Q] K^T
-                    write_p(s, fast);
+                    write_p(s, fast, G);
                     tc_fence_before();  // these TMEM reads precede the next chunk's [K;Q] K^T
                 }
                 named_bar_sync(BAR_PREP, NPREP);
@@ -513,6 +556,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 zero_tile_16(Tt, 16 * mt, 4 + nt, g, t4);
             }
             fence_proxy_async_smem();
+            if (warp == 3) cpa_wait_all();  // the next chunk's gates are in shared memory
             named_bar_sync(BAR_PREP, NPREP);
             if (tid == 0) mbar_arrive(&bar_prep[s]);
         }
@@ -532,12 +576,51 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             else if (p.init_mode == 2) x = (i == j) ? 1.f : 0.f;
             S[e] = x;
         }
-        auto store_state_bf16 = [&]() {
+        // S^T as the fp16 A operand of MMA1 (an S beyond fp16 range makes Delta non-finite, which E2
+        // reports)
+        // The K and Q tiles of chunk cn to fp16 in place, Q rows scaled by their output multiplier
+        // om_r = scale gamma_r (0 for padding), so that MMA1 gives om o (Q S) and MMA4 adds P Delta onto
+        // it.  Runs once the [K;Q] K^T MMA that read the tiles as bf16 is complete and the chunk's gate
+        // arrays are written.  Four 8 KB blocks (K and Q of the two key blocks); thread ct converts the
+        // 16-byte chunks ct and ct + 256 of each, rows ct / 8 and ct / 8 + 32.  An fp16 overflow here
+        // (inputs far outside unit norm) makes Delta or the output non-finite, which is reported.
+        auto convert_x = [&](int cn) {
+            const int xn = cn % NXS;
+            const uint32_t pn = (uint32_t)(cn / NXS) & 1u;
+            mbar_wait(&bar_kkx[xn], pn, serr, 9);
+            mbar_wait(&bar_gt[xn], pn, serr, 10);
+            const float* Gn = stG(xn);
+            uint8_t* X = stX(xn);
+            float f[2];
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int row = (ct >> 3) + 32 * i;
+                f[i] = Gn[G_VAL + row] != 0.f ? Gn[G_OM + row] : 0.f;
+            }
+#pragma unroll
+            for (int blk = 0; blk < 4; ++blk) {
+                uint4* base = reinterpret_cast<uint4*>(X + blk * 8192) + ct;
+                uint4 u[2];
+#pragma unroll
+                for (int i = 0; i < 2; ++i) u[i] = base[256 * i];
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    uint32_t w[4] = {u[i].x, u[i].y, u[i].z, u[i].w};
+#pragma unroll
+                    for (int k2 = 0; k2 < 4; ++k2)
+                        w[k2] = (blk & 1) ? pack_f16x2(f[i] * bf16_lo(w[k2]), f[i] * bf16_hi(w[k2]))
+                                          : pack_f16x2(bf16_lo(w[k2]), bf16_hi(w[k2]));
+                    base[256 * i] = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+            }
+            fence_proxy_async_smem();  // the converted tiles are read by MMA1 and MMA3 (async proxy)
+        };
+        auto store_state_op = [&]() {
 #pragma unroll
             for (int pc = 0; pc < 4; ++pc) {
                 uint32_t pk[8];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) pk[u] = pack_bf16x2(S[16 * pc + 2 * u], S[16 * pc + 2 * u + 1]);
+                for (int u = 0; u < 8; ++u) pk[u] = pack_f16x2(S[16 * pc + 2 * u], S[16 * pc + 2 * u + 1]);
                 tmem_st8(tl + TM_S + 32 * hh + 8 * pc, pk);
             }
         };
@@ -552,31 +635,45 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk)
                 umma_ts(tmem + tr, tmem + TM_S + 8 * kk, kdesc(X + (kk >> 2) * 16384 + (kk & 3) * 32),
-                        IDESC_M128_N128, kk > 0 ? 1u : 0u);
+                        IDESC_F16_M128_N128, kk > 0 ? 1u : 0u);
             umma_commit(bar_m1);
         };
         // Output of chunk cc: O[r][j] = scale gamma_r DQ[j][r] + DP[j][r] (0 for padding rows) into the
         // staging tile, as bf16 for the TMA store.  DQ sits in the upper half
         // of region cc & 1; MMA3 of chunk cc + 1 overwrites it and MMA4 of chunk cc + 1 overwrites DP,
         // so this runs in chunk cc + 1 between MMA2 and the barrier that precedes those MMAs.
+        // Output of chunk cc: O[r][j] = om_r (Q S)[r][j] + (P Delta)[r][j], accumulated in the upper half of
+        // region cc & 1 by MMA1 (Q rows pre-scaled by om_r, zero for padding) and MMA4 (P rows of
+        // padding zero), into the staging tile as bf16 for the TMA store (f32 straight to global memory
+        // in the training-scan instance).  MMA3 of chunk cc + 1 overwrites the region, so this runs in
+        // chunk cc + 1 between MMA2 and the barrier that precedes MMA3.
         auto write_output = [&](int cc) {
-            const float* omc = com + 128 * (cc & 1);
-            __nv_bfloat16* Os = reinterpret_cast<__nv_bfloat16*>(smem + OFF_O);
             const uint32_t tdq = TM_R0 + 128 * (cc & 1) + 64;
-            uint32_t o[32], pd[32];
+            uint32_t o[32];
             tmem_ld16(tl + tdq + 32 * hh, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
             tmem_ld16(tl + tdq + 32 * hh + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
-            tmem_ld16(tl + TM_PD + 32 * hh, *reinterpret_cast<uint32_t(*)[16]>(&pd[0]));
-            tmem_ld16(tl + TM_PD + 32 * hh + 16, *reinterpret_cast<uint32_t(*)[16]>(&pd[16]));
             tmem_ld_wait();
+            float big = 0.f;
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                const int r = 32 * hh + e;
-                Os[r * 128 + j] = __float2bfloat16_rn(fmaf(omc[r], __uint_as_float(o[e]), omc[64 + r] * __uint_as_float(pd[e])));
+            for (int e = 0; e < 32; ++e) big = fmaxf(big, fabsf(__uint_as_float(o[e])));
+            if (!(big <= 3.0e38f)) atomicExch(p.err, kTcRangeError);  // inf or NaN: an fp16 operand overflowed
+            if (TRAIN) {
+                // f32 rows straight to global memory: a warp writes 32 consecutive values per row
+                float* orow = p.out_f32 + (size_t)b * p.os[0] + (size_t)h * p.os[2] + j;
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    const int t = cc * C + 32 * hh + e;
+                    if (t < p.T) orow[(size_t)t * p.os[1]] = __uint_as_float(o[e]);
+                }
+                return;
             }
+            __nv_bfloat16* Os = reinterpret_cast<__nv_bfloat16*>(smem + OFF_O);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) Os[(32 * hh + e) * 128 + j] = __float2bfloat16_rn(__uint_as_float(o[e]));
             fence_proxy_async_smem();
         };
-        store_state_bf16();
+        convert_x(0);
+        store_state_op();
         tmem_st_wait();
         tc_fence_before();
         named_bar_sync(BAR_CHAIN, NCHAIN);
@@ -589,13 +686,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const uint32_t TM_D3 = TM_R0 + 128 * ((c & 1) ^ 1);  // (Gamma Delta)^T K, 128 cols
             mbar_wait(&bar_prep[s], (c >> 1) & 1, serr, 4);
             const float* G = stG(xs);
-            // private copy of what this chunk's output needs, so stage s can be reloaded early
-            float* om = com + 128 * (c & 1);  // [0, 64): scale gamma_r, [64, 128): the row's P Delta factor
-            if (ct < C) {
-                const bool ok = G[G_VAL + ct] != 0.f;
-                om[ct] = ok ? G[G_OM + ct] : 0.f;
-                om[64 + ct] = ok ? 1.f : 0.f;
-            }
             const float gC = G[G_GC];
             mbar_wait(bar_m1, par, serr, 5);
             if (!p.v_zero) mbar_wait(&bar_v[s], (uint32_t)(c >> 1) & 1u, serr, 8);
@@ -632,10 +722,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             tc_fence_before();
             named_bar_sync(BAR_CHAIN, NCHAIN);
-            // V stage s is read: it takes V of chunk c + 2
-            if (ct == 0 && c + 2 < nchunks) load_v(c + 2);
             // ---- MMA2: D2[j][r'] = sum_r R^T[j][r] T[r'][r]   (fp16; rows r = 16 kk .. 16 kk + 15 of R^T are
-            //      TMEM columns 32 (kk / 2) + 8 (kk % 2) ..)
+            //      TMEM columns 32 (kk / 2) + 8 (kk % 2) ..); then V stage s, read by E1, takes V of chunk c + 2
             if (ct == 0) {
                 tc_fence_after();
                 const uint8_t* Tt = stT(s);
@@ -644,6 +732,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     umma_ts(tmem + TM_D2, tmem + TM_D1 + 32 * (kk >> 1) + 8 * (kk & 1), kdesc(Tt + kk * 32),
                             IDESC_F16_M128_N64, kk > 0 ? 1u : 0u);
                 umma_commit(bar_m2);
+                if (c + 2 < nchunks) load_v(c + 2);
             }
             // while MMA2 runs: the output of chunk c - 1
             if (p.write_out && c >= 1) write_output(c - 1);
@@ -668,7 +757,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         const int r = 32 * hh + e;
                         const float x0 = __uint_as_float(d[e]), x1 = __uint_as_float(d[e + 1]);
                         big = fmaxf(big, fmaxf(fabsf(x0), fabsf(x1)));
-                        ps[u] = pack_bf16x2(x0 * G[G_CD + r], x1 * G[G_CD + r + 1]);
+                        ps[u] = pack_f16x2(x0 * G[G_CD + r], x1 * G[G_CD + r + 1]);
                         pp[u] = pack_f16x2(x0, x1);
                     }
                     tmem_st8(tl + col, ps);
@@ -677,13 +766,54 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 // an fp16 operand overflowed (R or T, so Delta is not finite) or Delta itself is out of
                 // fp16 range: report it (the NaN test is the negated comparison)
                 if (!(big <= kF16Max)) atomicExch(p.err, kTcRangeError);
+                if (TRAIN && p.scores) {
+                    // |edit_r|^2 = sum_j Delta[r][j]^2: a reduce-scatter over the warp's 32 columns
+                    // (lane l ends with row 32 hh + l), then the four warps of a row half in shared memory
+                    float v[32];
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(d[e]) * __uint_as_float(d[e]);
+                    const bool up16 = lane & 16, up8 = lane & 8, up4 = lane & 4, up2 = lane & 2, up1 = lane & 1;
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        const float keep = up16 ? v[e + 16] : v[e], send = up16 ? v[e] : v[e + 16];
+                        v[e] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+                    }
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const float keep = up8 ? v[e + 8] : v[e], send = up8 ? v[e] : v[e + 8];
+                        v[e] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+                    }
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float keep = up4 ? v[e + 4] : v[e], send = up4 ? v[e] : v[e + 4];
+                        v[e] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+                    }
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const float keep = up2 ? v[e + 2] : v[e], send = up2 ? v[e] : v[e + 2];
+                        v[e] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+                    }
+                    {
+                        const float keep = up1 ? v[1] : v[0], send = up1 ? v[0] : v[1];
+                        v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
+                    }
+                    reinterpret_cast<float*>(smem + OFF_SDD)[q * 64 + 32 * hh + lane] = v[0];
+                }
                 tmem_st_wait();
             }
             tc_fence_before();
             named_bar_sync(BAR_CHAIN, NCHAIN);
-            // ---- MMA3: D3 = (Gamma Delta)^T K (state increment); MMA4: DP = Delta^T P^T (output)
+            if (TRAIN && p.scores && ct < C) {
+                // score_r = |k_r| |edit_r| (0 for padding, whose edit is exactly zero)
+                const float* sdd = reinterpret_cast<const float*>(smem + OFF_SDD);
+                const float dd = sdd[ct] + sdd[64 + ct] + sdd[128 + ct] + sdd[192 + ct];
+                const int t = c * C + ct;
+                if (t < p.T) p.scores[((size_t)b * p.T + t) * p.H + h] = G[G_VAL + ct] != 0.f ? sqrtf(G[G_KK + ct] * dd) : 0.f;
+            }
+            // ---- MMA3: D3 = (Gamma Delta)^T K (state increment) issued by thread 0 of the chain, MMA4:
+            //      DP = Delta^T P^T (output) by thread 32 (independent accumulators; bar_m3 counts both commits)
             if (ct == 0) {
-                if (p.write_out && c >= 1) {
+                if (!TRAIN && p.write_out && c >= 1) {
                     tma_store_4d(&tm_o, smem + OFF_O, 0, (c - 1) * C, h, b);
                     tma_store_commit();
                 }
@@ -692,21 +822,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
                     umma_ts(tmem + TM_D3, tmem + TM_D2 + 16 * kk,
-                            umma_sdesc_sw128(smem_u32addr(X + kk * 2048), 16384, 1024), IDESC_M128_N128_BMN,
+                            umma_sdesc_sw128(smem_u32addr(X + kk * 2048), 16384, 1024), IDESC_F16_M128_N128_BMN,
                             kk > 0 ? 1u : 0u);
+                umma_commit(bar_m3);
+            } else if (ct == 32) {
+                tc_fence_after();
                 if (p.write_out) {
                     const uint8_t* P = stP(s);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
-                        umma_ts(tmem + TM_PD, tmem + TM_D2 + 16 * kk + 8, kdesc(P + kk * 32), IDESC_F16_M128_N64,
-                                kk > 0 ? 1u : 0u);
+                        umma_ts(tmem + TM_R0 + 128 * (c & 1) + 64, tmem + TM_D2 + 16 * kk + 8, kdesc(P + kk * 32),
+                                IDESC_F16_M128_N64, 1u);  // onto om o (Q S): the output
                 }
                 umma_commit(bar_m3);
             }
+            // while MMA3 / MMA4 run: the next chunk's tiles to fp16 (read by its MMA1 after E3)
+            if (c + 1 < nchunks) convert_x(c + 1);
             mbar_wait(bar_m3, par, serr, 7);
             tc_fence_after();
             // every MMA of chunk c is done: its K/Q stage takes chunk c + 3, and its T / P stage goes
-            // back to the prep warps (the output multipliers were copied to `com`)
+            // back to the prep warps
             if (ct == 0) {
                 if (c + NXS < nchunks) load_x(c + NXS);
                 mbar_arrive(&bar_tfree[s]);
@@ -724,7 +859,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
                     for (int e = 0; e < 32; ++e) S[32 * pc + e] = fmaf(gC, S[32 * pc + e], __uint_as_float(d[e]));
                 }
-                store_state_bf16();
+                store_state_op();
                 tmem_st_wait();
             }
             tc_fence_before();
@@ -738,7 +873,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             write_output(nchunks - 1);
             tc_fence_before();
             named_bar_sync(BAR_CHAIN, NCHAIN);
-            if (ct == 0) {
+            if (ct == 0 && !TRAIN) {
                 tma_store_4d(&tm_o, smem + OFF_O, 0, (nchunks - 1) * C, h, b);
                 tma_store_commit();
             }
@@ -856,13 +991,78 @@ int tc_prefill_launch(const dbl_prefill_args* a, const int64_t* qs, const int64_
     p.err = err;
     static std::atomic<uint64_t> attr_done{0};
     rc = once_per_device(attr_done, [] {
-        return cuda_status(cudaFuncSetAttribute(gdn2_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                (int)SMEM_BYTES),
+        return cuda_status(cudaFuncSetAttribute(gdn2_prefill_tc_kernel<false>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES),
                            "prefill_tc: cudaFuncSetAttribute");
     });
     if (rc != DBL_OK) return rc;
-    gdn2_prefill_tc_kernel<<<(unsigned)(a->batch * a->heads), NTHREADS, SMEM_BYTES, st>>>(mq, mk, mv, mo, p);
+    gdn2_prefill_tc_kernel<false><<<(unsigned)(a->batch * a->heads), NTHREADS, SMEM_BYTES, st>>>(mq, mk, mv, mo, p);
     return launch_status("gdn2_prefill_tc_kernel");
+}
+
+// The reference's stateful training scan (dbl_gdn_training_scan) on this kernel: bf16 q/k/v
+// [B,T,H,128] contiguous, gates read at channel 0 of the channel-wise [B,T,H,K|V] arrays (the caller
+// has checked, per (b, h), that they are constant across channels: `route`), separate erase and
+// write gates, valid / reset masks, optional initial and final states, f32 output and scores.  CTAs
+// whose route flag differs from `route_want` return at once.
+bool tc_training_scan_supported(const dbl_training_scan_args* a) {
+    if (a->dtype != DBL_BF16 || a->key_dim != 128 || a->value_dim != 128) return false;
+    if (a->batch * a->heads > 0x7fffffffLL) return false;
+    for (const void* ptr : {a->q, a->k, a->v})
+        if (!aligned(ptr, 16)) return false;
+    return aligned(a->output, 16);
+}
+
+int tc_training_scan_launch(const dbl_training_scan_args* a, const int* route, int route_want, cudaStream_t st) {
+    const int64_t T = a->time, H = a->heads;
+    const int64_t st4[4] = {T * H * 128, H * 128, 128, 1};
+    CUtensorMap mq, mk, mv, mo;
+    int rc = make_map(&mq, a->q, a->batch, T, H, st4, 64, true);
+    if (rc == DBL_OK) rc = make_map(&mk, a->k, a->batch, T, H, st4, 64, true);
+    if (rc == DBL_OK) rc = make_map(&mv, a->v, a->batch, T, H, st4, 128, false);
+    if (rc == DBL_OK) rc = make_map(&mo, a->k, a->batch, T, H, st4, 128, false);  // unused: f32 output path
+    if (rc != DBL_OK) return rc;
+    TcParams p{};
+    p.B = (int)a->batch;
+    p.T = (int)T;
+    p.H = (int)H;
+    p.nchunks = (int)((T + C - 1) / C);
+    p.scale = 1.f;  // the training scan takes q as it is
+    p.alpha = a->alpha;
+    p.beta = a->erase;
+    p.write = a->write;
+    const int64_t gk[3] = {T * H * a->key_dim, H * a->key_dim, a->key_dim};
+    const int64_t gv[3] = {T * H * a->value_dim, H * a->value_dim, a->value_dim};
+    for (int d = 0; d < 3; ++d) {
+        p.as[d] = gk[d];
+        p.bs[d] = gk[d];
+        p.ws[d] = gv[d];
+        p.os[d] = gv[d];
+    }
+    p.valid = a->valid;
+    p.reset = a->reset;
+    p.init_mode = a->initial_state ? 1 : 0;
+    p.initial = a->initial_state;
+    p.v_zero = 0;
+    p.write_out = 1;
+    p.out_f32 = a->output;
+    p.scores = a->scores;
+    p.final_state = a->final_state;
+    p.route = route;
+    p.route_want = route_want;
+    int* err = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_tc_error);
+    if (e != cudaSuccess) return cuda_status(e, "prefill_tc: error record");
+    p.err = err;
+    static std::atomic<uint64_t> attr_done{0};
+    rc = once_per_device(attr_done, [] {
+        return cuda_status(cudaFuncSetAttribute(gdn2_prefill_tc_kernel<true>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES),
+                           "prefill_tc: cudaFuncSetAttribute");
+    });
+    if (rc != DBL_OK) return rc;
+    gdn2_prefill_tc_kernel<true><<<(unsigned)(a->batch * a->heads), NTHREADS, SMEM_BYTES, st>>>(mq, mk, mv, mo, p);
+    return launch_status("gdn2_prefill_tc_kernel (training scan)");
 }
 
 int device_error_record(int** out) {

@@ -578,8 +578,6 @@ bool chunk_scan_supported(const SeqParams& p) {
            (int64_t)p.B * p.H * ((p.K + 31) / 32) * ((p.V + 63) / 64) <= 384;
 }
 
-namespace {
-
 // A stream-ordered pool per device for the chunk maps, created on first use; freed blocks stay in the
 // pool (release threshold: never) so that repeated calls reuse them without driver allocations.
 int scratch_pool(cudaMemPool_t* out) {
@@ -606,6 +604,8 @@ int scratch_pool(cudaMemPool_t* out) {
     *out = pools[dev];
     return DBL_OK;
 }
+
+namespace {
 
 template <int KMAX, int VG, int NTH>
 int launch_main_t(const SeqParams& p, const float* ws, float* part, int ngroups, int NB, int extra, size_t smem,

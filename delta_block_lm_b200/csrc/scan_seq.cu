@@ -47,6 +47,8 @@ __global__ void __launch_bounds__(512) seq_scan_kernel(const SeqParams p) {
     __shared__ float svw[TOK][256];       // write_j v_j (beta: v_j) of the staged tokens
 
     const int bh = blockIdx.x;
+    // routed launches: this (b, h) is served by the tensor-core kernel of the call
+    if (p.route && ((p.route[bh] != 0) != (p.route_want != 0))) return;
     const int b = bh / p.H, h = bh - b * p.H;
     const int tid = threadIdx.x, nthr = blockDim.x;
     const int warp = tid >> 5, lane = tid & 31, nwarps = nthr >> 5;
@@ -299,12 +301,89 @@ int training_scan_params(const dbl_training_scan_args* a, SeqParams* out) {
 }  // namespace dbl
 
 // delta_kernels::gdn_training_scan (crates/kernels/src/gdn_training_ops.rs:288-333) forward.
+namespace dbl {
+
+bool tc_training_scan_supported(const dbl_training_scan_args* a);
+int tc_training_scan_launch(const dbl_training_scan_args* a, const int* route, int route_want, cudaStream_t st);
+
+namespace {
+
+// flags[b * H + h] |= 1 when some token row of (b, h) has alpha, erase or write that differ across
+// channels.  One warp per (b, t, h) row; K = V = 128 (four channels per lane).
+__global__ void __launch_bounds__(256) gate_uniform_kernel(const float* __restrict__ alpha,
+                                                           const float* __restrict__ erase,
+                                                           const float* __restrict__ write, int64_t rows, int TH,
+                                                           int H, int* flags) {
+    const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    bool diff = false;
+    for (const float* g : {alpha, erase, write}) {
+        const float4 x = reinterpret_cast<const float4*>(g + row * 128)[lane];
+        const float x0 = __shfl_sync(0xffffffffu, x.x, 0);
+        diff |= (x.x != x0) | (x.y != x0) | (x.z != x0) | (x.w != x0);
+    }
+    if (__any_sync(0xffffffffu, diff) && lane == 0) {
+        const int64_t b = row / TH;
+        atomicOr(flags + b * H + (int)(row % H), 1);
+    }
+}
+
+}  // namespace
+
+// The training scan at K = V = 128 with bf16 inputs: a check kernel marks every (b, h) whose gates
+// vary across channels; the tensor-core kernel scans the others (gates read at channel 0) and the
+// token-sequential kernel the marked ones.  Both are launched; a CTA whose (b, h) belongs to the
+// other kernel returns at once, so the choice needs no host synchronisation.
+int training_scan_routed(const dbl_training_scan_args* a, SeqParams& p, cudaStream_t st) {
+    const int64_t nbh = a->batch * a->heads, rows = a->batch * a->time * a->heads;
+    for (const void* ptr : {static_cast<const void*>(a->alpha), static_cast<const void*>(a->erase),
+                            static_cast<const void*>(a->write)})
+        if (!aligned(ptr, 16)) return launch_seq_scan(p, a->dtype, st);
+    int* flags = nullptr;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    cudaError_t e = cudaStreamIsCapturing(st, &cap);
+    if (e != cudaSuccess) return cuda_status(e, "training scan: cudaStreamIsCapturing");
+    if (cap == cudaStreamCaptureStatusActive) {
+        e = cudaMallocAsync(reinterpret_cast<void**>(&flags), nbh * sizeof(int), st);
+    } else {
+        cudaMemPool_t pool = nullptr;
+        const int rc = scratch_pool(&pool);
+        if (rc != DBL_OK) return rc;
+        e = cudaMallocFromPoolAsync(reinterpret_cast<void**>(&flags), nbh * sizeof(int), pool, st);
+    }
+    if (e != cudaSuccess) return cuda_status(e, "training scan: route flags");
+    int rc = cuda_status(cudaMemsetAsync(flags, 0, nbh * sizeof(int), st), "training scan: clear route flags");
+    if (rc == DBL_OK) {
+        const int64_t blocks = (rows + 7) / 8;
+        if (blocks > 0x7fffffffLL) rc = fail(DBL_ERR_UNSUPPORTED, "training scan: too many rows");
+        else {
+            gate_uniform_kernel<<<(unsigned)blocks, 256, 0, st>>>(a->alpha, a->erase, a->write, rows,
+                                                                (int)(a->time * a->heads), (int)a->heads, flags);
+            rc = launch_status("gate_uniform_kernel");
+        }
+    }
+    if (rc == DBL_OK) rc = tc_training_scan_launch(a, flags, 0, st);
+    if (rc == DBL_OK) {
+        p.route = flags;
+        p.route_want = 1;
+        rc = launch_seq_scan(p, a->dtype, st);
+    }
+    const cudaError_t ef = cudaFreeAsync(flags, st);
+    if (rc == DBL_OK) rc = cuda_status(ef, "training scan: route flags release");
+    return rc;
+}
+
+}  // namespace dbl
+
 extern "C" int dbl_gdn_training_scan(const dbl_training_scan_args* a, dbl_stream_t stream) {
     using namespace dbl;
     SeqParams p{};
     const int rc = training_scan_params(a, &p);
     if (rc != DBL_OK) return rc;
-    return launch_seq_scan(p, a->dtype, reinterpret_cast<cudaStream_t>(stream));
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (tc_training_scan_supported(a)) return training_scan_routed(a, p, st);
+    return launch_seq_scan(p, a->dtype, st);
 }
 
 // delta_kernels::gdn2_scan (crates/kernels/src/ops.rs:251-276): doc-limit masks, zero initial.

@@ -30,7 +30,12 @@ struct SeqParams {
     float* chunk_states; // optional, chunked form only: the state at every 16-token chunk start,
                          // [B*H][ceil(T/16)][K][V]
     float* edits;        // optional, chunked form only: every token's edit, [B,T,H,V] f32
+    const int* route;    // optional per-(b,h) flags: a CTA runs only where (route != 0) == route_want
+    int route_want;
 };
+
+// The library's stream-ordered memory pool of the current device (scan_chunk.cu).
+int scratch_pool(cudaMemPool_t* out);
 
 // Checks the arguments of the training-scan forward (dbl_gdn_training_scan) and fills `out`.
 int training_scan_params(const dbl_training_scan_args* a, SeqParams* out);

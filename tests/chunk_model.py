@@ -1,10 +1,11 @@
 """numpy model of the tensor-core prefill kernel's arithmetic (prefill_tc.cu), for CPU tests.
 
 It follows the kernel step by step -- log-space decay products with reset counting, the inverse
-of (I + A) by block doubling, and rounding exactly where the kernel rounds an MMA operand (S and
-the Gamma-scaled Delta to bf16 because their partner operand is a bf16 input tile; T, R, the
-plain Delta and P to fp16) -- so the numerical error budget of the kernel can be checked against
-the oracle without a GPU.  Test infrastructure only.
+of (I + A) by block doubling, and rounding exactly where the kernel rounds an MMA operand: every
+operand of the state chain is fp16 (the chunk's K and Q tiles are converted in place, Q rows
+scaled by the output multiplier scale * gamma_r; S, R, T, Delta, the Gamma-scaled Delta and P),
+only [K;Q] K^T runs on the bf16 input tiles -- so the numerical error budget of the kernel can be
+checked against the oracle without a GPU.  Test infrastructure only.
 """
 from __future__ import annotations
 
@@ -86,15 +87,17 @@ def prefill_model(q, k, v, alpha, beta, scale, valid=None, reset=None, initial=N
                 A = np.where(low, be[:, None] * dec * (Kc @ Kc.T), 0.0).astype(np.float32)
                 P = h16(np.where(incl, scale * dec * (Qc @ Kc.T), 0.0))
                 Tm = h16(blocked_unit_lower_inverse(A))
-                Sb = rnd(S)
-                KS = Kc @ Sb
-                QS = Qc @ Sb
+                P = np.where(vf[:, None] != 0, P, 0.0)            # padding rows of P are zero
+                Kh = h16(Kc)                                         # the K tile in fp16
+                Qh = h16((vf * scale * gamma)[:, None] * Qc)         # Q rows scaled by om_r, fp16
+                Sb = h16(S)
+                KS = Kh @ Sb
                 R = h16(be[:, None] * Vc - (be * gamma)[:, None] * KS)
                 Delta = Tm @ R
-                Dt = rnd(Delta * dec[C - 1][:, None])
+                Dt = h16(Delta * dec[C - 1][:, None])
                 Dp = h16(Delta)
-                S = (gamma[C - 1] * S + Kc.T @ Dt).astype(np.float32)
-                O = np.where(vf[:, None] != 0, (scale * gamma)[:, None] * QS + P @ Dp, 0.0)
+                S = (gamma[C - 1] * S + Kh.T @ Dt).astype(np.float32)
+                O = Qh @ Sb + P @ Dp
                 out[b, t0:t0 + n, h] = rnd(O[:n])
             fin[b, h] = S
     return out, fin

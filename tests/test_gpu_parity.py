@@ -759,20 +759,34 @@ def test_single_token_inputs(cuda, native_lib):
 # --------------------------------------------------------------- full-size, size-independent checks
 def test_prefill_full_size_linear_in_values_and_permutation(cuda, native_lib):
     # BASELINE config 1 (B8/H16/T4096/d128 bf16) for every head: the output and final state are
-    # linear in v for a zero initial state, so doubling v doubles them (to 1e-3: doubling is exact in
-    # floating point except where the kernel's fp16 operands are subnormal); permuting the batch
-    # permutes them bit for bit (each (b, h) is computed on its own, so no pair leaks into another).
+    # linear in v for a zero initial state, so doubling v doubles them.  The kernel is deterministic
+    # (the same inputs give the same bits) and each (b, h) is computed on its own (permuting the batch
+    # permutes the results bit for bit).  Doubling is exact in floating point except for fp16 MMA
+    # operands below fp16's normal range (6.1e-5: a decay-scaled edit of a strongly decayed token),
+    # which round on a different grid once doubled; that moves outputs by about 1e-3 of their rms at
+    # a handful of near-zero elements and can flip an output's bf16 rounding, so linearity is held to
+    # one bf16 unit plus 2e-3 rms (outputs) and 1e-3 of the soft metric (final states).
     import bench
     q, k, v, alpha, beta = bench.make_prefill_inputs(torch, cuda, 4321)
     o1, f1 = dbl.gdn2_prefill(q, k, v, alpha, beta)
+    o1b, f1b = dbl.gdn2_prefill(q, k, v, alpha, beta)
     o2, f2 = dbl.gdn2_prefill(q, k, v * 2, alpha, beta)
     perm = torch.tensor([3, 0, 7, 1, 6, 2, 5, 4], device=cuda)
     o3, f3 = dbl.gdn2_prefill(q[perm], k[perm], v[perm], alpha[perm], beta[perm])
     torch.cuda.synchronize()
     assert _device_error_clear(native_lib) == (0, 0)
-    assert torch.isfinite(o1.float()).all() and torch.isfinite(f1).all()
-    assert rel_err(host(o2.float()), 2 * host(o1.float())) < 1e-3 and rel_err(host(f2), 2 * host(f1)) < 1e-3
+    # deterministic: the same inputs give the same bits
+    assert torch.equal(o1b, o1) and torch.equal(f1b, f1), int((o1b != o1).sum())
     assert torch.equal(o3, o1[perm]) and torch.equal(f3, f1[perm])
+    assert torch.isfinite(o1.float()).all() and torch.isfinite(f1).all()
+    # one bf16 unit of the element (a flipped output rounding) plus 2e-3 of the rms (near-zero
+    # outputs, where the shifted subnormal roundings of the operands are not small relative to |o|)
+    a2, e2 = host(o2.float()), 2 * host(o1.float())
+    rms = float(np.sqrt(np.mean(e2 * e2)))
+    excess = np.abs(a2 - e2) - (2.0 ** -7 * np.abs(e2) + 2e-3 * rms)
+    worst = np.unravel_index(np.argmax(excess), excess.shape)
+    assert excess[worst] <= 0, (worst, float(a2[worst]), float(e2[worst]), rms)
+    assert rel_err(host(f2), 2 * host(f1)) < 1e-3
 
 
 def test_prologue_full_size_sampled(cuda, native_lib):
