@@ -5,35 +5,35 @@
 // q.k * scale, a running maximum, sum of exp(score - max), output acc / sum, and the
 // statistics [max, sum] per query; a query with no eligible key writes o = 0, [0, 1].
 //
-// Work split (one grid, 256 threads per CTA):
-//   prefix CTAs (head h, prefix block pb): read the block's keys/values of head h ONCE and
+// One CTA (256 threads) per work item:
+//   prefix items (head h, prefix block pb): read the block's keys/values of head h ONCE and
 //       produce partials (max, sum, acc[D]) for the queries of EVERY sequence at head h, so the
-//       shared prefix is read once per head, never once per sequence.  bf16 inputs stream 512
-//       keys per CTA through tensor-core tiles (mma.sync m16n8k16, online softmax over 32-key
-//       sub-tiles; 8 warps = 4 query blocks x 2 output halves); f32 inputs use SIMT tiles of 64
-//       keys (two partials per CTA).
-//   own CTAs (sequence n, head h, 1024-key own block ob): one query against up to 1024 keys,
-//       streamed with 16-byte coalesced loads.  bf16: a single pass per warp with an online
-//       softmax, K and V rows of a key group loaded together (HBM-bound); f32: scores, then
-//       values, with the prefix path's exact arithmetic.
-// Each CTA writes its partials to the workspace and bumps a per-(n, h) arrival counter; the
-// CTA that completes a row merges its P partials (max of partial maxima, rescaled sums) and
+//       shared prefix is read once per head, never once per sequence.  bf16 streams 512 keys
+//       through tensor-core tiles (mma.sync m16n8k16, online softmax over 32-key sub-tiles, two
+//       tile buffers); f32 uses SIMT tiles of 64 keys (two partials per item).
+//   own items (sequence n, head h, 1024-key own block ob): one query against the block's keys.
+//       bf16: streamed through a bulk-copy ring (below); f32: scores then values with the prefix
+//       path's exact arithmetic.
+// Each item writes its partial to the workspace and bumps a per-(n, h) arrival counter; the
+// block that completes a row merges its P partials (max of partial maxima, rescaled sums) and
 // writes o, max and sum.  The host clears the counters before each launch.
 #include <float.h>
 
 #include "common.cuh"
+#include "tc_ptx.cuh"
 
 namespace dbl {
 namespace {
 
 constexpr int BP = 64;        // prefix keys per tile
 constexpr int KSPLIT = 2;     // f32 path: partials per prefix CTA (key halves of 32)
-constexpr int TILES_BF16 = 8; // bf16 path: 64-key tiles streamed by one prefix CTA (512 keys)
-constexpr int NQ = 64;        // queries per prefix tile
-constexpr int BO = 1024;      // own keys per own CTA
+constexpr int TILES_BF16 = 8; // bf16 path: 64-key tiles streamed by one prefix item (512 keys)
+constexpr int NQ = 64;        // queries per prefix pass
+constexpr int BO = 1024;      // f32: own keys per own CTA
 constexpr int THREADS = 256;
-constexpr int MIN_BLOCKS = 3; // CTAs per SM the register budget is sized for
+constexpr int MIN_BLOCKS_F32 = 3;  // f32 kernel: CTAs per SM its register budget is sized for
 constexpr int PAD = 8;        // bf16 row padding (row stride D+8 elements: conflict-free ldmatrix)
+constexpr int kRelayWaitFull = 30, kRelayWaitEmpty = 31;  // wait-site codes (dbl_device_error)
 
 struct RelayParams {
     int N, H, Lp, Lo, NPB, NOB, P;
@@ -45,6 +45,8 @@ struct RelayParams {
     float *row_max, *row_sum;
     float *part_acc, *part_max, *part_sum;  // [N,H,P,D], [N,H,P], [N,H,P]
     unsigned* counter;                      // [N,H]
+    int* err;                               // the library's device error word
+    int bo;                                 // own keys per own item
 };
 
 __device__ __forceinline__ float warp_max(float x) {
@@ -83,68 +85,107 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
 }
+// 16-byte asynchronous global -> shared copy through L2 only; src_bytes = 0 reads nothing and
+// fills the 16 bytes with zeros.
+__device__ __forceinline__ void cp16_zfill(void* sdst, const void* gsrc, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(sdst)), "l"(gsrc), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// Bulk (non-tensor, no multicast) global -> shared copy of `bytes` (a multiple of 16, both
+// addresses 16-byte aligned) completing on `bar` with a transaction count.
+__device__ __forceinline__ void bulk_g2s(void* sdst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(sdst)),
+                 "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+// Waits for phase `parity` of `bar` for at most kWaitLimitNs, whatever the block's error word says
+// (used to drain copies still in flight before a block leaves after an error).
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity))
+        if (globaltimer_ns() - t0 > kWaitLimitNs) return;
+}
 
-// Merges the P partials of row (n, h) and writes the final output and statistics.  The weights
-// exp(m_i - M) of the partials are computed once into shared memory (wsm, >= P floats).
+// Merges the P partials of row (n, h) and writes the final output and statistics; one warp.
+// Partial i carries (max m_i, sum s_i, acc_i[D]); with M the largest m_i of the partials with
+// s_i > 0, w_i = exp(m_i - M) (0 for an empty partial), o = (sum_i w_i acc_i) / (sum_i w_i s_i).
+// Lane l owns dims [l D/32, (l + 1) D/32); the weights of 32 partials at a time are held one per
+// lane and broadcast.
 template <int D, typename T>
-__device__ void merge_row(const RelayParams& p, int n, int h, float* wsm) {
-    __shared__ float s_m, s_tot;
-    __shared__ int s_any;
-    const int tid = threadIdx.x;
+__device__ void merge_row(const RelayParams& p, int n, int h, int lane) {
+    constexpr int DPL = D / 32;  // dims per lane
     const size_t row = (size_t)n * p.H + h;
     const float* pm = p.part_max + row * p.P;
     const float* ps = p.part_sum + row * p.P;
-    if (tid < 32) {
-        float m = -FLT_MAX;
-        int any = 0;
-        for (int i = tid; i < p.P; i += 32)
-            if (__ldcg(ps + i) > 0.f) {
-                m = fmaxf(m, __ldcg(pm + i));
-                any = 1;
-            }
-        m = warp_max(m);
-        any = __any_sync(0xffffffffu, any);
-        float tot = 0.f;
-        for (int i = tid; i < p.P; i += 32) {
-            const float si = __ldcg(ps + i);
-            const float w = si > 0.f ? __expf(__ldcg(pm + i) - m) : 0.f;
-            wsm[i] = w;
-            tot += si * w;
+    float m = -FLT_MAX;
+    int any = 0;
+    for (int i = lane; i < p.P; i += 32)
+        if (__ldcg(ps + i) > 0.f) {
+            m = fmaxf(m, __ldcg(pm + i));
+            any = 1;
         }
-        tot = warp_sum(tot);
-        if (tid == 0) {
-            s_m = m;
-            s_tot = tot;
-            s_any = any;
-        }
-    }
-    __syncthreads();
-    T* out = static_cast<T*>(p.out) + row * D;
-    if (!s_any) {
-        for (int d = tid; d < D; d += THREADS) out[d] = from_f32<T>(0.f);
-        if (tid == 0) {
+    m = warp_max(m);
+    any = __any_sync(0xffffffffu, any);
+    T* out = static_cast<T*>(p.out) + row * D + lane * DPL;
+    if (!any) {
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) out[d] = from_f32<T>(0.f);
+        if (lane == 0) {
             if (p.row_max) p.row_max[row] = 0.f;
             if (p.row_sum) p.row_sum[row] = 1.f;
         }
-    } else {
-        const float* pa = p.part_acc + row * p.P * D;
-        const float inv = 1.f / s_tot;
-        for (int d = tid; d < D; d += THREADS) {
-            float acc = 0.f;
-            for (int i = 0; i < p.P; ++i) acc = fmaf(wsm[i], __ldcg(pa + (size_t)i * D + d), acc);
-            out[d] = from_f32<T>(acc * inv);
+        return;
+    }
+    const float* pa = p.part_acc + row * p.P * D + lane * DPL;
+    float acc[DPL], tot = 0.f;
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) acc[d] = 0.f;
+    for (int i0 = 0; i0 < p.P; i0 += 32) {
+        const int i = i0 + lane;
+        float w = 0.f;
+        if (i < p.P) {
+            const float si = __ldcg(ps + i);
+            w = si > 0.f ? __expf(__ldcg(pm + i) - m) : 0.f;
+            tot += si * w;
         }
-        if (tid == 0) {
-            if (p.row_max) p.row_max[row] = s_m;
-            if (p.row_sum) p.row_sum[row] = s_tot;
+        const int cnt = min(32, p.P - i0);
+#pragma unroll 4
+        for (int j = 0; j < cnt; ++j) {
+            const float wj = __shfl_sync(0xffffffffu, w, j);
+            const float* src = pa + (size_t)(i0 + j) * D;
+            if constexpr (DPL == 4) {
+                const float4 x = __ldcg(reinterpret_cast<const float4*>(src));
+                acc[0] = fmaf(wj, x.x, acc[0]);
+                acc[1] = fmaf(wj, x.y, acc[1]);
+                acc[2] = fmaf(wj, x.z, acc[2]);
+                acc[3] = fmaf(wj, x.w, acc[3]);
+            } else {
+                const float2 x = __ldcg(reinterpret_cast<const float2*>(src));
+                acc[0] = fmaf(wj, x.x, acc[0]);
+                acc[1] = fmaf(wj, x.y, acc[1]);
+            }
         }
     }
-    __syncthreads();
+    tot = warp_sum(tot);
+    const float inv = 1.f / tot;
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) out[d] = from_f32<T>(acc[d] * inv);
+    if (lane == 0) {
+        if (p.row_max) p.row_max[row] = m;
+        if (p.row_sum) p.row_sum[row] = tot;
+    }
 }
 
-// Adds `inc` arrivals to rows (n0 + r, h), r < nq, and merges the rows this CTA completed.
+// Adds `inc` arrivals to rows (n0 + r, h), r < nq, and merges the rows this CTA completed, one
+// warp per row.
 template <int D, typename T>
-__device__ void arrive_rows(const RelayParams& p, int n0, int nq, int h, unsigned inc, float* wsm) {
+__device__ void arrive_rows(const RelayParams& p, int n0, int nq, int h, unsigned inc) {
     __shared__ int s_last[NQ];
     __shared__ int s_nlast;
     __threadfence();
@@ -159,30 +200,33 @@ __device__ void arrive_rows(const RelayParams& p, int n0, int nq, int h, unsigne
     const int nl = s_nlast;
     if (nl > 0) {
         __threadfence();
-        for (int i = 0; i < nl; ++i) {
-            merge_row<D, T>(p, s_last[i], h, wsm);
-            if (threadIdx.x == 0) p.counter[(size_t)s_last[i] * p.H + h] = 0u;
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        for (int i = warp; i < nl; i += THREADS / 32) {
+            merge_row<D, T>(p, s_last[i], h, lane);
+            if (lane == 0) p.counter[(size_t)s_last[i] * p.H + h] = 0u;
         }
     }
     __syncthreads();
 }
 
 // ------------------------------------------------------------------ prefix partials, bf16 MMA
-// A prefix CTA streams up to TILES_BF16 x 64 keys of head h through shared memory and keeps, per
-// query, an online-softmax partial (max, sum, acc[D]) -- the relay_attention_kernel.rs:73-111
-// recurrence, applied to 32-key sub-tiles of tensor-core scores.  Warp w owns queries
+// A prefix item (head h, prefix block pb) streams up to TILES_BF16 x 64 keys of head h through two
+// shared-memory buffers (the next tile in flight while one is computed) and keeps, per query, an
+// online-softmax partial (max, sum, acc[D]) -- the relay_attention_kernel.rs:73-111 recurrence,
+// applied to 32-key sub-tiles of tensor-core scores (mma.sync: a kernel with tcgen05 instructions
+// runs one CTA per SM, which would halve the own stream's residency).  Warp w owns queries
 // [16 (w & 3), +16) and output dimensions [D/2 (w >> 2), +D/2); both warps of a query block
 // compute the same scores.
 template <int D>
-__device__ void prefix_block_bf16(const RelayParams& p, unsigned char* smem) {
+__device__ void prefix_block_bf16(const RelayParams& p, unsigned char* smem, int item) {
     using T = __nv_bfloat16;
     constexpr int LD = D + PAD;
     constexpr int DH = D / 2;  // output dims per warp
     T* sQ = reinterpret_cast<T*>(smem);  // [NQ][LD]
-    T* sK = sQ + NQ * LD;                // [BP][LD]
-    T* sV = sK + BP * LD;                // [BP][LD]
+    T* sKb = sQ + NQ * LD;               // [2][BP][LD]: tile t in buffer t & 1
+    T* sVb = sKb + 2 * BP * LD;          // [2][BP][LD]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int h = blockIdx.x / p.NPB, pb = blockIdx.x - h * p.NPB;
+    const int h = item / p.NPB, pb = item - h * p.NPB;
     const int qb = warp & 3, dh = warp >> 2;
     const int keyA = pb * p.bpc;
     const int keyB = min(p.Lp, keyA + p.bpc);
@@ -200,22 +244,37 @@ __device__ void prefix_block_bf16(const RelayParams& p, unsigned char* smem) {
         float o[DH / 8][4];
 #pragma unroll
         for (int j = 0; j < DH / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-        for (int k0 = keyA; k0 < keyB; k0 += BP) {
+        // K and V tiles stream through two buffers: tile t + 1 is in flight (cp.async, keys past
+        // the block's end zero-filled) while tile t is computed.
+        auto fetch = [&](int k0, int buf) {
             const int nkeys = min(BP, keyB - k0);
             const T* kp = static_cast<const T*>(p.kp) + ((size_t)h * p.Lp + k0) * D;
             const T* vp = static_cast<const T*>(p.vp) + ((size_t)h * p.Lp + k0) * D;
-            __syncthreads();  // previous tile consumed
+            T* dK = sKb + buf * BP * LD;
+            T* dV = sVb + buf * BP * LD;
             for (int x = tid; x < BP * CPR; x += THREADS) {
                 const int r = x / CPR, c = (x - r * CPR) * 8;
-                uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-                if (r < nkeys) {
-                    kv = __ldcs(reinterpret_cast<const uint4*>(kp + (size_t)r * D + c));
-                    vv = __ldcs(reinterpret_cast<const uint4*>(vp + (size_t)r * D + c));
-                }
-                *reinterpret_cast<uint4*>(sK + r * LD + c) = kv;
-                *reinterpret_cast<uint4*>(sV + r * LD + c) = vv;
+                const bool ok = r < nkeys;
+                const size_t off = (size_t)(ok ? r : 0) * D + c;
+                cp16_zfill(dK + r * LD + c, kp + off, ok ? 16 : 0);
+                cp16_zfill(dV + r * LD + c, vp + off, ok ? 16 : 0);
             }
-            __syncthreads();
+            cp_commit();
+        };
+        __syncthreads();  // the previous query block's tiles are consumed
+        if (keyA < keyB) fetch(keyA, 0);
+        int buf = 0;
+        for (int k0 = keyA; k0 < keyB; k0 += BP, buf ^= 1) {
+            const int nkeys = min(BP, keyB - k0);
+            const T* sK = sKb + buf * BP * LD;
+            const T* sV = sVb + buf * BP * LD;
+            if (k0 + BP < keyB) {
+                fetch(k0 + BP, buf ^ 1);  // its buffer was released by the barrier that ended tile t - 1
+                cp_wait<1>();
+            } else {
+                cp_wait<0>();
+            }
+            __syncthreads();  // tile t visible to every warp
 #pragma unroll 1
             for (int sub = 0; sub < BP; sub += 32) {
                 // S[16 x 32] = Q[qb] K[sub..sub+32]^T
@@ -300,6 +359,7 @@ __device__ void prefix_block_bf16(const RelayParams& p, unsigned char* smem) {
                     }
                 }
             }
+            __syncthreads();  // every warp is done with buffer `buf` before it is refilled
         }
         const int pidx = pb;
 #pragma unroll
@@ -317,7 +377,7 @@ __device__ void prefix_block_bf16(const RelayParams& p, unsigned char* smem) {
                 }
             }
         }
-        arrive_rows<D, T>(p, n0, nq, h, 1u, reinterpret_cast<float*>(smem));
+        arrive_rows<D, T>(p, n0, nq, h, 1u);
     }
 }
 
@@ -403,12 +463,13 @@ __device__ void prefix_block_f32(const RelayParams& p, unsigned char* smem) {
         }
     }
     // Both partials of every row are written: KSPLIT arrivals per row.
-    for (int n0 = 0; n0 < p.N; n0 += NQ) arrive_rows<D, float>(p, n0, min(NQ, p.N - n0), h, KSPLIT, reinterpret_cast<float*>(smem));
+    for (int n0 = 0; n0 < p.N; n0 += NQ) arrive_rows<D, float>(p, n0, min(NQ, p.N - n0), h, KSPLIT);
 }
 
-// ------------------------------------------------------------------------- own-segment partials
-template <int D, typename T>
-__device__ void own_block(const RelayParams& p, unsigned char* smem) {
+// ------------------------------------------------------------------------- own partials, f32
+template <int D>
+__device__ void own_block_f32(const RelayParams& p, unsigned char* smem) {
+    using T = float;
     constexpr int EPL = 16 / sizeof(T);   // elements per 16-byte lane load
     constexpr int LPK = D / EPL;          // lanes per key row
     constexpr int KPW = 32 / LPK;         // keys per warp instruction
@@ -430,192 +491,321 @@ __device__ void own_block(const RelayParams& p, unsigned char* smem) {
     const T* vo = static_cast<const T*>(p.vo) + (row * p.Lo + key0) * D;
     constexpr int KEYS_PER_WARP = BO / NW;
     constexpr int ITER = KEYS_PER_WARP / KPW;
-    if constexpr (sizeof(T) == 4) {
-        // f32: the prefix SIMT path's exact arithmetic (pre-scaled q, one fma chain over d), so
-        // that equal keys in the two segments give bit-equal scores (relay_tests.rs:47-90).
-        float* sq = sacc;  // [D], reused before the value pass
-        for (int c = tid; c < D; c += THREADS) sq[c] = to_f32(static_cast<const T*>(p.q)[row * D + c]) * p.scale;
-        __syncthreads();
-        for (int key = tid; key < BO; key += THREADS) {
-            float d = 0.f;
-            if (key < nkeys) {
-                const T* kr = ko + (size_t)key * D;
+    // f32: the prefix SIMT path's exact arithmetic (pre-scaled q, one fma chain over d), so
+    // that equal keys in the two segments give bit-equal scores (relay_tests.rs:47-90).
+    float* sq = sacc;  // [D], reused before the value pass
+    for (int c = tid; c < D; c += THREADS) sq[c] = to_f32(static_cast<const T*>(p.q)[row * D + c]) * p.scale;
+    __syncthreads();
+    for (int key = tid; key < BO; key += THREADS) {
+        float d = 0.f;
+        if (key < nkeys) {
+            const T* kr = ko + (size_t)key * D;
 #pragma unroll 8
-                for (int c = 0; c < D; ++c) d = fmaf(sq[c], to_f32(kr[c]), d);
-            }
-            se[key] = key < nkeys ? d : -FLT_MAX;
+            for (int c = 0; c < D; ++c) d = fmaf(sq[c], to_f32(kr[c]), d);
         }
-        __syncthreads();
-        float m = -FLT_MAX;
-        for (int k = lane; k < BO; k += 32) m = fmaxf(m, se[k]);
-        m = warp_max(m);  // every warp computes the block max redundantly
-        __syncthreads();
-        float lsum = 0.f;
-        for (int k = tid; k < BO; k += THREADS) {
-            const float e = k < nkeys ? __expf(se[k] - m) : 0.f;
-            se[k] = e;
-            lsum += e;
-        }
-        lsum = warp_sum(lsum);
-        if (lane == 0) s_red[1][warp] = lsum;
-        __syncthreads();
-        float l = 0.f;
+        se[key] = key < nkeys ? d : -FLT_MAX;
+    }
+    __syncthreads();
+    float m = -FLT_MAX;
+    for (int k = lane; k < BO; k += 32) m = fmaxf(m, se[k]);
+    m = warp_max(m);  // every warp computes the block max redundantly
+    __syncthreads();
+    float lsum = 0.f;
+    for (int k = tid; k < BO; k += THREADS) {
+        const float e = k < nkeys ? __expf(se[k] - m) : 0.f;
+        se[k] = e;
+        lsum += e;
+    }
+    lsum = warp_sum(lsum);
+    if (lane == 0) s_red[1][warp] = lsum;
+    __syncthreads();
+    float l = 0.f;
 #pragma unroll
-        for (int w = 0; w < NW; ++w) l += s_red[1][w];
-        // acc[d] = sum_key e[key] v[key][d]; lane holds EPL dims of one key slot
-        float acc[EPL];
+    for (int w = 0; w < NW; ++w) l += s_red[1][w];
+    // acc[d] = sum_key e[key] v[key][d]; lane holds EPL dims of one key slot
+    float acc[EPL];
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
+    for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
 #pragma unroll 8
-        for (int it = 0; it < ITER; ++it) {
-            const int key = warp * KEYS_PER_WARP + it * KPW + sub;
-            if (key < nkeys) {
-                const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(vo + (size_t)key * D + part * EPL));
-                const T* x = reinterpret_cast<const T*>(&raw);
-                const float w = se[key];
+    for (int it = 0; it < ITER; ++it) {
+        const int key = warp * KEYS_PER_WARP + it * KPW + sub;
+        if (key < nkeys) {
+            const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(vo + (size_t)key * D + part * EPL));
+            const T* x = reinterpret_cast<const T*>(&raw);
+            const float w = se[key];
 #pragma unroll
-                for (int e = 0; e < EPL; ++e) acc[e] = fmaf(w, to_f32(x[e]), acc[e]);
-            }
-        }
-#pragma unroll
-        for (int o = LPK; o < 32; o <<= 1)
-#pragma unroll
-            for (int e = 0; e < EPL; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
-        if (sub == 0)
-#pragma unroll
-            for (int e = 0; e < EPL; ++e) sacc[warp * D + part * EPL + e] = acc[e];
-        __syncthreads();
-        const int pi = p.NPB * p.ppc + ob;
-        for (int d = tid; d < D; d += THREADS) {
-            float a = 0.f;
-#pragma unroll
-            for (int w = 0; w < NW; ++w) a += sacc[w * D + d];
-            p.part_acc[(row * p.P + pi) * D + d] = a;
-        }
-        if (tid == 0) {
-            p.part_max[row * p.P + pi] = m;
-            p.part_sum[row * p.P + pi] = nkeys > 0 ? l : 0.f;
-        }
-    } else {
-        // bf16: one pass.  Each warp runs an online softmax over its keys in groups of KPW x U,
-        // loading the K and V rows of a group together (2U 16-byte loads in flight per lane);
-        // products of bf16 values are exact in f32 and the score is scaled after the sum, as the
-        // tensor-core prefix path does.  The warps' (max, sum, acc) are merged at the end.
-        constexpr int U = 4;
-        float qv[EPL];
-        const T* q = static_cast<const T*>(p.q) + row * D + part * EPL;
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) qv[e] = to_f32(q[e]);
-        float m = -FLT_MAX, l = 0.f, acc[EPL];
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
-        for (int g = 0; g < ITER; g += U) {
-            uint4 kr[U], vr[U];
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int key = warp * KEYS_PER_WARP + (g + u) * KPW + sub;
-                if (key < nkeys) {
-                    kr[u] = __ldcs(reinterpret_cast<const uint4*>(ko + (size_t)key * D + part * EPL));
-                    vr[u] = __ldcs(reinterpret_cast<const uint4*>(vo + (size_t)key * D + part * EPL));
-                } else {
-                    kr[u] = make_uint4(0, 0, 0, 0);
-                    vr[u] = make_uint4(0, 0, 0, 0);
-                }
-            }
-            float sc[U];
-            float mg = -FLT_MAX;
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const T* x = reinterpret_cast<const T*>(&kr[u]);
-                float d = 0.f;
-#pragma unroll
-                for (int e = 0; e < EPL; ++e) d = fmaf(qv[e], to_f32(x[e]), d);
-#pragma unroll
-                for (int o = LPK / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-                const int key = warp * KEYS_PER_WARP + (g + u) * KPW + sub;
-                sc[u] = key < nkeys ? d * p.scale : -FLT_MAX;
-                mg = fmaxf(mg, sc[u]);
-            }
-#pragma unroll
-            for (int o = LPK; o < 32; o <<= 1) mg = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, o));  // every key slot
-            const float mn = fmaxf(m, mg);
-            const float corr = __expf(m - mn);  // 0 while nothing was seen (acc and l are 0 then)
-            l *= corr;
-#pragma unroll
-            for (int e = 0; e < EPL; ++e) acc[e] *= corr;
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int key = warp * KEYS_PER_WARP + (g + u) * KPW + sub;
-                const float w = key < nkeys ? __expf(sc[u] - mn) : 0.f;
-                if (part == 0) l += w;
-                const T* x = reinterpret_cast<const T*>(&vr[u]);
-#pragma unroll
-                for (int e = 0; e < EPL; ++e) acc[e] = fmaf(w, to_f32(x[e]), acc[e]);
-            }
-            m = mn;
-        }
-#pragma unroll
-        for (int o = LPK; o < 32; o <<= 1)
-#pragma unroll
-            for (int e = 0; e < EPL; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
-        l = warp_sum(l);
-        if (sub == 0)
-#pragma unroll
-            for (int e = 0; e < EPL; ++e) sacc[warp * D + part * EPL + e] = acc[e];
-        if (lane == 0) {
-            s_red[0][warp] = m;
-            s_red[1][warp] = l;
-        }
-        __syncthreads();
-        float mb = -FLT_MAX;
-#pragma unroll
-        for (int w = 0; w < NW; ++w) mb = fmaxf(mb, s_red[0][w]);
-        float fw[NW], lb = 0.f;
-#pragma unroll
-        for (int w = 0; w < NW; ++w) {
-            fw[w] = __expf(s_red[0][w] - mb);
-            lb = fmaf(fw[w], s_red[1][w], lb);
-        }
-        const int pi = p.NPB * p.ppc + ob;
-        for (int d = tid; d < D; d += THREADS) {
-            float a = 0.f;
-#pragma unroll
-            for (int w = 0; w < NW; ++w) a = fmaf(fw[w], sacc[w * D + d], a);
-            p.part_acc[(row * p.P + pi) * D + d] = a;
-        }
-        if (tid == 0) {
-            p.part_max[row * p.P + pi] = mb;
-            p.part_sum[row * p.P + pi] = nkeys > 0 ? lb : 0.f;
+            for (int e = 0; e < EPL; ++e) acc[e] = fmaf(w, to_f32(x[e]), acc[e]);
         }
     }
-    arrive_rows<D, T>(p, n, 1, h, 1u, se);
+#pragma unroll
+    for (int o = LPK; o < 32; o <<= 1)
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
+    if (sub == 0)
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) sacc[warp * D + part * EPL + e] = acc[e];
+    __syncthreads();
+    const int pi = p.NPB * p.ppc + ob;
+    for (int d = tid; d < D; d += THREADS) {
+        float a = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) a += sacc[w * D + d];
+        p.part_acc[(row * p.P + pi) * D + d] = a;
+    }
+    if (tid == 0) {
+        p.part_max[row * p.P + pi] = m;
+        p.part_sum[row * p.P + pi] = nkeys > 0 ? l : 0.f;
+    }
+    arrive_rows<D, T>(p, n, 1, h, 1u);
 }
 
-template <int D, typename T>
-__global__ void __launch_bounds__(THREADS, MIN_BLOCKS) relay_merge_kernel(const RelayParams p) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    if ((int)blockIdx.x < p.H * p.NPB) {
-        if constexpr (sizeof(T) == 2) prefix_block_bf16<D>(p, smem_raw);
-        else prefix_block_f32<D>(p, smem_raw);
-    } else {
-        own_block<D, T>(p, smem_raw);
+// ------------------------------------------------------------------ bf16: own items
+// An own CTA (sequence n, head h, 1024-key own block ob) streams its block through a ring of
+// OWN_NS stages of OWN_SK keys in shared memory (K rows, then V rows: two bulk copies per stage,
+// issued by thread 0, which refills a stage once every warp has released it).  Warp w reads keys
+// [w KW, (w + 1) KW) of every stage and runs an online softmax over them; the stage that holds the
+// block's end zeroes the keys past it in registers.  The arithmetic runs on packed f32 pairs
+// (fma.rn.f32x2: each half is one correctly rounded FMA): products of bf16 values are exact in f32,
+// the dot product keeps even and odd elements in two partial sums, and the score is scaled after
+// the sum, as the tensor-core prefix path does.  The warps' (max, sum, acc) are merged at the end.
+// (A persistent grid streaming several blocks per CTA through the same ring was measured slower:
+// the per-key arithmetic bounds the own segment, not the stream.)
+constexpr int OWN_SK = 64;    // keys per ring stage
+constexpr int OWN_NS = 3;     // ring stages
+constexpr int BO_BF16 = 1024; // own keys per bf16 own CTA
+
+template <int D>
+struct OwnLayout {
+    static constexpr int ROWB = D * 2;                        // bytes of one bf16 key row
+    static constexpr int STAGE = 2 * OWN_SK * ROWB;           // K rows, then V rows
+    static constexpr int OFF_BAR = OWN_NS * STAGE;            // full[NS], empty[NS]
+    static constexpr int OFF_ERR = OFF_BAR + 16 * OWN_NS;
+    static constexpr int OFF_ACC = OFF_ERR + 16;              // [NW][D] f32
+    static constexpr int BYTES = OFF_ACC + 4 * (THREADS / 32) * D;
+};
+
+// Two bf16 (element 2j in the low half) as an f32 pair.
+__device__ __forceinline__ float2 bf16x2_f32x2(uint32_t x) {
+    return make_float2(__uint_as_float(x << 16), __uint_as_float(x & 0xFFFF0000u));
+}
+// c = a * b + c on f32 pairs.
+__device__ __forceinline__ void ffma2(float2& c, float2 a, float2 b) {
+    asm("{.reg .b64 ra, rb, rc;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%0, %1};\n\t"
+        "fma.rn.f32x2 rc, ra, rb, rc;\n\tmov.b64 {%0, %1}, rc;\n\t}"
+        : "+f"(c.x), "+f"(c.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+}
+// c = c * s on an f32 pair.
+__device__ __forceinline__ void fmul2(float2& c, float s) {
+    asm("{.reg .b64 ra, rs;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rs, {%2, %2};\n\t"
+        "mul.rn.f32x2 ra, ra, rs;\n\tmov.b64 {%0, %1}, ra;\n\t}"
+        : "+f"(c.x), "+f"(c.y)
+        : "f"(s));
+}
+
+template <int D>
+__device__ void own_block_bf16(const RelayParams& p, unsigned char* smem) {
+    using L = OwnLayout<D>;
+    constexpr int EPL = 8;            // bf16 elements per 16-byte lane load
+    constexpr int LPK = D / EPL;      // lanes per key row
+    constexpr int KPW = 32 / LPK;     // keys per warp instruction
+    constexpr int NW = THREADS / 32;
+    constexpr int SK = OWN_SK, NS = OWN_NS;
+    constexpr int KW = SK / NW;       // keys of one warp in a stage
+    constexpr int U = KW / KPW;       // 16-byte loads per lane per stage, K and V each
+    constexpr int ROWB = L::ROWB;
+    static_assert(KW % KPW == 0 && U >= 1, "stage keys must cover whole warp instructions");
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+    uint64_t* empty = full + NS;
+    int* serr = reinterpret_cast<int*>(smem + L::OFF_ERR);
+    float* sacc = reinterpret_cast<float*>(smem + L::OFF_ACC);
+    __shared__ float s_red[2][NW];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int bid = blockIdx.x - p.H * p.NPB;
+    const int ob = bid % p.NOB;
+    const int nh = bid / p.NOB;
+    const int n = nh / p.H, h = nh - n * p.H;
+    const int own = p.own_len ? min(max(p.own_len[n], 0), p.Lo) : p.Lo;
+    const int key0 = ob * BO_BF16;
+    const int nkeys = max(0, min(BO_BF16, own - key0));
+    const size_t row = (size_t)n * p.H + h;
+    const int sub = lane / LPK, part = lane % LPK;  // key slot within the warp, chunk of the row
+    const __nv_bfloat16* ko = static_cast<const __nv_bfloat16*>(p.ko) + (row * p.Lo + key0) * D;
+    const __nv_bfloat16* vo = static_cast<const __nv_bfloat16*>(p.vo) + (row * p.Lo + key0) * D;
+    const int nst = (nkeys + SK - 1) / SK;
+    if (tid == 0) {
+        for (int i = 0; i < NS; ++i) {
+            mbar_init(full + i, 1);
+            mbar_init(empty + i, NW);
+        }
+        *serr = 0;
+        fence_mbar_init();
     }
+    __syncthreads();
+    int issued = 0;  // thread 0: stages whose copies were issued
+    auto issue = [&](int st) {
+        const int k0 = st * SK;
+        const uint32_t bytes = (uint32_t)min(SK, nkeys - k0) * ROWB;
+        unsigned char* dst = smem + (size_t)(st % NS) * L::STAGE;
+        mbar_arrive_expect_tx(full + st % NS, 2 * bytes);
+        bulk_g2s(dst, ko + (size_t)k0 * D, bytes, full + st % NS);
+        bulk_g2s(dst + SK * ROWB, vo + (size_t)k0 * D, bytes, full + st % NS);
+        issued = st + 1;
+    };
+    if (tid == 0)
+        for (int st = 0; st < min(NS, nst); ++st) issue(st);
+    float2 q2[EPL / 2];
+    {
+        const uint4 qx = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.q) + row * D + part * EPL);
+        q2[0] = bf16x2_f32x2(qx.x);
+        q2[1] = bf16x2_f32x2(qx.y);
+        q2[2] = bf16x2_f32x2(qx.z);
+        q2[3] = bf16x2_f32x2(qx.w);
+    }
+    float m = -FLT_MAX, l = 0.f;
+    float2 acc2[EPL / 2];
+#pragma unroll
+    for (int j = 0; j < EPL / 2; ++j) acc2[j] = make_float2(0.f, 0.f);
+    int consumed = 0;
+    for (int s = 0; s < nst; ++s) {
+        const int slot = s % NS;
+        const uint32_t par = (uint32_t)(s / NS) & 1u;
+        // warp-uniform: a warp leaves the loop whole if any of its lanes gave up
+        if (!__all_sync(0xffffffffu, mbar_wait(full + slot, par, serr, kRelayWaitFull))) break;
+        consumed = s + 1;
+        const bool tail = (s + 1) * SK > nkeys;  // the stage that holds the block's end (block-uniform)
+        const unsigned char* src = smem + (size_t)slot * L::STAGE + (size_t)(warp * KW + sub) * ROWB + part * 16;
+        uint4 kr[U], vr[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            kr[u] = *reinterpret_cast<const uint4*>(src + u * KPW * ROWB);
+            vr[u] = *reinterpret_cast<const uint4*>(src + SK * ROWB + u * KPW * ROWB);
+        }
+        if (tail) {  // rows past the block's end hold stale bytes: zero them
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+                if (s * SK + warp * KW + u * KPW + sub >= nkeys) kr[u] = vr[u] = make_uint4(0, 0, 0, 0);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + slot);  // this warp's reads of the slot are done
+        if (tid == 0 && s + NS < nst) {
+            if (mbar_wait(empty + slot, par, serr, kRelayWaitEmpty)) issue(s + NS);
+        }
+        float sc[U];
+        float mg = -FLT_MAX;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            float2 d2 = make_float2(0.f, 0.f);
+            ffma2(d2, q2[0], bf16x2_f32x2(kr[u].x));
+            ffma2(d2, q2[1], bf16x2_f32x2(kr[u].y));
+            ffma2(d2, q2[2], bf16x2_f32x2(kr[u].z));
+            ffma2(d2, q2[3], bf16x2_f32x2(kr[u].w));
+            float d = d2.x + d2.y;
+#pragma unroll
+            for (int o = LPK / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+            sc[u] = d * p.scale;
+            if (tail && s * SK + warp * KW + u * KPW + sub >= nkeys) sc[u] = -FLT_MAX;
+            mg = fmaxf(mg, sc[u]);
+        }
+#pragma unroll
+        for (int o = LPK; o < 32; o <<= 1) mg = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, o));  // every key slot
+        const float mn = fmaxf(m, mg);
+        const float corr = __expf(m - mn);  // 0 while nothing was seen (acc and l are 0 then)
+        l *= corr;
+#pragma unroll
+        for (int j = 0; j < EPL / 2; ++j) fmul2(acc2[j], corr);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            float w = __expf(sc[u] - mn);
+            if (tail && s * SK + warp * KW + u * KPW + sub >= nkeys) w = 0.f;
+            if (part == 0) l += w;
+            const float2 w2 = make_float2(w, w);
+            ffma2(acc2[0], w2, bf16x2_f32x2(vr[u].x));
+            ffma2(acc2[1], w2, bf16x2_f32x2(vr[u].y));
+            ffma2(acc2[2], w2, bf16x2_f32x2(vr[u].z));
+            ffma2(acc2[3], w2, bf16x2_f32x2(vr[u].w));
+        }
+        m = mn;
+    }
+    // A block that gave up at a wait still owns the copies it issued: let them land first.
+    if (tid == 0) {
+        for (int st = consumed; st < issued; ++st) mbar_drain(full + st % NS, (uint32_t)(st / NS) & 1u);
+        if (*serr != 0) atomicExch(p.err, *serr);
+    }
+    float acc[EPL];
+#pragma unroll
+    for (int j = 0; j < EPL / 2; ++j) {
+        acc[2 * j] = acc2[j].x;
+        acc[2 * j + 1] = acc2[j].y;
+    }
+#pragma unroll
+    for (int o = LPK; o < 32; o <<= 1)
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
+    l = warp_sum(l);
+    if (sub == 0)
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) sacc[warp * D + part * EPL + e] = acc[e];
+    if (lane == 0) {
+        s_red[0][warp] = m;
+        s_red[1][warp] = l;
+    }
+    __syncthreads();
+    float mb = -FLT_MAX;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) mb = fmaxf(mb, s_red[0][w]);
+    float fw[NW], lb = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+        fw[w] = __expf(s_red[0][w] - mb);
+        lb = fmaf(fw[w], s_red[1][w], lb);
+    }
+    const int pi = p.NPB * p.ppc + ob;
+    for (int d = tid; d < D; d += THREADS) {
+        float a = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) a = fmaf(fw[w], sacc[w * D + d], a);
+        p.part_acc[(row * p.P + pi) * D + d] = a;
+    }
+    if (tid == 0) {
+        p.part_max[row * p.P + pi] = mb;
+        p.part_sum[row * p.P + pi] = nkeys > 0 ? lb : 0.f;
+    }
+    arrive_rows<D, __nv_bfloat16>(p, n, 1, h, 1u);
+}
+
+template <int D>
+__global__ void __launch_bounds__(THREADS, 2) relay_merge_kernel_bf16(const RelayParams p) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    if ((int)blockIdx.x < p.H * p.NPB) prefix_block_bf16<D>(p, smem_raw, (int)blockIdx.x);
+    else own_block_bf16<D>(p, smem_raw);
+}
+
+
+template <int D>
+__global__ void __launch_bounds__(THREADS, MIN_BLOCKS_F32) relay_merge_kernel_f32(const RelayParams p) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    if ((int)blockIdx.x < p.H * p.NPB) prefix_block_f32<D>(p, smem_raw);
+    else own_block_f32<D>(p, smem_raw);
 }
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 struct Layout {
-    int NPB, NOB, P, bpc, ppc;
-    size_t off_acc, off_max, off_sum, off_cnt, total;
+    int NPB, NOB, P, bpc, ppc, bo;
+    size_t off_acc, off_max, off_sum, off_cnt, n_cnt, total;
 };
 
-// bf16: one partial per 512-key prefix CTA; f32: two partials per 64-key prefix CTA.
+// bf16: one partial per 512-key prefix CTA and per 1024-key own CTA; f32: two partials per 64-key
+// prefix CTA and one per 1024-key own CTA; one arrival counter per (n, h) row.
 Layout layout(int64_t N, int64_t H, int64_t D, int64_t Lp, int64_t Lo, bool bf16) {
     Layout L{};
     L.bpc = bf16 ? BP * TILES_BF16 : BP;
     L.ppc = bf16 ? 1 : KSPLIT;
+    L.bo = bf16 ? BO_BF16 : BO;
     L.NPB = (int)((Lp + L.bpc - 1) / L.bpc);
-    L.NOB = (int)((Lo + BO - 1) / BO);
+    L.NOB = (int)((Lo + L.bo - 1) / L.bo);
     if (L.NOB == 0) L.NOB = 1;  // one (empty) own partial keeps the arrival count uniform
     L.P = L.NPB * L.ppc + L.NOB;
     const size_t rows = (size_t)N * H;
@@ -623,29 +813,42 @@ Layout layout(int64_t N, int64_t H, int64_t D, int64_t Lp, int64_t Lo, bool bf16
     L.off_max = align_up(L.off_acc + rows * L.P * D * sizeof(float), 256);
     L.off_sum = align_up(L.off_max + rows * L.P * sizeof(float), 256);
     L.off_cnt = align_up(L.off_sum + rows * L.P * sizeof(float), 256);
-    L.total = align_up(L.off_cnt + rows * sizeof(unsigned), 256);
+    L.n_cnt = rows;
+    L.total = align_up(L.off_cnt + L.n_cnt * sizeof(unsigned), 256);
     return L;
 }
 
-template <int D, typename T>
-size_t relay_smem(int P) {
-    size_t prefix;
-    if (sizeof(T) == 2) prefix = sizeof(__nv_bfloat16) * (size_t)(NQ + 2 * BP) * (D + PAD);
-    else prefix = sizeof(float) * (size_t)((BP / KSPLIT) * (D + 1) + (BP / KSPLIT) * D + 32 * (D + 1) + 32 * (BP / KSPLIT + 1));
-    size_t own = sizeof(float) * (size_t)(BO + (THREADS / 32) * D);
-    if (own < sizeof(float) * (size_t)P) own = sizeof(float) * (size_t)P;  // merge weights
-    if (prefix < sizeof(float) * (size_t)P) prefix = sizeof(float) * (size_t)P;
+template <int D>
+size_t relay_smem_f32() {
+    const size_t prefix = sizeof(float) * (size_t)((BP / KSPLIT) * (D + 1) + (BP / KSPLIT) * D + 32 * (D + 1) + 32 * (BP / KSPLIT + 1));
+    const size_t own = sizeof(float) * (size_t)(BO + (THREADS / 32) * D);
+    return prefix > own ? prefix : own;
+}
+template <int D>
+size_t relay_smem_bf16() {
+    const size_t prefix = sizeof(__nv_bfloat16) * (size_t)(NQ + 4 * BP) * (D + PAD);
+    const size_t own = OwnLayout<D>::BYTES;
     return prefix > own ? prefix : own;
 }
 
-template <int D, typename T>
-int launch_relay(const RelayParams& p, cudaStream_t st) {
-    const size_t smem = relay_smem<D, T>(p.P);
-    cudaError_t e = cudaFuncSetAttribute(relay_merge_kernel<D, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+template <int D>
+int launch_relay_f32(const RelayParams& p, cudaStream_t st) {
+    const size_t smem = relay_smem_f32<D>();
+    cudaError_t e = cudaFuncSetAttribute(relay_merge_kernel_f32<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_status(e, "relay: cudaFuncSetAttribute");
     const unsigned grid = (unsigned)(p.H * p.NPB + p.N * p.H * p.NOB);
-    relay_merge_kernel<D, T><<<grid, THREADS, smem, st>>>(p);
-    return launch_status("relay_merge_kernel");
+    relay_merge_kernel_f32<D><<<grid, THREADS, smem, st>>>(p);
+    return launch_status("relay_merge_kernel_f32");
+}
+
+template <int D>
+int launch_relay_bf16(const RelayParams& p, cudaStream_t st) {
+    const size_t smem = relay_smem_bf16<D>();
+    cudaError_t e = cudaFuncSetAttribute(relay_merge_kernel_bf16<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_status(e, "relay: cudaFuncSetAttribute");
+    const unsigned grid = (unsigned)(p.H * p.NPB + p.N * p.H * p.NOB);
+    relay_merge_kernel_bf16<D><<<grid, THREADS, smem, st>>>(p);
+    return launch_status("relay_merge_kernel_bf16");
 }
 
 }  // namespace
@@ -715,11 +918,14 @@ int relay_launch(const dbl_relay_merge_args* a, void* ws, cudaStream_t st) {
     p.part_max = reinterpret_cast<float*>(base + L.off_max);
     p.part_sum = reinterpret_cast<float*>(base + L.off_sum);
     p.counter = reinterpret_cast<unsigned*>(base + L.off_cnt);
-    cudaError_t e = cudaMemsetAsync(p.counter, 0, sizeof(unsigned) * (size_t)p.N * p.H, st);
+    p.bo = L.bo;
+    int rc = device_error_record(&p.err);
+    if (rc != DBL_OK) return rc;
+    cudaError_t e = cudaMemsetAsync(p.counter, 0, sizeof(unsigned) * L.n_cnt, st);
     if (e != cudaSuccess) return cuda_status(e, "relay: clear counters");
     const bool bf = a->dtype == DBL_BF16;
-    if (a->head_dim == 128) return bf ? launch_relay<128, __nv_bfloat16>(p, st) : launch_relay<128, float>(p, st);
-    return bf ? launch_relay<64, __nv_bfloat16>(p, st) : launch_relay<64, float>(p, st);
+    if (a->head_dim == 128) return bf ? launch_relay_bf16<128>(p, st) : launch_relay_f32<128>(p, st);
+    return bf ? launch_relay_bf16<64>(p, st) : launch_relay_f32<64>(p, st);
 }
 
 }  // namespace dbl
