@@ -29,4 +29,4 @@ extern "C" const char* dbl_status_string(int status) {
 
 extern "C" const char* dbl_last_error(void) { return dbl::g_last_error; }
 
-extern "C" int dbl_abi_version(void) { return 10000; }
+extern "C" int dbl_abi_version(void) { return 10100; }  // 1.1.0: span fold, segmented and time-sharded prefill, per-call relay workspace size

@@ -51,8 +51,9 @@ const char *dbl_status_string(int status);
 const char *dbl_last_error(void);
 /* ABI version: major * 10000 + minor * 100 + patch. */
 int dbl_abi_version(void);
-/* Every wait inside the tensor-core kernels is bounded; one that gives up records a site code on
- * the current device and lets the kernel run to completion (its outputs are then undefined).  The
+/* Every wait inside the library's kernels (the tensor-core prefill and relay attention, the relay
+ * merge's copy ring) is bounded; one that gives up records a site code on the current device and
+ * lets the kernel run to completion (its outputs are then undefined).  The
  * tensor-core prefill also records code 100 when one of its fp16 MMA operands left fp16 range
  * (inputs far outside unit-norm keys and beta in [0, 1]; its outputs are then not valid), and
  * relay attention records code 101 when a live row's document id lies outside [0, documents).

@@ -66,7 +66,7 @@ def test_status_strings_and_version(native_lib):
     assert native_lib.dbl_status_string(0) == b"ok"
     assert native_lib.dbl_status_string(N.DBL_ERR_WORKSPACE).startswith(b"workspace")
     assert native_lib.dbl_status_string(99) == b"unknown status"
-    assert native_lib.dbl_abi_version() >= 10000
+    assert native_lib.dbl_abi_version() >= 10100
 
 
 def test_null_and_bad_arguments_return_status(native_lib):
