@@ -33,6 +33,7 @@ constexpr int BO = 1024;      // f32: own keys per own CTA
 constexpr int THREADS = 256;
 constexpr int MIN_BLOCKS_F32 = 3;  // f32 kernel: CTAs per SM its register budget is sized for
 constexpr int PAD = 8;        // bf16 row padding (row stride D+8 elements: conflict-free ldmatrix)
+constexpr int PLD = BP + 8;   // row stride of a prefix P tile (64 keys + 8: conflict-free ldmatrix)
 constexpr int kRelayWaitFull = 30, kRelayWaitEmpty = 31;  // wait-site codes (dbl_device_error)
 
 struct RelayParams {
@@ -84,6 +85,16 @@ __device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
+}
+// The two warps of prefix query block qb (warps qb and qb + 4) meet at named barrier 1 + qb; the
+// ids are spelled out so that the kernel reserves five barriers, not all sixteen.
+__device__ __forceinline__ void pair_sync(int qb) {
+    switch (qb) {
+        case 0: asm volatile("bar.sync 1, 64;" ::: "memory"); break;
+        case 1: asm volatile("bar.sync 2, 64;" ::: "memory"); break;
+        case 2: asm volatile("bar.sync 3, 64;" ::: "memory"); break;
+        default: asm volatile("bar.sync 4, 64;" ::: "memory"); break;
+    }
 }
 // 16-byte asynchronous global -> shared copy through L2 only; src_bytes = 0 reads nothing and
 // fills the 16 bytes with zeros.
@@ -213,10 +224,11 @@ __device__ void arrive_rows(const RelayParams& p, int n0, int nq, int h, unsigne
 // A prefix item (head h, prefix block pb) streams up to TILES_BF16 x 64 keys of head h through two
 // shared-memory buffers (the next tile in flight while one is computed) and keeps, per query, an
 // online-softmax partial (max, sum, acc[D]) -- the relay_attention_kernel.rs:73-111 recurrence,
-// applied to 32-key sub-tiles of tensor-core scores (mma.sync: a kernel with tcgen05 instructions
-// runs one CTA per SM, which would halve the own stream's residency).  Warp w owns queries
-// [16 (w & 3), +16) and output dimensions [D/2 (w >> 2), +D/2); both warps of a query block
-// compute the same scores.
+// applied to 64-key tiles of tensor-core scores (mma.sync: a kernel with tcgen05 instructions runs
+// one CTA per SM, which would halve the own stream's residency).  Warp w owns queries
+// [16 (w & 3), +16) and output dimensions [D/2 (w >> 2), +D/2); the two warps of a query block
+// score one 32-key half of the tile each and exchange their row maxima, row sums and bf16 P
+// through shared memory (double-buffered by tile parity, a 64-thread named barrier per pair).
 template <int D>
 __device__ void prefix_block_bf16(const RelayParams& p, unsigned char* smem, int item) {
     using T = __nv_bfloat16;
@@ -225,6 +237,9 @@ __device__ void prefix_block_bf16(const RelayParams& p, unsigned char* smem, int
     T* sQ = reinterpret_cast<T*>(smem);  // [NQ][LD]
     T* sKb = sQ + NQ * LD;               // [2][BP][LD]: tile t in buffer t & 1
     T* sVb = sKb + 2 * BP * LD;          // [2][BP][LD]
+    T* sP = sVb + 2 * BP * LD;           // [2][4][16][PLD]: each query block's P tile, by tile parity
+    float* spm = reinterpret_cast<float*>(sP + 2 * 4 * 16 * PLD);  // [2][4][2][16] row maxima per half
+    float* sps = spm + 2 * 4 * 2 * 16;                              // [2][4][2][16] row sums per half
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int h = item / p.NPB, pb = item - h * p.NPB;
     const int qb = warp & 3, dh = warp >> 2;
@@ -275,9 +290,9 @@ __device__ void prefix_block_bf16(const RelayParams& p, unsigned char* smem, int
                 cp_wait<0>();
             }
             __syncthreads();  // tile t visible to every warp
-#pragma unroll 1
-            for (int sub = 0; sub < BP; sub += 32) {
-                // S[16 x 32] = Q[qb] K[sub..sub+32]^T
+            {
+                // S[16 x 32] = Q[qb] K[sub..sub+32]^T for this warp's half of the tile
+                const int sub = 32 * dh;
                 float sc[4][4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
@@ -310,13 +325,22 @@ __device__ void prefix_block_bf16(const RelayParams& p, unsigned char* smem, int
                 t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, 2));
                 t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, 1));
                 t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, 2));
-                if (sub >= nkeys) continue;  // no key in this sub-tile
-                const float n0m = fmaxf(m0, t0), n1m = fmaxf(m1, t1);
+                // the pair's row maxima over the whole tile
+                const int g = lane >> 2;
+                float* pm = spm + ((buf * 4 + qb) * 2 + dh) * 16;
+                const float* pmo = spm + ((buf * 4 + qb) * 2 + (dh ^ 1)) * 16;
+                if ((lane & 3) == 0) {
+                    pm[g] = t0;
+                    pm[g + 8] = t1;
+                }
+                pair_sync(qb);
+                const float n0m = fmaxf(m0, fmaxf(t0, pmo[g])), n1m = fmaxf(m1, fmaxf(t1, pmo[g + 8]));
                 const float c0 = l0 > 0.f ? __expf(m0 - n0m) : 0.f, c1 = l1 > 0.f ? __expf(m1 - n1m) : 0.f;
                 m0 = n0m;
                 m1 = n1m;
+                // P of this half (bf16) into the pair's [16 x 64] tile, its row sums to the pair
+                T* P = sP + (buf * 4 + qb) * 16 * PLD;
                 float s0 = 0.f, s1 = 0.f;
-                uint32_t pa[2][4];
 #pragma unroll
                 for (int nt = 0; nt < 4; ++nt) {
                     float e0[2], e1[2];
@@ -328,16 +352,26 @@ __device__ void prefix_block_bf16(const RelayParams& p, unsigned char* smem, int
                         s0 += e0[e];
                         s1 += e1[e];
                     }
-                    const int ks = nt >> 1, hi = nt & 1;
-                    pa[ks][hi ? 2 : 0] = pack_bf16(e0[0], e0[1]);
-                    pa[ks][hi ? 3 : 1] = pack_bf16(e1[0], e1[1]);
+                    const int col = sub + nt * 8 + (lane & 3) * 2;
+                    *reinterpret_cast<uint32_t*>(P + g * PLD + col) = pack_bf16(e0[0], e0[1]);
+                    *reinterpret_cast<uint32_t*>(P + (g + 8) * PLD + col) = pack_bf16(e1[0], e1[1]);
                 }
                 s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
                 s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
                 s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
                 s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
-                l0 = l0 * c0 + s0;
-                l1 = l1 * c1 + s1;
+                float* ps = sps + ((buf * 4 + qb) * 2 + dh) * 16;
+                const float* pso = sps + ((buf * 4 + qb) * 2 + (dh ^ 1)) * 16;
+                if ((lane & 3) == 0) {
+                    ps[g] = s0;
+                    ps[g + 8] = s1;
+                }
+                pair_sync(qb);
+                // both warps of the pair form the same sums (half 0 + half 1)
+                const float r0 = dh == 0 ? s0 + pso[g] : pso[g] + s0;
+                const float r1 = dh == 0 ? s1 + pso[g + 8] : pso[g + 8] + s1;
+                l0 = l0 * c0 + r0;
+                l1 = l1 * c1 + r1;
 #pragma unroll
                 for (int j = 0; j < DH / 8; ++j) {
                     o[j][0] *= c0;
@@ -345,17 +379,19 @@ __device__ void prefix_block_bf16(const RelayParams& p, unsigned char* smem, int
                     o[j][2] *= c1;
                     o[j][3] *= c1;
                 }
-                // O[16 x DH] += P[16 x 32] V[sub..sub+32][dh*DH ..]
+                // O[16 x DH] += P[16 x 64] V[tile][dh*DH ..]
 #pragma unroll
-                for (int ks = 0; ks < 2; ++ks) {
+                for (int ks = 0; ks < BP / 16; ++ks) {
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4(smem_u32(P + (lane & 15) * PLD + ks * 16 + (lane >> 4) * 8), a0, a1, a2, a3);
 #pragma unroll
                     for (int dt = 0; dt < DH / 8; dt += 2) {
                         uint32_t b0, b1, b2, b3;
-                        ldsm_x4_t(smem_u32(sV + (sub + ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * LD + dh * DH + dt * 8 +
+                        ldsm_x4_t(smem_u32(sV + (ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * LD + dh * DH + dt * 8 +
                                            (lane >> 4) * 8),
                                   b0, b1, b2, b3);
-                        mma_bf16(o[dt], pa[ks][0], pa[ks][1], pa[ks][2], pa[ks][3], b0, b1);
-                        mma_bf16(o[dt + 1], pa[ks][0], pa[ks][1], pa[ks][2], pa[ks][3], b2, b3);
+                        mma_bf16(o[dt], a0, a1, a2, a3, b0, b1);
+                        mma_bf16(o[dt + 1], a0, a1, a2, a3, b2, b3);
                     }
                 }
             }
@@ -826,7 +862,8 @@ size_t relay_smem_f32() {
 }
 template <int D>
 size_t relay_smem_bf16() {
-    const size_t prefix = sizeof(__nv_bfloat16) * (size_t)(NQ + 4 * BP) * (D + PAD);
+    const size_t prefix = sizeof(__nv_bfloat16) * ((size_t)(NQ + 4 * BP) * (D + PAD) + 2 * 4 * 16 * PLD) +
+                          sizeof(float) * 2 * (2 * 4 * 2 * 16);
     const size_t own = OwnLayout<D>::BYTES;
     return prefix > own ? prefix : own;
 }
