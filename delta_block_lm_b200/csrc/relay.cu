@@ -8,7 +8,7 @@
 // One CTA (256 threads) per work item:
 //   prefix items (head h, prefix block pb): read the block's keys/values of head h ONCE and
 //       produce partials (max, sum, acc[D]) for the queries of EVERY sequence at head h, so the
-//       shared prefix is read once per head, never once per sequence.  bf16 streams 512 keys
+//       shared prefix is read once per head, never once per sequence.  bf16 streams 1024 keys
 //       through tensor-core tiles (mma.sync m16n8k16, online softmax over 32-key sub-tiles, two
 //       tile buffers); f32 uses SIMT tiles of 64 keys (two partials per item).
 //   own items (sequence n, head h, 1024-key own block ob): one query against the block's keys.
@@ -27,7 +27,7 @@ namespace {
 
 constexpr int BP = 64;        // prefix keys per tile
 constexpr int KSPLIT = 2;     // f32 path: partials per prefix CTA (key halves of 32)
-constexpr int TILES_BF16 = 8; // bf16 path: 64-key tiles streamed by one prefix item (512 keys)
+constexpr int TILES_BF16 = 16; // bf16 path: 64-key tiles streamed by one prefix item (1024 keys; 512 or 2048 measured slower)
 constexpr int NQ = 64;        // queries per prefix pass
 constexpr int BO = 1024;      // f32: own keys per own CTA
 constexpr int THREADS = 256;
@@ -833,7 +833,7 @@ struct Layout {
     size_t off_acc, off_max, off_sum, off_cnt, n_cnt, total;
 };
 
-// bf16: one partial per 512-key prefix CTA and per 1024-key own CTA; f32: two partials per 64-key
+// bf16: one partial per 1024-key prefix CTA and per 1024-key own CTA; f32: two partials per 64-key
 // prefix CTA and one per 1024-key own CTA; one arrival counter per (n, h) row.
 Layout layout(int64_t N, int64_t H, int64_t D, int64_t Lp, int64_t Lo, bool bf16) {
     Layout L{};
