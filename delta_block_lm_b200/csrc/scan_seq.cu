@@ -318,8 +318,10 @@ __global__ void __launch_bounds__(256) gate_uniform_kernel(const float* __restri
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
     bool diff = false;
-    for (const float* g : {alpha, erase, write}) {
-        const float4 x = reinterpret_cast<const float4*>(g + row * 128)[lane];
+    const int ng = write == erase ? 2 : 3;  // the same tensor as erase and write is read once
+    const float* gates[3] = {alpha, erase, write};
+    for (int i = 0; i < ng; ++i) {
+        const float4 x = reinterpret_cast<const float4*>(gates[i] + row * 128)[lane];
         const float x0 = __shfl_sync(0xffffffffu, x.x, 0);
         diff |= (x.x != x0) | (x.y != x0) | (x.z != x0) | (x.w != x0);
     }
