@@ -659,11 +659,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (!(big <= 3.0e38f)) atomicExch(p.err, kTcRangeError);  // inf or NaN: an fp16 operand overflowed
             if (TRAIN) {
                 // f32 rows straight to global memory: a warp writes 32 consecutive values per row
-                float* orow = p.out_f32 + (size_t)b * p.os[0] + (size_t)h * p.os[2] + j;
+                // (the row pointer and stride are formed once: per-element 64-bit index products cost
+                // about a fifth of the call; the tail chunk keeps static indices into o)
+                const int t0 = cc * C + 32 * hh;
+                const int64_t rs = p.os[1];
+                float* orow = p.out_f32 + (size_t)b * p.os[0] + (size_t)h * p.os[2] + j + (size_t)t0 * rs;
+                if (t0 + 32 <= p.T) {
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const int t = cc * C + 32 * hh + e;
-                    if (t < p.T) orow[(size_t)t * p.os[1]] = __uint_as_float(o[e]);
+                    for (int e = 0; e < 32; ++e) orow[e * rs] = __uint_as_float(o[e]);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e)
+                        if (e < p.T - t0) orow[e * rs] = __uint_as_float(o[e]);
                 }
                 return;
             }
