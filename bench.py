@@ -451,7 +451,7 @@ def bench_long(torch, dist, args, dev, rank, world):
             "limited_by": ("the hand-off (all_gather + fold)" if phases[1] > phases[0] + phases[2] else
                            "the per-chunk scan chain of the span maps and the rescan (pass 1 + pass 2: "
                            f"{100 * (phases[0] + phases[2]) / max(sum(phases), 1e-9):.0f}% of the step)"),
-            "handoff": "all_gather of (A_g [H,K,K], B_g [H,K,V]) f32 per rank",
+            "handoff": "one all_gather of (A_g | B_g) [H,K,K+V] f32 per rank",
             "handoff_bytes_gathered_per_rank": handoff_bytes,
             "one_call_ms": one_call_ms,
             "roofline": {"bound": "hbm", "algorithmic_bytes": alg,

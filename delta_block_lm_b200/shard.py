@@ -73,11 +73,12 @@ def exchange_span_states(first_or_transition: torch.Tensor, offset: Optional[tor
         Bv = first_or_transition
     else:
         A, Bv = first_or_transition, offset
-    As = [torch.empty_like(A) for _ in range(world)]
-    Bs = [torch.empty_like(Bv) for _ in range(world)]
-    dist.all_gather(As, A.contiguous(), group=group)
-    dist.all_gather(Bs, Bv.contiguous(), group=group)
-    return As, Bs
+    # one collective: each rank's (A_g | B_g) side by side, [.., K, K + V]
+    K = A.shape[-1]
+    packed = torch.cat([A, Bv], dim=-1).contiguous()
+    parts = [torch.empty_like(packed) for _ in range(world)]
+    dist.all_gather(parts, packed, group=group)
+    return [x[..., :K] for x in parts], [x[..., K:] for x in parts]
 
 
 def sm_count(device: Optional[torch.device] = None) -> int:
