@@ -270,6 +270,22 @@ def test_relay_merge_ragged_and_empty(cuda, native_lib):
     assert rel_err(got[0][1], ref[0][1]) < TOL_BF16
 
 
+@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 128), (torch.bfloat16, 64), (torch.float32, 64)])
+def test_relay_merge_many_sequences_and_blocks(cuda, native_lib, dtype, D):
+    # 150 sequences: three 64-query passes through every prefix block (its tile buffers and the
+    # pair-exchange buffers reused across passes); a 2500-key prefix: three prefix blocks, the last
+    # one short, ending in a 4-key tile; 1500 own keys: two own blocks, the second ending inside a
+    # ring stage; ragged own lengths on and around the block and stage boundaries
+    N_, H = 150, 2
+    own = np.random.default_rng(5).integers(0, 1501, N_).astype(np.int32)
+    own[:8] = [0, 1, 63, 64, 1023, 1024, 1025, 1500]
+    got, ref = _relay_case(cuda, dtype, N_, H, D, 2500, 1500, own_len=own, seed=11)
+    tol = TOL_BF16 if dtype == torch.bfloat16 else TOL_F32
+    assert rel_err(got[0], ref[0]) < tol
+    assert rel_err(got[1], ref[1]) < tol and rel_err(got[2], ref[2]) < tol
+    assert native_device_ok()
+
+
 def test_relay_merge_known_answers(cuda, native_lib):
     # relay_tests.rs:12-90 restated for the split layout (see tests/test_oracle.py).
     D = 64
