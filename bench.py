@@ -808,12 +808,14 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true", help="skip the decode / relay lines")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["prefill", "long", "decode", "relay", "backward", "prologue", "relay_attn"],
+    ap.add_argument("--workload", choices=["prefill", "long", "decode", "relay", "backward", "prologue", "relay_attn",
+                                           "config0", "dropin"],
                     default="prefill",
                     help="prefill: config 1 (the headline, weak-scaled); long: config 4 (time-sharded); "
                          "decode: config 2 alone; relay: config 3 alone; backward: the fused scan's "
                          "backward at the reference's training shape; prologue: the mixer prologue; "
-                         "relay_attn: reference-layout relay attention (1 GPU)")
+                         "relay_attn: reference-layout relay attention (1 GPU); config0: config 0 alone; "
+                         "dropin: the reference's gdn_training_scan call at the config-1 shape (1 GPU)")
     ap.add_argument("--long-tokens", type=int, default=131072)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -855,6 +857,13 @@ def main():
         if world > 1:
             raise SystemExit("--workload relay_attn runs on one GPU")
         print(json.dumps(bench_relay_attn(torch, args, dev, with_cpu=not args.no_cpu_baseline)), flush=True)
+        return 0
+    if args.workload in ("config0", "dropin"):
+        # the headline's `secondary.config0` and `secondary.training_scan_c1_dropin` measurements alone
+        if world > 1:
+            raise SystemExit("--workload config0/dropin runs on one GPU")
+        print(json.dumps(bench_config0(torch, dev) if args.workload == "config0" else bench_dropin_c1(torch, dev)),
+              flush=True)
         return 0
     if args.workload == "backward":
         if world > 1:
