@@ -378,9 +378,10 @@ def bench_long(torch, dist, args, dev, rank, world):
     """Config 4: one sequence B1/H16/T131072/d128 bf16, sharded along time over the ranks (strong
     scaling).  Phases, each max over ranks: pass 1 (the segment maps of this rank's span), the
     hand-off (the span map composed by the fold kernel, one all_gather of the span boundary objects
-    -- the only collective -- and the fold of the earlier ranks' maps), pass 2 (the fold of this
-    rank's segment starts and the rescan).  At one GPU the same work is also timed as the single
-    C-ABI call dbl_gdn2_prefill_segmented."""
+    -- the only collective -- and the fold of the earlier ranks' maps; on rank 0 the fold of its
+    segment starts and end state), pass 2 (the fold of this rank's segment starts where the hand-off
+    has not made them, and the rescan).  At one GPU there is no hand-off and the same work is also
+    timed as the single C-ABI call dbl_gdn2_prefill_segmented."""
     from delta_block_lm_b200 import kernels, shard
 
     t_total = args.long_tokens
@@ -395,18 +396,19 @@ def bench_long(torch, dist, args, dev, rank, world):
         rec(0)
         maps = shard.segment_maps(q, k, v, alpha, beta, segs)
         rec(1)
-        if rank == 0:
-            s0 = torch.zeros((1, H, K, V), device=dev, dtype=torch.float32)
-            _, e0, _ = kernels.gdn2_span_fold(maps[0], maps[1], s0[0])
-            if world > 1:
-                shard.exchange_span_states(e0.unsqueeze(0), None, rank, world)
-            start = s0
-        else:
+        starts = None
+        s0 = torch.zeros((1, H, K, V), device=dev, dtype=torch.float32)
+        start = s0
+        if rank == 0 and world > 1:
+            starts, e0 = shard.rank0_fold(maps, s0)
+            shard.exchange_span_states(e0.unsqueeze(0), None, rank, world)
+        elif rank > 0:
             At, Bt = shard.compose_maps(*maps)
             As, Bs = shard.exchange_span_states(At, Bt, rank, world)
             start = shard.fold_span_states(Bs[0], As, Bs, rank)
         rec(2)
-        out = shard.segmented_prefill(q, k, v, alpha, beta, segments=segs, maps=maps, start=start)
+        out = shard.segmented_prefill(q, k, v, alpha, beta, segments=segs, maps=maps, start=start,
+                                      starts=starts)
         rec(3)
         return out
 

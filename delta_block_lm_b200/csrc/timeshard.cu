@@ -25,13 +25,13 @@ int prefill_dispatch(const dbl_prefill_args* a, int mode, float* transition, cud
 
 namespace {
 
-constexpr int kFoldCols = 16;    // value columns per CTA
-constexpr int kFoldThreads = 256;  // thread t: state row t / 2, columns 8 (t % 2) .. + 8
+constexpr int kFoldThreads = 256;  // thread t: state rows t / 4 and t / 4 + 64, column group t % 4
+constexpr int kFoldLdA = 132;      // row stride (floats) of a staged transition: rows 4 banks apart
 constexpr int kChunk = 64;
 
-struct FoldParams {
-    int S, H, K, V;
-    const float* A;    // [S][H][K][K]
+// One fold: X_{s+1} = A_s X_s + B_s over `V` columns.
+struct FoldJob {
+    int V;
     const float* B;    // [S][H][K][V] or null (zero offsets)
     const float* X0;   // [H][K][V] or null (zeros); ignored when x0_identity
     int x0_identity;   // X_0 = I (V == K)
@@ -39,89 +39,199 @@ struct FoldParams {
     float* end;        // [H][K][V] or null: X_S
 };
 
-// X_{s+1} = A_s X_s + B_s for s = 0 .. S-1, one CTA per (16 value columns, head).  f32 FMAs: the
-// fold is short (S <= a few dozen steps of a K x K by K x 16 product) and its errors would reach
-// every later state, so it stays in full f32.
-__global__ void __launch_bounds__(kFoldThreads) span_fold_kernel(const FoldParams p) {
-    __shared__ __align__(16) float sX[128 * kFoldCols];
-    const int h = blockIdx.y, c0 = blockIdx.x * kFoldCols;
-    const int t = threadIdx.x, i = t >> 1, half = (t & 1) * 8;
-    const bool row = i < p.K;
-    const size_t xb = (size_t)h * p.K * p.V;
-    for (int e = t; e < p.K * kFoldCols; e += kFoldThreads) {
-        const int r = e / kFoldCols, c = e % kFoldCols;
+// Up to two folds over the same transitions in one launch (the composed transition and the
+// offset fold of a span are independent): column blocks [0, nx0) run job 0, the rest job 1.
+struct FoldParams {
+    int S, H, K;
+    const float* A;    // [S][H][K][K]
+    int nx0;
+    FoldJob job0, job1;
+};
+
+__device__ __forceinline__ void fold_cp16(void* dst, const void* src) {
+    const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(src) : "memory");
+}
+__device__ __forceinline__ void fold_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void fold_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+// c += a * (x.x, x.y) on an f32 pair: one fma.rn per lane, the same rounding as two fmaf.
+__device__ __forceinline__ void fold_fma2(float2& c, float a, float2 x) {
+    asm("{.reg .b64 ra, rx, rc;\n\t"
+        "mov.b64 ra, {%2, %2};\n\tmov.b64 rx, {%3, %4};\n\tmov.b64 rc, {%0, %1};\n\t"
+        "fma.rn.f32x2 rc, ra, rx, rc;\n\tmov.b64 {%0, %1}, rc;\n\t}"
+        : "+f"(c.x), "+f"(c.y)
+        : "f"(a), "f"(x.x), "f"(x.y));
+}
+
+// X_{s+1} = A_s X_s + B_s for s = 0 .. S-1, one CTA per (COLS columns, head).  f32 FMAs in
+// increasing k from the offset (the fold is short, S <= a few dozen steps of a K x K by K x COLS
+// product, and its errors would reach every later state, so it stays in full f32).  The step is a
+// dependency chain, so A_{s+1} and B_{s+1} are staged into shared memory by cp.async while step s
+// computes; X lives in shared memory, and each thread keeps 2 rows x COLS/4 columns in registers.
+template <int COLS>
+__global__ void __launch_bounds__(kFoldThreads, 1) span_fold_kernel(const FoldParams p) {
+    constexpr int CPT = COLS / 4;  // columns per thread (4 column groups)
+    extern __shared__ __align__(16) float fold_smem[];
+    float* sA = fold_smem;                    // [2][128][kFoldLdA]
+    float* sB = sA + 2 * 128 * kFoldLdA;      // [2][128][COLS]
+    float* sX = sB + 2 * 128 * COLS;          // [128][COLS]
+    const bool second = static_cast<int>(blockIdx.x) >= p.nx0;
+    const int bx = second ? blockIdx.x - p.nx0 : blockIdx.x;
+    const int V = second ? p.job1.V : p.job0.V;
+    const float* Bp = second ? p.job1.B : p.job0.B;
+    const float* X0 = second ? p.job1.X0 : p.job0.X0;
+    const int ident = second ? p.job1.x0_identity : p.job0.x0_identity;
+    float* starts = second ? p.job1.starts : p.job0.starts;
+    float* endp = second ? p.job1.end : p.job0.end;
+    const int h = blockIdx.y, c0 = bx * COLS, K = p.K, S = p.S;
+    const int t = threadIdx.x, rp = t >> 2, cc = (t & 3) * CPT;
+    const int rows[2] = {rp, rp + 64};
+    const bool act[2] = {rp < K, rp + 64 < K};
+    const size_t xb = (size_t)h * K * V;
+    const int q4 = K >> 2;
+
+    auto stage = [&](int s) {
+        const int buf = s & 1;
+        const float* As = p.A + ((size_t)s * p.H + h) * K * K;
+        float* dA = sA + buf * (128 * kFoldLdA);
+        for (int e = t; e < K * q4; e += kFoldThreads) {
+            const int r = e / q4, c = e - r * q4;
+            fold_cp16(dA + r * kFoldLdA + 4 * c, As + (size_t)r * K + 4 * c);
+        }
+        if (Bp) {
+            const float* Bs = Bp + ((size_t)s * p.H + h) * K * V + c0;
+            float* dB = sB + buf * (128 * COLS);
+            for (int e = t; e < K * (COLS / 4); e += kFoldThreads) {
+                const int r = e / (COLS / 4), c = e % (COLS / 4);
+                fold_cp16(dB + r * COLS + 4 * c, Bs + (size_t)r * V + 4 * c);
+            }
+        }
+        fold_commit();
+    };
+
+    if (S > 0) stage(0);
+    for (int e = t; e < K * COLS; e += kFoldThreads) {
+        const int r = e / COLS, c = e % COLS;
         float x = 0.f;
-        if (p.x0_identity) x = (r == c0 + c) ? 1.f : 0.f;
-        else if (p.X0) x = p.X0[xb + (size_t)r * p.V + c0 + c];
+        if (ident) x = (r == c0 + c) ? 1.f : 0.f;
+        else if (X0) x = X0[xb + (size_t)r * V + c0 + c];
         sX[e] = x;
     }
-    __syncthreads();
-    for (int s = 0; s < p.S; ++s) {
-        const size_t sb = ((size_t)s * p.H + h) * p.K * p.V;
-        float acc[8];
-        if (row) {
-            const float4* xr = reinterpret_cast<const float4*>(sX + i * kFoldCols + half);
-            if (p.starts) {
-                float4* dst = reinterpret_cast<float4*>(p.starts + sb + (size_t)i * p.V + c0 + half);
-                dst[0] = xr[0];
-                dst[1] = xr[1];
-            }
-            if (p.B) {
-                const float4* b4 = reinterpret_cast<const float4*>(p.B + sb + (size_t)i * p.V + c0 + half);
-                const float4 u = b4[0], w = b4[1];
-                acc[0] = u.x, acc[1] = u.y, acc[2] = u.z, acc[3] = u.w;
-                acc[4] = w.x, acc[5] = w.y, acc[6] = w.z, acc[7] = w.w;
-            } else {
+    for (int s = 0; s < S; ++s) {
+        if (s + 1 < S) {
+            stage(s + 1);  // buffer (s + 1) & 1 was last read in step s - 1, before its barriers
+            fold_wait<1>();
+        } else {
+            fold_wait<0>();
+        }
+        __syncthreads();  // A_s, B_s and X_s visible to every thread
+        const int buf = s & 1;
+        float2 acc[2][CPT / 2];
 #pragma unroll
-                for (int c = 0; c < 8; ++c) acc[c] = 0.f;
+        for (int i = 0; i < 2; ++i) {
+            const float* xr = sX + rows[i] * COLS + cc;
+            if (act[i] && starts) {
+                float* dst = starts + ((size_t)s * p.H + h) * K * V + (size_t)rows[i] * V + c0 + cc;
+#pragma unroll
+                for (int c4 = 0; c4 < CPT / 4; ++c4)
+                    reinterpret_cast<float4*>(dst)[c4] = reinterpret_cast<const float4*>(xr)[c4];
             }
-            const float4* ar = reinterpret_cast<const float4*>(p.A + (((size_t)s * p.H + h) * p.K + i) * p.K);
-            for (int k4 = 0; k4 < p.K / 4; ++k4) {
-                const float4 a = ar[k4];
-                const float av[4] = {a.x, a.y, a.z, a.w};
+            const float* br = sB + buf * (128 * COLS) + rows[i] * COLS + cc;
+#pragma unroll
+            for (int c2 = 0; c2 < CPT / 2; ++c2)
+                acc[i][c2] = (Bp && act[i]) ? reinterpret_cast<const float2*>(br)[c2] : make_float2(0.f, 0.f);
+        }
+        const float* a0 = sA + buf * (128 * kFoldLdA) + rp * kFoldLdA;
+        const float* a1 = a0 + 64 * kFoldLdA;
+        if (act[0]) {
+#pragma unroll 2
+            for (int k = 0; k < K; k += 4) {
+                const float4 u = *reinterpret_cast<const float4*>(a0 + k);
+                const float4 w = act[1] ? *reinterpret_cast<const float4*>(a1 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float ua[4] = {u.x, u.y, u.z, u.w}, wa[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
-                    const float4* xk = reinterpret_cast<const float4*>(sX + (4 * k4 + kk) * kFoldCols + half);
-                    const float4 x0 = xk[0], x1 = xk[1];
-                    acc[0] = fmaf(av[kk], x0.x, acc[0]);
-                    acc[1] = fmaf(av[kk], x0.y, acc[1]);
-                    acc[2] = fmaf(av[kk], x0.z, acc[2]);
-                    acc[3] = fmaf(av[kk], x0.w, acc[3]);
-                    acc[4] = fmaf(av[kk], x1.x, acc[4]);
-                    acc[5] = fmaf(av[kk], x1.y, acc[5]);
-                    acc[6] = fmaf(av[kk], x1.z, acc[6]);
-                    acc[7] = fmaf(av[kk], x1.w, acc[7]);
+                    const float4* xr = reinterpret_cast<const float4*>(sX + (k + kk) * COLS + cc);
+#pragma unroll
+                    for (int c4 = 0; c4 < CPT / 4; ++c4) {
+                        const float4 x = xr[c4];
+                        fold_fma2(acc[0][2 * c4], ua[kk], make_float2(x.x, x.y));
+                        fold_fma2(acc[0][2 * c4 + 1], ua[kk], make_float2(x.z, x.w));
+                        fold_fma2(acc[1][2 * c4], wa[kk], make_float2(x.x, x.y));
+                        fold_fma2(acc[1][2 * c4 + 1], wa[kk], make_float2(x.z, x.w));
+                    }
                 }
             }
         }
-        __syncthreads();
-        if (row) {
-            float4* xw = reinterpret_cast<float4*>(sX + i * kFoldCols + half);
-            xw[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-            xw[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        __syncthreads();  // every read of X_s and of this step's buffers is done
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            if (!act[i]) continue;
+            float2* xw = reinterpret_cast<float2*>(sX + rows[i] * COLS + cc);
+#pragma unroll
+            for (int c2 = 0; c2 < CPT / 2; ++c2) xw[c2] = acc[i][c2];
         }
-        __syncthreads();
     }
-    if (p.end && row) {
-        const float4* xr = reinterpret_cast<const float4*>(sX + i * kFoldCols + half);
-        float4* dst = reinterpret_cast<float4*>(p.end + xb + (size_t)i * p.V + c0 + half);
-        dst[0] = xr[0];
-        dst[1] = xr[1];
+    __syncthreads();
+    if (endp) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            if (!act[i]) continue;
+            const float4* xr = reinterpret_cast<const float4*>(sX + rows[i] * COLS + cc);
+            float4* dst = reinterpret_cast<float4*>(endp + xb + (size_t)rows[i] * V + c0 + cc);
+#pragma unroll
+            for (int c4 = 0; c4 < CPT / 4; ++c4) dst[c4] = xr[c4];
+        }
     }
 }
 
-int fold_launch(const FoldParams& p, cudaStream_t st) {
-    if (p.K <= 0 || p.K > 128 || p.K % 4 != 0 || p.V <= 0 || p.V % kFoldCols != 0 || p.H <= 0 || p.S < 0)
-        return fail(DBL_ERR_UNSUPPORTED, "span fold: key width must be a multiple of 4 up to 128 and value width a multiple of 16");
-    if (p.x0_identity && p.V != p.K) return fail(DBL_ERR_INVALID_ARGUMENT, "span fold: identity start needs V == K");
-    for (const void* ptr : {static_cast<const void*>(p.A), static_cast<const void*>(p.B), static_cast<const void*>(p.X0),
-                            static_cast<const void*>(p.starts), static_cast<const void*>(p.end)})
+template <int COLS>
+constexpr size_t fold_smem_bytes() {
+    return sizeof(float) * (2 * 128 * kFoldLdA + 2 * 128 * COLS + 128 * COLS);
+}
+
+int fold_check_job(const FoldJob& j, int K) {
+    if (j.V <= 0 || j.V % 16 != 0)
+        return fail(DBL_ERR_UNSUPPORTED, "span fold: value width must be a positive multiple of 16");
+    if (j.x0_identity && j.V != K) return fail(DBL_ERR_INVALID_ARGUMENT, "span fold: identity start needs V == K");
+    for (const void* ptr : {static_cast<const void*>(j.B), static_cast<const void*>(j.X0),
+                            static_cast<const void*>(j.starts), static_cast<const void*>(j.end)})
         if (ptr && !aligned(ptr, 16)) return fail(DBL_ERR_INVALID_ARGUMENT, "span fold: arrays must be 16-byte aligned");
-    if (p.S > 0 && !p.A) return fail(DBL_ERR_INVALID_ARGUMENT, "span fold: transitions are required");
-    if (p.H > 65535) return fail(DBL_ERR_UNSUPPORTED, "span fold: at most 65535 heads");
-    const dim3 grid((unsigned)(p.V / kFoldCols), (unsigned)p.H);
-    span_fold_kernel<<<grid, kFoldThreads, 0, st>>>(p);
+    return DBL_OK;
+}
+
+template <int COLS>
+int fold_launch_cols(const FoldParams& p, int nx, cudaStream_t st) {
+    constexpr size_t smem = fold_smem_bytes<COLS>();
+    cudaError_t e = cudaFuncSetAttribute(span_fold_kernel<COLS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_status(e, "span fold: cudaFuncSetAttribute");
+    span_fold_kernel<COLS><<<dim3((unsigned)nx, (unsigned)p.H), kFoldThreads, smem, st>>>(p);
     return launch_status("span_fold_kernel");
+}
+
+// One launch for job 0 and, when job1.V > 0, job 1.  Column blocks of 16 while the grid fits the
+// device in one wave, else of 32 (half the CTAs, twice the work each).
+int fold_launch(FoldParams p, cudaStream_t st) {
+    if (p.K <= 0 || p.K > 128 || p.K % 4 != 0 || p.H <= 0 || p.S < 0)
+        return fail(DBL_ERR_UNSUPPORTED, "span fold: key width must be a multiple of 4 up to 128");
+    if (p.S > 0 && (!p.A || !aligned(p.A, 16)))
+        return fail(DBL_ERR_INVALID_ARGUMENT, "span fold: 16-byte aligned transitions are required");
+    if (p.H > 65535) return fail(DBL_ERR_UNSUPPORTED, "span fold: at most 65535 heads");
+    int rc = fold_check_job(p.job0, p.K);
+    if (rc == DBL_OK && p.job1.V > 0) rc = fold_check_job(p.job1, p.K);
+    if (rc != DBL_OK) return rc;
+    const int w0 = p.job0.V, w1 = p.job1.V;
+    int sms = 148, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const bool wide = (w0 / 16 + w1 / 16) * p.H > sms && w0 % 32 == 0 && w1 % 32 == 0;
+    if (wide) {
+        p.nx0 = w0 / 32;
+        return fold_launch_cols<32>(p, p.nx0 + w1 / 32, st);
+    }
+    p.nx0 = w0 / 16;
+    return fold_launch_cols<16>(p, p.nx0 + w1 / 16, st);
 }
 
 // Segment maps and fold scratch of one span: A [S,H,K,K], B [S,H,K,V] (reused for the rescan's
@@ -210,12 +320,13 @@ int segment_maps(const dbl_prefill_args* a, int64_t S, unsigned char* ws, const 
 int segment_starts(const dbl_prefill_args* a, int64_t S, unsigned char* ws, const SegLayout& L, const float* start,
                    float* end, cudaStream_t st) {
     FoldParams f{};
-    f.S = (int)S, f.H = (int)a->heads, f.K = (int)a->key_dim, f.V = (int)a->value_dim;
+    f.S = (int)S, f.H = (int)a->heads, f.K = (int)a->key_dim;
     f.A = reinterpret_cast<const float*>(ws + L.off_a);
-    f.B = reinterpret_cast<const float*>(ws + L.off_b);
-    f.X0 = start;
-    f.starts = reinterpret_cast<float*>(ws + L.off_starts);
-    f.end = end;
+    f.job0.V = (int)a->value_dim;
+    f.job0.B = reinterpret_cast<const float*>(ws + L.off_b);
+    f.job0.X0 = start;
+    f.job0.starts = reinterpret_cast<float*>(ws + L.off_starts);
+    f.job0.end = end;
     return fold_launch(f, st);
 }
 
@@ -265,24 +376,29 @@ extern "C" int dbl_gdn2_span_fold(const float* transition, const float* offset, 
     FoldParams f{};
     f.S = (int)segments, f.H = (int)heads, f.K = (int)key_dim;
     f.A = transition;
-    int rc = DBL_OK;
+    // the composed transition (identity start, no offsets) and the offset fold share one launch
+    FoldJob comp{}, fold{};
     if (composed_transition) {
-        f.V = (int)key_dim;
-        f.x0_identity = 1;
-        f.end = composed_transition;
-        rc = fold_launch(f, st);
-        if (rc != DBL_OK) return rc;
+        comp.V = (int)key_dim;
+        comp.x0_identity = 1;
+        comp.end = composed_transition;
     }
     if (starts || end) {
-        f.V = (int)value_dim;
-        f.x0_identity = 0;
-        f.B = offset;
-        f.X0 = start;
-        f.starts = starts;
-        f.end = end;
-        rc = fold_launch(f, st);
+        fold.V = (int)value_dim;
+        fold.B = offset;
+        fold.X0 = start;
+        fold.starts = starts;
+        fold.end = end;
     }
-    return rc;
+    if (comp.V > 0) {
+        f.job0 = comp;
+        f.job1 = fold;
+    } else if (fold.V > 0) {
+        f.job0 = fold;
+    } else {
+        return DBL_OK;
+    }
+    return fold_launch(f, st);
 }
 
 extern "C" size_t dbl_gdn2_prefill_segmented_workspace_bytes(const dbl_prefill_args* a, int64_t segments) {

@@ -143,13 +143,14 @@ def segment_starts(A: torch.Tensor, Bm: torch.Tensor, start: torch.Tensor) -> to
 
 def segmented_prefill(q, k, v, alpha, beta, *, segments: Optional[int] = None, scale=None,
                       initial_state: Optional[torch.Tensor] = None, chunk_size: int = CHUNK,
-                      maps=None, start: Optional[torch.Tensor] = None):
+                      maps=None, start: Optional[torch.Tensor] = None, starts: Optional[torch.Tensor] = None):
     """Prefill of one long sequence [1, T, H, D] on one GPU through time segmentation.
 
     Returns (out [1, T, H, V], final_state [1, H, K, V]).  Without ``maps`` this is one C-ABI call
     (kernels.gdn2_prefill_segmented: pass 1, fold and rescan in the library); ``maps`` reuses
     pass-1 results computed by the caller and ``start`` overrides the span's start state (the
-    multi-GPU driver, which has already computed the maps to hand them off).
+    multi-GPU driver, which has already computed the maps to hand them off); ``starts``
+    [S, H, K, V] are the segment start states when the caller has already folded them.
     """
     if q.shape[0] != 1:
         raise ValueError("segmented_prefill handles one sequence (batch 1)")
@@ -167,7 +168,8 @@ def segmented_prefill(q, k, v, alpha, beta, *, segments: Optional[int] = None, s
     if start is None:
         start = initial_state if initial_state is not None else torch.zeros(
             (1, H, K, V), device=q.device, dtype=torch.float32)
-    starts = segment_starts(A, Bm, start.to(torch.float32))
+    if starts is None:
+        starts = segment_starts(A, Bm, start.to(torch.float32))
     out = torch.empty((1, T, H, V), device=q.device, dtype=q.dtype)
     _, fin = kernels.gdn2_prefill(_segments(q, S), _segments(k, S), _segments(v, S),
                                   _segments(alpha, S), _segments(beta, S), scale=scale,
@@ -208,10 +210,12 @@ def time_sharded_prefill(q, k, v, alpha, beta, *, group=None, scale: Optional[fl
                                     chunk_size=chunk_size)
     maps = segment_maps(q, k, v, alpha, beta, S, scale=scale, chunk_size=chunk_size)
     K, V = q.shape[3], v.shape[3]
+    starts = None
     if rank == 0:
         s0 = initial_state.to(torch.float32) if initial_state is not None else torch.zeros(
             (1, H, K, V), device=q.device, dtype=torch.float32)
-        _, end, _ = kernels.gdn2_span_fold(maps[0], maps[1], s0[0])
+        # the segment starts and the span's end state in one fold
+        starts, end = rank0_fold(maps, s0)
         exchange_span_states(end.unsqueeze(0), None, rank, world, group)
         start = s0
     else:
@@ -219,4 +223,15 @@ def time_sharded_prefill(q, k, v, alpha, beta, *, group=None, scale: Optional[fl
         As, Bs = exchange_span_states(At, Bt, rank, world, group)
         start = fold_span_states(Bs[0], As, Bs, rank)
     return segmented_prefill(q, k, v, alpha, beta, segments=S, scale=scale, chunk_size=chunk_size,
-                             maps=maps, start=start)
+                             maps=maps, start=start, starts=starts)
+
+
+def rank0_fold(maps, s0: torch.Tensor):
+    """Segment starts [S,H,K,V] and end state [H,K,V] of the first rank's span from its start
+    state s0 [1,H,K,V] (one fold kernel on CUDA tensors)."""
+    A, Bm = maps
+    if A.is_cuda:
+        starts, end, _ = kernels.gdn2_span_fold(A, Bm, s0[0], want_starts=True, want_end=True)
+        return starts, end
+    starts = segment_starts(A, Bm, s0)
+    return starts, torch.matmul(A[-1], starts[-1]) + Bm[-1]

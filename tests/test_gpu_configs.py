@@ -168,9 +168,14 @@ def test_config4_full_time_sharded_devices(cuda, native_lib):
     assert r["out"]["rel_err"] < TOL_BF16 and r["final_state"]["rel_err"] < TOL_BF16
 
 
-def test_span_fold_matches_f64(cuda, native_lib):
+@pytest.mark.parametrize("H", [3, 12])
+def test_span_fold_matches_f64(cuda, native_lib, H):
+    # H = 3: 16-column blocks.  H = 12, K = V = 128: the composed transition and the offset fold
+    # need (8 + 8) x 12 = 192 blocks of 16 columns, more than one wave of 148 SMs, so the launch
+    # takes 32-column blocks
     rng = np.random.default_rng(3)
-    S, H, K, V = 5, 3, 128, 64
+    S, K = 5, 128
+    V = 64 if H == 3 else 128
     A = (rng.standard_normal((S, H, K, K)) / np.sqrt(K) * 0.9).astype(np.float32)
     Bm = rng.standard_normal((S, H, K, V)).astype(np.float32)
     x0 = rng.standard_normal((H, K, V)).astype(np.float32)
@@ -184,7 +189,7 @@ def test_span_fold_matches_f64(cuda, native_lib):
         ref_starts.append(x)
         x = np.einsum("hik,hkv->hiv", A[s].astype(np.float64), x) + Bm[s]
         c = np.einsum("hik,hkj->hij", A[s].astype(np.float64), c)
-    r = report("span fold S5/H3/K128/V64 f32", starts=(host(starts), np.stack(ref_starts)), end=(host(end), x),
+    r = report(f"span fold S5/H{H}/K128/V{V} f32", starts=(host(starts), np.stack(ref_starts)), end=(host(end), x),
                composed=(host(comp), c))
     for name in ("starts", "end", "composed"):
         assert r[name]["rel_err"] < 1e-5, name
