@@ -15,6 +15,7 @@
 // cudaMemcpyPeerAsync each (ordered after the producing device's event), folds them into its start
 // state and runs its own fold and pass 2.  Peer memory is only read by copies, never by a kernel.
 // The reference has no time-parallel or multi-device code; this file is the B200 build's own.
+#include <mutex>
 #include <vector>
 
 #include "common.cuh"
@@ -346,6 +347,165 @@ int segment_rescan(const dbl_prefill_args* a, int64_t S, unsigned char* ws, cons
                        "segmented prefill: final state");
 }
 
+// Tokens [t0, t0 + batch x time) of `a`'s one sequence as `batch` consecutive segments of `time`
+// tokens: the same memory through offset pointers and strides.  initial_state and final_state
+// are cleared (the caller sets them); out keeps its offset when present.
+dbl_prefill_args span_view(const dbl_prefill_args* a, int64_t t0, int64_t batch, int64_t time) {
+    dbl_prefill_args v = *a;
+    const int64_t dk[4] = {a->batch, a->time, a->heads, a->key_dim};
+    const int64_t dv[4] = {a->batch, a->time, a->heads, a->value_dim};
+    const int64_t dg[3] = {a->batch, a->time, a->heads};
+    const size_t es = dtype_size(a->dtype);
+    int64_t st[4];
+    resolve_strides(a->q_stride, dk, 4, st);
+    v.q = static_cast<const unsigned char*>(a->q) + (size_t)(t0 * st[1]) * es;
+    v.q_stride[0] = time * st[1], v.q_stride[1] = st[1], v.q_stride[2] = st[2], v.q_stride[3] = st[3];
+    resolve_strides(a->k_stride, dk, 4, st);
+    v.k = static_cast<const unsigned char*>(a->k) + (size_t)(t0 * st[1]) * es;
+    v.k_stride[0] = time * st[1], v.k_stride[1] = st[1], v.k_stride[2] = st[2], v.k_stride[3] = st[3];
+    resolve_strides(a->v_stride, dv, 4, st);
+    v.v = static_cast<const unsigned char*>(a->v) + (size_t)(t0 * st[1]) * es;
+    v.v_stride[0] = time * st[1], v.v_stride[1] = st[1], v.v_stride[2] = st[2], v.v_stride[3] = st[3];
+    resolve_strides(a->out_stride, dv, 4, st);
+    v.out = a->out ? static_cast<unsigned char*>(a->out) + (size_t)(t0 * st[1]) * es : nullptr;
+    v.out_stride[0] = time * st[1], v.out_stride[1] = st[1], v.out_stride[2] = st[2], v.out_stride[3] = st[3];
+    resolve_strides(a->alpha_stride, dg, 3, st);
+    v.alpha = a->alpha + t0 * st[1];
+    v.alpha_stride[0] = time * st[1], v.alpha_stride[1] = st[1], v.alpha_stride[2] = st[2];
+    resolve_strides(a->beta_stride, dg, 3, st);
+    v.beta = a->beta + t0 * st[1];
+    v.beta_stride[0] = time * st[1], v.beta_stride[1] = st[1], v.beta_stride[2] = st[2];
+    // valid / reset are [1, T] contiguous, so [batch, time] contiguous from token t0
+    v.valid = a->valid ? a->valid + t0 : nullptr;
+    v.reset = a->reset ? a->reset + t0 : nullptr;
+    v.batch = batch;
+    v.time = time;
+    v.initial_state = nullptr;
+    v.final_state = nullptr;
+    return v;
+}
+
+// The one-device schedule with a lead segment.  The sequence is cut into a lead segment of t0
+// tokens and m segments of lt tokens.  The lead segment needs no span maps: it is scanned from
+// the initial state, with its outputs, on a side stream while the maps of segments 1 .. m-1 (two
+// launches of (m - 1) x H CTAs) run on the caller's stream; segment m needs no maps either.  The
+// fold then gives the starts of segments 1 .. m and one launch of m x H CTAs rescans them.  With
+// t0 about 1.8 lt the lead scan ends with the two map launches, so the step takes about three
+// scans of lt tokens, against three scans of T / S tokens for S equal segments (m x H <= SMs:
+// m = 9 at H = 16 on 148 SMs, lt = T / 10.8 against T / 8).
+struct LeadPlan {
+    int64_t m = 0, lt = 0, t0 = 0;
+};
+
+bool plan_lead(int64_t T, int64_t H, int sms, LeadPlan* out) {
+    if (T % kChunk != 0 || H <= 0) return false;
+    const int64_t n = T / kChunk;
+    for (int64_t m = sms / H; m >= 2; --m) {
+        // lt = ceil(n / (m + 1.8)) chunks: the lead scan writes outputs (about 4.5 us per chunk
+        // against 4.06 for a map launch on B200), so 1.8 lt of it end with the two map launches
+        const int64_t L = (5 * n + 5 * m + 8) / (5 * m + 9);
+        const int64_t l0 = n - m * L;  // <= 1.8 L + 1 by the choice of L
+        if (L >= 1 && l0 >= 1) {
+            out->m = m;
+            out->lt = L * kChunk;
+            out->t0 = l0 * kChunk;
+            return true;
+        }
+    }
+    return false;
+}
+
+// One side stream and its fork / join events per device, created on first use and kept for the
+// life of the process.  The fork, the side launches and the join are issued under g_side_mu, so
+// concurrent callers on one device cannot interleave their event records.
+struct SideStream {
+    cudaStream_t s = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
+std::mutex g_side_mu;
+SideStream g_side[64];
+
+int side_stream(SideStream** out) {
+    int dev = 0;
+    int rc = cuda_status(cudaGetDevice(&dev), "side stream: cudaGetDevice");
+    if (rc != DBL_OK) return rc;
+    if (dev < 0 || dev >= 64) return fail(DBL_ERR_UNSUPPORTED, "side stream: device index %d out of range", dev);
+    SideStream& ss = g_side[dev];
+    if (!ss.s) {
+        rc = cuda_status(cudaStreamCreateWithFlags(&ss.s, cudaStreamNonBlocking), "side stream: create");
+        if (rc == DBL_OK) rc = cuda_status(cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming), "side stream: event");
+        if (rc == DBL_OK) rc = cuda_status(cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming), "side stream: event");
+        if (rc != DBL_OK) return rc;
+    }
+    *out = &ss;
+    return DBL_OK;
+}
+
+int lead_prefill(const dbl_prefill_args* a, const LeadPlan& P, unsigned char* ws, const SegLayout& L, cudaStream_t st) {
+    const size_t state = (size_t)a->heads * a->key_dim * a->value_dim;
+    float* A = reinterpret_cast<float*>(ws + L.off_a);
+    float* Bm = reinterpret_cast<float*>(ws + L.off_b);
+    float* starts = reinterpret_cast<float*>(ws + L.off_starts);
+    int rc = DBL_OK;
+    {
+        std::lock_guard<std::mutex> lock(g_side_mu);
+        SideStream* ss = nullptr;
+        rc = side_stream(&ss);
+        if (rc != DBL_OK) return rc;
+        rc = cuda_status(cudaEventRecord(ss->fork, st), "lead prefill: fork");
+        if (rc == DBL_OK) rc = cuda_status(cudaStreamWaitEvent(ss->s, ss->fork, 0), "lead prefill: fork");
+        if (rc != DBL_OK) return rc;
+        // the lead segment: initial state -> outputs of tokens [0, t0) and the start of segment 1
+        dbl_prefill_args v0 = span_view(a, 0, 1, P.t0);
+        v0.initial_state = a->initial_state;
+        v0.final_state = starts;
+        const int rc_side = prefill_dispatch(&v0, 0, nullptr, ss->s);
+        // the maps of segments 1 .. m-1
+        dbl_prefill_args vm = span_view(a, P.t0, P.m - 1, P.lt);
+        vm.out = nullptr;
+        rc = prefill_dispatch(&vm, 1, A, st);
+        if (rc == DBL_OK) {
+            vm.final_state = Bm;
+            rc = prefill_dispatch(&vm, 0, nullptr, st);
+        }
+        // join even after a failed launch, so that nothing queued on the side stream outlives the call
+        const int rc_join = cuda_status(cudaEventRecord(ss->join, ss->s), "lead prefill: join");
+        const int rc_wait = rc_join == DBL_OK ? cuda_status(cudaStreamWaitEvent(st, ss->join, 0), "lead prefill: join") : rc_join;
+        if (rc == DBL_OK) rc = rc_side;
+        if (rc == DBL_OK) rc = rc_wait;
+        if (rc != DBL_OK) return rc;
+    }
+    // X_0 = the start of segment 1; X_{s+1} = A_s X_s + B_s over the maps of segments 1 .. m-1
+    FoldParams f{};
+    f.S = (int)(P.m - 1), f.H = (int)a->heads, f.K = (int)a->key_dim;
+    f.A = A;
+    f.job0.V = (int)a->value_dim;
+    f.job0.B = Bm;
+    f.job0.X0 = starts;
+    f.job0.starts = starts;
+    f.job0.end = starts + (size_t)(P.m - 1) * state;
+    rc = fold_launch(f, st);
+    if (rc != DBL_OK) return rc;
+    // segments 1 .. m from their starts
+    dbl_prefill_args vr = span_view(a, P.t0, P.m, P.lt);
+    vr.initial_state = starts;
+    vr.final_state = a->final_state ? Bm : nullptr;  // the offsets are consumed by the fold
+    rc = prefill_dispatch(&vr, 0, nullptr, st);
+    if (rc != DBL_OK || !a->final_state) return rc;
+    return cuda_status(cudaMemcpyAsync(a->final_state, Bm + (size_t)(P.m - 1) * state, state * sizeof(float),
+                                       cudaMemcpyDeviceToDevice, st),
+                       "segmented prefill: final state");
+}
+
+// segments = 0: the lead schedule when it applies (plan_lead), else 0 is resolved by
+// pick_segments as for explicit equal segments.
+int lead_plan_for(const dbl_prefill_args* a, int64_t segments, LeadPlan* P) {
+    if (segments != 0) return 0;
+    int sms = 0;
+    if (sm_count_current(&sms) != DBL_OK) return 0;
+    return plan_lead(a->time, a->heads, sms, P) ? 1 : 0;
+}
+
 int resolve_segments(const dbl_prefill_args* a, int64_t segments, int64_t* out) {
     int64_t S = segments;
     if (S == 0) {
@@ -404,6 +564,8 @@ extern "C" int dbl_gdn2_span_fold(const float* transition, const float* offset, 
 extern "C" size_t dbl_gdn2_prefill_segmented_workspace_bytes(const dbl_prefill_args* a, int64_t segments) {
     using namespace dbl;
     if (check_span(a, "segmented prefill") != DBL_OK) return 0;
+    LeadPlan P;
+    if (lead_plan_for(a, segments, &P)) return seg_layout(P.m, a->heads, a->key_dim, a->value_dim).total;
     int64_t S = 0;
     if (resolve_segments(a, segments, &S) != DBL_OK) return 0;
     return seg_layout(S, a->heads, a->key_dim, a->value_dim).total;
@@ -414,10 +576,19 @@ extern "C" int dbl_gdn2_prefill_segmented(const dbl_prefill_args* a, int64_t seg
     using namespace dbl;
     int rc = check_span(a, "segmented prefill");
     if (rc != DBL_OK) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    LeadPlan P;
+    if (lead_plan_for(a, segments, &P)) {
+        const SegLayout L = seg_layout(P.m, a->heads, a->key_dim, a->value_dim);
+        if (!workspace || workspace_bytes < L.total)
+            return fail(DBL_ERR_WORKSPACE, "segmented prefill: workspace of %zu bytes required (got %zu)", L.total,
+                        workspace_bytes);
+        if (!aligned(workspace, 256)) return fail(DBL_ERR_INVALID_ARGUMENT, "segmented prefill: workspace must be 256-byte aligned");
+        return lead_prefill(a, P, static_cast<unsigned char*>(workspace), L, st);
+    }
     int64_t S = 0;
     rc = resolve_segments(a, segments, &S);
     if (rc != DBL_OK) return rc;
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (S == 1) return dbl_gdn2_prefill(a, stream);
     const SegLayout L = seg_layout(S, a->heads, a->key_dim, a->value_dim);
     if (!workspace || workspace_bytes < L.total)

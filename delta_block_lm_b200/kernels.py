@@ -481,8 +481,10 @@ def gdn2_prefill_segmented(q, k, v, alpha, beta, *, segments: int = 0, scale: Op
                            valid=None, reset=None, initial_state=None, out=None, final_state=None):
     """``gdn2_prefill`` of ONE long sequence (batch 1) on one device by time segments (pass 1 the
     segment maps, a fold of their start states, pass 2 the rescan), in one C-ABI call
-    (dbl_gdn2_prefill_segmented).  segments = 0 picks the largest power of two with segments x H
-    <= the device's SM count.  Returns (out [1,T,H,V], final_state [1,H,K,V])."""
+    (dbl_gdn2_prefill_segmented).  segments = 0 lets the library pick the schedule: a lead segment
+    scanned from the initial state beside the maps of floor(SMs / H) - 1 equal segments, then one
+    rescan of floor(SMs / H) segments (T a multiple of 64), else the largest power of two with
+    segments x H <= the SM count.  Returns (out [1,T,H,V], final_state [1,H,K,V])."""
     dev = _require_cuda(q, k, v, alpha, beta, valid, reset, initial_state, out, final_state)
     _check_prefill_inputs(q, k, v, alpha, beta, valid, reset)
     B, T, H, K = q.shape

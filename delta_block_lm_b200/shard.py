@@ -10,7 +10,8 @@
       fold    the start state of every segment by composing the maps before it (one small
               kernel, dbl_gdn2_span_fold);
       pass 2  every segment rescanned from its exact start state in one batched launch.
-  On one device the three steps are one C-ABI call (dbl_gdn2_prefill_segmented).
+  On one device the whole span is one C-ABI call (dbl_gdn2_prefill_segmented), whose default
+  schedule scans a lead segment from the initial state beside the maps of the other segments.
   Across GPUs, rank g holds the contiguous span g; the ranks exchange their composed span maps
   with one ``all_gather`` (the only collective) and each rank folds the maps of the ranks before it
   into its own start state before the local fold.
@@ -155,6 +156,10 @@ def segmented_prefill(q, k, v, alpha, beta, *, segments: Optional[int] = None, s
     if q.shape[0] != 1:
         raise ValueError("segmented_prefill handles one sequence (batch 1)")
     T, H = q.shape[1], q.shape[2]
+    if maps is None and segments is None and chunk_size == CHUNK:
+        # the library's own schedule (a lead segment beside the maps of the others)
+        return kernels.gdn2_prefill_segmented(q, k, v, alpha, beta, segments=0, scale=scale,
+                                              initial_state=start if start is not None else initial_state)
     S = segments or pick_segments(T, H, sm_count(q.device))
     if S == 1 or T % S:
         return kernels.gdn2_prefill(q, k, v, alpha, beta, scale=scale,

@@ -115,15 +115,19 @@ int dbl_gdn2_span_fold(const float *transition, const float *offset, int64_t seg
                        int64_t key_dim, int64_t value_dim, const float *start, float *starts, float *end,
                        float *composed_transition, dbl_stream_t stream);
 
-/* Prefill of ONE long sequence (batch 1, config 4) on one device by time segments: the span is cut
- * into `segments` equal segments (0 = the largest power of two with segments x heads <= the
- * device's SM count and whole 64-token chunks per segment) that run side by side -- pass 1 the
- * segment maps, a fold of their start states from initial_state, pass 2 every segment rescanned
- * from its start.  Same arguments and results as dbl_gdn2_prefill (out, final_state); the result
- * agrees with the one-pass scan to the rounding of the maps.  workspace: device memory of
- * dbl_gdn2_prefill_segmented_workspace_bytes() bytes, 256-byte aligned.  Replaces, for one long
- * sequence, the chunk-boundary carry of chunk::scan (crates/mixers/src/chunk.rs:147-244), whose
- * chunk loop runs the whole sequence in order. */
+/* Prefill of ONE long sequence (batch 1, config 4) on one device by time segments that run side
+ * by side.  segments > 0: `segments` equal segments -- pass 1 the segment maps, a fold of their
+ * start states from initial_state, pass 2 every segment rescanned from its start.  segments = 0:
+ * when T is a multiple of 64 and m = floor(SMs / heads) >= 2, a lead segment and m equal segments
+ * of ceil(T / 64 / (m + 1.8)) chunks: the lead segment is scanned from initial_state on a side stream
+ * (one per device, created on first use) while the maps of segments 1 .. m-1 run on `stream`, then
+ * a fold and one rescan of segments 1 .. m; otherwise the largest power of two with segments x
+ * heads <= the SM count and whole 64-token chunks per segment.  Same arguments and results as
+ * dbl_gdn2_prefill (out, final_state); the result agrees with the one-pass scan to the rounding of
+ * the maps.  workspace: device memory of dbl_gdn2_prefill_segmented_workspace_bytes() bytes (same
+ * `segments`), 256-byte aligned.  Replaces, for one long sequence, the chunk-boundary carry of
+ * chunk::scan (crates/mixers/src/chunk.rs:147-244), whose chunk loop runs the whole sequence in
+ * order. */
 size_t dbl_gdn2_prefill_segmented_workspace_bytes(const dbl_prefill_args *args, int64_t segments);
 int dbl_gdn2_prefill_segmented(const dbl_prefill_args *args, int64_t segments, void *workspace,
                                size_t workspace_bytes, dbl_stream_t stream);

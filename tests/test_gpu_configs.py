@@ -195,21 +195,25 @@ def test_span_fold_matches_f64(cuda, native_lib, H):
         assert r[name]["rel_err"] < 1e-5, name
 
 
-def test_segmented_prefill_with_masks_and_initial(cuda, native_lib):
+# segments = 8: equal segments.  segments = 0: the lead schedule -- at H = 4 a lead segment of 4
+# chunks and 31 segments of 4 (30 map segments, a 30-step fold); at H = 16, T = 4096 a lead
+# segment of 10 chunks and 9 segments of 6
+@pytest.mark.parametrize("h,t,segments", [(4, 8192, 8), (4, 8192, 0), (16, 4096, 0)])
+def test_segmented_prefill_with_masks_and_initial(cuda, native_lib, h, t, segments):
     import bench
-    q, k, v, alpha, beta = bench.make_prefill_inputs(torch, cuda, 41, b=1, t=8192, h=4)
+    q, k, v, alpha, beta = bench.make_prefill_inputs(torch, cuda, 41, b=1, t=t, h=h)
     g = torch.Generator(device=cuda)
     g.manual_seed(2)
-    valid = (torch.rand((1, 8192), device=cuda, generator=g) > 0.05).float()
-    reset = (torch.rand((1, 8192), device=cuda, generator=g) > 0.998).float()
-    init = 0.02 * torch.randn((1, 4, 128, 128), device=cuda, generator=g)
-    out, fin = dbl.gdn2_prefill_segmented(q, k, v, alpha, beta, segments=8, valid=valid, reset=reset,
+    valid = (torch.rand((1, t), device=cuda, generator=g) > 0.05).float()
+    reset = (torch.rand((1, t), device=cuda, generator=g) > 0.998).float()
+    init = 0.02 * torch.randn((1, h, 128, 128), device=cuda, generator=g)
+    out, fin = dbl.gdn2_prefill_segmented(q, k, v, alpha, beta, segments=segments, valid=valid, reset=reset,
                                           initial_state=init)
     torch.cuda.synchronize()
     _no_device_error(native_lib)
     ro, rf, _ = O.scan_scalar(host(q), host(k), host(v), host(alpha), host(beta), host(valid) > 0,
                               host(reset) > 0, host(init))
-    r = report("segmented prefill B1/H4/T8192 d128 bf16, 8 segments, masks + initial state",
+    r = report(f"segmented prefill B1/H{h}/T{t} d128 bf16, segments={segments}, masks + initial state",
                out=(host(out), ro), final_state=(host(fin), rf))
     assert r["out"]["rel_err"] < TOL_BF16 and r["final_state"]["rel_err"] < TOL_BF16
     assert np.all(host(out)[0][host(valid)[0] == 0] == 0.0)
