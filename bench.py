@@ -433,6 +433,31 @@ def bench_long(torch, dist, args, dev, rank, world):
     ms_step = ms / args.steps
     schedule = f"{segs} equal segments per GPU: pass 1 maps, hand-off, pass 2 rescan"
     uniform = None
+    eager = None
+    if world > 1:
+        # the same step (shard.time_sharded_prefill) captured as one CUDA graph per rank
+        # (shard.TimeShardedPrefillGraph): the eager step above is many short launches from Python,
+        # and a rank whose host falls behind holds every rank at the all_gather
+        eager = {"ms_per_step": ms_step, "phases_ms": {"pass1_segment_maps": phases[0],
+                                                       "handoff_compose_allgather_fold": phases[1],
+                                                       "pass2_fold_and_rescan": phases[2]}}
+        plan = shard.TimeShardedPrefillGraph(q, k, v, alpha, beta, segments=segs, warmup=args.warmup)
+        for _ in range(args.warmup):
+            plan.replay()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(args.steps):
+            plan.replay()
+        g1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms_step = _max_over_ranks(torch, dist, world, dev, g0.elapsed_time(g1) / args.steps)
+        plan.release()
+        del plan
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        schedule += "; the step replayed as one CUDA graph per rank (shard.TimeShardedPrefillGraph)"
     if world == 1:
         # one GPU: the value is the single C-ABI call with the library's schedule (segments = 0: a
         # lead segment scanned from the initial state beside the maps of the other segments, which
@@ -462,14 +487,9 @@ def bench_long(torch, dist, args, dev, rank, world):
     return {"workload": f"c4 B1/H{H}/T{t_total}/d{D} bf16 chunk {CHUNK}, time-sharded over {world} GPU(s)",
             "value": t_total / (ms_step / 1e3) / 1e6, "unit": "Mtok/s", "ms_per_step": ms_step,
             "scaling": "strong", "span_tokens": hi - lo, "schedule": schedule,
-            "phases_ms": (None if world == 1 else
-                          {"pass1_segment_maps": phases[0], "handoff_compose_allgather_fold": phases[1],
-                           "pass2_fold_and_rescan": phases[2]}),
-            "limited_by": ("the per-chunk scan chain: three scans of a segment in sequence (maps A, maps B, "
-                           "rescan)" if world == 1 else
-                           "the hand-off (all_gather + fold)" if phases[1] > phases[0] + phases[2] else
-                           "the per-chunk scan chain of the span maps and the rescan (pass 1 + pass 2: "
-                           f"{100 * (phases[0] + phases[2]) / max(sum(phases), 1e-9):.0f}% of the step)"),
+            "eager_steps": eager,
+            "limited_by": "the per-chunk scan chain: three scans of a segment in sequence (maps A, maps B, "
+                          "rescan)" + ("" if world == 1 else ", plus the hand-off"),
             "handoff": "one all_gather of (A_g | B_g) [H,K,K+V] f32 per rank" if world > 1 else None,
             "handoff_bytes_gathered_per_rank": handoff_bytes,
             "equal_segments_one_gpu": uniform,

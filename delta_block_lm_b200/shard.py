@@ -240,3 +240,49 @@ def rank0_fold(maps, s0: torch.Tensor):
         return starts, end
     starts = segment_starts(A, Bm, s0)
     return starts, torch.matmul(A[-1], starts[-1]) + Bm[-1]
+
+
+class TimeShardedPrefillGraph:
+    """``time_sharded_prefill`` of fixed inputs captured as one CUDA graph per rank.
+
+    The step is many short launches (two map launches, the fold kernels, the packing copy, the
+    ``all_gather``, the rescan) issued from Python, so a rank whose host falls behind holds every
+    other rank at the collective.  Capturing the whole step (NCCL supports graph capture) replays
+    it with no host work between launches.  The inputs are the tensors given here: write new
+    values into them (``copy_``) and call ``replay()``; ``out`` and ``final_state`` are rewritten
+    in place by every replay.  Every rank must construct, replay and ``release()`` the graph in
+    the same order (the capture runs the collective twice during warm-up and once in the
+    capture).  Call ``release()`` before ``destroy_process_group``.
+    """
+
+    def __init__(self, q, k, v, alpha, beta, *, group=None, scale: Optional[float] = None,
+                 initial_state: Optional[torch.Tensor] = None, chunk_size: int = CHUNK,
+                 segments: Optional[int] = None, warmup: int = 2):
+        if not q.is_cuda:
+            raise ValueError("TimeShardedPrefillGraph needs CUDA tensors")
+        self._args = (q, k, v, alpha, beta)
+        self._kw = dict(group=group, scale=scale, initial_state=initial_state, chunk_size=chunk_size,
+                        segments=segments)
+        dev = q.device
+        cur = torch.cuda.current_stream(dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            for _ in range(max(1, warmup)):
+                time_sharded_prefill(*self._args, **self._kw)
+        cur.wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out, self.final_state = time_sharded_prefill(*self._args, **self._kw)
+
+    def replay(self) -> Tuple[torch.Tensor, torch.Tensor]:
+        """One step on the current values of the inputs; returns (out, final_state)."""
+        if self.graph is None:
+            raise RuntimeError("TimeShardedPrefillGraph was released")
+        self.graph.replay()
+        return self.out, self.final_state
+
+    def release(self) -> None:
+        """Frees the graph (and the collective it holds)."""
+        self.graph = None

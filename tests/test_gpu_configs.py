@@ -217,3 +217,23 @@ def test_segmented_prefill_with_masks_and_initial(cuda, native_lib, h, t, segmen
                out=(host(out), ro), final_state=(host(fin), rf))
     assert r["out"]["rel_err"] < TOL_BF16 and r["final_state"]["rel_err"] < TOL_BF16
     assert np.all(host(out)[0][host(valid)[0] == 0] == 0.0)
+
+
+def test_time_sharded_graph_one_device(cuda, native_lib):
+    # shard.TimeShardedPrefillGraph at world size 1 captures the library's lead schedule (a side
+    # stream forked and joined inside the call): replays match the eager call bit for bit, also
+    # after new values are copied into the captured inputs
+    import bench
+    from delta_block_lm_b200 import shard
+    q, k, v, alpha, beta = bench.make_prefill_inputs(torch, cuda, 43, b=1, t=16384)
+    plan = shard.TimeShardedPrefillGraph(q, k, v, alpha, beta)
+    for seed in (43, 44):
+        if seed != 43:
+            for dst, src in zip((q, k, v, alpha, beta), bench.make_prefill_inputs(torch, cuda, seed, b=1, t=16384)):
+                dst.copy_(src)
+        go, gf = plan.replay()
+        eo, ef = dbl.gdn2_prefill_segmented(q, k, v, alpha, beta)
+        torch.cuda.synchronize()
+        assert torch.equal(go, eo) and torch.equal(gf, ef)
+    plan.release()
+    _no_device_error(native_lib)

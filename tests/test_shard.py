@@ -100,12 +100,21 @@ def _gpu_worker(rank, world, port, tmpdir, result_q):
         # BASELINE config 4 at full size: B1/H16/T131072/d128 bf16, this rank's contiguous span
         q, k, v, alpha, beta = bench.make_prefill_inputs(torch, dev, 777, b=1, t=131072)
         lo, hi = shard.shard_bounds(q.shape[1], world, rank, align=64)
-        out, fin = shard.time_sharded_prefill(*(x[:, lo:hi].contiguous() for x in (q, k, v, alpha, beta)))
+        span = tuple(x[:, lo:hi].contiguous() for x in (q, k, v, alpha, beta))
+        out, fin = shard.time_sharded_prefill(*span)
         torch.cuda.synchronize()
         np.save(os.path.join(tmpdir, f"out{rank}.npy"), out[0, :, [0, 15]].float().cpu().numpy())
         if rank == world - 1:
             np.save(os.path.join(tmpdir, "fin.npy"), fin[0, [0, 15]].cpu().numpy())
-        result_q.put((rank, lo, hi))
+        # the same step captured as a CUDA graph (all_gather included) replays to the same bits
+        plan = shard.TimeShardedPrefillGraph(*span)
+        go, gf = plan.replay()
+        torch.cuda.synchronize()
+        same = bool(torch.equal(go, out) and torch.equal(gf, fin))
+        plan.release()
+        del plan
+        torch.cuda.synchronize()
+        result_q.put((rank, lo, hi, same))
     finally:
         dist.destroy_process_group()
 
@@ -130,11 +139,12 @@ def test_time_sharded_prefill_two_gpus(cuda, native_lib, tmp_path):
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
+    assert all(s[3] for s in spans), "graph replay differs from the eager step"
     q, k, v, alpha, beta = bench.make_prefill_inputs(torch, cuda, 777, b=1, t=131072)
     hs = [0, 15]
     seq = lambda t: t[0, :, hs].transpose(0, 1).unsqueeze(2).float().cpu().numpy()  # noqa: E731
     ro, rf, _ = O.scan_scalar(seq(q), seq(k), seq(v), seq(alpha), seq(beta))
-    got = np.concatenate([np.load(os.path.join(tmp_path, f"out{r}.npy")) for r, _, _ in spans], axis=0)
+    got = np.concatenate([np.load(os.path.join(tmp_path, f"out{s[0]}.npy")) for s in spans], axis=0)
     r = report("config4 B1/H16/T131072/d128 bf16, time-sharded over 2 NCCL ranks, heads 0 and 15",
                out=(got.transpose(1, 0, 2), ro[:, :, 0]), final_state=(np.load(os.path.join(tmp_path, "fin.npy")), rf[:, 0]))
     assert r["out"]["rel_err"] < TOL_BF16 and r["final_state"]["rel_err"] < TOL_BF16
