@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "tc_ptx.cuh"
 
 namespace dbl {
 
@@ -26,8 +27,8 @@ int prefill_dispatch(const dbl_prefill_args* a, int mode, float* transition, cud
 
 namespace {
 
-constexpr int kFoldThreads = 256;  // thread t: state rows t / 4 and t / 4 + 64, column group t % 4
-constexpr int kFoldLdA = 132;      // row stride (floats) of a staged transition: rows 4 banks apart
+constexpr int kFoldLdA = 132;  // row stride (floats) of a staged transition: 8 rows read at one k hit distinct banks
+constexpr int kFoldStages = 3;  // transitions in flight: A_{s+1}, A_{s+2} load while step s computes
 constexpr int kChunk = 64;
 
 // One fold: X_{s+1} = A_s X_s + B_s over `V` columns.
@@ -57,27 +58,29 @@ __device__ __forceinline__ void fold_commit() { asm volatile("cp.async.commit_gr
 template <int N>
 __device__ __forceinline__ void fold_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
-// c += a * (x.x, x.y) on an f32 pair: one fma.rn per lane, the same rounding as two fmaf.
-__device__ __forceinline__ void fold_fma2(float2& c, float a, float2 x) {
-    asm("{.reg .b64 ra, rx, rc;\n\t"
-        "mov.b64 ra, {%2, %2};\n\tmov.b64 rx, {%3, %4};\n\tmov.b64 rc, {%0, %1};\n\t"
-        "fma.rn.f32x2 rc, ra, rx, rc;\n\tmov.b64 {%0, %1}, rc;\n\t}"
-        : "+f"(c.x), "+f"(c.y)
-        : "f"(a), "f"(x.x), "f"(x.y));
+// x = hi + lo with hi, lo tf32 (round to nearest): hi carries the top 11 bits of the significand,
+// lo the next 11, so hi*hi' + hi*lo' + lo*hi' reproduces an f32 product to about 2^-22.
+__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+    hi = to_tf32(x);
+    lo = to_tf32(x - __uint_as_float(hi));
 }
 
-// X_{s+1} = A_s X_s + B_s for s = 0 .. S-1, one CTA per (COLS columns, head).  f32 FMAs in
-// increasing k from the offset (the fold is short, S <= a few dozen steps of a K x K by K x COLS
-// product, and its errors would reach every later state, so it stays in full f32).  The step is a
-// dependency chain, so A_{s+1} and B_{s+1} are staged into shared memory by cp.async while step s
-// computes; X lives in shared memory, and each thread keeps 2 rows x COLS/4 columns in registers.
+// X_{s+1} = A_s X_s + B_s for s = 0 .. S-1, one CTA of 8 warps per (COLS columns, head).  The step
+// is a dependency chain, so the transitions of the next two steps load by cp.async into a ring of
+// three while step s computes, and the next offsets into registers.  The K x K by K x COLS product
+// runs on mma.sync m16n8k8 tf32 with each operand split into two tf32 parts (three products per
+// tile, the lo x lo term dropped), accumulating in f32 from the offset: about f32 accuracy (the
+// fold's errors reach every later state).  On CUDA cores the same product is bound by shared-memory
+// wavefronts (every 16-byte load costs four, broadcast or not); the fragments here cost one per
+// 32 values.  Warp w owns rows [16 w, 16 w + 16) and every column of the block; X lives in shared
+// memory.
 template <int COLS>
-__global__ void __launch_bounds__(kFoldThreads, 1) span_fold_kernel(const FoldParams p) {
-    constexpr int CPT = COLS / 4;  // columns per thread (4 column groups)
+__global__ void __launch_bounds__(256, 1) span_fold_kernel(const FoldParams p) {
+    constexpr int NT = COLS / 8;      // n-tiles of 8 columns
+    constexpr int LDX = COLS + 8;     // X row stride: B fragments (4 rows x 8 columns) conflict-free
     extern __shared__ __align__(16) float fold_smem[];
-    float* sA = fold_smem;                    // [2][128][kFoldLdA]
-    float* sB = sA + 2 * 128 * kFoldLdA;      // [2][128][COLS]
-    float* sX = sB + 2 * 128 * COLS;          // [128][COLS]
+    float* sA = fold_smem;                                // [kFoldStages][128][kFoldLdA]
+    float* sX = sA + kFoldStages * 128 * kFoldLdA;        // [128][LDX]
     const bool second = static_cast<int>(blockIdx.x) >= p.nx0;
     const int bx = second ? blockIdx.x - p.nx0 : blockIdx.x;
     const int V = second ? p.job1.V : p.job0.V;
@@ -87,110 +90,106 @@ __global__ void __launch_bounds__(kFoldThreads, 1) span_fold_kernel(const FoldPa
     float* starts = second ? p.job1.starts : p.job0.starts;
     float* endp = second ? p.job1.end : p.job0.end;
     const int h = blockIdx.y, c0 = bx * COLS, K = p.K, S = p.S;
-    const int t = threadIdx.x, rp = t >> 2, cc = (t & 3) * CPT;
-    const int rows[2] = {rp, rp + 64};
-    const bool act[2] = {rp < K, rp + 64 < K};
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31, g = lane >> 2, t4 = lane & 3;
+    const int r0 = 16 * warp + g;  // accumulator rows r0 and r0 + 8
+    const bool act = 16 * warp < K;
     const size_t xb = (size_t)h * K * V;
-    const int q4 = K >> 2;
 
     auto stage = [&](int s) {
-        const int buf = s & 1;
         const float* As = p.A + ((size_t)s * p.H + h) * K * K;
-        float* dA = sA + buf * (128 * kFoldLdA);
-        for (int e = t; e < K * q4; e += kFoldThreads) {
+        float* dA = sA + (s % kFoldStages) * (128 * kFoldLdA);
+        const int q4 = K >> 2;
+        for (int e = t; e < K * q4; e += 256) {
             const int r = e / q4, c = e - r * q4;
             fold_cp16(dA + r * kFoldLdA + 4 * c, As + (size_t)r * K + 4 * c);
         }
-        if (Bp) {
-            const float* Bs = Bp + ((size_t)s * p.H + h) * K * V + c0;
-            float* dB = sB + buf * (128 * COLS);
-            for (int e = t; e < K * (COLS / 4); e += kFoldThreads) {
-                const int r = e / (COLS / 4), c = e % (COLS / 4);
-                fold_cp16(dB + r * COLS + 4 * c, Bs + (size_t)r * V + 4 * c);
-            }
+        fold_commit();  // one group per stage on every thread, empty or not
+    };
+    // the offsets of step s at this thread's accumulator positions (rows r0, r0 + 8; columns
+    // 8 nt + 2 t4, + 1)
+    auto load_b = [&](int s, float2 (&bb)[NT][2]) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) bb[nt][0] = bb[nt][1] = make_float2(0.f, 0.f);
+        if (!Bp || !act) return;
+        const float* Bs = Bp + ((size_t)s * p.H + h) * K * V + c0 + 2 * t4;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            bb[nt][0] = *reinterpret_cast<const float2*>(Bs + (size_t)r0 * V + 8 * nt);
+            bb[nt][1] = *reinterpret_cast<const float2*>(Bs + (size_t)(r0 + 8) * V + 8 * nt);
         }
-        fold_commit();
+    };
+    auto store_rows = [&](float* dst) {  // X (in shared memory) -> dst [K][V] at column c0
+        for (int e = t; e < K * (COLS / 4); e += 256) {
+            const int r = e / (COLS / 4), c4 = e % (COLS / 4);
+            *reinterpret_cast<float4*>(dst + (size_t)r * V + c0 + 4 * c4) =
+                *reinterpret_cast<const float4*>(sX + r * LDX + 4 * c4);
+        }
     };
 
-    if (S > 0) stage(0);
-    for (int e = t; e < K * COLS; e += kFoldThreads) {
+    float2 bnext[NT][2];
+    if (S > 0) {
+        stage(0);
+        if (S > 1) stage(1);
+        load_b(0, bnext);
+    }
+    for (int e = t; e < K * COLS; e += 256) {
         const int r = e / COLS, c = e % COLS;
         float x = 0.f;
         if (ident) x = (r == c0 + c) ? 1.f : 0.f;
         else if (X0) x = X0[xb + (size_t)r * V + c0 + c];
-        sX[e] = x;
+        sX[r * LDX + c] = x;
     }
     for (int s = 0; s < S; ++s) {
-        if (s + 1 < S) {
-            stage(s + 1);  // buffer (s + 1) & 1 was last read in step s - 1, before its barriers
-            fold_wait<1>();
-        } else {
-            fold_wait<0>();
+        if (s + 1 < S) fold_wait<1>();  // A_s landed; A_{s+1} may still be in flight
+        else fold_wait<0>();
+        __syncthreads();  // every thread's copies of A_s, and X_s
+        if (s + 2 < S) stage(s + 2);  // its slot held A_{s-1}, last read before the barrier above
+        float c[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            c[nt][0] = bnext[nt][0].x, c[nt][1] = bnext[nt][0].y;
+            c[nt][2] = bnext[nt][1].x, c[nt][3] = bnext[nt][1].y;
         }
-        __syncthreads();  // A_s, B_s and X_s visible to every thread
-        const int buf = s & 1;
-        float2 acc[2][CPT / 2];
+        if (s + 1 < S) load_b(s + 1, bnext);
+        if (starts) store_rows(starts + ((size_t)s * p.H + h) * K * V);
+        if (act) {
+            const float* Aw = sA + (s % kFoldStages) * (128 * kFoldLdA) + r0 * kFoldLdA + t4;
+#pragma unroll 4
+            for (int ks = 0; ks < K / 8; ++ks) {
+                const float* Ar = Aw + 8 * ks;
+                uint32_t ah[4], al[4];
+                split_tf32(Ar[0], ah[0], al[0]);
+                split_tf32(Ar[8 * kFoldLdA], ah[1], al[1]);
+                split_tf32(Ar[4], ah[2], al[2]);
+                split_tf32(Ar[8 * kFoldLdA + 4], ah[3], al[3]);
+                const float* Xr = sX + (8 * ks + t4) * LDX + g;
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const float* xr = sX + rows[i] * COLS + cc;
-            if (act[i] && starts) {
-                float* dst = starts + ((size_t)s * p.H + h) * K * V + (size_t)rows[i] * V + c0 + cc;
-#pragma unroll
-                for (int c4 = 0; c4 < CPT / 4; ++c4)
-                    reinterpret_cast<float4*>(dst)[c4] = reinterpret_cast<const float4*>(xr)[c4];
-            }
-            const float* br = sB + buf * (128 * COLS) + rows[i] * COLS + cc;
-#pragma unroll
-            for (int c2 = 0; c2 < CPT / 2; ++c2)
-                acc[i][c2] = (Bp && act[i]) ? reinterpret_cast<const float2*>(br)[c2] : make_float2(0.f, 0.f);
-        }
-        const float* a0 = sA + buf * (128 * kFoldLdA) + rp * kFoldLdA;
-        const float* a1 = a0 + 64 * kFoldLdA;
-        if (act[0]) {
-#pragma unroll 2
-            for (int k = 0; k < K; k += 4) {
-                const float4 u = *reinterpret_cast<const float4*>(a0 + k);
-                const float4 w = act[1] ? *reinterpret_cast<const float4*>(a1 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
-                const float ua[4] = {u.x, u.y, u.z, u.w}, wa[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                    const float4* xr = reinterpret_cast<const float4*>(sX + (k + kk) * COLS + cc);
-#pragma unroll
-                    for (int c4 = 0; c4 < CPT / 4; ++c4) {
-                        const float4 x = xr[c4];
-                        fold_fma2(acc[0][2 * c4], ua[kk], make_float2(x.x, x.y));
-                        fold_fma2(acc[0][2 * c4 + 1], ua[kk], make_float2(x.z, x.w));
-                        fold_fma2(acc[1][2 * c4], wa[kk], make_float2(x.x, x.y));
-                        fold_fma2(acc[1][2 * c4 + 1], wa[kk], make_float2(x.z, x.w));
-                    }
+                for (int nt = 0; nt < NT; ++nt) {
+                    uint32_t bh[2], bl[2];
+                    split_tf32(Xr[8 * nt], bh[0], bl[0]);
+                    split_tf32(Xr[4 * LDX + 8 * nt], bh[1], bl[1]);
+                    mma_tf32_16x8x8(c[nt], al[0], al[1], al[2], al[3], bh[0], bh[1]);
+                    mma_tf32_16x8x8(c[nt], ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
+                    mma_tf32_16x8x8(c[nt], ah[0], ah[1], ah[2], ah[3], bh[0], bh[1]);
                 }
             }
         }
-        __syncthreads();  // every read of X_s and of this step's buffers is done
+        __syncthreads();  // every read of X_s is done
+        if (act) {
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            if (!act[i]) continue;
-            float2* xw = reinterpret_cast<float2*>(sX + rows[i] * COLS + cc);
-#pragma unroll
-            for (int c2 = 0; c2 < CPT / 2; ++c2) xw[c2] = acc[i][c2];
+            for (int nt = 0; nt < NT; ++nt) {
+                *reinterpret_cast<float2*>(sX + r0 * LDX + 8 * nt + 2 * t4) = make_float2(c[nt][0], c[nt][1]);
+                *reinterpret_cast<float2*>(sX + (r0 + 8) * LDX + 8 * nt + 2 * t4) = make_float2(c[nt][2], c[nt][3]);
+            }
         }
     }
     __syncthreads();
-    if (endp) {
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            if (!act[i]) continue;
-            const float4* xr = reinterpret_cast<const float4*>(sX + rows[i] * COLS + cc);
-            float4* dst = reinterpret_cast<float4*>(endp + xb + (size_t)rows[i] * V + c0 + cc);
-#pragma unroll
-            for (int c4 = 0; c4 < CPT / 4; ++c4) dst[c4] = xr[c4];
-        }
-    }
+    if (endp) store_rows(endp + xb);
 }
 
 template <int COLS>
 constexpr size_t fold_smem_bytes() {
-    return sizeof(float) * (2 * 128 * kFoldLdA + 2 * 128 * COLS + 128 * COLS);
+    return sizeof(float) * (kFoldStages * 128 * kFoldLdA + 128 * (COLS + 8));
 }
 
 int fold_check_job(const FoldJob& j, int K) {
@@ -208,15 +207,15 @@ int fold_launch_cols(const FoldParams& p, int nx, cudaStream_t st) {
     constexpr size_t smem = fold_smem_bytes<COLS>();
     cudaError_t e = cudaFuncSetAttribute(span_fold_kernel<COLS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_status(e, "span fold: cudaFuncSetAttribute");
-    span_fold_kernel<COLS><<<dim3((unsigned)nx, (unsigned)p.H), kFoldThreads, smem, st>>>(p);
+    span_fold_kernel<COLS><<<dim3((unsigned)nx, (unsigned)p.H), 256, smem, st>>>(p);
     return launch_status("span_fold_kernel");
 }
 
 // One launch for job 0 and, when job1.V > 0, job 1.  Column blocks of 16 while the grid fits the
 // device in one wave, else of 32 (half the CTAs, twice the work each).
 int fold_launch(FoldParams p, cudaStream_t st) {
-    if (p.K <= 0 || p.K > 128 || p.K % 4 != 0 || p.H <= 0 || p.S < 0)
-        return fail(DBL_ERR_UNSUPPORTED, "span fold: key width must be a multiple of 4 up to 128");
+    if (p.K <= 0 || p.K > 128 || p.K % 16 != 0 || p.H <= 0 || p.S < 0)
+        return fail(DBL_ERR_UNSUPPORTED, "span fold: key width must be a multiple of 16 up to 128");
     if (p.S > 0 && (!p.A || !aligned(p.A, 16)))
         return fail(DBL_ERR_INVALID_ARGUMENT, "span fold: 16-byte aligned transitions are required");
     if (p.H > 65535) return fail(DBL_ERR_UNSUPPORTED, "span fold: at most 65535 heads");

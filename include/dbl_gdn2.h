@@ -109,8 +109,9 @@ int dbl_gdn2_span_transition(const dbl_prefill_args *args, float *transition,
  * spans (dbl_gdn2_span_transition and dbl_gdn2_prefill from a zero state); starts [S,H,K,V]
  * (optional) receives X_0 .. X_{S-1}, the start state of every span, end [H,K,V] (optional) X_S,
  * and composed_transition [H,K,K] (optional) transition[S-1] ... transition[0], the transition of
- * the whole run of spans.  K a multiple of 4 up to 128, V a multiple of 16; arrays contiguous and
- * 16-byte aligned.  No counterpart in the reference, which has no time sharding. */
+ * the whole run of spans.  K a multiple of 16 up to 128, V a multiple of 16; arrays contiguous and
+ * 16-byte aligned.  f32 accuracy: tensor-core products of operands split into two tf32 parts.
+ * No counterpart in the reference, which has no time sharding. */
 int dbl_gdn2_span_fold(const float *transition, const float *offset, int64_t segments, int64_t heads,
                        int64_t key_dim, int64_t value_dim, const float *start, float *starts, float *end,
                        float *composed_transition, dbl_stream_t stream);
