@@ -388,13 +388,14 @@ def bench_long(torch, dist, args, dev, rank, world):
     lo, hi = shard.shard_bounds(t_total, world, rank, align=CHUNK)
     q, k, v, alpha, beta = make_prefill_inputs(torch, dev, 777 + rank, b=1, t=hi - lo)
     stream = torch.cuda.current_stream(dev)
-    segs = shard.pick_segments(hi - lo, H, shard.sm_count(dev))
+    groups = shard.segment_groups(hi - lo, H, shard.sm_count(dev))
+    segs = sum(c for _, c, _ in groups)
     K = V = D
 
     def step(ev=None):
         rec = (lambda i: ev[i].record(stream)) if ev else (lambda i: None)
         rec(0)
-        maps = shard.segment_maps(q, k, v, alpha, beta, segs)
+        maps = shard.segment_maps(q, k, v, alpha, beta, groups=groups)
         rec(1)
         starts = None
         s0 = torch.zeros((1, H, K, V), device=dev, dtype=torch.float32)
@@ -407,7 +408,7 @@ def bench_long(torch, dist, args, dev, rank, world):
             As, Bs = shard.exchange_span_states(At, Bt, rank, world)
             start = shard.fold_span_states(Bs[0], As, Bs, rank)
         rec(2)
-        out = shard.segmented_prefill(q, k, v, alpha, beta, segments=segs, maps=maps, start=start,
+        out = shard.segmented_prefill(q, k, v, alpha, beta, groups=groups, maps=maps, start=start,
                                       starts=starts)
         rec(3)
         return out
@@ -431,7 +432,8 @@ def bench_long(torch, dist, args, dev, rank, world):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms, *phases = tt.tolist()
     ms_step = ms / args.steps
-    schedule = f"{segs} equal segments per GPU: pass 1 maps, hand-off, pass 2 rescan"
+    schedule = (f"{segs} segments per GPU ({' + '.join(f'{c} x {l // CHUNK}' for _, c, l in groups)} chunks): "
+                "pass 1 maps, hand-off, pass 2 rescan")
     uniform = None
     eager = None
     if world > 1:
@@ -441,7 +443,7 @@ def bench_long(torch, dist, args, dev, rank, world):
         eager = {"ms_per_step": ms_step, "phases_ms": {"pass1_segment_maps": phases[0],
                                                        "handoff_compose_allgather_fold": phases[1],
                                                        "pass2_fold_and_rescan": phases[2]}}
-        plan = shard.TimeShardedPrefillGraph(q, k, v, alpha, beta, segments=segs, warmup=args.warmup)
+        plan = shard.TimeShardedPrefillGraph(q, k, v, alpha, beta, warmup=args.warmup)
         for _ in range(args.warmup):
             plan.replay()
         torch.cuda.synchronize(dev)
@@ -462,7 +464,7 @@ def bench_long(torch, dist, args, dev, rank, world):
         # one GPU: the value is the single C-ABI call with the library's schedule (segments = 0: a
         # lead segment scanned from the initial state beside the maps of the other segments, which
         # needs no hand-off); the equal-segment steps timed above are kept for comparison
-        uniform = {"ms_per_step": ms_step,
+        uniform = {"schedule": schedule, "ms_per_step": ms_step,
                    "phases_ms": {"pass1_segment_maps": phases[0], "fold": phases[1],
                                  "pass2_fold_and_rescan": phases[2]}}
         for _ in range(args.warmup):
@@ -492,7 +494,7 @@ def bench_long(torch, dist, args, dev, rank, world):
                           "rescan)" + ("" if world == 1 else ", plus the hand-off"),
             "handoff": "one all_gather of (A_g | B_g) [H,K,K+V] f32 per rank" if world > 1 else None,
             "handoff_bytes_gathered_per_rank": handoff_bytes,
-            "equal_segments_one_gpu": uniform,
+            "python_segments_one_gpu": uniform,
             "roofline": {"bound": "hbm", "algorithmic_bytes": alg,
                          "achieved_gbs_aggregate": alg / (ms_step / 1e3) / 1e9, "peak_per_gpu": hbm,
                          "frac_of_aggregate_peak": alg / (ms_step / 1e3) / 1e9 / (hbm * world),

@@ -100,18 +100,83 @@ def pick_segments(t_span: int, heads: int, sms: int = 148) -> int:
     return s
 
 
-def _segments(x: torch.Tensor, S: int) -> torch.Tensor:
-    """[1, T, ...] -> [S, T/S, ...] view of the same memory (segment s = tokens [s T/S, ...))."""
-    return x.reshape((S, x.shape[1] // S) + tuple(x.shape[2:]))
+def segment_groups(t_span: int, heads: int, sms: int = 148) -> List[Tuple[int, int, int]]:
+    """The segments of one span as groups (t0, count, length): `count` consecutive segments of
+    `length` tokens from token t0.  Up to floor(sms / heads) segments of ceil(chunks / that) whole
+    64-token chunks, so one launch of segments x heads CTAs fills the device; when the chunks do
+    not divide evenly the last segment is shorter and forms a second group (a second, concurrent
+    launch).  A span that is not whole chunks is one segment."""
+    if t_span % CHUNK:
+        return [(0, 1, t_span)]
+    n = t_span // CHUNK
+    m = max(1, min(sms // max(1, heads), n))
+    L = -(-n // m)
+    full = n // L
+    groups = [(0, full, L * CHUNK)]
+    if n > full * L:
+        groups.append((full * L * CHUNK, 1, (n - full * L) * CHUNK))
+    return groups
 
 
-def segment_maps(q, k, v, alpha, beta, S: int, *, scale=None, chunk_size=CHUNK):
-    """(A [S,H,K,K], B [S,H,K,V]) of the S equal segments of a [1, T, H, D] span (pass 1)."""
-    A = kernels.gdn2_span_transition(_segments(k, S), _segments(alpha, S), _segments(beta, S),
+def _resolve_groups(t_span: int, heads: int, device, segments: Optional[int]):
+    """`segments` equal segments when given (None when they do not divide the span), else
+    segment_groups for the device."""
+    if segments:
+        return [(0, segments, t_span // segments)] if t_span % segments == 0 else None
+    return segment_groups(t_span, heads, sm_count(device))
+
+
+def _group_view(x: torch.Tensor, t0: int, count: int, length: int) -> torch.Tensor:
+    """Tokens [t0, t0 + count * length) of [1, T, ...] as [count, length, ...] (same memory)."""
+    return x[:, t0:t0 + count * length].reshape((count, length) + tuple(x.shape[2:]))
+
+
+_SIDE = {}
+
+
+def _on_groups(groups, fn, device: torch.device) -> None:
+    """fn(t0, count, length, s0) for every group (s0 = index of its first segment); the second group
+    runs on a side stream of `device`, joined before return, so the two launches share the GPU."""
+    s0 = 0
+    jobs = []
+    for t0, count, length in groups:
+        jobs.append((t0, count, length, s0))
+        s0 += count
+    if len(jobs) == 1:
+        fn(*jobs[0])
+        return
+    cur = torch.cuda.current_stream(device)
+    side = _SIDE.get(device.index)
+    if side is None:
+        side = _SIDE[device.index] = torch.cuda.Stream(device=device)
+    side.wait_stream(cur)
+    with torch.cuda.stream(cur):
+        fn(*jobs[0])
+    with torch.cuda.stream(side):
+        for job in jobs[1:]:
+            fn(*job)
+    cur.wait_stream(side)
+
+
+def segment_maps(q, k, v, alpha, beta, segments: Optional[int] = None, *, scale=None, chunk_size=CHUNK,
+                 groups=None):
+    """(A [S,H,K,K], B [S,H,K,V]) of the segments of a [1, T, H, D] span (pass 1): `segments`
+    equal ones, or segment_groups for the device (or the given `groups`)."""
+    T, H, K, V = q.shape[1], q.shape[2], q.shape[3], v.shape[3]
+    if groups is None:
+        groups = _resolve_groups(T, H, q.device, segments)
+    S = sum(c for _, c, _ in groups)
+    A = torch.empty((S, H, K, K), device=q.device, dtype=torch.float32)
+    Bm = torch.empty((S, H, K, V), device=q.device, dtype=torch.float32)
+
+    def run(t0, count, length, s0):
+        view = lambda x: _group_view(x, t0, count, length)  # noqa: E731
+        kernels.gdn2_span_transition(view(k), view(alpha), view(beta), transition=A[s0:s0 + count],
                                      chunk_size=chunk_size)
-    _, Bm = kernels.gdn2_prefill(_segments(q, S), _segments(k, S), _segments(v, S),
-                                 _segments(alpha, S), _segments(beta, S), scale=scale,
-                                 want_output=False, chunk_size=chunk_size)
+        kernels.gdn2_prefill(view(q), view(k), view(v), view(alpha), view(beta), scale=scale,
+                             want_output=False, final_state=Bm[s0:s0 + count], chunk_size=chunk_size)
+
+    _on_groups(groups, run, q.device)
     return A, Bm
 
 
@@ -144,30 +209,36 @@ def segment_starts(A: torch.Tensor, Bm: torch.Tensor, start: torch.Tensor) -> to
 
 def segmented_prefill(q, k, v, alpha, beta, *, segments: Optional[int] = None, scale=None,
                       initial_state: Optional[torch.Tensor] = None, chunk_size: int = CHUNK,
-                      maps=None, start: Optional[torch.Tensor] = None, starts: Optional[torch.Tensor] = None):
+                      maps=None, start: Optional[torch.Tensor] = None, starts: Optional[torch.Tensor] = None,
+                      groups=None):
     """Prefill of one long sequence [1, T, H, D] on one GPU through time segmentation.
 
     Returns (out [1, T, H, V], final_state [1, H, K, V]).  Without ``maps`` this is one C-ABI call
     (kernels.gdn2_prefill_segmented: pass 1, fold and rescan in the library); ``maps`` reuses
-    pass-1 results computed by the caller and ``start`` overrides the span's start state (the
-    multi-GPU driver, which has already computed the maps to hand them off); ``starts``
-    [S, H, K, V] are the segment start states when the caller has already folded them.
+    pass-1 results computed by the caller (``segment_maps`` with the same ``segments`` / ``groups``)
+    and ``start`` overrides the span's start state (the multi-GPU driver, which has already
+    computed the maps to hand them off); ``starts`` [S, H, K, V] are the segment start states when
+    the caller has already folded them.
     """
     if q.shape[0] != 1:
         raise ValueError("segmented_prefill handles one sequence (batch 1)")
     T, H = q.shape[1], q.shape[2]
-    if maps is None and segments is None and chunk_size == CHUNK:
+    if maps is None and segments is None and groups is None and chunk_size == CHUNK:
         # the library's own schedule (a lead segment beside the maps of the others)
         return kernels.gdn2_prefill_segmented(q, k, v, alpha, beta, segments=0, scale=scale,
                                               initial_state=start if start is not None else initial_state)
-    S = segments or pick_segments(T, H, sm_count(q.device))
-    if S == 1 or T % S:
+    if groups is None:
+        groups = _resolve_groups(T, H, q.device, segments)
+    S = 0 if groups is None else sum(c for _, c, _ in groups)
+    if S <= 1:
         return kernels.gdn2_prefill(q, k, v, alpha, beta, scale=scale,
                                     initial_state=start if start is not None else initial_state,
                                     chunk_size=chunk_size)
     if maps is None:
-        return kernels.gdn2_prefill_segmented(q, k, v, alpha, beta, segments=S, scale=scale,
-                                              initial_state=start if start is not None else initial_state)
+        if len(groups) == 1:
+            return kernels.gdn2_prefill_segmented(q, k, v, alpha, beta, segments=S, scale=scale,
+                                                  initial_state=start if start is not None else initial_state)
+        maps = segment_maps(q, k, v, alpha, beta, scale=scale, chunk_size=chunk_size, groups=groups)
     A, Bm = maps
     K, V = q.shape[3], v.shape[3]
     if start is None:
@@ -176,9 +247,15 @@ def segmented_prefill(q, k, v, alpha, beta, *, segments: Optional[int] = None, s
     if starts is None:
         starts = segment_starts(A, Bm, start.to(torch.float32))
     out = torch.empty((1, T, H, V), device=q.device, dtype=q.dtype)
-    _, fin = kernels.gdn2_prefill(_segments(q, S), _segments(k, S), _segments(v, S),
-                                  _segments(alpha, S), _segments(beta, S), scale=scale,
-                                  initial_state=starts, out=_segments(out, S), chunk_size=chunk_size)
+    fin = torch.empty((S, H, K, V), device=q.device, dtype=torch.float32)
+
+    def run(t0, count, length, s0):
+        view = lambda x: _group_view(x, t0, count, length)  # noqa: E731
+        kernels.gdn2_prefill(view(q), view(k), view(v), view(alpha), view(beta), scale=scale,
+                             initial_state=starts[s0:s0 + count], out=view(out),
+                             final_state=fin[s0:s0 + count], chunk_size=chunk_size)
+
+    _on_groups(groups, run, q.device)
     return out, fin[S - 1:S]
 
 
@@ -198,8 +275,8 @@ def time_sharded_prefill(q, k, v, alpha, beta, *, group=None, scale: Optional[fl
         return segmented_prefill(q, k, v, alpha, beta, segments=segments, scale=scale,
                                  initial_state=initial_state, chunk_size=chunk_size)
     T, H = q.shape[1], q.shape[2]
-    S = segments or pick_segments(T, H, sm_count(q.device))
-    if S == 1 or T % S:
+    groups = _resolve_groups(T, H, q.device, segments)
+    if groups is None or sum(c for _, c, _ in groups) == 1:
         # unsegmented span: rank 0 scans from the initial state, the others hand off (A_g, B_g)
         if rank == 0:
             out, fin = kernels.gdn2_prefill(q, k, v, alpha, beta, scale=scale,
@@ -213,7 +290,7 @@ def time_sharded_prefill(q, k, v, alpha, beta, *, group=None, scale: Optional[fl
         s_in = fold_span_states(Bs[0], As, Bs, rank)
         return kernels.gdn2_prefill(q, k, v, alpha, beta, scale=scale, initial_state=s_in,
                                     chunk_size=chunk_size)
-    maps = segment_maps(q, k, v, alpha, beta, S, scale=scale, chunk_size=chunk_size)
+    maps = segment_maps(q, k, v, alpha, beta, scale=scale, chunk_size=chunk_size, groups=groups)
     K, V = q.shape[3], v.shape[3]
     starts = None
     if rank == 0:
@@ -227,7 +304,7 @@ def time_sharded_prefill(q, k, v, alpha, beta, *, group=None, scale: Optional[fl
         At, Bt = compose_maps(*maps)
         As, Bs = exchange_span_states(At, Bt, rank, world, group)
         start = fold_span_states(Bs[0], As, Bs, rank)
-    return segmented_prefill(q, k, v, alpha, beta, segments=S, scale=scale, chunk_size=chunk_size,
+    return segmented_prefill(q, k, v, alpha, beta, scale=scale, chunk_size=chunk_size, groups=groups,
                              maps=maps, start=start, starts=starts)
 
 

@@ -237,3 +237,48 @@ def test_time_sharded_graph_one_device(cuda, native_lib):
         assert torch.equal(go, eo) and torch.equal(gf, ef)
     plan.release()
     _no_device_error(native_lib)
+
+
+def test_grouped_segments_one_device(cuda, native_lib):
+    # the multi-GPU rank path on one device: a T = 32768 span (a 4-GPU rank's share of config 4)
+    # as 8 segments of 57 chunks plus one of 56 (shard.segment_groups; the ninth runs on a side
+    # stream), its maps, fold and rescan, eager and captured as a CUDA graph, against the oracle on
+    # two heads and against the unsegmented kernel on all heads
+    import bench
+    from delta_block_lm_b200 import shard
+    T = 32768
+    q, k, v, alpha, beta = bench.make_prefill_inputs(torch, cuda, 45, b=1, t=T)
+    groups = shard.segment_groups(T, 16, shard.sm_count(cuda))
+    assert len(groups) == 2 and sum(c for _, c, _ in groups) == 9
+
+    def step():
+        maps = shard.segment_maps(q, k, v, alpha, beta, groups=groups)
+        return shard.segmented_prefill(q, k, v, alpha, beta, groups=groups, maps=maps)
+
+    out, fin = step()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        g_out, g_fin = step()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(g_out, out) and torch.equal(g_fin, fin)
+    del graph
+    _no_device_error(native_lib)
+    p_out, p_fin = dbl.gdn2_prefill(q, k, v, alpha, beta)
+    torch.cuda.synchronize()
+    r0 = report("grouped segments T32768/H16 (8 x 57 + 56 chunks) vs the unsegmented kernel",
+                out=(host(out), host(p_out)), final_state=(host(fin), host(p_fin)))
+    assert r0["out"]["rel_err"] < TOL_BF16 and r0["final_state"]["rel_err"] < TOL_BF16
+    heads = (0, 15)
+    ro, rf, _ = _config4_oracle(q, k, v, alpha, beta, heads)
+    got_o = np.stack([host(out[0, :, h]) for h in heads])
+    got_f = np.stack([host(fin[0, h]) for h in heads])
+    r = report("grouped segments T32768/H16, heads 0 and 15 vs the oracle",
+               out=(got_o, ro[:, :, 0]), final_state=(got_f, rf[:, 0]))
+    assert r["out"]["rel_err"] < TOL_BF16 and r["final_state"]["rel_err"] < TOL_BF16

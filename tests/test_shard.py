@@ -178,6 +178,22 @@ def test_segment_composition_matches_oracle():
     assert np.abs((torch.matmul(At, init) + Bt).numpy() - full).max() < 1e-10
 
 
+def test_segment_groups():
+    from delta_block_lm_b200.shard import segment_groups
+    # floor(148 / 16) = 9 segments: 8 of ceil(n / 9) chunks and a shorter ninth
+    assert segment_groups(32768, 16) == [(0, 8, 57 * 64), (456 * 64, 1, 56 * 64)]
+    assert segment_groups(16384, 16) == [(0, 8, 29 * 64), (232 * 64, 1, 24 * 64)]
+    assert segment_groups(4096, 16) == [(0, 8, 512)]            # 64 chunks: 8 x 8, no remainder
+    assert segment_groups(8192, 4) == [(0, 32, 256)]            # 37 allowed, 32 x 4 chunks cover 128
+    assert segment_groups(100, 16) == [(0, 1, 100)]             # not whole chunks
+    assert segment_groups(131072, 128) == [(0, 1, 131072)]      # heads already fill the GPU
+    for t, h in ((32768, 16), (65536, 16), (16384, 16), (8192, 4), (640, 16), (64 * 7, 3)):
+        g = segment_groups(t, h)
+        assert sum(c * l for _, c, l in g) == t and sum(c for _, c, _ in g) * h <= 148
+        assert all(l % 64 == 0 for _, _, l in g)
+        assert all(t0 == g[0][1] * g[0][2] for t0, _, _ in g[1:])
+
+
 def test_pick_segments():
     from delta_block_lm_b200.shard import pick_segments
     assert pick_segments(131072, 16) == 8      # 128 CTAs on 148 SMs
