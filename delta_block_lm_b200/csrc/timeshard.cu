@@ -28,7 +28,7 @@ int prefill_dispatch(const dbl_prefill_args* a, int mode, float* transition, cud
 namespace {
 
 constexpr int kFoldLdA = 132;  // row stride (floats) of a staged transition: 8 rows read at one k hit distinct banks
-constexpr int kFoldStages = 3;  // transitions in flight: A_{s+1}, A_{s+2} load while step s computes
+constexpr int kFoldStages = 2;  // transitions in flight: A_{s+1} loads while step s computes
 constexpr int kChunk = 64;
 
 // One fold: X_{s+1} = A_s X_s + B_s over `V` columns.
@@ -66,21 +66,24 @@ __device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) 
 }
 
 // X_{s+1} = A_s X_s + B_s for s = 0 .. S-1, one CTA of 8 warps per (COLS columns, head).  The step
-// is a dependency chain, so the transitions of the next two steps load by cp.async into a ring of
-// three while step s computes, and the next offsets into registers.  The K x K by K x COLS product
-// runs on mma.sync m16n8k8 tf32 with each operand split into two tf32 parts (three products per
-// tile, the lo x lo term dropped), accumulating in f32 from the offset: about f32 accuracy (the
+// is a dependency chain, so the next transition loads by cp.async (one warp per row, a lane per
+// 16 bytes) while step s computes, and the next offsets into registers.  The K x K by K x COLS
+// product runs on mma.sync m16n8k8 tf32 with each operand split into two tf32 parts (three products
+// per tile, the lo x lo term dropped), accumulating in f32 from the offset: about f32 accuracy (the
 // fold's errors reach every later state).  On CUDA cores the same product is bound by shared-memory
 // wavefronts (every 16-byte load costs four, broadcast or not); the fragments here cost one per
-// 32 values.  Warp w owns rows [16 w, 16 w + 16) and every column of the block; X lives in shared
-// memory.
+// 32 values.  Warp w owns rows [16 w, 16 w + 16) and every column of the block.  X is kept in
+// shared memory as its two tf32 parts, split once when a step's result is written back (every warp
+// reads every row of X, so splitting at the read repeated the work eight times); the starts and
+// the end state are stored from the f32 accumulators.
 template <int COLS>
 __global__ void __launch_bounds__(256, 1) span_fold_kernel(const FoldParams p) {
     constexpr int NT = COLS / 8;      // n-tiles of 8 columns
     constexpr int LDX = COLS + 8;     // X row stride: B fragments (4 rows x 8 columns) conflict-free
     extern __shared__ __align__(16) float fold_smem[];
-    float* sA = fold_smem;                                // [kFoldStages][128][kFoldLdA]
-    float* sX = sA + kFoldStages * 128 * kFoldLdA;        // [128][LDX]
+    float* sA = fold_smem;                                                   // [kFoldStages][128][kFoldLdA]
+    uint32_t* sXh = reinterpret_cast<uint32_t*>(sA + kFoldStages * 128 * kFoldLdA);  // [128][LDX] tf32 hi
+    uint32_t* sXl = sXh + 128 * LDX;                                         // [128][LDX] tf32 lo
     const bool second = static_cast<int>(blockIdx.x) >= p.nx0;
     const int bx = second ? blockIdx.x - p.nx0 : blockIdx.x;
     const int V = second ? p.job1.V : p.job0.V;
@@ -98,11 +101,9 @@ __global__ void __launch_bounds__(256, 1) span_fold_kernel(const FoldParams p) {
     auto stage = [&](int s) {
         const float* As = p.A + ((size_t)s * p.H + h) * K * K;
         float* dA = sA + (s % kFoldStages) * (128 * kFoldLdA);
-        const int q4 = K >> 2;
-        for (int e = t; e < K * q4; e += 256) {
-            const int r = e / q4, c = e - r * q4;
-            fold_cp16(dA + r * kFoldLdA + 4 * c, As + (size_t)r * K + 4 * c);
-        }
+        const int q4 = K >> 2;  // 16-byte pieces per row, <= 32
+        if (lane < q4)
+            for (int r = warp; r < K; r += 8) fold_cp16(dA + r * kFoldLdA + 4 * lane, As + (size_t)r * K + 4 * lane);
         fold_commit();  // one group per stage on every thread, empty or not
     };
     // the offsets of step s at this thread's accumulator positions (rows r0, r0 + 8; columns
@@ -118,18 +119,10 @@ __global__ void __launch_bounds__(256, 1) span_fold_kernel(const FoldParams p) {
             bb[nt][1] = *reinterpret_cast<const float2*>(Bs + (size_t)(r0 + 8) * V + 8 * nt);
         }
     };
-    auto store_rows = [&](float* dst) {  // X (in shared memory) -> dst [K][V] at column c0
-        for (int e = t; e < K * (COLS / 4); e += 256) {
-            const int r = e / (COLS / 4), c4 = e % (COLS / 4);
-            *reinterpret_cast<float4*>(dst + (size_t)r * V + c0 + 4 * c4) =
-                *reinterpret_cast<const float4*>(sX + r * LDX + 4 * c4);
-        }
-    };
 
     float2 bnext[NT][2];
     if (S > 0) {
         stage(0);
-        if (S > 1) stage(1);
         load_b(0, bnext);
     }
     for (int e = t; e < K * COLS; e += 256) {
@@ -137,13 +130,14 @@ __global__ void __launch_bounds__(256, 1) span_fold_kernel(const FoldParams p) {
         float x = 0.f;
         if (ident) x = (r == c0 + c) ? 1.f : 0.f;
         else if (X0) x = X0[xb + (size_t)r * V + c0 + c];
-        sX[r * LDX + c] = x;
+        if (S > 0 && starts) starts[xb + (size_t)r * V + c0 + c] = x;  // X_0, the start of segment 0
+        if (S == 0 && endp) endp[xb + (size_t)r * V + c0 + c] = x;
+        split_tf32(x, sXh[r * LDX + c], sXl[r * LDX + c]);
     }
     for (int s = 0; s < S; ++s) {
-        if (s + 1 < S) fold_wait<1>();  // A_s landed; A_{s+1} may still be in flight
-        else fold_wait<0>();
+        fold_wait<0>();   // this thread's copies of A_s
         __syncthreads();  // every thread's copies of A_s, and X_s
-        if (s + 2 < S) stage(s + 2);  // its slot held A_{s-1}, last read before the barrier above
+        if (s + 1 < S) stage(s + 1);  // its slot held A_{s-1}, last read before the barrier above
         float c[NT][4];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
@@ -151,7 +145,6 @@ __global__ void __launch_bounds__(256, 1) span_fold_kernel(const FoldParams p) {
             c[nt][2] = bnext[nt][1].x, c[nt][3] = bnext[nt][1].y;
         }
         if (s + 1 < S) load_b(s + 1, bnext);
-        if (starts) store_rows(starts + ((size_t)s * p.H + h) * K * V);
         if (act) {
             const float* Aw = sA + (s % kFoldStages) * (128 * kFoldLdA) + r0 * kFoldLdA + t4;
 #pragma unroll 4
@@ -162,34 +155,44 @@ __global__ void __launch_bounds__(256, 1) span_fold_kernel(const FoldParams p) {
                 split_tf32(Ar[8 * kFoldLdA], ah[1], al[1]);
                 split_tf32(Ar[4], ah[2], al[2]);
                 split_tf32(Ar[8 * kFoldLdA + 4], ah[3], al[3]);
-                const float* Xr = sX + (8 * ks + t4) * LDX + g;
+                const int xo = (8 * ks + t4) * LDX + g;
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
-                    uint32_t bh[2], bl[2];
-                    split_tf32(Xr[8 * nt], bh[0], bl[0]);
-                    split_tf32(Xr[4 * LDX + 8 * nt], bh[1], bl[1]);
-                    mma_tf32_16x8x8(c[nt], al[0], al[1], al[2], al[3], bh[0], bh[1]);
-                    mma_tf32_16x8x8(c[nt], ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
-                    mma_tf32_16x8x8(c[nt], ah[0], ah[1], ah[2], ah[3], bh[0], bh[1]);
+                    const uint32_t bh0 = sXh[xo + 8 * nt], bh1 = sXh[xo + 4 * LDX + 8 * nt];
+                    const uint32_t bl0 = sXl[xo + 8 * nt], bl1 = sXl[xo + 4 * LDX + 8 * nt];
+                    mma_tf32_16x8x8(c[nt], al[0], al[1], al[2], al[3], bh0, bh1);
+                    mma_tf32_16x8x8(c[nt], ah[0], ah[1], ah[2], ah[3], bl0, bl1);
+                    mma_tf32_16x8x8(c[nt], ah[0], ah[1], ah[2], ah[3], bh0, bh1);
                 }
             }
         }
         __syncthreads();  // every read of X_s is done
         if (act) {
+            // X_{s+1}: the start of segment s + 1 (or the end state after the last step) from the
+            // f32 accumulators, and its tf32 parts for the next step's products
+            float* dst = s + 1 < S ? (starts ? starts + ((size_t)(s + 1) * p.H + h) * K * V : nullptr)
+                                   : (endp ? endp + xb : nullptr);
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-                *reinterpret_cast<float2*>(sX + r0 * LDX + 8 * nt + 2 * t4) = make_float2(c[nt][0], c[nt][1]);
-                *reinterpret_cast<float2*>(sX + (r0 + 8) * LDX + 8 * nt + 2 * t4) = make_float2(c[nt][2], c[nt][3]);
+                const int col = 8 * nt + 2 * t4;
+                if (dst) {
+                    *reinterpret_cast<float2*>(dst + (size_t)r0 * V + c0 + col) = make_float2(c[nt][0], c[nt][1]);
+                    *reinterpret_cast<float2*>(dst + (size_t)(r0 + 8) * V + c0 + col) = make_float2(c[nt][2], c[nt][3]);
+                }
+                if (s + 1 < S) {
+                    split_tf32(c[nt][0], sXh[r0 * LDX + col], sXl[r0 * LDX + col]);
+                    split_tf32(c[nt][1], sXh[r0 * LDX + col + 1], sXl[r0 * LDX + col + 1]);
+                    split_tf32(c[nt][2], sXh[(r0 + 8) * LDX + col], sXl[(r0 + 8) * LDX + col]);
+                    split_tf32(c[nt][3], sXh[(r0 + 8) * LDX + col + 1], sXl[(r0 + 8) * LDX + col + 1]);
+                }
             }
         }
     }
-    __syncthreads();
-    if (endp) store_rows(endp + xb);
 }
 
 template <int COLS>
 constexpr size_t fold_smem_bytes() {
-    return sizeof(float) * (kFoldStages * 128 * kFoldLdA + 128 * (COLS + 8));
+    return sizeof(float) * (kFoldStages * 128 * kFoldLdA + 2 * 128 * (COLS + 8));
 }
 
 int fold_check_job(const FoldJob& j, int K) {
