@@ -537,8 +537,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     *reinterpret_cast<uint4*>(Tt + row * 128 + ((cc ^ (row & 7)) << 4)) =
                         make_uint4(pack_f16x2(u.x, u.y), pack_f16x2(u.z, u.w), pack_f16x2(w.x, w.y),
                                    pack_f16x2(w.z, w.w));
-                } else {
-                    // warps 2, 3, 6, 7 meanwhile: P from the Q rows of [K;Q] K^T
+                } else if (p.write_out) {
+                    // warps 2, 3, 6, 7 meanwhile: P from the Q rows of [K;Q] K^T (only the output
+                    // reads P: a launch without outputs, the span maps, skips it and MMA4)
                     write_p(s, fast, G);
                     tc_fence_before();  // these TMEM reads precede the next chunk's [K;Q] K^T
                 }
@@ -599,6 +600,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
 #pragma unroll
             for (int blk = 0; blk < 4; ++blk) {
+                // the Q blocks (odd) feed only the Q S half of MMA1, which only the output reads: a
+                // launch without outputs leaves them as they are (that half then holds values nothing
+                // reads; each MMA1 column depends on its own row of [K;Q] only)
+                if ((blk & 1) && !p.write_out) continue;
                 uint4* base = reinterpret_cast<uint4*>(X + blk * 8192) + ct;
                 uint4 u[2];
 #pragma unroll
