@@ -9,6 +9,10 @@
 //   pass 1  the maps (A_s, B_s) of every segment (two batched launches);
 //   fold    the start state of every segment, X_{s+1} = A_s X_s + B_s (span_fold_kernel);
 //   pass 2  every segment rescanned from its start state (one batched launch).
+// On one device the default schedule (segments = 0, lead_prefill) cuts the span into a lead
+// segment and m = SMs / H equal segments instead: the lead needs no maps, so it is scanned from the
+// initial state on a side stream while pass 1 runs over segments 1 .. m-1 (the last segment needs
+// no maps either), and the fold and one rescan of segments 1 .. m follow.
 // Across devices, device g holds time span g.  Each device composes its span's map
 // (A_g, B_g) = fold of its segment maps; device 0 instead folds its maps from the sequence's initial
 // state to its end state E_0.  Device g pulls E_0 and the maps of devices 1 .. g-1 with one

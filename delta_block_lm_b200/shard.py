@@ -93,7 +93,9 @@ def sm_count(device: Optional[torch.device] = None) -> int:
 def pick_segments(t_span: int, heads: int, sms: int = 148) -> int:
     """Segments per span: the largest power of two with segments x heads <= sms whose segments are
     whole 64-token chunks (1 when the span is short or heads alone fill the GPU).  `sms` is the
-    device's SM count (``sm_count``)."""
+    device's SM count (``sm_count``).  The C library's rule for equal segments when its lead
+    schedule does not apply, and for its multi-device entry; the drivers here use
+    ``segment_groups``."""
     s = 1
     while (s * 2) * heads <= sms and t_span % (s * 2 * CHUNK) == 0:
         s *= 2
